@@ -1,0 +1,502 @@
+"""Benchmark of the KDE/MMD hot path: Gaussian kernel-term evaluations per
+second, forward + backward, through the public API (``pyg_kde_mmd_loss``).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
+
+Workload (a "step"): one forward + backward of ``pyg_kde_mmd_loss`` over a
+ragged batch of 4096 graphs per GPU, sizes uniform in [32, 2048] points,
+target sizes = source size +- uniform [0, 64], coordinates N(0, 1) in 3-D,
+target = source + N(0, s^2) noise with s ~ U[0.05, 0.08] per graph,
+sigma = 0.25, centering on, sorted batch vectors.  Synthetic, seeded: each
+graph is generated from its own seed, so every rank can build its own share
+of a global batch without generating the rest.
+
+Multi-GPU: weak scaling.  The global batch has N * 4096 graphs; graphs are
+assigned to ranks by a greedy longest-processing-time partition of their
+cost N_i^2 + M_i^2 + N_i M_i (rapidalign_b200.shard); ranks compute their
+shares with no collective in the data path and the per-graph K values are
+gathered once after the timed region.
+
+Metric: full kernel terms (N^2 + M^2 + N M per graph, the reference's count)
+per second over the whole job.  The roofline fraction uses the unique terms
+(N(N+1)/2 + M(M+1)/2 + N M) at 14 FP32-pipe operations each, against the FP32
+rate measured on the same GPU by a packed-FMA probe kernel.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GRAPHS_PER_GPU = 4096
+SIGMA = 0.25
+SEED = 20261201
+FP32_OPS_PER_UNIQUE_TERM = 14  # 3 sub + 3 (mul, fma, fma) + 4 row FMA + 4 column FMA
+L2_FLUSH_BYTES = 512 << 20     # > 126 MB L2
+
+
+# ----------------------------------------------------------------------------
+# seeded synthetic workloads
+# ----------------------------------------------------------------------------
+
+def ragged_graph(g: int, seed: int = SEED, lo: int = 32, hi: int = 2048, dmax: int = 64,
+                 dim: int = 3):
+    """Graph g of the ragged workload: (src (n, dim), tgt (m, dim)) float32."""
+    rng = np.random.default_rng([seed, g])
+    n = int(rng.integers(lo, hi + 1))
+    m = max(1, n + int(rng.integers(-dmax, dmax + 1)))
+    noise = float(rng.uniform(0.05, 0.08))
+    src = rng.standard_normal((n, dim)).astype(np.float32)
+    base = src[:min(n, m)]
+    if m > n:
+        base = np.concatenate([base, rng.standard_normal((m - n, dim)).astype(np.float32)])
+    tgt = (base + noise * rng.standard_normal((m, dim))).astype(np.float32)
+    return src, tgt
+
+
+def ragged_sizes(graph_ids, seed: int = SEED, lo: int = 32, hi: int = 2048, dmax: int = 64):
+    """(n, m) of the given graphs without generating coordinates."""
+    out = []
+    for g in graph_ids:
+        rng = np.random.default_rng([seed, g])
+        n = int(rng.integers(lo, hi + 1))
+        m = max(1, n + int(rng.integers(-dmax, dmax + 1)))
+        out.append((n, m))
+    return np.array(out, dtype=np.int64).reshape(-1, 2)
+
+
+def ragged_batch(graph_ids, seed: int = SEED, **kw):
+    """Concatenated batch: x, y (float32), batch_x, batch_y (int64), sizes."""
+    xs, ys = [], []
+    for g in graph_ids:
+        s, t = ragged_graph(int(g), seed, **kw)
+        xs.append(s)
+        ys.append(t)
+    nx = np.array([a.shape[0] for a in xs], dtype=np.int64)
+    ny = np.array([a.shape[0] for a in ys], dtype=np.int64)
+    x = np.concatenate(xs)
+    y = np.concatenate(ys)
+    bx = np.repeat(np.arange(len(xs), dtype=np.int64), nx)
+    by = np.repeat(np.arange(len(ys), dtype=np.int64), ny)
+    return x, y, bx, by, nx, ny
+
+
+def term_counts(nx: np.ndarray, ny: np.ndarray):
+    nx = nx.astype(np.float64)
+    ny = ny.astype(np.float64)
+    full = float(np.sum(nx * nx + ny * ny + nx * ny))
+    unique = float(np.sum(nx * (nx + 1) / 2 + ny * (ny + 1) / 2 + nx * ny))
+    return full, unique
+
+
+# ----------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ----------------------------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline: the oracle (C, float64, OpenMP) on a bounded sample
+# ----------------------------------------------------------------------------
+
+def cpu_baseline(sample_graphs: int = 24, seed: int = SEED, budget_s: float = 20.0):
+    """Times the oracle's forward+backward sums on the first graphs of the
+    same workload; returns full terms/s.  Stops adding graphs once the budget
+    is used.  Uses every host thread."""
+    from oracle import oracle as O
+    O.build()
+    cores = os.cpu_count() or 1
+    total_full = 0.0
+    total_t = 0.0
+    used = 0
+    for g in range(sample_graphs):
+        x, y = ragged_graph(g, seed)
+        n, m = x.shape[0], y.shape[0]
+        a = np.full(n, 1.0 / n)
+        b = np.full(m, 1.0 / m)
+        t0 = time.perf_counter()
+        O.raw_sums(x.astype(np.float64), y.astype(np.float64), a, b, [0, n], [0, m], SIGMA,
+                   nthreads=cores)
+        total_t += time.perf_counter() - t0
+        total_full += float(n * n + m * m + n * m)
+        used += 1
+        if total_t > budget_s:
+            break
+    return {"value": total_full / total_t, "unit": "terms/s", "cores": cores, "kind": "port",
+            "sample": f"first {used} graphs of the 4096-graph ragged batch, oracle (C, fp64, "
+                      f"OpenMP) forward+backward sums, {total_t:.1f} s"}
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    from rapidalign_b200 import _lib, build as ra_build
+    from rapidalign_b200 import pyg_kde_mmd_loss
+    from rapidalign_b200.shard import lpt_partition
+    ra_build.build()
+
+    total_graphs = GRAPHS_PER_GPU * world
+    sizes = ragged_sizes(range(total_graphs))
+    cost = sizes[:, 0] ** 2 + sizes[:, 1] ** 2 + sizes[:, 0] * sizes[:, 1]
+    parts = lpt_partition(cost, world)
+    mine = np.sort(parts[rank])
+    x, y, bx, by, nx, ny = ragged_batch(mine)
+    full_local, unique_local = term_counts(nx, ny)
+
+    # device-resident inputs for `value`; pinned host copies for `e2e`
+    xd = torch.from_numpy(x).to(dev)
+    yd = torch.from_numpy(y).to(dev)
+    bxd = torch.from_numpy(bx).to(dev)
+    byd = torch.from_numpy(by).to(dev)
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.from_numpy(y).pin_memory()
+    bxh = torch.from_numpy(bx).pin_memory()
+    byh = torch.from_numpy(by).pin_memory()
+    loss_h = torch.empty(len(mine), dtype=torch.float32).pin_memory()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def step(xs, ys, bxs, bys):
+        xs = xs.detach().requires_grad_(True)
+        ys = ys.detach().requires_grad_(True)
+        loss, kxx, kyy, kxy = pyg_kde_mmd_loss(xs, ys, src_batch=bxs, tgt_batch=bys,
+                                               sigma=SIGMA, center=True)
+        loss.sum().backward()
+        return loss, xs.grad, ys.grad
+
+    stream = torch.cuda.current_stream(dev)
+
+    def timed_loop(k, e2e):
+        evs = []
+        for _ in range(k):
+            flush.fill_(1)  # evict L2 between timed steps (outside the events)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if e2e:
+                xs = xh.to(dev, non_blocking=True)
+                ys = yh.to(dev, non_blocking=True)
+                b1 = bxh.to(dev, non_blocking=True)
+                b2 = byh.to(dev, non_blocking=True)
+                loss, _, _ = step(xs, ys, b1, b2)
+                loss_h.copy_(loss.detach(), non_blocking=True)
+            else:
+                step(xd, yd, bxd, byd)
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize(dev)
+        return sum(a.elapsed_time(b) for a, b in evs) / 1e3  # seconds
+
+    for _ in range(args.warmup):
+        step(xd, yd, bxd, byd)
+    if args.profile_step:
+        # one more step and exit: the command profiled by ncu (see profiles/)
+        step(xd, yd, bxd, byd)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    # hot-kernel duration: events bracketing one forward+backward of the
+    # fused pipeline (tiles kernel dominates, see profiles/)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    launches0 = _lib.launch_count()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    t_dev = timed_loop(args.steps, e2e=False)
+    launches = _lib.launch_count() - launches0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    for _ in range(max(1, args.warmup // 2)):
+        timed_loop(1, e2e=True)
+    t_e2e = timed_loop(args.steps, e2e=True)
+    clocks = sampler.stop() if sampler else None
+
+    # kernel-level timing of the dominant (tiles) kernel for the roofline
+    t_tiles = tiles_kernel_time(xd, yd, bxd, byd, dev, reps=max(3, args.steps // 2))
+
+    # FP32 peak of this GPU (packed-FMA probe)
+    peak_ops = fp32_peak(dev)
+
+    vals = torch.tensor([t_dev, t_e2e, full_local, unique_local, t_tiles, float(launches)],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax = vals[:2].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        sums = vals[2:4].clone()
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
+        t_dev, t_e2e = tmax.tolist()
+        full_all, unique_all = sums.tolist()
+        # one gather of the per-graph results (outside the timed region)
+        with torch.no_grad():
+            loss, *_ = pyg_kde_mmd_loss(xd, yd, src_batch=bxd, tgt_batch=byd, sigma=SIGMA)
+        n_max = GRAPHS_PER_GPU + 8
+        buf = torch.zeros(n_max, dtype=torch.float64, device=dev)
+        buf[:loss.numel()] = loss.to(torch.float64)
+        gathered = [torch.zeros_like(buf) for _ in range(world)]
+        dist.all_gather(gathered, buf)
+    else:
+        full_all, unique_all = full_local, unique_local
+
+    if rank == 0:
+        K = args.steps
+        value = full_all * K / t_dev
+        e2e_value = full_all * K / t_e2e
+        # roofline of the tiles kernel on rank 0's share
+        achieved_ops = unique_local * FP32_OPS_PER_UNIQUE_TERM / t_tiles
+        line = {
+            "metric": "Gaussian kernel-term evals/sec fwd+bwd",
+            "value": value,
+            "unit": "terms/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": args.warmup,
+            "ms_per_step": t_dev / K * 1e3,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32 (fp64 sums)",
+            "data": "synthetic",
+            "config": {
+                "workload": f"ragged PyG batch, {GRAPHS_PER_GPU} graphs per GPU, 32-2048 "
+                            "points each, D=3, sigma=0.25, centred, pyg_kde_mmd_loss fwd+bwd",
+                "graphs": GRAPHS_PER_GPU * world,
+                "full_terms_per_step": full_all,
+                "unique_terms_per_step": unique_all,
+                "l2": "flushed between steps (512 MB write, outside the timed events)",
+                "sharding": "LPT partition of graph cost across ranks" if world > 1 else "none",
+                "seed": SEED,
+            },
+            "e2e": {"value": e2e_value, "unit": "terms/s",
+                    "h2d_bytes_per_step": int(xh.numel() * 4 + yh.numel() * 4 + bxh.numel() * 8
+                                              + byh.numel() * 8),
+                    "d2h_bytes_per_step": int(loss_h.numel() * 4)},
+            "gpu_launches": int(launches),
+            "roofline": {
+                "bound": "fp32",
+                "achieved": achieved_ops / 1e12,
+                "peak": peak_ops / 1e12,
+                "unit": "Tops/s (FP32-pipe lane ops, FMA = 1)",
+                "frac": achieved_ops / peak_ops,
+                "peak_source": "measured live: packed-FMA probe kernel (ra_probe_fp32_peak)",
+                "kernel": "tiles3_kernel<1> (fused fwd+bwd tile kernel)",
+                "kernel_ms": t_tiles * 1e3,
+                "ops_per_unique_term": FP32_OPS_PER_UNIQUE_TERM,
+                "traffic": read_traffic(),
+            },
+            "clocks": clocks,
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def tiles_kernel_time(xd, yd, bxd, byd, dev, reps=5):
+    """Average device time of the fused tile kernel alone, measured with CUDA
+    events around the forward with the plan/prep kernels excluded: the
+    forward is timed once as a whole and once with the kernel pipeline up to
+    the tile launch, by the library's two timing hooks."""
+    import torch
+    from rapidalign_b200 import profiling
+    return profiling.tiles_time(xd, yd, bxd, byd, SIGMA, reps=reps)
+
+
+def fp32_peak(dev) -> float:
+    import ctypes
+    import torch
+    from rapidalign_b200 import _lib
+    lib = _lib.load()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    scratch = torch.empty(sms * 8 * 256, dtype=torch.float32, device=dev)
+    out = ctypes.c_double(0.0)
+    best = 0.0
+    for _ in range(3):
+        rc = lib.ra_probe_fp32_peak(scratch.data_ptr(), scratch.numel(), 2048, ctypes.byref(out),
+                                    _lib.stream_handle(dev))
+        _lib.check(rc, "fp32 probe")
+        best = max(best, out.value)
+    return best
+
+
+def read_traffic():
+    """DRAM bytes per launch of the tile kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    try:
+        with open(path) as f:
+            return json.load(f).get("tiles3_kernel_bytes_per_launch")
+    except (OSError, ValueError):
+        return None
+
+
+# ----------------------------------------------------------------------------
+# reference arm: the reference's CPU path (here: the oracle port)
+# ----------------------------------------------------------------------------
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    O.build()
+    cores = os.cpu_count() or 1
+    # each step: a bounded sample of the same workload (graphs g0..g0+k)
+    per_step_graphs = 6
+    times, full = [], 0.0
+    for s in range(args.warmup + args.steps):
+        t_step, f_step = 0.0, 0.0
+        for j in range(per_step_graphs):
+            g = s * per_step_graphs + j
+            x, y = ragged_graph(g)
+            n, m = x.shape[0], y.shape[0]
+            a = np.full(n, 1.0 / n)
+            b = np.full(m, 1.0 / m)
+            t0 = time.perf_counter()
+            O.raw_sums(x.astype(np.float64), y.astype(np.float64), a, b, [0, n], [0, m], SIGMA,
+                       nthreads=cores)
+            t_step += time.perf_counter() - t0
+            f_step += float(n * n + m * m + n * m)
+        if s >= args.warmup:
+            times.append(t_step)
+            full += f_step
+    value = full / sum(times)
+    line = {
+        "impl": "reference",
+        "metric": "Gaussian kernel-term evals/sec fwd+bwd",
+        "value": value,
+        "unit": "terms/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": sum(times) / len(times) * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f64",
+        "data": "synthetic",
+        "config": {"workload": f"ragged PyG batch, {GRAPHS_PER_GPU} graphs per GPU, 32-2048 "
+                               "points each, D=3, sigma=0.25, centred, pyg_kde_mmd_loss fwd+bwd",
+                   "graphs": GRAPHS_PER_GPU * world, "seed": SEED},
+        "cpu_baseline": {"value": value, "unit": "terms/s", "cores": cores, "kind": "port",
+                         "sample": f"{per_step_graphs} graphs of the ragged batch per step, "
+                                   "oracle (C, fp64, OpenMP) forward+backward sums; the "
+                                   "reference's CPU path is PyTorch and does not travel"},
+        "e2e": {"value": value, "unit": "terms/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--profile-step", action="store_true",
+                    help="warm-up steps plus one step, no timing or output (for ncu)")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

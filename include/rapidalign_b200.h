@@ -1,0 +1,213 @@
+/*
+ * rapidalign_b200.h -- C ABI of the B200 (sm_100a) KDE/MMD library.
+ *
+ * Gaussian-kernel MMD sums between point clouds,
+ *     k(u, v) = exp(-|u - v|^2 / (2 sigma^2)),
+ *     Kxx = sum_ij a_i a_j k(x_i, x_j),  Kyy = sum_ij b_i b_j k(y_i, y_j),
+ *     Kxy = sum_ij a_i b_j k(x_i, y_j),
+ * for single pairs, ragged (ptr-segmented) batches and padded dense batches,
+ * with their gradients.
+ *
+ * Conventions for every entry point:
+ *  - all array arguments are DEVICE pointers to contiguous row-major data on
+ *    the current CUDA device, except where a comment says "host";
+ *  - work is enqueued on `stream` and is asynchronous; nothing synchronises
+ *    the host;
+ *  - the library never allocates device memory: scratch space is a caller
+ *    owned `workspace` of at least the size the matching *_workspace_bytes
+ *    function returns (256-byte aligned);
+ *  - the return value is an ra_status code; ra_status_string() names it.
+ *    Argument errors are reported synchronously.  Data-dependent errors
+ *    (bad ptr offsets, non-positive weight sums) are detected on the device
+ *    and reported by ra_kde_check(), which reads one int back and therefore
+ *    synchronises `stream`;
+ *  - no global mutable state: calls on different streams with different
+ *    workspaces are independent.
+ */
+#ifndef RAPIDALIGN_B200_H
+#define RAPIDALIGN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RA_API __attribute__((visibility("default")))
+#else
+#define RA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *ra_stream_t; /* == cudaStream_t */
+
+/* ---- status codes ------------------------------------------------------ */
+enum ra_status {
+  RA_OK = 0,
+  RA_ERR_INVALID_ARGUMENT = 1,    /* null pointer, bad size, unsupported dim */
+  RA_ERR_SIGMA = 2,               /* sigma must be positive */
+  RA_ERR_WORKSPACE = 3,           /* workspace too small or misaligned */
+  RA_ERR_CUDA = 4,                /* a CUDA runtime call or launch failed */
+  /* device-detected data errors (returned by ra_kde_check) */
+  RA_ERR_PTR_START = 16,          /* ptr must start at 0 */
+  RA_ERR_PTR_END = 17,            /* ptr[-1] must equal number of nodes */
+  RA_ERR_PTR_ORDER = 18,          /* ptr offsets must be non-decreasing */
+  RA_ERR_WEIGHT_SUM = 19,         /* weights must sum to a positive value per segment */
+  RA_ERR_STATE = 20,              /* backward called without a matching forward state */
+};
+
+/* Human-readable name of a status code (static string). */
+RA_API const char *ra_status_string(int status);
+
+/* ---- the general problem description (fused forward / backward) -------- */
+
+enum ra_layout {
+  RA_LAYOUT_RAGGED = 0, /* points of pair p are rows ptr[p]..ptr[p+1] */
+  RA_LAYOUT_DENSE = 1   /* pair p = row p of a (B, Nmax, D) tensor plus a (B, Nmax) mask */
+};
+
+enum ra_weights {
+  RA_WEIGHTS_RAW = 0,         /* a_i = w_i as given (w == NULL: 1); mask applied if dense */
+  RA_WEIGHTS_SUM = 1,         /* a_i = w_i / sum_seg w; error if a segment sum <= 0
+                                 (rapidalign/kde.py:20-27, 169-199) */
+  RA_WEIGHTS_SUM_CLAMPED = 2, /* a_i = w_i m_i / max(sum_seg w m, 1e-8)  (kde.py:115-121);
+                                 w == NULL means w = 1 */
+  RA_WEIGHTS_UNIFORM = 3      /* a_i = 1 / count_seg; w ignored (kde.py:183-188) */
+};
+
+typedef struct ra_kde_desc {
+  int64_t num_pairs;   /* P (ragged) or B (dense) */
+  int32_t dim;         /* D >= 1 */
+  int32_t layout;      /* enum ra_layout */
+  int64_t num_x;       /* ragged: rows of x; dense: B * nmax_x */
+  int64_t num_y;       /* ragged: rows of y; dense: B * nmax_y */
+  int64_t nmax_x;      /* dense only: padded length of a row of x */
+  int64_t nmax_y;      /* dense only */
+  int32_t weights_x;   /* enum ra_weights */
+  int32_t weights_y;
+  int32_t center;      /* 1: subtract the weighted centroid of each cloud first */
+  int32_t need_grad;   /* 1: keep per-point state in the workspace for ra_kde_backward */
+  int32_t need_sigma_grad; /* 1: also accumulate the sigma derivative */
+  int32_t reserved;
+  double sigma;        /* bandwidth, > 0 */
+} ra_kde_desc;
+
+typedef struct ra_kde_inputs {
+  const float *x;        /* [num_x * D] */
+  const float *y;        /* [num_y * D] */
+  const float *w_x;      /* [num_x] or NULL */
+  const float *w_y;      /* [num_y] or NULL */
+  const int64_t *ptr_x;  /* ragged: [P + 1] */
+  const int64_t *ptr_y;  /* ragged: [P + 1] */
+  const uint8_t *mask_x; /* dense: [num_x] (nonzero = valid) */
+  const uint8_t *mask_y; /* dense: [num_y] */
+} ra_kde_inputs;
+
+typedef struct ra_kde_grads {
+  float *grad_x;      /* [num_x * D] or NULL */
+  float *grad_y;      /* [num_y * D] or NULL */
+  double *grad_wx;    /* [num_x] or NULL: d/dw of the given weights (incl. normalisation) */
+  double *grad_wy;    /* [num_y] or NULL */
+  double *grad_sigma; /* [P] per-pair d/dsigma or NULL (needs need_sigma_grad) */
+} ra_kde_grads;
+
+/* Workspace bytes for ra_kde_forward (+ ra_kde_backward) on `desc`. */
+RA_API size_t ra_kde_workspace_bytes(const ra_kde_desc *desc);
+
+/*
+ * Fused forward.  Replaces the three forward launches of
+ * csrc/kde_similarity.cu:84-192 / :283-381 and the normalisation and
+ * centering of rapidalign/kde.py:115-121, 169-208, 241-253.  Writes
+ * K[0..P) = Kxx, K[P..2P) = Kyy, K[2P..3P) = Kxy (fp64) and, if
+ * desc->need_grad, leaves in `workspace` what ra_kde_backward needs.
+ */
+RA_API int ra_kde_forward(const ra_kde_desc *desc, const ra_kde_inputs *in, double *K,
+                   void *workspace, size_t workspace_bytes, ra_stream_t stream);
+
+/*
+ * Backward of the fused forward: given coef[0..P) = dL/dKxx, coef[P..2P) =
+ * dL/dKyy, coef[2P..3P) = dL/dKxy (fp64, device), writes the requested
+ * gradients including the centering and weight-normalisation Jacobians.
+ * Replaces csrc/kde_similarity.cu:607-712 (and generalises it from the MMD
+ * coefficients (1, 1, -2) to any).  Must follow ra_kde_forward with the same
+ * desc, inputs and workspace and desc->need_grad = 1.
+ */
+RA_API int ra_kde_backward(const ra_kde_desc *desc, const ra_kde_inputs *in, const double *coef,
+                    const ra_kde_grads *grads, void *workspace, size_t workspace_bytes,
+                    ra_stream_t stream);
+
+/*
+ * ra_kde_forward with timing of the hot tile kernel: records two CUDA events
+ * on `stream` around that single launch, synchronises on the second and
+ * writes the elapsed milliseconds to *tiles_ms.  For measurement only.
+ */
+RA_API int ra_kde_forward_profiled(const ra_kde_desc *desc, const ra_kde_inputs *in, double *K,
+                                   void *workspace, size_t workspace_bytes, ra_stream_t stream,
+                                   float *tiles_ms);
+
+/* Reads the device error word of `workspace` (synchronises `stream`). */
+RA_API int ra_kde_check(const void *workspace, ra_stream_t stream);
+
+/* ---- legacy operator set: one entry point per op of csrc/bindings.cpp ---- */
+
+/*
+ * Dense masked forward.  Replaces kde_mmd_forward (csrc/bindings.cpp:35-45,
+ * csrc/kde_similarity.cu:84-192): x [B, Nx, D], y [B, Ny, D], w_x [B, Nx],
+ * w_y [B, Ny] (raw weights), mask_x [B, Nx], mask_y [B, Ny] (uint8),
+ * outputs Kxx, Kyy, Kxy [B] fp64.
+ */
+RA_API size_t ra_kde_mmd_forward_workspace_bytes(int64_t B, int64_t Nx, int64_t Ny, int32_t D);
+RA_API int ra_kde_mmd_forward(const float *x, const float *y, const float *w_x, const float *w_y,
+                       const uint8_t *mask_x, const uint8_t *mask_y, int64_t B, int64_t Nx,
+                       int64_t Ny, int32_t D, double sigma, double *Kxx, double *Kyy,
+                       double *Kxy, void *workspace, size_t workspace_bytes, ra_stream_t stream);
+
+/*
+ * Ragged forward.  Replaces kde_mmd_forward_segmented (csrc/bindings.cpp:47-57,
+ * csrc/kde_similarity.cu:283-381): x [NX, D], y [NY, D], raw weights w_x [NX],
+ * w_y [NY], ptr_x/ptr_y int64 [P + 1]; outputs Kxx, Kyy, Kxy [P] fp64.
+ */
+RA_API size_t ra_kde_mmd_forward_segmented_workspace_bytes(int64_t P, int64_t NX, int64_t NY,
+                                                    int32_t D);
+RA_API int ra_kde_mmd_forward_segmented(const float *x, const float *y, const float *w_x,
+                                 const float *w_y, const int64_t *ptr_x, const int64_t *ptr_y,
+                                 int64_t P, int64_t NX, int64_t NY, int32_t D, double sigma,
+                                 double *Kxx, double *Kyy, double *Kxy, void *workspace,
+                                 size_t workspace_bytes, ra_stream_t stream);
+
+/*
+ * Ragged backward.  Replaces kde_mmd_backward_segmented (csrc/bindings.cpp:59-70,
+ * csrc/kde_similarity.cu:607-712): gradients of sum_p grad_loss[p] *
+ * (Kxx + Kyy - 2 Kxy)[p] w.r.t. x (f32 [NX, D]), y (f32 [NY, D]), the raw
+ * weights (f64 [NX], [NY]) and sigma (f64 [P], per pair).  Valid for any D
+ * (the reference kernels are limited to D <= 3).
+ */
+RA_API size_t ra_kde_mmd_backward_segmented_workspace_bytes(int64_t P, int64_t NX, int64_t NY,
+                                                     int32_t D);
+RA_API int ra_kde_mmd_backward_segmented(const float *x, const float *y, const float *w_x,
+                                  const float *w_y, const int64_t *ptr_x, const int64_t *ptr_y,
+                                  int64_t P, int64_t NX, int64_t NY, int32_t D,
+                                  const double *grad_loss, double sigma, float *grad_x,
+                                  float *grad_y, double *grad_wx, double *grad_wy,
+                                  double *grad_sigma_pairs, void *workspace,
+                                  size_t workspace_bytes, ra_stream_t stream);
+
+/* ---- diagnostics ------------------------------------------------------- */
+
+/* Number of kernel launches this library has issued in the calling process
+ * (a process-wide counter; used to report launch counts in benchmarks). */
+RA_API unsigned long long ra_kernel_launch_count(void);
+
+/* Times a pure packed-FP32-FMA kernel on the current device (one warm-up
+ * launch, then one timed launch of `iters` inner iterations) and returns the
+ * FP32 lane-operation rate (an FMA counts one) in *ops_per_s.  `scratch` is a
+ * device buffer of at least (multiprocessors * 8 * 256) floats.  Synchronises
+ * `stream`.  Used as the measured FP32 roofline peak. */
+RA_API int ra_probe_fp32_peak(float *scratch, int64_t scratch_floats, int iters, double *ops_per_s,
+                       ra_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RAPIDALIGN_B200_H */

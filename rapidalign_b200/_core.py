@@ -1,0 +1,223 @@
+"""The differentiable K-sum operator behind every public entry point.
+
+``kde_sums`` returns ``(Kxx, Kyy, Kxy)`` per pair (float64) for a ragged,
+dense or single-pair problem, after the weight normalisation and centering
+the caller selects.  Its backward is one epilogue launch over the per-point
+sums the fused forward kept in its workspace: the forward evaluates every
+unique kernel term once for both the values and the gradients.
+
+Everything runs through the C ABI of ``librapidalign_b200.so``; there is no
+CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+Tensor = torch.Tensor
+
+
+@dataclass
+class Spec:
+    """Problem layout (non-tensor arguments of the autograd Function)."""
+    layout: int
+    num_pairs: int
+    dim: int
+    num_x: int
+    num_y: int
+    nmax_x: int = 0
+    nmax_y: int = 0
+    weights_x: int = _lib.RA_WEIGHTS_UNIFORM
+    weights_y: int = _lib.RA_WEIGHTS_UNIFORM
+    center: bool = True
+    sigma: float = 0.2
+    ptr_x: Optional[Tensor] = None
+    ptr_y: Optional[Tensor] = None
+    mask_x: Optional[Tensor] = None
+    mask_y: Optional[Tensor] = None
+    # which device-detected errors can occur (and must be checked, at the
+    # price of one synchronisation): user ptr offsets, SUM-normalised weights
+    check_errors: bool = False
+    weight_error_message: str = "weights must sum to a positive value per segment"
+
+    def desc(self, need_grad: bool, need_sigma_grad: bool) -> _lib.RaKdeDesc:
+        d = _lib.RaKdeDesc()
+        d.num_pairs = self.num_pairs
+        d.dim = self.dim
+        d.layout = self.layout
+        d.num_x = self.num_x
+        d.num_y = self.num_y
+        d.nmax_x = self.nmax_x
+        d.nmax_y = self.nmax_y
+        d.weights_x = self.weights_x
+        d.weights_y = self.weights_y
+        d.center = 1 if self.center else 0
+        d.need_grad = 1 if need_grad else 0
+        d.need_sigma_grad = 1 if need_sigma_grad else 0
+        d.reserved = 0
+        d.sigma = float(self.sigma)
+        return d
+
+
+def _f32(t: Optional[Tensor]) -> Optional[Tensor]:
+    if t is None:
+        return None
+    return t.detach().to(torch.float32).contiguous()
+
+
+def _inputs(x32, y32, wx32, wy32, spec: Spec) -> _lib.RaKdeInputs:
+    i = _lib.RaKdeInputs()
+    i.x = _lib.ptr(x32)
+    i.y = _lib.ptr(y32)
+    i.w_x = _lib.ptr(wx32)
+    i.w_y = _lib.ptr(wy32)
+    i.ptr_x = _lib.ptr(spec.ptr_x)
+    i.ptr_y = _lib.ptr(spec.ptr_y)
+    i.mask_x = _lib.ptr(spec.mask_x)
+    i.mask_y = _lib.ptr(spec.mask_y)
+    return i
+
+
+def _raise_data_error(code: int, spec: Spec) -> None:
+    if code == _lib.RA_OK:
+        return
+    if code == _lib.RA_ERR_PTR_START:
+        raise ValueError("ptr must start at 0")
+    if code == _lib.RA_ERR_PTR_END:
+        raise ValueError("ptr[-1] must equal number of nodes")
+    if code == _lib.RA_ERR_PTR_ORDER:
+        raise ValueError("ptr offsets must match node stacks")
+    if code == _lib.RA_ERR_WEIGHT_SUM:
+        raise ValueError(spec.weight_error_message)
+    _lib.check(code, "kde forward")
+
+
+class _State:
+    """What a backward needs from its forward: the fp32 inputs, the workspace
+    holding the per-point sums, and the original dtypes/shapes."""
+
+    def __init__(self, spec, need_sigma_grad, keep, meta):
+        self.spec = spec
+        self.need_sigma_grad = need_sigma_grad
+        self.keep = keep
+        self.meta = meta
+
+
+def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tensor],
+                 sigma_t: Optional[Tensor], spec: Spec, need_grad: bool):
+    """Run the fused forward; returns (K float64 [3P], state or None)."""
+    lib = _lib.load()
+    device = x.device
+    need_sigma_grad = need_grad and sigma_t is not None and sigma_t.requires_grad
+    x32, y32 = _f32(x), _f32(y)
+    wx32, wy32 = _f32(w_x), _f32(w_y)
+    desc = spec.desc(need_grad, need_sigma_grad)
+    inp = _inputs(x32, y32, wx32, wy32, spec)
+    nbytes = lib.ra_kde_workspace_bytes(ctypes.byref(desc))
+    if nbytes == 0:
+        raise RuntimeError("rapidalign_b200: invalid problem description")
+    ws = _lib.workspace(nbytes, device)
+    K = torch.empty(3 * spec.num_pairs, dtype=torch.float64, device=device)
+    stream = _lib.stream_handle(device)
+    with torch.cuda.device(device):
+        rc = lib.ra_kde_forward(ctypes.byref(desc), ctypes.byref(inp), K.data_ptr(),
+                                ws.data_ptr(), ws.numel(), stream)
+        _lib.check(rc, "kde forward")
+        if spec.check_errors:
+            _raise_data_error(lib.ra_kde_check(ws.data_ptr(), stream), spec)
+    state = None
+    if need_grad:
+        state = _State(spec, need_sigma_grad,
+                       (x32, y32, wx32, wy32, ws, spec.ptr_x, spec.ptr_y, spec.mask_x,
+                        spec.mask_y),
+                       (x.dtype, x.shape, y.dtype, y.shape,
+                        None if w_x is None else (w_x.dtype, w_x.shape),
+                        None if w_y is None else (w_y.dtype, w_y.shape),
+                        None if sigma_t is None else (sigma_t.dtype, sigma_t.shape)))
+    return K, state
+
+
+def backward_sums(state: _State, coef: Tensor, need) -> tuple:
+    """Gradients (x, y, w_x, w_y, sigma) for coefficients coef = dL/d(Kxx|Kyy|Kxy)
+    (float64 [3P]); `need` flags which of the five are wanted."""
+    lib = _lib.load()
+    spec = state.spec
+    x32, y32, wx32, wy32, ws = state.keep[:5]
+    device = x32.device
+    P = spec.num_pairs
+    coef = coef.to(device=device, dtype=torch.float64).contiguous()
+    nx = x32.shape[0] if x32.dim() == 2 else x32.shape[0] * x32.shape[1]
+    ny = y32.shape[0] if y32.dim() == 2 else y32.shape[0] * y32.shape[1]
+    gx = torch.empty_like(x32) if need[0] else None
+    gy = torch.empty_like(y32) if need[1] else None
+    gwx = (torch.empty(nx, dtype=torch.float64, device=device)
+           if (need[2] and wx32 is not None) else None)
+    gwy = (torch.empty(ny, dtype=torch.float64, device=device)
+           if (need[3] and wy32 is not None) else None)
+    gsig = (torch.empty(P, dtype=torch.float64, device=device)
+            if (need[4] and state.need_sigma_grad) else None)
+    grads = _lib.RaKdeGrads()
+    grads.grad_x = _lib.ptr(gx)
+    grads.grad_y = _lib.ptr(gy)
+    grads.grad_wx = _lib.ptr(gwx)
+    grads.grad_wy = _lib.ptr(gwy)
+    grads.grad_sigma = _lib.ptr(gsig)
+    desc = spec.desc(True, state.need_sigma_grad)
+    inp = _inputs(x32, y32, wx32, wy32, spec)
+    with torch.cuda.device(device):
+        rc = lib.ra_kde_backward(ctypes.byref(desc), ctypes.byref(inp), coef.data_ptr(),
+                                 ctypes.byref(grads), ws.data_ptr(), ws.numel(),
+                                 _lib.stream_handle(device))
+    _lib.check(rc, "kde backward")
+    xdt, xsh, ydt, ysh, wxm, wym, sm = state.meta
+    out_x = gx.to(xdt).reshape(xsh) if gx is not None else None
+    out_y = gy.to(ydt).reshape(ysh) if gy is not None else None
+    out_wx = gwx.to(wxm[0]).reshape(wxm[1]) if gwx is not None else None
+    out_wy = gwy.to(wym[0]).reshape(wym[1]) if gwy is not None else None
+    out_s = gsig.sum().to(sm[0]).reshape(sm[1]) if gsig is not None else None
+    return out_x, out_y, out_wx, out_wy, out_s
+
+
+def needs_grad(*tensors) -> bool:
+    return torch.is_grad_enabled() and any(
+        t is not None and isinstance(t, Tensor) and t.requires_grad for t in tensors)
+
+
+class KDESums(torch.autograd.Function):
+    """(x, y, w_x, w_y, sigma) -> (Kxx, Kyy, Kxy), all float64 of shape (P,)."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tensor],
+                sigma_t: Optional[Tensor], spec: Spec, need_grad: bool):
+        K, state = forward_sums(x, y, w_x, w_y, sigma_t, spec, need_grad)
+        ctx.state = state
+        P = spec.num_pairs
+        return K[:P], K[P:2 * P], K[2 * P:]
+
+    @staticmethod
+    def backward(ctx, gKxx: Optional[Tensor], gKyy: Optional[Tensor], gKxy: Optional[Tensor]):
+        state = ctx.state
+        if state is None:
+            return None, None, None, None, None, None, None
+        P = state.spec.num_pairs
+        device = state.keep[0].device
+
+        def g_or_zero(g):
+            if g is None:
+                return torch.zeros(P, dtype=torch.float64, device=device)
+            return g.to(torch.float64)
+
+        coef = torch.cat([g_or_zero(gKxx), g_or_zero(gKyy), g_or_zero(gKxy)])
+        grads = backward_sums(state, coef, ctx.needs_input_grad[:5])
+        return grads + (None, None)
+
+
+def kde_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tensor],
+             sigma_t: Optional[Tensor], spec: Spec) -> Tuple[Tensor, Tensor, Tensor]:
+    need = needs_grad(x, y, w_x, w_y, sigma_t)
+    return KDESums.apply(x, y, w_x, w_y, sigma_t, spec, need)

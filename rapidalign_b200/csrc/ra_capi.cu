@@ -1,0 +1,680 @@
+// ra_capi.cu -- host side of the C ABI declared in include/rapidalign_b200.h.
+// Lays out the caller's workspace, validates arguments and enqueues the
+// kernel pipeline on the caller's stream:
+//   prep (per pair) -> plan count -> plan scan -> plan emit -> tiles ->
+//   finalize (per pair)                               [forward]
+//   epilogue (per pair and side)                       [backward]
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/rapidalign_b200.h"
+#include "ra_common.cuh"
+#include "ra_epilogue.cuh"
+#include "ra_plan.cuh"
+#include "ra_prep.cuh"
+#include "ra_tiles3.cuh"
+#include "ra_tilesg.cuh"
+
+namespace {
+
+using namespace ra;
+
+std::atomic<unsigned long long> g_launches{0};
+
+constexpr int kPrepThreads = 256;
+constexpr int kEpiThreads = 256;
+
+size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+int generic_dp(int D) {
+  int r = 4;
+  while (r < D) r <<= 1;
+  return r;
+}
+
+struct Layout {
+  bool packed3;
+  int DP;
+  int acc_stride;
+  int64_t max_items;
+  size_t hdr, seg, meta, cnt, item_off, boff, items, itemK, itemS, Kws, Sws, coef, Ktmp;
+  size_t Px, Py, Q[8], Gx, Gy, Ax, Ay, accX, accY;
+  size_t total;
+};
+
+// header block: int err @0, unsigned ticket @4, int has_state @8, int64 n_items @16
+constexpr size_t kHdrErr = 0, kHdrTicket = 4, kHdrState = 8, kHdrNItems = 16;
+
+bool desc_ok(const ra_kde_desc *d) {
+  if (d == nullptr) return false;
+  if (d->num_pairs < 0 || d->dim < 1 || d->dim > 256) return false;
+  if (d->layout != RA_LAYOUT_RAGGED && d->layout != RA_LAYOUT_DENSE) return false;
+  if (d->num_x < 0 || d->num_y < 0) return false;
+  if (d->layout == RA_LAYOUT_DENSE) {
+    if (d->nmax_x < 0 || d->nmax_y < 0) return false;
+    if (d->num_x != d->num_pairs * d->nmax_x || d->num_y != d->num_pairs * d->nmax_y)
+      return false;
+  }
+  if (d->weights_x < 0 || d->weights_x > 3 || d->weights_y < 0 || d->weights_y > 3) return false;
+  if (d->num_x > ((int64_t)1 << 40) || d->num_y > ((int64_t)1 << 40)) return false;
+  if (d->num_pairs > ((int64_t)1 << 30)) return false;
+  return true;
+}
+
+Layout make_layout(const ra_kde_desc *d) {
+  Layout L;
+  std::memset(&L, 0, sizeof(L));
+  const int64_t P = d->num_pairs, NX = d->num_x, NY = d->num_y;
+  L.packed3 = d->dim <= 3;
+  L.DP = L.packed3 ? 3 : generic_dp(d->dim);
+  L.acc_stride = L.packed3 ? 8 : 2 + 2 * L.DP;
+  // host bound on the number of items
+  int64_t tx, ty;  // sum over pairs of row tiles
+  const int64_t rows = L.packed3 ? kTile : kGenRows;
+  if (d->layout == RA_LAYOUT_DENSE) {
+    tx = P * ceil_div(d->nmax_x, rows);
+    ty = P * ceil_div(d->nmax_y, rows);
+  } else {
+    tx = ceil_div(NX, rows) + P;
+    ty = ceil_div(NY, rows) + P;
+  }
+  L.max_items = L.packed3 ? (int64_t)kSplitMax * (2 * tx + ty) : 2 * tx + 2 * ty;
+  if (L.max_items < 1) L.max_items = 1;
+  const bool grad = d->need_grad != 0;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o = a256(o + bytes);
+    return at;
+  };
+  const size_t P1 = (size_t)(P > 0 ? P : 1);
+  L.hdr = take(256);
+  L.seg = take(sizeof(Seg) * P1);
+  L.meta = take(sizeof(double) * P1 * meta_stride(L.DP));
+  L.cnt = take(sizeof(int64_t) * P1);
+  L.item_off = take(sizeof(int64_t) * (P1 + 1));
+  L.boff = take(sizeof(int64_t) * 4 * P1);
+  L.items = take(sizeof(Item) * (size_t)L.max_items);
+  L.itemK = take(sizeof(double) * (size_t)L.max_items);
+  L.itemS = take(sizeof(double) * (size_t)L.max_items);
+  L.Kws = take(sizeof(double) * 3 * P1);
+  L.Sws = take(sizeof(double) * 3 * P1);
+  L.coef = take(sizeof(double) * 3 * P1);
+  L.Ktmp = take(sizeof(double) * 3 * P1);
+  const size_t nx = (size_t)(NX > 0 ? NX : 1), ny = (size_t)(NY > 0 ? NY : 1);
+  if (L.packed3) {
+    L.Px = take(16 * nx);
+    L.Py = take(16 * ny);
+    const int nq = grad ? 4 : 2;
+    for (int i = 0; i < 4; ++i) {
+      L.Q[i] = i < nq ? take(16 * nx) : 0;
+      L.Q[4 + i] = i < nq ? take(16 * ny) : 0;
+    }
+  } else {
+    L.Gx = take(sizeof(float) * nx * L.DP);
+    L.Gy = take(sizeof(float) * ny * L.DP);
+    L.Ax = take(sizeof(float) * nx);
+    L.Ay = take(sizeof(float) * ny);
+  }
+  if (grad) {
+    L.accX = take(sizeof(float) * nx * L.acc_stride);
+    L.accY = take(sizeof(float) * ny * L.acc_stride);
+  }
+  L.total = o;
+  return L;
+}
+
+template <typename T>
+T *at(void *ws, size_t off) {
+  return reinterpret_cast<T *>(static_cast<char *>(ws) + off);
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? RA_OK : RA_ERR_CUDA; }
+
+float scale_for(double sigma) {
+  // k = exp(-r^2 / (2 sigma^2)) = 2^(-(c r)^2) with c^2 = log2(e) / (2 sigma^2)
+  return (float)std::sqrt(1.4426950408889634 / (2.0 * sigma * sigma));
+}
+
+int check_common(const ra_kde_desc *d, void *ws, size_t ws_bytes, size_t need) {
+  if (!desc_ok(d)) return RA_ERR_INVALID_ARGUMENT;
+  if (!(d->sigma > 0.0) || !std::isfinite(d->sigma)) return RA_ERR_SIGMA;
+  if (ws == nullptr || ((uintptr_t)ws & 255) != 0 || ws_bytes < need) return RA_ERR_WORKSPACE;
+  return RA_OK;
+}
+
+int launch_tiles3(int mode, const Tiles3Args &T, cudaStream_t st) {
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t e;
+  if (mode == 0)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<0>, 128, 0);
+  else if (mode == 1)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<1>, 128, 0);
+  else
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<2>, 128, 0);
+  if (e != cudaSuccess) return RA_ERR_CUDA;
+  if (per_sm < 1) per_sm = 1;
+  const int grid = sms * per_sm;
+  if (mode == 0)
+    tiles3_kernel<0><<<grid, 128, 0, st>>>(T);
+  else if (mode == 1)
+    tiles3_kernel<1><<<grid, 128, 0, st>>>(T);
+  else
+    tiles3_kernel<2><<<grid, 128, 0, st>>>(T);
+  ++g_launches;
+  return cuda_status(cudaGetLastError());
+}
+
+template <int DP>
+void launch_tilesg_dp(int mode, int64_t grid, const TilesGArgs &T, cudaStream_t st) {
+  if (mode == 0)
+    tilesg_kernel<DP, 0><<<(unsigned)grid, kGenRows, 0, st>>>(T);
+  else if (mode == 1)
+    tilesg_kernel<DP, 1><<<(unsigned)grid, kGenRows, 0, st>>>(T);
+  else
+    tilesg_kernel<DP, 2><<<(unsigned)grid, kGenRows, 0, st>>>(T);
+}
+
+int launch_tilesg(int DP, int mode, int64_t grid, const TilesGArgs &T, cudaStream_t st) {
+  switch (DP) {
+    case 4: launch_tilesg_dp<4>(mode, grid, T, st); break;
+    case 8: launch_tilesg_dp<8>(mode, grid, T, st); break;
+    case 16: launch_tilesg_dp<16>(mode, grid, T, st); break;
+    case 32: launch_tilesg_dp<32>(mode, grid, T, st); break;
+    case 64: launch_tilesg_dp<64>(mode, grid, T, st); break;
+    case 128: launch_tilesg_dp<128>(mode, grid, T, st); break;
+    case 256: launch_tilesg_dp<256>(mode, grid, T, st); break;
+    default: return RA_ERR_INVALID_ARGUMENT;
+  }
+  ++g_launches;
+  return cuda_status(cudaGetLastError());
+}
+
+int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, double *Kyy,
+                 double *Kxy, void *ws, size_t ws_bytes, cudaStream_t st,
+                 cudaEvent_t ev0 = nullptr, cudaEvent_t ev1 = nullptr) {
+  const Layout L = make_layout(d);
+  int rc = check_common(d, ws, ws_bytes, L.total);
+  if (rc) return rc;
+  if (in == nullptr || Kxx == nullptr || Kyy == nullptr || Kxy == nullptr)
+    return RA_ERR_INVALID_ARGUMENT;
+  const int64_t P = d->num_pairs;
+  if ((d->num_x > 0 && in->x == nullptr) || (d->num_y > 0 && in->y == nullptr))
+    return RA_ERR_INVALID_ARGUMENT;
+  if (d->layout == RA_LAYOUT_RAGGED && P > 0 && (in->ptr_x == nullptr || in->ptr_y == nullptr))
+    return RA_ERR_INVALID_ARGUMENT;
+  // header: error word, ticket, state flag, item count
+  if (cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return RA_ERR_CUDA;
+  if (P == 0) return RA_OK;
+  const bool grad = d->need_grad != 0;
+  const int mode = !grad ? 0 : (d->need_sigma_grad ? 2 : 1);
+  if (grad) {
+    if (cudaMemsetAsync(at<char>(ws, L.accX), 0,
+                        sizeof(float) * (size_t)(d->num_x > 0 ? d->num_x : 1) * L.acc_stride,
+                        st) != cudaSuccess)
+      return RA_ERR_CUDA;
+    if (cudaMemsetAsync(at<char>(ws, L.accY), 0,
+                        sizeof(float) * (size_t)(d->num_y > 0 ? d->num_y : 1) * L.acc_stride,
+                        st) != cudaSuccess)
+      return RA_ERR_CUDA;
+  }
+  const float scale = scale_for(d->sigma);
+
+  // ---- prep ----
+  PrepArgs pa;
+  std::memset(&pa, 0, sizeof(pa));
+  pa.P = P;
+  pa.D = d->dim;
+  pa.DP = L.DP;
+  pa.layout = d->layout;
+  pa.wmode_x = d->weights_x;
+  pa.wmode_y = d->weights_y;
+  pa.center = d->center;
+  pa.packed3 = L.packed3 ? 1 : 0;
+  pa.num_x = d->num_x;
+  pa.num_y = d->num_y;
+  pa.nmax_x = d->nmax_x;
+  pa.nmax_y = d->nmax_y;
+  pa.scale = scale;
+  pa.x = in->x;
+  pa.y = in->y;
+  pa.w_x = in->w_x;
+  pa.w_y = in->w_y;
+  pa.ptr_x = in->ptr_x;
+  pa.ptr_y = in->ptr_y;
+  pa.mask_x = d->layout == RA_LAYOUT_DENSE ? in->mask_x : nullptr;
+  pa.mask_y = d->layout == RA_LAYOUT_DENSE ? in->mask_y : nullptr;
+  pa.seg = at<Seg>(ws, L.seg);
+  pa.meta = at<double>(ws, L.meta);
+  pa.err = at<int>(ws, L.hdr + kHdrErr);
+  if (L.packed3) {
+    pa.Px = at<float4>(ws, L.Px);
+    pa.Py = at<float4>(ws, L.Py);
+    pa.Qx0 = at<float4>(ws, L.Q[0]);
+    pa.Qx1 = at<float4>(ws, L.Q[1]);
+    pa.Qy0 = at<float4>(ws, L.Q[4]);
+    pa.Qy1 = at<float4>(ws, L.Q[5]);
+    if (grad) {
+      pa.Qx2 = at<float4>(ws, L.Q[2]);
+      pa.Qx3 = at<float4>(ws, L.Q[3]);
+      pa.Qy2 = at<float4>(ws, L.Q[6]);
+      pa.Qy3 = at<float4>(ws, L.Q[7]);
+    }
+  } else {
+    pa.Gx = at<float>(ws, L.Gx);
+    pa.Gy = at<float>(ws, L.Gy);
+    pa.Ax = at<float>(ws, L.Ax);
+    pa.Ay = at<float>(ws, L.Ay);
+  }
+  if (!L.packed3 || grad) {
+    // the four-array column layout is only needed with gradients; without,
+    // the prep still writes Q0/Q1 (guarded by Q0 != nullptr)
+  }
+  const size_t prep_smem = sizeof(double) * (3 * kPrepThreads + 257);
+  prep_kernel<kPrepThreads><<<(unsigned)P, kPrepThreads, prep_smem, st>>>(pa);
+  ++g_launches;
+  if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
+
+  // ---- plan ----
+  PlanArgs pl;
+  pl.P = P;
+  pl.generic = L.packed3 ? 0 : 1;
+  pl.seg = at<Seg>(ws, L.seg);
+  pl.cnt = at<int64_t>(ws, L.cnt);
+  pl.boff = at<int64_t>(ws, L.boff);
+  pl.item_off = at<int64_t>(ws, L.item_off);
+  pl.n_items = at<int64_t>(ws, L.hdr + kHdrNItems);
+  pl.items = at<Item>(ws, L.items);
+  pl.max_items = L.max_items;
+  plan_count_kernel<<<(unsigned)ceil_div(P, 256), 256, 0, st>>>(pl);
+  plan_scan_kernel<<<1, 1024, 0, st>>>(pl);
+  plan_emit_kernel<<<(unsigned)P, 256, 0, st>>>(pl);
+  g_launches += 3;
+  if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
+
+  // ---- tiles ----
+  if (ev0 != nullptr && cudaEventRecord(ev0, st) != cudaSuccess) return RA_ERR_CUDA;
+  if (L.packed3) {
+    Tiles3Args T;
+    T.items = at<Item>(ws, L.items);
+    T.n_items = at<int64_t>(ws, L.hdr + kHdrNItems);
+    T.ticket = at<unsigned>(ws, L.hdr + kHdrTicket);
+    T.seg = at<Seg>(ws, L.seg);
+    T.Px = at<float4>(ws, L.Px);
+    T.Py = at<float4>(ws, L.Py);
+    T.Qx0 = at<ulonglong2>(ws, L.Q[0]);
+    T.Qx1 = at<ulonglong2>(ws, L.Q[1]);
+    T.Qy0 = at<ulonglong2>(ws, L.Q[4]);
+    T.Qy1 = at<ulonglong2>(ws, L.Q[5]);
+    T.Qx2 = grad ? at<ulonglong2>(ws, L.Q[2]) : nullptr;
+    T.Qx3 = grad ? at<ulonglong2>(ws, L.Q[3]) : nullptr;
+    T.Qy2 = grad ? at<ulonglong2>(ws, L.Q[6]) : nullptr;
+    T.Qy3 = grad ? at<ulonglong2>(ws, L.Q[7]) : nullptr;
+    T.accX = grad ? at<float>(ws, L.accX) : nullptr;
+    T.accY = grad ? at<float>(ws, L.accY) : nullptr;
+    T.itemK = at<double>(ws, L.itemK);
+    T.itemS = at<double>(ws, L.itemS);
+    rc = launch_tiles3(mode, T, st);
+    if (rc) return rc;
+  } else {
+    TilesGArgs T;
+    T.items = at<Item>(ws, L.items);
+    T.n_items = at<int64_t>(ws, L.hdr + kHdrNItems);
+    T.seg = at<Seg>(ws, L.seg);
+    T.Gx = at<float>(ws, L.Gx);
+    T.Gy = at<float>(ws, L.Gy);
+    T.Ax = at<float>(ws, L.Ax);
+    T.Ay = at<float>(ws, L.Ay);
+    T.accX = grad ? at<float>(ws, L.accX) : nullptr;
+    T.accY = grad ? at<float>(ws, L.accY) : nullptr;
+    T.itemK = at<double>(ws, L.itemK);
+    T.itemS = at<double>(ws, L.itemS);
+    T.need_rows = grad ? 1 : 0;
+    rc = launch_tilesg(L.DP, mode, L.max_items, T, st);
+    if (rc) return rc;
+  }
+
+  if (ev1 != nullptr && cudaEventRecord(ev1, st) != cudaSuccess) return RA_ERR_CUDA;
+
+  // ---- finalize ----
+  FinalizeArgs fa;
+  fa.P = P;
+  fa.item_off = at<int64_t>(ws, L.item_off);
+  fa.boff = at<int64_t>(ws, L.boff);
+  fa.itemK = at<double>(ws, L.itemK);
+  fa.itemS = at<double>(ws, L.itemS);
+  fa.K_ws = at<double>(ws, L.Kws);
+  fa.S_ws = at<double>(ws, L.Sws);
+  // finalize writes Kxx | Kyy | Kxy contiguously into K_ws; copy out below
+  fa.K_out = at<double>(ws, L.Ktmp);
+  finalize_kernel<<<(unsigned)ceil_div(P * 32, 256), 256, 0, st>>>(fa);
+  ++g_launches;
+  if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
+  const size_t pb = sizeof(double) * (size_t)P;
+  double *Kt = at<double>(ws, L.Ktmp);
+  if ((Kxx != Kt && cudaMemcpyAsync(Kxx, Kt, pb, cudaMemcpyDeviceToDevice, st)) ||
+      (Kyy != Kt + P && cudaMemcpyAsync(Kyy, Kt + P, pb, cudaMemcpyDeviceToDevice, st)) ||
+      (Kxy != Kt + 2 * P && cudaMemcpyAsync(Kxy, Kt + 2 * P, pb, cudaMemcpyDeviceToDevice, st)))
+    return RA_ERR_CUDA;
+  if (grad) {
+    const int one = 1;
+    if (cudaMemcpyAsync(at<char>(ws, L.hdr + kHdrState), &one, sizeof(int),
+                        cudaMemcpyHostToDevice, st) != cudaSuccess)
+      return RA_ERR_CUDA;
+  }
+  return RA_OK;
+}
+
+int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *coef,
+                  const ra_kde_grads *gr, void *ws, size_t ws_bytes, cudaStream_t st) {
+  const Layout L = make_layout(d);
+  int rc = check_common(d, ws, ws_bytes, L.total);
+  if (rc) return rc;
+  if (in == nullptr || gr == nullptr || coef == nullptr) return RA_ERR_INVALID_ARGUMENT;
+  if (!d->need_grad) return RA_ERR_STATE;
+  if (gr->grad_sigma != nullptr && !d->need_sigma_grad) return RA_ERR_STATE;
+  const int64_t P = d->num_pairs;
+  if (P == 0) return RA_OK;
+  EpilogueArgs ea;
+  std::memset(&ea, 0, sizeof(ea));
+  ea.P = P;
+  ea.D = d->dim;
+  ea.DP = L.DP;
+  ea.packed3 = L.packed3 ? 1 : 0;
+  ea.center = d->center;
+  ea.wmode_x = d->weights_x;
+  ea.wmode_y = d->weights_y;
+  ea.scale = (double)scale_for(d->sigma);
+  ea.sigma = d->sigma;
+  ea.seg = at<Seg>(ws, L.seg);
+  ea.meta = at<double>(ws, L.meta);
+  ea.coef = coef;
+  ea.S_ws = at<double>(ws, L.Sws);
+  ea.x = in->x;
+  ea.y = in->y;
+  ea.mask_x = d->layout == RA_LAYOUT_DENSE ? in->mask_x : nullptr;
+  ea.mask_y = d->layout == RA_LAYOUT_DENSE ? in->mask_y : nullptr;
+  if (L.packed3) {
+    ea.Px = at<float4>(ws, L.Px);
+    ea.Py = at<float4>(ws, L.Py);
+  } else {
+    ea.Gx = at<float>(ws, L.Gx);
+    ea.Gy = at<float>(ws, L.Gy);
+    ea.Ax = at<float>(ws, L.Ax);
+    ea.Ay = at<float>(ws, L.Ay);
+  }
+  ea.accX = at<float>(ws, L.accX);
+  ea.accY = at<float>(ws, L.accY);
+  ea.acc_stride = L.acc_stride;
+  ea.grad_x = gr->grad_x;
+  ea.grad_y = gr->grad_y;
+  ea.grad_wx = gr->grad_wx;
+  ea.grad_wy = gr->grad_wy;
+  ea.grad_sigma = gr->grad_sigma;
+  if (L.packed3)
+    epilogue3_kernel<kEpiThreads><<<(unsigned)(2 * P), kEpiThreads, 0, st>>>(ea);
+  else
+    epilogueg_kernel<kEpiThreads><<<(unsigned)(2 * P), kEpiThreads, 0, st>>>(ea);
+  ++g_launches;
+  return cuda_status(cudaGetLastError());
+}
+
+// coef = (g, g, -2 g) for the legacy MMD backward
+__global__ void mmd_coef_kernel(int64_t P, const double *g, double *coef) {
+  const int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (p >= P) return;
+  const double v = g[p];
+  coef[p] = v;
+  coef[P + p] = v;
+  coef[2 * P + p] = -2.0 * v;
+}
+
+ra_kde_desc legacy_desc(int layout, int64_t P, int64_t NX, int64_t NY, int64_t nmx, int64_t nmy,
+                        int32_t D, double sigma, int grad) {
+  ra_kde_desc d;
+  std::memset(&d, 0, sizeof(d));
+  d.num_pairs = P;
+  d.dim = D;
+  d.layout = layout;
+  d.num_x = NX;
+  d.num_y = NY;
+  d.nmax_x = nmx;
+  d.nmax_y = nmy;
+  d.weights_x = RA_WEIGHTS_RAW;
+  d.weights_y = RA_WEIGHTS_RAW;
+  d.center = 0;
+  d.need_grad = grad;
+  d.need_sigma_grad = grad;
+  d.sigma = sigma;
+  return d;
+}
+
+// ---- FP32 peak probe -------------------------------------------------------
+__global__ void fp32_probe_kernel(float *out, int iters, float seed) {
+  f2_t acc[8];
+  for (int i = 0; i < 8; ++i) acc[i] = pk(seed + threadIdx.x * 1e-3f + i, seed - i);
+  const f2_t m = pk(0.9999f, 0.9999f), c = pk(1e-4f, 1e-4f);
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fma2(acc[i], m, c);
+    }
+  }
+  float s = 0.f;
+  for (int i = 0; i < 8; ++i) s += lo_of(acc[i]) + hi_of(acc[i]);
+  out[blockIdx.x * blockDim.x + threadIdx.x] = s;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *ra_status_string(int status) {
+  switch (status) {
+    case RA_OK: return "ok";
+    case RA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case RA_ERR_SIGMA: return "sigma must be positive";
+    case RA_ERR_WORKSPACE: return "workspace too small or not 256-byte aligned";
+    case RA_ERR_CUDA: return "CUDA error";
+    case RA_ERR_PTR_START: return "ptr must start at 0";
+    case RA_ERR_PTR_END: return "ptr[-1] must equal number of nodes";
+    case RA_ERR_PTR_ORDER: return "ptr offsets must be non-decreasing";
+    case RA_ERR_WEIGHT_SUM: return "weights must sum to a positive value per segment";
+    case RA_ERR_STATE: return "backward needs a forward run with need_grad (and need_sigma_grad)";
+    default: return "unknown status";
+  }
+}
+
+size_t ra_kde_workspace_bytes(const ra_kde_desc *desc) {
+  if (!desc_ok(desc)) return 0;
+  return make_layout(desc).total;
+}
+
+int ra_kde_forward(const ra_kde_desc *desc, const ra_kde_inputs *in, double *K, void *workspace,
+                   size_t workspace_bytes, ra_stream_t stream) {
+  if (!desc_ok(desc) || K == nullptr) return RA_ERR_INVALID_ARGUMENT;
+  const int64_t P = desc->num_pairs;
+  return forward_impl(desc, in, K, K + P, K + 2 * P, workspace, workspace_bytes,
+                      (cudaStream_t)stream);
+}
+
+int ra_kde_backward(const ra_kde_desc *desc, const ra_kde_inputs *in, const double *coef,
+                    const ra_kde_grads *grads, void *workspace, size_t workspace_bytes,
+                    ra_stream_t stream) {
+  return backward_impl(desc, in, coef, grads, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int ra_kde_forward_profiled(const ra_kde_desc *desc, const ra_kde_inputs *in, double *K,
+                            void *workspace, size_t workspace_bytes, ra_stream_t stream,
+                            float *tiles_ms) {
+  if (!desc_ok(desc) || K == nullptr || tiles_ms == nullptr) return RA_ERR_INVALID_ARGUMENT;
+  cudaEvent_t e0, e1;
+  if (cudaEventCreate(&e0) != cudaSuccess) return RA_ERR_CUDA;
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return RA_ERR_CUDA;
+  }
+  const int64_t P = desc->num_pairs;
+  int rc = forward_impl(desc, in, K, K + P, K + 2 * P, workspace, workspace_bytes,
+                        (cudaStream_t)stream, e0, e1);
+  *tiles_ms = 0.f;
+  if (rc == RA_OK && P > 0) {
+    if (cudaEventSynchronize(e1) != cudaSuccess || cudaEventElapsedTime(tiles_ms, e0, e1))
+      rc = RA_ERR_CUDA;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  return rc;
+}
+
+int ra_kde_check(const void *workspace, ra_stream_t stream) {
+  if (workspace == nullptr) return RA_ERR_INVALID_ARGUMENT;
+  int err = 0;
+  if (cudaMemcpyAsync(&err, static_cast<const char *>(workspace) + kHdrErr, sizeof(int),
+                      cudaMemcpyDeviceToHost, (cudaStream_t)stream) != cudaSuccess)
+    return RA_ERR_CUDA;
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return RA_ERR_CUDA;
+  if (err & kErrPtrStart) return RA_ERR_PTR_START;
+  if (err & kErrPtrEnd) return RA_ERR_PTR_END;
+  if (err & kErrPtrOrder) return RA_ERR_PTR_ORDER;
+  if (err & kErrWeightSum) return RA_ERR_WEIGHT_SUM;
+  return RA_OK;
+}
+
+size_t ra_kde_mmd_forward_workspace_bytes(int64_t B, int64_t Nx, int64_t Ny, int32_t D) {
+  ra_kde_desc d = legacy_desc(RA_LAYOUT_DENSE, B, B * Nx, B * Ny, Nx, Ny, D, 1.0, 0);
+  return ra_kde_workspace_bytes(&d);
+}
+
+int ra_kde_mmd_forward(const float *x, const float *y, const float *w_x, const float *w_y,
+                       const uint8_t *mask_x, const uint8_t *mask_y, int64_t B, int64_t Nx,
+                       int64_t Ny, int32_t D, double sigma, double *Kxx, double *Kyy,
+                       double *Kxy, void *workspace, size_t workspace_bytes,
+                       ra_stream_t stream) {
+  if (B < 0 || Nx < 0 || Ny < 0) return RA_ERR_INVALID_ARGUMENT;
+  if (B > 0 && (w_x == nullptr || w_y == nullptr || mask_x == nullptr || mask_y == nullptr))
+    return RA_ERR_INVALID_ARGUMENT;
+  ra_kde_desc d = legacy_desc(RA_LAYOUT_DENSE, B, B * Nx, B * Ny, Nx, Ny, D, sigma, 0);
+  ra_kde_inputs in;
+  std::memset(&in, 0, sizeof(in));
+  in.x = x;
+  in.y = y;
+  in.w_x = w_x;
+  in.w_y = w_y;
+  in.mask_x = mask_x;
+  in.mask_y = mask_y;
+  return forward_impl(&d, &in, Kxx, Kyy, Kxy, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+size_t ra_kde_mmd_forward_segmented_workspace_bytes(int64_t P, int64_t NX, int64_t NY,
+                                                    int32_t D) {
+  ra_kde_desc d = legacy_desc(RA_LAYOUT_RAGGED, P, NX, NY, 0, 0, D, 1.0, 0);
+  return ra_kde_workspace_bytes(&d);
+}
+
+int ra_kde_mmd_forward_segmented(const float *x, const float *y, const float *w_x,
+                                 const float *w_y, const int64_t *ptr_x, const int64_t *ptr_y,
+                                 int64_t P, int64_t NX, int64_t NY, int32_t D, double sigma,
+                                 double *Kxx, double *Kyy, double *Kxy, void *workspace,
+                                 size_t workspace_bytes, ra_stream_t stream) {
+  if ((NX > 0 && w_x == nullptr) || (NY > 0 && w_y == nullptr)) return RA_ERR_INVALID_ARGUMENT;
+  ra_kde_desc d = legacy_desc(RA_LAYOUT_RAGGED, P, NX, NY, 0, 0, D, sigma, 0);
+  ra_kde_inputs in;
+  std::memset(&in, 0, sizeof(in));
+  in.x = x;
+  in.y = y;
+  in.w_x = w_x;
+  in.w_y = w_y;
+  in.ptr_x = ptr_x;
+  in.ptr_y = ptr_y;
+  return forward_impl(&d, &in, Kxx, Kyy, Kxy, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+size_t ra_kde_mmd_backward_segmented_workspace_bytes(int64_t P, int64_t NX, int64_t NY,
+                                                     int32_t D) {
+  ra_kde_desc d = legacy_desc(RA_LAYOUT_RAGGED, P, NX, NY, 0, 0, D, 1.0, 1);
+  return ra_kde_workspace_bytes(&d);
+}
+
+int ra_kde_mmd_backward_segmented(const float *x, const float *y, const float *w_x,
+                                  const float *w_y, const int64_t *ptr_x, const int64_t *ptr_y,
+                                  int64_t P, int64_t NX, int64_t NY, int32_t D,
+                                  const double *grad_loss, double sigma, float *grad_x,
+                                  float *grad_y, double *grad_wx, double *grad_wy,
+                                  double *grad_sigma_pairs, void *workspace,
+                                  size_t workspace_bytes, ra_stream_t stream) {
+  if ((NX > 0 && w_x == nullptr) || (NY > 0 && w_y == nullptr)) return RA_ERR_INVALID_ARGUMENT;
+  if (P > 0 && grad_loss == nullptr) return RA_ERR_INVALID_ARGUMENT;
+  ra_kde_desc d = legacy_desc(RA_LAYOUT_RAGGED, P, NX, NY, 0, 0, D, sigma, 1);
+  const Layout L = make_layout(&d);
+  int rc = check_common(&d, workspace, workspace_bytes, L.total);
+  if (rc) return rc;
+  ra_kde_inputs in;
+  std::memset(&in, 0, sizeof(in));
+  in.x = x;
+  in.y = y;
+  in.w_x = w_x;
+  in.w_y = w_y;
+  in.ptr_x = ptr_x;
+  in.ptr_y = ptr_y;
+  cudaStream_t st = (cudaStream_t)stream;
+  double *Kt = at<double>(workspace, L.Ktmp);
+  // the forward leaves K in Ktmp (no copy: the destinations are Ktmp itself)
+  rc = forward_impl(&d, &in, Kt, Kt + P, Kt + 2 * P, workspace, workspace_bytes, st);
+  if (rc || P == 0) return rc;
+  double *coef = at<double>(workspace, L.coef);
+  mmd_coef_kernel<<<(unsigned)ceil_div(P, 256), 256, 0, st>>>(P, grad_loss, coef);
+  ++g_launches;
+  if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
+  ra_kde_grads g;
+  g.grad_x = grad_x;
+  g.grad_y = grad_y;
+  g.grad_wx = grad_wx;
+  g.grad_wy = grad_wy;
+  g.grad_sigma = grad_sigma_pairs;
+  return backward_impl(&d, &in, coef, &g, workspace, workspace_bytes, st);
+}
+
+unsigned long long ra_kernel_launch_count(void) { return g_launches.load(); }
+
+int ra_probe_fp32_peak(float *scratch, int64_t scratch_floats, int iters, double *ops_per_s,
+                       ra_stream_t stream) {
+  if (scratch == nullptr || ops_per_s == nullptr || iters <= 0) return RA_ERR_INVALID_ARGUMENT;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int threads = 256, blocks = sms * 8;
+  if (scratch_floats < (int64_t)threads * blocks) return RA_ERR_WORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaEvent_t e0, e1;
+  if (cudaEventCreate(&e0) != cudaSuccess) return RA_ERR_CUDA;
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return RA_ERR_CUDA;
+  }
+  fp32_probe_kernel<<<blocks, threads, 0, st>>>(scratch, iters / 4 + 1, 1.0f);  // warm-up
+  cudaEventRecord(e0, st);
+  fp32_probe_kernel<<<blocks, threads, 0, st>>>(scratch, iters, 1.0f);
+  cudaEventRecord(e1, st);
+  g_launches += 2;
+  int rc = RA_OK;
+  if (cudaEventSynchronize(e1) != cudaSuccess) rc = RA_ERR_CUDA;
+  float ms = 0.f;
+  if (!rc && cudaEventElapsedTime(&ms, e0, e1) != cudaSuccess) rc = RA_ERR_CUDA;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc) return rc;
+  // each fma2 = 2 FP32 lane operations
+  const double ops = (double)blocks * threads * iters * 16.0 * 8.0 * 2.0;
+  *ops_per_s = ops / (ms * 1e-3);
+  return RA_OK;
+}
+
+}  // extern "C"

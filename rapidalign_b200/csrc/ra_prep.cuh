@@ -1,0 +1,251 @@
+// ra_prep.cuh -- per-pair preparation: segment bounds, weight normalisation,
+// weighted centroids and packing of the points into the layouts the tile
+// kernels read.  One CTA per pair.
+//
+// Semantics follow rapidalign/kde.py:
+//   ptr checks            kde.py:124-156 (plus a monotonicity check)
+//   weight normalisation  kde.py:20-27 (single), 169-199 (ragged),
+//                         115-121 (dense, clamped), 183-188 (uniform)
+//   centering             kde.py:77-81, 202-208, 246-253
+// Distances are translation invariant, so without centering both clouds are
+// still shifted by one common anchor (the x centroid); this keeps the packed
+// coordinates small and changes no result.
+#pragma once
+
+#include "ra_common.cuh"
+
+namespace ra {
+
+// Per-pair metadata (fp64), layout with DP = padded dimension:
+//   [0] Wx  normaliser of x weights (a = w' / Wx; 1 for raw weights)
+//   [1] Wy
+//   [2] Wx_raw  sum of effective x weights before clamping
+//   [3] Wy_raw
+//   [4, 4+DP)        mu_x   (weighted centroid, sum_i a_i x_i)
+//   [4+DP, 4+2DP)    mu_y
+//   [4+2DP, 4+3DP)   anchor subtracted from x before packing
+//   [4+3DP, 4+4DP)   anchor subtracted from y before packing
+__host__ __device__ __forceinline__ int meta_stride(int DP) { return 4 + 4 * DP; }
+
+struct PrepArgs {
+  int64_t P;
+  int D, DP;     // DP: 3 for the D <= 3 path, else the padded generic width
+  int layout;    // 0 ragged, 1 dense
+  int wmode_x, wmode_y, center;
+  int packed3;   // 1: write the D <= 3 tile layout, 0: the generic layout
+  int64_t num_x, num_y, nmax_x, nmax_y;
+  float scale;   // sqrt(log2(e) / (2 sigma^2)): packed coords are scale * (p - anchor)
+  const float *x, *y, *w_x, *w_y;
+  const int64_t *ptr_x, *ptr_y;
+  const uint8_t *mask_x, *mask_y;
+  Seg *seg;
+  double *meta;
+  int *err;
+  // D <= 3 layout: rows {x', y', z', a}; columns as four SoA arrays of
+  // duplicated pairs {x',x',y',y'}, {z',z',a,a}, {a x',a x',a y',a y'}, {a z',a z',0,0}
+  float4 *Px, *Py;
+  float4 *Qx0, *Qx1, *Qx2, *Qx3, *Qy0, *Qy1, *Qy2, *Qy3;
+  // generic layout: coords [num * DP] (zero padded) and weights [num]
+  float *Gx, *Gy, *Ax, *Ay;
+};
+
+// Effective (masked, raw) weight of point i.
+__device__ __forceinline__ float eff_weight(const float *w, const uint8_t *mask, int wmode,
+                                            int64_t i) {
+  float v = (wmode == 3 || w == nullptr) ? 1.0f : w[i];
+  if (mask != nullptr && mask[i] == 0) v = 0.0f;
+  return v;
+}
+
+// Reduction width: power of two >= D (at least 4).
+__device__ __forceinline__ int red_width(int D) {
+  int r = 4;
+  while (r < D) r <<= 1;
+  return r;
+}
+
+template <int NT>
+__device__ void prep_side(const PrepArgs &A, int64_t p, int side, double *sh, int64_t *shl) {
+  const int tid = threadIdx.x;
+  const int D = A.D, DP = A.DP;
+  const float *pts = side == 0 ? A.x : A.y;
+  const float *w = side == 0 ? A.w_x : A.w_y;
+  const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+  const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+  const int64_t num = side == 0 ? A.num_x : A.num_y;
+  const int64_t *ptr = side == 0 ? A.ptr_x : A.ptr_y;
+  const int64_t nmax = side == 0 ? A.nmax_x : A.nmax_y;
+  double *meta = A.meta + p * meta_stride(DP);
+  Seg &sg = A.seg[p];
+
+  // ---- segment bounds ------------------------------------------------------
+  int64_t s, span;
+  if (A.layout == 0) {
+    int64_t a0 = ptr[p], a1 = ptr[p + 1];
+    if (tid == 0) {
+      int e = 0;
+      if (p == 0 && a0 != 0) e |= kErrPtrStart;
+      if (p == A.P - 1 && a1 != num) e |= kErrPtrEnd;
+      if (a1 < a0) e |= kErrPtrOrder;
+      if (e) atomicOr(A.err, e);
+    }
+    // clamp so that a malformed ptr can never send a kernel out of bounds
+    a0 = a0 < 0 ? 0 : (a0 > num ? num : a0);
+    a1 = a1 < a0 ? a0 : (a1 > num ? num : a1);
+    s = a0;
+    span = a1 - a0;
+  } else {
+    s = p * nmax;
+    span = nmax;
+  }
+
+  // ---- pass 1: weight sum, weighted coordinate sums, last valid index -------
+  const int RW = red_width(D);
+  const int lanes = NT / RW;  // point lanes
+  const int d = tid % RW, pl = tid / RW;
+  double acc = 0.0, wsum = 0.0;
+  int64_t last = -1;
+  int64_t nvalid = 0;
+  for (int64_t i = pl; i < span; i += lanes) {
+    const int64_t g = s + i;
+    const float wi = eff_weight(w, mask, wmode, g);
+    if (d < D) acc += (double)wi * (double)pts[g * D + d];
+    if (d == 0) {
+      wsum += (double)wi;
+      const bool valid = mask == nullptr || mask[g] != 0;
+      if (valid) {
+        last = i;
+        ++nvalid;
+      }
+    }
+  }
+  sh[tid] = acc;
+  __syncthreads();
+  double coord_sum = 0.0;
+  if (tid < RW)
+    for (int l = 0; l < lanes; ++l) coord_sum += sh[l * RW + tid];
+  __syncthreads();
+  sh[tid] = wsum;
+  shl[tid] = last;
+  shl[NT + tid] = nvalid;
+  __syncthreads();
+  if (tid == 0) {
+    double W = 0.0;
+    int64_t lst = -1, nv = 0;
+    for (int l = 0; l < lanes; ++l) {
+      W += sh[l * RW];
+      lst = shl[l * RW] > lst ? shl[l * RW] : lst;
+      nv += shl[NT + l * RW];
+    }
+    const int64_t count = A.layout == 0 ? span : lst + 1;
+    double Wn;
+    if (wmode == 0) {
+      Wn = 1.0;  // raw weights
+    } else if (wmode == 3) {
+      Wn = nv > 0 ? (double)nv : 1.0;  // uniform 1/count
+    } else if (wmode == 2) {
+      Wn = W > 1e-8 ? W : 1e-8;  // clamp_min(1e-8)
+    } else {
+      Wn = W;
+      if (count > 0 && !(W > 0.0) && !(W != W)) atomicOr(A.err, (int)kErrWeightSum);
+      if (!(W > 0.0)) Wn = 1.0;  // keep the kernels finite; the error is reported
+    }
+    meta[side] = Wn;
+    meta[2 + side] = W;
+    if (side == 0) {
+      sg.xs = s;
+      sg.xspan = span;
+      sg.xcount = count;
+    } else {
+      sg.ys = s;
+      sg.yspan = span;
+      sg.ycount = count;
+    }
+    sh[NT] = Wn;
+  }
+  __syncthreads();
+  const double Wn = sh[NT];
+  // centroid mu = sum_i a_i p_i = sum_i w'_i p_i / Wn
+  if (tid < DP) {
+    const double mu = tid < D ? coord_sum / Wn : 0.0;
+    meta[4 + side * DP + tid] = mu;
+  }
+  __syncthreads();
+  // anchors: x always uses mu_x; y uses mu_y when centering, else the common
+  // anchor mu_x (or mu_y when x is empty)
+  if (tid < DP) {
+    double anc;
+    if (side == 0) {
+      anc = meta[4 + tid];
+    } else if (A.center) {
+      anc = meta[4 + DP + tid];
+    } else {
+      anc = sg.xcount > 0 ? meta[4 + tid] : meta[4 + DP + tid];
+    }
+    meta[4 + (2 + side) * DP + tid] = anc;
+    sh[NT + 1 + tid] = anc;
+  }
+  __syncthreads();
+
+  // ---- pass 2: pack -------------------------------------------------------
+  const int64_t count = side == 0 ? sg.xcount : sg.ycount;
+  const float scale = A.scale;
+  const float inv_w = (float)(1.0 / Wn);
+  if (A.packed3) {
+    float4 *Pr = side == 0 ? A.Px : A.Py;
+    float4 *Q0 = side == 0 ? A.Qx0 : A.Qy0;
+    float4 *Q1 = side == 0 ? A.Qx1 : A.Qy1;
+    float4 *Q2 = side == 0 ? A.Qx2 : A.Qy2;
+    float4 *Q3 = side == 0 ? A.Qx3 : A.Qy3;
+    const float ax = (float)sh[NT + 1], ay = (float)sh[NT + 2], az = (float)sh[NT + 3];
+    for (int64_t i = tid; i < count; i += NT) {
+      const int64_t g = s + i;
+      const float wi = eff_weight(w, mask, wmode, g);
+      const float a = (float)((double)wi / Wn);
+      float c0 = 0.f, c1 = 0.f, c2 = 0.f;
+      c0 = scale * (pts[g * D + 0] - ax);
+      if (D > 1) c1 = scale * (pts[g * D + 1] - ay);
+      if (D > 2) c2 = scale * (pts[g * D + 2] - az);
+      Pr[g] = make_float4(c0, c1, c2, a);
+      if (Q0 != nullptr) {
+        Q0[g] = make_float4(c0, c0, c1, c1);
+        Q1[g] = make_float4(c2, c2, a, a);
+        Q2[g] = make_float4(a * c0, a * c0, a * c1, a * c1);
+        Q3[g] = make_float4(a * c2, a * c2, 0.f, 0.f);
+      }
+    }
+    (void)inv_w;
+  } else {
+    float *Gp = side == 0 ? A.Gx : A.Gy;
+    float *Ap = side == 0 ? A.Ax : A.Ay;
+    for (int64_t i = pl; i < count; i += lanes) {
+      const int64_t g = s + i;
+      if (d < DP) {
+        float v = 0.f;
+        if (d < D) v = scale * (float)((double)pts[g * D + d] - sh[NT + 1 + d]);
+        Gp[g * DP + d] = v;
+      }
+      if (d == 0) {
+        const float wi = eff_weight(w, mask, wmode, g);
+        Ap[g] = (float)((double)wi / Wn);
+      }
+    }
+    // RW may be < DP never happens: RW >= D and DP is D rounded up to the
+    // generic width which is <= RW by construction (see host code)
+  }
+  __syncthreads();
+}
+
+template <int NT>
+__global__ void __launch_bounds__(NT) prep_kernel(PrepArgs A) {
+  // sh: NT doubles for reductions + 1 + DP anchors; shl: 2*NT ints
+  extern __shared__ double smem[];
+  double *sh = smem;
+  int64_t *shl = (int64_t *)(smem + NT + 1 + 256);
+  const int64_t p = blockIdx.x;
+  if (p >= A.P) return;
+  prep_side<NT>(A, p, 0, sh, shl);
+  prep_side<NT>(A, p, 1, sh, shl);
+}
+
+}  // namespace ra

@@ -1,0 +1,284 @@
+// ra_tiles3.cuh -- the hot kernel for point clouds with D <= 3.
+//
+// Computes, for every pair and every block (x-y, x-x, y-y), the Gaussian
+// kernel terms k = 2^(-|x' - y'|^2) on pre-scaled coordinates
+// (x' = sqrt(log2(e) / (2 sigma^2)) * (x - anchor), so k = exp(-|x-y|^2/(2 sigma^2)),
+// rapidalign/kde_gradients.py:32-36) and reduces them into
+//   * per-item fp64 partials of K = sum a_i b_j k  (and of S = sum a b k r^2),
+//   * per-point fp32 row sums for the backward:
+//       s_i = sum_j b_j k_ij,   T_i = sum_j b_j y'_j k_ij     (rows)
+//       s_j = sum_i a_i k_ij,   T_j = sum_i a_i x'_i k_ij     (columns)
+//     from which the epilogue forms G_i = x'_i s_i - T_i = sum_j b_j k_ij (x'_i - y'_j).
+// One pass over the UNIQUE terms: the self blocks visit only tiles J >= I;
+// off-diagonal tiles feed both their rows and their columns, the diagonal
+// tile is evaluated in full feeding only its rows.
+//
+// Work decomposition (B200: 148 SMs, FP32-pipe bound): a persistent grid of
+// independent warps pulls items (pair, block, 64-row tile, column split) from
+// a global ticket.  Inside a warp the 32 lanes form 4 rings of 8 lanes.  Every
+// ring holds the same 64 rows (8 per lane, as 4 packed row pairs) and owns 16
+// of the 64 columns of the current column tile; the column accumulators
+// travel around the ring (one shuffle per step), so each column sum is
+// complete after 8 steps without any cross-lane reduction arithmetic.  Row
+// accumulators are combined across the 4 rings once per item.
+//
+// Arithmetic per unique term (fwd+bwd): 3 sub + 3 mul/fma (r^2) + 1 EX2 +
+// 4 FMA (row s, T) + 4 FMA (column s, T) = 14 FP32-pipe ops, issued as
+// packed f32x2 instructions where both lanes of a row pair share operands.
+// Accumulation order is fixed except for the fp32 red.add of per-point row
+// sums at L2; K and S partials are fp64 and reduced in a fixed order.
+#pragma once
+
+#include "ra_common.cuh"
+
+namespace ra {
+
+struct Tiles3Args {
+  const Item *items;
+  const int64_t *n_items;  // device scalar
+  unsigned int *ticket;    // zeroed before the launch
+  const Seg *seg;
+  const float4 *Px, *Py;
+  const ulonglong2 *Qx0, *Qx1, *Qx2, *Qx3;
+  const ulonglong2 *Qy0, *Qy1, *Qy2, *Qy3;
+  float *accX, *accY;  // [num][8]: self (s, T0, T1, T2), cross (s, T0, T1, T2)
+  double *itemK, *itemS;
+};
+
+// MODE 0: K only.  MODE 1: K + per-point sums.  MODE 2: also S (sigma grad).
+template <int MODE, bool DIAG>
+__device__ __forceinline__ void tiles3_coltile(
+    const int64_t J, const int64_t ccnt, const int64_t cbase, const ulonglong2 *__restrict__ C0,
+    const ulonglong2 *__restrict__ C1, const ulonglong2 *__restrict__ C2,
+    const ulonglong2 *__restrict__ C3, float *__restrict__ accC, const int offC, const int lane,
+    const f2_t (&X0)[4], const f2_t (&X1)[4], const f2_t (&X2)[4], const f2_t (&Aw)[4],
+    const f2_t (&AX0)[4], const f2_t (&AX1)[4], const f2_t (&AX2)[4], f2_t (&st)[4],
+    f2_t (&T0)[4], f2_t (&T1)[4], f2_t (&T2)[4], f2_t (&sgt)[4]) {
+  constexpr bool GRAD = MODE >= 1;
+  constexpr bool SIG = MODE == 2;
+  constexpr bool COLS = GRAD && !DIAG;
+  const int q = lane >> 3, p = lane & 7;
+  const int ring_base = lane & ~7;
+  float cs[2], c0[2], c1[2], c2[2];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) cs[c] = c0[c] = c1[c] = c2[c] = 0.f;
+
+#pragma unroll 1
+  for (int t = 0; t < 8; ++t) {
+    const int pos = (p + t) & 7;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int64_t col = J * kTile + c * 32 + q * 8 + pos;
+      const bool cv = col < ccnt;
+      const int64_t g = cbase + col;
+      const ulonglong2 z = make_ulonglong2(0ull, 0ull);
+      const ulonglong2 q0 = cv ? C0[g] : z;
+      const ulonglong2 q1 = cv ? C1[g] : z;
+      ulonglong2 q2 = z, q3 = z;
+      if (GRAD) {
+        q2 = cv ? C2[g] : z;
+        q3 = cv ? C3[g] : z;
+      }
+      const f2_t Y0 = q0.x, Y1 = q0.y, Y2 = q1.x, B = q1.y;
+#pragma unroll
+      for (int rp = 0; rp < 4; ++rp) {
+        const f2_t dx = sub2(X0[rp], Y0);
+        const f2_t dy = sub2(X1[rp], Y1);
+        const f2_t dz = sub2(X2[rp], Y2);
+        f2_t r2 = mul2(dx, dx);
+        r2 = fma2(dy, dy, r2);
+        r2 = fma2(dz, dz, r2);
+        float r_lo, r_hi;
+        upk(r2, r_lo, r_hi);
+        const float k_lo = ex2(-r_lo), k_hi = ex2(-r_hi);
+        const f2_t k = pk(k_lo, k_hi);
+        if (SIG) {
+          const f2_t wk = mul2(B, k);
+          st[rp] = add2(st[rp], wk);
+          sgt[rp] = fma2(wk, r2, sgt[rp]);
+        } else {
+          st[rp] = fma2(B, k, st[rp]);
+        }
+        if (GRAD) {
+          T0[rp] = fma2(q2.x, k, T0[rp]);
+          T1[rp] = fma2(q2.y, k, T1[rp]);
+          T2[rp] = fma2(q3.x, k, T2[rp]);
+        }
+        if (COLS) {
+          float a_lo, a_hi;
+          upk(Aw[rp], a_lo, a_hi);
+          cs[c] = fmaf(a_lo, k_lo, cs[c]);
+          cs[c] = fmaf(a_hi, k_hi, cs[c]);
+          upk(AX0[rp], a_lo, a_hi);
+          c0[c] = fmaf(a_lo, k_lo, c0[c]);
+          c0[c] = fmaf(a_hi, k_hi, c0[c]);
+          upk(AX1[rp], a_lo, a_hi);
+          c1[c] = fmaf(a_lo, k_lo, c1[c]);
+          c1[c] = fmaf(a_hi, k_hi, c1[c]);
+          upk(AX2[rp], a_lo, a_hi);
+          c2[c] = fmaf(a_lo, k_lo, c2[c]);
+          c2[c] = fmaf(a_hi, k_hi, c2[c]);
+        }
+      }
+    }
+    if (COLS && t < 7) {
+      // pass the column accumulators one position back around the ring
+      const int src = ring_base | ((p + 1) & 7);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        cs[c] = __shfl_sync(kFull, cs[c], src);
+        c0[c] = __shfl_sync(kFull, c0[c], src);
+        c1[c] = __shfl_sync(kFull, c1[c], src);
+        c2[c] = __shfl_sync(kFull, c2[c], src);
+      }
+    }
+  }
+  if (COLS) {
+    // after step 7 this lane holds the sums of position (p + 7) & 7
+    const int pos = (p + 7) & 7;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int64_t col = J * kTile + c * 32 + q * 8 + pos;
+      if (col < ccnt) red_add_v4(accC + (cbase + col) * 8 + offC, cs[c], c0[c], c1[c], c2[c]);
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(128, 3) tiles3_kernel(Tiles3Args A) {
+  constexpr bool GRAD = MODE >= 1;
+  constexpr bool SIG = MODE == 2;
+  const int lane = threadIdx.x & 31;
+  const int q = lane >> 3, p = lane & 7;
+  const int64_t total = *A.n_items;
+  for (;;) {
+    unsigned it = 0;
+    if (lane == 0) it = atomicAdd(A.ticket, 1u);
+    it = __shfl_sync(kFull, it, 0);
+    if ((int64_t)it >= total) break;
+    const Item item = A.items[it];
+    const Seg sg = A.seg[item.pair];
+    const int blk = item.block;
+    const bool sym = blk != 0;
+    const int64_t rbase = blk == 2 ? sg.ys : sg.xs;
+    const int64_t rcnt = blk == 2 ? sg.ycount : sg.xcount;
+    const int64_t cbase = blk == 1 ? sg.xs : sg.ys;
+    const int64_t ccnt = blk == 1 ? sg.xcount : sg.ycount;
+    const float4 *__restrict__ Pr = blk == 2 ? A.Py : A.Px;
+    const ulonglong2 *C0 = blk == 1 ? A.Qx0 : A.Qy0;
+    const ulonglong2 *C1 = blk == 1 ? A.Qx1 : A.Qy1;
+    const ulonglong2 *C2 = blk == 1 ? A.Qx2 : A.Qy2;
+    const ulonglong2 *C3 = blk == 1 ? A.Qx3 : A.Qy3;
+    float *accR = blk == 2 ? A.accY : A.accX;
+    float *accC = blk == 1 ? A.accX : A.accY;
+    const int off = blk == 0 ? 4 : 0;  // cross sums in [4, 8), self sums in [0, 4)
+
+    const int64_t nTc = ceil_div(ccnt, (int64_t)kTile);
+    const int64_t S = splits_for(nTc);
+    const int64_t L = ceil_div(nTc, S);
+    const int64_t I = item.tile;
+    int64_t J0 = (int64_t)item.split * L;
+    const int64_t J1 = J0 + L < nTc ? J0 + L : nTc;
+    if (sym && J0 < I) J0 = I;
+    if (J0 >= J1) {
+      if (lane == 0) {
+        A.itemK[it] = 0.0;
+        A.itemS[it] = 0.0;
+      }
+      continue;
+    }
+
+    // ---- rows: 8 per lane as 4 packed pairs; zero weight beyond the count ----
+    f2_t X0[4], X1[4], X2[4], Aw[4], AX0[4], AX1[4], AX2[4];
+#pragma unroll
+    for (int rp = 0; rp < 4; ++rp) {
+      const int64_t r0 = I * kTile + p * 8 + 2 * rp;
+      const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 v0 = r0 < rcnt ? Pr[rbase + r0] : zero;
+      const float4 v1 = r0 + 1 < rcnt ? Pr[rbase + r0 + 1] : zero;
+      X0[rp] = pk(v0.x, v1.x);
+      X1[rp] = pk(v0.y, v1.y);
+      X2[rp] = pk(v0.z, v1.z);
+      Aw[rp] = pk(v0.w, v1.w);
+      AX0[rp] = pk(v0.w * v0.x, v1.w * v1.x);
+      AX1[rp] = pk(v0.w * v0.y, v1.w * v1.y);
+      AX2[rp] = pk(v0.w * v0.z, v1.w * v1.z);
+    }
+    f2_t st[4], stot[4], T0[4], T1[4], T2[4], sgt[4];
+    const f2_t z2 = pk(0.f, 0.f);
+#pragma unroll
+    for (int rp = 0; rp < 4; ++rp) st[rp] = stot[rp] = T0[rp] = T1[rp] = T2[rp] = sgt[rp] = z2;
+    double ktot = 0.0, kd = 0.0, stot_sig = 0.0, sd = 0.0;
+
+#pragma unroll 1
+    for (int64_t J = J0; J < J1; ++J) {
+      const bool diag = sym && J == I;
+      if (diag)
+        tiles3_coltile<MODE, true>(J, ccnt, cbase, C0, C1, C2, C3, accC, off, lane, X0, X1, X2,
+                                   Aw, AX0, AX1, AX2, st, T0, T1, T2, sgt);
+      else
+        tiles3_coltile<MODE, false>(J, ccnt, cbase, C0, C1, C2, C3, accC, off, lane, X0, X1, X2,
+                                    Aw, AX0, AX1, AX2, st, T0, T1, T2, sgt);
+      // fold the per-tile fp32 row sums into fp64 pair partials
+#pragma unroll
+      for (int rp = 0; rp < 4; ++rp) {
+        float s_lo, s_hi, a_lo, a_hi;
+        upk(st[rp], s_lo, s_hi);
+        upk(Aw[rp], a_lo, a_hi);
+        ktot = fma((double)a_lo, (double)s_lo, ktot);
+        ktot = fma((double)a_hi, (double)s_hi, ktot);
+        if (GRAD) stot[rp] = add2(stot[rp], st[rp]);
+        st[rp] = z2;
+        if (SIG) {
+          upk(sgt[rp], s_lo, s_hi);
+          stot_sig = fma((double)a_lo, (double)s_lo, stot_sig);
+          stot_sig = fma((double)a_hi, (double)s_hi, stot_sig);
+          sgt[rp] = z2;
+        }
+      }
+      if (diag) {
+        kd = ktot;
+        sd = stot_sig;
+      }
+    }
+
+    // ---- pair partials: off-diagonal self terms count twice ----------------
+    const double kl = sym ? 2.0 * ktot - kd : ktot;
+    const double kw = warp_sum(kl);
+    double sw = 0.0;
+    if (SIG) sw = warp_sum(sym ? 2.0 * stot_sig - sd : stot_sig);
+    if (lane == 0) {
+      A.itemK[it] = kw;
+      A.itemS[it] = sw;
+    }
+
+    // ---- per-point row sums: combine the 4 rings, then one lane per row ----
+    if (GRAD) {
+#pragma unroll
+      for (int rp = 0; rp < 4; ++rp) {
+#pragma unroll
+        for (int o = 8; o <= 16; o <<= 1) {
+          stot[rp] = add2(stot[rp], __shfl_xor_sync(kFull, stot[rp], o));
+          T0[rp] = add2(T0[rp], __shfl_xor_sync(kFull, T0[rp], o));
+          T1[rp] = add2(T1[rp], __shfl_xor_sync(kFull, T1[rp], o));
+          T2[rp] = add2(T2[rp], __shfl_xor_sync(kFull, T2[rp], o));
+        }
+      }
+#pragma unroll
+      for (int rp = 0; rp < 4; ++rp) {
+        if (rp == q) {
+          const int64_t r0 = I * kTile + p * 8 + 2 * rp;
+          float s_lo, s_hi, t0l, t0h, t1l, t1h, t2l, t2h;
+          upk(stot[rp], s_lo, s_hi);
+          upk(T0[rp], t0l, t0h);
+          upk(T1[rp], t1l, t1h);
+          upk(T2[rp], t2l, t2h);
+          if (r0 < rcnt) red_add_v4(accR + (rbase + r0) * 8 + off, s_lo, t0l, t1l, t2l);
+          if (r0 + 1 < rcnt) red_add_v4(accR + (rbase + r0 + 1) * 8 + off, s_hi, t0h, t1h, t2h);
+        }
+      }
+    }
+  }
+}
+
+}  // namespace ra

@@ -1,0 +1,121 @@
+// ra_tilesg.cuh -- generic-dimension kernel (D >= 4, DP = D rounded up to a
+// power of two).  One thread per row, 128 rows per CTA, columns staged through
+// shared memory 32 at a time.  Every block is visited in both orientations
+// (x-y, x-x, y-y, y-x), so each point's row sums are complete when its CTA
+// finishes and are written without atomics.  This path covers any D; the
+// D <= 3 point-cloud path is ra_tiles3.cuh.
+#pragma once
+
+#include "ra_common.cuh"
+
+namespace ra {
+
+struct TilesGArgs {
+  const Item *items;
+  const int64_t *n_items;
+  const Seg *seg;
+  const float *Gx, *Gy;  // [num * DP] packed coordinates
+  const float *Ax, *Ay;  // [num] normalised weights
+  float *accX, *accY;    // [num][2 + 2*DP]: self (s, T[DP]), cross (s, T[DP])
+  double *itemK, *itemS;
+  int need_rows;         // 1: write the per-point sums (backward requested)
+};
+
+template <int DP, int MODE>
+__global__ void __launch_bounds__(kGenRows) tilesg_kernel(TilesGArgs A) {
+  constexpr bool SIG = MODE == 2;
+  __shared__ float ycol[kGenCols * DP];
+  __shared__ float bcol[kGenCols];
+  __shared__ double red[kGenRows / 32 * 2];
+  const int64_t it = blockIdx.x;
+  if (it >= *A.n_items) return;
+  const Item item = A.items[it];
+  const Seg sg = A.seg[item.pair];
+  const int o = item.block;  // 0: x-y, 1: x-x, 2: y-y, 3: y-x
+  const bool rows_x = (o == 0 || o == 1);
+  const bool cols_x = (o == 1 || o == 3);
+  const int64_t rbase = rows_x ? sg.xs : sg.ys, rcnt = rows_x ? sg.xcount : sg.ycount;
+  const int64_t cbase = cols_x ? sg.xs : sg.ys, ccnt = cols_x ? sg.xcount : sg.ycount;
+  const float *Gr = rows_x ? A.Gx : A.Gy;
+  const float *Ar = rows_x ? A.Ax : A.Ay;
+  const float *Gc = cols_x ? A.Gx : A.Gy;
+  const float *Ac = cols_x ? A.Ax : A.Ay;
+  float *acc = rows_x ? A.accX : A.accY;
+  const int off = (o == 0 || o == 3) ? 1 + DP : 0;
+
+  const int tid = threadIdx.x;
+  const int64_t row = (int64_t)item.tile * kGenRows + tid;
+  const bool rv = row < rcnt;
+  float xr[DP];
+#pragma unroll
+  for (int d = 0; d < DP; ++d) xr[d] = rv ? Gr[(rbase + row) * DP + d] : 0.f;
+  const float a = rv ? Ar[rbase + row] : 0.f;
+  float s = 0.f, sg2 = 0.f;
+  float T[DP];
+#pragma unroll
+  for (int d = 0; d < DP; ++d) T[d] = 0.f;
+  double s64 = 0.0, sg64 = 0.0;
+
+  for (int64_t j0 = 0; j0 < ccnt; j0 += kGenCols) {
+    __syncthreads();
+    for (int e = tid; e < kGenCols * DP; e += kGenRows) {
+      const int jj = e / DP, d = e % DP;
+      const int64_t j = j0 + jj;
+      ycol[e] = j < ccnt ? Gc[(cbase + j) * DP + d] : 0.f;
+    }
+    for (int jj = tid; jj < kGenCols; jj += kGenRows) {
+      const int64_t j = j0 + jj;
+      bcol[jj] = j < ccnt ? Ac[cbase + j] : 0.f;
+    }
+    __syncthreads();
+    float st = 0.f, sgt = 0.f;
+#pragma unroll 1
+    for (int jj = 0; jj < kGenCols; ++jj) {
+      const float *yj = ycol + jj * DP;
+      float r2 = 0.f;
+#pragma unroll
+      for (int d = 0; d < DP; ++d) {
+        const float t = xr[d] - yj[d];
+        r2 = fmaf(t, t, r2);
+      }
+      const float w = bcol[jj] * ex2(-r2);
+      st += w;
+      if (SIG) sgt = fmaf(w, r2, sgt);
+      if (MODE >= 1) {
+#pragma unroll
+        for (int d = 0; d < DP; ++d) T[d] = fmaf(w, yj[d], T[d]);
+      }
+    }
+    s += st;
+    s64 += (double)st;
+    if (SIG) sg64 += (double)sgt;
+  }
+  (void)sg2;
+  if (MODE >= 1 && A.need_rows && rv) {
+    float *dst = acc + (rbase + row) * (2 + 2 * DP) + off;
+    dst[0] = s;
+#pragma unroll
+    for (int d = 0; d < DP; ++d) dst[1 + d] = T[d];
+  }
+  // pair partials: K from x-y, x-x and y-y only (y-x would count Kxy twice)
+  double kv = (double)a * s64, sv = (double)a * sg64;
+  kv = warp_sum(kv);
+  sv = warp_sum(sv);
+  const int lane = tid & 31, wid = tid >> 5;
+  if (lane == 0) {
+    red[wid] = kv;
+    red[kGenRows / 32 + wid] = sv;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double K = 0.0, S = 0.0;
+    for (int w = 0; w < kGenRows / 32; ++w) {
+      K += red[w];
+      S += red[kGenRows / 32 + w];
+    }
+    A.itemK[it] = o == 3 ? 0.0 : K;
+    A.itemS[it] = o == 3 ? 0.0 : S;
+  }
+}
+
+}  // namespace ra

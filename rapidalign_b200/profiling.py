@@ -1,0 +1,40 @@
+"""Measurement helpers: device time of the hot tile kernel alone, for the
+roofline of the ragged forward+backward (CUDA events recorded by the library
+on the launch stream around that one launch)."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._core import Spec, _f32, _inputs
+from .kde import _ensure_ptr
+
+
+def tiles_time(x: torch.Tensor, y: torch.Tensor, batch_x: torch.Tensor, batch_y: torch.Tensor,
+               sigma: float, reps: int = 5, center: bool = True, need_grad: bool = True) -> float:
+    """Mean seconds of the fused tile kernel for the pyg_kde_mmd_loss problem
+    (uniform weights) with gradients requested."""
+    lib = _lib.load()
+    dev = x.device
+    ptr_x, P, _ = _ensure_ptr(None, batch_x, x.shape[0], dev)
+    ptr_y, _, _ = _ensure_ptr(None, batch_y, y.shape[0], dev)
+    spec = Spec(layout=_lib.RA_LAYOUT_RAGGED, num_pairs=P, dim=x.shape[1], num_x=x.shape[0],
+                num_y=y.shape[0], center=center, sigma=sigma, ptr_x=ptr_x, ptr_y=ptr_y)
+    x32, y32 = _f32(x), _f32(y)
+    desc = spec.desc(need_grad, False)
+    inp = _inputs(x32, y32, None, None, spec)
+    ws = _lib.workspace(lib.ra_kde_workspace_bytes(ctypes.byref(desc)), dev)
+    K = torch.empty(3 * P, dtype=torch.float64, device=dev)
+    ms = ctypes.c_float(0.0)
+    total = 0.0
+    with torch.cuda.device(dev):
+        for r in range(reps + 1):
+            rc = lib.ra_kde_forward_profiled(ctypes.byref(desc), ctypes.byref(inp), K.data_ptr(),
+                                             ws.data_ptr(), ws.numel(),
+                                             _lib.stream_handle(dev), ctypes.byref(ms))
+            _lib.check(rc, "profiled forward")
+            if r > 0:  # first run warms up
+                total += ms.value
+    return total / reps / 1e3
