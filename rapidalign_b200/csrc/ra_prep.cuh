@@ -103,13 +103,18 @@ __device__ void prep_side(const PrepArgs &A, int64_t p, int side, double *sh, in
   const int RW = red_width(D);
   const int lanes = NT / RW;  // point lanes
   const int d = tid % RW, pl = tid / RW;
-  double acc = 0.0, wsum = 0.0;
+  double acc = 0.0, accu = 0.0, wsum = 0.0;
   int64_t last = -1;
   int64_t nvalid = 0;
   for (int64_t i = pl; i < span; i += lanes) {
     const int64_t g = s + i;
     const float wi = eff_weight(w, mask, wmode, g);
-    if (d < D) acc += (double)wi * (double)pts[g * D + d];
+    const bool valid_pt = mask == nullptr || mask[g] != 0;
+    if (d < D) {
+      const double v = (double)pts[g * D + d];
+      acc += (double)wi * v;
+      if (valid_pt) accu += v;
+    }
     if (d == 0) {
       wsum += (double)wi;
       const bool valid = mask == nullptr || mask[g] != 0;
@@ -124,6 +129,12 @@ __device__ void prep_side(const PrepArgs &A, int64_t p, int side, double *sh, in
   double coord_sum = 0.0;
   if (tid < RW)
     for (int l = 0; l < lanes; ++l) coord_sum += sh[l * RW + tid];
+  __syncthreads();
+  sh[tid] = accu;
+  __syncthreads();
+  double plain_sum = 0.0;  // unweighted sum of the valid points (anchor)
+  if (tid < RW)
+    for (int l = 0; l < lanes; ++l) plain_sum += sh[l * RW + tid];
   __syncthreads();
   sh[tid] = wsum;
   shl[tid] = last;
@@ -162,25 +173,31 @@ __device__ void prep_side(const PrepArgs &A, int64_t p, int side, double *sh, in
       sg.ycount = count;
     }
     sh[NT] = Wn;
+    shl[0] = nv;
   }
   __syncthreads();
   const double Wn = sh[NT];
+  const int64_t nvalid_all = shl[0];
   // centroid mu = sum_i a_i p_i = sum_i w'_i p_i / Wn
   if (tid < DP) {
     const double mu = tid < D ? coord_sum / Wn : 0.0;
     meta[4 + side * DP + tid] = mu;
   }
   __syncthreads();
-  // anchors: x always uses mu_x; y uses mu_y when centering, else the common
-  // anchor mu_x (or mu_y when x is empty)
+  // anchors.  Centering: each cloud is shifted by its weighted centroid (the
+  // semantics).  Otherwise both clouds share one anchor, the unweighted mean
+  // of the valid x points (of the y points when x has none): distances do not
+  // change, and the packed coordinates stay as small as the clouds themselves
+  // whatever the weights are (raw weights may be negative).
   if (tid < DP) {
+    const double mean = (tid < D && nvalid_all > 0) ? plain_sum / (double)nvalid_all : 0.0;
     double anc;
-    if (side == 0) {
-      anc = meta[4 + tid];
-    } else if (A.center) {
-      anc = meta[4 + DP + tid];
+    if (A.center) {
+      anc = meta[4 + side * DP + tid];
+    } else if (side == 0) {
+      anc = mean;
     } else {
-      anc = sg.xcount > 0 ? meta[4 + tid] : meta[4 + DP + tid];
+      anc = sg.xcount > 0 ? meta[4 + 2 * DP + tid] : mean;
     }
     meta[4 + (2 + side) * DP + tid] = anc;
     sh[NT + 1 + tid] = anc;
@@ -207,9 +224,10 @@ __device__ void prep_side(const PrepArgs &A, int64_t p, int side, double *sh, in
       if (D > 1) c1 = scale * (pts[g * D + 1] - ay);
       if (D > 2) c2 = scale * (pts[g * D + 2] - az);
       Pr[g] = make_float4(c0, c1, c2, a);
-      if (Q0 != nullptr) {
-        Q0[g] = make_float4(c0, c0, c1, c1);
-        Q1[g] = make_float4(c2, c2, a, a);
+      Q0[g] = make_float4(c0, c0, c1, c1);
+      Q1[g] = make_float4(c2, c2, a, a);
+      // the weighted-coordinate columns exist only when gradients are requested
+      if (Q2 != nullptr) {
         Q2[g] = make_float4(a * c0, a * c0, a * c1, a * c1);
         Q3[g] = make_float4(a * c2, a * c2, 0.f, 0.f);
       }
