@@ -55,6 +55,7 @@ enum ra_status {
   RA_ERR_PTR_ORDER = 18,          /* ptr offsets must be non-decreasing */
   RA_ERR_WEIGHT_SUM = 19,         /* weights must sum to a positive value per segment */
   RA_ERR_STATE = 20,              /* backward called without a matching forward state */
+  RA_ERR_SCRATCH_LIMIT = 21,      /* problem needs more than the fixed no-alloc scratch */
 };
 
 /* Human-readable name of a status code (static string). */
@@ -192,6 +193,36 @@ RA_API int ra_kde_mmd_backward_segmented(const float *x, const float *y, const f
                                   float *grad_y, double *grad_wx, double *grad_wy,
                                   double *grad_sigma_pairs, void *workspace,
                                   size_t workspace_bytes, ra_stream_t stream);
+
+/*
+ * Ragged forward that allocates nothing.  No counterpart in the reference.
+ *
+ * Same arguments and results as ra_kde_mmd_forward_segmented, minus the
+ * workspace: the scratch comes from a fixed 64 MiB array that the library
+ * keeps in device memory (every GPU that loads the library holds it until the
+ * process exits).  Meant for callers that cannot call cudaMalloc: hosts whose
+ * plugin contract leaves all device memory to their own pool and hand a
+ * library nothing but input and output buffers, and loops that must not
+ * allocate (or synchronise the device, as an allocation may) once running.
+ *
+ * Limits and rules:
+ *  - problems whose workspace (ra_kde_mmd_forward_segmented_workspace_bytes)
+ *    exceeds 64 MiB are rejected with RA_ERR_SCRATCH_LIMIT before any work
+ *    is enqueued;
+ *  - the first call on a device looks up that device's address of the
+ *    scratch array (with the device current); make that first call before
+ *    any stream capture;
+ *  - all calls on a device share the one array and it keeps the previous
+ *    call's contents; the call clears what must start at zero, but calls
+ *    whose GPU work overlaps (other streams, other host threads) race on it:
+ *    serialise them.
+ */
+RA_API int ra_kde_mmd_forward_segmented_noalloc(const float *x, const float *y,
+                                                const float *w_x, const float *w_y,
+                                                const int64_t *ptr_x, const int64_t *ptr_y,
+                                                int64_t P, int64_t NX, int64_t NY, int32_t D,
+                                                double sigma, double *Kxx, double *Kyy,
+                                                double *Kxy, ra_stream_t stream);
 
 /* ---- diagnostics ------------------------------------------------------- */
 

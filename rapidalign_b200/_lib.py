@@ -29,6 +29,7 @@ RA_ERR_PTR_END = 17
 RA_ERR_PTR_ORDER = 18
 RA_ERR_WEIGHT_SUM = 19
 RA_ERR_STATE = 20
+RA_ERR_SCRATCH_LIMIT = 21
 
 RA_LAYOUT_RAGGED = 0
 RA_LAYOUT_DENSE = 1
@@ -108,6 +109,8 @@ SIGNATURES = {
     "ra_kde_mmd_backward_segmented": (ctypes.c_int, [_V, _V, _V, _V, _V, _V, _I64, _I64, _I64,
                                                      _I32, _V, _D, _V, _V, _V, _V, _V, _V, _SZ,
                                                      _V]),
+    "ra_kde_mmd_forward_segmented_noalloc": (ctypes.c_int, [_V, _V, _V, _V, _V, _V, _I64, _I64,
+                                                            _I64, _I32, _D, _V, _V, _V, _V]),
     "ra_kernel_launch_count": (ctypes.c_ulonglong, []),
     "ra_probe_fp32_peak": (ctypes.c_int, [_V, _I64, ctypes.c_int, ctypes.POINTER(_D), _V]),
 }

@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/rapidalign_b200.h"
 #include "ra_common.cuh"
@@ -472,6 +473,31 @@ __global__ void fp32_probe_kernel(float *out, int iters, float seed) {
   out[blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
+// Fixed scratch of ra_kde_mmd_forward_segmented_noalloc.  In host code the
+// name is only a stand-in: the device address comes from cudaGetSymbolAddress,
+// looked up once per device with that device current.
+constexpr size_t kNoallocScratchBytes = (size_t)64 << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[kMaxDevices] = {};
+
+int noalloc_scratch_address(void **out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return RA_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return RA_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return RA_ERR_CUDA;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return RA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -488,6 +514,8 @@ const char *ra_status_string(int status) {
     case RA_ERR_PTR_ORDER: return "ptr offsets must be non-decreasing";
     case RA_ERR_WEIGHT_SUM: return "weights must sum to a positive value per segment";
     case RA_ERR_STATE: return "backward needs a forward run with need_grad (and need_sigma_grad)";
+    case RA_ERR_SCRATCH_LIMIT:
+      return "problem too large for the 64 MiB fixed scratch of the no-alloc entry point";
     default: return "unknown status";
   }
 }
@@ -640,6 +668,23 @@ int ra_kde_mmd_backward_segmented(const float *x, const float *y, const float *w
   g.grad_wy = grad_wy;
   g.grad_sigma = grad_sigma_pairs;
   return backward_impl(&d, &in, coef, &g, workspace, workspace_bytes, st);
+}
+
+int ra_kde_mmd_forward_segmented_noalloc(const float *x, const float *y, const float *w_x,
+                                         const float *w_y, const int64_t *ptr_x,
+                                         const int64_t *ptr_y, int64_t P, int64_t NX,
+                                         int64_t NY, int32_t D, double sigma, double *Kxx,
+                                         double *Kyy, double *Kxy, ra_stream_t stream) {
+  const size_t need = ra_kde_mmd_forward_segmented_workspace_bytes(P, NX, NY, D);
+  if (need == 0) return RA_ERR_INVALID_ARGUMENT;
+  if (need > kNoallocScratchBytes) return RA_ERR_SCRATCH_LIMIT;
+  void *scratch = nullptr;
+  const int rc = noalloc_scratch_address(&scratch);
+  if (rc) return rc;
+  // the forward zeroes the scratch header itself; everything else it reads
+  // is written earlier in the same call
+  return ra_kde_mmd_forward_segmented(x, y, w_x, w_y, ptr_x, ptr_y, P, NX, NY, D, sigma, Kxx,
+                                      Kyy, Kxy, scratch, kNoallocScratchBytes, stream);
 }
 
 unsigned long long ra_kernel_launch_count(void) { return g_launches.load(); }
