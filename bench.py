@@ -167,7 +167,7 @@ class ClockSampler:
 # CPU baseline: the oracle (C, float64, OpenMP) on a bounded sample
 # ----------------------------------------------------------------------------
 
-def cpu_baseline(sample_graphs: int = 24, seed: int = SEED, budget_s: float = 20.0):
+def cpu_baseline(sample_graphs: int = GRAPHS_PER_GPU, seed: int = SEED, budget_s: float = 15.0):
     """Times the oracle's forward+backward sums on the first graphs of the
     same workload; returns full terms/s.  Stops adding graphs once the budget
     is used.  Uses every host thread."""

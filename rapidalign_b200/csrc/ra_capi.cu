@@ -40,10 +40,14 @@ int generic_dp(int D) {
 struct Layout {
   bool packed3;
   int DP;
+  int nq;           // packed3: arrays per tile (4 with gradients, 2 without)
   int acc_stride;
   int64_t max_items;
-  size_t hdr, seg, meta, cnt, item_off, boff, items, itemK, itemS, Kws, Sws, coef, Ktmp;
-  size_t Px, Py, Q[8], Gx, Gy, Ax, Ay, accX, accY;
+  int64_t max_tiles_x, max_tiles_y;  // packed3: bound on the padded tiles
+  size_t hdr, seg, meta, cnt, item_off, tbase_x, tbase_y, boff, items, itemK, itemS, Kws, Sws,
+      coef, Ktmp;
+  size_t tiles_x, tiles_y, Gx, Gy, Ax, Ay, accX, accY;
+  size_t acc_x_bytes, acc_y_bytes;
   size_t total;
 };
 
@@ -85,7 +89,10 @@ Layout make_layout(const ra_kde_desc *d) {
   }
   L.max_items = L.packed3 ? (int64_t)kSplitMax * (2 * tx + ty) : 2 * tx + 2 * ty;
   if (L.max_items < 1) L.max_items = 1;
+  L.max_tiles_x = L.packed3 ? (tx > 0 ? tx : 1) : 0;
+  L.max_tiles_y = L.packed3 ? (ty > 0 ? ty : 1) : 0;
   const bool grad = d->need_grad != 0;
+  L.nq = grad ? 4 : 2;
   size_t o = 0;
   auto take = [&](size_t bytes) {
     size_t at = o;
@@ -96,8 +103,10 @@ Layout make_layout(const ra_kde_desc *d) {
   L.hdr = take(256);
   L.seg = take(sizeof(Seg) * P1);
   L.meta = take(sizeof(double) * P1 * meta_stride(L.DP));
-  L.cnt = take(sizeof(int64_t) * P1);
+  L.cnt = take(sizeof(int64_t) * 3 * P1);
   L.item_off = take(sizeof(int64_t) * (P1 + 1));
+  L.tbase_x = take(sizeof(int64_t) * (P1 + 1));
+  L.tbase_y = take(sizeof(int64_t) * (P1 + 1));
   L.boff = take(sizeof(int64_t) * 4 * P1);
   L.items = take(sizeof(Item) * (size_t)L.max_items);
   L.itemK = take(sizeof(double) * (size_t)L.max_items);
@@ -108,22 +117,21 @@ Layout make_layout(const ra_kde_desc *d) {
   L.Ktmp = take(sizeof(double) * 3 * P1);
   const size_t nx = (size_t)(NX > 0 ? NX : 1), ny = (size_t)(NY > 0 ? NY : 1);
   if (L.packed3) {
-    L.Px = take(16 * nx);
-    L.Py = take(16 * ny);
-    const int nq = grad ? 4 : 2;
-    for (int i = 0; i < 4; ++i) {
-      L.Q[i] = i < nq ? take(16 * nx) : 0;
-      L.Q[4 + i] = i < nq ? take(16 * ny) : 0;
-    }
+    L.tiles_x = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_x);
+    L.tiles_y = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_y);
+    L.acc_x_bytes = sizeof(float) * 8 * kTile * (size_t)L.max_tiles_x;
+    L.acc_y_bytes = sizeof(float) * 8 * kTile * (size_t)L.max_tiles_y;
   } else {
     L.Gx = take(sizeof(float) * nx * L.DP);
     L.Gy = take(sizeof(float) * ny * L.DP);
     L.Ax = take(sizeof(float) * nx);
     L.Ay = take(sizeof(float) * ny);
+    L.acc_x_bytes = sizeof(float) * nx * L.acc_stride;
+    L.acc_y_bytes = sizeof(float) * ny * L.acc_stride;
   }
   if (grad) {
-    L.accX = take(sizeof(float) * nx * L.acc_stride);
-    L.accY = take(sizeof(float) * ny * L.acc_stride);
+    L.accX = take(L.acc_x_bytes);
+    L.accY = take(L.acc_y_bytes);
   }
   L.total = o;
   return L;
@@ -216,13 +224,8 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   const bool grad = d->need_grad != 0;
   const int mode = !grad ? 0 : (d->need_sigma_grad ? 2 : 1);
   if (grad) {
-    if (cudaMemsetAsync(at<char>(ws, L.accX), 0,
-                        sizeof(float) * (size_t)(d->num_x > 0 ? d->num_x : 1) * L.acc_stride,
-                        st) != cudaSuccess)
-      return RA_ERR_CUDA;
-    if (cudaMemsetAsync(at<char>(ws, L.accY), 0,
-                        sizeof(float) * (size_t)(d->num_y > 0 ? d->num_y : 1) * L.acc_stride,
-                        st) != cudaSuccess)
+    if (cudaMemsetAsync(at<char>(ws, L.accX), 0, L.acc_x_bytes, st) != cudaSuccess ||
+        cudaMemsetAsync(at<char>(ws, L.accY), 0, L.acc_y_bytes, st) != cudaSuccess)
       return RA_ERR_CUDA;
   }
   const float scale = scale_for(d->sigma);
@@ -254,28 +257,11 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   pa.seg = at<Seg>(ws, L.seg);
   pa.meta = at<double>(ws, L.meta);
   pa.err = at<int>(ws, L.hdr + kHdrErr);
-  if (L.packed3) {
-    pa.Px = at<float4>(ws, L.Px);
-    pa.Py = at<float4>(ws, L.Py);
-    pa.Qx0 = at<float4>(ws, L.Q[0]);
-    pa.Qx1 = at<float4>(ws, L.Q[1]);
-    pa.Qy0 = at<float4>(ws, L.Q[4]);
-    pa.Qy1 = at<float4>(ws, L.Q[5]);
-    if (grad) {
-      pa.Qx2 = at<float4>(ws, L.Q[2]);
-      pa.Qx3 = at<float4>(ws, L.Q[3]);
-      pa.Qy2 = at<float4>(ws, L.Q[6]);
-      pa.Qy3 = at<float4>(ws, L.Q[7]);
-    }
-  } else {
+  if (!L.packed3) {
     pa.Gx = at<float>(ws, L.Gx);
     pa.Gy = at<float>(ws, L.Gy);
     pa.Ax = at<float>(ws, L.Ax);
     pa.Ay = at<float>(ws, L.Ay);
-  }
-  if (!L.packed3 || grad) {
-    // the four-array column layout is only needed with gradients; without,
-    // the prep still writes Q0/Q1 (guarded by Q0 != nullptr)
   }
   const size_t prep_smem = sizeof(double) * (3 * kPrepThreads + 257);
   prep_kernel<kPrepThreads><<<(unsigned)P, kPrepThreads, prep_smem, st>>>(pa);
@@ -290,6 +276,8 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   pl.cnt = at<int64_t>(ws, L.cnt);
   pl.boff = at<int64_t>(ws, L.boff);
   pl.item_off = at<int64_t>(ws, L.item_off);
+  pl.tbase_x = at<int64_t>(ws, L.tbase_x);
+  pl.tbase_y = at<int64_t>(ws, L.tbase_y);
   pl.n_items = at<int64_t>(ws, L.hdr + kHdrNItems);
   pl.items = at<Item>(ws, L.items);
   pl.max_items = L.max_items;
@@ -299,6 +287,35 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   g_launches += 3;
   if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
 
+  // ---- pack the D <= 3 tile layout (needs the tile bases of all pairs) ----
+  if (L.packed3) {
+    PackArgs pk;
+    std::memset(&pk, 0, sizeof(pk));
+    pk.P = P;
+    pk.D = d->dim;
+    pk.nq = L.nq;
+    pk.scale = scale;
+    pk.x = in->x;
+    pk.y = in->y;
+    pk.w_x = in->w_x;
+    pk.w_y = in->w_y;
+    pk.mask_x = pa.mask_x;
+    pk.mask_y = pa.mask_y;
+    pk.wmode_x = d->weights_x;
+    pk.wmode_y = d->weights_y;
+    pk.seg = at<Seg>(ws, L.seg);
+    pk.meta = at<double>(ws, L.meta);
+    pk.tbase_x = at<int64_t>(ws, L.tbase_x);
+    pk.tbase_y = at<int64_t>(ws, L.tbase_y);
+    pk.max_tiles_x = L.max_tiles_x;
+    pk.max_tiles_y = L.max_tiles_y;
+    pk.tiles_x = at<ulonglong2>(ws, L.tiles_x);
+    pk.tiles_y = at<ulonglong2>(ws, L.tiles_y);
+    pack3_kernel<kPrepThreads><<<(unsigned)(2 * P), kPrepThreads, 0, st>>>(pk);
+    ++g_launches;
+    if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
+  }
+
   // ---- tiles ----
   if (ev0 != nullptr && cudaEventRecord(ev0, st) != cudaSuccess) return RA_ERR_CUDA;
   if (L.packed3) {
@@ -307,18 +324,12 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.n_items = at<int64_t>(ws, L.hdr + kHdrNItems);
     T.ticket = at<unsigned>(ws, L.hdr + kHdrTicket);
     T.seg = at<Seg>(ws, L.seg);
-    T.Px = at<float4>(ws, L.Px);
-    T.Py = at<float4>(ws, L.Py);
-    T.Qx0 = at<ulonglong2>(ws, L.Q[0]);
-    T.Qx1 = at<ulonglong2>(ws, L.Q[1]);
-    T.Qy0 = at<ulonglong2>(ws, L.Q[4]);
-    T.Qy1 = at<ulonglong2>(ws, L.Q[5]);
-    T.Qx2 = grad ? at<ulonglong2>(ws, L.Q[2]) : nullptr;
-    T.Qx3 = grad ? at<ulonglong2>(ws, L.Q[3]) : nullptr;
-    T.Qy2 = grad ? at<ulonglong2>(ws, L.Q[6]) : nullptr;
-    T.Qy3 = grad ? at<ulonglong2>(ws, L.Q[7]) : nullptr;
-    T.accX = grad ? at<float>(ws, L.accX) : nullptr;
-    T.accY = grad ? at<float>(ws, L.accY) : nullptr;
+    T.tbase_x = at<int64_t>(ws, L.tbase_x);
+    T.tbase_y = at<int64_t>(ws, L.tbase_y);
+    T.tiles_x = at<ulonglong2>(ws, L.tiles_x);
+    T.tiles_y = at<ulonglong2>(ws, L.tiles_y);
+    T.acc_x = grad ? at<float>(ws, L.accX) : nullptr;
+    T.acc_y = grad ? at<float>(ws, L.accY) : nullptr;
     T.itemK = at<double>(ws, L.itemK);
     T.itemS = at<double>(ws, L.itemS);
     rc = launch_tiles3(mode, T, st);
@@ -402,8 +413,11 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.mask_x = d->layout == RA_LAYOUT_DENSE ? in->mask_x : nullptr;
   ea.mask_y = d->layout == RA_LAYOUT_DENSE ? in->mask_y : nullptr;
   if (L.packed3) {
-    ea.Px = at<float4>(ws, L.Px);
-    ea.Py = at<float4>(ws, L.Py);
+    ea.tiles_x = at<ulonglong2>(ws, L.tiles_x);
+    ea.tiles_y = at<ulonglong2>(ws, L.tiles_y);
+    ea.tbase_x = at<int64_t>(ws, L.tbase_x);
+    ea.tbase_y = at<int64_t>(ws, L.tbase_y);
+    ea.nq = L.nq;
   } else {
     ea.Gx = at<float>(ws, L.Gx);
     ea.Gy = at<float>(ws, L.Gy);

@@ -24,6 +24,9 @@ __device__ __forceinline__ f2_t pk(float lo, float hi) {
 __device__ __forceinline__ void upk(f2_t v, float &lo, float &hi) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
+__device__ __forceinline__ unsigned long long pk2u(float lo, float hi) {
+  return ((unsigned long long)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
 __device__ __forceinline__ float lo_of(f2_t v) {
   float lo, hi;
   upk(v, lo, hi);

@@ -74,34 +74,40 @@ struct EpilogueArgs {
   const double *S_ws;  // [3P]
   const float *x, *y;  // original coordinates
   const uint8_t *mask_x, *mask_y;
-  const float4 *Px, *Py;              // packed3
-  const float *Gx, *Gy, *Ax, *Ay;     // generic
-  const float *accX, *accY;
+  const ulonglong2 *tiles_x, *tiles_y;  // packed3: tile layout (ra_prep.cuh)
+  const int64_t *tbase_x, *tbase_y;     // packed3: first tile of each pair
+  int nq;                               // packed3: arrays per tile
+  const float *Gx, *Gy, *Ax, *Ay;       // generic
+  const float *accX, *accY;  // packed3: [tiles * 64][8]; generic: [num][acc_stride]
   int acc_stride;
   float *grad_x, *grad_y;
   double *grad_wx, *grad_wy;
   double *grad_sigma;
 };
 
-// Per-point backward quantities of point g (pair-local coefficients cs, cc).
+// Per-point backward quantities.  packed3: `slot` = tile * 64 + lane of the
+// point in the tile layout; generic: `slot` = the point's row index.
 // Returns gxt[0..D) (dL/dx~) and ga (dL/da, direct part).
 template <int MAXD>
-__device__ __forceinline__ void point_grads(const EpilogueArgs &A, int side, int64_t g,
+__device__ __forceinline__ void point_grads(const EpilogueArgs &A, int side, int64_t slot,
                                             double cs, double cc, double k_x, double *gxt,
                                             double &ga, double &a_out) {
   const int D = A.D;
-  const float *acc = (side == 0 ? A.accX : A.accY) + g * A.acc_stride;
+  const float *acc = (side == 0 ? A.accX : A.accY) + slot * A.acc_stride;
   double a;
   double xp[MAXD];
   if (A.packed3) {
-    const float4 v = (side == 0 ? A.Px : A.Py)[g];
-    a = v.w;
-    xp[0] = v.x;
-    if (MAXD > 1) xp[1] = v.y;
-    if (MAXD > 2) xp[2] = v.z;
+    const ulonglong2 *tiles = side == 0 ? A.tiles_x : A.tiles_y;
+    const int64_t t = slot / kTile, l = slot % kTile;
+    const ulonglong2 q0 = tiles[(t * A.nq) * kTile + l];
+    const ulonglong2 q1 = tiles[(t * A.nq + 1) * kTile + l];
+    xp[0] = lo_of(q0.x);
+    if (MAXD > 1) xp[1] = lo_of(q0.y);
+    if (MAXD > 2) xp[2] = lo_of(q1.x);
+    a = lo_of(q1.y);
   } else {
-    a = (side == 0 ? A.Ax : A.Ay)[g];
-    const float *gp = (side == 0 ? A.Gx : A.Gy) + g * A.DP;
+    a = (side == 0 ? A.Ax : A.Ay)[slot];
+    const float *gp = (side == 0 ? A.Gx : A.Gy) + slot * A.DP;
     for (int d = 0; d < D && d < MAXD; ++d) xp[d] = gp[d];
   }
   const int cross = A.packed3 ? 4 : 1 + A.DP;
@@ -140,11 +146,12 @@ __global__ void __launch_bounds__(NT) epilogue3_kernel(EpilogueArgs A) {
   float *gout = side == 0 ? A.grad_x : A.grad_y;
   double *wout = side == 0 ? A.grad_wx : A.grad_wy;
 
+  const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
   // pass 1: R = sum dL/dx~ (D values), Q = sum a dL/da
   double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
   for (int64_t i = threadIdx.x; i < count; i += NT) {
     double gxt[3], ga, a;
-    point_grads<3>(A, side, s + i, cs, cc, k_x, gxt, ga, a);
+    point_grads<3>(A, side, slot0 + i, cs, cc, k_x, gxt, ga, a);
     for (int d = 0; d < D; ++d) R[d] += gxt[d];
     Q += a * ga;
   }
@@ -159,7 +166,7 @@ __global__ void __launch_bounds__(NT) epilogue3_kernel(EpilogueArgs A) {
     const int64_t g = s + i;
     double gxt[3] = {0.0, 0.0, 0.0}, ga = 0.0, a = 0.0;
     const bool live = i < count;
-    if (live) point_grads<3>(A, side, g, cs, cc, k_x, gxt, ga, a);
+    if (live) point_grads<3>(A, side, slot0 + i, cs, cc, k_x, gxt, ga, a);
     if (gout != nullptr) {
       for (int d = 0; d < D; ++d) {
         double v = gxt[d];

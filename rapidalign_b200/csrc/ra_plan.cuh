@@ -11,9 +11,11 @@ struct PlanArgs {
   int64_t P;
   int generic;        // 0: D <= 3 tiles (3 blocks), 1: generic rows (4 orientations)
   const Seg *seg;
-  int64_t *cnt;       // [P]: items of pair p, then (after the scan) offsets [P + 1]
+  int64_t *cnt;       // [3][P]: items, x tiles, y tiles of pair p
   int64_t *boff;      // [P * 4]: local start of each block inside the pair's items
   int64_t *item_off;  // [P + 1]
+  int64_t *tbase_x;   // [P + 1]: first x tile of each pair (D <= 3 tile layout)
+  int64_t *tbase_y;   // [P + 1]
   int64_t *n_items;   // device scalar (== item_off[P])
   Item *items;
   int64_t max_items;  // capacity of `items` (the host bound)
@@ -47,47 +49,58 @@ __global__ void plan_count_kernel(PlanArgs A) {
   A.boff[p * 4 + 2] = c[0] + c[1];
   A.boff[p * 4 + 3] = c[0] + c[1] + c[2];
   A.cnt[p] = c[0] + c[1] + c[2] + c[3];
+  const Seg &sg = A.seg[p];
+  A.cnt[A.P + p] = ceil_div(sg.xcount, (int64_t)kTile);
+  A.cnt[2 * A.P + p] = ceil_div(sg.ycount, (int64_t)kTile);
 }
 
-// Exclusive scan of cnt[0..P) into item_off[0..P], one CTA of 1024 threads.
+// Exclusive scans of the three per-pair counts (items, x tiles, y tiles) into
+// item_off, tbase_x and tbase_y (each [P + 1]); one CTA of 1024 threads.
 __global__ void __launch_bounds__(1024) plan_scan_kernel(PlanArgs A) {
   __shared__ int64_t warp_tot[32];
   __shared__ int64_t carry_sh;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  if (tid == 0) carry_sh = 0;
-  __syncthreads();
-  for (int64_t base = 0; base < A.P; base += 1024) {
-    const int64_t i = base + tid;
-    const int64_t v = i < A.P ? A.cnt[i] : 0;
-    int64_t incl = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int64_t n = __shfl_up_sync(kFull, incl, o);
-      if (lane >= o) incl += n;
-    }
-    if (lane == 31) warp_tot[wid] = incl;
+  for (int arr = 0; arr < 3; ++arr) {
+    const int64_t *src = A.cnt + arr * A.P;
+    int64_t *dst = arr == 0 ? A.item_off : (arr == 1 ? A.tbase_x : A.tbase_y);
+    if (tid == 0) carry_sh = 0;
     __syncthreads();
-    if (wid == 0) {
-      int64_t t = warp_tot[lane];
+    for (int64_t base = 0; base < A.P; base += 1024) {
+      const int64_t i = base + tid;
+      const int64_t v = i < A.P ? src[i] : 0;
+      int64_t incl = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int64_t n = __shfl_up_sync(kFull, t, o);
-        if (lane >= o) t += n;
+        const int64_t n = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += n;
       }
-      warp_tot[lane] = t;  // inclusive over warps
+      if (lane == 31) warp_tot[wid] = incl;
+      __syncthreads();
+      if (wid == 0) {
+        int64_t t = warp_tot[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int64_t n = __shfl_up_sync(kFull, t, o);
+          if (lane >= o) t += n;
+        }
+        warp_tot[lane] = t;  // inclusive over warps
+      }
+      __syncthreads();
+      const int64_t before = carry_sh + (wid > 0 ? warp_tot[wid - 1] : 0);
+      if (i < A.P) dst[i] = before + incl - v;
+      __syncthreads();
+      if (tid == 1023) carry_sh = before + incl;
+      __syncthreads();
+    }
+    if (tid == 0) {
+      int64_t tot = carry_sh;
+      if (arr == 0) {
+        if (tot > A.max_items) tot = A.max_items;  // cannot happen with the host bound
+        *A.n_items = tot;
+      }
+      dst[A.P] = tot;
     }
     __syncthreads();
-    const int64_t before = carry_sh + (wid > 0 ? warp_tot[wid - 1] : 0);
-    if (i < A.P) A.item_off[i] = before + incl - v;
-    __syncthreads();
-    if (tid == 1023) carry_sh = before + incl;
-    __syncthreads();
-  }
-  if (tid == 0) {
-    int64_t tot = carry_sh;
-    if (tot > A.max_items) tot = A.max_items;  // cannot happen with the host bound
-    A.item_off[A.P] = tot;
-    *A.n_items = tot;
   }
 }
 

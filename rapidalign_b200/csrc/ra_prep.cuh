@@ -41,11 +41,7 @@ struct PrepArgs {
   Seg *seg;
   double *meta;
   int *err;
-  // D <= 3 layout: rows {x', y', z', a}; columns as four SoA arrays of
-  // duplicated pairs {x',x',y',y'}, {z',z',a,a}, {a x',a x',a y',a y'}, {a z',a z',0,0}
-  float4 *Px, *Py;
-  float4 *Qx0, *Qx1, *Qx2, *Qx3, *Qy0, *Qy1, *Qy2, *Qy3;
-  // generic layout: coords [num * DP] (zero padded) and weights [num]
+  // generic layout (D >= 4): coords [num * DP] (zero padded) and weights [num]
   float *Gx, *Gy, *Ax, *Ay;
 };
 
@@ -204,36 +200,12 @@ __device__ void prep_side(const PrepArgs &A, int64_t p, int side, double *sh, in
   }
   __syncthreads();
 
-  // ---- pass 2: pack -------------------------------------------------------
+  // ---- pass 2 (generic layout only): pack ---------------------------------
+  // (the D <= 3 tile layout is written by pack3_kernel once the tile bases
+  // of all pairs are known)
   const int64_t count = side == 0 ? sg.xcount : sg.ycount;
   const float scale = A.scale;
-  const float inv_w = (float)(1.0 / Wn);
-  if (A.packed3) {
-    float4 *Pr = side == 0 ? A.Px : A.Py;
-    float4 *Q0 = side == 0 ? A.Qx0 : A.Qy0;
-    float4 *Q1 = side == 0 ? A.Qx1 : A.Qy1;
-    float4 *Q2 = side == 0 ? A.Qx2 : A.Qy2;
-    float4 *Q3 = side == 0 ? A.Qx3 : A.Qy3;
-    const float ax = (float)sh[NT + 1], ay = (float)sh[NT + 2], az = (float)sh[NT + 3];
-    for (int64_t i = tid; i < count; i += NT) {
-      const int64_t g = s + i;
-      const float wi = eff_weight(w, mask, wmode, g);
-      const float a = (float)((double)wi / Wn);
-      float c0 = 0.f, c1 = 0.f, c2 = 0.f;
-      c0 = scale * (pts[g * D + 0] - ax);
-      if (D > 1) c1 = scale * (pts[g * D + 1] - ay);
-      if (D > 2) c2 = scale * (pts[g * D + 2] - az);
-      Pr[g] = make_float4(c0, c1, c2, a);
-      Q0[g] = make_float4(c0, c0, c1, c1);
-      Q1[g] = make_float4(c2, c2, a, a);
-      // the weighted-coordinate columns exist only when gradients are requested
-      if (Q2 != nullptr) {
-        Q2[g] = make_float4(a * c0, a * c0, a * c1, a * c1);
-        Q3[g] = make_float4(a * c2, a * c2, 0.f, 0.f);
-      }
-    }
-    (void)inv_w;
-  } else {
+  if (!A.packed3) {
     float *Gp = side == 0 ? A.Gx : A.Gy;
     float *Ap = side == 0 ? A.Ax : A.Ay;
     for (int64_t i = pl; i < count; i += lanes) {
@@ -248,8 +220,6 @@ __device__ void prep_side(const PrepArgs &A, int64_t p, int side, double *sh, in
         Ap[g] = (float)((double)wi / Wn);
       }
     }
-    // RW may be < DP never happens: RW >= D and DP is D rounded up to the
-    // generic width which is <= RW by construction (see host code)
   }
   __syncthreads();
 }
@@ -265,5 +235,77 @@ __global__ void __launch_bounds__(NT) prep_kernel(PrepArgs A) {
   prep_side<NT>(A, p, 0, sh, shl);
   prep_side<NT>(A, p, 1, sh, shl);
 }
+
+// ---------------------------------------------------------------------------
+// D <= 3 tile layout.  Each cloud is cut into 64-point tiles, zero-weight
+// padded; pair p's x tiles start at tile tbase_x[p] (exclusive scan of
+// ceil(count / 64)).  A tile stores NQ arrays of 64 duplicated pairs
+// (16 bytes per point each):
+//   q = 0: {x', x', y', y'}      q = 1: {z', z', a, a}
+//   q = 2: {a x', a x', a y', a y'}   q = 3: {a z', a z', 0, 0}   (gradients only)
+// so one column feeds packed f32x2 arithmetic against two rows, and a warp
+// reads any column of a tile at an immediate offset from the tile base.
+// ---------------------------------------------------------------------------
+struct PackArgs {
+  int64_t P;
+  int D, nq;
+  float scale;
+  const float *x, *y, *w_x, *w_y;
+  const uint8_t *mask_x, *mask_y;
+  int wmode_x, wmode_y;
+  const Seg *seg;
+  const double *meta;
+  const int64_t *tbase_x, *tbase_y;  // [P + 1]
+  int64_t max_tiles_x, max_tiles_y;
+  ulonglong2 *tiles_x, *tiles_y;     // [tiles][nq][64]
+};
+
+template <int NT>
+__global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
+  const int64_t p = blockIdx.x >> 1;
+  const int side = blockIdx.x & 1;
+  if (p >= A.P) return;
+  const Seg sg = A.seg[p];
+  const int D = A.D;
+  const int64_t s = side == 0 ? sg.xs : sg.ys;
+  const int64_t count = side == 0 ? sg.xcount : sg.ycount;
+  const int64_t t0 = (side == 0 ? A.tbase_x : A.tbase_y)[p];
+  const int64_t t1 = (side == 0 ? A.tbase_x : A.tbase_y)[p + 1];
+  const int64_t tmax = side == 0 ? A.max_tiles_x : A.max_tiles_y;
+  const float *pts = side == 0 ? A.x : A.y;
+  const float *w = side == 0 ? A.w_x : A.w_y;
+  const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+  const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+  ulonglong2 *tiles = side == 0 ? A.tiles_x : A.tiles_y;
+  const double *meta = A.meta + p * meta_stride(3);
+  const double Wn = meta[side];
+  const float ax = (float)meta[4 + (2 + side) * 3 + 0];
+  const float ay = (float)meta[4 + (2 + side) * 3 + 1];
+  const float az = (float)meta[4 + (2 + side) * 3 + 2];
+  const float scale = A.scale;
+  const int nq = A.nq;
+  const int64_t npad = (t1 - t0) * kTile;
+  for (int64_t i = threadIdx.x; i < npad; i += NT) {
+    const int64_t t = t0 + i / kTile;
+    if (t >= tmax) break;  // malformed ptr overflowing the bound (error already flagged)
+    float c0 = 0.f, c1 = 0.f, c2 = 0.f, a = 0.f;
+    if (i < count) {
+      const int64_t g = s + i;
+      a = (float)((double)eff_weight(w, mask, wmode, g) / Wn);
+      c0 = scale * (pts[g * D + 0] - ax);
+      if (D > 1) c1 = scale * (pts[g * D + 1] - ay);
+      if (D > 2) c2 = scale * (pts[g * D + 2] - az);
+    }
+    ulonglong2 *tp = tiles + t * (int64_t)(nq * kTile) + (i % kTile);
+    tp[0] = make_ulonglong2(pk2u(c0, c0), pk2u(c1, c1));
+    tp[kTile] = make_ulonglong2(pk2u(c2, c2), pk2u(a, a));
+    if (nq > 2) {
+      const float b0 = a * c0, b1 = a * c1, b2 = a * c2;
+      tp[2 * kTile] = make_ulonglong2(pk2u(b0, b0), pk2u(b1, b1));
+      tp[3 * kTile] = make_ulonglong2(pk2u(b2, b2), 0ull);
+    }
+  }
+}
+
 
 }  // namespace ra

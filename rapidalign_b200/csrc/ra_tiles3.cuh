@@ -22,6 +22,12 @@
 // complete after 8 steps without any cross-lane reduction arithmetic.  Row
 // accumulators are combined across the 4 rings once per item.
 //
+// Data come from the padded tile layout written by pack3_kernel
+// (ra_prep.cuh): a column is one 16-byte slot in each of the tile's NQ
+// arrays, every slot of a padded tile exists and padding carries zero
+// weight, so the inner loop has no bounds tests and addresses all loads of a
+// step at immediate offsets from one pointer.
+//
 // Arithmetic per unique term (fwd+bwd): 3 sub + 3 mul/fma (r^2) + 1 EX2 +
 // 4 FMA (row s, T) + 4 FMA (column s, T) = 14 FP32-pipe ops, issued as
 // packed f32x2 instructions where both lanes of a row pair share operands.
@@ -38,24 +44,29 @@ struct Tiles3Args {
   const int64_t *n_items;  // device scalar
   unsigned int *ticket;    // zeroed before the launch
   const Seg *seg;
-  const float4 *Px, *Py;
-  const ulonglong2 *Qx0, *Qx1, *Qx2, *Qx3;
-  const ulonglong2 *Qy0, *Qy1, *Qy2, *Qy3;
-  float *accX, *accY;  // [num][8]: self (s, T0, T1, T2), cross (s, T0, T1, T2)
+  const int64_t *tbase_x, *tbase_y;     // first tile of each pair's cloud
+  const ulonglong2 *tiles_x, *tiles_y;  // [tiles][NQ][64]
+  float *acc_x, *acc_y;                 // [tiles * 64][8]: self (s, T0..T2), cross (s, T0..T2)
   double *itemK, *itemS;
 };
 
 // MODE 0: K only.  MODE 1: K + per-point sums.  MODE 2: also S (sigma grad).
+template <int MODE>
+struct Tiles3Mode {
+  static constexpr bool GRAD = MODE >= 1;
+  static constexpr bool SIG = MODE == 2;
+  static constexpr int NQ = GRAD ? 4 : 2;
+};
+
 template <int MODE, bool DIAG>
 __device__ __forceinline__ void tiles3_coltile(
-    const int64_t J, const int64_t ccnt, const int64_t cbase, const ulonglong2 *__restrict__ C0,
-    const ulonglong2 *__restrict__ C1, const ulonglong2 *__restrict__ C2,
-    const ulonglong2 *__restrict__ C3, float *__restrict__ accC, const int offC, const int lane,
-    const f2_t (&X0)[4], const f2_t (&X1)[4], const f2_t (&X2)[4], const f2_t (&Aw)[4],
-    const f2_t (&AX0)[4], const f2_t (&AX1)[4], const f2_t (&AX2)[4], f2_t (&st)[4],
-    f2_t (&T0)[4], f2_t (&T1)[4], f2_t (&T2)[4], f2_t (&sgt)[4]) {
-  constexpr bool GRAD = MODE >= 1;
-  constexpr bool SIG = MODE == 2;
+    const ulonglong2 *__restrict__ ct, const int64_t col0, const int64_t ccnt,
+    float *__restrict__ accC, const int lane, const f2_t (&X0)[4], const f2_t (&X1)[4],
+    const f2_t (&X2)[4], const f2_t (&Aw)[4], const f2_t (&AX0)[4], const f2_t (&AX1)[4],
+    const f2_t (&AX2)[4], f2_t (&st)[4], f2_t (&T0)[4], f2_t (&T1)[4], f2_t (&T2)[4],
+    f2_t (&sgt)[4]) {
+  constexpr bool GRAD = Tiles3Mode<MODE>::GRAD;
+  constexpr bool SIG = Tiles3Mode<MODE>::SIG;
   constexpr bool COLS = GRAD && !DIAG;
   const int q = lane >> 3, p = lane & 7;
   const int ring_base = lane & ~7;
@@ -65,19 +76,15 @@ __device__ __forceinline__ void tiles3_coltile(
 
 #pragma unroll 1
   for (int t = 0; t < 8; ++t) {
-    const int pos = (p + t) & 7;
+    const ulonglong2 *cp = ct + q * 8 + ((p + t) & 7);
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
-      const int64_t col = J * kTile + c * 32 + q * 8 + pos;
-      const bool cv = col < ccnt;
-      const int64_t g = cbase + col;
-      const ulonglong2 z = make_ulonglong2(0ull, 0ull);
-      const ulonglong2 q0 = cv ? C0[g] : z;
-      const ulonglong2 q1 = cv ? C1[g] : z;
-      ulonglong2 q2 = z, q3 = z;
+      const ulonglong2 q0 = cp[c * 32];
+      const ulonglong2 q1 = cp[c * 32 + kTile];
+      ulonglong2 q2 = make_ulonglong2(0ull, 0ull), q3 = q2;
       if (GRAD) {
-        q2 = cv ? C2[g] : z;
-        q3 = cv ? C3[g] : z;
+        q2 = cp[c * 32 + 2 * kTile];
+        q3 = cp[c * 32 + 3 * kTile];
       }
       const f2_t Y0 = q0.x, Y1 = q0.y, Y2 = q1.x, B = q1.y;
 #pragma unroll
@@ -138,16 +145,18 @@ __device__ __forceinline__ void tiles3_coltile(
     const int pos = (p + 7) & 7;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
-      const int64_t col = J * kTile + c * 32 + q * 8 + pos;
-      if (col < ccnt) red_add_v4(accC + (cbase + col) * 8 + offC, cs[c], c0[c], c1[c], c2[c]);
+      const int in_tile = c * 32 + q * 8 + pos;
+      if (col0 + in_tile < ccnt) red_add_v4(accC + in_tile * 8, cs[c], c0[c], c1[c], c2[c]);
     }
   }
 }
 
 template <int MODE>
 __global__ void __launch_bounds__(128, 3) tiles3_kernel(Tiles3Args A) {
-  constexpr bool GRAD = MODE >= 1;
-  constexpr bool SIG = MODE == 2;
+  constexpr bool GRAD = Tiles3Mode<MODE>::GRAD;
+  constexpr bool SIG = Tiles3Mode<MODE>::SIG;
+  constexpr int NQ = Tiles3Mode<MODE>::NQ;
+  constexpr int TILE_U2 = NQ * kTile;  // 16-byte slots per tile
   const int lane = threadIdx.x & 31;
   const int q = lane >> 3, p = lane & 7;
   const int64_t total = *A.n_items;
@@ -160,17 +169,15 @@ __global__ void __launch_bounds__(128, 3) tiles3_kernel(Tiles3Args A) {
     const Seg sg = A.seg[item.pair];
     const int blk = item.block;
     const bool sym = blk != 0;
-    const int64_t rbase = blk == 2 ? sg.ys : sg.xs;
-    const int64_t rcnt = blk == 2 ? sg.ycount : sg.xcount;
-    const int64_t cbase = blk == 1 ? sg.xs : sg.ys;
-    const int64_t ccnt = blk == 1 ? sg.xcount : sg.ycount;
-    const float4 *__restrict__ Pr = blk == 2 ? A.Py : A.Px;
-    const ulonglong2 *C0 = blk == 1 ? A.Qx0 : A.Qy0;
-    const ulonglong2 *C1 = blk == 1 ? A.Qx1 : A.Qy1;
-    const ulonglong2 *C2 = blk == 1 ? A.Qx2 : A.Qy2;
-    const ulonglong2 *C3 = blk == 1 ? A.Qx3 : A.Qy3;
-    float *accR = blk == 2 ? A.accY : A.accX;
-    float *accC = blk == 1 ? A.accX : A.accY;
+    const bool rows_y = blk == 2, cols_x = blk == 1;
+    const int64_t rcnt = rows_y ? sg.ycount : sg.xcount;
+    const int64_t ccnt = cols_x ? sg.xcount : sg.ycount;
+    const int64_t rtb = (rows_y ? A.tbase_y : A.tbase_x)[item.pair];
+    const int64_t ctb = (cols_x ? A.tbase_x : A.tbase_y)[item.pair];
+    const ulonglong2 *__restrict__ rt = rows_y ? A.tiles_y : A.tiles_x;
+    const ulonglong2 *__restrict__ ctiles = cols_x ? A.tiles_x : A.tiles_y;
+    float *accR = rows_y ? A.acc_y : A.acc_x;
+    float *accC = cols_x ? A.acc_x : A.acc_y;
     const int off = blk == 0 ? 4 : 0;  // cross sums in [4, 8), self sums in [0, 4)
 
     const int64_t nTc = ceil_div(ccnt, (int64_t)kTile);
@@ -188,21 +195,28 @@ __global__ void __launch_bounds__(128, 3) tiles3_kernel(Tiles3Args A) {
       continue;
     }
 
-    // ---- rows: 8 per lane as 4 packed pairs; zero weight beyond the count ----
+    // ---- rows: 8 per lane as 4 packed pairs (padding rows have zero weight) --
     f2_t X0[4], X1[4], X2[4], Aw[4], AX0[4], AX1[4], AX2[4];
+    {
+      const ulonglong2 *rp0 = rt + (rtb + I) * TILE_U2 + p * 8;
 #pragma unroll
-    for (int rp = 0; rp < 4; ++rp) {
-      const int64_t r0 = I * kTile + p * 8 + 2 * rp;
-      const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-      const float4 v0 = r0 < rcnt ? Pr[rbase + r0] : zero;
-      const float4 v1 = r0 + 1 < rcnt ? Pr[rbase + r0 + 1] : zero;
-      X0[rp] = pk(v0.x, v1.x);
-      X1[rp] = pk(v0.y, v1.y);
-      X2[rp] = pk(v0.z, v1.z);
-      Aw[rp] = pk(v0.w, v1.w);
-      AX0[rp] = pk(v0.w * v0.x, v1.w * v1.x);
-      AX1[rp] = pk(v0.w * v0.y, v1.w * v1.y);
-      AX2[rp] = pk(v0.w * v0.z, v1.w * v1.z);
+      for (int rp = 0; rp < 4; ++rp) {
+        const ulonglong2 a0 = rp0[2 * rp], b0 = rp0[2 * rp + 1];                  // x', y'
+        const ulonglong2 a1 = rp0[kTile + 2 * rp], b1 = rp0[kTile + 2 * rp + 1];  // z', a
+        X0[rp] = pk(lo_of(a0.x), lo_of(b0.x));
+        X1[rp] = pk(lo_of(a0.y), lo_of(b0.y));
+        X2[rp] = pk(lo_of(a1.x), lo_of(b1.x));
+        Aw[rp] = pk(lo_of(a1.y), lo_of(b1.y));
+        if (GRAD) {
+          const ulonglong2 a2 = rp0[2 * kTile + 2 * rp], b2 = rp0[2 * kTile + 2 * rp + 1];
+          const ulonglong2 a3 = rp0[3 * kTile + 2 * rp], b3 = rp0[3 * kTile + 2 * rp + 1];
+          AX0[rp] = pk(lo_of(a2.x), lo_of(b2.x));
+          AX1[rp] = pk(lo_of(a2.y), lo_of(b2.y));
+          AX2[rp] = pk(lo_of(a3.x), lo_of(b3.x));
+        } else {
+          AX0[rp] = AX1[rp] = AX2[rp] = 0ull;
+        }
+      }
     }
     f2_t st[4], stot[4], T0[4], T1[4], T2[4], sgt[4];
     const f2_t z2 = pk(0.f, 0.f);
@@ -213,12 +227,14 @@ __global__ void __launch_bounds__(128, 3) tiles3_kernel(Tiles3Args A) {
 #pragma unroll 1
     for (int64_t J = J0; J < J1; ++J) {
       const bool diag = sym && J == I;
+      const ulonglong2 *ct = ctiles + (ctb + J) * TILE_U2;
+      float *accJ = accC + ((ctb + J) * kTile) * 8 + off;
       if (diag)
-        tiles3_coltile<MODE, true>(J, ccnt, cbase, C0, C1, C2, C3, accC, off, lane, X0, X1, X2,
-                                   Aw, AX0, AX1, AX2, st, T0, T1, T2, sgt);
+        tiles3_coltile<MODE, true>(ct, J * kTile, ccnt, accJ, lane, X0, X1, X2, Aw, AX0, AX1,
+                                   AX2, st, T0, T1, T2, sgt);
       else
-        tiles3_coltile<MODE, false>(J, ccnt, cbase, C0, C1, C2, C3, accC, off, lane, X0, X1, X2,
-                                    Aw, AX0, AX1, AX2, st, T0, T1, T2, sgt);
+        tiles3_coltile<MODE, false>(ct, J * kTile, ccnt, accJ, lane, X0, X1, X2, Aw, AX0, AX1,
+                                    AX2, st, T0, T1, T2, sgt);
       // fold the per-tile fp32 row sums into fp64 pair partials
 #pragma unroll
       for (int rp = 0; rp < 4; ++rp) {
@@ -264,17 +280,18 @@ __global__ void __launch_bounds__(128, 3) tiles3_kernel(Tiles3Args A) {
           T2[rp] = add2(T2[rp], __shfl_xor_sync(kFull, T2[rp], o));
         }
       }
+      float *accI = accR + ((rtb + I) * kTile) * 8 + off;
 #pragma unroll
       for (int rp = 0; rp < 4; ++rp) {
         if (rp == q) {
-          const int64_t r0 = I * kTile + p * 8 + 2 * rp;
+          const int r0 = p * 8 + 2 * rp;
           float s_lo, s_hi, t0l, t0h, t1l, t1h, t2l, t2h;
           upk(stot[rp], s_lo, s_hi);
           upk(T0[rp], t0l, t0h);
           upk(T1[rp], t1l, t1h);
           upk(T2[rp], t2l, t2h);
-          if (r0 < rcnt) red_add_v4(accR + (rbase + r0) * 8 + off, s_lo, t0l, t1l, t2l);
-          if (r0 + 1 < rcnt) red_add_v4(accR + (rbase + r0 + 1) * 8 + off, s_hi, t0h, t1h, t2h);
+          if (I * kTile + r0 < rcnt) red_add_v4(accI + r0 * 8, s_lo, t0l, t1l, t2l);
+          if (I * kTile + r0 + 1 < rcnt) red_add_v4(accI + (r0 + 1) * 8, s_hi, t0h, t1h, t2h);
         }
       }
     }
