@@ -250,6 +250,8 @@ def run_ours(args):
 
     stream = torch.cuda.current_stream(dev)
 
+    h2d_times = []
+
     def timed_loop(k, e2e):
         evs = []
         for _ in range(k):
@@ -257,19 +259,24 @@ def run_ours(args):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
+            eh = None
             if e2e:
                 xs = xh.to(dev, non_blocking=True)
                 ys = yh.to(dev, non_blocking=True)
                 b1 = bxh.to(dev, non_blocking=True)
                 b2 = byh.to(dev, non_blocking=True)
+                eh = torch.cuda.Event(enable_timing=True)
+                eh.record(stream)
                 loss, _, _ = step(xs, ys, b1, b2)
                 loss_h.copy_(loss.detach(), non_blocking=True)
             else:
                 step(xd, yd, bxd, byd)
             e1.record(stream)
-            evs.append((e0, e1))
+            evs.append((e0, e1, eh))
         torch.cuda.synchronize(dev)
-        return sum(a.elapsed_time(b) for a, b in evs) / 1e3  # seconds
+        if e2e:
+            h2d_times.extend(a.elapsed_time(h) for a, _, h in evs)
+        return sum(a.elapsed_time(b) for a, b, _ in evs) / 1e3  # seconds
 
     for _ in range(args.warmup):
         step(xd, yd, bxd, byd)
@@ -355,6 +362,8 @@ def run_ours(args):
                 "seed": SEED,
             },
             "e2e": {"value": e2e_value, "unit": "terms/s",
+                    "ms_per_step": t_e2e / K * 1e3,
+                    "h2d_ms_per_step": (statistics.median(h2d_times[-K:]) if h2d_times else None),
                     "h2d_bytes_per_step": int(xh.numel() * 4 + yh.numel() * 4 + bxh.numel() * 8
                                               + byh.numel() * 8),
                     "d2h_bytes_per_step": int(loss_h.numel() * 4)},

@@ -76,7 +76,7 @@ Layout make_layout(const ra_kde_desc *d) {
   const int64_t P = d->num_pairs, NX = d->num_x, NY = d->num_y;
   L.packed3 = d->dim <= 3;
   L.DP = L.packed3 ? 3 : generic_dp(d->dim);
-  L.acc_stride = L.packed3 ? 8 : 2 + 2 * L.DP;
+  L.acc_stride = L.packed3 ? kAcc3Stride : 2 + 2 * L.DP;
   // host bound on the number of items
   int64_t tx, ty;  // sum over pairs of row tiles
   const int64_t rows = L.packed3 ? kTile : kGenRows;
@@ -119,8 +119,8 @@ Layout make_layout(const ra_kde_desc *d) {
   if (L.packed3) {
     L.tiles_x = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_x);
     L.tiles_y = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_y);
-    L.acc_x_bytes = sizeof(float) * 8 * kTile * (size_t)L.max_tiles_x;
-    L.acc_y_bytes = sizeof(float) * 8 * kTile * (size_t)L.max_tiles_y;
+    L.acc_x_bytes = sizeof(float) * kAcc3Stride * kTile * (size_t)L.max_tiles_x;
+    L.acc_y_bytes = sizeof(float) * kAcc3Stride * kTile * (size_t)L.max_tiles_y;
   } else {
     L.Gx = take(sizeof(float) * nx * L.DP);
     L.Gy = take(sizeof(float) * ny * L.DP);
@@ -156,26 +156,27 @@ int check_common(const ra_kde_desc *d, void *ws, size_t ws_bytes, size_t need) {
   return RA_OK;
 }
 
-int launch_tiles3(int mode, const Tiles3Args &T, cudaStream_t st) {
+int launch_tiles3(int mode, const Tiles3Args &Targs, cudaStream_t st) {
   int dev = 0, sms = 0, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaError_t e;
+  constexpr int T = kT3Threads;
   if (mode == 0)
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<0>, 128, 0);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<0>, T, 0);
   else if (mode == 1)
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<1>, 128, 0);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<1>, T, 0);
   else
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<2>, 128, 0);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<2>, T, 0);
   if (e != cudaSuccess) return RA_ERR_CUDA;
   if (per_sm < 1) per_sm = 1;
   const int grid = sms * per_sm;
   if (mode == 0)
-    tiles3_kernel<0><<<grid, 128, 0, st>>>(T);
+    tiles3_kernel<0><<<grid, kT3Threads, 0, st>>>(Targs);
   else if (mode == 1)
-    tiles3_kernel<1><<<grid, 128, 0, st>>>(T);
+    tiles3_kernel<1><<<grid, kT3Threads, 0, st>>>(Targs);
   else
-    tiles3_kernel<2><<<grid, 128, 0, st>>>(T);
+    tiles3_kernel<2><<<grid, kT3Threads, 0, st>>>(Targs);
   ++g_launches;
   return cuda_status(cudaGetLastError());
 }

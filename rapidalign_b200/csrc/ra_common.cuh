@@ -117,6 +117,11 @@ struct Seg {
   int64_t ys, yspan, ycount;
 };
 
+// floats per point in the D <= 3 accumulator record: per block (self, then
+// cross) the sums (s, T0, T1, T2)
+constexpr int kAcc3Stride = 8;
+constexpr int kAcc3Block = 4;
+
 // Tile geometry of the D <= 3 kernel.
 constexpr int kTile = 64;          // rows per warp item and columns per tile
 constexpr int kSplitMax = 16;      // max column splits of one row tile

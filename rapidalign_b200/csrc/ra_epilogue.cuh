@@ -110,7 +110,7 @@ __device__ __forceinline__ void point_grads(const EpilogueArgs &A, int side, int
     const float *gp = (side == 0 ? A.Gx : A.Gy) + slot * A.DP;
     for (int d = 0; d < D && d < MAXD; ++d) xp[d] = gp[d];
   }
-  const int cross = A.packed3 ? 4 : 1 + A.DP;
+  const int cross = A.packed3 ? kAcc3Block : 1 + A.DP;
   const double s_self = acc[0], s_cross = acc[cross];
   for (int d = 0; d < D && d < MAXD; ++d) {
     const double Gs = xp[d] * s_self - (double)acc[1 + d];

@@ -31,13 +31,20 @@
 // Arithmetic per unique term (fwd+bwd): 3 sub + 3 mul/fma (r^2) + 1 EX2 +
 // 4 FMA (row s, T) + 4 FMA (column s, T) = 14 FP32-pipe ops, issued as
 // packed f32x2 instructions where both lanes of a row pair share operands.
-// Accumulation order is fixed except for the fp32 red.add of per-point row
-// sums at L2; K and S partials are fp64 and reduced in a fixed order.
+// Row sums accumulate in fp32 over an item (at most 4096 columns) and are
+// folded once into the fp64 K and S partials, which are reduced in a fixed
+// order; only the per-point fp32 red.add at L2 depends on timing.  The next
+// column tile is prefetched into L1 while the current one is processed.
 #pragma once
 
 #include "ra_common.cuh"
 
+
 namespace ra {
+
+// 4 warps per CTA, 3 CTAs (12 warps) per SM at <= 168 registers: measured
+// best on B200 against 14-16 warps at 128 registers (which spill).
+constexpr int kT3Threads = 128;
 
 struct Tiles3Args {
   const Item *items;
@@ -146,13 +153,13 @@ __device__ __forceinline__ void tiles3_coltile(
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       const int in_tile = c * 32 + q * 8 + pos;
-      if (col0 + in_tile < ccnt) red_add_v4(accC + in_tile * 8, cs[c], c0[c], c1[c], c2[c]);
+      if (col0 + in_tile < ccnt) red_add_v4(accC + in_tile * kAcc3Stride, cs[c], c0[c], c1[c], c2[c]);
     }
   }
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(128, 3) tiles3_kernel(Tiles3Args A) {
+__global__ void __launch_bounds__(kT3Threads, 3) tiles3_kernel(Tiles3Args A) {
   constexpr bool GRAD = Tiles3Mode<MODE>::GRAD;
   constexpr bool SIG = Tiles3Mode<MODE>::SIG;
   constexpr int NQ = Tiles3Mode<MODE>::NQ;
@@ -178,7 +185,7 @@ __global__ void __launch_bounds__(128, 3) tiles3_kernel(Tiles3Args A) {
     const ulonglong2 *__restrict__ ctiles = cols_x ? A.tiles_x : A.tiles_y;
     float *accR = rows_y ? A.acc_y : A.acc_x;
     float *accC = cols_x ? A.acc_x : A.acc_y;
-    const int off = blk == 0 ? 4 : 0;  // cross sums in [4, 8), self sums in [0, 4)
+    const int off = blk == 0 ? kAcc3Block : 0;  // cross block after the self block
 
     const int64_t nTc = ceil_div(ccnt, (int64_t)kTile);
     const int64_t S = splits_for(nTc);
@@ -218,43 +225,57 @@ __global__ void __launch_bounds__(128, 3) tiles3_kernel(Tiles3Args A) {
         }
       }
     }
-    f2_t st[4], stot[4], T0[4], T1[4], T2[4], sgt[4];
+    f2_t st[4], T0[4], T1[4], T2[4], sgt[4];
     const f2_t z2 = pk(0.f, 0.f);
 #pragma unroll
-    for (int rp = 0; rp < 4; ++rp) st[rp] = stot[rp] = T0[rp] = T1[rp] = T2[rp] = sgt[rp] = z2;
+    for (int rp = 0; rp < 4; ++rp) st[rp] = T0[rp] = T1[rp] = T2[rp] = sgt[rp] = z2;
     double ktot = 0.0, kd = 0.0, stot_sig = 0.0, sd = 0.0;
 
 #pragma unroll 1
     for (int64_t J = J0; J < J1; ++J) {
       const bool diag = sym && J == I;
       const ulonglong2 *ct = ctiles + (ctb + J) * TILE_U2;
-      float *accJ = accC + ((ctb + J) * kTile) * 8 + off;
+      if (J + 1 < J1) {
+        // one 128-byte line per lane covers the next tile (NQ * 64 * 16 bytes)
+        const char *nxt = reinterpret_cast<const char *>(ct + TILE_U2);
+        for (int l = lane; l < TILE_U2 / 8; l += 32)
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(nxt + l * 128));
+      }
+      float *accJ = accC + ((ctb + J) * kTile) * kAcc3Stride + off;
       if (diag)
         tiles3_coltile<MODE, true>(ct, J * kTile, ccnt, accJ, lane, X0, X1, X2, Aw, AX0, AX1,
                                    AX2, st, T0, T1, T2, sgt);
       else
         tiles3_coltile<MODE, false>(ct, J * kTile, ccnt, accJ, lane, X0, X1, X2, Aw, AX0, AX1,
                                     AX2, st, T0, T1, T2, sgt);
-      // fold the per-tile fp32 row sums into fp64 pair partials
+      if (diag) {  // the diagonal tile's share, counted once
 #pragma unroll
-      for (int rp = 0; rp < 4; ++rp) {
-        float s_lo, s_hi, a_lo, a_hi;
-        upk(st[rp], s_lo, s_hi);
-        upk(Aw[rp], a_lo, a_hi);
-        ktot = fma((double)a_lo, (double)s_lo, ktot);
-        ktot = fma((double)a_hi, (double)s_hi, ktot);
-        if (GRAD) stot[rp] = add2(stot[rp], st[rp]);
-        st[rp] = z2;
-        if (SIG) {
-          upk(sgt[rp], s_lo, s_hi);
-          stot_sig = fma((double)a_lo, (double)s_lo, stot_sig);
-          stot_sig = fma((double)a_hi, (double)s_hi, stot_sig);
-          sgt[rp] = z2;
+        for (int rp = 0; rp < 4; ++rp) {
+          float s_lo, s_hi, a_lo, a_hi;
+          upk(st[rp], s_lo, s_hi);
+          upk(Aw[rp], a_lo, a_hi);
+          kd = fma((double)a_lo, (double)s_lo, kd);
+          kd = fma((double)a_hi, (double)s_hi, kd);
+          if (SIG) {
+            upk(sgt[rp], s_lo, s_hi);
+            sd = fma((double)a_lo, (double)s_lo, sd);
+            sd = fma((double)a_hi, (double)s_hi, sd);
+          }
         }
       }
-      if (diag) {
-        kd = ktot;
-        sd = stot_sig;
+    }
+    // row sums accumulated in fp32 over the item: fold once into fp64
+#pragma unroll
+    for (int rp = 0; rp < 4; ++rp) {
+      float s_lo, s_hi, a_lo, a_hi;
+      upk(st[rp], s_lo, s_hi);
+      upk(Aw[rp], a_lo, a_hi);
+      ktot = fma((double)a_lo, (double)s_lo, ktot);
+      ktot = fma((double)a_hi, (double)s_hi, ktot);
+      if (SIG) {
+        upk(sgt[rp], s_lo, s_hi);
+        stot_sig = fma((double)a_lo, (double)s_lo, stot_sig);
+        stot_sig = fma((double)a_hi, (double)s_hi, stot_sig);
       }
     }
 
@@ -274,24 +295,25 @@ __global__ void __launch_bounds__(128, 3) tiles3_kernel(Tiles3Args A) {
       for (int rp = 0; rp < 4; ++rp) {
 #pragma unroll
         for (int o = 8; o <= 16; o <<= 1) {
-          stot[rp] = add2(stot[rp], __shfl_xor_sync(kFull, stot[rp], o));
+          st[rp] = add2(st[rp], __shfl_xor_sync(kFull, st[rp], o));
           T0[rp] = add2(T0[rp], __shfl_xor_sync(kFull, T0[rp], o));
           T1[rp] = add2(T1[rp], __shfl_xor_sync(kFull, T1[rp], o));
           T2[rp] = add2(T2[rp], __shfl_xor_sync(kFull, T2[rp], o));
         }
       }
-      float *accI = accR + ((rtb + I) * kTile) * 8 + off;
+      float *accI = accR + ((rtb + I) * kTile) * kAcc3Stride + off;
 #pragma unroll
       for (int rp = 0; rp < 4; ++rp) {
         if (rp == q) {
           const int r0 = p * 8 + 2 * rp;
           float s_lo, s_hi, t0l, t0h, t1l, t1h, t2l, t2h;
-          upk(stot[rp], s_lo, s_hi);
+          upk(st[rp], s_lo, s_hi);
           upk(T0[rp], t0l, t0h);
           upk(T1[rp], t1l, t1h);
           upk(T2[rp], t2l, t2h);
-          if (I * kTile + r0 < rcnt) red_add_v4(accI + r0 * 8, s_lo, t0l, t1l, t2l);
-          if (I * kTile + r0 + 1 < rcnt) red_add_v4(accI + (r0 + 1) * 8, s_hi, t0h, t1h, t2h);
+          if (I * kTile + r0 < rcnt) red_add_v4(accI + r0 * kAcc3Stride, s_lo, t0l, t1l, t2l);
+          if (I * kTile + r0 + 1 < rcnt)
+            red_add_v4(accI + (r0 + 1) * kAcc3Stride, s_hi, t0h, t1h, t2h);
         }
       }
     }
