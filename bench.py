@@ -196,6 +196,195 @@ def cpu_baseline(sample_graphs: int = GRAPHS_PER_GPU, seed: int = SEED, budget_s
 
 
 # ----------------------------------------------------------------------------
+# workloads (one "step" = one forward + backward through the public API)
+# ----------------------------------------------------------------------------
+
+def random_rotation(rng) -> np.ndarray:
+    """Uniform rotation in SO(3) from a normalised Gaussian quaternion."""
+    q = rng.standard_normal(4)
+    q /= np.linalg.norm(q)
+    w, x, y, z = q
+    return np.array([[1 - 2 * (y * y + z * z), 2 * (x * y - z * w), 2 * (x * z + y * w)],
+                     [2 * (x * y + z * w), 1 - 2 * (x * x + z * z), 2 * (y * z - x * w)],
+                     [2 * (x * z - y * w), 2 * (y * z + x * w), 1 - 2 * (x * x + y * y)]])
+
+
+class RaggedWorkload:
+    """4096 graphs per GPU (weak scaling), LPT-partitioned across ranks."""
+    scaling = "weak"
+
+    def __init__(self, rank, world, dev, graphs_per_gpu=GRAPHS_PER_GPU, dim=3, lo=32, hi=2048,
+                 sigma=SIGMA, center=True, name=None):
+        import torch
+        from rapidalign_b200.shard import lpt_partition
+        total = graphs_per_gpu * world
+        sizes = ragged_sizes(range(total), lo=lo, hi=hi)
+        cost = sizes[:, 0] ** 2 + sizes[:, 1] ** 2 + sizes[:, 0] * sizes[:, 1]
+        self.mine = np.sort(lpt_partition(cost, world)[rank])
+        x, y, bx, by, nx, ny = ragged_batch(self.mine, lo=lo, hi=hi, dim=dim)
+        self.full_local, self.unique_local = term_counts(nx, ny)
+        self.sigma, self.center, self.dim = sigma, center, dim
+        self.dev = dev
+        self.d = {k: torch.from_numpy(v).to(dev) for k, v in
+                  dict(x=x, y=y, bx=bx, by=by).items()}
+        self.h = {k: torch.from_numpy(v).pin_memory() for k, v in
+                  dict(x=x, y=y, bx=bx, by=by).items()}
+        self.result_host = torch.empty(len(self.mine), dtype=torch.float32).pin_memory()
+        self.config = {
+            "workload": name or (f"ragged PyG batch, {graphs_per_gpu} graphs per GPU, {lo}-{hi} "
+                                 f"points each, D={dim}, sigma={sigma}, "
+                                 f"{'centred' if center else 'uncentred'}, pyg_kde_mmd_loss "
+                                 "fwd+bwd"),
+            "graphs": total,
+        }
+
+    def step(self, t):
+        from rapidalign_b200 import pyg_kde_mmd_loss
+        xs = t["x"].detach().requires_grad_(True)
+        ys = t["y"].detach().requires_grad_(True)
+        loss, _, _, _ = pyg_kde_mmd_loss(xs, ys, src_batch=t["bx"], tgt_batch=t["by"],
+                                         sigma=self.sigma, center=self.center)
+        loss.sum().backward()
+        return loss
+
+    def tiles_time(self, reps):
+        from rapidalign_b200 import profiling
+        return profiling.tiles_time(self.d["x"], self.d["y"], self.d["bx"], self.d["by"],
+                                    self.sigma, reps=reps, center=self.center)
+
+
+class HugePairWorkload:
+    """One pair of N = M = 262144 points split across the ranks (strong
+    scaling): src ~ N(0, 1), tgt = R (src + 0.05 noise) with R uniform in
+    SO(3), sigma 0.2, centred."""
+    scaling = "strong"
+
+    def __init__(self, rank, world, dev, n=262144, sigma=0.2):
+        import torch
+        import torch.distributed as dist
+        rng = np.random.default_rng([SEED, 4])
+        src = rng.standard_normal((n, 3)).astype(np.float32)
+        R = random_rotation(rng)
+        tgt = ((src + 0.05 * rng.standard_normal((n, 3))) @ R.T).astype(np.float32)
+        self.group = dist.group.WORLD if world > 1 else None
+        self.world = world
+        full, unique = term_counts(np.array([n]), np.array([n]))
+        self.full_local, self.unique_local = full / world, unique / world
+        self.full_job, self.unique_job = full, unique
+        self.sigma = sigma
+        self.dev = dev
+        self.d = {"x": torch.from_numpy(src).to(dev), "y": torch.from_numpy(tgt).to(dev)}
+        self.h = {"x": torch.from_numpy(src).pin_memory(), "y": torch.from_numpy(tgt).pin_memory()}
+        self.result_host = torch.empty(1, dtype=torch.float32).pin_memory()
+        self.config = {"workload": f"single pair N = M = {n}, D=3, tgt = R(src + 0.05 noise), "
+                                   f"sigma={sigma}, centred, split over the GPUs by row tiles "
+                                   "(shard.split_pair_kde_mmd_loss) fwd+bwd",
+                       "points": n}
+
+    def step(self, t):
+        from rapidalign_b200.shard import split_pair_kde_mmd_loss
+        from rapidalign_b200 import kde_mmd_loss
+        xs = t["x"].detach().requires_grad_(True)
+        ys = t["y"].detach().requires_grad_(True)
+        if self.world > 1:
+            loss, _, _, _ = split_pair_kde_mmd_loss(xs, ys, sigma=self.sigma, center=True,
+                                                    group=self.group)
+        else:
+            loss, _, _, _ = kde_mmd_loss(xs, ys, sigma=self.sigma, center=True)
+        loss.backward()
+        return loss.reshape(1)
+
+    def tiles_time(self, reps):
+        from rapidalign_b200 import profiling
+        import torch.distributed as dist
+        rank = dist.get_rank() if self.world > 1 else 0
+        return profiling.tiles_time_pair(self.d["x"], self.d["y"], self.sigma, reps=reps,
+                                         shard_index=rank, shard_count=self.world)
+
+
+class DenseWorkload:
+    """Padded batch: B = 64 clouds of Nmax = 1024 points per GPU, valid lengths
+    uniform in [512, 1024] (prefix masks), tgt = src + 0.05 noise, sigma 0.25,
+    centred, kde_mmd_loss_dense fwd+bwd (weak scaling)."""
+    scaling = "weak"
+
+    def __init__(self, rank, world, dev, B=64, nmax=1024, sigma=SIGMA):
+        import torch
+        rng = np.random.default_rng([SEED, 2, rank])
+        x = rng.standard_normal((B, nmax, 3)).astype(np.float32)
+        y = (x + 0.05 * rng.standard_normal((B, nmax, 3))).astype(np.float32)
+        lx = rng.integers(512, nmax + 1, B)
+        ly = rng.integers(512, nmax + 1, B)
+        mx = np.arange(nmax)[None, :] < lx[:, None]
+        my = np.arange(nmax)[None, :] < ly[:, None]
+        self.full_local, self.unique_local = term_counts(lx, ly)
+        self.sigma = sigma
+        self.dev = dev
+        self.d = {k: torch.from_numpy(v).to(dev) for k, v in dict(x=x, y=y, mx=mx, my=my).items()}
+        self.h = {k: torch.from_numpy(v).pin_memory() for k, v in
+                  dict(x=x, y=y, mx=mx, my=my).items()}
+        self.result_host = torch.empty(B, dtype=torch.float32).pin_memory()
+        self.config = {"workload": f"dense padded batch, B={B} clouds of Nmax={nmax} per GPU, "
+                                   "valid 512-1024 (prefix masks), D=3, sigma=0.25, centred, "
+                                   "kde_mmd_loss_dense fwd+bwd", "clouds": B * world}
+
+    def step(self, t):
+        from rapidalign_b200 import kde_mmd_loss_dense
+        xs = t["x"].detach().requires_grad_(True)
+        ys = t["y"].detach().requires_grad_(True)
+        loss, _, _, _ = kde_mmd_loss_dense(xs, ys, t["mx"], t["my"], sigma=self.sigma,
+                                           center=True)
+        loss.sum().backward()
+        return loss
+
+    def tiles_time(self, reps):
+        return None
+
+
+class EmbedWorkload(RaggedWorkload):
+    """High-dimensional embeddings: 1024 graphs per GPU of 64-512 nodes, D=128,
+    x ~ N(0, 1/D), tgt = src + 0.1 noise (same sizes), sigma 1.0, uncentred."""
+
+    def __init__(self, rank, world, dev):
+        import torch
+        from rapidalign_b200.shard import lpt_partition
+        total = 1024 * world
+        rng_sizes = [int(np.random.default_rng([SEED, 5, g]).integers(64, 513))
+                     for g in range(total)]
+        sizes = np.array(rng_sizes)
+        cost = 3.0 * sizes.astype(np.float64) ** 2
+        self.mine = np.sort(lpt_partition(cost, world)[rank])
+        xs, ys = [], []
+        for g in self.mine:
+            r = np.random.default_rng([SEED, 5, int(g)])
+            n = int(r.integers(64, 513))
+            a = (r.standard_normal((n, 128)) / np.sqrt(128)).astype(np.float32)
+            xs.append(a)
+            ys.append((a + 0.1 * r.standard_normal((n, 128))).astype(np.float32))
+        nx = np.array([a.shape[0] for a in xs])
+        x, y = np.concatenate(xs), np.concatenate(ys)
+        bx = np.repeat(np.arange(len(xs)), nx)
+        self.full_local, self.unique_local = term_counts(nx, nx)
+        self.sigma, self.center, self.dim = 1.0, False, 128
+        self.dev = dev
+        self.d = {k: torch.from_numpy(v).to(dev) for k, v in
+                  dict(x=x, y=y, bx=bx, by=bx).items()}
+        self.h = {k: torch.from_numpy(v).pin_memory() for k, v in
+                  dict(x=x, y=y, bx=bx, by=bx).items()}
+        self.result_host = torch.empty(len(self.mine), dtype=torch.float32).pin_memory()
+        self.config = {"workload": "graph embeddings, 1024 graphs per GPU of 64-512 nodes, "
+                                   "D=128, sigma=1.0, uncentred, pyg_kde_mmd_loss fwd+bwd",
+                       "graphs": total}
+
+    def tiles_time(self, reps):
+        return None
+
+
+WORKLOADS = {"ragged": RaggedWorkload, "huge-pair": HugePairWorkload, "dense": DenseWorkload,
+             "embed128": EmbedWorkload}
+
+
+# ----------------------------------------------------------------------------
 # our arm
 # ----------------------------------------------------------------------------
 
@@ -216,40 +405,11 @@ def run_ours(args):
                                 device_id=dev)
 
     from rapidalign_b200 import _lib, build as ra_build
-    from rapidalign_b200 import pyg_kde_mmd_loss
-    from rapidalign_b200.shard import lpt_partition
     ra_build.build()
 
-    total_graphs = GRAPHS_PER_GPU * world
-    sizes = ragged_sizes(range(total_graphs))
-    cost = sizes[:, 0] ** 2 + sizes[:, 1] ** 2 + sizes[:, 0] * sizes[:, 1]
-    parts = lpt_partition(cost, world)
-    mine = np.sort(parts[rank])
-    x, y, bx, by, nx, ny = ragged_batch(mine)
-    full_local, unique_local = term_counts(nx, ny)
-
-    # device-resident inputs for `value`; pinned host copies for `e2e`
-    xd = torch.from_numpy(x).to(dev)
-    yd = torch.from_numpy(y).to(dev)
-    bxd = torch.from_numpy(bx).to(dev)
-    byd = torch.from_numpy(by).to(dev)
-    xh = torch.from_numpy(x).pin_memory()
-    yh = torch.from_numpy(y).pin_memory()
-    bxh = torch.from_numpy(bx).pin_memory()
-    byh = torch.from_numpy(by).pin_memory()
-    loss_h = torch.empty(len(mine), dtype=torch.float32).pin_memory()
+    wl = WORKLOADS[args.workload](rank, world, dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-
-    def step(xs, ys, bxs, bys):
-        xs = xs.detach().requires_grad_(True)
-        ys = ys.detach().requires_grad_(True)
-        loss, kxx, kyy, kxy = pyg_kde_mmd_loss(xs, ys, src_batch=bxs, tgt_batch=bys,
-                                               sigma=SIGMA, center=True)
-        loss.sum().backward()
-        return loss, xs.grad, ys.grad
-
     stream = torch.cuda.current_stream(dev)
-
     h2d_times = []
 
     def timed_loop(k, e2e):
@@ -261,16 +421,13 @@ def run_ours(args):
             e0.record(stream)
             eh = None
             if e2e:
-                xs = xh.to(dev, non_blocking=True)
-                ys = yh.to(dev, non_blocking=True)
-                b1 = bxh.to(dev, non_blocking=True)
-                b2 = byh.to(dev, non_blocking=True)
+                t = {k_: v.to(dev, non_blocking=True) for k_, v in wl.h.items()}
                 eh = torch.cuda.Event(enable_timing=True)
                 eh.record(stream)
-                loss, _, _ = step(xs, ys, b1, b2)
-                loss_h.copy_(loss.detach(), non_blocking=True)
+                res = wl.step(t)
+                wl.result_host.copy_(res.detach().reshape(-1), non_blocking=True)
             else:
-                step(xd, yd, bxd, byd)
+                wl.step(wl.d)
             e1.record(stream)
             evs.append((e0, e1, eh))
         torch.cuda.synchronize(dev)
@@ -279,16 +436,14 @@ def run_ours(args):
         return sum(a.elapsed_time(b) for a, b, _ in evs) / 1e3  # seconds
 
     for _ in range(args.warmup):
-        step(xd, yd, bxd, byd)
+        wl.step(wl.d)
     if args.profile_step:
         # one more step and exit: the command profiled by ncu (see profiles/)
-        step(xd, yd, bxd, byd)
+        wl.step(wl.d)
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.destroy_process_group()
         return
-    # hot-kernel duration: events bracketing one forward+backward of the
-    # fused pipeline (tiles kernel dominates, see profiles/)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -301,74 +456,33 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    for _ in range(max(1, args.warmup // 2)):
+    for _ in range(args.warmup):
         timed_loop(1, e2e=True)
     t_e2e = timed_loop(args.steps, e2e=True)
     clocks = sampler.stop() if sampler else None
 
-    # kernel-level timing of the dominant (tiles) kernel for the roofline
-    t_tiles = tiles_kernel_time(xd, yd, bxd, byd, dev, reps=max(3, args.steps // 2))
-
-    # FP32 peak of this GPU (packed-FMA probe)
+    # the dominant (tile) kernel alone, for the roofline; FP32 peak of this GPU
+    t_tiles = wl.tiles_time(max(3, args.steps // 2))
     peak_ops = fp32_peak(dev)
 
-    vals = torch.tensor([t_dev, t_e2e, full_local, unique_local, t_tiles, float(launches)],
-                        dtype=torch.float64, device=dev)
     if world > 1:
-        tmax = vals[:2].clone()
+        tmax = torch.tensor([t_dev, t_e2e], dtype=torch.float64, device=dev)
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        sums = vals[2:4].clone()
-        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
         t_dev, t_e2e = tmax.tolist()
+        sums = torch.tensor([wl.full_local, wl.unique_local], dtype=torch.float64, device=dev)
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
         full_all, unique_all = sums.tolist()
-        # one gather of the per-graph results (outside the timed region)
-        with torch.no_grad():
-            loss, *_ = pyg_kde_mmd_loss(xd, yd, src_batch=bxd, tgt_batch=byd, sigma=SIGMA)
-        n_max = GRAPHS_PER_GPU + 8
-        buf = torch.zeros(n_max, dtype=torch.float64, device=dev)
-        buf[:loss.numel()] = loss.to(torch.float64)
-        gathered = [torch.zeros_like(buf) for _ in range(world)]
-        dist.all_gather(gathered, buf)
     else:
-        full_all, unique_all = full_local, unique_local
+        full_all, unique_all = wl.full_local, wl.unique_local
 
     if rank == 0:
         K = args.steps
         value = full_all * K / t_dev
         e2e_value = full_all * K / t_e2e
-        # roofline of the tiles kernel on rank 0's share
-        achieved_ops = unique_local * FP32_OPS_PER_UNIQUE_TERM / t_tiles
-        line = {
-            "metric": "Gaussian kernel-term evals/sec fwd+bwd",
-            "value": value,
-            "unit": "terms/s",
-            "n_gpus": world,
-            "steps": K,
-            "warmup": args.warmup,
-            "ms_per_step": t_dev / K * 1e3,
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "f32 (fp64 sums)",
-            "data": "synthetic",
-            "config": {
-                "workload": f"ragged PyG batch, {GRAPHS_PER_GPU} graphs per GPU, 32-2048 "
-                            "points each, D=3, sigma=0.25, centred, pyg_kde_mmd_loss fwd+bwd",
-                "graphs": GRAPHS_PER_GPU * world,
-                "full_terms_per_step": full_all,
-                "unique_terms_per_step": unique_all,
-                "l2": "flushed between steps (512 MB write, outside the timed events)",
-                "sharding": "LPT partition of graph cost across ranks" if world > 1 else "none",
-                "seed": SEED,
-            },
-            "e2e": {"value": e2e_value, "unit": "terms/s",
-                    "ms_per_step": t_e2e / K * 1e3,
-                    "h2d_ms_per_step": (statistics.median(h2d_times[-K:]) if h2d_times else None),
-                    "h2d_bytes_per_step": int(xh.numel() * 4 + yh.numel() * 4 + bxh.numel() * 8
-                                              + byh.numel() * 8),
-                    "d2h_bytes_per_step": int(loss_h.numel() * 4)},
-            "gpu_launches": int(launches),
-            "roofline": {
+        roofline = None
+        if t_tiles:
+            achieved_ops = wl.unique_local * FP32_OPS_PER_UNIQUE_TERM / t_tiles
+            roofline = {
                 "bound": "fp32",
                 "achieved": achieved_ops / 1e12,
                 "peak": peak_ops / 1e12,
@@ -378,8 +492,40 @@ def run_ours(args):
                 "kernel": "tiles3_kernel<1> (fused fwd+bwd tile kernel)",
                 "kernel_ms": t_tiles * 1e3,
                 "ops_per_unique_term": FP32_OPS_PER_UNIQUE_TERM,
-                "traffic": read_traffic(),
-            },
+                "traffic": read_traffic() if args.workload == "ragged" else None,
+            }
+        config = dict(wl.config)
+        config.update({
+            "full_terms_per_step": full_all,
+            "unique_terms_per_step": unique_all,
+            "l2": "flushed between steps (512 MB write, outside the timed events)",
+            "sharding": ("none" if world == 1 else
+                         ("LPT partition of graphs across ranks" if wl.scaling == "weak"
+                          else "work items of the one pair split round-robin, one all-reduce")),
+            "seed": SEED,
+        })
+        line = {
+            "metric": "Gaussian kernel-term evals/sec fwd+bwd",
+            "value": value,
+            "unit": "terms/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": args.warmup,
+            "ms_per_step": t_dev / K * 1e3,
+            "higher_is_better": True,
+            "scaling": wl.scaling,
+            "vs_baseline": None,
+            "dtype": "f32 (fp64 sums)",
+            "data": "synthetic",
+            "config": config,
+            "e2e": {"value": e2e_value, "unit": "terms/s",
+                    "ms_per_step": t_e2e / K * 1e3,
+                    "h2d_ms_per_step": (statistics.median(h2d_times[-K:]) if h2d_times else None),
+                    "h2d_bytes_per_step": int(sum(v.numel() * v.element_size()
+                                                  for v in wl.h.values())),
+                    "d2h_bytes_per_step": int(wl.result_host.numel() * 4)},
+            "gpu_launches": int(launches),
+            "roofline": roofline,
             "clocks": clocks,
         }
         if not args.no_cpu_baseline:
@@ -388,16 +534,6 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-
-
-def tiles_kernel_time(xd, yd, bxd, byd, dev, reps=5):
-    """Average device time of the fused tile kernel alone, measured with CUDA
-    events around the forward with the plan/prep kernels excluded: the
-    forward is timed once as a whole and once with the kernel pipeline up to
-    the tile launch, by the library's two timing hooks."""
-    import torch
-    from rapidalign_b200 import profiling
-    return profiling.tiles_time(xd, yd, bxd, byd, SIGMA, reps=reps)
 
 
 def fp32_peak(dev) -> float:
@@ -494,6 +630,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="ragged", choices=sorted(WORKLOADS),
+                    help="ragged (default, the headline workload), huge-pair, dense, embed128")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--profile-step", action="store_true",

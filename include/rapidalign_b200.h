@@ -90,7 +90,9 @@ typedef struct ra_kde_desc {
   int32_t center;      /* 1: subtract the weighted centroid of each cloud first */
   int32_t need_grad;   /* 1: keep per-point state in the workspace for ra_kde_backward */
   int32_t need_sigma_grad; /* 1: also accumulate the sigma derivative */
-  int32_t reserved;
+  int32_t shard_index; /* splitting one problem over shard_count processes (GPUs): */
+  int32_t shard_count; /* this process evaluates work items shard_index, shard_index +
+                          shard_count, ...; 0 or 1 = no split (see ra_kde_forward) */
   double sigma;        /* bandwidth, > 0 */
 } ra_kde_desc;
 
@@ -137,6 +139,22 @@ RA_API int ra_kde_forward(const ra_kde_desc *desc, const ra_kde_inputs *in, doub
 RA_API int ra_kde_backward(const ra_kde_desc *desc, const ra_kde_inputs *in, const double *coef,
                     const ra_kde_grads *grads, void *workspace, size_t workspace_bytes,
                     ra_stream_t stream);
+
+/*
+ * Split evaluation of one problem over several GPUs (e.g. a single very large
+ * pair).  With desc->shard_count > 1, ra_kde_forward evaluates only this
+ * shard's work items and stops before forming K: every process then sums the
+ * two partial buffers reported by ra_kde_partials over the group (an
+ * all-reduce of fp64 and fp32 data, in place), and calls
+ * ra_kde_forward_finish to form K (and the backward state).  Inputs must be
+ * identical on all shards.  No counterpart in the reference (its kernels put a
+ * whole pair on one thread block, csrc/kde_similarity.cu:196-279).
+ */
+RA_API int ra_kde_partials(const ra_kde_desc *desc, void *workspace, size_t workspace_bytes,
+                           double **f64_buf, size_t *f64_count, float **f32_buf,
+                           size_t *f32_count);
+RA_API int ra_kde_forward_finish(const ra_kde_desc *desc, double *K, void *workspace,
+                                 size_t workspace_bytes, ra_stream_t stream);
 
 /*
  * ra_kde_forward with timing of the hot tile kernel: records two CUDA events

@@ -43,6 +43,9 @@ class Spec:
     # which device-detected errors can occur (and must be checked, at the
     # price of one synchronisation): user ptr offsets, SUM-normalised weights
     check_errors: bool = False
+    # split evaluation of one problem across a process group (see shard.py)
+    shard_index: int = 0
+    shard_count: int = 1
     weight_error_message: str = "weights must sum to a positive value per segment"
 
     def desc(self, need_grad: bool, need_sigma_grad: bool) -> _lib.RaKdeDesc:
@@ -59,7 +62,8 @@ class Spec:
         d.center = 1 if self.center else 0
         d.need_grad = 1 if need_grad else 0
         d.need_sigma_grad = 1 if need_sigma_grad else 0
-        d.reserved = 0
+        d.shard_index = self.shard_index
+        d.shard_count = self.shard_count
         d.sigma = float(self.sigma)
         return d
 
@@ -108,9 +112,31 @@ class _State:
         self.meta = meta
 
 
+def partial_buffers(lib, desc, ws: Tensor) -> Tuple[Tensor, Optional[Tensor]]:
+    """Views of the two workspace regions a split evaluation sums across its
+    group: the fp64 item partials and the fp32 per-point sums (or None)."""
+    f64, n64 = ctypes.c_void_p(), ctypes.c_size_t()
+    f32, n32 = ctypes.c_void_p(), ctypes.c_size_t()
+    rc = lib.ra_kde_partials(ctypes.byref(desc), ws.data_ptr(), ws.numel(), ctypes.byref(f64),
+                             ctypes.byref(n64), ctypes.byref(f32), ctypes.byref(n32))
+    _lib.check(rc, "kde partials")
+    base = ws.data_ptr()
+    o64 = f64.value - base
+    t64 = ws[o64:o64 + 8 * n64.value].view(torch.float64)
+    t32 = None
+    if n32.value:
+        o32 = f32.value - base
+        t32 = ws[o32:o32 + 4 * n32.value].view(torch.float32)
+    return t64, t32
+
+
 def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tensor],
-                 sigma_t: Optional[Tensor], spec: Spec, need_grad: bool):
-    """Run the fused forward; returns (K float64 [3P], state or None)."""
+                 sigma_t: Optional[Tensor], spec: Spec, need_grad: bool, reduce=None):
+    """Run the fused forward; returns (K float64 [3P], state or None).
+
+    With spec.shard_count > 1 the forward evaluates this shard's work items
+    only; `reduce(f64_view, f32_view)` must then sum the partial buffers
+    across the group in place before K is formed."""
     lib = _lib.load()
     device = x.device
     need_sigma_grad = need_grad and sigma_t is not None and sigma_t.requires_grad
@@ -128,6 +154,13 @@ def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tens
         rc = lib.ra_kde_forward(ctypes.byref(desc), ctypes.byref(inp), K.data_ptr(),
                                 ws.data_ptr(), ws.numel(), stream)
         _lib.check(rc, "kde forward")
+        if spec.shard_count > 1:
+            if reduce is None:
+                raise RuntimeError("a split evaluation needs a reduction of its partials")
+            reduce(*partial_buffers(lib, desc, ws))
+            rc = lib.ra_kde_forward_finish(ctypes.byref(desc), K.data_ptr(), ws.data_ptr(),
+                                           ws.numel(), stream)
+            _lib.check(rc, "kde forward finish")
         if spec.check_errors:
             _raise_data_error(lib.ra_kde_check(ws.data_ptr(), stream), spec)
     state = None
@@ -193,8 +226,8 @@ class KDESums(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tensor],
-                sigma_t: Optional[Tensor], spec: Spec, need_grad: bool):
-        K, state = forward_sums(x, y, w_x, w_y, sigma_t, spec, need_grad)
+                sigma_t: Optional[Tensor], spec: Spec, need_grad: bool, reduce=None):
+        K, state = forward_sums(x, y, w_x, w_y, sigma_t, spec, need_grad, reduce)
         ctx.state = state
         P = spec.num_pairs
         return K[:P], K[P:2 * P], K[2 * P:]
@@ -203,7 +236,7 @@ class KDESums(torch.autograd.Function):
     def backward(ctx, gKxx: Optional[Tensor], gKyy: Optional[Tensor], gKxy: Optional[Tensor]):
         state = ctx.state
         if state is None:
-            return None, None, None, None, None, None, None
+            return None, None, None, None, None, None, None, None
         P = state.spec.num_pairs
         device = state.keep[0].device
 
@@ -214,10 +247,10 @@ class KDESums(torch.autograd.Function):
 
         coef = torch.cat([g_or_zero(gKxx), g_or_zero(gKyy), g_or_zero(gKxy)])
         grads = backward_sums(state, coef, ctx.needs_input_grad[:5])
-        return grads + (None, None)
+        return grads + (None, None, None)
 
 
 def kde_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tensor],
-             sigma_t: Optional[Tensor], spec: Spec) -> Tuple[Tensor, Tensor, Tensor]:
+             sigma_t: Optional[Tensor], spec: Spec, reduce=None) -> Tuple[Tensor, Tensor, Tensor]:
     need = needs_grad(x, y, w_x, w_y, sigma_t)
-    return KDESums.apply(x, y, w_x, w_y, sigma_t, spec, need)
+    return KDESums.apply(x, y, w_x, w_y, sigma_t, spec, need, reduce)

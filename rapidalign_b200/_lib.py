@@ -54,7 +54,8 @@ class RaKdeDesc(ctypes.Structure):
         ("center", ctypes.c_int32),
         ("need_grad", ctypes.c_int32),
         ("need_sigma_grad", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("shard_index", ctypes.c_int32),
+        ("shard_count", ctypes.c_int32),
         ("sigma", ctypes.c_double),
     ]
 
@@ -96,6 +97,10 @@ SIGNATURES = {
     "ra_kde_backward": (ctypes.c_int, [ctypes.POINTER(RaKdeDesc), ctypes.POINTER(RaKdeInputs),
                                        _V, ctypes.POINTER(RaKdeGrads), _V, _SZ, _V]),
     "ra_kde_check": (ctypes.c_int, [_V, _V]),
+    "ra_kde_partials": (ctypes.c_int, [ctypes.POINTER(RaKdeDesc), _V, _SZ,
+                                       ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(_SZ),
+                                       ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(_SZ)]),
+    "ra_kde_forward_finish": (ctypes.c_int, [ctypes.POINTER(RaKdeDesc), _V, _V, _SZ, _V]),
     "ra_kde_forward_profiled": (ctypes.c_int, [ctypes.POINTER(RaKdeDesc),
                                                ctypes.POINTER(RaKdeInputs), _V, _V, _SZ, _V,
                                                ctypes.POINTER(ctypes.c_float)]),

@@ -67,6 +67,9 @@ bool desc_ok(const ra_kde_desc *d) {
   if (d->weights_x < 0 || d->weights_x > 3 || d->weights_y < 0 || d->weights_y > 3) return false;
   if (d->num_x > ((int64_t)1 << 40) || d->num_y > ((int64_t)1 << 40)) return false;
   if (d->num_pairs > ((int64_t)1 << 30)) return false;
+  if (d->shard_count < 0 || (d->shard_count > 1 &&
+                             (d->shard_index < 0 || d->shard_index >= d->shard_count)))
+    return false;
   return true;
 }
 
@@ -109,8 +112,9 @@ Layout make_layout(const ra_kde_desc *d) {
   L.tbase_y = take(sizeof(int64_t) * (P1 + 1));
   L.boff = take(sizeof(int64_t) * 4 * P1);
   L.items = take(sizeof(Item) * (size_t)L.max_items);
-  L.itemK = take(sizeof(double) * (size_t)L.max_items);
-  L.itemS = take(sizeof(double) * (size_t)L.max_items);
+  // itemK and itemS form one contiguous fp64 region (reduced across shards)
+  L.itemK = take(sizeof(double) * 2 * (size_t)L.max_items);
+  L.itemS = L.itemK + sizeof(double) * (size_t)L.max_items;
   L.Kws = take(sizeof(double) * 3 * P1);
   L.Sws = take(sizeof(double) * 3 * P1);
   L.coef = take(sizeof(double) * 3 * P1);
@@ -205,6 +209,9 @@ int launch_tilesg(int DP, int mode, int64_t grid, const TilesGArgs &T, cudaStrea
   ++g_launches;
   return cuda_status(cudaGetLastError());
 }
+
+int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy, double *Kxy,
+                void *ws, cudaStream_t st);
 
 int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, double *Kyy,
                  double *Kxy, void *ws, size_t ws_bytes, cudaStream_t st,
@@ -317,6 +324,13 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
   }
 
+  const bool sharded = d->shard_count > 1;
+  const int sh_idx = sharded ? d->shard_index : 0, sh_cnt = sharded ? d->shard_count : 1;
+  if (sharded &&
+      cudaMemsetAsync(at<char>(ws, L.itemK), 0, sizeof(double) * 2 * (size_t)L.max_items, st) !=
+          cudaSuccess)
+    return RA_ERR_CUDA;  // items of other shards contribute zeros to the reduction
+
   // ---- tiles ----
   if (ev0 != nullptr && cudaEventRecord(ev0, st) != cudaSuccess) return RA_ERR_CUDA;
   if (L.packed3) {
@@ -333,6 +347,8 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.acc_y = grad ? at<float>(ws, L.accY) : nullptr;
     T.itemK = at<double>(ws, L.itemK);
     T.itemS = at<double>(ws, L.itemS);
+    T.shard_index = sh_idx;
+    T.shard_count = sh_cnt;
     rc = launch_tiles3(mode, T, st);
     if (rc) return rc;
   } else {
@@ -349,12 +365,23 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.itemK = at<double>(ws, L.itemK);
     T.itemS = at<double>(ws, L.itemS);
     T.need_rows = grad ? 1 : 0;
+    T.shard_index = sh_idx;
+    T.shard_count = sh_cnt;
     rc = launch_tilesg(L.DP, mode, L.max_items, T, st);
     if (rc) return rc;
   }
 
   if (ev1 != nullptr && cudaEventRecord(ev1, st) != cudaSuccess) return RA_ERR_CUDA;
+  if (sharded) return RA_OK;  // partials are reduced by the caller, then finish_impl
+  return finish_impl(d, L, Kxx, Kyy, Kxy, ws, st);
+}
 
+// Per-pair K from the item partials, the K copy for the caller, the state flag.
+int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy, double *Kxy,
+                void *ws, cudaStream_t st) {
+  const int64_t P = d->num_pairs;
+  const bool grad = d->need_grad != 0;
+  if (P == 0) return RA_OK;
   // ---- finalize ----
   FinalizeArgs fa;
   fa.P = P;
@@ -575,6 +602,35 @@ int ra_kde_forward_profiled(const ra_kde_desc *desc, const ra_kde_inputs *in, do
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   return rc;
+}
+
+int ra_kde_partials(const ra_kde_desc *desc, void *workspace, size_t workspace_bytes,
+                    double **f64_buf, size_t *f64_count, float **f32_buf, size_t *f32_count) {
+  if (!desc_ok(desc) || f64_buf == nullptr || f64_count == nullptr || f32_buf == nullptr ||
+      f32_count == nullptr)
+    return RA_ERR_INVALID_ARGUMENT;
+  const Layout L = make_layout(desc);
+  if (workspace == nullptr || workspace_bytes < L.total) return RA_ERR_WORKSPACE;
+  *f64_buf = at<double>(workspace, L.itemK);
+  *f64_count = 2 * (size_t)L.max_items;
+  if (desc->need_grad) {
+    *f32_buf = at<float>(workspace, L.accX);
+    *f32_count = (L.accY + L.acc_y_bytes - L.accX) / sizeof(float);
+  } else {
+    *f32_buf = nullptr;
+    *f32_count = 0;
+  }
+  return RA_OK;
+}
+
+int ra_kde_forward_finish(const ra_kde_desc *desc, double *K, void *workspace,
+                          size_t workspace_bytes, ra_stream_t stream) {
+  if (!desc_ok(desc) || K == nullptr) return RA_ERR_INVALID_ARGUMENT;
+  const Layout L = make_layout(desc);
+  const int rc = check_common(desc, workspace, workspace_bytes, L.total);
+  if (rc) return rc;
+  const int64_t P = desc->num_pairs;
+  return finish_impl(desc, L, K, K + P, K + 2 * P, workspace, (cudaStream_t)stream);
 }
 
 int ra_kde_check(const void *workspace, ra_stream_t stream) {

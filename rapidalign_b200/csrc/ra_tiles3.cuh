@@ -45,6 +45,10 @@ namespace ra {
 // 4 warps per CTA, 3 CTAs (12 warps) per SM at <= 168 registers: measured
 // best on B200 against 14-16 warps at 128 registers (which spill).
 constexpr int kT3Threads = 128;
+#ifndef RA_T3_MINB
+#define RA_T3_MINB 3
+#endif
+constexpr int kT3MinBlocks = RA_T3_MINB;
 
 struct Tiles3Args {
   const Item *items;
@@ -55,6 +59,7 @@ struct Tiles3Args {
   const ulonglong2 *tiles_x, *tiles_y;  // [tiles][NQ][64]
   float *acc_x, *acc_y;                 // [tiles * 64][8]: self (s, T0..T2), cross (s, T0..T2)
   double *itemK, *itemS;
+  int shard_index, shard_count;  // this process evaluates items shard_index + k * shard_count
 };
 
 // MODE 0: K only.  MODE 1: K + per-point sums.  MODE 2: also S (sigma grad).
@@ -67,7 +72,7 @@ struct Tiles3Mode {
 
 template <int MODE, bool DIAG>
 __device__ __forceinline__ void tiles3_coltile(
-    const ulonglong2 *__restrict__ ct, const int64_t col0, const int64_t ccnt,
+    const ulonglong2 *__restrict__ ct, const int col0, const int ccnt,
     float *__restrict__ accC, const int lane, const f2_t (&X0)[4], const f2_t (&X1)[4],
     const f2_t (&X2)[4], const f2_t (&Aw)[4], const f2_t (&AX0)[4], const f2_t (&AX1)[4],
     const f2_t (&AX2)[4], f2_t (&st)[4], f2_t (&T0)[4], f2_t (&T1)[4], f2_t (&T2)[4],
@@ -159,7 +164,7 @@ __device__ __forceinline__ void tiles3_coltile(
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kT3Threads, 3) tiles3_kernel(Tiles3Args A) {
+__global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3Args A) {
   constexpr bool GRAD = Tiles3Mode<MODE>::GRAD;
   constexpr bool SIG = Tiles3Mode<MODE>::SIG;
   constexpr int NQ = Tiles3Mode<MODE>::NQ;
@@ -168,10 +173,11 @@ __global__ void __launch_bounds__(kT3Threads, 3) tiles3_kernel(Tiles3Args A) {
   const int q = lane >> 3, p = lane & 7;
   const int64_t total = *A.n_items;
   for (;;) {
-    unsigned it = 0;
-    if (lane == 0) it = atomicAdd(A.ticket, 1u);
-    it = __shfl_sync(kFull, it, 0);
-    if ((int64_t)it >= total) break;
+    unsigned ticket = 0;
+    if (lane == 0) ticket = atomicAdd(A.ticket, 1u);
+    ticket = __shfl_sync(kFull, ticket, 0);
+    const int64_t it = A.shard_index + (int64_t)ticket * A.shard_count;
+    if (it >= total) break;
     const Item item = A.items[it];
     const Seg sg = A.seg[item.pair];
     const int blk = item.block;
@@ -187,12 +193,13 @@ __global__ void __launch_bounds__(kT3Threads, 3) tiles3_kernel(Tiles3Args A) {
     float *accC = cols_x ? A.acc_x : A.acc_y;
     const int off = blk == 0 ? kAcc3Block : 0;  // cross block after the self block
 
-    const int64_t nTc = ceil_div(ccnt, (int64_t)kTile);
-    const int64_t S = splits_for(nTc);
-    const int64_t L = ceil_div(nTc, S);
-    const int64_t I = item.tile;
-    int64_t J0 = (int64_t)item.split * L;
-    const int64_t J1 = J0 + L < nTc ? J0 + L : nTc;
+    // 32-bit tile/column indices: a pair's cloud has < 2^31 points
+    const int nTc = (int)ceil_div(ccnt, (int64_t)kTile);
+    const int S = (int)splits_for(nTc);
+    const int L = (nTc + S - 1) / S;
+    const int I = item.tile;
+    int J0 = item.split * L;
+    const int J1 = J0 + L < nTc ? J0 + L : nTc;
     if (sym && J0 < I) J0 = I;
     if (J0 >= J1) {
       if (lane == 0) {
@@ -201,6 +208,9 @@ __global__ void __launch_bounds__(kT3Threads, 3) tiles3_kernel(Tiles3Args A) {
       }
       continue;
     }
+    const int cc = (int)ccnt;
+    const ulonglong2 *__restrict__ ct0 = ctiles + ctb * TILE_U2;  // the pair's first column tile
+    float *accC0 = accC + ctb * (kTile * kAcc3Stride) + off;
 
     // ---- rows: 8 per lane as 4 packed pairs (padding rows have zero weight) --
     f2_t X0[4], X1[4], X2[4], Aw[4], AX0[4], AX1[4], AX2[4];
@@ -231,38 +241,38 @@ __global__ void __launch_bounds__(kT3Threads, 3) tiles3_kernel(Tiles3Args A) {
     for (int rp = 0; rp < 4; ++rp) st[rp] = T0[rp] = T1[rp] = T2[rp] = sgt[rp] = z2;
     double ktot = 0.0, kd = 0.0, stot_sig = 0.0, sd = 0.0;
 
+    // ---- the diagonal tile of a self block first (rows only, counted once) --
+    if (sym && J0 == I) {
+      tiles3_coltile<MODE, true>(ct0 + I * TILE_U2, I * kTile, cc,
+                                 accC0 + I * (kTile * kAcc3Stride), lane, X0, X1, X2, Aw, AX0,
+                                 AX1, AX2, st, T0, T1, T2, sgt);
+#pragma unroll
+      for (int rp = 0; rp < 4; ++rp) {
+        float s_lo, s_hi, a_lo, a_hi;
+        upk(st[rp], s_lo, s_hi);
+        upk(Aw[rp], a_lo, a_hi);
+        kd = fma((double)a_lo, (double)s_lo, kd);
+        kd = fma((double)a_hi, (double)s_hi, kd);
+        if (SIG) {
+          upk(sgt[rp], s_lo, s_hi);
+          sd = fma((double)a_lo, (double)s_lo, sd);
+          sd = fma((double)a_hi, (double)s_hi, sd);
+        }
+      }
+      ++J0;
+    }
+    // ---- off-diagonal tiles: rows and columns ------------------------------
 #pragma unroll 1
-    for (int64_t J = J0; J < J1; ++J) {
-      const bool diag = sym && J == I;
-      const ulonglong2 *ct = ctiles + (ctb + J) * TILE_U2;
+    for (int J = J0; J < J1; ++J) {
+      const ulonglong2 *ct = ct0 + J * TILE_U2;
       if (J + 1 < J1) {
         // one 128-byte line per lane covers the next tile (NQ * 64 * 16 bytes)
         const char *nxt = reinterpret_cast<const char *>(ct + TILE_U2);
         for (int l = lane; l < TILE_U2 / 8; l += 32)
           asm volatile("prefetch.global.L1 [%0];" ::"l"(nxt + l * 128));
       }
-      float *accJ = accC + ((ctb + J) * kTile) * kAcc3Stride + off;
-      if (diag)
-        tiles3_coltile<MODE, true>(ct, J * kTile, ccnt, accJ, lane, X0, X1, X2, Aw, AX0, AX1,
-                                   AX2, st, T0, T1, T2, sgt);
-      else
-        tiles3_coltile<MODE, false>(ct, J * kTile, ccnt, accJ, lane, X0, X1, X2, Aw, AX0, AX1,
-                                    AX2, st, T0, T1, T2, sgt);
-      if (diag) {  // the diagonal tile's share, counted once
-#pragma unroll
-        for (int rp = 0; rp < 4; ++rp) {
-          float s_lo, s_hi, a_lo, a_hi;
-          upk(st[rp], s_lo, s_hi);
-          upk(Aw[rp], a_lo, a_hi);
-          kd = fma((double)a_lo, (double)s_lo, kd);
-          kd = fma((double)a_hi, (double)s_hi, kd);
-          if (SIG) {
-            upk(sgt[rp], s_lo, s_hi);
-            sd = fma((double)a_lo, (double)s_lo, sd);
-            sd = fma((double)a_hi, (double)s_hi, sd);
-          }
-        }
-      }
+      tiles3_coltile<MODE, false>(ct, J * kTile, cc, accC0 + J * (kTile * kAcc3Stride), lane,
+                                  X0, X1, X2, Aw, AX0, AX1, AX2, st, T0, T1, T2, sgt);
     }
     // row sums accumulated in fp32 over the item: fold once into fp64
 #pragma unroll
@@ -311,8 +321,8 @@ __global__ void __launch_bounds__(kT3Threads, 3) tiles3_kernel(Tiles3Args A) {
           upk(T0[rp], t0l, t0h);
           upk(T1[rp], t1l, t1h);
           upk(T2[rp], t2l, t2h);
-          if (I * kTile + r0 < rcnt) red_add_v4(accI + r0 * kAcc3Stride, s_lo, t0l, t1l, t2l);
-          if (I * kTile + r0 + 1 < rcnt)
+          if ((int64_t)I * kTile + r0 < rcnt) red_add_v4(accI + r0 * kAcc3Stride, s_lo, t0l, t1l, t2l);
+          if ((int64_t)I * kTile + r0 + 1 < rcnt)
             red_add_v4(accI + (r0 + 1) * kAcc3Stride, s_hi, t0h, t1h, t2h);
         }
       }

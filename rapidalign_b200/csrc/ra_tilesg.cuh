@@ -19,6 +19,7 @@ struct TilesGArgs {
   float *accX, *accY;    // [num][2 + 2*DP]: self (s, T[DP]), cross (s, T[DP])
   double *itemK, *itemS;
   int need_rows;         // 1: write the per-point sums (backward requested)
+  int shard_index, shard_count;  // evaluate only items shard_index + k * shard_count
 };
 
 template <int DP, int MODE>
@@ -28,7 +29,7 @@ __global__ void __launch_bounds__(kGenRows) tilesg_kernel(TilesGArgs A) {
   __shared__ float bcol[kGenCols];
   __shared__ double red[kGenRows / 32 * 2];
   const int64_t it = blockIdx.x;
-  if (it >= *A.n_items) return;
+  if (it >= *A.n_items || it % A.shard_count != A.shard_index) return;
   const Item item = A.items[it];
   const Seg sg = A.seg[item.pair];
   const int o = item.block;  // 0: x-y, 1: x-x, 2: y-y, 3: y-x

@@ -38,3 +38,30 @@ def tiles_time(x: torch.Tensor, y: torch.Tensor, batch_x: torch.Tensor, batch_y:
             if r > 0:  # first run warms up
                 total += ms.value
     return total / reps / 1e3
+
+
+def tiles_time_pair(x: torch.Tensor, y: torch.Tensor, sigma: float, reps: int = 3,
+                    center: bool = True, shard_index: int = 0, shard_count: int = 1) -> float:
+    """Mean seconds of the tile kernel for one pair (kde_mmd_loss with uniform
+    weights and gradients), or of this shard's items of a split evaluation."""
+    lib = _lib.load()
+    dev = x.device
+    spec = Spec(layout=_lib.RA_LAYOUT_DENSE, num_pairs=1, dim=x.shape[1], num_x=x.shape[0],
+                num_y=y.shape[0], nmax_x=x.shape[0], nmax_y=y.shape[0], center=center,
+                sigma=sigma, shard_index=shard_index, shard_count=shard_count)
+    x32, y32 = _f32(x), _f32(y)
+    desc = spec.desc(True, False)
+    inp = _inputs(x32, y32, None, None, spec)
+    ws = _lib.workspace(lib.ra_kde_workspace_bytes(ctypes.byref(desc)), dev)
+    K = torch.empty(3, dtype=torch.float64, device=dev)
+    ms = ctypes.c_float(0.0)
+    total = 0.0
+    with torch.cuda.device(dev):
+        for r in range(reps + 1):
+            rc = lib.ra_kde_forward_profiled(ctypes.byref(desc), ctypes.byref(inp), K.data_ptr(),
+                                             ws.data_ptr(), ws.numel(),
+                                             _lib.stream_handle(dev), ctypes.byref(ms))
+            _lib.check(rc, "profiled forward")
+            if r > 0:
+                total += ms.value
+    return total / reps / 1e3

@@ -1,6 +1,14 @@
-"""Multi-GPU sharding of ragged batches: graphs are independent, so each rank
-computes a share of the pairs with no collective in the data path; one
-all_gather returns the per-graph results to every rank afterwards.
+"""Multi-GPU execution.
+
+Ragged batches: graphs are independent, so each rank computes a share of the
+pairs with no collective in the data path; one all_gather returns the
+per-graph results to every rank afterwards.
+
+One very large pair (split_pair_kde_mmd_loss): every rank holds the same two
+clouds and evaluates every world-th work item (64-row tiles of the x-y, x-x
+and y-y blocks, column-split); one all_reduce of the fp64 item partials and
+one of the fp32 per-point sums complete the sums on every rank, which then
+forms K, the loss and (locally, O(N)) the full gradients.
 
 The partition is a greedy longest-processing-time assignment of the graph
 costs N_i^2 + M_i^2 + N_i M_i (the kernel-term count) to the least-loaded
@@ -14,7 +22,7 @@ from typing import Callable, List, Optional, Sequence
 import numpy as np
 import torch
 
-__all__ = ["lpt_partition", "graph_costs", "sharded_pair_results"]
+__all__ = ["lpt_partition", "graph_costs", "sharded_pair_results", "split_pair_kde_mmd_loss"]
 
 
 def graph_costs(nx: Sequence[int], ny: Sequence[int]) -> np.ndarray:
@@ -66,3 +74,44 @@ def sharded_pair_results(num_graphs: int, costs: Sequence[float],
         if len(p):
             out[torch.as_tensor(p, device=local.device)] = gathered[r][:len(p)]
     return out
+
+
+def split_pair_kde_mmd_loss(x: torch.Tensor, y: torch.Tensor, x_w=None, y_w=None,
+                            sigma: float = 0.2, center: bool = True, cosine: bool = False,
+                            eps: float = 1e-8, group=None):
+    """kde_mmd_loss (rapidalign/kde.py:39-109) for one pair split across the
+    ranks of `group` (one process per GPU, NCCL).  Inputs must be identical on
+    all ranks; every rank returns the full (loss, Kxx, Kyy, Kxy) and, through
+    autograd, the full gradients."""
+    import torch.distributed as dist
+    from . import _lib
+    from ._core import Spec, kde_sums
+    from .kde import _loss_from_k, _sigma_value
+    if x.ndim != 2 or y.ndim != 2 or x.size(-1) != y.size(-1):
+        raise ValueError("x and y must be (N,d) and (M,d) with same d")
+    if (isinstance(sigma, torch.Tensor) and bool((sigma <= 0).any())) or \
+            (not isinstance(sigma, torch.Tensor) and not sigma > 0):
+        raise ValueError("sigma must be positive")
+    device = _lib.require_cuda(x, y, x_w, y_w)
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    sig, sig_t = _sigma_value(sigma, device)
+    spec = Spec(
+        layout=_lib.RA_LAYOUT_DENSE, num_pairs=1, dim=x.shape[1], num_x=x.shape[0],
+        num_y=y.shape[0], nmax_x=x.shape[0], nmax_y=y.shape[0],
+        weights_x=_lib.RA_WEIGHTS_SUM if x_w is not None else _lib.RA_WEIGHTS_UNIFORM,
+        weights_y=_lib.RA_WEIGHTS_SUM if y_w is not None else _lib.RA_WEIGHTS_UNIFORM,
+        center=center, sigma=sig, check_errors=(x_w is not None or y_w is not None),
+        weight_error_message="weights must sum to a positive value",
+        shard_index=rank, shard_count=world)
+
+    def reduce(f64, f32):
+        dist.all_reduce(f64, group=group)
+        if f32 is not None:
+            dist.all_reduce(f32, group=group)
+
+    Kxx, Kyy, Kxy = kde_sums(x, y, x_w, y_w, sig_t, spec,
+                             reduce=reduce if world > 1 else None)
+    loss = _loss_from_k(Kxx, Kyy, Kxy, cosine, eps)
+    dtype = x.dtype
+    return loss[0].to(dtype), Kxx[0].to(dtype), Kyy[0].to(dtype), Kxy[0].to(dtype)

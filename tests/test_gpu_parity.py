@@ -266,3 +266,61 @@ def test_fp64_inputs_and_dtypes(cuda_device):
     assert loss.dtype == torch.float64 and loss.dim() == 0
     loss.backward()
     assert x.grad.dtype == torch.float64 and x.grad.shape == x.shape
+
+
+def test_split_evaluation_matches_unsplit(cuda_device):
+    """One pair evaluated as two shards (emulated in one process: the second
+    shard's partial sums are added by hand) equals the unsplit evaluation,
+    gradients included (the all-reduce path of shard.split_pair_kde_mmd_loss)."""
+    from rapidalign_b200 import _lib
+    from rapidalign_b200._core import Spec, backward_sums, forward_sums
+    rng = np.random.default_rng(11)
+    n, m = 5000, 4700
+    dev = cuda_device
+    x = torch.from_numpy(rng.standard_normal((n, 3)).astype(np.float32)).to(dev)
+    y = torch.from_numpy(rng.standard_normal((m, 3)).astype(np.float32)).to(dev)
+    wx = torch.from_numpy((rng.random(n) + 0.1).astype(np.float32)).to(dev)
+
+    def spec(idx, cnt):
+        return Spec(layout=_lib.RA_LAYOUT_DENSE, num_pairs=1, dim=3, num_x=n, num_y=m, nmax_x=n,
+                    nmax_y=m, weights_x=_lib.RA_WEIGHTS_SUM, weights_y=_lib.RA_WEIGHTS_UNIFORM,
+                    center=True, sigma=0.2, shard_index=idx, shard_count=cnt)
+
+    K_ref, st_ref = forward_sums(x, y, wx, None, None, spec(0, 1), True)
+    stash = {}
+
+    def grab(f64, f32):
+        stash["f64"], stash["f32"] = f64.clone(), f32.clone()
+
+    def add(f64, f32):
+        f64 += stash["f64"]
+        f32 += stash["f32"]
+
+    forward_sums(x, y, wx, None, None, spec(1, 2), True, reduce=grab)
+    K_sp, st_sp = forward_sums(x, y, wx, None, None, spec(0, 2), True, reduce=add)
+    assert_k(_np(K_sp), _np(K_ref))
+    coef = torch.tensor([1.0, 1.0, -2.0], dtype=torch.float64, device=dev)
+    need = (True, True, True, False, False)
+    g_ref = backward_sums(st_ref, coef, need)
+    g_sp = backward_sums(st_sp, coef, need)
+    for a, b in zip(g_sp[:3], g_ref[:3]):
+        assert_grad(_np(a), _np(b))
+
+
+def test_mid_size_single_pair_matches_oracle(cuda_device):
+    """N = M = 20000: many 64-row items and column splits of one pair."""
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(12)
+    n = 20000
+    x = rng.standard_normal((n, 3)).astype(np.float32)
+    y = (x + 0.05 * rng.standard_normal((n, 3))).astype(np.float32)
+    dev = cuda_device
+    xt, yt = _cuda(x, dev, True), _cuda(y, dev, True)
+    loss, Kxx, Kyy, Kxy = ra.kde_mmd_loss(xt, yt, sigma=0.2, center=True)
+    loss.backward()
+    r = O.kde_mmd_loss(x, y, sigma=0.2, center=True, upstream=[1.0, 0.0, 0.0, 0.0])
+    assert_k(_np(Kxx), r.Kxx)
+    assert_k(_np(Kxy), r.Kxy)
+    assert_loss(_np(loss), r.loss, r.Kxx, r.Kyy)
+    assert_grad(_np(xt.grad), r.grad_x)
+    assert_grad(_np(yt.grad), r.grad_y)
