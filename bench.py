@@ -20,7 +20,7 @@ gathered once after the timed region.
 
 Metric: full kernel terms (N^2 + M^2 + N M per graph, the reference's count)
 per second over the whole job.  The roofline fraction uses the unique terms
-(N(N+1)/2 + M(M+1)/2 + N M) at 14 FP32-pipe operations each, against the FP32
+(N(N+1)/2 + M(M+1)/2 + N M) at 16 FP32-pipe operations each, against the FP32
 rate measured on the same GPU by a packed-FMA probe kernel.
 """
 from __future__ import annotations
@@ -43,7 +43,9 @@ if ROOT not in sys.path:
 GRAPHS_PER_GPU = 4096
 SIGMA = 0.25
 SEED = 20261201
-FP32_OPS_PER_UNIQUE_TERM = 14  # 3 sub + 3 (mul, fma, fma) + 4 row FMA + 4 column FMA
+# per unique term: 3 sub + 3 (mul, fma, fma) for r^2, then w = b k, s += w,
+# G += w d (5) for the row and the same 5 for the column
+FP32_OPS_PER_UNIQUE_TERM = 16
 L2_FLUSH_BYTES = 512 << 20     # > 126 MB L2
 
 

@@ -40,7 +40,7 @@ int generic_dp(int D) {
 struct Layout {
   bool packed3;
   int DP;
-  int nq;           // packed3: arrays per tile (4 with gradients, 2 without)
+  int nq;           // packed3: 16-byte arrays per tile
   int acc_stride;
   int64_t max_items;
   int64_t max_tiles_x, max_tiles_y;  // packed3: bound on the padded tiles
@@ -95,7 +95,7 @@ Layout make_layout(const ra_kde_desc *d) {
   L.max_tiles_x = L.packed3 ? (tx > 0 ? tx : 1) : 0;
   L.max_tiles_y = L.packed3 ? (ty > 0 ? ty : 1) : 0;
   const bool grad = d->need_grad != 0;
-  L.nq = grad ? 4 : 2;
+  L.nq = kT3Arrays;
   size_t o = 0;
   auto take = [&](size_t bytes) {
     size_t at = o;

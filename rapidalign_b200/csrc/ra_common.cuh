@@ -118,7 +118,7 @@ struct Seg {
 };
 
 // floats per point in the D <= 3 accumulator record: per block (self, then
-// cross) the sums (s, T0, T1, T2)
+// cross) the sums (s, G0, G1, G2)
 constexpr int kAcc3Stride = 8;
 constexpr int kAcc3Block = 4;
 

@@ -1,8 +1,9 @@
 // ra_epilogue.cuh -- per-pair finalisation of the K/S sums and the backward
 // epilogue that turns the per-point row sums into gradients.
 //
-// Backward math (pre-scaled coordinates x' = c (x~ - 0), c = sqrt(log2 e / (2 sigma^2))):
-//   G'_i  = x'_i s_i - T_i = c * sum_j w_j k_ij (x~_i - y~_j)
+// Backward math (pre-scaled coordinates x' = c (x~ - anchor), c = sqrt(log2 e / (2 sigma^2))):
+//   G'_i  = c * sum_j w_j k_ij (x~_i - y~_j), accumulated directly by the D <= 3
+//           kernel and as x'_i s_i - T_i (T = sum w k y') by the generic one
 //   dL/dx~_i = -(a_i / (c sigma^2)) (2 cxx G'_self,i + cxy G'_cross,i)
 //   dL/da_i  = 2 cxx s_self,i + cxy s_cross,i                (kde_gradients.py:98-113)
 // then the centering Jacobian of x~ = x - sum_k a_k x_k (kde.py:77-81, 202-208):
@@ -113,8 +114,14 @@ __device__ __forceinline__ void point_grads(const EpilogueArgs &A, int side, int
   const int cross = A.packed3 ? kAcc3Block : 1 + A.DP;
   const double s_self = acc[0], s_cross = acc[cross];
   for (int d = 0; d < D && d < MAXD; ++d) {
-    const double Gs = xp[d] * s_self - (double)acc[1 + d];
-    const double Gc = xp[d] * s_cross - (double)acc[cross + 1 + d];
+    double Gs, Gc;
+    if (A.packed3) {  // difference form: G = sum w k (x' - y') directly
+      Gs = acc[1 + d];
+      Gc = acc[cross + 1 + d];
+    } else {          // folded form: G = x' s - sum w k y'
+      Gs = xp[d] * s_self - (double)acc[1 + d];
+      Gc = xp[d] * s_cross - (double)acc[cross + 1 + d];
+    }
     gxt[d] = -a * k_x * (cs * Gs + cc * Gc);
   }
   ga = cs * s_self + cc * s_cross;

@@ -239,10 +239,8 @@ __global__ void __launch_bounds__(NT) prep_kernel(PrepArgs A) {
 // ---------------------------------------------------------------------------
 // D <= 3 tile layout.  Each cloud is cut into 64-point tiles, zero-weight
 // padded; pair p's x tiles start at tile tbase_x[p] (exclusive scan of
-// ceil(count / 64)).  A tile stores NQ arrays of 64 duplicated pairs
-// (16 bytes per point each):
-//   q = 0: {x', x', y', y'}      q = 1: {z', z', a, a}
-//   q = 2: {a x', a x', a y', a y'}   q = 3: {a z', a z', 0, 0}   (gradients only)
+// ceil(count / 64)).  A tile stores two arrays of 64 duplicated pairs
+// (16 bytes per point each):  {x', x', y', y'}  and  {z', z', w, w}
 // so one column feeds packed f32x2 arithmetic against two rows, and a warp
 // reads any column of a tile at an immediate offset from the tile base.
 // ---------------------------------------------------------------------------
@@ -257,7 +255,7 @@ struct PackArgs {
   const double *meta;
   const int64_t *tbase_x, *tbase_y;  // [P + 1]
   int64_t max_tiles_x, max_tiles_y;
-  ulonglong2 *tiles_x, *tiles_y;     // [tiles][nq][64]
+  ulonglong2 *tiles_x, *tiles_y;     // [tiles][nq = 2][64]
 };
 
 template <int NT>
@@ -299,11 +297,6 @@ __global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
     ulonglong2 *tp = tiles + t * (int64_t)(nq * kTile) + (i % kTile);
     tp[0] = make_ulonglong2(pk2u(c0, c0), pk2u(c1, c1));
     tp[kTile] = make_ulonglong2(pk2u(c2, c2), pk2u(a, a));
-    if (nq > 2) {
-      const float b0 = a * c0, b1 = a * c1, b2 = a * c2;
-      tp[2 * kTile] = make_ulonglong2(pk2u(b0, b0), pk2u(b1, b1));
-      tp[3 * kTile] = make_ulonglong2(pk2u(b2, b2), 0ull);
-    }
   }
 }
 
