@@ -95,6 +95,36 @@ def ragged_batch(graph_ids, seed: int = SEED, **kw):
     return x, y, bx, by, nx, ny
 
 
+def huge_pair_data(n: int = 262144):
+    """The huge-pair workload's clouds: src ~ N(0, 1), tgt = R (src + 0.05
+    noise) with R uniform in SO(3)."""
+    rng = np.random.default_rng([SEED, 4])
+    src = rng.standard_normal((n, 3)).astype(np.float32)
+    R = random_rotation(rng)
+    tgt = ((src + 0.05 * rng.standard_normal((n, 3))) @ R.T).astype(np.float32)
+    return src, tgt
+
+
+def dense_data(rank: int, B: int = 64, nmax: int = 1024):
+    """The dense workload's padded batch of one rank: x, y (B, nmax, 3) and the
+    valid lengths lx, ly (prefix masks)."""
+    rng = np.random.default_rng([SEED, 2, rank])
+    x = rng.standard_normal((B, nmax, 3)).astype(np.float32)
+    y = (x + 0.05 * rng.standard_normal((B, nmax, 3))).astype(np.float32)
+    lx = rng.integers(512, nmax + 1, B)
+    ly = rng.integers(512, nmax + 1, B)
+    return x, y, lx, ly
+
+
+def embed_graph(g: int):
+    """Graph g of the embedding workload: n in [64, 512] nodes, D = 128,
+    x ~ N(0, 1/D), tgt = src + 0.1 noise."""
+    r = np.random.default_rng([SEED, 5, int(g)])
+    n = int(r.integers(64, 513))
+    a = (r.standard_normal((n, 128)) / np.sqrt(128)).astype(np.float32)
+    return a, (a + 0.1 * r.standard_normal((n, 128))).astype(np.float32)
+
+
 def term_counts(nx: np.ndarray, ny: np.ndarray):
     nx = nx.astype(np.float64)
     ny = ny.astype(np.float64)
@@ -169,32 +199,74 @@ class ClockSampler:
 # CPU baseline: the oracle (C, float64, OpenMP) on a bounded sample
 # ----------------------------------------------------------------------------
 
-def cpu_baseline(sample_graphs: int = GRAPHS_PER_GPU, seed: int = SEED, budget_s: float = 15.0):
-    """Times the oracle's forward+backward sums on the first graphs of the
-    same workload; returns full terms/s.  Stops adding graphs once the budget
-    is used.  Uses every host thread."""
+def cpu_units(name: str):
+    """Units of oracle work (C, float64, OpenMP) drawn from the named workload:
+    yields (run, label) where run(cores) computes the forward+backward sums of
+    one unit and returns the full kernel terms it covered.  Data generation
+    stays outside run()."""
     from oracle import oracle as O
     O.build()
-    cores = os.cpu_count() or 1
-    total_full = 0.0
-    total_t = 0.0
-    used = 0
-    for g in range(sample_graphs):
-        x, y = ragged_graph(g, seed)
+    f64 = lambda v: np.ascontiguousarray(v, dtype=np.float64)
+    if name == "huge-pair":
+        src, tgt = huge_pair_data()
+        x, y = f64(src), f64(tgt)
         n, m = x.shape[0], y.shape[0]
-        a = np.full(n, 1.0 / n)
-        b = np.full(m, 1.0 / m)
+        a, b = np.full(n, 1.0 / n), np.full(m, 1.0 / m)
+        rows = 256
+        for u in range(10 ** 9):
+            side = u % 2
+            r0 = (u // 2) * rows % (n if side == 0 else m)
+            sel = np.arange(r0, r0 + rows, dtype=np.int64)
+
+            def run(cores, side=side, sel=sel):
+                O.rows_sums(side, x, y, a, b, 0.2, sel, nthreads=cores)
+                return float(sel.size * (n + m))
+            yield run, f"row blocks of {rows} rows of the {n}-point pair (both clouds)"
+    elif name == "dense":
+        xb, yb, lx, ly = dense_data(0)
+        for c in range(10 ** 9):
+            k = c % xb.shape[0]
+            x, y = f64(xb[k, :lx[k]]), f64(yb[k, :ly[k]])
+
+            def run(cores, x=x, y=y):
+                n, m = x.shape[0], y.shape[0]
+                O.raw_sums(x, y, np.full(n, 1.0 / n), np.full(m, 1.0 / m), [0, n], [0, m],
+                           SIGMA, nthreads=cores)
+                return float(n * n + m * m + n * m)
+            yield run, "clouds of the dense batch (valid prefixes)"
+    else:
+        for g in range(10 ** 9):
+            if name == "embed128":
+                sx, sy = embed_graph(g)
+                sigma = 1.0
+            else:
+                sx, sy = ragged_graph(g)
+                sigma = SIGMA
+            x, y = f64(sx), f64(sy)
+
+            def run(cores, x=x, y=y, sigma=sigma):
+                n, m = x.shape[0], y.shape[0]
+                O.raw_sums(x, y, np.full(n, 1.0 / n), np.full(m, 1.0 / m), [0, n], [0, m],
+                           sigma, nthreads=cores)
+                return float(n * n + m * m + n * m)
+            yield run, f"graphs of the {name} batch"
+
+
+def cpu_baseline(name: str, budget_s: float = 15.0):
+    """The oracle timed on the first units of the same workload until the
+    budget is used; full terms/s on every host thread."""
+    cores = os.cpu_count() or 1
+    total_full, total_t, used, label = 0.0, 0.0, 0, ""
+    for run, label in cpu_units(name):
         t0 = time.perf_counter()
-        O.raw_sums(x.astype(np.float64), y.astype(np.float64), a, b, [0, n], [0, m], SIGMA,
-                   nthreads=cores)
+        total_full += run(cores)
         total_t += time.perf_counter() - t0
-        total_full += float(n * n + m * m + n * m)
         used += 1
         if total_t > budget_s:
             break
     return {"value": total_full / total_t, "unit": "terms/s", "cores": cores, "kind": "port",
-            "sample": f"first {used} graphs of the 4096-graph ragged batch, oracle (C, fp64, "
-                      f"OpenMP) forward+backward sums, {total_t:.1f} s"}
+            "sample": f"first {used} {label}, oracle (C, fp64, OpenMP) forward+backward sums, "
+                      f"{total_t:.1f} s"}
 
 
 # ----------------------------------------------------------------------------
@@ -216,7 +288,7 @@ class RaggedWorkload:
     scaling = "weak"
 
     def __init__(self, rank, world, dev, graphs_per_gpu=GRAPHS_PER_GPU, dim=3, lo=32, hi=2048,
-                 sigma=SIGMA, center=True, name=None):
+                 sigma=SIGMA, center=True):
         import torch
         from rapidalign_b200.shard import lpt_partition
         total = graphs_per_gpu * world
@@ -232,13 +304,13 @@ class RaggedWorkload:
         self.h = {k: torch.from_numpy(v).pin_memory() for k, v in
                   dict(x=x, y=y, bx=bx, by=by).items()}
         self.result_host = torch.empty(len(self.mine), dtype=torch.float32).pin_memory()
-        self.config = {
-            "workload": name or (f"ragged PyG batch, {graphs_per_gpu} graphs per GPU, {lo}-{hi} "
-                                 f"points each, D={dim}, sigma={sigma}, "
-                                 f"{'centred' if center else 'uncentred'}, pyg_kde_mmd_loss "
-                                 "fwd+bwd"),
-            "graphs": total,
-        }
+        self.config = self.describe(world)
+
+    @staticmethod
+    def describe(world):
+        return {"workload": f"ragged PyG batch, {GRAPHS_PER_GPU} graphs per GPU, 32-2048 points "
+                            f"each, D=3, sigma={SIGMA}, centred, pyg_kde_mmd_loss fwd+bwd",
+                "graphs": GRAPHS_PER_GPU * world}
 
     def step(self, t):
         from rapidalign_b200 import pyg_kde_mmd_loss
@@ -264,10 +336,7 @@ class HugePairWorkload:
     def __init__(self, rank, world, dev, n=262144, sigma=0.2):
         import torch
         import torch.distributed as dist
-        rng = np.random.default_rng([SEED, 4])
-        src = rng.standard_normal((n, 3)).astype(np.float32)
-        R = random_rotation(rng)
-        tgt = ((src + 0.05 * rng.standard_normal((n, 3))) @ R.T).astype(np.float32)
+        src, tgt = huge_pair_data(n)
         self.group = dist.group.WORLD if world > 1 else None
         self.world = world
         full, unique = term_counts(np.array([n]), np.array([n]))
@@ -278,10 +347,14 @@ class HugePairWorkload:
         self.d = {"x": torch.from_numpy(src).to(dev), "y": torch.from_numpy(tgt).to(dev)}
         self.h = {"x": torch.from_numpy(src).pin_memory(), "y": torch.from_numpy(tgt).pin_memory()}
         self.result_host = torch.empty(1, dtype=torch.float32).pin_memory()
-        self.config = {"workload": f"single pair N = M = {n}, D=3, tgt = R(src + 0.05 noise), "
-                                   f"sigma={sigma}, centred, split over the GPUs by row tiles "
-                                   "(shard.split_pair_kde_mmd_loss) fwd+bwd",
-                       "points": n}
+        self.config = self.describe(world)
+
+    @staticmethod
+    def describe(world):
+        return {"workload": "single pair N = M = 262144, D=3, tgt = R(src + 0.05 noise), "
+                            "sigma=0.2, centred, split over the GPUs by row tiles "
+                            "(shard.split_pair_kde_mmd_loss) fwd+bwd",
+                "points": 262144}
 
     def step(self, t):
         from rapidalign_b200.shard import split_pair_kde_mmd_loss
@@ -312,11 +385,7 @@ class DenseWorkload:
 
     def __init__(self, rank, world, dev, B=64, nmax=1024, sigma=SIGMA):
         import torch
-        rng = np.random.default_rng([SEED, 2, rank])
-        x = rng.standard_normal((B, nmax, 3)).astype(np.float32)
-        y = (x + 0.05 * rng.standard_normal((B, nmax, 3))).astype(np.float32)
-        lx = rng.integers(512, nmax + 1, B)
-        ly = rng.integers(512, nmax + 1, B)
+        x, y, lx, ly = dense_data(rank, B, nmax)
         mx = np.arange(nmax)[None, :] < lx[:, None]
         my = np.arange(nmax)[None, :] < ly[:, None]
         self.full_local, self.unique_local = term_counts(lx, ly)
@@ -326,9 +395,13 @@ class DenseWorkload:
         self.h = {k: torch.from_numpy(v).pin_memory() for k, v in
                   dict(x=x, y=y, mx=mx, my=my).items()}
         self.result_host = torch.empty(B, dtype=torch.float32).pin_memory()
-        self.config = {"workload": f"dense padded batch, B={B} clouds of Nmax={nmax} per GPU, "
-                                   "valid 512-1024 (prefix masks), D=3, sigma=0.25, centred, "
-                                   "kde_mmd_loss_dense fwd+bwd", "clouds": B * world}
+        self.config = self.describe(world)
+
+    @staticmethod
+    def describe(world):
+        return {"workload": "dense padded batch, B=64 clouds of Nmax=1024 per GPU, valid "
+                            "512-1024 (prefix masks), D=3, sigma=0.25, centred, "
+                            "kde_mmd_loss_dense fwd+bwd", "clouds": 64 * world}
 
     def step(self, t):
         from rapidalign_b200 import kde_mmd_loss_dense
@@ -358,11 +431,9 @@ class EmbedWorkload(RaggedWorkload):
         self.mine = np.sort(lpt_partition(cost, world)[rank])
         xs, ys = [], []
         for g in self.mine:
-            r = np.random.default_rng([SEED, 5, int(g)])
-            n = int(r.integers(64, 513))
-            a = (r.standard_normal((n, 128)) / np.sqrt(128)).astype(np.float32)
+            a, b = embed_graph(int(g))
             xs.append(a)
-            ys.append((a + 0.1 * r.standard_normal((n, 128))).astype(np.float32))
+            ys.append(b)
         nx = np.array([a.shape[0] for a in xs])
         x, y = np.concatenate(xs), np.concatenate(ys)
         bx = np.repeat(np.arange(len(xs)), nx)
@@ -374,9 +445,13 @@ class EmbedWorkload(RaggedWorkload):
         self.h = {k: torch.from_numpy(v).pin_memory() for k, v in
                   dict(x=x, y=y, bx=bx, by=bx).items()}
         self.result_host = torch.empty(len(self.mine), dtype=torch.float32).pin_memory()
-        self.config = {"workload": "graph embeddings, 1024 graphs per GPU of 64-512 nodes, "
-                                   "D=128, sigma=1.0, uncentred, pyg_kde_mmd_loss fwd+bwd",
-                       "graphs": total}
+        self.config = self.describe(world)
+
+    @staticmethod
+    def describe(world):
+        return {"workload": "graph embeddings, 1024 graphs per GPU of 64-512 nodes, D=128, "
+                            "sigma=1.0, uncentred, pyg_kde_mmd_loss fwd+bwd",
+                "graphs": 1024 * world}
 
     def tiles_time(self, reps):
         return None
@@ -531,7 +606,7 @@ def run_ours(args):
             "clocks": clocks,
         }
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+            line["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_budget)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -571,34 +646,34 @@ def read_traffic():
 # reference arm: the reference's CPU path (here: the oracle port)
 # ----------------------------------------------------------------------------
 
+# oracle units per reference step (about a second of host work each)
+REFERENCE_UNITS_PER_STEP = {"ragged": 6, "embed128": 8, "dense": 4, "huge-pair": 4}
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from oracle import oracle as O
-    O.build()
     cores = os.cpu_count() or 1
-    # each step: a bounded sample of the same workload (graphs g0..g0+k)
-    per_step_graphs = 6
-    times, full = [], 0.0
+    # each step: a bounded sample of the same workload (the next units)
+    per_step = REFERENCE_UNITS_PER_STEP[args.workload]
+    units = cpu_units(args.workload)
+    times, full, label = [], 0.0, ""
     for s in range(args.warmup + args.steps):
         t_step, f_step = 0.0, 0.0
-        for j in range(per_step_graphs):
-            g = s * per_step_graphs + j
-            x, y = ragged_graph(g)
-            n, m = x.shape[0], y.shape[0]
-            a = np.full(n, 1.0 / n)
-            b = np.full(m, 1.0 / m)
+        for _ in range(per_step):
+            run, label = next(units)
             t0 = time.perf_counter()
-            O.raw_sums(x.astype(np.float64), y.astype(np.float64), a, b, [0, n], [0, m], SIGMA,
-                       nthreads=cores)
+            f_step += run(cores)
             t_step += time.perf_counter() - t0
-            f_step += float(n * n + m * m + n * m)
         if s >= args.warmup:
             times.append(t_step)
             full += f_step
     value = full / sum(times)
+    wl = WORKLOADS[args.workload]
+    config = dict(wl.describe(world))
+    config["seed"] = SEED
     line = {
         "impl": "reference",
         "metric": "Gaussian kernel-term evals/sec fwd+bwd",
@@ -609,17 +684,15 @@ def run_reference(args):
         "warmup": args.warmup,
         "ms_per_step": sum(times) / len(times) * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": wl.scaling,
         "vs_baseline": None,
         "dtype": "f64",
         "data": "synthetic",
-        "config": {"workload": f"ragged PyG batch, {GRAPHS_PER_GPU} graphs per GPU, 32-2048 "
-                               "points each, D=3, sigma=0.25, centred, pyg_kde_mmd_loss fwd+bwd",
-                   "graphs": GRAPHS_PER_GPU * world, "seed": SEED},
+        "config": config,
         "cpu_baseline": {"value": value, "unit": "terms/s", "cores": cores, "kind": "port",
-                         "sample": f"{per_step_graphs} graphs of the ragged batch per step, "
-                                   "oracle (C, fp64, OpenMP) forward+backward sums; the "
-                                   "reference's CPU path is PyTorch and does not travel"},
+                         "sample": f"{per_step} {label} per step, oracle (C, fp64, OpenMP) "
+                                   "forward+backward sums; the reference's CPU path is "
+                                   "PyTorch and does not travel"},
         "e2e": {"value": value, "unit": "terms/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

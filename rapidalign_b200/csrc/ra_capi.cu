@@ -1,9 +1,10 @@
 // ra_capi.cu -- host side of the C ABI declared in include/rapidalign_b200.h.
 // Lays out the caller's workspace, validates arguments and enqueues the
 // kernel pipeline on the caller's stream:
-//   prep (per pair) -> plan count -> plan scan -> plan emit -> tiles ->
-//   finalize (per pair)                               [forward]
-//   epilogue (per pair and side)                       [backward]
+//   segments + chunk map -> stats (per chunk) -> meta (per pair) ->
+//   [generic pack] -> plan count -> plan scan -> plan emit -> [tile pack] ->
+//   tiles -> finalize (per pair)                                 [forward]
+//   epilogue partials (per chunk) -> epilogue write (per chunk)  [backward]
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -13,6 +14,7 @@
 #include <mutex>
 
 #include "../../include/rapidalign_b200.h"
+#include "ra_chunks.cuh"
 #include "ra_common.cuh"
 #include "ra_epilogue.cuh"
 #include "ra_plan.cuh"
@@ -28,6 +30,7 @@ std::atomic<unsigned long long> g_launches{0};
 
 constexpr int kPrepThreads = 256;
 constexpr int kEpiThreads = 256;
+constexpr int kChunkCtasPerSm = 8;  // 256-thread CTAs of the per-chunk passes
 
 size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
@@ -44,8 +47,9 @@ struct Layout {
   int acc_stride;
   int64_t max_items;
   int64_t max_tiles_x, max_tiles_y;  // packed3: bound on the padded tiles
+  int64_t max_chunks;                // bound on the virtual chunks (ra_chunks.cuh)
   size_t hdr, seg, meta, cnt, item_off, tbase_x, tbase_y, boff, items, itemK, itemS, Kws, Sws,
-      coef, Ktmp;
+      coef, Ktmp, chcnt, chx, choff, rec;
   size_t tiles_x, tiles_y, Gx, Gy, Ax, Ay, accX, accY;
   size_t acc_x_bytes, acc_y_bytes;
   size_t total;
@@ -92,6 +96,11 @@ Layout make_layout(const ra_kde_desc *d) {
   }
   L.max_items = L.packed3 ? (int64_t)kSplitMax * (2 * tx + ty) : 2 * tx + 2 * ty;
   if (L.max_items < 1) L.max_items = 1;
+  if (d->layout == RA_LAYOUT_DENSE)
+    L.max_chunks = P * (ceil_div(d->nmax_x, kChunk) + ceil_div(d->nmax_y, kChunk));
+  else
+    L.max_chunks = ceil_div(NX, kChunk) + ceil_div(NY, kChunk) + 2 * P;
+  if (L.max_chunks < 1) L.max_chunks = 1;
   L.max_tiles_x = L.packed3 ? (tx > 0 ? tx : 1) : 0;
   L.max_tiles_y = L.packed3 ? (ty > 0 ? ty : 1) : 0;
   const bool grad = d->need_grad != 0;
@@ -119,6 +128,10 @@ Layout make_layout(const ra_kde_desc *d) {
   L.Sws = take(sizeof(double) * 3 * P1);
   L.coef = take(sizeof(double) * 3 * P1);
   L.Ktmp = take(sizeof(double) * 3 * P1);
+  L.chcnt = take(sizeof(int64_t) * P1);
+  L.chx = take(sizeof(int64_t) * P1);
+  L.choff = take(sizeof(int64_t) * (P1 + 1));
+  L.rec = take(sizeof(double) * (size_t)L.max_chunks * stats_stride(L.DP));
   const size_t nx = (size_t)(NX > 0 ? NX : 1), ny = (size_t)(NY > 0 ? NY : 1);
   if (L.packed3) {
     L.tiles_x = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_x);
@@ -158,6 +171,17 @@ int check_common(const ra_kde_desc *d, void *ws, size_t ws_bytes, size_t need) {
   if (!(d->sigma > 0.0) || !std::isfinite(d->sigma)) return RA_ERR_SIGMA;
   if (ws == nullptr || ((uintptr_t)ws & 255) != 0 || ws_bytes < need) return RA_ERR_WORKSPACE;
   return RA_OK;
+}
+
+// Grid of the per-chunk passes: enough CTAs to fill the GPU, never more than
+// there can be chunks.
+unsigned chunk_grid(const Layout &L) {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms < 1) sms = 1;
+  const int64_t g = (int64_t)sms * kChunkCtasPerSm;
+  return (unsigned)(L.max_chunks < g ? L.max_chunks : g);
 }
 
 int launch_tiles3(int mode, const Tiles3Args &Targs, cudaStream_t st) {
@@ -248,11 +272,11 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   pa.wmode_x = d->weights_x;
   pa.wmode_y = d->weights_y;
   pa.center = d->center;
-  pa.packed3 = L.packed3 ? 1 : 0;
   pa.num_x = d->num_x;
   pa.num_y = d->num_y;
   pa.nmax_x = d->nmax_x;
   pa.nmax_y = d->nmax_y;
+  pa.chunk_cap = L.max_chunks;
   pa.scale = scale;
   pa.x = in->x;
   pa.y = in->y;
@@ -264,6 +288,10 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   pa.mask_y = d->layout == RA_LAYOUT_DENSE ? in->mask_y : nullptr;
   pa.seg = at<Seg>(ws, L.seg);
   pa.meta = at<double>(ws, L.meta);
+  pa.rec = at<double>(ws, L.rec);
+  pa.chcnt = at<int64_t>(ws, L.chcnt);
+  pa.chx = at<int64_t>(ws, L.chx);
+  pa.choff = at<int64_t>(ws, L.choff);
   pa.err = at<int>(ws, L.hdr + kHdrErr);
   if (!L.packed3) {
     pa.Gx = at<float>(ws, L.Gx);
@@ -271,9 +299,15 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     pa.Ax = at<float>(ws, L.Ax);
     pa.Ay = at<float>(ws, L.Ay);
   }
-  const size_t prep_smem = sizeof(double) * (3 * kPrepThreads + 257);
-  prep_kernel<kPrepThreads><<<(unsigned)P, kPrepThreads, prep_smem, st>>>(pa);
-  ++g_launches;
+  const unsigned cgrid = chunk_grid(L);
+  segment_kernel<<<1, 1024, 0, st>>>(pa);
+  stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+  meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
+  g_launches += 3;
+  if (!L.packed3) {
+    packg_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+    ++g_launches;
+  }
   if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
 
   // ---- plan ----
@@ -313,13 +347,15 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     pk.wmode_y = d->weights_y;
     pk.seg = at<Seg>(ws, L.seg);
     pk.meta = at<double>(ws, L.meta);
+    pk.choff = at<int64_t>(ws, L.choff);
+    pk.chx = at<int64_t>(ws, L.chx);
     pk.tbase_x = at<int64_t>(ws, L.tbase_x);
     pk.tbase_y = at<int64_t>(ws, L.tbase_y);
     pk.max_tiles_x = L.max_tiles_x;
     pk.max_tiles_y = L.max_tiles_y;
     pk.tiles_x = at<ulonglong2>(ws, L.tiles_x);
     pk.tiles_y = at<ulonglong2>(ws, L.tiles_y);
-    pack3_kernel<kPrepThreads><<<(unsigned)(2 * P), kPrepThreads, 0, st>>>(pk);
+    pack3_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pk);
     ++g_launches;
     if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
   }
@@ -376,7 +412,7 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   return finish_impl(d, L, Kxx, Kyy, Kxy, ws, st);
 }
 
-// Per-pair K from the item partials, the K copy for the caller, the state flag.
+// Per-pair K from the item partials (into the caller's arrays), the state flag.
 int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy, double *Kxy,
                 void *ws, cudaStream_t st) {
   const int64_t P = d->num_pairs;
@@ -391,24 +427,16 @@ int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy,
   fa.itemS = at<double>(ws, L.itemS);
   fa.K_ws = at<double>(ws, L.Kws);
   fa.S_ws = at<double>(ws, L.Sws);
-  // finalize writes Kxx | Kyy | Kxy contiguously into K_ws; copy out below
-  fa.K_out = at<double>(ws, L.Ktmp);
-  finalize_kernel<<<(unsigned)ceil_div(P * 32, 256), 256, 0, st>>>(fa);
+  // the caller's three K arrays are written by the kernel itself
+  fa.K_out[0] = Kxx;
+  fa.K_out[1] = Kyy;
+  fa.K_out[2] = Kxy;
+  // the state flag marks a workspace whose forward kept what a backward needs;
+  // the kernel writes it, so no host memory is involved
+  fa.state = grad ? at<int>(ws, L.hdr + kHdrState) : nullptr;
+  finalize_kernel<256><<<(unsigned)P, 256, 0, st>>>(fa);
   ++g_launches;
-  if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
-  const size_t pb = sizeof(double) * (size_t)P;
-  double *Kt = at<double>(ws, L.Ktmp);
-  if ((Kxx != Kt && cudaMemcpyAsync(Kxx, Kt, pb, cudaMemcpyDeviceToDevice, st)) ||
-      (Kyy != Kt + P && cudaMemcpyAsync(Kyy, Kt + P, pb, cudaMemcpyDeviceToDevice, st)) ||
-      (Kxy != Kt + 2 * P && cudaMemcpyAsync(Kxy, Kt + 2 * P, pb, cudaMemcpyDeviceToDevice, st)))
-    return RA_ERR_CUDA;
-  if (grad) {
-    const int one = 1;
-    if (cudaMemcpyAsync(at<char>(ws, L.hdr + kHdrState), &one, sizeof(int),
-                        cudaMemcpyHostToDevice, st) != cudaSuccess)
-      return RA_ERR_CUDA;
-  }
-  return RA_OK;
+  return cuda_status(cudaGetLastError());
 }
 
 int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *coef,
@@ -436,6 +464,9 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.meta = at<double>(ws, L.meta);
   ea.coef = coef;
   ea.S_ws = at<double>(ws, L.Sws);
+  ea.choff = at<int64_t>(ws, L.choff);
+  ea.chx = at<int64_t>(ws, L.chx);
+  ea.rec = at<double>(ws, L.rec);
   ea.x = in->x;
   ea.y = in->y;
   ea.mask_x = d->layout == RA_LAYOUT_DENSE ? in->mask_x : nullptr;
@@ -460,11 +491,19 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.grad_wx = gr->grad_wx;
   ea.grad_wy = gr->grad_wy;
   ea.grad_sigma = gr->grad_sigma;
-  if (L.packed3)
-    epilogue3_kernel<kEpiThreads><<<(unsigned)(2 * P), kEpiThreads, 0, st>>>(ea);
-  else
-    epilogueg_kernel<kEpiThreads><<<(unsigned)(2 * P), kEpiThreads, 0, st>>>(ea);
-  ++g_launches;
+  const unsigned cgrid = chunk_grid(L);
+  if (L.packed3) {
+    epi3_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+    epi3_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+  } else {
+    epig_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+    epig_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+  }
+  g_launches += 2;
+  if (ea.grad_sigma != nullptr) {
+    sigma_grad_kernel<<<(unsigned)ceil_div(P, 256), 256, 0, st>>>(ea);
+    ++g_launches;
+  }
   return cuda_status(cudaGetLastError());
 }
 
@@ -725,7 +764,7 @@ int ra_kde_mmd_backward_segmented(const float *x, const float *y, const float *w
   in.ptr_y = ptr_y;
   cudaStream_t st = (cudaStream_t)stream;
   double *Kt = at<double>(workspace, L.Ktmp);
-  // the forward leaves K in Ktmp (no copy: the destinations are Ktmp itself)
+  // the forward writes K into the workspace's Ktmp region
   rc = forward_impl(&d, &in, Kt, Kt + P, Kt + 2 * P, workspace, workspace_bytes, st);
   if (rc || P == 0) return rc;
   double *coef = at<double>(workspace, L.coef);

@@ -14,6 +14,7 @@
 // sigma: dK/dsigma = S / sigma^3 with S = sum w w' k r^2 (kde_gradients.py:115-123).
 #pragma once
 
+#include "ra_chunks.cuh"
 #include "ra_common.cuh"
 #include "ra_prep.cuh"
 
@@ -24,39 +25,52 @@ struct FinalizeArgs {
   const int64_t *item_off;
   const int64_t *boff;
   const double *itemK, *itemS;
-  double *K_out;  // [3P] Kxx | Kyy | Kxy (caller's buffer)
+  double *K_out[3];  // caller's Kxx, Kyy, Kxy ([P] each)
   double *K_ws;   // [3P] copy kept in the workspace
   double *S_ws;   // [3P]
+  int *state;     // set to 1 when not null
 };
 
-// one warp per pair; block b of the items maps to K index (xy -> 2, xx -> 0, yy -> 1)
-__global__ void finalize_kernel(FinalizeArgs A) {
-  const int64_t p = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+// One CTA per pair; block b of the items maps to K index (xy -> 2, xx -> 0,
+// yy -> 1).  Four independent accumulators per thread keep enough loads in
+// flight for pairs with hundreds of thousands of items.
+template <int NT>
+__global__ void __launch_bounds__(NT) finalize_kernel(FinalizeArgs A) {
+  __shared__ double sh[NT / 32];
+  const int64_t p = blockIdx.x;
   if (p >= A.P) return;
+  if (p == 0 && threadIdx.x == 0 && A.state != nullptr) *A.state = 1;
   // item_off[P] is the (clamped) number of items actually emitted: never read
   // partials beyond it, even for a malformed ptr that overflowed the bound
   const int64_t lim = A.item_off[A.P];
   const int64_t base = A.item_off[p];
   const int64_t end = A.item_off[p + 1] < lim ? A.item_off[p + 1] : lim;
   const int kidx[3] = {2, 0, 1};
-#pragma unroll
+#pragma unroll 1
   for (int b = 0; b < 3; ++b) {
     int64_t b0 = base + A.boff[p * 4 + b];
     const int64_t b1 = b < 2 ? base + A.boff[p * 4 + b + 1] : base + A.boff[p * 4 + 3];
     const int64_t e = b1 < end ? b1 : end;
     if (b0 > e) b0 = e;
-    double k = 0.0, s = 0.0;
-    for (int64_t i = b0 + lane; i < e; i += 32) {
-      k += A.itemK[i];
-      s += A.itemS[i];
+    double k[4] = {0.0, 0.0, 0.0, 0.0}, s[4] = {0.0, 0.0, 0.0, 0.0};
+    int64_t i = b0 + threadIdx.x;
+    for (; i + 3 * NT < e; i += 4 * NT) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        k[u] += A.itemK[i + u * NT];
+        s[u] += A.itemS[i + u * NT];
+      }
     }
-    k = warp_sum(k);
-    s = warp_sum(s);
-    if (lane == 0) {
-      A.K_out[kidx[b] * A.P + p] = k;
-      A.K_ws[kidx[b] * A.P + p] = k;
-      A.S_ws[kidx[b] * A.P + p] = s;
+    for (; i < e; i += NT) {
+      k[0] += A.itemK[i];
+      s[0] += A.itemS[i];
+    }
+    const double kt = block_sum((k[0] + k[1]) + (k[2] + k[3]), sh);
+    const double st = block_sum((s[0] + s[1]) + (s[2] + s[3]), sh);
+    if (threadIdx.x == 0) {
+      A.K_out[kidx[b]][p] = kt;
+      A.K_ws[kidx[b] * A.P + p] = kt;
+      A.S_ws[kidx[b] * A.P + p] = st;
     }
   }
 }
@@ -73,6 +87,8 @@ struct EpilogueArgs {
   const double *meta;
   const double *coef;  // [3P]: dL/dKxx | dL/dKyy | dL/dKxy
   const double *S_ws;  // [3P]
+  const int64_t *choff, *chx;  // chunk map (ra_chunks.cuh)
+  double *rec;         // per-chunk (Q, R[DP]) partials, stride stats_stride(DP)
   const float *x, *y;  // original coordinates
   const uint8_t *mask_x, *mask_y;
   const ulonglong2 *tiles_x, *tiles_y;  // packed3: tile layout (ra_prep.cuh)
@@ -86,224 +102,282 @@ struct EpilogueArgs {
   double *grad_sigma;
 };
 
-// Per-point backward quantities.  packed3: `slot` = tile * 64 + lane of the
-// point in the tile layout; generic: `slot` = the point's row index.
-// Returns gxt[0..D) (dL/dx~) and ga (dL/da, direct part).
+// Per-point backward quantities of the D <= 3 layout: `slot` = tile * 64 +
+// lane of the point in the tile layout.  Returns gxt[0..D) (dL/dx~) and ga
+// (dL/da, direct part).
 template <int MAXD>
 __device__ __forceinline__ void point_grads(const EpilogueArgs &A, int side, int64_t slot,
                                             double cs, double cc, double k_x, double *gxt,
                                             double &ga, double &a_out) {
   const int D = A.D;
   const float *acc = (side == 0 ? A.accX : A.accY) + slot * A.acc_stride;
-  double a;
-  double xp[MAXD];
-  if (A.packed3) {
-    const ulonglong2 *tiles = side == 0 ? A.tiles_x : A.tiles_y;
-    const int64_t t = slot / kTile, l = slot % kTile;
-    const ulonglong2 q0 = tiles[(t * A.nq) * kTile + l];
-    const ulonglong2 q1 = tiles[(t * A.nq + 1) * kTile + l];
-    xp[0] = lo_of(q0.x);
-    if (MAXD > 1) xp[1] = lo_of(q0.y);
-    if (MAXD > 2) xp[2] = lo_of(q1.x);
-    a = lo_of(q1.y);
-  } else {
-    a = (side == 0 ? A.Ax : A.Ay)[slot];
-    const float *gp = (side == 0 ? A.Gx : A.Gy) + slot * A.DP;
-    for (int d = 0; d < D && d < MAXD; ++d) xp[d] = gp[d];
-  }
-  const int cross = A.packed3 ? kAcc3Block : 1 + A.DP;
+  const ulonglong2 *tiles = side == 0 ? A.tiles_x : A.tiles_y;
+  const int64_t t = slot / kTile, l = slot % kTile;
+  const double a = lo_of(tiles[(t * A.nq + 1) * kTile + l].y);
+  const int cross = kAcc3Block;
   const double s_self = acc[0], s_cross = acc[cross];
-  for (int d = 0; d < D && d < MAXD; ++d) {
-    double Gs, Gc;
-    if (A.packed3) {  // difference form: G = sum w k (x' - y') directly
-      Gs = acc[1 + d];
-      Gc = acc[cross + 1 + d];
-    } else {          // folded form: G = x' s - sum w k y'
-      Gs = xp[d] * s_self - (double)acc[1 + d];
-      Gc = xp[d] * s_cross - (double)acc[cross + 1 + d];
-    }
-    gxt[d] = -a * k_x * (cs * Gs + cc * Gc);
+#pragma unroll
+  for (int d = 0; d < MAXD; ++d) {
+    // difference form: G = sum w k (x' - y') accumulated directly
+    gxt[d] = d < D ? -a * k_x * (cs * acc[1 + d] + cc * acc[cross + 1 + d]) : 0.0;
   }
   ga = cs * s_self + cc * s_cross;
   a_out = a;
 }
 
-// One CTA per (pair, side), one thread per point; D <= 3 (packed3) only.
-template <int NT>
-__global__ void __launch_bounds__(NT) epilogue3_kernel(EpilogueArgs A) {
-  __shared__ double sh[NT / 32];
-  const int64_t p = blockIdx.x >> 1;
-  const int side = blockIdx.x & 1;
-  if (p >= A.P) return;
+// Per (pair, side) constants of the epilogue.
+struct EpiSide {
+  double cxx, cyy, cxy, cs, cc, k_x, W, Wraw;
+  const double *mu;
+  int64_t s, span, count;
+};
+
+__device__ __forceinline__ EpiSide epi_side(const EpilogueArgs &A, int64_t p, int side) {
+  EpiSide E;
   const Seg sg = A.seg[p];
-  const int64_t s = side == 0 ? sg.xs : sg.ys;
-  const int64_t span = side == 0 ? sg.xspan : sg.yspan;
-  const int64_t count = side == 0 ? sg.xcount : sg.ycount;
-  const int D = A.D;
-  const double cxx = A.coef[p], cyy = A.coef[A.P + p], cxy = A.coef[2 * A.P + p];
-  const double cs = side == 0 ? 2.0 * cxx : 2.0 * cyy;
-  const double cc = cxy;
-  const double k_x = 1.0 / (A.scale * A.sigma * A.sigma);
+  E.s = side == 0 ? sg.xs : sg.ys;
+  E.span = side == 0 ? sg.xspan : sg.yspan;
+  E.count = side == 0 ? sg.xcount : sg.ycount;
+  E.cxx = A.coef[p];
+  E.cyy = A.coef[A.P + p];
+  E.cxy = A.coef[2 * A.P + p];
+  E.cs = side == 0 ? 2.0 * E.cxx : 2.0 * E.cyy;
+  E.cc = E.cxy;
+  E.k_x = 1.0 / (A.scale * A.sigma * A.sigma);
   const double *meta = A.meta + p * meta_stride(A.DP);
-  const double W = meta[side], Wraw = meta[2 + side];
-  const double *mu = meta + 4 + side * A.DP;
-  const float *pts = side == 0 ? A.x : A.y;
-  const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
-  const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-  float *gout = side == 0 ? A.grad_x : A.grad_y;
-  double *wout = side == 0 ? A.grad_wx : A.grad_wy;
-
-  const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
-  // pass 1: R = sum dL/dx~ (D values), Q = sum a dL/da
-  double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
-  for (int64_t i = threadIdx.x; i < count; i += NT) {
-    double gxt[3], ga, a;
-    point_grads<3>(A, side, slot0 + i, cs, cc, k_x, gxt, ga, a);
-    for (int d = 0; d < D; ++d) R[d] += gxt[d];
-    Q += a * ga;
-  }
-  for (int d = 0; d < D; ++d) R[d] = block_sum(R[d], sh);
-  Q = block_sum(Q, sh);
-  double Qt = Q;
-  if (A.center)
-    for (int d = 0; d < D; ++d) Qt -= mu[d] * R[d];
-
-  // pass 2: gradients (zeros for the padded tail of a dense row)
-  for (int64_t i = threadIdx.x; i < span; i += NT) {
-    const int64_t g = s + i;
-    double gxt[3] = {0.0, 0.0, 0.0}, ga = 0.0, a = 0.0;
-    const bool live = i < count;
-    if (live) point_grads<3>(A, side, slot0 + i, cs, cc, k_x, gxt, ga, a);
-    if (gout != nullptr) {
-      for (int d = 0; d < D; ++d) {
-        double v = gxt[d];
-        if (A.center && live) v -= a * R[d];
-        gout[g * D + d] = (float)v;
-      }
-    }
-    if (wout != nullptr && wmode != 3) {
-      double gat = ga;
-      if (A.center && live)
-        for (int d = 0; d < D; ++d) gat -= (double)pts[g * D + d] * R[d];
-      const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
-      double gw;
-      if (!live) {
-        gw = 0.0;
-      } else if (wmode == 0) {
-        gw = m * gat;
-      } else if (wmode == 2 && !(Wraw > 1e-8)) {
-        gw = m * gat / 1e-8;
-      } else {
-        gw = m * (gat - Qt) / W;
-      }
-      wout[g] = gw;
-    }
-  }
-  if (side == 0 && threadIdx.x == 0 && A.grad_sigma != nullptr) {
-    const double c2 = A.scale * A.scale, s3 = A.sigma * A.sigma * A.sigma;
-    const double Sxx = A.S_ws[p], Syy = A.S_ws[A.P + p], Sxy = A.S_ws[2 * A.P + p];
-    A.grad_sigma[p] = (cxx * Sxx + cyy * Syy + cxy * Sxy) / (c2 * s3);
-  }
+  E.W = meta[side];
+  E.Wraw = meta[2 + side];
+  E.mu = meta + 4 + side * A.DP;
+  return E;
 }
 
-// Generic D: one CTA per (pair, side); RW threads per point (one per dim).
+// dL/dsigma per pair (every pair, empty ones included).
+__global__ void sigma_grad_kernel(EpilogueArgs A) {
+  const int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (p >= A.P) return;
+  const double cxx = A.coef[p], cyy = A.coef[A.P + p], cxy = A.coef[2 * A.P + p];
+  const double c2 = A.scale * A.scale, s3 = A.sigma * A.sigma * A.sigma;
+  const double Sxx = A.S_ws[p], Syy = A.S_ws[A.P + p], Sxy = A.S_ws[2 * A.P + p];
+  A.grad_sigma[p] = (cxx * Sxx + cyy * Syy + cxy * Sxy) / (c2 * s3);
+}
+
+// dL/dw_i from dL/da_i (centering part already applied) -- kde.py weight
+// normalisation: raw (identity), clamped sum, plain sum.
+__device__ __forceinline__ double weight_grad(int wmode, double m, double gat, double Qt,
+                                              const EpiSide &E) {
+  if (wmode == 0) return m * gat;
+  if (wmode == 2 && !(E.Wraw > 1e-8)) return m * gat / 1e-8;
+  return m * (gat - Qt) / E.W;
+}
+
+// ---- D <= 3 (packed3): one thread per point --------------------------------
+// Pass 1: per chunk, R = sum dL/dx~ (D values) and Q = sum a dL/da.
 template <int NT>
-__global__ void __launch_bounds__(NT) epilogueg_kernel(EpilogueArgs A) {
+__global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
+  __shared__ double sh[NT / 32];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int rs = stats_stride(A.DP);
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
+    const EpiSide E = epi_side(A, p, side);
+    const int D = A.D;
+    const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
+    const int64_t b = c * kChunk, e = b + kChunk < E.count ? b + kChunk : E.count;
+    double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
+    for (int64_t i = b + threadIdx.x; i < e; i += NT) {
+      double gxt[3], ga, a;
+      point_grads<3>(A, side, slot0 + i, E.cs, E.cc, E.k_x, gxt, ga, a);
+#pragma unroll
+      for (int d = 0; d < 3; ++d) R[d] += gxt[d];  // gxt[d >= D] == 0
+      Q += a * ga;
+    }
+    double *rec = A.rec + v * rs;
+    Q = block_sum(Q, sh);
+    if (threadIdx.x == 0) rec[0] = Q;
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+      const double t = block_sum(R[d], sh);
+      if (threadIdx.x == 0) rec[1 + d] = t;
+    }
+  });
+}
+
+// Pass 2: per chunk, combine the side's partials (thread-strided over the
+// chunks, fixed-order block sums) and write the gradients of the chunk's
+// points (zeros for the padded tail of a dense row).
+template <int NT>
+__global__ void __launch_bounds__(NT) epi3_write_kernel(EpilogueArgs A) {
+  __shared__ double sh[NT / 32];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int rs = stats_stride(A.DP);
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t first, int64_t n) {
+    const EpiSide E = epi_side(A, p, side);
+    const int D = A.D;
+    double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
+    for (int64_t k = threadIdx.x; k < n; k += NT) {
+      const double *r = A.rec + (first + k) * rs;
+      Q += r[0];
+      R[0] += r[1];
+      R[1] += r[2];
+      R[2] += r[3];
+    }
+    Q = block_sum(Q, sh);
+#pragma unroll
+    for (int d = 0; d < 3; ++d) R[d] = block_sum(R[d], sh);
+    double Qt = Q;
+    if (A.center) {
+#pragma unroll
+      for (int d = 0; d < 3; ++d)
+        if (d < D) Qt -= E.mu[d] * R[d];
+    }
+
+    const float *pts = side == 0 ? A.x : A.y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    float *gout = side == 0 ? A.grad_x : A.grad_y;
+    double *wout = side == 0 ? A.grad_wx : A.grad_wy;
+    const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
+    const int64_t b = c * kChunk, e = b + kChunk < E.span ? b + kChunk : E.span;
+    for (int64_t i = b + threadIdx.x; i < e; i += NT) {
+      const int64_t g = E.s + i;
+      double gxt[3] = {0.0, 0.0, 0.0}, ga = 0.0, a = 0.0;
+      const bool live = i < E.count;
+      if (live) point_grads<3>(A, side, slot0 + i, E.cs, E.cc, E.k_x, gxt, ga, a);
+      if (gout != nullptr) {
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+          if (d >= D) break;
+          double val = gxt[d];
+          if (A.center && live) val -= a * R[d];
+          gout[g * D + d] = (float)val;
+        }
+      }
+      if (wout != nullptr && wmode != 3) {
+        double gat = ga;
+        if (A.center && live) {
+#pragma unroll
+          for (int d = 0; d < 3; ++d)
+            if (d < D) gat -= (double)pts[g * D + d] * R[d];
+        }
+        const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
+        wout[g] = live ? weight_grad(wmode, m, gat, Qt, E) : 0.0;
+      }
+    }
+  });
+}
+
+// ---- generic D: RW = DP threads per point (one per dimension) -------------
+__device__ __forceinline__ double gen_gxt(const EpilogueArgs &A, int side, int64_t g, int d,
+                                          const EpiSide &E, double &a, double &ga) {
+  const int DP = A.DP;
+  const float *acc = (side == 0 ? A.accX : A.accY) + g * A.acc_stride;
+  a = (side == 0 ? A.Ax : A.Ay)[g];
+  const int cross = 1 + DP;
+  // the stored self sums leave out the diagonal term (k_ii = 1, weight a_i)
+  const double s_self = acc[0], s_cross = acc[cross];
+  ga = E.cs * (s_self + a) + E.cc * s_cross;
+  if (d >= A.D) return 0.0;
+  const double xp = (side == 0 ? A.Gx : A.Gy)[g * DP + d];
+  const double Gs = xp * s_self - (double)acc[1 + d];
+  const double Gc = xp * s_cross - (double)acc[cross + 1 + d];
+  return -a * E.k_x * (E.cs * Gs + E.cc * Gc);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(NT) epig_partial_kernel(EpilogueArgs A) {
   __shared__ double sh[NT];
   __shared__ double shd[NT];
-  const int64_t p = blockIdx.x >> 1;
-  const int side = blockIdx.x & 1;
-  if (p >= A.P) return;
-  const Seg sg = A.seg[p];
-  const int64_t s = side == 0 ? sg.xs : sg.ys;
-  const int64_t span = side == 0 ? sg.xspan : sg.yspan;
-  const int64_t count = side == 0 ? sg.xcount : sg.ycount;
-  const int D = A.D, DP = A.DP;
-  const int RW = DP;  // generic DP is a power of two >= 4 and <= NT
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int DP = A.DP, RW = DP;  // generic DP is a power of two >= 4 and <= NT
   const int lanes = NT / RW;
   const int tid = threadIdx.x, d = tid % RW, pl = tid / RW;
-  const double cxx = A.coef[p], cyy = A.coef[A.P + p], cxy = A.coef[2 * A.P + p];
-  const double cs = side == 0 ? 2.0 * cxx : 2.0 * cyy;
-  const double cc = cxy;
-  const double k_x = 1.0 / (A.scale * A.sigma * A.sigma);
-  const double *meta = A.meta + p * meta_stride(DP);
-  const double W = meta[side], Wraw = meta[2 + side];
-  const double *mu = meta + 4 + side * DP;
-  const float *pts = side == 0 ? A.x : A.y;
-  const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
-  const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-  float *gout = side == 0 ? A.grad_x : A.grad_y;
-  double *wout = side == 0 ? A.grad_wx : A.grad_wy;
-  const float *accb = side == 0 ? A.accX : A.accY;
-  const float *Gp = side == 0 ? A.Gx : A.Gy;
-  const float *Ap = side == 0 ? A.Ax : A.Ay;
-  const int cross = 1 + DP;
-
-  auto gxt_of = [&](int64_t g, double &a, double &ga) -> double {
-    const float *acc = accb + g * A.acc_stride;
-    a = Ap[g];
-    const double s_self = acc[0], s_cross = acc[cross];
-    ga = cs * s_self + cc * s_cross;
-    if (d >= D) return 0.0;
-    const double xp = Gp[g * DP + d];
-    const double Gs = xp * s_self - (double)acc[1 + d];
-    const double Gc = xp * s_cross - (double)acc[cross + 1 + d];
-    return -a * k_x * (cs * Gs + cc * Gc);
-  };
-
-  double Rd = 0.0, Q = 0.0;
-  for (int64_t i = pl; i < count; i += lanes) {
-    double a, ga;
-    Rd += gxt_of(s + i, a, ga);
-    if (d == 0) Q += a * ga;
-  }
-  sh[tid] = Rd;
-  shd[tid] = Q;
-  __syncthreads();
-  double Rtot = 0.0;
-  for (int l = 0; l < lanes; ++l) Rtot += sh[l * RW + d];
-  double Qtot = 0.0;
-  for (int l = 0; l < lanes; ++l) Qtot += shd[l * RW];
-  __syncthreads();
-  // mu . R
-  sh[tid] = (pl == 0 && d < D) ? mu[d] * Rtot : 0.0;
-  __syncthreads();
-  double muR = 0.0;
-  for (int e = 0; e < RW; ++e) muR += sh[e];
-  __syncthreads();
-  const double Qt = A.center ? Qtot - muR : Qtot;
-
-  for (int64_t i0 = 0; i0 < span; i0 += lanes) {
-    const int64_t i = i0 + pl;
-    const bool inb = i < span;
-    const bool live = i < count;
-    const int64_t g = s + i;
-    double a = 0.0, ga = 0.0, gx = 0.0;
-    if (live) gx = gxt_of(g, a, ga);
-    if (A.center && live) gx -= a * Rtot;
-    if (inb && gout != nullptr && d < D) gout[g * D + d] = (float)gx;
-    // x_i . R across the RW threads of this point
-    sh[tid] = (live && d < D && A.center) ? (double)pts[g * D + d] * Rtot : 0.0;
+  const int rs = stats_stride(DP);
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
+    const EpiSide E = epi_side(A, p, side);
+    const int64_t b = c * kChunk, e = b + kChunk < E.count ? b + kChunk : E.count;
+    double Rd = 0.0, Q = 0.0;
+    for (int64_t i = b + pl; i < e; i += lanes) {
+      double a, ga;
+      Rd += gen_gxt(A, side, E.s + i, d, E, a, ga);
+      if (d == 0) Q += a * ga;
+    }
+    sh[tid] = Rd;
+    shd[tid] = Q;
     __syncthreads();
-    if (d == 0 && inb && wout != nullptr && wmode != 3) {
-      double xr = 0.0;
-      for (int e = 0; e < RW; ++e) xr += sh[pl * RW + e];
-      const double gat = ga - xr;
-      const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
-      double gw;
-      if (!live) gw = 0.0;
-      else if (wmode == 0) gw = m * gat;
-      else if (wmode == 2 && !(Wraw > 1e-8)) gw = m * gat / 1e-8;
-      else gw = m * (gat - Qt) / W;
-      wout[g] = gw;
+    double *rec = A.rec + v * rs;
+    if (tid < DP) {
+      double t = 0.0;
+      for (int l = 0; l < lanes; ++l) t += sh[l * RW + tid];
+      rec[1 + tid] = t;
+    }
+    if (tid == 0) {
+      double t = 0.0;
+      for (int l = 0; l < lanes; ++l) t += shd[l * RW];
+      rec[0] = t;
     }
     __syncthreads();
-  }
-  if (side == 0 && tid == 0 && A.grad_sigma != nullptr) {
-    const double c2 = A.scale * A.scale, s3 = A.sigma * A.sigma * A.sigma;
-    const double Sxx = A.S_ws[p], Syy = A.S_ws[A.P + p], Sxy = A.S_ws[2 * A.P + p];
-    A.grad_sigma[p] = (cxx * Sxx + cyy * Syy + cxy * Sxy) / (c2 * s3);
-  }
+  });
+}
+
+template <int NT>
+__global__ void __launch_bounds__(NT) epig_write_kernel(EpilogueArgs A) {
+  __shared__ double sh[NT];
+  __shared__ double shd[NT];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int D = A.D, DP = A.DP, RW = DP;
+  const int lanes = NT / RW;
+  const int tid = threadIdx.x, d = tid % RW, pl = tid / RW;
+  const int rs = stats_stride(DP);
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t first, int64_t n) {
+    const EpiSide E = epi_side(A, p, side);
+    // totals of the side: point lane pl takes chunks pl, pl + lanes, ...
+    double Rd = 0.0, Q = 0.0;
+    for (int64_t k = pl; k < n; k += lanes) {
+      const double *r = A.rec + (first + k) * rs;
+      Rd += r[1 + d];
+      if (d == 0) Q += r[0];
+    }
+    sh[tid] = Rd;
+    shd[tid] = Q;
+    __syncthreads();
+    double Rtot = 0.0, Qtot = 0.0;
+    for (int l = 0; l < lanes; ++l) Rtot += sh[l * RW + d];
+    for (int l = 0; l < lanes; ++l) Qtot += shd[l * RW];
+    __syncthreads();
+    // mu . R
+    sh[tid] = (pl == 0 && d < D) ? E.mu[d] * Rtot : 0.0;
+    __syncthreads();
+    double muR = 0.0;
+    for (int k = 0; k < RW; ++k) muR += sh[k];
+    __syncthreads();
+    const double Qt = A.center ? Qtot - muR : Qtot;
+
+    const float *pts = side == 0 ? A.x : A.y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    float *gout = side == 0 ? A.grad_x : A.grad_y;
+    double *wout = side == 0 ? A.grad_wx : A.grad_wy;
+    const int64_t b = c * kChunk, e = b + kChunk < E.span ? b + kChunk : E.span;
+    for (int64_t i0 = b; i0 < e; i0 += lanes) {
+      const int64_t i = i0 + pl;
+      const bool inb = i < e;
+      const bool live = i < E.count && inb;
+      const int64_t g = E.s + i;
+      double a = 0.0, ga = 0.0, gx = 0.0;
+      if (live) gx = gen_gxt(A, side, g, d, E, a, ga);
+      if (A.center && live) gx -= a * Rtot;
+      if (inb && gout != nullptr && d < D) gout[g * D + d] = (float)gx;
+      // x_i . R across the RW threads of this point
+      sh[tid] = (live && d < D && A.center) ? (double)pts[g * D + d] * Rtot : 0.0;
+      __syncthreads();
+      if (d == 0 && inb && wout != nullptr && wmode != 3) {
+        double xr = 0.0;
+        for (int k = 0; k < RW; ++k) xr += sh[pl * RW + k];
+        const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
+        wout[g] = live ? weight_grad(wmode, m, ga - xr, Qt, E) : 0.0;
+      }
+      __syncthreads();
+    }
+  });
 }
 
 }  // namespace ra

@@ -1,6 +1,6 @@
 // ra_prep.cuh -- per-pair preparation: segment bounds, weight normalisation,
 // weighted centroids and packing of the points into the layouts the tile
-// kernels read.  One CTA per pair.
+// kernels read.
 //
 // Semantics follow rapidalign/kde.py:
 //   ptr checks            kde.py:124-156 (plus a monotonicity check)
@@ -8,10 +8,14 @@
 //                         115-121 (dense, clamped), 183-188 (uniform)
 //   centering             kde.py:77-81, 202-208, 246-253
 // Distances are translation invariant, so without centering both clouds are
-// still shifted by one common anchor (the x centroid); this keeps the packed
-// coordinates small and changes no result.
+// shifted by one common anchor (the unweighted mean of the x points); this
+// keeps the packed coordinates small and changes no result.
+//
+// Pipeline: segment_kernel (bounds, ptr checks, chunk map) -> stats_kernel (per-chunk partial sums) -> meta_kernel (per pair, combines
+// the partials in chunk order) -> pack kernels (per chunk).
 #pragma once
 
+#include "ra_chunks.cuh"
 #include "ra_common.cuh"
 
 namespace ra {
@@ -27,19 +31,35 @@ namespace ra {
 //   [4+3DP, 4+4DP)   anchor subtracted from y before packing
 __host__ __device__ __forceinline__ int meta_stride(int DP) { return 4 + 4 * DP; }
 
+// Partial-sum record of one chunk (fp64): [0] sum of effective weights,
+// [1] valid points, [2] last valid index (-1: none), [3, 3+DP) sum w' p,
+// [3+DP, 3+2DP) sum p over the valid points.  The backward epilogue reuses the
+// same slots for its (Q, R[DP]) partials.
+__host__ __device__ __forceinline__ int stats_stride(int DP) { return 3 + 2 * DP; }
+
+// Reduction width: power of two >= D (at least 4); thread (pl, d) of a CTA
+// handles dimension d of point lane pl.
+__host__ __device__ __forceinline__ int red_width(int D) {
+  int r = 4;
+  while (r < D) r <<= 1;
+  return r;
+}
+
 struct PrepArgs {
   int64_t P;
   int D, DP;     // DP: 3 for the D <= 3 path, else the padded generic width
   int layout;    // 0 ragged, 1 dense
   int wmode_x, wmode_y, center;
-  int packed3;   // 1: write the D <= 3 tile layout, 0: the generic layout
   int64_t num_x, num_y, nmax_x, nmax_y;
+  int64_t chunk_cap;  // capacity of the chunk records (host bound)
   float scale;   // sqrt(log2(e) / (2 sigma^2)): packed coords are scale * (p - anchor)
   const float *x, *y, *w_x, *w_y;
   const int64_t *ptr_x, *ptr_y;
   const uint8_t *mask_x, *mask_y;
   Seg *seg;
   double *meta;
+  double *rec;    // [chunk_cap][stats_stride]
+  int64_t *chcnt, *chx, *choff;  // [P], [P], [P + 1]
   int *err;
   // generic layout (D >= 4): coords [num * DP] (zero padded) and weights [num]
   float *Gx, *Gy, *Ax, *Ay;
@@ -53,187 +73,266 @@ __device__ __forceinline__ float eff_weight(const float *w, const uint8_t *mask,
   return v;
 }
 
-// Reduction width: power of two >= D (at least 4).
-__device__ __forceinline__ int red_width(int D) {
-  int r = 4;
-  while (r < D) r <<= 1;
-  return r;
-}
-
-template <int NT>
-__device__ void prep_side(const PrepArgs &A, int64_t p, int side, double *sh, int64_t *shl) {
+// Segment bounds, chunk counts and the chunk map; one CTA of 1024 threads.
+// Ragged bounds come from the running maximum of ptr, clamped to [0, num]:
+// for a valid ptr that is ptr itself, and for a malformed one (reported
+// through the error word) the segments still never overlap, so every bound
+// the host derived from num_x and num_y holds.
+__global__ void __launch_bounds__(1024) segment_kernel(PrepArgs A) {
+  __shared__ int64_t warp_tot[32];
+  __shared__ int64_t carry;
   const int tid = threadIdx.x;
-  const int D = A.D, DP = A.DP;
-  const float *pts = side == 0 ? A.x : A.y;
-  const float *w = side == 0 ? A.w_x : A.w_y;
-  const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
-  const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-  const int64_t num = side == 0 ? A.num_x : A.num_y;
-  const int64_t *ptr = side == 0 ? A.ptr_x : A.ptr_y;
-  const int64_t nmax = side == 0 ? A.nmax_x : A.nmax_y;
-  double *meta = A.meta + p * meta_stride(DP);
-  Seg &sg = A.seg[p];
-
-  // ---- segment bounds ------------------------------------------------------
-  int64_t s, span;
-  if (A.layout == 0) {
-    int64_t a0 = ptr[p], a1 = ptr[p + 1];
-    if (tid == 0) {
-      int e = 0;
-      if (p == 0 && a0 != 0) e |= kErrPtrStart;
-      if (p == A.P - 1 && a1 != num) e |= kErrPtrEnd;
-      if (a1 < a0) e |= kErrPtrOrder;
-      if (e) atomicOr(A.err, e);
-    }
-    // clamp so that a malformed ptr can never send a kernel out of bounds
-    a0 = a0 < 0 ? 0 : (a0 > num ? num : a0);
-    a1 = a1 < a0 ? a0 : (a1 > num ? num : a1);
-    s = a0;
-    span = a1 - a0;
-  } else {
-    s = p * nmax;
-    span = nmax;
-  }
-
-  // ---- pass 1: weight sum, weighted coordinate sums, last valid index -------
-  const int RW = red_width(D);
-  const int lanes = NT / RW;  // point lanes
-  const int d = tid % RW, pl = tid / RW;
-  double acc = 0.0, accu = 0.0, wsum = 0.0;
-  int64_t last = -1;
-  int64_t nvalid = 0;
-  for (int64_t i = pl; i < span; i += lanes) {
-    const int64_t g = s + i;
-    const float wi = eff_weight(w, mask, wmode, g);
-    const bool valid_pt = mask == nullptr || mask[g] != 0;
-    if (d < D) {
-      const double v = (double)pts[g * D + d];
-      acc += (double)wi * v;
-      if (valid_pt) accu += v;
-    }
-    if (d == 0) {
-      wsum += (double)wi;
-      const bool valid = mask == nullptr || mask[g] != 0;
-      if (valid) {
-        last = i;
-        ++nvalid;
+  int e = 0;
+  for (int side = 0; side < 2; ++side) {
+    const int64_t *ptr = side == 0 ? A.ptr_x : A.ptr_y;
+    const int64_t num = side == 0 ? A.num_x : A.num_y;
+    const int64_t nmax = side == 0 ? A.nmax_x : A.nmax_y;
+    if (tid == 0) carry = INT64_MIN;
+    __syncthreads();
+    for (int64_t base = 0; base < A.P; base += 1024) {
+      const int64_t p = base + tid;
+      int64_t s, span;
+      if (A.layout == 0) {
+        const int64_t v = p < A.P ? ptr[p] : INT64_MIN;
+        const int64_t pm = block_scan_step<true>(v, warp_tot, &carry);  // max(ptr[0..p])
+        if (p >= A.P) continue;
+        const int64_t nxt = ptr[p + 1];
+        if (p == 0 && v != 0) e |= kErrPtrStart;
+        if (p == A.P - 1 && nxt != num) e |= kErrPtrEnd;
+        if (nxt < v) e |= kErrPtrOrder;
+        int64_t a0 = pm, a1 = nxt > pm ? nxt : pm;
+        a0 = a0 < 0 ? 0 : (a0 > num ? num : a0);
+        a1 = a1 < 0 ? 0 : (a1 > num ? num : a1);
+        s = a0;
+        span = a1 - a0;
+      } else {
+        if (p >= A.P) continue;
+        s = p * nmax;
+        span = nmax;
+      }
+      Seg &sg = A.seg[p];
+      if (side == 0) {
+        sg.xs = s;
+        sg.xspan = span;
+        A.chx[p] = ceil_div(span, (int64_t)kChunk);
+      } else {
+        sg.ys = s;
+        sg.yspan = span;
+        A.chcnt[p] = A.chx[p] + ceil_div(span, (int64_t)kChunk);
       }
     }
+    __syncthreads();
   }
-  sh[tid] = acc;
-  __syncthreads();
-  double coord_sum = 0.0;
-  if (tid < RW)
-    for (int l = 0; l < lanes; ++l) coord_sum += sh[l * RW + tid];
-  __syncthreads();
-  sh[tid] = accu;
-  __syncthreads();
-  double plain_sum = 0.0;  // unweighted sum of the valid points (anchor)
-  if (tid < RW)
-    for (int l = 0; l < lanes; ++l) plain_sum += sh[l * RW + tid];
-  __syncthreads();
-  sh[tid] = wsum;
-  shl[tid] = last;
-  shl[NT + tid] = nvalid;
-  __syncthreads();
-  if (tid == 0) {
-    double W = 0.0;
-    int64_t lst = -1, nv = 0;
-    for (int l = 0; l < lanes; ++l) {
-      W += sh[l * RW];
-      lst = shl[l * RW] > lst ? shl[l * RW] : lst;
-      nv += shl[NT + l * RW];
+  if (e) atomicOr(A.err, e);
+  block_exclusive_scan(A.chcnt, A.choff, A.P, A.chunk_cap, warp_tot, &carry);
+}
+
+// Pass 1: per-chunk partial sums of weights and coordinates.
+template <int NT>
+__global__ void __launch_bounds__(NT) stats_kernel(PrepArgs A) {
+  __shared__ double sh[NT];
+  __shared__ int64_t shl[NT];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int tid = threadIdx.x;
+  const int D = A.D, DP = A.DP;
+  const int RW = red_width(D);
+  const int lanes = NT / RW;
+  const int d = tid % RW, pl = tid / RW;
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
+    const float *pts = side == 0 ? A.x : A.y;
+    const float *w = side == 0 ? A.w_x : A.w_y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    const Seg sg = A.seg[p];
+    const int64_t s = side == 0 ? sg.xs : sg.ys;
+    const int64_t span = side == 0 ? sg.xspan : sg.yspan;
+    const int64_t b = c * kChunk, e = b + kChunk < span ? b + kChunk : span;
+    double acc = 0.0, accu = 0.0, wsum = 0.0;
+    int64_t last = -1, nvalid = 0;
+    for (int64_t i = b + pl; i < e; i += lanes) {
+      const int64_t g = s + i;
+      const float wi = eff_weight(w, mask, wmode, g);
+      const bool valid = mask == nullptr || mask[g] != 0;
+      if (d < D) {
+        const double val = (double)pts[g * D + d];
+        acc += (double)wi * val;
+        if (valid) accu += val;
+      }
+      if (d == 0) {
+        wsum += (double)wi;
+        if (valid) {
+          last = i;
+          ++nvalid;
+        }
+      }
     }
-    const int64_t count = A.layout == 0 ? span : lst + 1;
+    double *rec = A.rec + v * stats_stride(DP);
+    // coordinate sums: reduce over the point lanes in lane order
+    sh[tid] = acc;
+    __syncthreads();
+    if (tid < DP) {
+      double t = 0.0;
+      for (int l = 0; l < lanes; ++l) t += sh[l * RW + tid];
+      rec[3 + tid] = t;
+    }
+    __syncthreads();
+    sh[tid] = accu;
+    __syncthreads();
+    if (tid < DP) {
+      double t = 0.0;
+      for (int l = 0; l < lanes; ++l) t += sh[l * RW + tid];
+      rec[3 + DP + tid] = t;
+    }
+    __syncthreads();
+    sh[tid] = wsum;
+    shl[tid] = last;
+    __syncthreads();
+    if (tid == 0) {
+      double W = 0.0;
+      int64_t lst = -1;
+      for (int l = 0; l < lanes; ++l) {
+        W += sh[l * RW];
+        lst = shl[l * RW] > lst ? shl[l * RW] : lst;
+      }
+      rec[0] = W;
+      rec[2] = (double)lst;
+    }
+    __syncthreads();
+    shl[tid] = nvalid;
+    __syncthreads();
+    if (tid == 0) {
+      int64_t nv = 0;
+      for (int l = 0; l < lanes; ++l) nv += shl[l * RW];
+      rec[1] = (double)nv;
+    }
+    __syncthreads();
+  });
+}
+
+__device__ __forceinline__ double warp_max(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
+
+// Pass 2: one warp per pair combines its chunk records (lane-strided over the
+// chunks, then a fixed shuffle tree) into the segment bounds, normalisers,
+// centroids and anchors.
+__global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
+  const int64_t p = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (p >= A.P) return;
+  const int D = A.D, DP = A.DP;
+  const int rs = stats_stride(DP);
+  double *meta = A.meta + p * meta_stride(DP);
+  const int64_t lo = A.choff[p], hi = A.choff[p + 1];
+  int64_t cxn = A.chx[p];
+  if (cxn > hi - lo) cxn = hi - lo;
+  int64_t count_x = 0;
+  for (int side = 0; side < 2; ++side) {
+    const int64_t first = side == 0 ? lo : lo + cxn;
+    const int64_t n = side == 0 ? cxn : (hi - lo) - cxn;
+    const double *r0 = A.rec + first * rs;
+    double W = 0.0, nv = 0.0, lst = -1.0;
+    for (int64_t c = lane; c < n; c += 32) {
+      W += r0[c * rs + 0];
+      nv += r0[c * rs + 1];
+      lst = fmax(lst, r0[c * rs + 2]);
+    }
+    W = warp_sum(W);
+    nv = warp_sum(nv);
+    lst = warp_max(lst);
+    const int64_t span = side == 0 ? A.seg[p].xspan : A.seg[p].yspan;
+    const int64_t count = A.layout == 0 ? span : (int64_t)lst + 1;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
     double Wn;
     if (wmode == 0) {
       Wn = 1.0;  // raw weights
     } else if (wmode == 3) {
-      Wn = nv > 0 ? (double)nv : 1.0;  // uniform 1/count
+      Wn = nv > 0 ? nv : 1.0;  // uniform 1/count
     } else if (wmode == 2) {
       Wn = W > 1e-8 ? W : 1e-8;  // clamp_min(1e-8)
     } else {
       Wn = W;
-      if (count > 0 && !(W > 0.0) && !(W != W)) atomicOr(A.err, (int)kErrWeightSum);
+      if (lane == 0 && count > 0 && !(W > 0.0) && !(W != W)) atomicOr(A.err, (int)kErrWeightSum);
       if (!(W > 0.0)) Wn = 1.0;  // keep the kernels finite; the error is reported
     }
-    meta[side] = Wn;
-    meta[2 + side] = W;
-    if (side == 0) {
-      sg.xs = s;
-      sg.xspan = span;
-      sg.xcount = count;
-    } else {
-      sg.ys = s;
-      sg.yspan = span;
-      sg.ycount = count;
+    if (lane == 0) {
+      meta[side] = Wn;
+      meta[2 + side] = W;
+      if (side == 0) A.seg[p].xcount = count;
+      else A.seg[p].ycount = count;
     }
-    sh[NT] = Wn;
-    shl[0] = nv;
-  }
-  __syncthreads();
-  const double Wn = sh[NT];
-  const int64_t nvalid_all = shl[0];
-  // centroid mu = sum_i a_i p_i = sum_i w'_i p_i / Wn
-  if (tid < DP) {
-    const double mu = tid < D ? coord_sum / Wn : 0.0;
-    meta[4 + side * DP + tid] = mu;
-  }
-  __syncthreads();
-  // anchors.  Centering: each cloud is shifted by its weighted centroid (the
-  // semantics).  Otherwise both clouds share one anchor, the unweighted mean
-  // of the valid x points (of the y points when x has none): distances do not
-  // change, and the packed coordinates stay as small as the clouds themselves
-  // whatever the weights are (raw weights may be negative).
-  if (tid < DP) {
-    const double mean = (tid < D && nvalid_all > 0) ? plain_sum / (double)nvalid_all : 0.0;
-    double anc;
-    if (A.center) {
-      anc = meta[4 + side * DP + tid];
-    } else if (side == 0) {
-      anc = mean;
-    } else {
-      anc = sg.xcount > 0 ? meta[4 + 2 * DP + tid] : mean;
-    }
-    meta[4 + (2 + side) * DP + tid] = anc;
-    sh[NT + 1 + tid] = anc;
-  }
-  __syncthreads();
-
-  // ---- pass 2 (generic layout only): pack ---------------------------------
-  // (the D <= 3 tile layout is written by pack3_kernel once the tile bases
-  // of all pairs are known)
-  const int64_t count = side == 0 ? sg.xcount : sg.ycount;
-  const float scale = A.scale;
-  if (!A.packed3) {
-    float *Gp = side == 0 ? A.Gx : A.Gy;
-    float *Ap = side == 0 ? A.Ax : A.Ay;
-    for (int64_t i = pl; i < count; i += lanes) {
-      const int64_t g = s + i;
-      if (d < DP) {
-        float v = 0.f;
-        if (d < D) v = scale * (float)((double)pts[g * D + d] - sh[NT + 1 + d]);
-        Gp[g * DP + d] = v;
+    if (side == 0) count_x = count;
+    for (int dd = 0; dd < DP; ++dd) {
+      double cs = 0.0, ps = 0.0;
+      for (int64_t c = lane; c < n; c += 32) {
+        cs += r0[c * rs + 3 + dd];
+        ps += r0[c * rs + 3 + DP + dd];
       }
-      if (d == 0) {
-        const float wi = eff_weight(w, mask, wmode, g);
-        Ap[g] = (float)((double)wi / Wn);
+      cs = warp_sum(cs);
+      ps = warp_sum(ps);
+      if (lane == 0) {
+        // centroid mu = sum_i a_i p_i = sum_i w'_i p_i / Wn; plain mean for the anchor
+        const double mu = dd < D ? cs / Wn : 0.0;
+        const double mean = (dd < D && nv > 0) ? ps / nv : 0.0;
+        meta[4 + side * DP + dd] = mu;
+        if (side == 0) {
+          meta[4 + 2 * DP + dd] = mean;  // provisional: replaced by the anchor below
+        } else {
+          // anchors.  Centering: each cloud is shifted by its weighted
+          // centroid (the semantics).  Otherwise both clouds share one anchor,
+          // the unweighted mean of the valid x points (of the y points when x
+          // has none): distances do not change, and the packed coordinates
+          // stay as small as the clouds themselves whatever the weights are.
+          double ax, ay;
+          if (A.center) {
+            ax = meta[4 + dd];
+            ay = mu;
+          } else {
+            ax = count_x > 0 ? meta[4 + 2 * DP + dd] : mean;
+            ay = ax;
+          }
+          meta[4 + 2 * DP + dd] = ax;
+          meta[4 + 3 * DP + dd] = ay;
+        }
       }
     }
   }
-  __syncthreads();
 }
 
+// Generic layout (D >= 4): scaled, anchored coordinates and normalised weights.
 template <int NT>
-__global__ void __launch_bounds__(NT) prep_kernel(PrepArgs A) {
-  // sh: NT doubles for reductions + 1 + DP anchors; shl: 2*NT ints
-  extern __shared__ double smem[];
-  double *sh = smem;
-  int64_t *shl = (int64_t *)(smem + NT + 1 + 256);
-  const int64_t p = blockIdx.x;
-  if (p >= A.P) return;
-  prep_side<NT>(A, p, 0, sh, shl);
-  prep_side<NT>(A, p, 1, sh, shl);
+__global__ void __launch_bounds__(NT) packg_kernel(PrepArgs A) {
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int D = A.D, DP = A.DP;
+  const int RW = red_width(D);
+  const int lanes = NT / RW;
+  const int d = threadIdx.x % RW, pl = threadIdx.x / RW;
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t, int64_t) {
+    const Seg sg = A.seg[p];
+    const int64_t s = side == 0 ? sg.xs : sg.ys;
+    const int64_t count = side == 0 ? sg.xcount : sg.ycount;
+    const float *pts = side == 0 ? A.x : A.y;
+    const float *w = side == 0 ? A.w_x : A.w_y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    float *Gp = side == 0 ? A.Gx : A.Gy;
+    float *Ap = side == 0 ? A.Ax : A.Ay;
+    const double *meta = A.meta + p * meta_stride(DP);
+    const double Wn = meta[side];
+    const double *anc = meta + 4 + (2 + side) * DP;
+    const int64_t b = c * kChunk, e = b + kChunk < count ? b + kChunk : count;
+    for (int64_t i = b + pl; i < e; i += lanes) {
+      const int64_t g = s + i;
+      if (d < DP) {
+        float val = 0.f;
+        if (d < D) val = A.scale * (float)((double)pts[g * D + d] - anc[d]);
+        Gp[g * DP + d] = val;
+      }
+      if (d == 0) Ap[g] = (float)((double)eff_weight(w, mask, wmode, g) / Wn);
+    }
+  });
 }
 
 // ---------------------------------------------------------------------------
@@ -253,6 +352,7 @@ struct PackArgs {
   int wmode_x, wmode_y;
   const Seg *seg;
   const double *meta;
+  const int64_t *choff, *chx;
   const int64_t *tbase_x, *tbase_y;  // [P + 1]
   int64_t max_tiles_x, max_tiles_y;
   ulonglong2 *tiles_x, *tiles_y;     // [tiles][nq = 2][64]
@@ -260,45 +360,45 @@ struct PackArgs {
 
 template <int NT>
 __global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
-  const int64_t p = blockIdx.x >> 1;
-  const int side = blockIdx.x & 1;
-  if (p >= A.P) return;
-  const Seg sg = A.seg[p];
-  const int D = A.D;
-  const int64_t s = side == 0 ? sg.xs : sg.ys;
-  const int64_t count = side == 0 ? sg.xcount : sg.ycount;
-  const int64_t t0 = (side == 0 ? A.tbase_x : A.tbase_y)[p];
-  const int64_t t1 = (side == 0 ? A.tbase_x : A.tbase_y)[p + 1];
-  const int64_t tmax = side == 0 ? A.max_tiles_x : A.max_tiles_y;
-  const float *pts = side == 0 ? A.x : A.y;
-  const float *w = side == 0 ? A.w_x : A.w_y;
-  const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
-  const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-  ulonglong2 *tiles = side == 0 ? A.tiles_x : A.tiles_y;
-  const double *meta = A.meta + p * meta_stride(3);
-  const double Wn = meta[side];
-  const float ax = (float)meta[4 + (2 + side) * 3 + 0];
-  const float ay = (float)meta[4 + (2 + side) * 3 + 1];
-  const float az = (float)meta[4 + (2 + side) * 3 + 2];
-  const float scale = A.scale;
-  const int nq = A.nq;
-  const int64_t npad = (t1 - t0) * kTile;
-  for (int64_t i = threadIdx.x; i < npad; i += NT) {
-    const int64_t t = t0 + i / kTile;
-    if (t >= tmax) break;  // malformed ptr overflowing the bound (error already flagged)
-    float c0 = 0.f, c1 = 0.f, c2 = 0.f, a = 0.f;
-    if (i < count) {
-      const int64_t g = s + i;
-      a = (float)((double)eff_weight(w, mask, wmode, g) / Wn);
-      c0 = scale * (pts[g * D + 0] - ax);
-      if (D > 1) c1 = scale * (pts[g * D + 1] - ay);
-      if (D > 2) c2 = scale * (pts[g * D + 2] - az);
+  const ChunkMap M{A.P, A.choff, A.chx};
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t, int64_t) {
+    const Seg sg = A.seg[p];
+    const int D = A.D;
+    const int64_t s = side == 0 ? sg.xs : sg.ys;
+    const int64_t count = side == 0 ? sg.xcount : sg.ycount;
+    const int64_t t0 = (side == 0 ? A.tbase_x : A.tbase_y)[p];
+    const int64_t t1 = (side == 0 ? A.tbase_x : A.tbase_y)[p + 1];
+    const int64_t tmax = side == 0 ? A.max_tiles_x : A.max_tiles_y;
+    const float *pts = side == 0 ? A.x : A.y;
+    const float *w = side == 0 ? A.w_x : A.w_y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    ulonglong2 *tiles = side == 0 ? A.tiles_x : A.tiles_y;
+    const double *meta = A.meta + p * meta_stride(3);
+    const double Wn = meta[side];
+    const float ax = (float)meta[4 + (2 + side) * 3 + 0];
+    const float ay = (float)meta[4 + (2 + side) * 3 + 1];
+    const float az = (float)meta[4 + (2 + side) * 3 + 2];
+    const float scale = A.scale;
+    const int nq = A.nq;
+    const int64_t npad = (t1 - t0) * kTile;
+    const int64_t b = c * kChunk, e = b + kChunk < npad ? b + kChunk : npad;
+    for (int64_t i = b + threadIdx.x; i < e; i += NT) {
+      const int64_t t = t0 + i / kTile;
+      if (t >= tmax) break;  // malformed ptr overflowing the bound (error already flagged)
+      float c0 = 0.f, c1 = 0.f, c2 = 0.f, a = 0.f;
+      if (i < count) {
+        const int64_t g = s + i;
+        a = (float)((double)eff_weight(w, mask, wmode, g) / Wn);
+        c0 = scale * (pts[g * D + 0] - ax);
+        if (D > 1) c1 = scale * (pts[g * D + 1] - ay);
+        if (D > 2) c2 = scale * (pts[g * D + 2] - az);
+      }
+      ulonglong2 *tp = tiles + t * (int64_t)(nq * kTile) + (i % kTile);
+      tp[0] = make_ulonglong2(pk2u(c0, c0), pk2u(c1, c1));
+      tp[kTile] = make_ulonglong2(pk2u(c2, c2), pk2u(a, a));
     }
-    ulonglong2 *tp = tiles + t * (int64_t)(nq * kTile) + (i % kTile);
-    tp[0] = make_ulonglong2(pk2u(c0, c0), pk2u(c1, c1));
-    tp[kTile] = make_ulonglong2(pk2u(c2, c2), pk2u(a, a));
-  }
+  });
 }
-
 
 }  // namespace ra

@@ -4,6 +4,13 @@
 // (x-y, x-x, y-y, y-x), so each point's row sums are complete when its CTA
 // finishes and are written without atomics.  This path covers any D; the
 // D <= 3 point-cloud path is ra_tiles3.cuh.
+//
+// The row sums are kept in folded form, G_i = x'_i s_i - T_i with
+// T_i = sum_j w_j k_ij y'_j.  In a self block the diagonal term (j == i,
+// k_ii = 1) would put w_i x'_i into T_i and w_i into s_i, to cancel in G_i only
+// up to fp32 rounding -- an error far above the true G_i when the kernel is
+// narrow.  The stored sums therefore leave the diagonal out; it re-enters
+// exactly: in the pair sum here and in dL/da in the epilogue.
 #pragma once
 
 #include "ra_common.cuh"
@@ -21,6 +28,33 @@ struct TilesGArgs {
   int need_rows;         // 1: write the per-point sums (backward requested)
   int shard_index, shard_count;  // evaluate only items shard_index + k * shard_count
 };
+
+// One staged column tile against this thread's row: st += sum w, T += sum w y'
+// (and sgt += sum w r^2).  DIAG: the term in column `diag` is left out.
+template <int DP, int MODE, bool DIAG>
+__device__ __forceinline__ void gen_cols(const float *ycol, const float *bcol,
+                                         const float (&xr)[DP], float (&T)[DP], float &st,
+                                         float &sgt, int diag) {
+  constexpr bool SIG = MODE == 2;
+#pragma unroll 1
+  for (int jj = 0; jj < kGenCols; ++jj) {
+    const float *yj = ycol + jj * DP;
+    float r2 = 0.f;
+#pragma unroll
+    for (int d = 0; d < DP; ++d) {
+      const float t = xr[d] - yj[d];
+      r2 = fmaf(t, t, r2);
+    }
+    float w = bcol[jj] * ex2(-r2);
+    if (DIAG && jj == diag) w = 0.f;
+    st += w;
+    if (SIG) sgt = fmaf(w, r2, sgt);
+    if (MODE >= 1) {
+#pragma unroll
+      for (int d = 0; d < DP; ++d) T[d] = fmaf(w, yj[d], T[d]);
+    }
+  }
+}
 
 template <int DP, int MODE>
 __global__ void __launch_bounds__(kGenRows) tilesg_kernel(TilesGArgs A) {
@@ -43,6 +77,7 @@ __global__ void __launch_bounds__(kGenRows) tilesg_kernel(TilesGArgs A) {
   const float *Ac = cols_x ? A.Ax : A.Ay;
   float *acc = rows_x ? A.accX : A.accY;
   const int off = (o == 0 || o == 3) ? 1 + DP : 0;
+  const bool self = (o == 1 || o == 2);
 
   const int tid = threadIdx.x;
   const int64_t row = (int64_t)item.tile * kGenRows + tid;
@@ -70,22 +105,15 @@ __global__ void __launch_bounds__(kGenRows) tilesg_kernel(TilesGArgs A) {
     }
     __syncthreads();
     float st = 0.f, sgt = 0.f;
-#pragma unroll 1
-    for (int jj = 0; jj < kGenCols; ++jj) {
-      const float *yj = ycol + jj * DP;
-      float r2 = 0.f;
-#pragma unroll
-      for (int d = 0; d < DP; ++d) {
-        const float t = xr[d] - yj[d];
-        r2 = fmaf(t, t, r2);
-      }
-      const float w = bcol[jj] * ex2(-r2);
-      st += w;
-      if (SIG) sgt = fmaf(w, r2, sgt);
-      if (MODE >= 1) {
-#pragma unroll
-        for (int d = 0; d < DP; ++d) T[d] = fmaf(w, yj[d], T[d]);
-      }
+    // Only the column tiles that meet this CTA's rows in a self block hold
+    // diagonal terms; they take the predicated loop, all others the plain one.
+    const int64_t r0 = (int64_t)item.tile * kGenRows;
+    if (self && j0 < r0 + kGenRows && j0 + kGenCols > r0) {
+      const int64_t dj = row - j0;  // column of this row's diagonal term in the tile
+      const int diag = (dj >= 0 && dj < kGenCols) ? (int)dj : -1;
+      gen_cols<DP, MODE, true>(ycol, bcol, xr, T, st, sgt, diag);
+    } else {
+      gen_cols<DP, MODE, false>(ycol, bcol, xr, T, st, sgt, -1);
     }
     s += st;
     s64 += (double)st;
@@ -98,8 +126,9 @@ __global__ void __launch_bounds__(kGenRows) tilesg_kernel(TilesGArgs A) {
 #pragma unroll
     for (int d = 0; d < DP; ++d) dst[1 + d] = T[d];
   }
-  // pair partials: K from x-y, x-x and y-y only (y-x would count Kxy twice)
-  double kv = (double)a * s64, sv = (double)a * sg64;
+  // pair partials: K from x-y, x-x and y-y only (y-x would count Kxy twice);
+  // a self block adds the diagonal a_i * a_i * k_ii = a_i^2 here
+  double kv = (double)a * (s64 + (self ? (double)a : 0.0)), sv = (double)a * sg64;
   kv = warp_sum(kv);
   sv = warp_sum(sv);
   const int lane = tid & 31, wid = tid >> 5;

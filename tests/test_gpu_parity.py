@@ -252,6 +252,14 @@ def test_device_detected_errors(cuda_device):
                             tgt_ptr=torch.tensor([0, 5, 10], device=dev), src_w=w)
     with pytest.raises(ValueError, match="weights must sum to a positive value"):
         ra.kde_mmd_loss(x, x, x_w=-torch.ones(10, device=dev))
+    # a decreasing ptr whose clamped ranges would overlap (and, summed, need
+    # more tiles than the points allow) is reported and stays in bounds
+    n = 6400
+    xb = torch.randn(n, 3, device=dev)
+    bad = torch.tensor([0, n, 0, n], device=dev)
+    good = torch.tensor([0, 2000, 4000, n], device=dev)
+    with pytest.raises(ValueError, match="ptr offsets must match node stacks"):
+        ra.pyg_kde_mmd_loss(xb, xb, src_ptr=bad, tgt_ptr=good)
     with pytest.raises(ValueError, match="sorted"):
         ra.pyg_kde_mmd_loss(x, x, src_batch=torch.tensor([0, 1] * 5, device=dev),
                             tgt_batch=torch.zeros(10, dtype=torch.long, device=dev))
@@ -324,3 +332,64 @@ def test_mid_size_single_pair_matches_oracle(cuda_device):
     assert_loss(_np(loss), r.loss, r.Kxx, r.Kyy)
     assert_grad(_np(xt.grad), r.grad_x)
     assert_grad(_np(yt.grad), r.grad_y)
+
+
+def test_multi_chunk_dense_masked_with_weights(cuda_device):
+    """Rows of several 1024-point chunks: masked holes and an unmasked-free
+    tail (count < Nmax), weights, centering; every gradient."""
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(14)
+    B, Nx, Ny, D = 3, 2600, 2300, 3
+    x = rng.standard_normal((B, Nx, D)).astype(np.float32)
+    y = (rng.standard_normal((B, Ny, D)) * 0.8 + 0.1).astype(np.float32)
+    wx = rng.uniform(0.2, 1.0, (B, Nx)).astype(np.float32)
+    wy = rng.uniform(0.2, 1.0, (B, Ny)).astype(np.float32)
+    mx = rng.random((B, Nx)) < 0.8
+    my = rng.random((B, Ny)) < 0.9
+    mx[0, 1500:] = False  # count 1500: the last chunk of the row is padding
+    my[2, 1100:] = False
+    dev = cuda_device
+    xt, yt = _cuda(x, dev, True), _cuda(y, dev, True)
+    wxt, wyt = _cuda(wx, dev, True), _cuda(wy, dev, True)
+    outs = ra.kde_mmd_loss_dense(xt, yt, _cuda(mx, dev), _cuda(my, dev), x_w=wxt, y_w=wyt,
+                                 sigma=0.3, center=True)
+    up = [rng.uniform(0.5, 1.5, B) for _ in range(4)]
+    total = sum((torch.as_tensor(u, device=dev) * o.double()).sum() for u, o in zip(up, outs))
+    total.backward()
+    r = O.kde_mmd_loss_dense(x, y, mx, my, wx, wy, sigma=0.3, center=True, upstream=up)
+    assert_k(_np(outs[1]), r.Kxx)
+    assert_k(_np(outs[2]), r.Kyy)
+    assert_k(_np(outs[3]), r.Kxy)
+    assert_loss(_np(outs[0]), r.loss, r.Kxx, r.Kyy)
+    assert_grad(_np(xt.grad), r.grad_x, "grad_x")
+    assert_grad(_np(yt.grad), r.grad_y, "grad_y")
+    assert_grad(_np(wxt.grad), r.grad_wx, "grad_wx")
+    assert_grad(_np(wyt.grad), r.grad_wy, "grad_wy")
+
+
+@pytest.mark.parametrize("d", [5, 16])
+def test_multi_chunk_generic_dims(d, cuda_device):
+    """Generic-D layout with pairs of several chunks next to tiny ones."""
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(15 + d)
+    x, y, ptr_x, ptr_y = _ragged(rng, [3100, 3, 0, 1500], [2900, 1, 4, 1700], d)
+    wx = rng.uniform(0.2, 1.0, x.shape[0]).astype(np.float32)
+    wy = rng.uniform(0.2, 1.0, y.shape[0]).astype(np.float32)
+    dev = cuda_device
+    xt, yt = _cuda(x, dev, True), _cuda(y, dev, True)
+    wxt, wyt = _cuda(wx, dev, True), _cuda(wy, dev, True)
+    sigma = 0.2 * np.sqrt(d)
+    outs = ra.pyg_kde_mmd_loss(xt, yt, src_ptr=_cuda(ptr_x, dev), tgt_ptr=_cuda(ptr_y, dev),
+                               src_w=wxt, tgt_w=wyt, sigma=sigma, center=True)
+    up = [rng.uniform(0.5, 1.5, 4) for _ in range(4)]
+    total = sum((torch.as_tensor(u, device=dev) * o.double()).sum() for u, o in zip(up, outs))
+    total.backward()
+    r = O.pyg_kde_mmd_loss(x, y, ptr_x, ptr_y, wx, wy, sigma=sigma, center=True, upstream=up)
+    assert_k(_np(outs[1]), r.Kxx)
+    assert_k(_np(outs[2]), r.Kyy)
+    assert_k(_np(outs[3]), r.Kxy)
+    assert_loss(_np(outs[0]), r.loss, r.Kxx, r.Kyy)
+    assert_grad(_np(xt.grad), r.grad_x, "grad_x")
+    assert_grad(_np(yt.grad), r.grad_y, "grad_y")
+    assert_grad(_np(wxt.grad), r.grad_wx, "grad_wx")
+    assert_grad(_np(wyt.grad), r.grad_wy, "grad_wy")
