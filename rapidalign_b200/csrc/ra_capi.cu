@@ -301,7 +301,10 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   }
   const unsigned cgrid = chunk_grid(L);
   segment_kernel<<<1, 1024, 0, st>>>(pa);
-  stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+  if (L.packed3)
+    stats3_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+  else
+    stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
   meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
   g_launches += 3;
   if (!L.packed3) {

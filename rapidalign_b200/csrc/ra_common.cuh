@@ -97,6 +97,37 @@ __device__ __forceinline__ double block_sum(double v, double *sh) {
   return t;
 }
 
+// Block-wide sums of N doubles at once (all threads get the results): a
+// shuffle tree inside each warp, then the warps in order -- deterministic.
+// `sh` must hold (blockDim.x / 32) * N doubles; two __syncthreads.
+template <int N>
+__device__ __forceinline__ void block_sum_n(double (&v)[N], double *sh) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int k = 0; k < N; ++k) v[k] = warp_sum(v[k]);
+  if (lane == 0) {
+#pragma unroll
+    for (int k = 0; k < N; ++k) sh[wid * N + k] = v[k];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    double t = 0.0;
+    for (int w = 0; w < nw; ++w) t += sh[w * N + k];
+    v[k] = t;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ long long warp_max(long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const long long u = __shfl_xor_sync(kFull, v, o);
+    v = u > v ? u : v;
+  }
+  return v;
+}
+
 // ---------------------------------------------------------------------------
 // Internal data structures (live in the caller's workspace).
 // ---------------------------------------------------------------------------

@@ -174,12 +174,11 @@ __device__ __forceinline__ double weight_grad(int wmode, double m, double gat, d
 // Pass 1: per chunk, R = sum dL/dx~ (D values) and Q = sum a dL/da.
 template <int NT>
 __global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
-  __shared__ double sh[NT / 32];
+  __shared__ double sh[(NT / 32) * 4];
   const ChunkMap M{A.P, A.choff, A.chx};
   const int rs = stats_stride(A.DP);
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
     const EpiSide E = epi_side(A, p, side);
-    const int D = A.D;
     const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
     const int64_t b = c * kChunk, e = b + kChunk < E.count ? b + kChunk : E.count;
     double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
@@ -191,12 +190,11 @@ __global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
       Q += a * ga;
     }
     double *rec = A.rec + v * rs;
-    Q = block_sum(Q, sh);
-    if (threadIdx.x == 0) rec[0] = Q;
+    double vals[4] = {Q, R[0], R[1], R[2]};
+    block_sum_n<4>(vals, sh);
+    if (threadIdx.x == 0) {
 #pragma unroll
-    for (int d = 0; d < 3; ++d) {
-      const double t = block_sum(R[d], sh);
-      if (threadIdx.x == 0) rec[1 + d] = t;
+      for (int k = 0; k < 4; ++k) rec[k] = vals[k];
     }
   });
 }
@@ -206,7 +204,7 @@ __global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
 // points (zeros for the padded tail of a dense row).
 template <int NT>
 __global__ void __launch_bounds__(NT) epi3_write_kernel(EpilogueArgs A) {
-  __shared__ double sh[NT / 32];
+  __shared__ double sh[(NT / 32) * 4];
   const ChunkMap M{A.P, A.choff, A.chx};
   const int rs = stats_stride(A.DP);
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t first, int64_t n) {
@@ -220,9 +218,11 @@ __global__ void __launch_bounds__(NT) epi3_write_kernel(EpilogueArgs A) {
       R[1] += r[2];
       R[2] += r[3];
     }
-    Q = block_sum(Q, sh);
+    double vals[4] = {Q, R[0], R[1], R[2]};
+    block_sum_n<4>(vals, sh);
+    Q = vals[0];
 #pragma unroll
-    for (int d = 0; d < 3; ++d) R[d] = block_sum(R[d], sh);
+    for (int d = 0; d < 3; ++d) R[d] = vals[1 + d];
     double Qt = Q;
     if (A.center) {
 #pragma unroll

@@ -209,6 +209,66 @@ __global__ void __launch_bounds__(NT) stats_kernel(PrepArgs A) {
   });
 }
 
+// Pass 1 for D <= 3: one thread per point, all nine partial sums reduced at
+// once (shuffle trees, then the 8 warps in order) -- one barrier pair per
+// chunk instead of the generic kernel's three lane-serial reductions.
+template <int NT>
+__global__ void __launch_bounds__(NT) stats3_kernel(PrepArgs A) {
+  __shared__ double sh[(NT / 32) * 8];
+  __shared__ long long shl[NT / 32];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int D = A.D;
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
+    const float *pts = side == 0 ? A.x : A.y;
+    const float *w = side == 0 ? A.w_x : A.w_y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    const Seg sg = A.seg[p];
+    const int64_t s = side == 0 ? sg.xs : sg.ys;
+    const int64_t span = side == 0 ? sg.xspan : sg.yspan;
+    const int64_t b = c * kChunk, e = b + kChunk < span ? b + kChunk : span;
+    // vals: W, valid count, sum w' p (3), sum p over valid points (3)
+    double vals[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+    long long last = -1;
+    for (int64_t i = b + tid; i < e; i += NT) {
+      const int64_t g = s + i;
+      const float wi = eff_weight(w, mask, wmode, g);
+      const bool valid = mask == nullptr || mask[g] != 0;
+      vals[0] += (double)wi;
+#pragma unroll
+      for (int d = 0; d < 3; ++d) {
+        if (d < D) {
+          const double pv = (double)pts[g * D + d];
+          vals[2 + d] += (double)wi * pv;
+          if (valid) vals[5 + d] += pv;
+        }
+      }
+      if (valid) {
+        vals[1] += 1.0;
+        last = i;
+      }
+    }
+    last = warp_max(last);
+    if (lane == 0) shl[wid] = last;
+    block_sum_n<8>(vals, sh);  // its first barrier also publishes shl
+    if (tid == 0) {
+      double *rec = A.rec + v * stats_stride(3);
+      long long lst = -1;
+      for (int k = 0; k < NT / 32; ++k) lst = shl[k] > lst ? shl[k] : lst;
+      rec[0] = vals[0];
+      rec[1] = vals[1];
+      rec[2] = (double)lst;
+#pragma unroll
+      for (int d = 0; d < 3; ++d) {
+        rec[3 + d] = vals[2 + d];
+        rec[6 + d] = vals[5 + d];
+      }
+    }
+    // the next chunk's shl writes happen after block_sum_n's trailing barrier
+  });
+}
+
 __device__ __forceinline__ double warp_max(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFull, v, o));
