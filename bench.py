@@ -221,7 +221,7 @@ def cpu_units(name: str):
             def run(cores, side=side, sel=sel):
                 O.rows_sums(side, x, y, a, b, 0.2, sel, nthreads=cores)
                 return float(sel.size * (n + m))
-            yield run, f"row blocks of {rows} rows of the {n}-point pair (both clouds)"
+            yield run, f"row blocks of {rows} rows of the {n}-point pair (both clouds, cycling)"
     elif name == "dense":
         xb, yb, lx, ly = dense_data(0)
         for c in range(10 ** 9):
@@ -233,14 +233,14 @@ def cpu_units(name: str):
                 O.raw_sums(x, y, np.full(n, 1.0 / n), np.full(m, 1.0 / m), [0, n], [0, m],
                            SIGMA, nthreads=cores)
                 return float(n * n + m * m + n * m)
-            yield run, "clouds of the dense batch (valid prefixes)"
+            yield run, "clouds of the dense batch (valid prefixes, in order, cycling)"
     else:
-        for g in range(10 ** 9):
+        for u in range(10 ** 9):
             if name == "embed128":
-                sx, sy = embed_graph(g)
+                sx, sy = embed_graph(u % 1024)
                 sigma = 1.0
             else:
-                sx, sy = ragged_graph(g)
+                sx, sy = ragged_graph(u % GRAPHS_PER_GPU)
                 sigma = SIGMA
             x, y = f64(sx), f64(sy)
 
@@ -249,7 +249,7 @@ def cpu_units(name: str):
                 O.raw_sums(x, y, np.full(n, 1.0 / n), np.full(m, 1.0 / m), [0, n], [0, m],
                            sigma, nthreads=cores)
                 return float(n * n + m * m + n * m)
-            yield run, f"graphs of the {name} batch"
+            yield run, f"graphs of the {name} batch (in order, cycling)"
 
 
 def cpu_baseline(name: str, budget_s: float = 15.0):
