@@ -56,6 +56,7 @@ enum ra_status {
   RA_ERR_WEIGHT_SUM = 19,         /* weights must sum to a positive value per segment */
   RA_ERR_STATE = 20,              /* backward called without a matching forward state */
   RA_ERR_SCRATCH_LIMIT = 21,      /* problem needs more than the fixed no-alloc scratch */
+  RA_ERR_DEVICE_TIMEOUT = 22,     /* a bounded wait inside a kernel expired (reported, not hung) */
 };
 
 /* Human-readable name of a status code (static string). */
@@ -77,6 +78,13 @@ enum ra_weights {
   RA_WEIGHTS_UNIFORM = 3      /* a_i = 1 / count_seg; w ignored (kde.py:183-188) */
 };
 
+/* Kernel family for the generic (dim >= 4) layout. */
+enum ra_engine {
+  RA_ENGINE_AUTO = 0,
+  RA_ENGINE_SIMT = 1,   /* one thread per row, columns staged in shared memory */
+  RA_ENGINE_TENSOR = 2  /* tcgen05 (3xTF32) Gram and weighted-sum GEMMs */
+};
+
 typedef struct ra_kde_desc {
   int64_t num_pairs;   /* P (ragged) or B (dense) */
   int32_t dim;         /* D >= 1 */
@@ -94,6 +102,10 @@ typedef struct ra_kde_desc {
   int32_t shard_count; /* this process evaluates work items shard_index, shard_index +
                           shard_count, ...; 0 or 1 = no split (see ra_kde_forward) */
   double sigma;        /* bandwidth, > 0 */
+  int32_t engine;      /* kernel family for dim >= 4 (enum ra_engine): RA_ENGINE_AUTO =
+                          tensor cores when the padded dim is 32, 64 or 128, else SIMT;
+                          RA_ENGINE_TENSOR on another padded dim is
+                          RA_ERR_INVALID_ARGUMENT.  Ignored for dim <= 3. */
 } ra_kde_desc;
 
 typedef struct ra_kde_inputs {

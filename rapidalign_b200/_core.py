@@ -46,6 +46,7 @@ class Spec:
     # split evaluation of one problem across a process group (see shard.py)
     shard_index: int = 0
     shard_count: int = 1
+    engine: int = 0  # _lib.RA_ENGINE_*: kernel family for dim >= 4 (0 = automatic)
     weight_error_message: str = "weights must sum to a positive value per segment"
 
     def desc(self, need_grad: bool, need_sigma_grad: bool) -> _lib.RaKdeDesc:
@@ -65,6 +66,7 @@ class Spec:
         d.shard_index = self.shard_index
         d.shard_count = self.shard_count
         d.sigma = float(self.sigma)
+        d.engine = int(self.engine)
         return d
 
 

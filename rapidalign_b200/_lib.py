@@ -30,6 +30,7 @@ RA_ERR_PTR_ORDER = 18
 RA_ERR_WEIGHT_SUM = 19
 RA_ERR_STATE = 20
 RA_ERR_SCRATCH_LIMIT = 21
+RA_ERR_DEVICE_TIMEOUT = 22
 
 RA_LAYOUT_RAGGED = 0
 RA_LAYOUT_DENSE = 1
@@ -38,6 +39,10 @@ RA_WEIGHTS_RAW = 0
 RA_WEIGHTS_SUM = 1
 RA_WEIGHTS_SUM_CLAMPED = 2
 RA_WEIGHTS_UNIFORM = 3
+
+RA_ENGINE_AUTO = 0
+RA_ENGINE_SIMT = 1
+RA_ENGINE_TENSOR = 2
 
 
 class RaKdeDesc(ctypes.Structure):
@@ -57,6 +62,7 @@ class RaKdeDesc(ctypes.Structure):
         ("shard_index", ctypes.c_int32),
         ("shard_count", ctypes.c_int32),
         ("sigma", ctypes.c_double),
+        ("engine", ctypes.c_int32),
     ]
 
 

@@ -19,6 +19,7 @@
 #include "ra_epilogue.cuh"
 #include "ra_plan.cuh"
 #include "ra_prep.cuh"
+#include "ra_tc.cuh"
 #include "ra_tiles3.cuh"
 #include "ra_tilesg.cuh"
 
@@ -71,6 +72,11 @@ bool desc_ok(const ra_kde_desc *d) {
   if (d->weights_x < 0 || d->weights_x > 3 || d->weights_y < 0 || d->weights_y > 3) return false;
   if (d->num_x > ((int64_t)1 << 40) || d->num_y > ((int64_t)1 << 40)) return false;
   if (d->num_pairs > ((int64_t)1 << 30)) return false;
+  if (d->engine < RA_ENGINE_AUTO || d->engine > RA_ENGINE_TENSOR) return false;
+  if (d->engine == RA_ENGINE_TENSOR && d->dim > 3) {
+    const int dp = generic_dp(d->dim);
+    if (dp != 32 && dp != 64 && dp != 128) return false;
+  }
   if (d->shard_count < 0 || (d->shard_count > 1 &&
                              (d->shard_index < 0 || d->shard_index >= d->shard_count)))
     return false;
@@ -219,6 +225,48 @@ void launch_tilesg_dp(int mode, int64_t grid, const TilesGArgs &T, cudaStream_t 
     tilesg_kernel<DP, 2><<<(unsigned)grid, kGenRows, 0, st>>>(T);
 }
 
+// Tensor-core path: a persistent grid, as many CTAs per SM as TMEM allows.
+template <int DP, int MODE>
+int launch_tilestc_dm(int64_t max_items, const TilesGArgs &T, cudaStream_t st) {
+  const size_t smem = tc_smem_request(DP);
+  static_assert(tc_smem_bytes(DP) <= tc_smem_request(DP), "shared memory request too small");
+  if (cudaFuncSetAttribute(tilestc_kernel<DP, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return RA_ERR_CUDA;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t per_sm = 512 / tc_tmem_cols(DP);
+  int64_t grid = (int64_t)(sms > 0 ? sms : 1) * per_sm;
+  if (grid > max_items) grid = max_items;
+  tilestc_kernel<DP, MODE><<<(unsigned)grid, kTcThreads, smem, st>>>(T);
+  return cuda_status(cudaGetLastError());
+}
+
+template <int DP>
+int launch_tilestc_d(int mode, int64_t max_items, const TilesGArgs &T, cudaStream_t st) {
+  if (mode == 0) return launch_tilestc_dm<DP, 0>(max_items, T, st);
+  if (mode == 1) return launch_tilestc_dm<DP, 1>(max_items, T, st);
+  return launch_tilestc_dm<DP, 2>(max_items, T, st);
+}
+
+int launch_tilestc(int DP, int mode, int64_t max_items, const TilesGArgs &T, cudaStream_t st) {
+  int rc;
+  switch (DP) {
+    case 32: rc = launch_tilestc_d<32>(mode, max_items, T, st); break;
+    case 64: rc = launch_tilestc_d<64>(mode, max_items, T, st); break;
+    case 128: rc = launch_tilestc_d<128>(mode, max_items, T, st); break;
+    default: return RA_ERR_INVALID_ARGUMENT;
+  }
+  ++g_launches;
+  return rc;
+}
+
+bool use_tensor_cores(const ra_kde_desc *d, int DP) {
+  if (d->dim <= 3 || d->engine == RA_ENGINE_SIMT) return false;
+  return DP == 32 || DP == 64 || DP == 128;
+}
+
 int launch_tilesg(int DP, int mode, int64_t grid, const TilesGArgs &T, cudaStream_t st) {
   switch (DP) {
     case 4: launch_tilesg_dp<4>(mode, grid, T, st); break;
@@ -303,6 +351,14 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   segment_kernel<<<1, 1024, 0, st>>>(pa);
   if (L.packed3)
     stats3_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+  else if (L.DP == 32)
+    statsw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
+  else if (L.DP == 64)
+    statsw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
+  else if (L.DP == 128)
+    statsw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
+  else if (L.DP == 256)
+    statsw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
   else
     stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
   meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
@@ -406,7 +462,9 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.need_rows = grad ? 1 : 0;
     T.shard_index = sh_idx;
     T.shard_count = sh_cnt;
-    rc = launch_tilesg(L.DP, mode, L.max_items, T, st);
+    T.err = at<int>(ws, L.hdr + kHdrErr);
+    rc = use_tensor_cores(d, L.DP) ? launch_tilestc(L.DP, mode, L.max_items, T, st)
+                                   : launch_tilesg(L.DP, mode, L.max_items, T, st);
     if (rc) return rc;
   }
 
@@ -498,6 +556,25 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   if (L.packed3) {
     epi3_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
     epi3_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+  } else if (L.DP >= 32) {
+    switch (L.DP) {
+      case 32:
+        epigw_partial_kernel<32><<<cgrid, 256, 0, st>>>(ea);
+        epigw_write_kernel<32><<<cgrid, 256, 0, st>>>(ea);
+        break;
+      case 64:
+        epigw_partial_kernel<64><<<cgrid, 256, 0, st>>>(ea);
+        epigw_write_kernel<64><<<cgrid, 256, 0, st>>>(ea);
+        break;
+      case 128:
+        epigw_partial_kernel<128><<<cgrid, 256, 0, st>>>(ea);
+        epigw_write_kernel<128><<<cgrid, 256, 0, st>>>(ea);
+        break;
+      default:
+        epigw_partial_kernel<256><<<cgrid, 256, 0, st>>>(ea);
+        epigw_write_kernel<256><<<cgrid, 256, 0, st>>>(ea);
+        break;
+    }
   } else {
     epig_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
     epig_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
@@ -598,6 +675,8 @@ const char *ra_status_string(int status) {
     case RA_ERR_PTR_ORDER: return "ptr offsets must be non-decreasing";
     case RA_ERR_WEIGHT_SUM: return "weights must sum to a positive value per segment";
     case RA_ERR_STATE: return "backward needs a forward run with need_grad (and need_sigma_grad)";
+    case RA_ERR_DEVICE_TIMEOUT:
+      return "a bounded wait inside a kernel expired (tensor-core path); results are invalid";
     case RA_ERR_SCRATCH_LIMIT:
       return "problem too large for the 64 MiB fixed scratch of the no-alloc entry point";
     default: return "unknown status";
@@ -686,6 +765,7 @@ int ra_kde_check(const void *workspace, ra_stream_t stream) {
   if (err & kErrPtrEnd) return RA_ERR_PTR_END;
   if (err & kErrPtrOrder) return RA_ERR_PTR_ORDER;
   if (err & kErrWeightSum) return RA_ERR_WEIGHT_SUM;
+  if (err & kErrTimeout) return RA_ERR_DEVICE_TIMEOUT;
   return RA_OK;
 }
 

@@ -138,6 +138,7 @@ enum : int {
   kErrPtrEnd = 2,
   kErrPtrOrder = 4,
   kErrWeightSum = 8,
+  kErrTimeout = 16,  // a bounded device-side wait expired (tensor-core path)
 };
 
 // Per pair: where its points live and how many of them the kernels visit.

@@ -380,4 +380,134 @@ __global__ void __launch_bounds__(NT) epig_write_kernel(EpilogueArgs A) {
   });
 }
 
+// ---- generic D, wide points (DP >= 32): one warp per point ----------------
+// Lane l handles coordinates l, l + 32, ...; chunk partials are combined over
+// the 8 warps in order (deterministic), the dot products x . R by warp
+// shuffles -- no barrier per point.
+__device__ __forceinline__ double genw_gxt(const EpilogueArgs &A, const float *acc, double a,
+                                           double s_self, double s_cross, const float *gp,
+                                           int d, const EpiSide &E) {
+  const int cross = 1 + A.DP;
+  const double xp = gp[d];
+  const double Gs = xp * s_self - (double)acc[1 + d];
+  const double Gc = xp * s_cross - (double)acc[cross + 1 + d];
+  return -a * E.k_x * (E.cs * Gs + E.cc * Gc);
+}
+
+template <int DP>
+__global__ void __launch_bounds__(256) epigw_partial_kernel(EpilogueArgs A) {
+  constexpr int NW = 8, KL = DP / 32;
+  __shared__ double sh[NW][DP + 1];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int D = A.D, rs = stats_stride(DP);
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
+    const EpiSide E = epi_side(A, p, side);
+    const float *accb = side == 0 ? A.accX : A.accY;
+    const float *Gp = side == 0 ? A.Gx : A.Gy;
+    const float *Ap = side == 0 ? A.Ax : A.Ay;
+    const int64_t b = c * kChunk, e = b + kChunk < E.count ? b + kChunk : E.count;
+    double R[KL], Q = 0.0;
+#pragma unroll
+    for (int k = 0; k < KL; ++k) R[k] = 0.0;
+    for (int64_t i = b + wid; i < e; i += NW) {
+      const int64_t g = E.s + i;
+      const float *acc = accb + g * A.acc_stride;
+      const double a = Ap[g], s_self = acc[0], s_cross = acc[1 + DP];
+#pragma unroll
+      for (int k = 0; k < KL; ++k) {
+        const int d = lane + 32 * k;
+        if (d < D) R[k] += genw_gxt(A, acc, a, s_self, s_cross, Gp + g * DP, d, E);
+      }
+      // the stored self sums leave out the diagonal term (k_ii = 1, weight a_i)
+      Q += a * (E.cs * (s_self + a) + E.cc * s_cross);
+    }
+#pragma unroll
+    for (int k = 0; k < KL; ++k) sh[wid][lane + 32 * k] = R[k];
+    if (lane == 0) sh[wid][DP] = Q;
+    __syncthreads();
+    double *rec = A.rec + v * rs;
+    for (int t = tid; t < DP + 1; t += 256) {
+      double tot = 0.0;
+      for (int q = 0; q < NW; ++q) tot += sh[q][t];
+      if (t < DP) rec[1 + t] = tot;
+      else rec[0] = tot;
+    }
+    __syncthreads();
+  });
+}
+
+template <int DP>
+__global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
+  constexpr int NW = 8, KL = DP / 32;
+  __shared__ double Rsh[DP + 1];
+  __shared__ double red[NW];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int D = A.D, rs = stats_stride(DP);
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t first, int64_t n) {
+    const EpiSide E = epi_side(A, p, side);
+    // the side's totals, summed over its chunks in order
+    for (int t = tid; t < DP + 1; t += 256) {
+      double tot = 0.0;
+      for (int64_t kk = 0; kk < n; ++kk) tot += A.rec[(first + kk) * rs + (t < DP ? 1 + t : 0)];
+      Rsh[t] = tot;  // Rsh[DP] = Q
+    }
+    __syncthreads();
+    double mr = 0.0;
+    for (int t = tid; t < D; t += 256) mr += E.mu[t] * Rsh[t];
+    mr = warp_sum(mr);
+    if (lane == 0) red[wid] = mr;
+    __syncthreads();
+    double muR = 0.0;
+    for (int q = 0; q < NW; ++q) muR += red[q];
+    const double Qt = A.center ? Rsh[DP] - muR : Rsh[DP];
+
+    const float *pts = side == 0 ? A.x : A.y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    float *gout = side == 0 ? A.grad_x : A.grad_y;
+    double *wout = side == 0 ? A.grad_wx : A.grad_wy;
+    const float *accb = side == 0 ? A.accX : A.accY;
+    const float *Gp = side == 0 ? A.Gx : A.Gy;
+    const float *Ap = side == 0 ? A.Ax : A.Ay;
+    const int64_t b = c * kChunk, e = b + kChunk < E.span ? b + kChunk : E.span;
+    for (int64_t i = b + wid; i < e; i += NW) {
+      const int64_t g = E.s + i;
+      const bool live = i < E.count;
+      double a = 0.0, ga = 0.0, xr = 0.0;
+      if (live) {
+        const float *acc = accb + g * A.acc_stride;
+        const double s_self = acc[0], s_cross = acc[1 + DP];
+        a = Ap[g];
+        ga = E.cs * (s_self + a) + E.cc * s_cross;
+#pragma unroll
+        for (int k = 0; k < KL; ++k) {
+          const int d = lane + 32 * k;
+          if (d < D) {
+            double gx = genw_gxt(A, acc, a, s_self, s_cross, Gp + g * DP, d, E);
+            if (A.center) {
+              gx -= a * Rsh[d];
+              xr += (double)pts[g * D + d] * Rsh[d];
+            }
+            if (gout != nullptr) gout[g * D + d] = (float)gx;
+          }
+        }
+      } else if (gout != nullptr) {
+#pragma unroll
+        for (int k = 0; k < KL; ++k) {
+          const int d = lane + 32 * k;
+          if (d < D) gout[g * D + d] = 0.f;
+        }
+      }
+      xr = warp_sum(xr);
+      if (lane == 0 && wout != nullptr && wmode != 3) {
+        const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
+        wout[g] = live ? weight_grad(wmode, m, ga - xr, Qt, E) : 0.0;
+      }
+    }
+    __syncthreads();  // Rsh and red are rewritten by the next chunk
+  });
+}
+
 }  // namespace ra

@@ -269,6 +269,76 @@ __global__ void __launch_bounds__(NT) stats3_kernel(PrepArgs A) {
   });
 }
 
+// Pass 1 for wide points (DP >= 32): one warp per point, lane l holding
+// coordinates l, l + 32, ...; a chunk's partials are combined over the 8
+// warps in order through shared memory, one barrier pair per chunk.
+template <int DP>
+__global__ void __launch_bounds__(256) statsw_kernel(PrepArgs A) {
+  constexpr int NW = 8, KL = DP / 32;
+  __shared__ double sh[NW][2 * DP + 2];
+  __shared__ long long shl[NW];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int D = A.D;
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
+    const float *pts = side == 0 ? A.x : A.y;
+    const float *w = side == 0 ? A.w_x : A.w_y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    const Seg sg = A.seg[p];
+    const int64_t s = side == 0 ? sg.xs : sg.ys;
+    const int64_t span = side == 0 ? sg.xspan : sg.yspan;
+    const int64_t b = c * kChunk, e = b + kChunk < span ? b + kChunk : span;
+    double acc[KL], accu[KL], W = 0.0, nv = 0.0;
+    long long last = -1;
+#pragma unroll
+    for (int k = 0; k < KL; ++k) acc[k] = accu[k] = 0.0;
+    for (int64_t i = b + wid; i < e; i += NW) {
+      const int64_t g = s + i;
+      const float wi = eff_weight(w, mask, wmode, g);
+      const bool valid = mask == nullptr || mask[g] != 0;
+#pragma unroll
+      for (int k = 0; k < KL; ++k) {
+        const int d = lane + 32 * k;
+        if (d < D) {
+          const double pv = (double)pts[g * D + d];
+          acc[k] += (double)wi * pv;
+          if (valid) accu[k] += pv;
+        }
+      }
+      W += (double)wi;
+      if (valid) {
+        nv += 1.0;
+        last = i;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < KL; ++k) {
+      sh[wid][lane + 32 * k] = acc[k];
+      sh[wid][DP + lane + 32 * k] = accu[k];
+    }
+    if (lane == 0) {
+      sh[wid][2 * DP] = W;
+      sh[wid][2 * DP + 1] = nv;
+      shl[wid] = last;
+    }
+    __syncthreads();
+    double *rec = A.rec + v * stats_stride(DP);
+    for (int t = tid; t < 2 * DP + 2; t += 256) {
+      double tot = 0.0;
+      for (int q = 0; q < NW; ++q) tot += sh[q][t];
+      if (t < 2 * DP) rec[3 + t] = tot;  // sum w' p, then sum p (valid points)
+      else rec[t - 2 * DP] = tot;        // W, valid count
+    }
+    if (tid == 0) {
+      long long lst = -1;
+      for (int q = 0; q < NW; ++q) lst = shl[q] > lst ? shl[q] : lst;
+      rec[2] = (double)lst;
+    }
+    __syncthreads();
+  });
+}
+
 __device__ __forceinline__ double warp_max(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFull, v, o));

@@ -27,6 +27,7 @@ struct TilesGArgs {
   double *itemK, *itemS;
   int need_rows;         // 1: write the per-point sums (backward requested)
   int shard_index, shard_count;  // evaluate only items shard_index + k * shard_count
+  int *err;                      // error word (the tensor-core path's wait limits)
 };
 
 // One staged column tile against this thread's row: st += sum w, T += sum w y'

@@ -1,0 +1,188 @@
+"""Tensor-core (tcgen05, 3xTF32) path of the generic layout: padded dims 32,
+64 and 128 take it automatically.  Checked against the float64 oracle.
+
+Stated tolerances of this path: K within 2e-6 relative and gradients within
+1e-4 of max |g| (as on the SIMT path); losses within
+|L - L_ref| <= 1e-5 |L_ref| + 1e-6 (Kxx + Kyy).
+The absolute term is there because r^2 = |x'|^2 + |y'|^2 - 2 x'.y' (the GEMM
+form, which is also how the reference's own PyTorch path computes
+distances) carries ~1e-7 absolute error even with three TF32 products
+(hi*hi + hi*lo + lo*hi): the tensor core accumulates in float32.  K then
+agrees to ~2e-7 relative, and a loss that cancels K to 1e-2 shows that as
+~2e-5 relative.  On the embedding workload's data (well-separated clouds)
+the plain 1e-5 relative bar holds (last test)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from test_gpu_parity import _cuda, _np, _ragged, assert_grad, assert_k
+
+LOSS_REL = 1e-5
+LOSS_ABS_OF_K = 1e-6  # of (Kxx + Kyy); see the module docstring
+
+
+def assert_loss(got, ref, kxx, kyy, name=""):
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    bound = LOSS_REL * np.abs(ref) + LOSS_ABS_OF_K * (np.abs(kxx) + np.abs(kyy))
+    excess = np.abs(got - ref) / np.maximum(bound, 1e-300)
+    assert np.all(excess <= 1.0), (name, float(excess.max()))
+
+pytestmark = pytest.mark.gpu
+
+
+def _embed_batch(rng, sizes_x, sizes_y, d, noise=0.1):
+    x, y, ptr_x, ptr_y = _ragged(rng, sizes_x, sizes_y, d, noise=noise)
+    return (x / np.sqrt(d)).astype(np.float32), (y / np.sqrt(d)).astype(np.float32), ptr_x, ptr_y
+
+
+@pytest.mark.parametrize("d", [32, 64, 128])
+@pytest.mark.parametrize("center", [False, True])
+def test_tensor_core_ragged_matches_oracle(d, center, cuda_device):
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(40 + d + int(center))
+    # sizes around the 128-row and 64-column tiles, an empty side, a tiny pair
+    x, y, ptr_x, ptr_y = _embed_batch(rng, [300, 3, 0, 128, 65], [270, 1, 7, 129, 64], d)
+    wx = rng.uniform(0.2, 1.0, x.shape[0]).astype(np.float32)
+    wy = rng.uniform(0.2, 1.0, y.shape[0]).astype(np.float32)
+    dev = cuda_device
+    xt, yt = _cuda(x, dev, True), _cuda(y, dev, True)
+    wxt, wyt = _cuda(wx, dev, True), _cuda(wy, dev, True)
+    outs = ra.pyg_kde_mmd_loss(xt, yt, src_ptr=_cuda(ptr_x, dev), tgt_ptr=_cuda(ptr_y, dev),
+                               src_w=wxt, tgt_w=wyt, sigma=1.0, center=center)
+    up = [rng.uniform(0.5, 1.5, len(ptr_x) - 1) for _ in range(4)]
+    total = sum((torch.as_tensor(u, device=dev) * o.double()).sum() for u, o in zip(up, outs))
+    total.backward()
+    r = O.pyg_kde_mmd_loss(x, y, ptr_x, ptr_y, wx, wy, sigma=1.0, center=center, upstream=up)
+    assert_k(_np(outs[1]), r.Kxx, "Kxx")
+    assert_k(_np(outs[2]), r.Kyy, "Kyy")
+    assert_k(_np(outs[3]), r.Kxy, "Kxy")
+    assert_loss(_np(outs[0]), r.loss, r.Kxx, r.Kyy, "loss")
+    assert_grad(_np(xt.grad), r.grad_x, "grad_x")
+    assert_grad(_np(yt.grad), r.grad_y, "grad_y")
+    assert_grad(_np(wxt.grad), r.grad_wx, "grad_wx")
+    assert_grad(_np(wyt.grad), r.grad_wy, "grad_wy")
+
+
+def test_tensor_core_large_pair(cuda_device):
+    """One pair of 1500 x 1400 points, D=128: many row and column tiles."""
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(77)
+    x, y, ptr_x, ptr_y = _embed_batch(rng, [1500], [1400], 128)
+    dev = cuda_device
+    xt, yt = _cuda(x, dev, True), _cuda(y, dev, True)
+    loss, Kxx, Kyy, Kxy = ra.pyg_kde_mmd_loss(xt, yt, src_ptr=_cuda(ptr_x, dev),
+                                              tgt_ptr=_cuda(ptr_y, dev), sigma=1.0,
+                                              center=False)
+    loss.sum().backward()
+    r = O.pyg_kde_mmd_loss(x, y, ptr_x, ptr_y, sigma=1.0, center=False,
+                           upstream=[np.ones(1), np.zeros(1), np.zeros(1), np.zeros(1)])
+    assert_k(_np(Kxx), r.Kxx)
+    assert_k(_np(Kxy), r.Kxy)
+    assert_loss(_np(loss), r.loss, r.Kxx, r.Kyy)
+    assert_grad(_np(xt.grad), r.grad_x)
+    assert_grad(_np(yt.grad), r.grad_y)
+
+
+def test_tensor_core_dense_masked(cuda_device):
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(78)
+    B, N, M, D = 3, 200, 150, 64
+    x = (rng.standard_normal((B, N, D)) / 8).astype(np.float32)
+    y = (rng.standard_normal((B, M, D)) / 8).astype(np.float32)
+    mx = rng.random((B, N)) < 0.8
+    my = rng.random((B, M)) < 0.9
+    mx[1, 70:] = False
+    dev = cuda_device
+    xt, yt = _cuda(x, dev, True), _cuda(y, dev, True)
+    outs = ra.kde_mmd_loss_dense(xt, yt, _cuda(mx, dev), _cuda(my, dev), sigma=0.7, center=True)
+    up = [rng.uniform(0.5, 1.5, B) for _ in range(4)]
+    total = sum((torch.as_tensor(u, device=dev) * o.double()).sum() for u, o in zip(up, outs))
+    total.backward()
+    r = O.kde_mmd_loss_dense(x, y, mx, my, sigma=0.7, center=True, upstream=up)
+    assert_k(_np(outs[1]), r.Kxx)
+    assert_k(_np(outs[3]), r.Kxy)
+    assert_loss(_np(outs[0]), r.loss, r.Kxx, r.Kyy)
+    assert_grad(_np(xt.grad), r.grad_x, "grad_x")
+    assert_grad(_np(yt.grad), r.grad_y, "grad_y")
+
+
+def test_tensor_core_segmented_sigma_grad(cuda_device):
+    """segmented_kde_loss (raw weights, sigma gradient) on D=32."""
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(79)
+    x, y, ptr_x, ptr_y = _embed_batch(rng, [140, 60], [120, 80], 32)
+    wx = rng.uniform(0.2, 1.0, x.shape[0])
+    wy = rng.uniform(0.2, 1.0, y.shape[0])
+    dev = cuda_device
+    xt, yt = _cuda(x, dev, True), _cuda(y, dev, True)
+    wxt = torch.tensor(wx, device=dev, requires_grad=True)
+    wyt = torch.tensor(wy, device=dev, requires_grad=True)
+    sig = torch.tensor(0.8, dtype=torch.float64, device=dev, requires_grad=True)
+    losses = ra.segmented_kde_loss(xt, yt, wxt, wyt, _cuda(ptr_x, dev), _cuda(ptr_y, dev), sig)
+    gl = rng.uniform(0.5, 1.5, 2)
+    (losses * torch.as_tensor(gl, device=dev)).sum().backward()
+    loss_ref, (gx, gy, gwx, gwy, gsig) = O.segmented_kde_loss(x, y, wx, wy, ptr_x, ptr_y, 0.8,
+                                                              grad_loss=gl)
+    rs = O.raw_sums(x, y, wx, wy, ptr_x, ptr_y, 0.8)
+    assert_loss(_np(losses), loss_ref, rs.K[:, 0], rs.K[:, 1])
+    assert_grad(_np(xt.grad), gx, "grad_x")
+    assert_grad(_np(yt.grad), gy, "grad_y")
+    assert_grad(_np(wxt.grad), gwx, "grad_wx")
+    assert_grad(_np(wyt.grad), gwy, "grad_wy")
+    assert abs(float(sig.grad) - gsig) <= 1e-4 * abs(gsig)
+
+
+def test_tensor_core_agrees_with_simt_engine(cuda_device):
+    """The same forward through both kernel families (forced by the engine
+    field of the descriptor)."""
+    from rapidalign_b200 import _lib
+    from rapidalign_b200._core import Spec, forward_sums
+    rng = np.random.default_rng(80)
+    x, y, ptr_x, ptr_y = _embed_batch(rng, [300, 17, 200], [250, 40, 199], 128)
+    dev = cuda_device
+    xt, yt = _cuda(x, dev), _cuda(y, dev)
+    K = {}
+    for eng in (_lib.RA_ENGINE_SIMT, _lib.RA_ENGINE_TENSOR):
+        spec = Spec(layout=_lib.RA_LAYOUT_RAGGED, num_pairs=3, dim=128, num_x=x.shape[0],
+                    num_y=y.shape[0], center=False, sigma=1.0, ptr_x=_cuda(ptr_x, dev),
+                    ptr_y=_cuda(ptr_y, dev), check_errors=True, engine=eng)
+        K[eng], _ = forward_sums(xt, yt, None, None, None, spec, False)
+    a, b = _np(K[_lib.RA_ENGINE_SIMT]), _np(K[_lib.RA_ENGINE_TENSOR])
+    assert np.max(np.abs(a - b) / np.abs(a)) < 2e-6
+
+
+def test_tensor_engine_rejects_unsupported_dim(cuda_device):
+    from rapidalign_b200 import _lib
+    from rapidalign_b200._core import Spec, forward_sums
+    dev = cuda_device
+    x = torch.randn(10, 8, device=dev)
+    spec = Spec(layout=_lib.RA_LAYOUT_RAGGED, num_pairs=1, dim=8, num_x=10, num_y=10,
+                center=False, sigma=1.0, ptr_x=torch.tensor([0, 10], device=dev),
+                ptr_y=torch.tensor([0, 10], device=dev), engine=_lib.RA_ENGINE_TENSOR)
+    with pytest.raises(RuntimeError, match="invalid"):
+        forward_sums(x, x, None, None, None, spec, False)
+
+
+def test_tensor_core_embedding_workload_loss_is_relative(cuda_device):
+    """Graphs shaped like the embedding benchmark (x ~ N(0, 1/D), tgt = src +
+    0.1 N(0, 1), sigma 1): the loss is far from zero and agrees to 1e-5
+    relative with no floor."""
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(81)
+    sizes = [64, 200, 512, 97]
+    xs = [(rng.standard_normal((n, 128)) / np.sqrt(128)).astype(np.float32) for n in sizes]
+    ys = [(a + 0.1 * rng.standard_normal(a.shape)).astype(np.float32) for a in xs]
+    x, y = np.concatenate(xs), np.concatenate(ys)
+    ptr = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    dev = cuda_device
+    xt, yt = _cuda(x, dev, True), _cuda(y, dev, True)
+    loss, Kxx, Kyy, Kxy = ra.pyg_kde_mmd_loss(xt, yt, src_ptr=_cuda(ptr, dev),
+                                              tgt_ptr=_cuda(ptr, dev), sigma=1.0, center=False)
+    loss.sum().backward()
+    r = O.pyg_kde_mmd_loss(x, y, ptr, ptr, sigma=1.0, center=False,
+                           upstream=[np.ones(4), np.zeros(4), np.zeros(4), np.zeros(4)])
+    rel = np.abs(_np(loss) - r.loss) / np.abs(r.loss)
+    assert np.all(rel <= 1e-5), float(rel.max())
+    assert_grad(_np(xt.grad), r.grad_x, "grad_x")
+    assert_grad(_np(yt.grad), r.grad_y, "grad_y")
