@@ -132,8 +132,13 @@ __global__ void plan_emit_kernel(PlanArgs A) {
     Item it;
     it.pair = (int)p;
     it.block = b;
-    it.tile = (int)(loc / S[b]);
-    it.split = (int)(loc % S[b]);
+    // split-major, row tiles fastest: a split evaluation that deals items out
+    // round-robin (item % shard_count) then gives every shard an equal share
+    // of each split's row tiles -- in self blocks the late splits hold most of
+    // the work -- and consecutive tickets read the same column tiles
+    const int64_t nr = c[b] / S[b];  // row tiles of this block
+    it.tile = (int)(loc % nr);
+    it.split = (int)(loc / nr);
     A.items[base + l] = it;
   }
 }
