@@ -188,6 +188,40 @@ def case_segmented(name, ptr_x, ptr_y, d, sigma, seed):
          raw_gsigma_pairs=raw["sigma_per_pair"].numpy())
 
 
+def case_learned(name, kind, n, m, seed):
+    """learned_kernel.py modules (float64; the gate's float32 cast is undone by
+    a forward pre-hook so that the whole module runs in float64)."""
+    from rapidalign.learned_kernel import LearnedKernel, SingleSigmaKernel, StructuredKernel
+    torch.manual_seed(seed)
+    g = torch.Generator().manual_seed(seed + 1)
+    x = f32(torch.randn(n, 2, generator=g))
+    y = f32(1.1 * torch.randn(m, 2, generator=g) + 0.05)
+    x.requires_grad_(True)
+    y.requires_grad_(True)
+    extra = {}
+    if kind == "multi":
+        mod = LearnedKernel(sigmas=(0.15, 0.3, 0.6), coord_dim=2).double()
+        mod.gate.register_forward_pre_hook(lambda mdl, inp: (inp[0].double(),))
+        loss = mod(x, y)
+    elif kind == "single":
+        mod = SingleSigmaKernel(init_sigma=0.3, use_weight_net=True, coord_dim=2).double()
+        loss = mod(x, y)
+    else:
+        mod = StructuredKernel(init_sigma=0.3, feature_dim=5, descriptor_dim=4).double()
+        fb = f32(torch.randn(n, 5, generator=g))
+        ft = f32(torch.randn(m, 5, generator=g))
+        db = f32(torch.randn(4, generator=g))
+        dt = f32(torch.randn(4, generator=g))
+        loss = mod(dict(pos=x, feat=fb, desc=db), dict(pos=y, feat=ft, desc=dt))
+        extra = dict(feat_x=fb.numpy(), feat_y=ft.numpy(), desc_x=db.numpy(), desc_y=dt.numpy())
+    loss.backward()
+    params = {"p_" + k: v.detach().numpy() for k, v in mod.state_dict().items()}
+    grads = {"g_" + k: prm.grad.numpy() for k, prm in mod.named_parameters()
+             if prm.grad is not None}
+    save(name, loss=loss.detach().numpy(), x=x.detach().numpy(), y=y.detach().numpy(),
+         grad_x=x.grad.numpy(), grad_y=y.grad.numpy(), **extra, **params, **grads)
+
+
 def main():
     torch.set_default_dtype(torch.float64)
     # single pair: the CPU-runnable headline shape (128 x 3, sigma 0.2, centred) and variants
@@ -216,6 +250,10 @@ def main():
     case_segmented("segmented_ragged", [0, 10, 11, 40, 40, 57], [0, 8, 20, 41, 44, 60], 3, 0.25,
                    7)
     case_segmented("segmented_d2", [0, 2, 5], [0, 3, 4], 2, 0.25, 6)
+    # learned-kernel callers (learned_kernel.py:41-202)
+    case_learned("learned_multi", "multi", 60, 45, 30)
+    case_learned("learned_single", "single", 50, 64, 31)
+    case_learned("learned_structured", "structured", 40, 37, 32)
 
 
 if __name__ == "__main__":
