@@ -236,62 +236,74 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
     }
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 
+    // Column tiles are loaded into registers one tile ahead: thread t takes
+    // 4-point x 4-coordinate blocks (q = t % 16, coordinates 4c..4c+3 for
+    // c = t / 16 + 8 i), all loads of a tile in flight at once; the next
+    // tile's loads are issued right after GEMM 2 of this one is launched.
+    constexpr int KB = NCH / (kTcThreads / NQ);  // blocks per thread
+    const int q = tid & (NQ - 1), c0 = tid / NQ, rot = tid & 3;
+    float4 E[KB][4];
+    float bw[4];
+    auto load_tile = [&](int64_t jt) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t j = jt + 4 * q + u;
+        const bool cv = j < ccnt;
+        const float4 *src = reinterpret_cast<const float4 *>(Gc + (cbase + j) * DP);
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb)
+          E[kb][u] = cv ? src[c0 + kb * (kTcThreads / NQ)] : make_float4(0.f, 0.f, 0.f, 0.f);
+        bw[u] = (c0 == 0 && cv) ? Ac[cbase + j] : 0.f;
+      }
+    };
+    // Split into tf32 hi/lo and store both K-major layouts; the order of the
+    // four 16-byte stores is rotated by lane so that a quarter-warp touches
+    // at least four distinct bank groups.
+    auto store_tile = [&](int64_t jt) {
+      float part[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb) {
+        const int c = c0 + kb * (kTcThreads / NQ);
+        uint32_t hh[4][4], ll[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float e[4] = {E[kb][u].x, E[kb][u].y, E[kb][u].z, E[kb][u].w};
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            part[u] = fmaf(e[v], e[v], part[u]);
+            hh[u][v] = to_tf32(e[v]);
+            ll[u][v] = to_tf32(e[v] - __uint_as_float(hh[u][v]));
+          }
+        }
+#pragma unroll
+        for (int s4 = 0; s4 < 4; ++s4) {
+          const int u = (s4 + rot) & 3;  // point (row layout) / coordinate (transposed)
+          const int jo = c * (kTcCols * 16) + (4 * q + u) * 16;
+          *reinterpret_cast<uint4 *>(yhi + jo) = make_uint4(hh[u][0], hh[u][1], hh[u][2], hh[u][3]);
+          *reinterpret_cast<uint4 *>(ylo + jo) = make_uint4(ll[u][0], ll[u][1], ll[u][2], ll[u][3]);
+          const int d = 4 * c + u;
+          const int to = (d >> 3) * (NQ * 128) + q * 128 + (d & 7) * 16;
+          *reinterpret_cast<uint4 *>(yth + to) = make_uint4(hh[0][u], hh[1][u], hh[2][u], hh[3][u]);
+          *reinterpret_cast<uint4 *>(ytl + to) = make_uint4(ll[0][u], ll[1][u], ll[2][u], ll[3][u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) ysq[c0 * kTcCols + 4 * q + u] = part[u];
+      if (c0 == 0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) bcol[4 * q + u] = bw[u];
+      }
+      (void)jt;
+    };
+    if (ccnt > 0) load_tile(0);
+
     float s = 0.f, sig = 0.f;
     double s64 = 0.0, sg64 = 0.0;
     bool first = true;
 #pragma unroll 1
     for (int64_t j0 = 0; j0 < ccnt && ok; j0 += kTcCols) {
-      // ---- column tile -> Y (both layouts, hi/lo) in smem, weights, |y'|^2 ---
-      // Thread t takes 4-point x 4-coordinate blocks (q = t % 16, c = t / 16 +
-      // 8 i); the order of its four 16-byte stores is rotated by lane so that
-      // a quarter-warp touches at least four distinct bank groups.
-      {
-        const int q = tid & (NQ - 1), c0 = tid / NQ, rot = tid & 3;
-        float part[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-        for (int c = c0; c < NCH; c += kTcThreads / NQ) {
-          float e[4][4];  // e[point u][coordinate v]
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int64_t j = j0 + 4 * q + u;
-            const float4 v = j < ccnt ? reinterpret_cast<const float4 *>(Gc + (cbase + j) * DP)[c]
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-            e[u][0] = v.x;
-            e[u][1] = v.y;
-            e[u][2] = v.z;
-            e[u][3] = v.w;
-          }
-          uint32_t hh[4][4], ll[4][4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              part[u] = fmaf(e[u][v], e[u][v], part[u]);
-              hh[u][v] = to_tf32(e[u][v]);
-              ll[u][v] = to_tf32(e[u][v] - __uint_as_float(hh[u][v]));
-            }
-#pragma unroll
-          for (int s4 = 0; s4 < 4; ++s4) {
-            const int u = (s4 + rot) & 3;  // point (row layout) / coordinate (transposed)
-            const int jo = c * (kTcCols * 16) + (4 * q + u) * 16;
-            *reinterpret_cast<uint4 *>(yhi + jo) = make_uint4(hh[u][0], hh[u][1], hh[u][2], hh[u][3]);
-            *reinterpret_cast<uint4 *>(ylo + jo) = make_uint4(ll[u][0], ll[u][1], ll[u][2], ll[u][3]);
-            const int d = 4 * c + u;
-            const int to = (d >> 3) * (NQ * 128) + q * 128 + (d & 7) * 16;
-            *reinterpret_cast<uint4 *>(yth + to) = make_uint4(hh[0][u], hh[1][u], hh[2][u], hh[3][u]);
-            *reinterpret_cast<uint4 *>(ytl + to) = make_uint4(ll[0][u], ll[1][u], ll[2][u], ll[3][u]);
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) ysq[c0 * kTcCols + 4 * q + u] = part[u];
-        if (c0 == 0) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int64_t j = j0 + 4 * q + u;
-            bcol[4 * q + u] = j < ccnt ? Ac[cbase + j] : 0.f;
-          }
-        }
-      }
+      // ---- column tile (registers, loaded earlier) -> Y in smem, |y'|^2 ------
+      store_tile(j0);
       fence_async_smem();
       tc_fence_before();
       __syncthreads();
@@ -373,6 +385,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
           }
           tc_commit(mb);
         }
+        if (j0 + kTcCols < ccnt) load_tile(j0 + kTcCols);  // in flight during GEMM 2
         if (__syncthreads_or(!mbar_wait(mb, phase))) {
           ok = false;
           break;
@@ -385,6 +398,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
+        if (j0 + kTcCols < ccnt) load_tile(j0 + kTcCols);
       }
     }
     if (!ok) break;
