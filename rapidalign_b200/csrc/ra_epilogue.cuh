@@ -472,38 +472,66 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
     const float *Gp = side == 0 ? A.Gx : A.Gy;
     const float *Ap = side == 0 ? A.Ax : A.Ay;
     const int64_t b = c * kChunk, e = b + kChunk < E.span ? b + kChunk : E.span;
-    for (int64_t i = b + wid; i < e; i += NW) {
-      const int64_t g = E.s + i;
-      const bool live = i < E.count;
-      double a = 0.0, ga = 0.0, xr = 0.0;
-      if (live) {
-        const float *acc = accb + g * A.acc_stride;
-        const double s_self = acc[0], s_cross = acc[1 + DP];
-        a = Ap[g];
-        ga = E.cs * (s_self + a) + E.cc * s_cross;
+
+    // weight gradients: a warp per point, 4 points in flight, x . R by shuffles
+    if (wout != nullptr && wmode != 3) {
+      for (int64_t i0 = b + 4 * wid; i0 < e; i0 += 4 * NW) {
+        double xr[4] = {0.0, 0.0, 0.0, 0.0};
+        if (A.center) {
 #pragma unroll
-        for (int k = 0; k < KL; ++k) {
-          const int d = lane + 32 * k;
-          if (d < D) {
-            double gx = genw_gxt(A, acc, a, s_self, s_cross, Gp + g * DP, d, E);
-            if (A.center) {
-              gx -= a * Rsh[d];
-              xr += (double)pts[g * D + d] * Rsh[d];
+          for (int u = 0; u < 4; ++u) {
+            const int64_t i = i0 + u;
+            if (i < e && i < E.count) {
+              const int64_t g = E.s + i;
+#pragma unroll
+              for (int k = 0; k < KL; ++k) {
+                const int dd = lane + 32 * k;
+                if (dd < D) xr[u] += (double)pts[g * D + dd] * Rsh[dd];
+              }
             }
-            if (gout != nullptr) gout[g * D + d] = (float)gx;
           }
         }
-      } else if (gout != nullptr) {
 #pragma unroll
-        for (int k = 0; k < KL; ++k) {
-          const int d = lane + 32 * k;
-          if (d < D) gout[g * D + d] = 0.f;
+        for (int u = 0; u < 4; ++u) xr[u] = warp_sum(xr[u]);
+        if (lane < 4) {
+          const int64_t i = i0 + lane;
+          if (i < e) {
+            const int64_t g = E.s + i;
+            double gw = 0.0;
+            if (i < E.count) {
+              const float *acc = accb + g * A.acc_stride;
+              const double a = Ap[g], s_self = acc[0], s_cross = acc[1 + DP];
+              const double ga = E.cs * (s_self + a) + E.cc * s_cross;
+              const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
+              const double xrl = lane == 0 ? xr[0] : lane == 1 ? xr[1] : lane == 2 ? xr[2] : xr[3];
+              gw = weight_grad(wmode, m, ga - xrl, Qt, E);
+            }
+            wout[g] = gw;
+          }
         }
       }
-      xr = warp_sum(xr);
-      if (lane == 0 && wout != nullptr && wmode != 3) {
-        const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
-        wout[g] = live ? weight_grad(wmode, m, ga - xr, Qt, E) : 0.0;
+    }
+    // position gradients: the chunk's (point, coordinate) elements taken flat
+    if (gout != nullptr) {
+      const int64_t nel = (e - b) * D;
+      for (int64_t k0 = tid; k0 < nel; k0 += 4 * 256) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t k = k0 + u * 256;
+          if (k < nel) {
+            const int64_t i = b + k / D;
+            const int dd = (int)(k % D);
+            const int64_t g = E.s + i;
+            double gx = 0.0;
+            if (i < E.count) {
+              const float *acc = accb + g * A.acc_stride;
+              const double a = Ap[g];
+              gx = genw_gxt(A, acc, a, acc[0], acc[1 + DP], Gp + g * DP, dd, E);
+              if (A.center) gx -= a * Rsh[dd];
+            }
+            gout[g * D + dd] = (float)gx;
+          }
+        }
       }
     }
     __syncthreads();  // Rsh and red are rewritten by the next chunk
