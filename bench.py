@@ -438,6 +438,12 @@ class EmbedWorkload(RaggedWorkload):
         x, y = np.concatenate(xs), np.concatenate(ys)
         bx = np.repeat(np.arange(len(xs)), nx)
         self.full_local, self.unique_local = term_counts(nx, nx)
+        # tensor work of one launch of the tensor-core kernel: per graph 4 row-only
+        # orientations of ceil(n/128) row tiles x ceil(n/64) column tiles, each a
+        # 128 x 64 x 128 Gram GEMM and a 128 x 128 x 64 weighted-sum GEMM,
+        # three TF32 products apiece (hi*hi + hi*lo + lo*hi)
+        tiles = float(np.sum(4 * np.ceil(nx / 128.0) * np.ceil(nx / 64.0)))
+        self.tensor_flops_issued = tiles * 2 * 3 * (2.0 * 128 * 64 * 128)
         self.sigma, self.center, self.dim = 1.0, False, 128
         self.dev = dev
         self.d = {k: torch.from_numpy(v).to(dev) for k, v in
@@ -453,7 +459,39 @@ class EmbedWorkload(RaggedWorkload):
                             "sigma=1.0, uncentred, pyg_kde_mmd_loss fwd+bwd",
                 "graphs": 1024 * world}
 
-    def tiles_time(self, reps):
+    def roofline(self, t_tiles, peak_fp32):
+        """Tensor roofline: algorithmic flops = full terms x (Gram + weighted
+        sum) x 2 D, against the TF32 peak (half the measured dense bf16 rate)."""
+        peaks = read_measured_peaks()
+        measured = bool(peaks and peaks.get("bf16_tflops"))
+        bf16 = peaks["bf16_tflops"] if measured else 1590.0  # fallback: earlier pool measurement
+        tf32 = bf16 * 1e12 / 2.0
+        algo = self.full_local * 2 * 2.0 * self.dim
+        return {
+            "bound": "tensor",
+            "achieved": algo / t_tiles / 1e12,
+            "peak": tf32 / 1e12,
+            "unit": "TFLOP/s",
+            "frac": algo / t_tiles / tf32,
+            "peak_source": ("MEASURED_PEAKS.json bf16_tflops" if measured else
+                            "fallback 1.59 PFLOP/s bf16") + " / 2 (dense TF32 runs at half the "
+                           "bf16 rate)",
+            "kernel": "tilestc_kernel<128,1> (tcgen05 kind::tf32, 3xTF32)",
+            "kernel_ms": t_tiles * 1e3,
+            "flops_per_full_term": 4.0 * self.dim,
+            "issued_frac": self.tensor_flops_issued / t_tiles / tf32,
+            "issued_note": "tensor flops the kernel issues (three TF32 products, four row-only "
+                           "orientations, tile padding) over the same peak",
+            "traffic": None,
+        }
+
+
+def read_measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
         return None
 
 
@@ -557,7 +595,9 @@ def run_ours(args):
         value = full_all * K / t_dev
         e2e_value = full_all * K / t_e2e
         roofline = None
-        if t_tiles:
+        if t_tiles and hasattr(wl, "roofline"):
+            roofline = wl.roofline(t_tiles, peak_ops)
+        elif t_tiles:
             achieved_ops = wl.unique_local * FP32_OPS_PER_UNIQUE_TERM / t_tiles
             roofline = {
                 "bound": "fp32",
