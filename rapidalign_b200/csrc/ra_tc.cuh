@@ -47,9 +47,9 @@ __host__ __device__ constexpr int tc_tmem_cols(int DP) {
   return 3 * DP + 2 * kTcCols <= 256 ? 256 : 512;
 }
 __host__ __device__ constexpr size_t tc_smem_bytes(int DP) {
-  // Y_hi, Y_lo, Yt_hi, Yt_lo, column weights, 8 partial |y'|^2 per point,
-  // barrier and TMEM address
-  return (size_t)4 * kTcCols * DP * 4 + kTcCols * 4 * 9 + 16;
+  // Y_hi, Y_lo, Yt_hi, Yt_lo, column weights, 8 partial |y'|^2 per point and
+  // their totals, barrier and TMEM address
+  return (size_t)4 * kTcCols * DP * 4 + kTcCols * 4 * 10 + 16;
 }
 // Dynamic shared memory requested per CTA: enough that no more CTAs share an
 // SM than its 512 TMEM columns hold (a CTA that cannot allocate would wait
@@ -168,8 +168,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
   uint8_t *yth = tc_smem + 2 * kTcCols * DP * 4;
   uint8_t *ytl = tc_smem + 3 * kTcCols * DP * 4;
   float *bcol = reinterpret_cast<float *>(tc_smem + 4 * kTcCols * DP * 4);
-  float *ysq = bcol + kTcCols;  // [8][64] partial |y'|^2, summed in order
-  uint64_t *mbar = reinterpret_cast<uint64_t *>(ysq + 8 * kTcCols);
+  float *ysq = bcol + kTcCols;        // [8][64] partial |y'|^2
+  float *ytot = ysq + 8 * kTcCols;    // [64] their totals, summed in order
+  uint64_t *mbar = reinterpret_cast<uint64_t *>(ytot + kTcCols);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mbar + 1);
   __shared__ double red[kTcThreads / 32 * 2];
 
@@ -216,23 +217,36 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
 
     // ---- this row -> X_hi / X_lo in TMEM (lane = row), |x'|^2 ----------------
     float xsq = 0.f;
+    {
+      // chunks of 32 coordinates, the next one loading while this one is
+      // split and written to TMEM
+      const float4 *src = reinterpret_cast<const float4 *>(Gr + (rbase + row) * DP);
+      float4 cur[8], nxt[8];
+#pragma unroll
+      for (int q8 = 0; q8 < 8; ++q8) cur[q8] = rv ? src[q8] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-    for (int d0 = 0; d0 < DP; d0 += 32) {
-      uint32_t h[32], l[32];
-      const float4 *src = reinterpret_cast<const float4 *>(Gr + (rbase + row) * DP + d0);
+      for (int d0 = 0; d0 < DP; d0 += 32) {
+        if (d0 + 32 < DP) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 v = rv ? src[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          xsq = fmaf(e[u], e[u], xsq);
-          h[4 * q + u] = to_tf32(e[u]);
-          l[4 * q + u] = to_tf32(e[u] - __uint_as_float(h[4 * q + u]));
+          for (int q8 = 0; q8 < 8; ++q8)
+            nxt[q8] = rv ? src[(d0 + 32) / 4 + q8] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        uint32_t h[32], l[32];
+#pragma unroll
+        for (int q8 = 0; q8 < 8; ++q8) {
+          const float e[4] = {cur[q8].x, cur[q8].y, cur[q8].z, cur[q8].w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            xsq = fmaf(e[u], e[u], xsq);
+            h[4 * q8 + u] = to_tf32(e[u]);
+            l[4 * q8 + u] = to_tf32(e[u] - __uint_as_float(h[4 * q8 + u]));
+          }
+        }
+        tmem_st32(tlane + C_XH + d0, h);
+        tmem_st32(tlane + C_XL + d0, l);
+#pragma unroll
+        for (int q8 = 0; q8 < 8; ++q8) cur[q8] = nxt[q8];
       }
-      tmem_st32(tlane + C_XH + d0, h);
-      tmem_st32(tlane + C_XL + d0, l);
     }
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 
@@ -323,6 +337,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
         }
         tc_commit(mb);
       }
+      // |y'|^2 totals for the epilogue, while GEMM 1 runs (published by the
+      // barrier after its wait)
+      if (tid < kTcCols) {
+        float t = 0.f;
+#pragma unroll
+        for (int g = 0; g < kTcThreads / NQ; ++g) t += ysq[g * kTcCols + tid];
+        ytot[tid] = t;
+      }
       // the decision to stop is taken by the whole CTA at once
       if (__syncthreads_or(!mbar_wait(mb, phase))) {
         ok = false;
@@ -343,9 +365,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
 #pragma unroll
         for (int u = 0; u < 32; ++u) {
           const int j = c0 + u;
-          float yq = 0.f;
-#pragma unroll
-          for (int g = 0; g < kTcThreads / NQ; ++g) yq += ysq[g * kTcCols + j];
+          const float yq = ytot[j];
           const float r2 = fmaxf(xsq + yq - 2.f * S[u], 0.f);
           float w = bcol[j] * ex2(-r2);
           if (j == diag) w = 0.f;
