@@ -89,7 +89,7 @@ Layout make_layout(const ra_kde_desc *d) {
   const int64_t P = d->num_pairs, NX = d->num_x, NY = d->num_y;
   L.packed3 = d->dim <= 3;
   L.DP = L.packed3 ? 3 : generic_dp(d->dim);
-  L.acc_stride = L.packed3 ? kAcc3Stride : 2 + 2 * L.DP;
+  L.acc_stride = L.packed3 ? kAcc3Stride : gen_acc_stride(L.DP);
   // host bound on the number of items
   int64_t tx, ty;  // sum over pairs of row tiles
   const int64_t rows = L.packed3 ? kTile : kGenRows;

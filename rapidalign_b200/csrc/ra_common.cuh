@@ -159,6 +159,11 @@ constexpr int kTile = 64;          // rows per warp item and columns per tile
 constexpr int kSplitMax = 16;      // max column splits of one row tile
 constexpr int kSplitMinTiles = 64; // a split covers at least this many col tiles
 
+// Per-point record of the generic (D >= 4) layout, in floats: T_self[DP],
+// T_cross[DP], s_self, s_cross, 2 pad.  The T segments start 16-byte
+// aligned, so kernels write and read them as float4.
+__host__ __device__ constexpr int gen_acc_stride(int DP) { return 2 * DP + 4; }
+
 // Tile geometry of the generic-D kernel (one thread per row).
 constexpr int kGenRows = 128;
 constexpr int kGenCols = 32;

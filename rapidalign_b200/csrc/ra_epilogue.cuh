@@ -271,14 +271,13 @@ __device__ __forceinline__ double gen_gxt(const EpilogueArgs &A, int side, int64
   const int DP = A.DP;
   const float *acc = (side == 0 ? A.accX : A.accY) + g * A.acc_stride;
   a = (side == 0 ? A.Ax : A.Ay)[g];
-  const int cross = 1 + DP;
   // the stored self sums leave out the diagonal term (k_ii = 1, weight a_i)
-  const double s_self = acc[0], s_cross = acc[cross];
+  const double s_self = acc[2 * DP], s_cross = acc[2 * DP + 1];
   ga = E.cs * (s_self + a) + E.cc * s_cross;
   if (d >= A.D) return 0.0;
   const double xp = (side == 0 ? A.Gx : A.Gy)[g * DP + d];
-  const double Gs = xp * s_self - (double)acc[1 + d];
-  const double Gc = xp * s_cross - (double)acc[cross + 1 + d];
+  const double Gs = xp * s_self - (double)acc[d];
+  const double Gc = xp * s_cross - (double)acc[DP + d];
   return -a * E.k_x * (E.cs * Gs + E.cc * Gc);
 }
 
@@ -387,10 +386,10 @@ __global__ void __launch_bounds__(NT) epig_write_kernel(EpilogueArgs A) {
 __device__ __forceinline__ double genw_gxt(const EpilogueArgs &A, const float *acc, double a,
                                            double s_self, double s_cross, const float *gp,
                                            int d, const EpiSide &E) {
-  const int cross = 1 + A.DP;
+  const int DP = A.DP;
   const double xp = gp[d];
-  const double Gs = xp * s_self - (double)acc[1 + d];
-  const double Gc = xp * s_cross - (double)acc[cross + 1 + d];
+  const double Gs = xp * s_self - (double)acc[d];
+  const double Gc = xp * s_cross - (double)acc[DP + d];
   return -a * E.k_x * (E.cs * Gs + E.cc * Gc);
 }
 
@@ -413,7 +412,7 @@ __global__ void __launch_bounds__(256) epigw_partial_kernel(EpilogueArgs A) {
     for (int64_t i = b + wid; i < e; i += NW) {
       const int64_t g = E.s + i;
       const float *acc = accb + g * A.acc_stride;
-      const double a = Ap[g], s_self = acc[0], s_cross = acc[1 + DP];
+      const double a = Ap[g], s_self = acc[2 * DP], s_cross = acc[2 * DP + 1];
 #pragma unroll
       for (int k = 0; k < KL; ++k) {
         const int d = lane + 32 * k;
@@ -500,7 +499,7 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
             double gw = 0.0;
             if (i < E.count) {
               const float *acc = accb + g * A.acc_stride;
-              const double a = Ap[g], s_self = acc[0], s_cross = acc[1 + DP];
+              const double a = Ap[g], s_self = acc[2 * DP], s_cross = acc[2 * DP + 1];
               const double ga = E.cs * (s_self + a) + E.cc * s_cross;
               const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
               const double xrl = lane == 0 ? xr[0] : lane == 1 ? xr[1] : lane == 2 ? xr[2] : xr[3];
@@ -526,7 +525,7 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
             if (i < E.count) {
               const float *acc = accb + g * A.acc_stride;
               const double a = Ap[g];
-              gx = genw_gxt(A, acc, a, acc[0], acc[1 + DP], Gp + g * DP, dd, E);
+              gx = genw_gxt(A, acc, a, acc[2 * DP], acc[2 * DP + 1], Gp + g * DP, dd, E);
               if (A.center) gx -= a * Rsh[dd];
             }
             gout[g * D + dd] = (float)gx;

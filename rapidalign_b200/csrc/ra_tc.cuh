@@ -210,7 +210,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
     const float *Gc = cols_x ? A.Gx : A.Gy;
     const float *Ac = cols_x ? A.Ax : A.Ay;
     float *acc = rows_x ? A.accX : A.accY;
-    const int off = (o == 0 || o == 3) ? 1 + DP : 0;
+    const bool crossb = (o == 0 || o == 3);
+    const int toff = crossb ? DP : 0, soff = 2 * DP + (crossb ? 1 : 0);
     const int64_t row = (int64_t)item.tile * kTcRows + tid;
     const bool rv = row < rcnt;
     const float a = rv ? Ar[rbase + row] : 0.f;
@@ -425,7 +426,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
 
     // ---- item outputs ---------------------------------------------------------
     if (GRAD && A.need_rows) {
-      float *dst = acc + (rbase + row) * (2 + 2 * DP) + off;
+      float *dst = acc + (rbase + row) * gen_acc_stride(DP);
 #pragma unroll 1
       for (int d0 = 0; d0 < DP; d0 += 32) {
         float T[32];
@@ -437,10 +438,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
         }
         if (rv) {
 #pragma unroll
-          for (int u = 0; u < 32; ++u) dst[1 + d0 + u] = T[u];
+          for (int u = 0; u < 32; u += 4)
+            *reinterpret_cast<float4 *>(dst + toff + d0 + u) =
+                make_float4(T[u], T[u + 1], T[u + 2], T[u + 3]);
         }
       }
-      if (rv) dst[0] = s;
+      if (rv) dst[soff] = s;
     }
     (void)sig;
     // pair partials (x-y, x-x, y-y; y-x would count Kxy twice); a self block

@@ -77,7 +77,8 @@ __global__ void __launch_bounds__(kGenRows) tilesg_kernel(TilesGArgs A) {
   const float *Gc = cols_x ? A.Gx : A.Gy;
   const float *Ac = cols_x ? A.Ax : A.Ay;
   float *acc = rows_x ? A.accX : A.accY;
-  const int off = (o == 0 || o == 3) ? 1 + DP : 0;
+  const bool crossb = (o == 0 || o == 3);
+  const int toff = crossb ? DP : 0, soff = 2 * DP + (crossb ? 1 : 0);
   const bool self = (o == 1 || o == 2);
 
   const int tid = threadIdx.x;
@@ -122,10 +123,10 @@ __global__ void __launch_bounds__(kGenRows) tilesg_kernel(TilesGArgs A) {
   }
   (void)sg2;
   if (MODE >= 1 && A.need_rows && rv) {
-    float *dst = acc + (rbase + row) * (2 + 2 * DP) + off;
-    dst[0] = s;
+    float *dst = acc + (rbase + row) * gen_acc_stride(DP);
+    dst[soff] = s;
 #pragma unroll
-    for (int d = 0; d < DP; ++d) dst[1 + d] = T[d];
+    for (int d = 0; d < DP; ++d) dst[toff + d] = T[d];
   }
   // pair partials: K from x-y, x-x and y-y only (y-x would count Kxy twice);
   // a self block adds the diagonal a_i * a_i * k_ii = a_i^2 here
