@@ -364,7 +364,16 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
   g_launches += 3;
   if (!L.packed3) {
-    packg_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+    if (d->dim % 4 == 0 && L.DP == 32)
+      packgw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
+    else if (d->dim % 4 == 0 && L.DP == 64)
+      packgw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
+    else if (d->dim % 4 == 0 && L.DP == 128)
+      packgw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
+    else if (d->dim % 4 == 0 && L.DP == 256)
+      packgw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
+    else
+      packg_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
     ++g_launches;
   }
   if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;

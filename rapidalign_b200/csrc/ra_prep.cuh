@@ -465,6 +465,56 @@ __global__ void __launch_bounds__(NT) packg_kernel(PrepArgs A) {
   });
 }
 
+// Generic layout for wide points (DP >= 32, D a multiple of 4): float4
+// elements (point, coordinates 4c..4c+3) taken flat.  With 256 threads and
+// DP / 4 dividing 256, a thread always handles the same c, so its four
+// anchors are loaded once per pair side.
+template <int DP>
+__global__ void __launch_bounds__(256) packgw_kernel(PrepArgs A) {
+  constexpr int NC = DP / 4;  // float4 chunks per packed point
+  static_assert(256 % NC == 0, "a thread keeps one chunk");
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int D = A.D, c = threadIdx.x % NC;
+  for_each_chunk(M, [&](int64_t p, int side, int64_t ch, int64_t, int64_t, int64_t) {
+    const Seg sg = A.seg[p];
+    const int64_t s = side == 0 ? sg.xs : sg.ys;
+    const int64_t count = side == 0 ? sg.xcount : sg.ycount;
+    const float *pts = side == 0 ? A.x : A.y;
+    const float *w = side == 0 ? A.w_x : A.w_y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    float4 *Gp = reinterpret_cast<float4 *>(side == 0 ? A.Gx : A.Gy);
+    float *Ap = side == 0 ? A.Ax : A.Ay;
+    const double *meta = A.meta + p * meta_stride(DP);
+    const double Wn = meta[side];
+    const double *anc = meta + 4 + (2 + side) * DP;
+    const bool live = 4 * c < D;
+    // anchors kept in fp64: the same packed values as the scalar kernel
+    const double a0 = live ? anc[4 * c] : 0.0, a1 = live ? anc[4 * c + 1] : 0.0;
+    const double a2 = live ? anc[4 * c + 2] : 0.0, a3 = live ? anc[4 * c + 3] : 0.0;
+    const float sc = A.scale;
+    const int64_t b = ch * kChunk, e = b + kChunk < count ? b + kChunk : count;
+    const int64_t nel = (e - b) * NC;
+    for (int64_t k0 = threadIdx.x; k0 < nel; k0 += 4 * 256) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t k = k0 + u * 256;
+        if (k < nel) {
+          const int64_t g = s + b + k / NC;
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (live) {
+            const float4 x = *reinterpret_cast<const float4 *>(pts + g * D + 4 * c);
+            v = make_float4(sc * (float)((double)x.x - a0), sc * (float)((double)x.y - a1),
+                            sc * (float)((double)x.z - a2), sc * (float)((double)x.w - a3));
+          }
+          Gp[g * NC + c] = v;
+          if (c == 0) Ap[g] = (float)((double)eff_weight(w, mask, wmode, g) / Wn);
+        }
+      }
+    }
+  });
+}
+
 // ---------------------------------------------------------------------------
 // D <= 3 tile layout.  Each cloud is cut into 64-point tiles, zero-weight
 // padded; pair p's x tiles start at tile tbase_x[p] (exclusive scan of
