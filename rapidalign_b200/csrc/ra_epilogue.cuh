@@ -510,8 +510,46 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
         }
       }
     }
-    // position gradients: the chunk's (point, coordinate) elements taken flat
-    if (gout != nullptr) {
+    // position gradients over flat elements: float4 (point, 4 coordinates)
+    // when D is a multiple of 4 -- a thread then keeps one coordinate chunk
+    // and loads each point's scalars once per 4 coordinates -- else scalars
+    if (gout != nullptr && D % 4 == 0) {
+      constexpr int NC = DP / 4;
+      const int ncd = D / 4;  // chunks that hold coordinates
+      const int cc = tid % NC;
+      const int64_t nel = (e - b) * NC;
+      for (int64_t k0 = tid; k0 < nel; k0 += 4 * 256) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t k = k0 + u * 256;
+          if (k < nel && cc < ncd) {
+            const int64_t i = b + k / NC;
+            const int64_t g = E.s + i;
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < E.count) {
+              const float *acc = accb + g * A.acc_stride;
+              const double a = Ap[g], s_self = acc[2 * DP], s_cross = acc[2 * DP + 1];
+              const float4 ts = *reinterpret_cast<const float4 *>(acc + 4 * cc);
+              const float4 tc = *reinterpret_cast<const float4 *>(acc + DP + 4 * cc);
+              const float4 xp = *reinterpret_cast<const float4 *>(Gp + g * DP + 4 * cc);
+              const float tsv[4] = {ts.x, ts.y, ts.z, ts.w}, tcv[4] = {tc.x, tc.y, tc.z, tc.w};
+              const float xv[4] = {xp.x, xp.y, xp.z, xp.w};
+              float r[4];
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                const double Gs = xv[v] * s_self - (double)tsv[v];
+                const double Gc = xv[v] * s_cross - (double)tcv[v];
+                double gx = -a * E.k_x * (E.cs * Gs + E.cc * Gc);
+                if (A.center) gx -= a * Rsh[4 * cc + v];
+                r[v] = (float)gx;
+              }
+              o = make_float4(r[0], r[1], r[2], r[3]);
+            }
+            *reinterpret_cast<float4 *>(gout + g * D + 4 * cc) = o;
+          }
+        }
+      }
+    } else if (gout != nullptr) {
       const int64_t nel = (e - b) * D;
       for (int64_t k0 = tid; k0 < nel; k0 += 4 * 256) {
 #pragma unroll
