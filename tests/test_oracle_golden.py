@@ -17,7 +17,12 @@ def rel(a, b):
     return float(np.max(np.abs(a - b))) / scale if b.size else 0.0
 
 
-@pytest.mark.parametrize("name", golden_cases())
+# the loss fixtures (the learned-kernel module fixtures are checked in
+# test_learned_kernel.py)
+LOSS_CASES = [n for n in golden_cases() if not n.startswith("learned")]
+
+
+@pytest.mark.parametrize("name", LOSS_CASES)
 def test_oracle_matches_reference(name):
     z = load_golden(name)
     if name.startswith("segmented"):
