@@ -142,6 +142,8 @@ Layout make_layout(const ra_kde_desc *d) {
   if (L.packed3) {
     L.tiles_x = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_x);
     L.tiles_y = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_y);
+    L.Ax = take(sizeof(float) * kTile * (size_t)L.max_tiles_x);  // a~ per slot
+    L.Ay = take(sizeof(float) * kTile * (size_t)L.max_tiles_y);
     L.acc_x_bytes = sizeof(float) * kAcc3Stride * kTile * (size_t)L.max_tiles_x;
     L.acc_y_bytes = sizeof(float) * kAcc3Stride * kTile * (size_t)L.max_tiles_y;
   } else {
@@ -341,6 +343,7 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   pa.chx = at<int64_t>(ws, L.chx);
   pa.choff = at<int64_t>(ws, L.choff);
   pa.err = at<int>(ws, L.hdr + kHdrErr);
+  pa.allow_fold = mode == 2 ? 0 : 1;
   if (!L.packed3) {
     pa.Gx = at<float>(ws, L.Gx);
     pa.Gy = at<float>(ws, L.Gy);
@@ -423,6 +426,8 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     pk.max_tiles_y = L.max_tiles_y;
     pk.tiles_x = at<ulonglong2>(ws, L.tiles_x);
     pk.tiles_y = at<ulonglong2>(ws, L.tiles_y);
+    pk.aw_x = at<float>(ws, L.Ax);
+    pk.aw_y = at<float>(ws, L.Ay);
     pack3_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pk);
     ++g_launches;
     if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
@@ -447,6 +452,9 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.tbase_y = at<int64_t>(ws, L.tbase_y);
     T.tiles_x = at<ulonglong2>(ws, L.tiles_x);
     T.tiles_y = at<ulonglong2>(ws, L.tiles_y);
+    T.aw_x = at<float>(ws, L.Ax);
+    T.aw_y = at<float>(ws, L.Ay);
+    T.meta = at<double>(ws, L.meta);
     T.acc_x = grad ? at<float>(ws, L.accX) : nullptr;
     T.acc_y = grad ? at<float>(ws, L.accY) : nullptr;
     T.itemK = at<double>(ws, L.itemK);
@@ -547,6 +555,8 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
     ea.tbase_x = at<int64_t>(ws, L.tbase_x);
     ea.tbase_y = at<int64_t>(ws, L.tbase_y);
     ea.nq = L.nq;
+    ea.aw_x = at<float>(ws, L.Ax);
+    ea.aw_y = at<float>(ws, L.Ay);
   } else {
     ea.Gx = at<float>(ws, L.Gx);
     ea.Gy = at<float>(ws, L.Gy);

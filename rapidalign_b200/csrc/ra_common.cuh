@@ -127,6 +127,11 @@ __device__ __forceinline__ long long warp_max(long long v) {
   }
   return v;
 }
+__device__ __forceinline__ double warp_fmax(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
 
 // ---------------------------------------------------------------------------
 // Internal data structures (live in the caller's workspace).

@@ -92,6 +92,7 @@ struct EpilogueArgs {
   const float *x, *y;  // original coordinates
   const uint8_t *mask_x, *mask_y;
   const ulonglong2 *tiles_x, *tiles_y;  // packed3: tile layout (ra_prep.cuh)
+  const float *aw_x, *aw_y;             // packed3: a~ = a / m per slot
   const int64_t *tbase_x, *tbase_y;     // packed3: first tile of each pair
   int nq;                               // packed3: arrays per tile
   const float *Gx, *Gy, *Ax, *Ay;       // generic
@@ -105,29 +106,32 @@ struct EpilogueArgs {
 // Per-point backward quantities of the D <= 3 layout: `slot` = tile * 64 +
 // lane of the point in the tile layout.  Returns gxt[0..D) (dL/dx~) and ga
 // (dL/da, direct part).
+// The tile kernel's sums carry the factor 1 / m of the cloud the point was
+// paired with (m_own for the self block, m_par for the cross block), and the
+// packed weight is a / m_own: both are undone here.
 template <int MAXD>
 __device__ __forceinline__ void point_grads(const EpilogueArgs &A, int side, int64_t slot,
-                                            double cs, double cc, double k_x, double *gxt,
-                                            double &ga, double &a_out) {
+                                            double cs, double cc, double k_x, double m_own,
+                                            double m_par, double *gxt, double &ga,
+                                            double &a_out) {
   const int D = A.D;
   const float *acc = (side == 0 ? A.accX : A.accY) + slot * A.acc_stride;
-  const ulonglong2 *tiles = side == 0 ? A.tiles_x : A.tiles_y;
-  const int64_t t = slot / kTile, l = slot % kTile;
-  const double a = lo_of(tiles[(t * A.nq + 1) * kTile + l].y);
+  const double a = (double)(side == 0 ? A.aw_x : A.aw_y)[slot] * m_own;
   const int cross = kAcc3Block;
-  const double s_self = acc[0], s_cross = acc[cross];
+  const double ws = cs * m_own, wc = cc * m_par;
 #pragma unroll
   for (int d = 0; d < MAXD; ++d) {
     // difference form: G = sum w k (x' - y') accumulated directly
-    gxt[d] = d < D ? -a * k_x * (cs * acc[1 + d] + cc * acc[cross + 1 + d]) : 0.0;
+    gxt[d] = d < D ? -a * k_x * (ws * acc[1 + d] + wc * acc[cross + 1 + d]) : 0.0;
   }
-  ga = cs * s_self + cc * s_cross;
+  ga = ws * acc[0] + wc * acc[cross];
   a_out = a;
 }
 
 // Per (pair, side) constants of the epilogue.
 struct EpiSide {
   double cxx, cyy, cxy, cs, cc, k_x, W, Wraw;
+  double m_own, m_par;  // D <= 3: weight scales of this side and of the other
   const double *mu;
   int64_t s, span, count;
 };
@@ -147,6 +151,8 @@ __device__ __forceinline__ EpiSide epi_side(const EpilogueArgs &A, int64_t p, in
   const double *meta = A.meta + p * meta_stride(A.DP);
   E.W = meta[side];
   E.Wraw = meta[2 + side];
+  E.m_own = meta[meta_wscale(A.DP) + side];
+  E.m_par = meta[meta_wscale(A.DP) + 1 - side];
   E.mu = meta + 4 + side * A.DP;
   return E;
 }
@@ -184,7 +190,7 @@ __global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
     double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
     for (int64_t i = b + threadIdx.x; i < e; i += NT) {
       double gxt[3], ga, a;
-      point_grads<3>(A, side, slot0 + i, E.cs, E.cc, E.k_x, gxt, ga, a);
+      point_grads<3>(A, side, slot0 + i, E.cs, E.cc, E.k_x, E.m_own, E.m_par, gxt, ga, a);
 #pragma unroll
       for (int d = 0; d < 3; ++d) R[d] += gxt[d];  // gxt[d >= D] == 0
       Q += a * ga;
@@ -241,7 +247,7 @@ __global__ void __launch_bounds__(NT) epi3_write_kernel(EpilogueArgs A) {
       const int64_t g = E.s + i;
       double gxt[3] = {0.0, 0.0, 0.0}, ga = 0.0, a = 0.0;
       const bool live = i < E.count;
-      if (live) point_grads<3>(A, side, slot0 + i, E.cs, E.cc, E.k_x, gxt, ga, a);
+      if (live) point_grads<3>(A, side, slot0 + i, E.cs, E.cc, E.k_x, E.m_own, E.m_par, gxt, ga, a);
       if (gout != nullptr) {
 #pragma unroll
         for (int d = 0; d < 3; ++d) {

@@ -29,13 +29,21 @@ namespace ra {
 //   [4+DP, 4+2DP)    mu_y
 //   [4+2DP, 4+3DP)   anchor subtracted from x before packing
 //   [4+3DP, 4+4DP)   anchor subtracted from y before packing
-__host__ __device__ __forceinline__ int meta_stride(int DP) { return 4 + 4 * DP; }
+//   [4+4DP + side]   D <= 3 layout: the side's weight scale m (the largest
+//                    normalised weight when the side's weights are folded
+//                    into the exponent, else 1); packed weights are a / m
+//   [6+4DP + side]   D <= 3 layout: 1 when the side's weights are folded
+//                    (all >= 0, some > 0, no sigma gradient), else 0
+__host__ __device__ __forceinline__ int meta_stride(int DP) { return 8 + 4 * DP; }
+__host__ __device__ __forceinline__ int meta_wscale(int DP) { return 4 + 4 * DP; }
+__host__ __device__ __forceinline__ int meta_fold(int DP) { return 6 + 4 * DP; }
 
 // Partial-sum record of one chunk (fp64): [0] sum of effective weights,
 // [1] valid points, [2] last valid index (-1: none), [3, 3+DP) sum w' p,
-// [3+DP, 3+2DP) sum p over the valid points.  The backward epilogue reuses the
-// same slots for its (Q, R[DP]) partials.
-__host__ __device__ __forceinline__ int stats_stride(int DP) { return 3 + 2 * DP; }
+// [3+DP, 3+2DP) sum p over the valid points, [3+2DP] largest and [4+2DP]
+// smallest effective weight (D <= 3 layout only).  The backward epilogue
+// reuses the same slots for its (Q, R[DP]) partials.
+__host__ __device__ __forceinline__ int stats_stride(int DP) { return 5 + 2 * DP; }
 
 // Reduction width: power of two >= D (at least 4); thread (pl, d) of a CTA
 // handles dimension d of point lane pl.
@@ -61,6 +69,7 @@ struct PrepArgs {
   double *rec;    // [chunk_cap][stats_stride]
   int64_t *chcnt, *chx, *choff;  // [P], [P], [P + 1]
   int *err;
+  int allow_fold;  // D <= 3: weights may be folded into the exponent (no sigma gradient)
   // generic layout (D >= 4): coords [num * DP] (zero padded) and weights [num]
   float *Gx, *Gy, *Ax, *Ay;
 };
@@ -216,6 +225,7 @@ template <int NT>
 __global__ void __launch_bounds__(NT) stats3_kernel(PrepArgs A) {
   __shared__ double sh[(NT / 32) * 8];
   __shared__ long long shl[NT / 32];
+  __shared__ double shm[NT / 32][2];
   const ChunkMap M{A.P, A.choff, A.chx};
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int D = A.D;
@@ -231,11 +241,14 @@ __global__ void __launch_bounds__(NT) stats3_kernel(PrepArgs A) {
     // vals: W, valid count, sum w' p (3), sum p over valid points (3)
     double vals[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
     long long last = -1;
+    double wmax = -INFINITY, nwmin = -INFINITY;
     for (int64_t i = b + tid; i < e; i += NT) {
       const int64_t g = s + i;
       const float wi = eff_weight(w, mask, wmode, g);
       const bool valid = mask == nullptr || mask[g] != 0;
       vals[0] += (double)wi;
+      wmax = fmax(wmax, (double)wi);
+      nwmin = fmax(nwmin, -(double)wi);
 #pragma unroll
       for (int d = 0; d < 3; ++d) {
         if (d < D) {
@@ -250,12 +263,25 @@ __global__ void __launch_bounds__(NT) stats3_kernel(PrepArgs A) {
       }
     }
     last = warp_max(last);
-    if (lane == 0) shl[wid] = last;
-    block_sum_n<8>(vals, sh);  // its first barrier also publishes shl
+    wmax = warp_fmax(wmax);
+    nwmin = warp_fmax(nwmin);
+    if (lane == 0) {
+      shl[wid] = last;
+      shm[wid][0] = wmax;
+      shm[wid][1] = nwmin;
+    }
+    block_sum_n<8>(vals, sh);  // its first barrier also publishes shl and shm
     if (tid == 0) {
       double *rec = A.rec + v * stats_stride(3);
       long long lst = -1;
-      for (int k = 0; k < NT / 32; ++k) lst = shl[k] > lst ? shl[k] : lst;
+      double mx = -INFINITY, nmn = -INFINITY;
+      for (int k = 0; k < NT / 32; ++k) {
+        lst = shl[k] > lst ? shl[k] : lst;
+        mx = fmax(mx, shm[k][0]);
+        nmn = fmax(nmn, shm[k][1]);
+      }
+      rec[9] = mx;
+      rec[10] = -nmn;
       rec[0] = vals[0];
       rec[1] = vals[1];
       rec[2] = (double)lst;
@@ -265,7 +291,7 @@ __global__ void __launch_bounds__(NT) stats3_kernel(PrepArgs A) {
         rec[6 + d] = vals[5 + d];
       }
     }
-    // the next chunk's shl writes happen after block_sum_n's trailing barrier
+    // the next chunk's shl / shm writes happen after block_sum_n's trailing barrier
   });
 }
 
@@ -387,9 +413,27 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
       if (lane == 0 && count > 0 && !(W > 0.0) && !(W != W)) atomicOr(A.err, (int)kErrWeightSum);
       if (!(W > 0.0)) Wn = 1.0;  // keep the kernels finite; the error is reported
     }
+    // D <= 3: fold the weights into the exponent when they are all >= 0
+    // (k' = 2^(-(r^2 - log2(a / m))) = (a / m) k, m the largest weight)
+    double m = 1.0, fold = 0.0;
+    if (DP == 3) {
+      double wmax = -INFINITY, nwmin = -INFINITY;
+      for (int64_t c = lane; c < n; c += 32) {
+        wmax = fmax(wmax, r0[c * rs + 9]);
+        nwmin = fmax(nwmin, -r0[c * rs + 10]);
+      }
+      wmax = warp_fmax(wmax);
+      nwmin = warp_fmax(nwmin);
+      if (A.allow_fold && -nwmin >= 0.0 && wmax > 0.0 && Wn > 0.0 && wmax / Wn < INFINITY) {
+        m = wmax / Wn;
+        fold = 1.0;
+      }
+    }
     if (lane == 0) {
       meta[side] = Wn;
       meta[2 + side] = W;
+      meta[meta_wscale(DP) + side] = m;
+      meta[meta_fold(DP) + side] = fold;
       if (side == 0) A.seg[p].xcount = count;
       else A.seg[p].ycount = count;
     }
@@ -519,9 +563,13 @@ __global__ void __launch_bounds__(256) packgw_kernel(PrepArgs A) {
 // D <= 3 tile layout.  Each cloud is cut into 64-point tiles, zero-weight
 // padded; pair p's x tiles start at tile tbase_x[p] (exclusive scan of
 // ceil(count / 64)).  A tile stores two arrays of 64 duplicated pairs
-// (16 bytes per point each):  {x', x', y', y'}  and  {z', z', w, w}
+// (16 bytes per point each):  {x', x', y', y'}  and  {z', z', v, v}
 // so one column feeds packed f32x2 arithmetic against two rows, and a warp
 // reads any column of a tile at an immediate offset from the tile base.
+// With m the side's weight scale and a~ = a / m (also stored alone, per
+// slot, in aw_x / aw_y), v is -log2(a~) for a side whose weights are folded
+// into the exponent (64 for a zero weight, +inf for padding) and a~ itself
+// otherwise.
 // ---------------------------------------------------------------------------
 struct PackArgs {
   int64_t P;
@@ -536,6 +584,7 @@ struct PackArgs {
   const int64_t *tbase_x, *tbase_y;  // [P + 1]
   int64_t max_tiles_x, max_tiles_y;
   ulonglong2 *tiles_x, *tiles_y;     // [tiles][nq = 2][64]
+  float *aw_x, *aw_y;                // [tiles * 64] a~ per slot
 };
 
 template <int NT>
@@ -554,8 +603,10 @@ __global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
     const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
     const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
     ulonglong2 *tiles = side == 0 ? A.tiles_x : A.tiles_y;
+    float *aw = side == 0 ? A.aw_x : A.aw_y;
     const double *meta = A.meta + p * meta_stride(3);
-    const double Wn = meta[side];
+    const double Wm = meta[side] * meta[meta_wscale(3) + side];  // a~ = w' / Wm
+    const bool fold = meta[meta_fold(3) + side] != 0.0;
     const float ax = (float)meta[4 + (2 + side) * 3 + 0];
     const float ay = (float)meta[4 + (2 + side) * 3 + 1];
     const float az = (float)meta[4 + (2 + side) * 3 + 2];
@@ -566,17 +617,23 @@ __global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
     for (int64_t i = b + threadIdx.x; i < e; i += NT) {
       const int64_t t = t0 + i / kTile;
       if (t >= tmax) break;  // malformed ptr overflowing the bound (error already flagged)
-      float c0 = 0.f, c1 = 0.f, c2 = 0.f, a = 0.f;
+      float c0 = 0.f, c1 = 0.f, c2 = 0.f, a = 0.f, v = fold ? INFINITY : 0.f;
       if (i < count) {
         const int64_t g = s + i;
-        a = (float)((double)eff_weight(w, mask, wmode, g) / Wn);
+        const double at = (double)eff_weight(w, mask, wmode, g) / Wm;
+        a = (float)at;
+        // folded: a~ in [0, 1]; a zero weight becomes 2^-64, which leaves the
+        // other points' sums unchanged to 5e-20 and keeps the point's own
+        // row sums (its weight gradient) finite
+        v = fold ? (at >= 1.0 ? 0.f : at > 0x1p-64 ? (float)-log2(at) : 64.f) : a;
         c0 = scale * (pts[g * D + 0] - ax);
         if (D > 1) c1 = scale * (pts[g * D + 1] - ay);
         if (D > 2) c2 = scale * (pts[g * D + 2] - az);
       }
       ulonglong2 *tp = tiles + t * (int64_t)(nq * kTile) + (i % kTile);
       tp[0] = make_ulonglong2(pk2u(c0, c0), pk2u(c1, c1));
-      tp[kTile] = make_ulonglong2(pk2u(c2, c2), pk2u(a, a));
+      tp[kTile] = make_ulonglong2(pk2u(c2, c2), pk2u(v, v));
+      aw[t * (int64_t)kTile + (i % kTile)] = a;
     }
   });
 }

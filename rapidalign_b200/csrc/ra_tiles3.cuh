@@ -34,15 +34,27 @@
 // Arithmetic per unique term (fwd+bwd): 3 sub + 3 mul/fma (r^2) + 1 EX2 +
 // w = b k, s += w, G += w d (5) for the row + the same 5 for the column =
 // 16 FP32-pipe operations, issued mostly as packed f32x2 instructions in
-// which the two rows of a row pair share the column operand.
+// which the two rows of a row pair share the column operand.  When the
+// column cloud's weights are all >= 0 they are folded into the exponent:
+// the column slot holds -log2(b~_j) (b~ = b / max b), the r^2 chain starts
+// from it instead of a plain product, and EX2 returns w = b~_j k directly,
+// which drops the row-side multiply: 15 operations per unique term.  The
+// per-point sums then carry the factor 1 / max b of the partner cloud,
+// which the epilogue restores.
 // Row sums accumulate in fp32 over an item (at most 4096 columns) and are
 // folded once into the fp64 K and S partials, which are reduced in a fixed
 // order; only the per-point fp32 red.add at L2 depends on timing.
 #pragma once
 
 #include "ra_common.cuh"
+#include "ra_prep.cuh"
 
 namespace ra {
+
+template <bool V>
+struct BoolTag {
+  static constexpr bool value = V;
+};
 
 // 4 warps per CTA, 3 CTAs (12 warps) per SM at <= 168 registers.
 constexpr int kT3Threads = 128;
@@ -60,6 +72,8 @@ struct Tiles3Args {
   const Seg *seg;
   const int64_t *tbase_x, *tbase_y;     // first tile of each pair's cloud
   const ulonglong2 *tiles_x, *tiles_y;  // [tiles][2][64]
+  const float *aw_x, *aw_y;             // [tiles * 64] a~ = a / m per slot
+  const double *meta;                   // per-pair metadata (ra_prep.cuh)
   float *acc_x, *acc_y;                 // [tiles * 64][8]: self (s, G0..G2), cross (s, G0..G2)
   double *itemK, *itemS;
   int shard_index, shard_count;  // this process evaluates items shard_index + k * shard_count
@@ -74,7 +88,8 @@ struct Tiles3Mode {
 
 // One column half (32 columns: 8 per ring position) against the lane's 4 row
 // pairs: updates the row sums and this half's travelling column sums.
-template <int MODE, bool COLS>
+// FOLD: the column's fourth value is -log2(b~) (see the file comment).
+template <int MODE, bool COLS, bool FOLD>
 __device__ __forceinline__ void t3_half(const ulonglong2 q0, const ulonglong2 q1,
                                         const f2_t (&X0)[4], const f2_t (&X1)[4],
                                         const f2_t (&X2)[4], const f2_t (&Aw)[4], f2_t (&st)[4],
@@ -88,21 +103,21 @@ __device__ __forceinline__ void t3_half(const ulonglong2 q0, const ulonglong2 q1
     const f2_t dx = sub2(X0[rp], Y0);
     const f2_t dy = sub2(X1[rp], Y1);
     const f2_t dz = sub2(X2[rp], Y2);
-    f2_t r2 = mul2(dx, dx);
+    f2_t r2 = FOLD ? fma2(dx, dx, B) : mul2(dx, dx);
     r2 = fma2(dy, dy, r2);
     r2 = fma2(dz, dz, r2);
     float r_lo, r_hi;
     upk(r2, r_lo, r_hi);
-    const f2_t k = pk(ex2(-r_lo), ex2(-r_hi));
+    const f2_t k = pk(ex2(-r_lo), ex2(-r_hi));  // FOLD: b~_j k_ij
     if (GRAD) {
-      const f2_t w = mul2(B, k);  // b_j k_ij for the two rows
+      const f2_t w = FOLD ? k : mul2(B, k);  // b_j k_ij for the two rows
       st[rp] = add2(st[rp], w);
       G0[rp] = fma2(w, dx, G0[rp]);
       G1[rp] = fma2(w, dy, G1[rp]);
       G2[rp] = fma2(w, dz, G2[rp]);
-      if (SIG) sgt[rp] = fma2(w, r2, sgt[rp]);
+      if (SIG) sgt[rp] = fma2(w, r2, sgt[rp]);  // never folded: r2 is r^2
     } else {
-      st[rp] = fma2(B, k, st[rp]);
+      st[rp] = FOLD ? add2(st[rp], k) : fma2(B, k, st[rp]);
     }
     if (COLS) {
       const f2_t wc = mul2(Aw[rp], k);  // a_i k_ij for the two rows
@@ -127,7 +142,7 @@ __device__ __forceinline__ void t3_rotate(f2_t &cs, f2_t &c0, f2_t &c1, f2_t &c2
 // done, so the shuffles of one half overlap the arithmetic of the other and
 // the steps interleave (6 % faster than a rolled loop that rotates both
 // halves at the end of a step).
-template <int MODE, bool DIAG>
+template <int MODE, bool DIAG, bool FOLD>
 __device__ __forceinline__ void tiles3_coltile(
     const ulonglong2 *__restrict__ ct, const int col0, const int ccnt,
     float *__restrict__ accC, const int lane, const f2_t (&X0)[4], const f2_t (&X1)[4],
@@ -148,10 +163,10 @@ __device__ __forceinline__ void tiles3_coltile(
     for (int t = 0; t < 8; ++t) {
       const ulonglong2 *cp = cb + ((p + t) & 7);
       const ulonglong2 a00 = cp[0], a01 = cp[kTile], a10 = cp[32], a11 = cp[32 + kTile];
-      t3_half<MODE, false>(a00, a01, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[0], c0[0], c1[0],
-                           c2[0]);
-      t3_half<MODE, false>(a10, a11, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[1], c0[1], c1[1],
-                           c2[1]);
+      t3_half<MODE, false, FOLD>(a00, a01, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[0], c0[0],
+                                 c1[0], c2[0]);
+      t3_half<MODE, false, FOLD>(a10, a11, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[1], c0[1],
+                                 c1[1], c2[1]);
     }
     return;
   }
@@ -159,23 +174,33 @@ __device__ __forceinline__ void tiles3_coltile(
   for (int t = 0; t < 8; ++t) {
     const ulonglong2 *cp = cb + ((p + t) & 7);
     const ulonglong2 a00 = cp[0], a01 = cp[kTile], a10 = cp[32], a11 = cp[32 + kTile];
-    t3_half<MODE, COLS>(a00, a01, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[0], c0[0], c1[0],
-                        c2[0]);
+    t3_half<MODE, COLS, FOLD>(a00, a01, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[0], c0[0], c1[0],
+                              c2[0]);
     if (t < 7) t3_rotate(cs[0], c0[0], c1[0], c2[0], src);
-    t3_half<MODE, COLS>(a10, a11, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[1], c0[1], c1[1],
-                        c2[1]);
+    t3_half<MODE, COLS, FOLD>(a10, a11, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[1], c0[1], c1[1],
+                              c2[1]);
     if (t < 7) t3_rotate(cs[1], c0[1], c1[1], c2[1], src);
   }
   {
     // after step 7 this lane holds the sums of position (p + 7) & 7; the
-    // columns' own differences are y'_j - x'_i, hence the sign
+    // columns' own differences are y'_j - x'_i, hence the sign.  Folded
+    // columns carry b~_j in every term: divide it out (2^(-log2 b~_j)).
     const int pos = (p + 7) & 7;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       const int in_tile = c * 32 + q * 8 + pos;
-      const float vs = lo_of(cs[c]) + hi_of(cs[c]), v0 = lo_of(c0[c]) + hi_of(c0[c]);
-      const float v1 = lo_of(c1[c]) + hi_of(c1[c]), v2 = lo_of(c2[c]) + hi_of(c2[c]);
-      if (col0 + in_tile < ccnt) red_add_v4(accC + in_tile * kAcc3Stride, vs, -v0, -v1, -v2);
+      float vs = lo_of(cs[c]) + hi_of(cs[c]), v0 = lo_of(c0[c]) + hi_of(c0[c]);
+      float v1 = lo_of(c1[c]) + hi_of(c1[c]), v2 = lo_of(c2[c]) + hi_of(c2[c]);
+      if (col0 + in_tile < ccnt) {
+        if (FOLD) {
+          const float inv = ex2(lo_of(ct[kTile + in_tile].y));
+          vs *= inv;
+          v0 *= inv;
+          v1 *= inv;
+          v2 *= inv;
+        }
+        red_add_v4(accC + in_tile * kAcc3Stride, vs, -v0, -v1, -v2);
+      }
     }
   }
 }
@@ -207,6 +232,12 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     float *accR = rows_y ? A.acc_y : A.acc_x;
     float *accC = cols_x ? A.acc_x : A.acc_y;
     const int off = blk == 0 ? kAcc3Block : 0;  // cross block after the self block
+    const float *__restrict__ awr = rows_y ? A.aw_y : A.aw_x;
+    const double *meta = A.meta + item.pair * (int64_t)meta_stride(3);
+    const int rside = rows_y ? 1 : 0, cside = cols_x ? 0 : 1;
+    // the column weights are folded into the exponent when all >= 0 (never
+    // with the sigma gradient, whose r^2 the fold would shift)
+    const bool fold = !SIG && meta[meta_fold(3) + cside] != 0.0;
 
     // 32-bit tile/column indices: a pair's cloud has < 2^31 points
     const int nTc = (int)ceil_div(ccnt, (int64_t)kTile);
@@ -231,14 +262,17 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     f2_t X0[4], X1[4], X2[4], Aw[4];
     {
       const ulonglong2 *rp0 = rt + (rtb + I) * kT3TileU2 + p * 8;
+      const float4 *ap = reinterpret_cast<const float4 *>(awr + (rtb + I) * kTile + p * 8);
+      const float4 aw0 = ap[0], aw1 = ap[1];
+      const float awv[8] = {aw0.x, aw0.y, aw0.z, aw0.w, aw1.x, aw1.y, aw1.z, aw1.w};
 #pragma unroll
       for (int rp = 0; rp < 4; ++rp) {
         const ulonglong2 a0 = rp0[2 * rp], b0 = rp0[2 * rp + 1];                  // x', y'
-        const ulonglong2 a1 = rp0[kTile + 2 * rp], b1 = rp0[kTile + 2 * rp + 1];  // z', w
+        const ulonglong2 a1 = rp0[kTile + 2 * rp], b1 = rp0[kTile + 2 * rp + 1];  // z', v
         X0[rp] = pk(lo_of(a0.x), lo_of(b0.x));
         X1[rp] = pk(lo_of(a0.y), lo_of(b0.y));
         X2[rp] = pk(lo_of(a1.x), lo_of(b1.x));
-        Aw[rp] = pk(lo_of(a1.y), lo_of(b1.y));
+        Aw[rp] = pk(awv[2 * rp], awv[2 * rp + 1]);
       }
     }
     f2_t st[4], G0[4], G1[4], G2[4], sgt[4];
@@ -249,9 +283,14 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
 
     // ---- the diagonal tile of a self block first (rows only, counted once) --
     if (sym && J0 == I) {
-      tiles3_coltile<MODE, true>(ct0 + I * kT3TileU2, I * kTile, cc,
-                                 accC0 + I * (kTile * kAcc3Stride), lane, X0, X1, X2, Aw, st,
-                                 G0, G1, G2, sgt);
+      if (fold)
+        tiles3_coltile<MODE, true, !SIG>(ct0 + I * kT3TileU2, I * kTile, cc,
+                                         accC0 + I * (kTile * kAcc3Stride), lane, X0, X1, X2, Aw,
+                                         st, G0, G1, G2, sgt);
+      else
+        tiles3_coltile<MODE, true, false>(ct0 + I * kT3TileU2, I * kTile, cc,
+                                          accC0 + I * (kTile * kAcc3Stride), lane, X0, X1, X2,
+                                          Aw, st, G0, G1, G2, sgt);
 #pragma unroll
       for (int rp = 0; rp < 4; ++rp) {
         float s_lo, s_hi, a_lo, a_hi;
@@ -268,17 +307,32 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
       ++J0;
     }
     // ---- off-diagonal tiles: rows and columns ------------------------------
+    auto offdiag = [&](auto fold_tag) {
+      constexpr bool F = decltype(fold_tag)::value;
 #pragma unroll 1
-    for (int J = J0; J < J1; ++J) {
-      const ulonglong2 *ct = ct0 + J * kT3TileU2;
-      if (J + 1 < J1) {
-        // 2 KB tile = 16 lines of 128 bytes: lanes 0..15 prefetch one each
-        const char *nxt = reinterpret_cast<const char *>(ct + kT3TileU2);
-        if (lane < kT3TileU2 / 8) asm volatile("prefetch.global.L1 [%0];" ::"l"(nxt + lane * 128));
+      for (int J = J0; J < J1; ++J) {
+        const ulonglong2 *ct = ct0 + J * kT3TileU2;
+        if (J + 1 < J1) {
+          // 2 KB tile = 16 lines of 128 bytes: lanes 0..15 prefetch one each
+          const char *nxt = reinterpret_cast<const char *>(ct + kT3TileU2);
+          if (lane < kT3TileU2 / 8)
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(nxt + lane * 128));
+        }
+        // row sums: a fresh fp32 subtotal per tile, added to the item's
+        // total (64-term then tile-count-long fp32 sums instead of one long one)
+        f2_t stt[4];
+#pragma unroll
+        for (int rp = 0; rp < 4; ++rp) stt[rp] = z2;
+        tiles3_coltile<MODE, false, F>(ct, J * kTile, cc, accC0 + J * (kTile * kAcc3Stride),
+                                       lane, X0, X1, X2, Aw, stt, G0, G1, G2, sgt);
+#pragma unroll
+        for (int rp = 0; rp < 4; ++rp) st[rp] = add2(st[rp], stt[rp]);
       }
-      tiles3_coltile<MODE, false>(ct, J * kTile, cc, accC0 + J * (kTile * kAcc3Stride), lane,
-                                  X0, X1, X2, Aw, st, G0, G1, G2, sgt);
-    }
+    };
+    if (fold)
+      offdiag(BoolTag<!SIG>{});
+    else
+      offdiag(BoolTag<false>{});
     // row sums accumulated in fp32 over the item: fold once into fp64
 #pragma unroll
     for (int rp = 0; rp < 4; ++rp) {
@@ -300,8 +354,10 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     double sw = 0.0;
     if (SIG) sw = warp_sum(sym ? 2.0 * stot_sig - sd : stot_sig);
     if (lane == 0) {
-      A.itemK[it] = kw;
-      A.itemS[it] = sw;
+      // K = m_r m_c sum a~_i s~_i
+      const double kscale = meta[meta_wscale(3) + rside] * meta[meta_wscale(3) + cside];
+      A.itemK[it] = kw * kscale;
+      A.itemS[it] = sw * kscale;
     }
 
     // ---- per-point row sums: combine the 4 rings, then one lane per row ----
