@@ -33,7 +33,8 @@ namespace ra {
 //                    normalised weight when the side's weights are folded
 //                    into the exponent, else 1); packed weights are a / m
 //   [6+4DP + side]   D <= 3 layout: 1 when the side's weights are folded
-//                    (all >= 0, some > 0, no sigma gradient), else 0
+//                    (all >= 0, some > 0, no sigma gradient), 2 when they are
+//                    moreover all equal (a~ = 1 on every point), else 0
 __host__ __device__ __forceinline__ int meta_stride(int DP) { return 8 + 4 * DP; }
 __host__ __device__ __forceinline__ int meta_wscale(int DP) { return 4 + 4 * DP; }
 __host__ __device__ __forceinline__ int meta_fold(int DP) { return 6 + 4 * DP; }
@@ -426,7 +427,7 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
       nwmin = warp_fmax(nwmin);
       if (A.allow_fold && -nwmin >= 0.0 && wmax > 0.0 && Wn > 0.0 && wmax / Wn < INFINITY) {
         m = wmax / Wn;
-        fold = 1.0;
+        fold = -nwmin == wmax ? 2.0 : 1.0;
       }
     }
     if (lane == 0) {
@@ -569,7 +570,9 @@ __global__ void __launch_bounds__(256) packgw_kernel(PrepArgs A) {
 // With m the side's weight scale and a~ = a / m (also stored alone, per
 // slot, in aw_x / aw_y), v is -log2(a~) for a side whose weights are folded
 // into the exponent (64 for a zero weight, +inf for padding) and a~ itself
-// otherwise.
+// otherwise.  On a side with equal weights (a~ = 1) the padding slots sit at
+// coordinate 1e18, so that as rows they give k = 0 without the weight
+// (valid while the scaled coordinates |x'| stay far below that).
 // ---------------------------------------------------------------------------
 struct PackArgs {
   int64_t P;
@@ -607,6 +610,8 @@ __global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
     const double *meta = A.meta + p * meta_stride(3);
     const double Wm = meta[side] * meta[meta_wscale(3) + side];  // a~ = w' / Wm
     const bool fold = meta[meta_fold(3) + side] != 0.0;
+    const bool uni = meta[meta_fold(3) + side] == 2.0;
+    const float pad = uni ? 1e18f : 0.f;
     const float ax = (float)meta[4 + (2 + side) * 3 + 0];
     const float ay = (float)meta[4 + (2 + side) * 3 + 1];
     const float az = (float)meta[4 + (2 + side) * 3 + 2];
@@ -617,11 +622,12 @@ __global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
     for (int64_t i = b + threadIdx.x; i < e; i += NT) {
       const int64_t t = t0 + i / kTile;
       if (t >= tmax) break;  // malformed ptr overflowing the bound (error already flagged)
-      float c0 = 0.f, c1 = 0.f, c2 = 0.f, a = 0.f, v = fold ? INFINITY : 0.f;
+      float c0 = pad, c1 = pad, c2 = pad, a = 0.f, v = fold ? INFINITY : 0.f;
       if (i < count) {
         const int64_t g = s + i;
-        const double at = (double)eff_weight(w, mask, wmode, g) / Wm;
+        const double at = uni ? 1.0 : (double)eff_weight(w, mask, wmode, g) / Wm;
         a = (float)at;
+        c1 = c2 = 0.f;
         // folded: a~ in [0, 1]; a zero weight becomes 2^-64, which leaves the
         // other points' sums unchanged to 5e-20 and keeps the point's own
         // row sums (its weight gradient) finite

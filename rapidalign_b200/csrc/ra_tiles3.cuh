@@ -40,7 +40,9 @@
 // from it instead of a plain product, and EX2 returns w = b~_j k directly,
 // which drops the row-side multiply: 15 operations per unique term.  The
 // per-point sums then carry the factor 1 / max b of the partner cloud,
-// which the epilogue restores.
+// which the epilogue restores.  When the row cloud's weights are moreover all
+// equal (a~ = 1, padding rows far away so that their k is 0) the column-side
+// multiply by a~_i goes too: 14 operations per unique term.
 // Row sums accumulate in fp32 over an item (at most 4096 columns) and are
 // folded once into the fp64 K and S partials, which are reduced in a fixed
 // order; only the per-point fp32 red.add at L2 depends on timing.
@@ -89,7 +91,8 @@ struct Tiles3Mode {
 // One column half (32 columns: 8 per ring position) against the lane's 4 row
 // pairs: updates the row sums and this half's travelling column sums.
 // FOLD: the column's fourth value is -log2(b~) (see the file comment).
-template <int MODE, bool COLS, bool FOLD>
+// RUNI: every row has a~ = 1 (or is padding with k = 0).
+template <int MODE, bool COLS, bool FOLD, bool RUNI = false>
 __device__ __forceinline__ void t3_half(const ulonglong2 q0, const ulonglong2 q1,
                                         const f2_t (&X0)[4], const f2_t (&X1)[4],
                                         const f2_t (&X2)[4], const f2_t (&Aw)[4], f2_t (&st)[4],
@@ -120,7 +123,7 @@ __device__ __forceinline__ void t3_half(const ulonglong2 q0, const ulonglong2 q1
       st[rp] = FOLD ? add2(st[rp], k) : fma2(B, k, st[rp]);
     }
     if (COLS) {
-      const f2_t wc = mul2(Aw[rp], k);  // a_i k_ij for the two rows
+      const f2_t wc = RUNI ? k : mul2(Aw[rp], k);  // a_i k_ij for the two rows
       cs = add2(cs, wc);
       c0 = fma2(wc, dx, c0);
       c1 = fma2(wc, dy, c1);
@@ -142,7 +145,7 @@ __device__ __forceinline__ void t3_rotate(f2_t &cs, f2_t &c0, f2_t &c1, f2_t &c2
 // done, so the shuffles of one half overlap the arithmetic of the other and
 // the steps interleave (6 % faster than a rolled loop that rotates both
 // halves at the end of a step).
-template <int MODE, bool DIAG, bool FOLD>
+template <int MODE, bool DIAG, bool FOLD, bool RUNI = false>
 __device__ __forceinline__ void tiles3_coltile(
     const ulonglong2 *__restrict__ ct, const int col0, const int ccnt,
     float *__restrict__ accC, const int lane, const f2_t (&X0)[4], const f2_t (&X1)[4],
@@ -174,11 +177,11 @@ __device__ __forceinline__ void tiles3_coltile(
   for (int t = 0; t < 8; ++t) {
     const ulonglong2 *cp = cb + ((p + t) & 7);
     const ulonglong2 a00 = cp[0], a01 = cp[kTile], a10 = cp[32], a11 = cp[32 + kTile];
-    t3_half<MODE, COLS, FOLD>(a00, a01, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[0], c0[0], c1[0],
-                              c2[0]);
+    t3_half<MODE, COLS, FOLD, RUNI>(a00, a01, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[0], c0[0],
+                                    c1[0], c2[0]);
     if (t < 7) t3_rotate(cs[0], c0[0], c1[0], c2[0], src);
-    t3_half<MODE, COLS, FOLD>(a10, a11, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[1], c0[1], c1[1],
-                              c2[1]);
+    t3_half<MODE, COLS, FOLD, RUNI>(a10, a11, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[1], c0[1],
+                                    c1[1], c2[1]);
     if (t < 7) t3_rotate(cs[1], c0[1], c1[1], c2[1], src);
   }
   {
@@ -238,6 +241,7 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     // the column weights are folded into the exponent when all >= 0 (never
     // with the sigma gradient, whose r^2 the fold would shift)
     const bool fold = !SIG && meta[meta_fold(3) + cside] != 0.0;
+    const bool runi = fold && meta[meta_fold(3) + rside] == 2.0;
 
     // 32-bit tile/column indices: a pair's cloud has < 2^31 points
     const int nTc = (int)ceil_div(ccnt, (int64_t)kTile);
@@ -307,8 +311,9 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
       ++J0;
     }
     // ---- off-diagonal tiles: rows and columns ------------------------------
-    auto offdiag = [&](auto fold_tag) {
+    auto offdiag = [&](auto fold_tag, auto uni_tag) {
       constexpr bool F = decltype(fold_tag)::value;
+      constexpr bool U = decltype(uni_tag)::value;
 #pragma unroll 1
       for (int J = J0; J < J1; ++J) {
         const ulonglong2 *ct = ct0 + J * kT3TileU2;
@@ -323,16 +328,19 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
         f2_t stt[4];
 #pragma unroll
         for (int rp = 0; rp < 4; ++rp) stt[rp] = z2;
-        tiles3_coltile<MODE, false, F>(ct, J * kTile, cc, accC0 + J * (kTile * kAcc3Stride),
-                                       lane, X0, X1, X2, Aw, stt, G0, G1, G2, sgt);
+        tiles3_coltile<MODE, false, F, U>(ct, J * kTile, cc,
+                                          accC0 + J * (kTile * kAcc3Stride), lane, X0, X1, X2,
+                                          Aw, stt, G0, G1, G2, sgt);
 #pragma unroll
         for (int rp = 0; rp < 4; ++rp) st[rp] = add2(st[rp], stt[rp]);
       }
     };
-    if (fold)
-      offdiag(BoolTag<!SIG>{});
+    if (runi)
+      offdiag(BoolTag<!SIG>{}, BoolTag<!SIG>{});
+    else if (fold)
+      offdiag(BoolTag<!SIG>{}, BoolTag<false>{});
     else
-      offdiag(BoolTag<false>{});
+      offdiag(BoolTag<false>{}, BoolTag<false>{});
     // row sums accumulated in fp32 over the item: fold once into fp64
 #pragma unroll
     for (int rp = 0; rp < 4; ++rp) {
