@@ -11,9 +11,13 @@
 //       S = X Y^T, 3xTF32 (x = x_hi + x_lo; S = hi*hi + hi*lo + lo*hi), so S
 //       keeps ~fp32 accuracy; plain TF32 would put a 1e-3 relative error on
 //       r^2 = |x'|^2 + |y'|^2 - 2 S.
-//   epilogue (registers): r^2, k = ex2(-r^2), w = b_j k (diagonal left out in
-//       self blocks), row sums s_i = sum w, S_i = sum w r^2, and P = w split
-//       into tf32 hi/lo and stored back into TMEM.
+//   epilogue (registers): w = b_j 2^(-r^2) (diagonal left out in self
+//       blocks), row sums s_i = sum w, S_i = sum w r^2, and P = w split into
+//       tf32 hi/lo and stored back into TMEM.  With the tile's weights all
+//       >= 0 the weight is folded into the exponent: w = 2^(2S - |x'|^2 -
+//       (|y'|^2 - log2 b_j)), one FADD + one FFMA + EX2 per term; P's hi half
+//       is w with the low 13 mantissa bits cleared (exact in tf32) and lo the
+//       exact remainder.
 //   GEMM 2 (A = P from TMEM, B = the Y tile stored transposed):
 //       T_i += sum_j w_ij y'_j, again 3xTF32, accumulated in TMEM over all
 //       column tiles of the item.
@@ -47,9 +51,9 @@ __host__ __device__ constexpr int tc_tmem_cols(int DP) {
   return 3 * DP + 2 * kTcCols <= 256 ? 256 : 512;
 }
 __host__ __device__ constexpr size_t tc_smem_bytes(int DP) {
-  // Y_hi, Y_lo, Yt_hi, Yt_lo, column weights, 8 partial |y'|^2 per point and
-  // their totals, barrier and TMEM address
-  return (size_t)4 * kTcCols * DP * 4 + kTcCols * 4 * 10 + 16;
+  // Y_hi, Y_lo, Yt_hi, Yt_lo, column weights, 8 partial |y'|^2 per point,
+  // their totals and the totals less log2 b, barrier and TMEM address
+  return (size_t)4 * kTcCols * DP * 4 + kTcCols * 4 * 11 + 16;
 }
 // Dynamic shared memory requested per CTA: enough that no more CTAs share an
 // SM than its 512 TMEM columns hold (a CTA that cannot allocate would wait
@@ -149,6 +153,11 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+template <bool V>
+struct BoolC {
+  static constexpr bool value = V;
+};
+
 // ---- the kernel -------------------------------------------------------------
 template <int DP, int MODE>
 __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
@@ -170,7 +179,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
   float *bcol = reinterpret_cast<float *>(tc_smem + 4 * kTcCols * DP * 4);
   float *ysq = bcol + kTcCols;        // [8][64] partial |y'|^2
   float *ytot = ysq + 8 * kTcCols;    // [64] their totals, summed in order
-  uint64_t *mbar = reinterpret_cast<uint64_t *>(ytot + kTcCols);
+  float *yqf = ytot + kTcCols;        // [64] |y'|^2 - log2 b (folded weight)
+  uint64_t *mbar = reinterpret_cast<uint64_t *>(yqf + kTcCols);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mbar + 1);
   __shared__ double red[kTcThreads / 32 * 2];
 
@@ -252,11 +262,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 
     // Column tiles are loaded into registers one tile ahead: thread t takes
-    // 4-point x 4-coordinate blocks (q = t % 16, coordinates 4c..4c+3 for
-    // c = t / 16 + 8 i), all loads of a tile in flight at once; the next
-    // tile's loads are issued right after GEMM 2 of this one is launched.
+    // 4-point x 4-coordinate blocks (point group q, coordinates 4c..4c+3 for
+    // c = c0 + 8 i), all loads of a tile in flight at once; the next tile's
+    // loads are issued right after GEMM 2 of this one is launched.  The
+    // (q, c0) assignment makes every 8-thread phase of a 16-byte store hit 8
+    // distinct bank groups in both layouts: q & 1 = t2, c0 & 1 = t0 ^ t2,
+    // and the store order rotates with t & 3.
     constexpr int KB = NCH / (kTcThreads / NQ);  // blocks per thread
-    const int q = tid & (NQ - 1), c0 = tid / NQ, rot = tid & 3;
+    static_assert(NQ == 16 && kTcThreads == 128, "thread mapping assumes 16 x 8");
+    const int tb0 = tid & 1, tb1 = (tid >> 1) & 1, tb2 = (tid >> 2) & 1;
+    const int q = tb2 | (tb1 << 1) | (((tid >> 3) & 3) << 2);
+    const int c0 = (tb0 ^ tb2) | (((tid >> 5) & 3) << 1), rot = tid & 3;
     float4 E[KB][4];
     float bw[4];
     auto load_tile = [&](int64_t jt) {
@@ -315,13 +331,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
     float s = 0.f, sig = 0.f;
     double s64 = 0.0, sg64 = 0.0;
     bool first = true;
+    const float nxsq = -xsq;
+    const int64_t row0 = (int64_t)item.tile * kTcRows;  // first row of the item
 #pragma unroll 1
     for (int64_t j0 = 0; j0 < ccnt && ok; j0 += kTcCols) {
       // ---- column tile (registers, loaded earlier) -> Y in smem, |y'|^2 ------
       store_tile(j0);
       fence_async_smem();
       tc_fence_before();
-      __syncthreads();
+      // a negative column weight cannot be folded into the exponent
+      const bool anyneg = __syncthreads_or(c0 == 0 && (bw[0] < 0.f || bw[1] < 0.f ||
+                                                       bw[2] < 0.f || bw[3] < 0.f)) != 0;
       tc_fence_after();
 
       // ---- GEMM 1: S = X Y^T (3xTF32), one thread issues -------------------
@@ -345,6 +365,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
 #pragma unroll
         for (int g = 0; g < kTcThreads / NQ; ++g) t += ysq[g * kTcCols + tid];
         ytot[tid] = t;
+        yqf[tid] = t - log2f(bcol[tid]);  // +inf for zero weight and padding
       }
       // the decision to stop is taken by the whole CTA at once
       if (__syncthreads_or(!mbar_wait(mb, phase))) {
@@ -358,28 +379,45 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
       const int64_t dj = row - j0;  // this row's diagonal column in the tile
       const int diag = (self && dj >= 0 && dj < kTcCols) ? (int)dj : -1;
       float st = 0.f, sgt = 0.f;
+      auto epilogue = [&](auto fold_t, auto diag_t) {
+        constexpr bool FOLD = decltype(fold_t)::value, DG = decltype(diag_t)::value;
 #pragma unroll 1
-      for (int c0 = 0; c0 < kTcCols; c0 += 32) {
-        float S[32];
-        tmem_ld32(tlane + C_S + c0, S);
-        uint32_t ph[32], pl[32];
+        for (int cb = 0; cb < kTcCols; cb += 32) {
+          float S[32];
+          tmem_ld32(tlane + C_S + cb, S);
+          uint32_t ph[32], pl[32];
 #pragma unroll
-        for (int u = 0; u < 32; ++u) {
-          const int j = c0 + u;
-          const float yq = ytot[j];
-          const float r2 = fmaxf(xsq + yq - 2.f * S[u], 0.f);
-          float w = bcol[j] * ex2(-r2);
-          if (j == diag) w = 0.f;
-          st += w;
-          if (SIG) sgt = fmaf(w, r2, sgt);
-          ph[u] = to_tf32(w);
-          pl[u] = to_tf32(w - __uint_as_float(ph[u]));
+          for (int u = 0; u < 32; ++u) {
+            const int j = cb + u;
+            float w, r2 = 0.f;
+            if (FOLD) {
+              w = ex2(fmaf(2.f, S[u], nxsq - yqf[j]));  // b_j 2^(-r^2)
+              if (SIG) r2 = fmaxf(xsq + ytot[j] - 2.f * S[u], 0.f);
+            } else {
+              r2 = fmaxf(xsq + ytot[j] - 2.f * S[u], 0.f);
+              w = bcol[j] * ex2(-r2);
+            }
+            if (DG && j == diag) w = 0.f;
+            st += w;
+            if (SIG) sgt = fmaf(w, r2, sgt);
+            const float hi = __uint_as_float(__float_as_uint(w) & 0xFFFFE000u);
+            ph[u] = __float_as_uint(hi);
+            pl[u] = __float_as_uint(w - hi);
+          }
+          if (GRAD) {
+            tmem_st32(tlane + C_S + cb, ph);  // P_hi overwrites S (already read)
+            tmem_st32(tlane + C_PL + cb, pl);
+          }
         }
-        if (GRAD) {
-          tmem_st32(tlane + C_S + c0, ph);  // P_hi overwrites S (already read)
-          tmem_st32(tlane + C_PL + c0, pl);
-        }
-      }
+      };
+      // the tile meets the diagonal of a self block (CTA-uniform)
+      const bool dtile = self && j0 < row0 + kTcRows && row0 < j0 + kTcCols;
+      if (anyneg)
+        epilogue(BoolC<false>{}, BoolC<true>{});
+      else if (dtile)
+        epilogue(BoolC<true>{}, BoolC<true>{});
+      else
+        epilogue(BoolC<true>{}, BoolC<false>{});
       s += st;
       s64 += (double)st;
       if (SIG) {
