@@ -268,6 +268,36 @@ RA_API unsigned long long ra_kernel_launch_count(void);
 RA_API int ra_probe_fp32_peak(float *scratch, int64_t scratch_floats, int iters, double *ops_per_s,
                        ra_stream_t stream);
 
+/* ---- float64 verification path --------------------------------------- */
+/* Replaces rapidalign/kde_gradients.py:39-193 (kde_mmd_forward_cpu,
+ * kde_mmd_backward_cpu, kde_mmd_backward_ragged_cpu): closed-form sums and
+ * gradients of the raw-weight loss L = Kxx + Kyy - 2 Kxy per pair, every
+ * term in double precision (exp, direct differences), for verification on
+ * small problems (O(N^2 D) per pair, one thread per point).
+ *
+ * x [NX, D], y [NY, D], w_x [NX], w_y [NY], ptr_x / ptr_y [P + 1]: device
+ * arrays.  Outputs (device, caller-allocated): Kxx, Kyy, Kxy [P] (required);
+ * loss [P], grad_x [NX, D], grad_y [NY, D], grad_wx [NX], grad_wy [NY],
+ * grad_sigma [P] (each may be NULL).  The workspace (256-byte aligned) holds
+ * at least ra_kde_exact_workspace_bytes(NX, NY).  The call synchronises
+ * `stream` once to read the ptr checks (RA_ERR_PTR_*), which must pass
+ * before any segment is walked. */
+RA_API size_t ra_kde_exact_workspace_bytes(int64_t NX, int64_t NY);
+RA_API int ra_kde_exact_f64(const double *x, const double *y, const double *w_x,
+                            const double *w_y, const int64_t *ptr_x, const int64_t *ptr_y,
+                            int64_t P, int64_t NX, int64_t NY, int32_t D, double sigma,
+                            double *loss, double *Kxx, double *Kyy, double *Kxy, double *grad_x,
+                            double *grad_y, double *grad_wx, double *grad_wy, double *grad_sigma,
+                            void *workspace, size_t workspace_bytes, ra_stream_t stream);
+
+/* Dense matrices of one pair (kde_gradients.py:32-36):
+ * G[i][j] = exp(-|a_i - b_j|^2 / (2 sigma^2)) [n, m] and
+ * diff[i][j][d] = a_i[d] - b_j[d] [n, m, D], float64; either output may be
+ * NULL.  At most 2^36 entries. */
+RA_API int ra_kde_exact_matrices_f64(const double *a, int64_t n, const double *b, int64_t m,
+                                     int32_t D, double sigma, double *G, double *diff,
+                                     ra_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -122,6 +122,10 @@ SIGNATURES = {
                                                      _V]),
     "ra_kde_mmd_forward_segmented_noalloc": (ctypes.c_int, [_V, _V, _V, _V, _V, _V, _I64, _I64,
                                                             _I64, _I32, _D, _V, _V, _V, _V]),
+    "ra_kde_exact_workspace_bytes": (_SZ, [_I64, _I64]),
+    "ra_kde_exact_f64": (ctypes.c_int, [_V, _V, _V, _V, _V, _V, _I64, _I64, _I64, _I32, _D,
+                                        _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
+    "ra_kde_exact_matrices_f64": (ctypes.c_int, [_V, _I64, _V, _I64, _I32, _D, _V, _V, _V]),
     "ra_kernel_launch_count": (ctypes.c_ulonglong, []),
     "ra_probe_fp32_peak": (ctypes.c_int, [_V, _I64, ctypes.c_int, ctypes.POINTER(_D), _V]),
 }

@@ -17,6 +17,7 @@
 #include "ra_chunks.cuh"
 #include "ra_common.cuh"
 #include "ra_epilogue.cuh"
+#include "ra_exact.cuh"
 #include "ra_plan.cuh"
 #include "ra_prep.cuh"
 #include "ra_tc.cuh"
@@ -932,6 +933,83 @@ int ra_probe_fp32_peak(float *scratch, int64_t scratch_floats, int iters, double
   const double ops = (double)blocks * threads * iters * 16.0 * 8.0 * 2.0;
   *ops_per_s = ops / (ms * 1e-3);
   return RA_OK;
+}
+
+// ---- float64 verification path (ra_exact.cuh) ------------------------------
+
+size_t ra_kde_exact_workspace_bytes(int64_t NX, int64_t NY) {
+  if (NX < 0 || NY < 0) return 0;
+  return 256 + sizeof(double) * 4 * (size_t)(NX + NY);
+}
+
+int ra_kde_exact_f64(const double *x, const double *y, const double *w_x, const double *w_y,
+                     const int64_t *ptr_x, const int64_t *ptr_y, int64_t P, int64_t NX,
+                     int64_t NY, int32_t D, double sigma, double *loss, double *Kxx, double *Kyy,
+                     double *Kxy, double *grad_x, double *grad_y, double *grad_wx,
+                     double *grad_wy, double *grad_sigma, void *workspace,
+                     size_t workspace_bytes, ra_stream_t stream) {
+  if (P < 0 || NX < 0 || NY < 0 || D < 1 || D > kExactMaxD) return RA_ERR_INVALID_ARGUMENT;
+  if (!(sigma > 0.0)) return RA_ERR_SIGMA;
+  if (ptr_x == nullptr || ptr_y == nullptr || Kxx == nullptr || Kyy == nullptr ||
+      Kxy == nullptr || workspace == nullptr)
+    return RA_ERR_INVALID_ARGUMENT;
+  if ((NX > 0 && (x == nullptr || w_x == nullptr)) || (NY > 0 && (y == nullptr || w_y == nullptr)))
+    return RA_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < ra_kde_exact_workspace_bytes(NX, NY) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return RA_ERR_WORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  ExactArgs A;
+  A.P = P;
+  A.NX = NX;
+  A.NY = NY;
+  A.D = D;
+  A.sigma = sigma;
+  A.x = x;
+  A.y = y;
+  A.w_x = w_x;
+  A.w_y = w_y;
+  A.ptr_x = ptr_x;
+  A.ptr_y = ptr_y;
+  A.grad_x = grad_x;
+  A.grad_y = grad_y;
+  A.grad_wx = grad_wx;
+  A.grad_wy = grad_wy;
+  A.err = static_cast<int *>(workspace);
+  A.work = reinterpret_cast<double *>(static_cast<char *>(workspace) + 256);
+  // the ptr checks must pass before any kernel walks the segments: this
+  // verification path synchronises the stream once to read them
+  if (cudaMemsetAsync(A.err, 0, sizeof(int), st) != cudaSuccess) return RA_ERR_CUDA;
+  exact_check_kernel<<<(unsigned)ceil_div(P + 1, (int64_t)256), 256, 0, st>>>(A);
+  ++g_launches;
+  int err = 0;
+  if (cudaMemcpyAsync(&err, A.err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return RA_ERR_CUDA;
+  if (err & kErrPtrStart) return RA_ERR_PTR_START;
+  if (err & kErrPtrEnd) return RA_ERR_PTR_END;
+  if (err & kErrPtrOrder) return RA_ERR_PTR_ORDER;
+  if (P == 0) return RA_OK;
+  if (NX + NY > 0) {
+    exact_points_kernel<<<(unsigned)ceil_div(NX + NY, (int64_t)128), 128, 0, st>>>(A);
+    ++g_launches;
+  }
+  exact_pairs_kernel<<<(unsigned)P, 256, 0, st>>>(A, Kxx, Kyy, Kxy, loss, grad_sigma);
+  ++g_launches;
+  return cuda_status(cudaGetLastError());
+}
+
+int ra_kde_exact_matrices_f64(const double *a, int64_t n, const double *b, int64_t m, int32_t D,
+                              double sigma, double *G, double *diff, ra_stream_t stream) {
+  if (n < 0 || m < 0 || D < 1 || D > kExactMaxD) return RA_ERR_INVALID_ARGUMENT;
+  if (!(sigma > 0.0)) return RA_ERR_SIGMA;
+  if ((n > 0 && a == nullptr) || (m > 0 && b == nullptr)) return RA_ERR_INVALID_ARGUMENT;
+  if (n * m > ((int64_t)1 << 36)) return RA_ERR_INVALID_ARGUMENT;
+  if (n == 0 || m == 0 || (G == nullptr && diff == nullptr)) return RA_OK;
+  exact_matrices_kernel<<<(unsigned)ceil_div(n * m, (int64_t)256), 256, 0,
+                          (cudaStream_t)stream>>>(a, n, b, m, D, sigma, G, diff);
+  ++g_launches;
+  return cuda_status(cudaGetLastError());
 }
 
 }  // extern "C"

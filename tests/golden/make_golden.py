@@ -188,6 +188,24 @@ def case_segmented(name, ptr_x, ptr_y, d, sigma, seed):
          raw_gsigma_pairs=raw["sigma_per_pair"].numpy())
 
 
+def case_gradients(name, n, m, d, sigma, seed):
+    """kde_gradients.py single-pair helpers: forward matrices and backward."""
+    from rapidalign.kde_gradients import kde_mmd_backward_cpu
+    g = torch.Generator().manual_seed(seed)
+    x = f32(torch.randn(n, d, generator=g))
+    y = f32(torch.randn(m, d, generator=g) * 1.1 + 0.1)
+    wx = f32(torch.rand(n, generator=g) + 0.1)
+    wy = f32(torch.rand(m, generator=g) + 0.1)
+    out = kde_mmd_backward_cpu(x, y, wx, wy, sigma)
+    fwd = out["forward"]
+    save(name, x=x.numpy(), y=y.numpy(), w_x=wx.numpy(), w_y=wy.numpy(), sigma=np.float64(sigma),
+         loss=fwd.loss.numpy(), Kxx=fwd.Kxx.numpy(), Kyy=fwd.Kyy.numpy(), Kxy=fwd.Kxy.numpy(),
+         Gxx=fwd.Gxx.numpy(), Gyy=fwd.Gyy.numpy(), Gxy=fwd.Gxy.numpy(),
+         diff_xx=fwd.diff_xx.numpy(), diff_yy=fwd.diff_yy.numpy(), diff_xy=fwd.diff_xy.numpy(),
+         grad_x=out["x"].numpy(), grad_y=out["y"].numpy(), grad_wx=out["w_x"].numpy(),
+         grad_wy=out["w_y"].numpy(), grad_sigma=out["sigma"].numpy())
+
+
 def case_learned(name, kind, n, m, seed):
     """learned_kernel.py modules (float64; the gate's float32 cast is undone by
     a forward pre-hook so that the whole module runs in float64)."""
@@ -250,6 +268,9 @@ def main():
     case_segmented("segmented_ragged", [0, 10, 11, 40, 40, 57], [0, 8, 20, 41, 44, 60], 3, 0.25,
                    7)
     case_segmented("segmented_d2", [0, 2, 5], [0, 3, 4], 2, 0.25, 6)
+    # the float64 verification helpers (kde_gradients.py:39-132), one pair
+    case_gradients("gradients_d3", 23, 17, 3, 0.4, 40)
+    case_gradients("gradients_d16", 12, 9, 16, 1.3, 41)
     # learned-kernel callers (learned_kernel.py:41-202)
     case_learned("learned_multi", "multi", 60, 45, 30)
     case_learned("learned_single", "single", 50, 64, 31)

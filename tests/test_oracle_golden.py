@@ -18,8 +18,30 @@ def rel(a, b):
 
 
 # the loss fixtures (the learned-kernel module fixtures are checked in
-# test_learned_kernel.py)
-LOSS_CASES = [n for n in golden_cases() if not n.startswith("learned")]
+# test_learned_kernel.py, the single-pair helper fixtures below)
+LOSS_CASES = [n for n in golden_cases()
+              if not n.startswith("learned") and not n.startswith("gradients")]
+
+
+@pytest.mark.parametrize("name", golden_cases("gradients"))
+def test_oracle_matches_gradient_helpers(name):
+    """kde_gradients.py single-pair helpers (raw weights, one pair)."""
+    z = load_golden(name)
+    n, m = z["x"].shape[0], z["y"].shape[0]
+    px, py = np.array([0, n]), np.array([0, m])
+    sigma = float(z["sigma"])
+    Kxx, Kyy, Kxy = O.legacy_forward_segmented(z["x"], z["y"], z["w_x"], z["w_y"], px, py, sigma)
+    assert rel(Kxx, np.atleast_1d(z["Kxx"])) < TOL and rel(Kyy, np.atleast_1d(z["Kyy"])) < TOL
+    assert rel(Kxy, np.atleast_1d(z["Kxy"])) < TOL
+    gx, gy, gwx, gwy, gs = O.legacy_backward_segmented(z["x"], z["y"], z["w_x"], z["w_y"], px, py,
+                                                       np.ones(1), sigma)
+    assert rel(gx, z["grad_x"]) < TOL and rel(gy, z["grad_y"]) < TOL
+    assert rel(gwx, z["grad_wx"]) < TOL and rel(gwy, z["grad_wy"]) < TOL
+    assert rel(gs, np.atleast_1d(z["grad_sigma"])) < TOL
+    # the matrices by their definition (kde_gradients.py:32-36)
+    d = z["x"][:, None, :] - z["y"][None, :, :]
+    assert rel(d, z["diff_xy"]) < TOL
+    assert rel(np.exp(-(d ** 2).sum(-1) / (2 * sigma ** 2)), z["Gxy"]) < TOL
 
 
 @pytest.mark.parametrize("name", LOSS_CASES)
