@@ -57,6 +57,7 @@ enum ra_status {
   RA_ERR_STATE = 20,              /* backward called without a matching forward state */
   RA_ERR_SCRATCH_LIMIT = 21,      /* problem needs more than the fixed no-alloc scratch */
   RA_ERR_DEVICE_TIMEOUT = 22,     /* a bounded wait inside a kernel expired (reported, not hung) */
+  /* RA_ERR_SIGMA is also returned by ra_kde_check for a per-pair sigma <= 0 */
 };
 
 /* Human-readable name of a status code (static string). */
@@ -117,6 +118,9 @@ typedef struct ra_kde_inputs {
   const int64_t *ptr_y;  /* ragged: [P + 1] */
   const uint8_t *mask_x; /* dense: [num_x] (nonzero = valid) */
   const uint8_t *mask_y; /* dense: [num_y] */
+  const double *sigma_pairs; /* [P] per-pair bandwidths (all > 0), or NULL: desc->sigma
+                                for every pair.  Several bandwidths of one pair of clouds
+                                in one call = the clouds repeated as P pairs. */
 } ra_kde_inputs;
 
 typedef struct ra_kde_grads {

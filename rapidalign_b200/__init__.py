@@ -1,11 +1,12 @@
 """rapidalign_b200 -- B200-native (sm_100a) KDE/MMD loss, API-compatible with
 ``rapidalign`` (kde_mmd_loss, kde_mmd_loss_dense, pyg_kde_mmd_loss and the
 differentiable segmented_kde_loss)."""
-from .kde import kde_mmd_loss, kde_mmd_loss_dense, pyg_kde_mmd_loss
+from .kde import kde_mmd_loss, kde_mmd_loss_bands, kde_mmd_loss_dense, pyg_kde_mmd_loss
 from .autograd_kde import SegmentedKDELossFunction, segmented_kde_loss
 
 __all__ = [
     "kde_mmd_loss",
+    "kde_mmd_loss_bands",
     "kde_mmd_loss_dense",
     "pyg_kde_mmd_loss",
     "segmented_kde_loss",

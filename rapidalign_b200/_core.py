@@ -40,6 +40,9 @@ class Spec:
     ptr_y: Optional[Tensor] = None
     mask_x: Optional[Tensor] = None
     mask_y: Optional[Tensor] = None
+    # float64 [P] per-pair bandwidths (then `sigma` is ignored by the kernels
+    # and a sigma tensor gets one gradient per pair)
+    sigma_pairs: Optional[Tensor] = None
     # which device-detected errors can occur (and must be checked, at the
     # price of one synchronisation): user ptr offsets, SUM-normalised weights
     check_errors: bool = False
@@ -86,6 +89,7 @@ def _inputs(x32, y32, wx32, wy32, spec: Spec) -> _lib.RaKdeInputs:
     i.ptr_y = _lib.ptr(spec.ptr_y)
     i.mask_x = _lib.ptr(spec.mask_x)
     i.mask_y = _lib.ptr(spec.mask_y)
+    i.sigma_pairs = _lib.ptr(spec.sigma_pairs)
     return i
 
 
@@ -214,7 +218,12 @@ def backward_sums(state: _State, coef: Tensor, need) -> tuple:
     out_y = gy.to(ydt).reshape(ysh) if gy is not None else None
     out_wx = gwx.to(wxm[0]).reshape(wxm[1]) if gwx is not None else None
     out_wy = gwy.to(wym[0]).reshape(wym[1]) if gwy is not None else None
-    out_s = gsig.sum().to(sm[0]).reshape(sm[1]) if gsig is not None else None
+    if gsig is None:
+        out_s = None
+    elif spec.sigma_pairs is not None:  # one bandwidth per pair
+        out_s = gsig.to(sm[0]).reshape(sm[1])
+    else:
+        out_s = gsig.sum().to(sm[0]).reshape(sm[1])
     return out_x, out_y, out_wx, out_wy, out_s
 
 

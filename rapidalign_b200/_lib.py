@@ -76,6 +76,7 @@ class RaKdeInputs(ctypes.Structure):
         ("ptr_y", ctypes.c_void_p),
         ("mask_x", ctypes.c_void_p),
         ("mask_y", ctypes.c_void_p),
+        ("sigma_pairs", ctypes.c_void_p),
     ]
 
 

@@ -170,10 +170,7 @@ T *at(void *ws, size_t off) {
 
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? RA_OK : RA_ERR_CUDA; }
 
-float scale_for(double sigma) {
-  // k = exp(-r^2 / (2 sigma^2)) = 2^(-(c r)^2) with c^2 = log2(e) / (2 sigma^2)
-  return (float)std::sqrt(1.4426950408889634 / (2.0 * sigma * sigma));
-}
+float scale_for(double sigma) { return scale_of_sigma(sigma); }
 
 int check_common(const ra_kde_desc *d, void *ws, size_t ws_bytes, size_t need) {
   if (!desc_ok(d)) return RA_ERR_INVALID_ARGUMENT;
@@ -329,6 +326,7 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   pa.nmax_y = d->nmax_y;
   pa.chunk_cap = L.max_chunks;
   pa.scale = scale;
+  pa.sigma_p = in->sigma_pairs;
   pa.x = in->x;
   pa.y = in->y;
   pa.w_x = in->w_x;
@@ -409,6 +407,7 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     pk.D = d->dim;
     pk.nq = L.nq;
     pk.scale = scale;
+    pk.sigma_p = in->sigma_pairs;
     pk.x = in->x;
     pk.y = in->y;
     pk.w_x = in->w_x;
@@ -539,6 +538,7 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.wmode_y = d->weights_y;
   ea.scale = (double)scale_for(d->sigma);
   ea.sigma = d->sigma;
+  ea.sigma_p = in->sigma_pairs;
   ea.seg = at<Seg>(ws, L.seg);
   ea.meta = at<double>(ws, L.meta);
   ea.coef = coef;
@@ -786,6 +786,7 @@ int ra_kde_check(const void *workspace, ra_stream_t stream) {
   if (err & kErrPtrOrder) return RA_ERR_PTR_ORDER;
   if (err & kErrWeightSum) return RA_ERR_WEIGHT_SUM;
   if (err & kErrTimeout) return RA_ERR_DEVICE_TIMEOUT;
+  if (err & kErrSigma) return RA_ERR_SIGMA;
   return RA_OK;
 }
 

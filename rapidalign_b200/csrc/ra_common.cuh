@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <math.h>
 #include <stdint.h>
 
 namespace ra {
@@ -56,6 +57,14 @@ __device__ __forceinline__ f2_t fma2(f2_t a, f2_t b, f2_t c) {
   f2_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
+}
+
+// Coordinate pre-scale for bandwidth sigma: packed coordinates are
+// c (p - anchor) with c^2 = log2(e) / (2 sigma^2), so that
+// exp(-|u - v|^2 / (2 sigma^2)) = 2^(-|c u - c v|^2).  The same float on the
+// host and on the device (sqrt is correctly rounded on both).
+__host__ __device__ __forceinline__ float scale_of_sigma(double sigma) {
+  return (float)sqrt(1.4426950408889634 / (2.0 * sigma * sigma));
 }
 
 // 2^x on the SFU (MUFU.EX2), flush-to-zero: inputs below -126 give 0, which
@@ -144,6 +153,7 @@ enum : int {
   kErrPtrOrder = 4,
   kErrWeightSum = 8,
   kErrTimeout = 16,  // a bounded device-side wait expired (tensor-core path)
+  kErrSigma = 32,    // a per-pair bandwidth is not > 0
 };
 
 // Per pair: where its points live and how many of them the kernels visit.

@@ -93,6 +93,7 @@ struct EpilogueArgs {
   const uint8_t *mask_x, *mask_y;
   const ulonglong2 *tiles_x, *tiles_y;  // packed3: tile layout (ra_prep.cuh)
   const float *aw_x, *aw_y;             // packed3: a~ = a / m per slot
+  const double *sigma_p;                // [P] per-pair bandwidths, or null
   const int64_t *tbase_x, *tbase_y;     // packed3: first tile of each pair
   int nq;                               // packed3: arrays per tile
   const float *Gx, *Gy, *Ax, *Ay;       // generic
@@ -147,7 +148,9 @@ __device__ __forceinline__ EpiSide epi_side(const EpilogueArgs &A, int64_t p, in
   E.cxy = A.coef[2 * A.P + p];
   E.cs = side == 0 ? 2.0 * E.cxx : 2.0 * E.cyy;
   E.cc = E.cxy;
-  E.k_x = 1.0 / (A.scale * A.sigma * A.sigma);
+  const double sgm = A.sigma_p != nullptr ? A.sigma_p[p] : A.sigma;
+  const double sc = A.sigma_p != nullptr ? (double)scale_of_sigma(sgm) : A.scale;
+  E.k_x = 1.0 / (sc * sgm * sgm);
   const double *meta = A.meta + p * meta_stride(A.DP);
   E.W = meta[side];
   E.Wraw = meta[2 + side];
@@ -162,7 +165,9 @@ __global__ void sigma_grad_kernel(EpilogueArgs A) {
   const int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (p >= A.P) return;
   const double cxx = A.coef[p], cyy = A.coef[A.P + p], cxy = A.coef[2 * A.P + p];
-  const double c2 = A.scale * A.scale, s3 = A.sigma * A.sigma * A.sigma;
+  const double sg = A.sigma_p != nullptr ? A.sigma_p[p] : A.sigma;
+  const double sc = A.sigma_p != nullptr ? (double)scale_of_sigma(sg) : A.scale;
+  const double c2 = sc * sc, s3 = sg * sg * sg;
   const double Sxx = A.S_ws[p], Syy = A.S_ws[A.P + p], Sxy = A.S_ws[2 * A.P + p];
   A.grad_sigma[p] = (cxx * Sxx + cyy * Syy + cxy * Sxy) / (c2 * s3);
 }

@@ -62,6 +62,7 @@ struct PrepArgs {
   int64_t num_x, num_y, nmax_x, nmax_y;
   int64_t chunk_cap;  // capacity of the chunk records (host bound)
   float scale;   // sqrt(log2(e) / (2 sigma^2)): packed coords are scale * (p - anchor)
+  const double *sigma_p;  // [P] per-pair bandwidths, or null: `scale` for every pair
   const float *x, *y, *w_x, *w_y;
   const int64_t *ptr_x, *ptr_y;
   const uint8_t *mask_x, *mask_y;
@@ -74,6 +75,11 @@ struct PrepArgs {
   // generic layout (D >= 4): coords [num * DP] (zero padded) and weights [num]
   float *Gx, *Gy, *Ax, *Ay;
 };
+
+// The coordinate pre-scale of pair p.
+__device__ __forceinline__ float pair_scale(float scale, const double *sigma_p, int64_t p) {
+  return sigma_p != nullptr ? scale_of_sigma(sigma_p[p]) : scale;
+}
 
 // Effective (masked, raw) weight of point i.
 __device__ __forceinline__ float eff_weight(const float *w, const uint8_t *mask, int wmode,
@@ -380,6 +386,7 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
   const int lane = threadIdx.x & 31;
   if (p >= A.P) return;
   const int D = A.D, DP = A.DP;
+  if (A.sigma_p != nullptr && lane == 0 && !(A.sigma_p[p] > 0.0)) atomicOr(A.err, (int)kErrSigma);
   const int rs = stats_stride(DP);
   double *meta = A.meta + p * meta_stride(DP);
   const int64_t lo = A.choff[p], hi = A.choff[p + 1];
@@ -497,12 +504,13 @@ __global__ void __launch_bounds__(NT) packg_kernel(PrepArgs A) {
     const double *meta = A.meta + p * meta_stride(DP);
     const double Wn = meta[side];
     const double *anc = meta + 4 + (2 + side) * DP;
+    const float sc = pair_scale(A.scale, A.sigma_p, p);
     const int64_t b = c * kChunk, e = b + kChunk < count ? b + kChunk : count;
     for (int64_t i = b + pl; i < e; i += lanes) {
       const int64_t g = s + i;
       if (d < DP) {
         float val = 0.f;
-        if (d < D) val = A.scale * (float)((double)pts[g * D + d] - anc[d]);
+        if (d < D) val = sc * (float)((double)pts[g * D + d] - anc[d]);
         Gp[g * DP + d] = val;
       }
       if (d == 0) Ap[g] = (float)((double)eff_weight(w, mask, wmode, g) / Wn);
@@ -537,7 +545,7 @@ __global__ void __launch_bounds__(256) packgw_kernel(PrepArgs A) {
     // anchors kept in fp64: the same packed values as the scalar kernel
     const double a0 = live ? anc[4 * c] : 0.0, a1 = live ? anc[4 * c + 1] : 0.0;
     const double a2 = live ? anc[4 * c + 2] : 0.0, a3 = live ? anc[4 * c + 3] : 0.0;
-    const float sc = A.scale;
+    const float sc = pair_scale(A.scale, A.sigma_p, p);
     const int64_t b = ch * kChunk, e = b + kChunk < count ? b + kChunk : count;
     const int64_t nel = (e - b) * NC;
     for (int64_t k0 = threadIdx.x; k0 < nel; k0 += 4 * 256) {
@@ -578,6 +586,7 @@ struct PackArgs {
   int64_t P;
   int D, nq;
   float scale;
+  const double *sigma_p;  // [P] per-pair bandwidths, or null
   const float *x, *y, *w_x, *w_y;
   const uint8_t *mask_x, *mask_y;
   int wmode_x, wmode_y;
@@ -615,7 +624,7 @@ __global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
     const float ax = (float)meta[4 + (2 + side) * 3 + 0];
     const float ay = (float)meta[4 + (2 + side) * 3 + 1];
     const float az = (float)meta[4 + (2 + side) * 3 + 2];
-    const float scale = A.scale;
+    const float scale = pair_scale(A.scale, A.sigma_p, p);
     const int nq = A.nq;
     const int64_t npad = (t1 - t0) * kTile;
     const int64_t b = c * kChunk, e = b + kChunk < npad ? b + kChunk : npad;

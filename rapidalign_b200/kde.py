@@ -27,7 +27,7 @@ from ._core import Spec, kde_sums
 
 Tensor = torch.Tensor
 
-__all__ = ["kde_mmd_loss", "kde_mmd_loss_dense", "pyg_kde_mmd_loss"]
+__all__ = ["kde_mmd_loss", "kde_mmd_loss_bands", "kde_mmd_loss_dense", "pyg_kde_mmd_loss"]
 
 
 def _loss_from_k(Kxx: Tensor, Kyy: Tensor, Kxy: Tensor, cosine: bool, eps: float) -> Tensor:
@@ -92,6 +92,63 @@ def kde_mmd_loss(
     Kxx, Kyy, Kxy = kde_sums(x, y, x_w, y_w, sig_t, spec)
     loss = _loss_from_k(Kxx, Kyy, Kxy, cosine, eps)
     return (loss[0].to(dtype), Kxx[0].to(dtype), Kyy[0].to(dtype), Kxy[0].to(dtype))
+
+
+def kde_mmd_loss_bands(
+    x: Tensor,
+    y: Tensor,
+    x_w: Optional[Tensor] = None,
+    y_w: Optional[Tensor] = None,
+    sigmas=(0.05, 0.1, 0.2),
+    center: bool = True,
+    cosine: bool = False,
+    eps: float = 1e-8,
+) -> Tuple[Tensor, Tensor, Tensor, Tensor]:
+    """``kde_mmd_loss`` for S bandwidths of one pair of clouds in one call.
+
+    Equivalent to ``[kde_mmd_loss(x, y, x_w, y_w, sigma=s, ...) for s in
+    sigmas]`` stacked (the multi-band use of rapidalign/learned_kernel.py:89-
+    115): returns (loss, Kxx, Kyy, Kxy) of shape (S,).  The S bands run as S
+    pairs of one launch sequence with a per-pair bandwidth, so a small cloud
+    pays the fixed cost of the fused pipeline once instead of S times.
+    ``sigmas`` is a sequence of floats or a 1-D tensor (differentiable: each
+    band gets its own gradient).
+    """
+    if x.ndim != 2 or y.ndim != 2 or x.size(-1) != y.size(-1):
+        raise ValueError("x and y must be (N,d) and (M,d) with same d")
+    if x_w is not None and x_w.numel() != x.shape[0]:
+        raise ValueError("weights length must equal number of nodes")
+    if y_w is not None and y_w.numel() != y.shape[0]:
+        raise ValueError("weights length must equal number of nodes")
+    if (x_w is not None and x_w.numel() == 0) or (y_w is not None and y_w.numel() == 0):
+        raise ValueError("weights must sum to a positive value")
+    device = _lib.require_cuda(x, y, x_w, y_w)
+    sig = sigmas if isinstance(sigmas, Tensor) else torch.tensor(list(sigmas),
+                                                                 dtype=torch.float64)
+    if sig.ndim != 1 or sig.numel() == 0:
+        raise ValueError("sigmas must be a non-empty 1-D sequence")
+    sig64 = sig.detach().to(device=device, dtype=torch.float64).contiguous()
+    if bool((sig64 <= 0).any()):
+        raise ValueError("sigma must be positive")
+    S, N, M, D = sig.numel(), x.shape[0], y.shape[0], x.shape[1]
+    dtype = x.dtype
+    spec = Spec(
+        layout=_lib.RA_LAYOUT_DENSE, num_pairs=S, dim=D, num_x=S * N, num_y=S * M,
+        nmax_x=N, nmax_y=M,
+        weights_x=_lib.RA_WEIGHTS_SUM if x_w is not None else _lib.RA_WEIGHTS_UNIFORM,
+        weights_y=_lib.RA_WEIGHTS_SUM if y_w is not None else _lib.RA_WEIGHTS_UNIFORM,
+        center=center, sigma=1.0, sigma_pairs=sig64,
+        check_errors=(x_w is not None or y_w is not None),
+        weight_error_message="weights must sum to a positive value")
+    # the bands as S rows of a dense batch (gradients of the repeats add up)
+    xr = x.unsqueeze(0).expand(S, N, D)
+    yr = y.unsqueeze(0).expand(S, M, D)
+    xwr = None if x_w is None else x_w.reshape(1, N).expand(S, N)
+    ywr = None if y_w is None else y_w.reshape(1, M).expand(S, M)
+    sig_t = sig.to(device) if isinstance(sigmas, Tensor) and sigmas.requires_grad else None
+    Kxx, Kyy, Kxy = kde_sums(xr, yr, xwr, ywr, sig_t, spec)
+    loss = _loss_from_k(Kxx, Kyy, Kxy, cosine, eps)
+    return loss.to(dtype), Kxx.to(dtype), Kyy.to(dtype), Kxy.to(dtype)
 
 
 def kde_mmd_loss_dense(

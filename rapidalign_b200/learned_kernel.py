@@ -2,9 +2,11 @@
 
 The same modules with the same parameters (names, shapes and
 initialisation, so state dicts load either way): every kernel sum goes
-through :func:`rapidalign_b200.kde_mmd_loss`, i.e. the fused CUDA kernels,
-with gradients to the positions (and so to the anisotropic scale), to the
-node weights (and so to the weight network) and to sigma.
+through the fused CUDA kernels (:func:`rapidalign_b200.kde_mmd_loss`, and
+:func:`rapidalign_b200.kde_mmd_loss_bands` for the multi-band module: all
+bandwidths in one call), with gradients to the positions (and so to the
+anisotropic scale), to the node weights (and so to the weight network) and
+to sigma.
 
 * ``NodeWeightNet``   -- learned_kernel.py:23-38
 * ``LearnedKernel``   -- learned_kernel.py:41-115 (multi-band, gated)
@@ -25,7 +27,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from .kde import kde_mmd_loss
+from .kde import kde_mmd_loss, kde_mmd_loss_bands
 
 Tensor = torch.Tensor
 
@@ -85,9 +87,8 @@ class LearnedKernel(nn.Module):
         target = self._scale_points(target_points)
         w_base = self._weights(base)
         w_target = self._weights(target)
-        per_band = torch.stack([
-            kde_mmd_loss(base, target, w_base, w_target, sigma=sigma, center=True)[0]
-            for sigma in torch.exp(self.log_sigmas)])
+        per_band = kde_mmd_loss_bands(base, target, w_base, w_target,
+                                      sigmas=torch.exp(self.log_sigmas), center=True)[0]
         with torch.no_grad():
             dist = _full_cdist(base, target)
             stats = torch.stack([
