@@ -21,6 +21,7 @@
 #include "ra_plan.cuh"
 #include "ra_prep.cuh"
 #include "ra_tc.cuh"
+#include "ra_tcws.cuh"
 #include "ra_tiles3.cuh"
 #include "ra_tilesg.cuh"
 
@@ -226,8 +227,23 @@ void launch_tilesg_dp(int mode, int64_t grid, const TilesGArgs &T, cudaStream_t 
 }
 
 // Tensor-core path: a persistent grid, as many CTAs per SM as TMEM allows.
+// Padded widths 64 and 128 (one CTA per SM) take the warp-specialised kernel.
 template <int DP, int MODE>
 int launch_tilestc_dm(int64_t max_items, const TilesGArgs &T, cudaStream_t st) {
+  if constexpr (DP >= 64) {
+    const size_t smem = tc_ws_smem_request(DP);
+    if (cudaFuncSetAttribute(tilestc_ws_kernel<DP, MODE>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return RA_ERR_CUDA;
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int64_t grid = sms > 0 ? sms : 1;
+    if (grid > max_items) grid = max_items;
+    tilestc_ws_kernel<DP, MODE><<<(unsigned)grid, kWsThreads, smem, st>>>(T);
+    return cuda_status(cudaGetLastError());
+  }
   const size_t smem = tc_smem_request(DP);
   static_assert(tc_smem_bytes(DP) <= tc_smem_request(DP), "shared memory request too small");
   if (cudaFuncSetAttribute(tilestc_kernel<DP, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
