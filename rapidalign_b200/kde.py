@@ -27,7 +27,8 @@ from ._core import Spec, kde_sums
 
 Tensor = torch.Tensor
 
-__all__ = ["kde_mmd_loss", "kde_mmd_loss_bands", "kde_mmd_loss_dense", "pyg_kde_mmd_loss"]
+__all__ = ["kde_mmd_loss", "kde_mmd_loss_bands", "kde_mmd_loss_dense", "pyg_kde_mmd_loss",
+           "pyg_batch_kde_mmd_loss"]
 
 
 def _loss_from_k(Kxx: Tensor, Kyy: Tensor, Kxy: Tensor, cosine: bool, eps: float) -> Tensor:
@@ -305,3 +306,34 @@ def pyg_kde_mmd_loss(
     Kxx, Kyy, Kxy = kde_sums(src_pos, tgt_pos, xw, yw, sig_t, spec)
     loss = _loss_from_k(Kxx, Kyy, Kxy, cosine, eps)
     return loss.to(dtype), Kxx.to(dtype), Kyy.to(dtype), Kxy.to(dtype)
+
+
+def pyg_batch_kde_mmd_loss(src, tgt, *, pos: str = "pos", weight: Optional[str] = None,
+                           sigma: float = 0.2, center: bool = True, cosine: bool = False,
+                           eps: float = 1e-8) -> Tuple[Tensor, Tensor, Tensor, Tensor]:
+    """``pyg_kde_mmd_loss`` on two PyG-style batch objects.
+
+    Takes the point tensors from attribute ``pos`` and optional node weights
+    from attribute ``weight`` of ``src`` and ``tgt`` (a
+    ``torch_geometric.data.Batch`` or anything with the same attributes).
+    The segments come from the batches' ``ptr`` when they carry one -- the
+    offsets PyG keeps for every batch, whose checks run on the device with
+    no host synchronisation -- else from their sorted ``batch`` vectors
+    (kde.py:124-156, one synchronisation for the graph count).
+    """
+    def field(obj, name):
+        if name is None:
+            return None
+        val = getattr(obj, name, None)
+        if val is None:
+            raise ValueError(f"batch has no attribute '{name}'")
+        return val
+
+    src_pos, tgt_pos = field(src, pos), field(tgt, pos)
+    kw = dict(src_w=field(src, weight), tgt_w=field(tgt, weight), sigma=sigma, center=center,
+              cosine=cosine, eps=eps)
+    s_ptr, t_ptr = getattr(src, "ptr", None), getattr(tgt, "ptr", None)
+    if s_ptr is not None and t_ptr is not None:
+        return pyg_kde_mmd_loss(src_pos, tgt_pos, src_ptr=s_ptr, tgt_ptr=t_ptr, **kw)
+    return pyg_kde_mmd_loss(src_pos, tgt_pos, src_batch=field(src, "batch"),
+                            tgt_batch=field(tgt, "batch"), **kw)

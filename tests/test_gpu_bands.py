@@ -96,3 +96,31 @@ def test_per_pair_sigma_checked_on_device(cuda_device):
                 sigma_pairs=torch.tensor([0.5, -1.0], dtype=torch.float64, device=dev))
     with pytest.raises(ValueError, match="sigma must be positive"):
         forward_sums(x, x, None, None, None, spec, False)
+
+
+def test_pyg_batch_adapter(cuda_device):
+    """pyg_batch_kde_mmd_loss on batch-like objects: with ptr (no host sync)
+    and with batch vectors only, equal to pyg_kde_mmd_loss."""
+    from types import SimpleNamespace
+    import rapidalign_b200 as ra
+    from test_gpu_parity import _ragged
+    rng = np.random.default_rng(71)
+    x, y, ptr_x, ptr_y = _ragged(rng, [40, 7, 90], [35, 9, 88], 3)
+    dev = cuda_device
+    bx = np.repeat(np.arange(3), np.diff(ptr_x))
+    by = np.repeat(np.arange(3), np.diff(ptr_y))
+    wx = rng.uniform(0.2, 1.0, x.shape[0]).astype(np.float32)
+    wy = rng.uniform(0.2, 1.0, y.shape[0]).astype(np.float32)
+    src = SimpleNamespace(pos=_cuda(x, dev), batch=_cuda(bx, dev), ptr=_cuda(ptr_x, dev),
+                          w=_cuda(wx, dev))
+    tgt = SimpleNamespace(pos=_cuda(y, dev), batch=_cuda(by, dev), ptr=_cuda(ptr_y, dev),
+                          w=_cuda(wy, dev))
+    ref = ra.pyg_kde_mmd_loss(src.pos, tgt.pos, src_ptr=src.ptr, tgt_ptr=tgt.ptr, src_w=src.w,
+                              tgt_w=tgt.w, sigma=0.3)
+    a = ra.pyg_batch_kde_mmd_loss(src, tgt, weight="w", sigma=0.3)
+    del src.ptr, tgt.ptr
+    b = ra.pyg_batch_kde_mmd_loss(src, tgt, weight="w", sigma=0.3)
+    for r, u, v in zip(ref, a, b):
+        assert torch.equal(r, u) and torch.equal(r, v)
+    with pytest.raises(ValueError, match="no attribute 'feat'"):
+        ra.pyg_batch_kde_mmd_loss(src, tgt, weight="feat")
