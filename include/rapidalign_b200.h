@@ -302,6 +302,39 @@ RA_API int ra_kde_exact_matrices_f64(const double *a, int64_t n, const double *b
                                      int32_t D, double sigma, double *G, double *diff,
                                      ra_stream_t stream);
 
+/* ---- pairwise-distance spectrum loss ------------------------------------ */
+/* Replaces the per-graph loop of rapidalign/algorithms.py:54-90
+ * (pairwise_distance_loss): per group g, the sorted distances of all point
+ * pairs of the source group and of the target group, the shorter list padded
+ * with zeros at its end, loss[g] = mean of the squared differences over the
+ * longer length (NaN when both groups have < 2 points).
+ *
+ * A cloud: points [N, D] (float32), optional perm [N] (the point at grouped
+ * position k is perm[k]; NULL = identity), ptr [G + 1] (grouped positions of
+ * each group), pair_offsets [G + 1] (exclusive scan of n_g (n_g - 1) / 2),
+ * all device arrays; num_pairs = pair_offsets[G] and max_group = the largest
+ * n_g, both known to the host (at most 65536 points per group and
+ * 2^31 - 1 pairs per cloud).  The backward reads the sorted distances the
+ * forward left in the workspace. */
+typedef struct ra_pdl_cloud {
+  const float *points;
+  const int64_t *perm;
+  const int64_t *ptr;
+  const int64_t *pair_offsets;
+  int64_t num_pairs;
+  int64_t max_group;
+} ra_pdl_cloud;
+
+RA_API size_t ra_pdl_workspace_bytes(int64_t G, int64_t pairs_src, int64_t pairs_tgt);
+RA_API int ra_pdl_forward(const ra_pdl_cloud *src, const ra_pdl_cloud *tgt, int64_t G,
+                          int32_t D, double *loss, void *workspace, size_t workspace_bytes,
+                          ra_stream_t stream);
+/* Adds d(sum_g grad_loss[g] loss[g]) / d points into grad_src / grad_tgt
+ * (float32 [N, D], caller-zeroed; either may be NULL). */
+RA_API int ra_pdl_backward(const ra_pdl_cloud *src, const ra_pdl_cloud *tgt, int64_t G,
+                           int32_t D, const double *grad_loss, float *grad_src, float *grad_tgt,
+                           void *workspace, size_t workspace_bytes, ra_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

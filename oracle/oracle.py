@@ -432,3 +432,90 @@ def segmented_kde_loss(x, y, w_x, w_y, ptr_x, ptr_y, sigma, grad_loss=None):
     gx, gy, gwx, gwy, gsig = legacy_backward_segmented(x, y, w_x, w_y, ptr_x, ptr_y,
                                                        grad_loss, sigma)
     return loss, (gx, gy, gwx, gwy, float(np.sum(gsig)))
+
+
+# ---------------------------------------------------------------------------
+# pairwise-distance spectrum loss (rapidalign/algorithms.py:19-90)
+# ---------------------------------------------------------------------------
+
+def _groups(points: np.ndarray, batch) -> list:
+    """algorithms.py:19-34: the point sets of the sorted unique batch ids (the
+    points of one id keep their order)."""
+    if batch is None:
+        return [np.arange(points.shape[0])]
+    batch = np.asarray(batch).reshape(-1)
+    return [np.nonzero(batch == g)[0] for g in np.unique(batch)]
+
+
+def _triu_dists(p: np.ndarray):
+    """algorithms.py:37-44: distances of all pairs i < j (row-major upper
+    triangle), with the pair indices, before sorting."""
+    n = p.shape[0]
+    if n < 2:
+        return np.zeros(0), np.zeros(0, dtype=np.int64), np.zeros(0, dtype=np.int64)
+    i, j = np.triu_indices(n, k=1)
+    d = np.sqrt(((p[i] - p[j]) ** 2).sum(axis=1))
+    return d, i, j
+
+
+def pairwise_distance_loss(src, tgt, src_batch=None, tgt_batch=None, reduction="mean",
+                           upstream=None):
+    """algorithms.py:54-90 in float64: per group, the sorted pair distances of
+    src and tgt, the shorter padded with zeros at the end, their mean squared
+    difference; then the reduction.  With ``upstream`` (dL/d of the returned
+    value, shape of the result) also returns (grad_src, grad_tgt): the sort
+    passes each position's gradient to its pair, the norm's gradient at a
+    zero distance is 0 (as torch.linalg.norm's)."""
+    src = _f64(src)
+    tgt = _f64(tgt)
+    gs, gt = _groups(src, src_batch), _groups(tgt, tgt_batch)
+    if len(gs) != len(gt):
+        raise ValueError("src and tgt batch counts must match")
+    losses = []
+    parts = []
+    for a, b in zip(gs, gt):
+        ds, si, sj = _triu_dists(src[a])
+        dt, ti, tj = _triu_dists(tgt[b])
+        os_, ot = np.argsort(ds, kind="stable"), np.argsort(dt, kind="stable")
+        L = max(ds.size, dt.size)
+        sv = np.zeros(L)
+        tv = np.zeros(L)
+        sv[:ds.size] = ds[os_]
+        tv[:dt.size] = dt[ot]
+        losses.append(np.mean((sv - tv) ** 2) if L else np.nan)
+        parts.append((a, b, ds, si, sj, os_, dt, ti, tj, ot, sv, tv, L))
+    losses = np.array(losses)
+    if reduction == "mean":
+        out = losses.mean()
+    elif reduction == "sum":
+        out = losses.sum()
+    elif reduction == "none":
+        out = losses
+    else:
+        raise ValueError(f"Unsupported reduction: {reduction}")
+    if upstream is None:
+        return out
+    up = np.broadcast_to(np.asarray(upstream, dtype=np.float64), losses.shape) \
+        if reduction == "none" else np.full(losses.shape, float(upstream))
+    if reduction == "mean":
+        up = up / len(losses)
+    grad_src = np.zeros_like(src)
+    grad_tgt = np.zeros_like(tgt)
+    for g, (a, b, ds, si, sj, os_, dt, ti, tj, ot, sv, tv, L) in enumerate(parts):
+        if L == 0:
+            continue
+        gpos = 2.0 * (sv - tv) / L * up[g]  # d loss / d sv (and minus for tv)
+        for pts, grad, d, pi, pj, order, sign, cnt in (
+                (src[a], grad_src, ds, si, sj, os_, 1.0, ds.size),
+                (tgt[b], grad_tgt, dt, ti, tj, ot, -1.0, dt.size)):
+            if cnt == 0:
+                continue
+            gd = np.zeros(cnt)
+            gd[order] = sign * gpos[:cnt]
+            with np.errstate(invalid="ignore", divide="ignore"):
+                coef = np.where(d > 0, gd / d, 0.0)
+            vec = coef[:, None] * (pts[pi] - pts[pj])
+            idx = a if sign > 0 else b
+            np.add.at(grad, idx[pi], vec)
+            np.add.at(grad, idx[pj], -vec)
+    return out, grad_src, grad_tgt

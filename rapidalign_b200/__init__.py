@@ -3,6 +3,7 @@
 differentiable segmented_kde_loss)."""
 from .kde import (kde_mmd_loss, kde_mmd_loss_bands, kde_mmd_loss_dense, pyg_batch_kde_mmd_loss,
                   pyg_kde_mmd_loss)
+from .algorithms import pairwise_distance_loss
 from .autograd_kde import SegmentedKDELossFunction, segmented_kde_loss
 
 __all__ = [
@@ -12,5 +13,6 @@ __all__ = [
     "pyg_kde_mmd_loss",
     "pyg_batch_kde_mmd_loss",
     "segmented_kde_loss",
+    "pairwise_distance_loss",
     "SegmentedKDELossFunction",
 ]

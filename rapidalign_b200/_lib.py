@@ -66,6 +66,17 @@ class RaKdeDesc(ctypes.Structure):
     ]
 
 
+class RaPdlCloud(ctypes.Structure):
+    _fields_ = [
+        ("points", ctypes.c_void_p),
+        ("perm", ctypes.c_void_p),
+        ("ptr", ctypes.c_void_p),
+        ("pair_offsets", ctypes.c_void_p),
+        ("num_pairs", ctypes.c_int64),
+        ("max_group", ctypes.c_int64),
+    ]
+
+
 class RaKdeInputs(ctypes.Structure):
     _fields_ = [
         ("x", ctypes.c_void_p),
@@ -127,6 +138,11 @@ SIGNATURES = {
     "ra_kde_exact_f64": (ctypes.c_int, [_V, _V, _V, _V, _V, _V, _I64, _I64, _I64, _I32, _D,
                                         _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _SZ, _V]),
     "ra_kde_exact_matrices_f64": (ctypes.c_int, [_V, _I64, _V, _I64, _I32, _D, _V, _V, _V]),
+    "ra_pdl_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "ra_pdl_forward": (ctypes.c_int, [ctypes.POINTER(RaPdlCloud), ctypes.POINTER(RaPdlCloud),
+                                      _I64, _I32, _V, _V, _SZ, _V]),
+    "ra_pdl_backward": (ctypes.c_int, [ctypes.POINTER(RaPdlCloud), ctypes.POINTER(RaPdlCloud),
+                                       _I64, _I32, _V, _V, _V, _V, _SZ, _V]),
     "ra_kernel_launch_count": (ctypes.c_ulonglong, []),
     "ra_probe_fp32_peak": (ctypes.c_int, [_V, _I64, ctypes.c_int, ctypes.POINTER(_D), _V]),
 }

@@ -18,6 +18,7 @@
 #include "ra_common.cuh"
 #include "ra_epilogue.cuh"
 #include "ra_exact.cuh"
+#include "ra_pdl.cuh"
 #include "ra_plan.cuh"
 #include "ra_prep.cuh"
 #include "ra_tc.cuh"
@@ -1026,6 +1027,129 @@ int ra_kde_exact_matrices_f64(const double *a, int64_t n, const double *b, int64
   exact_matrices_kernel<<<(unsigned)ceil_div(n * m, (int64_t)256), 256, 0,
                           (cudaStream_t)stream>>>(a, n, b, m, D, sigma, G, diff);
   ++g_launches;
+  return cuda_status(cudaGetLastError());
+}
+
+// ---- pairwise-distance spectrum loss (ra_pdl.cuh) ---------------------------
+
+namespace {
+struct PdlLayout {
+  size_t temp, keys_in[2], keys_out[2], vals_in[2], vals_out[2], total;
+};
+bool pdl_layout(int64_t G, int64_t Ps, int64_t Pt, PdlLayout &L) {
+  if (G < 0 || Ps < 0 || Pt < 0 || Ps > INT32_MAX || Pt > INT32_MAX || G > INT32_MAX)
+    return false;
+  size_t temp = 0;
+  for (int64_t P : {Ps, Pt}) {
+    size_t t = 0;
+    if (P > 0 && cub::DeviceSegmentedSort::SortPairs(
+                     nullptr, t, (const float *)nullptr, (float *)nullptr,
+                     (const uint32_t *)nullptr, (uint32_t *)nullptr, (int)P, (int)G,
+                     (const int64_t *)nullptr, (const int64_t *)nullptr) != cudaSuccess)
+      return false;
+    temp = t > temp ? t : temp;
+  }
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = a256(o + bytes);
+    return at;
+  };
+  L.temp = take(temp > 0 ? temp : 1);
+  const int64_t P[2] = {Ps, Pt};
+  for (int s = 0; s < 2; ++s) {
+    L.keys_in[s] = take(sizeof(float) * (size_t)(P[s] > 0 ? P[s] : 1));
+    L.keys_out[s] = take(sizeof(float) * (size_t)(P[s] > 0 ? P[s] : 1));
+    L.vals_in[s] = take(sizeof(uint32_t) * (size_t)(P[s] > 0 ? P[s] : 1));
+    L.vals_out[s] = take(sizeof(uint32_t) * (size_t)(P[s] > 0 ? P[s] : 1));
+  }
+  L.total = o;
+  return true;
+}
+PdlSide pdl_side(const ra_pdl_cloud *c, void *ws, const PdlLayout &L, int s, bool sorted) {
+  PdlSide S;
+  S.pts = c->points;
+  S.perm = c->perm;
+  S.ptr = c->ptr;
+  S.poff = c->pair_offsets;
+  S.pairs = c->num_pairs;
+  S.keys = at<float>(ws, sorted ? L.keys_out[s] : L.keys_in[s]);
+  S.vals = at<uint32_t>(ws, sorted ? L.vals_out[s] : L.vals_in[s]);
+  return S;
+}
+bool pdl_ok(const ra_pdl_cloud *c) {
+  return c != nullptr && c->ptr != nullptr && c->pair_offsets != nullptr && c->num_pairs >= 0 &&
+         (c->num_pairs == 0 || c->points != nullptr) && c->max_group <= 65536;
+}
+}  // namespace
+
+size_t ra_pdl_workspace_bytes(int64_t G, int64_t pairs_src, int64_t pairs_tgt) {
+  PdlLayout L;
+  return pdl_layout(G, pairs_src, pairs_tgt, L) ? L.total : 0;
+}
+
+int ra_pdl_forward(const ra_pdl_cloud *src, const ra_pdl_cloud *tgt, int64_t G, int32_t D,
+                   double *loss, void *workspace, size_t workspace_bytes, ra_stream_t stream) {
+  if (G < 0 || D < 1 || !pdl_ok(src) || !pdl_ok(tgt) || (G > 0 && loss == nullptr))
+    return RA_ERR_INVALID_ARGUMENT;
+  PdlLayout L;
+  if (!pdl_layout(G, src->num_pairs, tgt->num_pairs, L)) return RA_ERR_INVALID_ARGUMENT;
+  if (workspace == nullptr || workspace_bytes < L.total ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return RA_ERR_WORKSPACE;
+  if (G == 0) return RA_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const ra_pdl_cloud *cl[2] = {src, tgt};
+  for (int s = 0; s < 2; ++s) {
+    const int64_t P = cl[s]->num_pairs;
+    if (P == 0) continue;
+    PdlSide S = pdl_side(cl[s], workspace, L, s, false);
+    const int64_t blocks = ceil_div(P, (int64_t)256);
+    pdl_dist_kernel<<<(unsigned)(blocks < (int64_t)sms * 16 ? blocks : (int64_t)sms * 16), 256, 0,
+                      st>>>(S, G, D);
+    size_t temp = L.keys_in[0] - L.temp;  // capacity of the sort's temp region
+    if (cub::DeviceSegmentedSort::SortPairs(
+            at<void>(workspace, L.temp), temp, at<const float>(workspace, L.keys_in[s]),
+            at<float>(workspace, L.keys_out[s]), at<const uint32_t>(workspace, L.vals_in[s]),
+            at<uint32_t>(workspace, L.vals_out[s]), (int)P, (int)G, cl[s]->pair_offsets,
+            cl[s]->pair_offsets + 1, st) != cudaSuccess)
+      return RA_ERR_CUDA;
+    g_launches += 2;
+  }
+  pdl_loss_kernel<<<(unsigned)G, 256, 0, st>>>(pdl_side(src, workspace, L, 0, true),
+                                               pdl_side(tgt, workspace, L, 1, true), G, loss);
+  ++g_launches;
+  return cuda_status(cudaGetLastError());
+}
+
+int ra_pdl_backward(const ra_pdl_cloud *src, const ra_pdl_cloud *tgt, int64_t G, int32_t D,
+                    const double *grad_loss, float *grad_src, float *grad_tgt, void *workspace,
+                    size_t workspace_bytes, ra_stream_t stream) {
+  if (G < 0 || D < 1 || !pdl_ok(src) || !pdl_ok(tgt) || (G > 0 && grad_loss == nullptr))
+    return RA_ERR_INVALID_ARGUMENT;
+  PdlLayout L;
+  if (!pdl_layout(G, src->num_pairs, tgt->num_pairs, L)) return RA_ERR_INVALID_ARGUMENT;
+  if (workspace == nullptr || workspace_bytes < L.total ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return RA_ERR_WORKSPACE;
+  if (G == 0) return RA_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const PdlSide Sx = pdl_side(src, workspace, L, 0, true), Sy = pdl_side(tgt, workspace, L, 1, true);
+  float *grads[2] = {grad_src, grad_tgt};
+  const PdlSide *sides[2] = {&Sx, &Sy};
+  for (int s = 0; s < 2; ++s) {
+    if (grads[s] == nullptr || sides[s]->pairs == 0) continue;
+    const int64_t blocks = ceil_div(sides[s]->pairs, (int64_t)256);
+    pdl_grad_kernel<<<(unsigned)(blocks < (int64_t)sms * 16 ? blocks : (int64_t)sms * 16), 256, 0,
+                      st>>>(*sides[s], *sides[1 - s], G, D, grad_loss, grads[s]);
+    ++g_launches;
+  }
   return cuda_status(cudaGetLastError());
 }
 

@@ -242,6 +242,35 @@ def _ensure_ptr(ptr: Optional[Tensor], batch: Optional[Tensor], total_nodes: int
     return ptr, num_graphs, False
 
 
+def _ensure_ptrs(src_ptr: Optional[Tensor], src_batch: Optional[Tensor], n_src: int,
+                 tgt_ptr: Optional[Tensor], tgt_batch: Optional[Tensor], n_tgt: int,
+                 device) -> Tuple[Tensor, int, bool, Tensor, int, bool]:
+    """_ensure_ptr for both sides with a single host synchronisation when
+    both come as batch vectors (the checks and graph counts of the two sides
+    are read back together); same results and errors, source side first."""
+    if src_ptr is not None or tgt_ptr is not None or src_batch is None or tgt_batch is None:
+        return (*_ensure_ptr(src_ptr, src_batch, n_src, device),
+                *_ensure_ptr(tgt_ptr, tgt_batch, n_tgt, device))
+    sb = src_batch.to(device=device, dtype=torch.long).contiguous()
+    tb = tgt_batch.to(device=device, dtype=torch.long).contiguous()
+    if sb.numel() != n_src or tb.numel() != n_tgt:
+        raise ValueError("batch length must match number of nodes")
+    if sb.numel() < 2 or tb.numel() < 2:
+        return (*_ensure_ptr(None, sb, n_src, device), *_ensure_ptr(None, tb, n_tgt, device))
+    info = torch.stack([(sb[:-1] > sb[1:]).any().to(torch.long), sb[-1], sb[0],
+                        (tb[:-1] > tb[1:]).any().to(torch.long), tb[-1], tb[0]]).tolist()
+    out = []
+    for b, (unsorted, last, first) in ((sb, info[:3]), (tb, info[3:])):
+        if unsorted:
+            raise ValueError("batch indices must be sorted for contiguous blocks")
+        if first < 0:
+            raise ValueError("batch indices must be non-negative")
+        num_graphs = int(last) + 1
+        bounds = torch.arange(num_graphs + 1, device=device, dtype=torch.long)
+        out += [torch.searchsorted(b, bounds, right=False).contiguous(), num_graphs, False]
+    return tuple(out)
+
+
 def pyg_kde_mmd_loss(
     src_pos: Tensor,
     tgt_pos: Tensor,
@@ -274,8 +303,8 @@ def pyg_kde_mmd_loss(
     dtype = src_pos.dtype
     _lib.require_cuda(src_pos, tgt_pos)
 
-    src_ptr_t, num_src, user_x = _ensure_ptr(src_ptr, src_batch, src_pos.size(0), device)
-    tgt_ptr_t, num_tgt, user_y = _ensure_ptr(tgt_ptr, tgt_batch, tgt_pos.size(0), device)
+    src_ptr_t, num_src, user_x, tgt_ptr_t, num_tgt, user_y = _ensure_ptrs(
+        src_ptr, src_batch, src_pos.size(0), tgt_ptr, tgt_batch, tgt_pos.size(0), device)
     if num_src != num_tgt:
         raise ValueError("source and target batches must have the same length")
 

@@ -206,6 +206,32 @@ def case_gradients(name, n, m, d, sigma, seed):
          grad_wy=out["w_y"].numpy(), grad_sigma=out["sigma"].numpy())
 
 
+def case_pairwise(name, sizes_src, sizes_tgt, d, reduction, shuffle, seed, no_batch=False):
+    """algorithms.py:54-90 (float64, autograd through sort and norm); batch ids
+    may be unsorted (the reference groups by value, not by position)."""
+    from rapidalign.algorithms import pairwise_distance_loss
+    g = torch.Generator().manual_seed(seed)
+    src = f32(torch.randn(sum(sizes_src), d, generator=g)).requires_grad_(True)
+    tgt = f32(1.05 * torch.randn(sum(sizes_tgt), d, generator=g)).requires_grad_(True)
+    bs = torch.repeat_interleave(torch.arange(len(sizes_src)), torch.tensor(sizes_src))
+    bt = torch.repeat_interleave(torch.arange(len(sizes_tgt)), torch.tensor(sizes_tgt))
+    if shuffle:
+        bs = bs[torch.randperm(bs.numel(), generator=g)]
+        bt = bt[torch.randperm(bt.numel(), generator=g)]
+    if no_batch:
+        out = pairwise_distance_loss(src, tgt, reduction=reduction)
+    else:
+        out = pairwise_distance_loss(src, tgt, bs, bt, reduction=reduction)
+    up = torch.linspace(0.5, 1.5, out.numel(), dtype=torch.float64).reshape(out.shape)
+    (out * up).sum().backward()
+    arrays = dict(src=src.detach().numpy(), tgt=tgt.detach().numpy(), out=out.detach().numpy(),
+                  upstream=up.numpy(), grad_src=src.grad.numpy(), grad_tgt=tgt.grad.numpy(),
+                  reduction=np.array(reduction))
+    if not no_batch:
+        arrays.update(src_batch=bs.numpy(), tgt_batch=bt.numpy())
+    save(name, **arrays)
+
+
 def case_learned(name, kind, n, m, seed):
     """learned_kernel.py modules (float64; the gate's float32 cast is undone by
     a forward pre-hook so that the whole module runs in float64)."""
@@ -271,6 +297,11 @@ def main():
     # the float64 verification helpers (kde_gradients.py:39-132), one pair
     case_gradients("gradients_d3", 23, 17, 3, 0.4, 40)
     case_gradients("gradients_d16", 12, 9, 16, 1.3, 41)
+    # the pairwise-distance spectrum loss (algorithms.py:54-90)
+    case_pairwise("pairwise_mean", [12, 1, 30, 7], [10, 3, 33, 7], 3, "mean", False, 50)
+    case_pairwise("pairwise_none_shuffled", [9, 20, 2], [11, 18, 5], 3, "none", True, 51)
+    case_pairwise("pairwise_sum_d2", [25, 6], [20, 6], 2, "sum", False, 52)
+    case_pairwise("pairwise_single", [40], [37], 3, "mean", False, 53, no_batch=True)
     # learned-kernel callers (learned_kernel.py:41-202)
     case_learned("learned_multi", "multi", 60, 45, 30)
     case_learned("learned_single", "single", 50, 64, 31)

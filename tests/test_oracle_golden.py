@@ -20,7 +20,18 @@ def rel(a, b):
 # the loss fixtures (the learned-kernel module fixtures are checked in
 # test_learned_kernel.py, the single-pair helper fixtures below)
 LOSS_CASES = [n for n in golden_cases()
-              if not n.startswith("learned") and not n.startswith("gradients")]
+              if not n.startswith(("learned", "gradients", "pairwise"))]
+
+
+@pytest.mark.parametrize("name", golden_cases("pairwise"))
+def test_oracle_matches_pairwise_distance_loss(name):
+    """algorithms.py:54-90: value and gradients (through sort and norm)."""
+    z = load_golden(name)
+    out, gs, gt = O.pairwise_distance_loss(z["src"], z["tgt"], z.get("src_batch"),
+                                           z.get("tgt_batch"), str(z["reduction"]),
+                                           upstream=z["upstream"])
+    assert rel(out, z["out"]) < TOL
+    assert rel(gs, z["grad_src"]) < TOL and rel(gt, z["grad_tgt"]) < TOL
 
 
 @pytest.mark.parametrize("name", golden_cases("gradients"))
