@@ -76,6 +76,12 @@ __device__ __forceinline__ bool ws_wait(uint32_t mbar, uint32_t parity,
   }
   return false;
 }
+// a[u] for a runtime u in 0..3 by selects (no local-memory array)
+__device__ __forceinline__ uint32_t sel4(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         int u) {
+  const uint32_t lo = (u & 1) ? a1 : a0, hi = (u & 1) ? a3 : a2;
+  return (u & 2) ? hi : lo;
+}
 // Named barrier among the threads of one role (ids 1 and 2; 0 is
 // __syncthreads).
 __device__ __forceinline__ void role_sync(int id, int nthreads) {
@@ -399,10 +405,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
           for (int s4 = 0; s4 < 4; ++s4) {
             const int u = (s4 + rot) & 3;
             const int jo = c * (kTcCols * 16) + (4 * q + u) * 16;
-            *reinterpret_cast<uint4 *>(yhi + jo) =
-                make_uint4(hh[u][0], hh[u][1], hh[u][2], hh[u][3]);
-            *reinterpret_cast<uint4 *>(ylo + jo) =
-                make_uint4(ll[u][0], ll[u][1], ll[u][2], ll[u][3]);
+            uint32_t H[4], Lw[4];
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              H[v] = sel4(hh[0][v], hh[1][v], hh[2][v], hh[3][v], u);
+              Lw[v] = sel4(ll[0][v], ll[1][v], ll[2][v], ll[3][v], u);
+            }
+            *reinterpret_cast<uint4 *>(yhi + jo) = make_uint4(H[0], H[1], H[2], H[3]);
+            *reinterpret_cast<uint4 *>(ylo + jo) = make_uint4(Lw[0], Lw[1], Lw[2], Lw[3]);
           }
         }
 #pragma unroll
@@ -454,10 +464,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
               const int u = (s4 + rot) & 3;
               const int d = 4 * c + u;
               const int to = (d >> 3) * (NQ * 128) + q * 128 + (d & 7) * 16;
-              *reinterpret_cast<uint4 *>(yth + to) =
-                  make_uint4(hh[0][u], hh[1][u], hh[2][u], hh[3][u]);
-              *reinterpret_cast<uint4 *>(ytl + to) =
-                  make_uint4(ll[0][u], ll[1][u], ll[2][u], ll[3][u]);
+              uint32_t H[4], Lw[4];
+#pragma unroll
+              for (int p = 0; p < 4; ++p) {
+                H[p] = sel4(hh[p][0], hh[p][1], hh[p][2], hh[p][3], u);
+                Lw[p] = sel4(ll[p][0], ll[p][1], ll[p][2], ll[p][3], u);
+              }
+              *reinterpret_cast<uint4 *>(yth + to) = make_uint4(H[0], H[1], H[2], H[3]);
+              *reinterpret_cast<uint4 *>(ytl + to) = make_uint4(Lw[0], Lw[1], Lw[2], Lw[3]);
             }
           }
           fence_async_smem();
