@@ -378,9 +378,10 @@ __device__ __forceinline__ double warp_max(double v) {
   return v;
 }
 
-// Pass 2: one warp per pair combines its chunk records (lane-strided over the
-// chunks, then a fixed shuffle tree) into the segment bounds, normalisers,
-// centroids and anchors.
+// Pass 2: one warp per pair combines its chunk records into the segment
+// bounds and normalisers (lane-strided over the chunks, then a fixed shuffle
+// tree) and the centroids and anchors (one lane per coordinate, the chunks in
+// order).
 __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
   const int64_t p = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -446,15 +447,15 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
       else A.seg[p].ycount = count;
     }
     if (side == 0) count_x = count;
-    for (int dd = 0; dd < DP; ++dd) {
+    // one lane per coordinate, the chunks summed in order (fixed order:
+    // deterministic); each lane also finishes its own coordinates below
+    for (int dd = lane; dd < DP; dd += 32) {
       double cs = 0.0, ps = 0.0;
-      for (int64_t c = lane; c < n; c += 32) {
+      for (int64_t c = 0; c < n; ++c) {
         cs += r0[c * rs + 3 + dd];
         ps += r0[c * rs + 3 + DP + dd];
       }
-      cs = warp_sum(cs);
-      ps = warp_sum(ps);
-      if (lane == 0) {
+      {
         // centroid mu = sum_i a_i p_i = sum_i w'_i p_i / Wn; plain mean for the anchor
         const double mu = dd < D ? cs / Wn : 0.0;
         const double mean = (dd < D && nv > 0) ? ps / nv : 0.0;
