@@ -419,7 +419,9 @@ class DenseWorkload:
         return loss
 
     def tiles_time(self, reps):
-        return None
+        from rapidalign_b200 import profiling
+        return profiling.tiles_time_dense(self.d["x"], self.d["y"], self.d["mx"], self.d["my"],
+                                          self.sigma, reps=reps, center=True)
 
 
 class EmbedWorkload(RaggedWorkload):
