@@ -181,6 +181,12 @@ struct BoolC {
   static constexpr bool value = V;
 };
 
+// a[u] for a runtime u in 0..3 by selects (no local-memory array)
+__device__ __forceinline__ uint32_t sel4(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         int u) {
+  const uint32_t lo = (u & 1) ? a1 : a0, hi = (u & 1) ? a3 : a2;
+  return (u & 2) ? hi : lo;
+}
 // ---- the kernel -------------------------------------------------------------
 template <int DP, int MODE>
 __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
@@ -333,12 +339,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
         for (int s4 = 0; s4 < 4; ++s4) {
           const int u = (s4 + rot) & 3;  // point (row layout) / coordinate (transposed)
           const int jo = c * (kTcCols * 16) + (4 * q + u) * 16;
-          *reinterpret_cast<uint4 *>(yhi + jo) = make_uint4(hh[u][0], hh[u][1], hh[u][2], hh[u][3]);
-          *reinterpret_cast<uint4 *>(ylo + jo) = make_uint4(ll[u][0], ll[u][1], ll[u][2], ll[u][3]);
+          uint32_t H[4], Lw[4], Ht[4], Lt[4];
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            H[v] = sel4(hh[0][v], hh[1][v], hh[2][v], hh[3][v], u);
+            Lw[v] = sel4(ll[0][v], ll[1][v], ll[2][v], ll[3][v], u);
+            Ht[v] = sel4(hh[v][0], hh[v][1], hh[v][2], hh[v][3], u);
+            Lt[v] = sel4(ll[v][0], ll[v][1], ll[v][2], ll[v][3], u);
+          }
+          *reinterpret_cast<uint4 *>(yhi + jo) = make_uint4(H[0], H[1], H[2], H[3]);
+          *reinterpret_cast<uint4 *>(ylo + jo) = make_uint4(Lw[0], Lw[1], Lw[2], Lw[3]);
           const int d = 4 * c + u;
           const int to = (d >> 3) * (NQ * 128) + q * 128 + (d & 7) * 16;
-          *reinterpret_cast<uint4 *>(yth + to) = make_uint4(hh[0][u], hh[1][u], hh[2][u], hh[3][u]);
-          *reinterpret_cast<uint4 *>(ytl + to) = make_uint4(ll[0][u], ll[1][u], ll[2][u], ll[3][u]);
+          *reinterpret_cast<uint4 *>(yth + to) = make_uint4(Ht[0], Ht[1], Ht[2], Ht[3]);
+          *reinterpret_cast<uint4 *>(ytl + to) = make_uint4(Lt[0], Lt[1], Lt[2], Lt[3]);
         }
       }
 #pragma unroll

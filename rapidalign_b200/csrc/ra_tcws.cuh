@@ -76,12 +76,6 @@ __device__ __forceinline__ bool ws_wait(uint32_t mbar, uint32_t parity,
   }
   return false;
 }
-// a[u] for a runtime u in 0..3 by selects (no local-memory array)
-__device__ __forceinline__ uint32_t sel4(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         int u) {
-  const uint32_t lo = (u & 1) ? a1 : a0, hi = (u & 1) ? a3 : a2;
-  return (u & 2) ? hi : lo;
-}
 // Named barrier among the threads of one role (ids 1 and 2; 0 is
 // __syncthreads).
 __device__ __forceinline__ void role_sync(int id, int nthreads) {
