@@ -115,17 +115,21 @@ __device__ __forceinline__ void point_grads(const EpilogueArgs &A, int side, int
                                             double cs, double cc, double k_x, double m_own,
                                             double m_par, double *gxt, double &ga,
                                             double &a_out) {
+  static_assert(kAcc3Stride == 8 && kAcc3Block == 4, "record = two float4 blocks");
   const int D = A.D;
-  const float *acc = (side == 0 ? A.accX : A.accY) + slot * A.acc_stride;
+  // the record (32-byte aligned): self (s, G0..G2), cross (s, G0..G2)
+  const float4 *rec = reinterpret_cast<const float4 *>((side == 0 ? A.accX : A.accY) +
+                                                       slot * kAcc3Stride);
+  const float4 self4 = rec[0], cross4 = rec[1];
+  const float gs[3] = {self4.y, self4.z, self4.w}, gc[3] = {cross4.y, cross4.z, cross4.w};
   const double a = (double)(side == 0 ? A.aw_x : A.aw_y)[slot] * m_own;
-  const int cross = kAcc3Block;
   const double ws = cs * m_own, wc = cc * m_par;
 #pragma unroll
   for (int d = 0; d < MAXD; ++d) {
     // difference form: G = sum w k (x' - y') accumulated directly
-    gxt[d] = d < D ? -a * k_x * (ws * acc[1 + d] + wc * acc[cross + 1 + d]) : 0.0;
+    gxt[d] = d < D ? -a * k_x * (ws * gs[d] + wc * gc[d]) : 0.0;
   }
-  ga = ws * acc[0] + wc * acc[cross];
+  ga = ws * self4.x + wc * cross4.x;
   a_out = a;
 }
 
