@@ -28,7 +28,7 @@ from ._core import Spec, kde_sums
 Tensor = torch.Tensor
 
 __all__ = ["kde_mmd_loss", "kde_mmd_loss_bands", "kde_mmd_loss_dense", "pyg_kde_mmd_loss",
-           "pyg_batch_kde_mmd_loss"]
+           "pyg_batch_kde_mmd_loss", "batch_ptrs"]
 
 
 def _loss_from_k(Kxx: Tensor, Kyy: Tensor, Kxy: Tensor, cosine: bool, eps: float) -> Tensor:
@@ -204,6 +204,18 @@ def kde_mmd_loss_dense(
     return loss.to(dtype), Kxx.to(dtype), Kyy.to(dtype), Kxy.to(dtype)
 
 
+def _read_back(values: Tensor) -> list:
+    """A few device values on the host, waiting only for the current stream
+    (a pinned copy plus an event, where ``tolist()`` would wait for the
+    device's default stream too)."""
+    host = torch.empty(values.shape, dtype=values.dtype, pin_memory=True)
+    host.copy_(values, non_blocking=True)
+    done = torch.cuda.Event()
+    done.record(torch.cuda.current_stream(values.device))
+    done.synchronize()
+    return host.tolist()
+
+
 def _ensure_ptr(ptr: Optional[Tensor], batch: Optional[Tensor], total_nodes: int,
                 device) -> Tuple[Tensor, int, bool]:
     """kde.py:124-156.  Returns (ptr, num_graphs, user_given).  The value
@@ -228,7 +240,7 @@ def _ensure_ptr(ptr: Optional[Tensor], batch: Optional[Tensor], total_nodes: int
     # one synchronisation for both the order check and the graph count
     if batch.numel() > 1:
         unsorted = (batch[:-1] > batch[1:]).any()
-        info = torch.stack([unsorted.to(torch.long), batch[-1], batch[0]]).tolist()
+        info = _read_back(torch.stack([unsorted.to(torch.long), batch[-1], batch[0]]))
     else:
         info = [0, int(batch[0].item()), int(batch[0].item())]
     if info[0]:
@@ -257,8 +269,8 @@ def _ensure_ptrs(src_ptr: Optional[Tensor], src_batch: Optional[Tensor], n_src: 
         raise ValueError("batch length must match number of nodes")
     if sb.numel() < 2 or tb.numel() < 2:
         return (*_ensure_ptr(None, sb, n_src, device), *_ensure_ptr(None, tb, n_tgt, device))
-    info = torch.stack([(sb[:-1] > sb[1:]).any().to(torch.long), sb[-1], sb[0],
-                        (tb[:-1] > tb[1:]).any().to(torch.long), tb[-1], tb[0]]).tolist()
+    info = _read_back(torch.stack([(sb[:-1] > sb[1:]).any().to(torch.long), sb[-1], sb[0],
+                                   (tb[:-1] > tb[1:]).any().to(torch.long), tb[-1], tb[0]]))
     out = []
     for b, (unsorted, last, first) in ((sb, info[:3]), (tb, info[3:])):
         if unsorted:
@@ -269,6 +281,15 @@ def _ensure_ptrs(src_ptr: Optional[Tensor], src_batch: Optional[Tensor], n_src: 
         bounds = torch.arange(num_graphs + 1, device=device, dtype=torch.long)
         out += [torch.searchsorted(b, bounds, right=False).contiguous(), num_graphs, False]
     return tuple(out)
+
+
+def batch_ptrs(src_batch: Tensor, tgt_batch: Tensor) -> Tuple[Tensor, Tensor]:
+    """ptr offsets of two sorted batch vectors (kde.py:124-156 semantics and
+    errors), with one host synchronisation for both; on the current stream.
+    ``pyg_kde_mmd_loss(..., src_ptr=, tgt_ptr=)`` then needs none."""
+    ps, _, _, pt, _, _ = _ensure_ptrs(None, src_batch, src_batch.numel(), None, tgt_batch,
+                                      tgt_batch.numel(), src_batch.device)
+    return ps, pt
 
 
 def pyg_kde_mmd_loss(

@@ -14,6 +14,9 @@ stream waits for a batch's copy on the device (an event), never on the host.
             pf.put(next_host_batch)     # starts copying while this step runs
         loss = pyg_kde_mmd_loss(batch["x"], batch["y"], ...)
 
+``get(prepare=...)`` can derive per-batch tensors on the copy stream (for
+example ptr offsets with ``rapidalign_b200.batch_ptrs``).
+
 Pinned (page-locked) host tensors copy asynchronously; pageable ones make
 the copy synchronous and gain nothing.  The device buffers are allocated on
 the copy stream and handed to the compute stream with ``record_stream``, so
@@ -21,7 +24,7 @@ the caching allocator does not reuse them while the compute still reads them.
 """
 from __future__ import annotations
 
-from typing import Dict, Optional
+from typing import Callable, Dict, Optional
 
 import torch
 
@@ -54,11 +57,23 @@ class DevicePrefetcher:
         self._staged, self._ready = staged, end
         self.copy_start, self.copy_end = start, end
 
-    def get(self) -> Dict[str, Tensor]:
+    def get(self, prepare: Optional[Callable[[Dict[str, Tensor]], Dict[str, Tensor]]] = None
+            ) -> Dict[str, Tensor]:
         """The staged batch, usable on the current stream (which waits for
-        its copy on the device)."""
+        its copy on the device).
+
+        ``prepare(batch)``, if given, runs first on the copy stream and its
+        returned tensors join the batch: per-batch work that needs a host
+        synchronisation, e.g. ptr offsets from batch vectors (``batch_ptrs``),
+        then waits for the copy only -- issued a step earlier, it is done --
+        instead of for the compute stream's queue."""
         if self._staged is None:
             raise RuntimeError("no batch staged: put() one first")
+        if prepare is not None:
+            with torch.cuda.stream(self.copy_stream):
+                self._staged.update(prepare(self._staged))
+                self._ready = torch.cuda.Event()
+                self._ready.record(self.copy_stream)
         cur = torch.cuda.current_stream(self.device)
         cur.wait_event(self._ready)
         for t in self._staged.values():
