@@ -533,22 +533,39 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
       const int ncd = D / 4;  // chunks that hold coordinates
       const int cc = tid % NC;
       const int64_t nel = (e - b) * NC;
-      for (int64_t k0 = tid; k0 < nel; k0 += 4 * 256) {
+      constexpr int kAhead = 2;  // 4 doubles the registers (126 -> 156) for nothing
+      for (int64_t k0 = tid; k0 < nel; k0 += kAhead * 256) {
+        // the loads of kAhead elements go out before the first store (a
+        // store to gout might alias them as far as the compiler knows)
+        float4 ts[kAhead], tc[kAhead], xp[kAhead];
+        float av[kAhead], ssv[kAhead], scv[kAhead];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kAhead; ++u) {
+          const int64_t k = k0 + u * 256;
+          const int64_t i = b + k / NC;
+          if (k < nel && cc < ncd && i < E.count) {
+            const int64_t g = E.s + i;
+            const float *acc = accb + g * A.acc_stride;
+            av[u] = Ap[g];
+            ssv[u] = acc[2 * DP];
+            scv[u] = acc[2 * DP + 1];
+            ts[u] = *reinterpret_cast<const float4 *>(acc + 4 * cc);
+            tc[u] = *reinterpret_cast<const float4 *>(acc + DP + 4 * cc);
+            xp[u] = *reinterpret_cast<const float4 *>(Gp + g * DP + 4 * cc);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kAhead; ++u) {
           const int64_t k = k0 + u * 256;
           if (k < nel && cc < ncd) {
             const int64_t i = b + k / NC;
             const int64_t g = E.s + i;
             float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
             if (i < E.count) {
-              const float *acc = accb + g * A.acc_stride;
-              const double a = Ap[g], s_self = acc[2 * DP], s_cross = acc[2 * DP + 1];
-              const float4 ts = *reinterpret_cast<const float4 *>(acc + 4 * cc);
-              const float4 tc = *reinterpret_cast<const float4 *>(acc + DP + 4 * cc);
-              const float4 xp = *reinterpret_cast<const float4 *>(Gp + g * DP + 4 * cc);
-              const float tsv[4] = {ts.x, ts.y, ts.z, ts.w}, tcv[4] = {tc.x, tc.y, tc.z, tc.w};
-              const float xv[4] = {xp.x, xp.y, xp.z, xp.w};
+              const double a = av[u], s_self = ssv[u], s_cross = scv[u];
+              const float tsv[4] = {ts[u].x, ts[u].y, ts[u].z, ts[u].w};
+              const float tcv[4] = {tc[u].x, tc[u].y, tc[u].z, tc[u].w};
+              const float xv[4] = {xp[u].x, xp[u].y, xp[u].z, xp[u].w};
               float r[4];
 #pragma unroll
               for (int v = 0; v < 4; ++v) {

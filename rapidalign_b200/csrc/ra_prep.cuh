@@ -524,7 +524,7 @@ __global__ void __launch_bounds__(NT) packg_kernel(PrepArgs A) {
 // DP / 4 dividing 256, a thread always handles the same c, so its four
 // anchors are loaded once per pair side.
 template <int DP>
-__global__ void __launch_bounds__(256) packgw_kernel(PrepArgs A) {
+__global__ void __launch_bounds__(256, 4) packgw_kernel(PrepArgs A) {
   constexpr int NC = DP / 4;  // float4 chunks per packed point
   static_assert(256 % NC == 0, "a thread keeps one chunk");
   const ChunkMap M{A.P, A.choff, A.chx};
@@ -550,22 +550,31 @@ __global__ void __launch_bounds__(256) packgw_kernel(PrepArgs A) {
     const int64_t b = ch * kChunk, e = b + kChunk < count ? b + kChunk : count;
     const int64_t nel = (e - b) * NC;
     for (int64_t k0 = threadIdx.x; k0 < nel; k0 += 4 * 256) {
+      // the 4 loads go out before the first store (a store to Gp might
+      // alias pts as far as the compiler knows, which would serialise them)
+      float4 xv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t k = k0 + u * 256;
+        xv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (k < nel && live)
+          xv[u] = *reinterpret_cast<const float4 *>(pts + (s + b + k / NC) * D + 4 * c);
+      }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int64_t k = k0 + u * 256;
         if (k < nel) {
-          const int64_t g = s + b + k / NC;
-          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (live) {
-            const float4 x = *reinterpret_cast<const float4 *>(pts + g * D + 4 * c);
-            v = make_float4(sc * (float)((double)x.x - a0), sc * (float)((double)x.y - a1),
-                            sc * (float)((double)x.z - a2), sc * (float)((double)x.w - a3));
-          }
-          Gp[g * NC + c] = v;
-          if (c == 0) Ap[g] = (float)((double)eff_weight(w, mask, wmode, g) / Wn);
+          const float4 x = xv[u];
+          Gp[(s + b + k / NC) * NC + c] =
+              live ? make_float4(sc * (float)((double)x.x - a0), sc * (float)((double)x.y - a1),
+                                 sc * (float)((double)x.z - a2), sc * (float)((double)x.w - a3))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
     }
+    // normalised weights, one point per thread
+    for (int64_t i = b + threadIdx.x; i < e; i += 256)
+      Ap[s + i] = (float)((double)eff_weight(w, mask, wmode, s + i) / Wn);
   });
 }
 
