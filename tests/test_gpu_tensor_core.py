@@ -36,9 +36,11 @@ def _embed_batch(rng, sizes_x, sizes_y, d, noise=0.1):
     return (x / np.sqrt(d)).astype(np.float32), (y / np.sqrt(d)).astype(np.float32), ptr_x, ptr_y
 
 
-@pytest.mark.parametrize("d", [32, 64, 128])
+@pytest.mark.parametrize("d", [20, 32, 36, 64, 128])
 @pytest.mark.parametrize("center", [False, True])
 def test_tensor_core_ragged_matches_oracle(d, center, cuda_device):
+    """Padded widths 32, 64 and 128; d = 20 and 36 leave zero-padded float4
+    chunks at the end of every packed point."""
     import rapidalign_b200 as ra
     rng = np.random.default_rng(40 + d + int(center))
     # sizes around the 128-row and 64-column tiles, an empty side, a tiny pair
