@@ -424,17 +424,45 @@ __global__ void __launch_bounds__(256) epigw_partial_kernel(EpilogueArgs A) {
     double R[KL], Q = 0.0;
 #pragma unroll
     for (int k = 0; k < KL; ++k) R[k] = 0.0;
-    for (int64_t i = b + wid; i < e; i += NW) {
+    // software-pipelined: the next point's loads are in flight while this
+    // one is summed (same points, same order)
+    struct Pt {
+      float a, ss, sc, ts[KL], tc[KL], xp[KL];
+    };
+    auto load = [&](int64_t i) {
+      Pt q;
       const int64_t g = E.s + i;
       const float *acc = accb + g * A.acc_stride;
-      const double a = Ap[g], s_self = acc[2 * DP], s_cross = acc[2 * DP + 1];
+      q.a = Ap[g];
+      q.ss = acc[2 * DP];
+      q.sc = acc[2 * DP + 1];
 #pragma unroll
       for (int k = 0; k < KL; ++k) {
         const int d = lane + 32 * k;
-        if (d < D) R[k] += genw_gxt(A, acc, a, s_self, s_cross, Gp + g * DP, d, E);
+        q.ts[k] = d < D ? acc[d] : 0.f;
+        q.tc[k] = d < D ? acc[DP + d] : 0.f;
+        q.xp[k] = d < D ? Gp[g * DP + d] : 0.f;
+      }
+      return q;
+    };
+    Pt cur;
+    if (b + wid < e) cur = load(b + wid);
+    for (int64_t i = b + wid; i < e; i += NW) {
+      Pt nxt;
+      if (i + NW < e) nxt = load(i + NW);
+      const double a = cur.a, s_self = cur.ss, s_cross = cur.sc;
+#pragma unroll
+      for (int k = 0; k < KL; ++k) {
+        if (lane + 32 * k < D) {
+          const double xp = cur.xp[k];
+          const double Gs = xp * s_self - (double)cur.ts[k];
+          const double Gc = xp * s_cross - (double)cur.tc[k];
+          R[k] += -a * E.k_x * (E.cs * Gs + E.cc * Gc);
+        }
       }
       // the stored self sums leave out the diagonal term (k_ii = 1, weight a_i)
       Q += a * (E.cs * (s_self + a) + E.cc * s_cross);
+      cur = nxt;
     }
 #pragma unroll
     for (int k = 0; k < KL; ++k) sh[wid][lane + 32 * k] = R[k];
