@@ -104,6 +104,23 @@ struct EpilogueArgs {
   double *grad_sigma;
 };
 
+// One point's record (self (s, G0..G2), cross (s, G0..G2), 32-byte aligned)
+// and packed weight, loaded ahead of point_grads.
+struct PointRec3 {
+  float4 self4, cross4;
+  float aw;
+};
+__device__ __forceinline__ PointRec3 load_point3(const EpilogueArgs &A, int side, int64_t slot) {
+  static_assert(kAcc3Stride == 8 && kAcc3Block == 4, "record = two float4 blocks");
+  const float4 *rec = reinterpret_cast<const float4 *>((side == 0 ? A.accX : A.accY) +
+                                                       slot * kAcc3Stride);
+  PointRec3 r;
+  r.self4 = rec[0];
+  r.cross4 = rec[1];
+  r.aw = (side == 0 ? A.aw_x : A.aw_y)[slot];
+  return r;
+}
+
 // Per-point backward quantities of the D <= 3 layout: `slot` = tile * 64 +
 // lane of the point in the tile layout.  Returns gxt[0..D) (dL/dx~) and ga
 // (dL/da, direct part).
@@ -111,25 +128,19 @@ struct EpilogueArgs {
 // paired with (m_own for the self block, m_par for the cross block), and the
 // packed weight is a / m_own: both are undone here.
 template <int MAXD>
-__device__ __forceinline__ void point_grads(const EpilogueArgs &A, int side, int64_t slot,
-                                            double cs, double cc, double k_x, double m_own,
-                                            double m_par, double *gxt, double &ga,
-                                            double &a_out) {
-  static_assert(kAcc3Stride == 8 && kAcc3Block == 4, "record = two float4 blocks");
-  const int D = A.D;
-  // the record (32-byte aligned): self (s, G0..G2), cross (s, G0..G2)
-  const float4 *rec = reinterpret_cast<const float4 *>((side == 0 ? A.accX : A.accY) +
-                                                       slot * kAcc3Stride);
-  const float4 self4 = rec[0], cross4 = rec[1];
-  const float gs[3] = {self4.y, self4.z, self4.w}, gc[3] = {cross4.y, cross4.z, cross4.w};
-  const double a = (double)(side == 0 ? A.aw_x : A.aw_y)[slot] * m_own;
+__device__ __forceinline__ void point_grads(const PointRec3 &R, int D, double cs, double cc,
+                                            double k_x, double m_own, double m_par, double *gxt,
+                                            double &ga, double &a_out) {
+  const float gs[3] = {R.self4.y, R.self4.z, R.self4.w};
+  const float gc[3] = {R.cross4.y, R.cross4.z, R.cross4.w};
+  const double a = (double)R.aw * m_own;
   const double ws = cs * m_own, wc = cc * m_par;
 #pragma unroll
   for (int d = 0; d < MAXD; ++d) {
     // difference form: G = sum w k (x' - y') accumulated directly
     gxt[d] = d < D ? -a * k_x * (ws * gs[d] + wc * gc[d]) : 0.0;
   }
-  ga = ws * self4.x + wc * cross4.x;
+  ga = ws * R.self4.x + wc * R.cross4.x;
   a_out = a;
 }
 
@@ -197,12 +208,19 @@ __global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
     const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
     const int64_t b = c * kChunk, e = b + kChunk < E.count ? b + kChunk : E.count;
     double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
+    // software-pipelined: the next point's record is in flight while this
+    // one is summed (same points, same order)
+    PointRec3 cur;
+    if (b + threadIdx.x < e) cur = load_point3(A, side, slot0 + b + threadIdx.x);
     for (int64_t i = b + threadIdx.x; i < e; i += NT) {
+      PointRec3 nxt;
+      if (i + NT < e) nxt = load_point3(A, side, slot0 + i + NT);
       double gxt[3], ga, a;
-      point_grads<3>(A, side, slot0 + i, E.cs, E.cc, E.k_x, E.m_own, E.m_par, gxt, ga, a);
+      point_grads<3>(cur, A.D, E.cs, E.cc, E.k_x, E.m_own, E.m_par, gxt, ga, a);
 #pragma unroll
       for (int d = 0; d < 3; ++d) R[d] += gxt[d];  // gxt[d >= D] == 0
       Q += a * ga;
+      cur = nxt;
     }
     double *rec = A.rec + v * rs;
     double vals[4] = {Q, R[0], R[1], R[2]};
@@ -218,7 +236,7 @@ __global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
 // chunks, fixed-order block sums) and write the gradients of the chunk's
 // points (zeros for the padded tail of a dense row).
 template <int NT>
-__global__ void __launch_bounds__(NT) epi3_write_kernel(EpilogueArgs A) {
+__global__ void __launch_bounds__(NT, 3) epi3_write_kernel(EpilogueArgs A) {
   __shared__ double sh[(NT / 32) * 4];
   const ChunkMap M{A.P, A.choff, A.chx};
   const int rs = stats_stride(A.DP);
@@ -252,11 +270,19 @@ __global__ void __launch_bounds__(NT) epi3_write_kernel(EpilogueArgs A) {
     double *wout = side == 0 ? A.grad_wx : A.grad_wy;
     const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
     const int64_t b = c * kChunk, e = b + kChunk < E.span ? b + kChunk : E.span;
+    // software-pipelined: the next point's record is loaded before this
+    // point's stores (which might alias it as far as the compiler knows)
+    PointRec3 cur;
+    if (b + threadIdx.x < e && b + threadIdx.x < E.count)
+      cur = load_point3(A, side, slot0 + b + threadIdx.x);
     for (int64_t i = b + threadIdx.x; i < e; i += NT) {
+      PointRec3 nxt;
+      if (i + NT < e && i + NT < E.count) nxt = load_point3(A, side, slot0 + i + NT);
       const int64_t g = E.s + i;
       double gxt[3] = {0.0, 0.0, 0.0}, ga = 0.0, a = 0.0;
       const bool live = i < E.count;
-      if (live) point_grads<3>(A, side, slot0 + i, E.cs, E.cc, E.k_x, E.m_own, E.m_par, gxt, ga, a);
+      if (live) point_grads<3>(cur, D, E.cs, E.cc, E.k_x, E.m_own, E.m_par, gxt, ga, a);
+      cur = nxt;
       if (gout != nullptr) {
 #pragma unroll
         for (int d = 0; d < 3; ++d) {
