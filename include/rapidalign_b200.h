@@ -15,14 +15,18 @@
  *    the host;
  *  - the library never allocates device memory: scratch space is a caller
  *    owned `workspace` of at least the size the matching *_workspace_bytes
- *    function returns (256-byte aligned);
+ *    function returns (256-byte aligned).  The one exception is
+ *    ra_kde_mmd_forward_segmented_noalloc, whose scratch is a fixed array
+ *    inside the library (see its comment);
  *  - the return value is an ra_status code; ra_status_string() names it.
  *    Argument errors are reported synchronously.  Data-dependent errors
  *    (bad ptr offsets, non-positive weight sums) are detected on the device
  *    and reported by ra_kde_check(), which reads one int back and therefore
  *    synchronises `stream`;
- *  - no global mutable state: calls on different streams with different
- *    workspaces are independent.
+ *  - calls on different streams with different workspaces are independent.
+ *    The library's only global mutable state is the no-alloc entry point's
+ *    scratch array (shared by its calls, see there) and a process-wide
+ *    launch counter (ra_kernel_launch_count, diagnostics only).
  */
 #ifndef RAPIDALIGN_B200_H
 #define RAPIDALIGN_B200_H
@@ -107,7 +111,17 @@ typedef struct ra_kde_desc {
                           tensor cores when the padded dim is 32, 64 or 128, else SIMT;
                           RA_ENGINE_TENSOR on another padded dim is
                           RA_ERR_INVALID_ARGUMENT.  Ignored for dim <= 3. */
+  int32_t test_hooks;  /* 0 in normal use.  Bits of enum ra_test_hook, for tests of the
+                          library's own failure paths only. */
 } ra_kde_desc;
+
+/* Test hooks (ra_kde_desc.test_hooks).  RA_TEST_NO_MMA: the tensor-core kernels
+ * (dim >= 4 on the tensor-core engine) issue no MMA at all and bound each wait
+ * to 4096 polls, so their first wait for a GEMM expires with nothing in flight:
+ * the kernel records the timeout, frees its tensor memory and returns, and
+ * ra_kde_check reports RA_ERR_DEVICE_TIMEOUT.  The results of such a call are
+ * invalid. */
+enum ra_test_hook { RA_TEST_NO_MMA = 1 };
 
 typedef struct ra_kde_inputs {
   const float *x;        /* [num_x * D] */
@@ -184,6 +198,11 @@ RA_API int ra_kde_forward_profiled(const ra_kde_desc *desc, const ra_kde_inputs 
 /* Reads the device error word of `workspace` (synchronises `stream`). */
 RA_API int ra_kde_check(const void *workspace, ra_stream_t stream);
 
+/* The status a device error word stands for (RA_OK for 0): for callers that
+ * copy the word themselves (the first 4 bytes of the workspace, an int) to
+ * read it without synchronising the stream. */
+RA_API int ra_kde_status_of_error_word(int word);
+
 /* ---- legacy operator set: one entry point per op of csrc/bindings.cpp ---- */
 
 /*
@@ -249,7 +268,13 @@ RA_API int ra_kde_mmd_backward_segmented(const float *x, const float *y, const f
  *  - all calls on a device share the one array and it keeps the previous
  *    call's contents; the call clears what must start at zero, but calls
  *    whose GPU work overlaps (other streams, other host threads) race on it:
- *    serialise them.
+ *    serialise them;
+ *  - every call looks the array's device address up again (which allocates
+ *    nothing), so a device reset between calls does not leave a stale
+ *    address behind;
+ *  - data errors found on the device (bad ptr offsets, a non-positive weight
+ *    sum, a tensor-core wait that expired) are read back by
+ *    ra_kde_check_noalloc, as ra_kde_check does for a caller's workspace.
  */
 RA_API int ra_kde_mmd_forward_segmented_noalloc(const float *x, const float *y,
                                                 const float *w_x, const float *w_y,
@@ -257,6 +282,11 @@ RA_API int ra_kde_mmd_forward_segmented_noalloc(const float *x, const float *y,
                                                 int64_t P, int64_t NX, int64_t NY, int32_t D,
                                                 double sigma, double *Kxx, double *Kyy,
                                                 double *Kxy, ra_stream_t stream);
+
+/* The device error word of the no-alloc scratch on the current device, as a
+ * status (the same codes as ra_kde_check; synchronises `stream`).  Reports on
+ * the last ra_kde_mmd_forward_segmented_noalloc enqueued on this device. */
+RA_API int ra_kde_check_noalloc(ra_stream_t stream);
 
 /* ---- diagnostics ------------------------------------------------------- */
 

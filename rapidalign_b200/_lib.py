@@ -44,6 +44,8 @@ RA_ENGINE_AUTO = 0
 RA_ENGINE_SIMT = 1
 RA_ENGINE_TENSOR = 2
 
+RA_TEST_NO_MMA = 1
+
 
 class RaKdeDesc(ctypes.Structure):
     _fields_ = [
@@ -63,6 +65,7 @@ class RaKdeDesc(ctypes.Structure):
         ("shard_count", ctypes.c_int32),
         ("sigma", ctypes.c_double),
         ("engine", ctypes.c_int32),
+        ("test_hooks", ctypes.c_int32),
     ]
 
 
@@ -115,6 +118,8 @@ SIGNATURES = {
     "ra_kde_backward": (ctypes.c_int, [ctypes.POINTER(RaKdeDesc), ctypes.POINTER(RaKdeInputs),
                                        _V, ctypes.POINTER(RaKdeGrads), _V, _SZ, _V]),
     "ra_kde_check": (ctypes.c_int, [_V, _V]),
+    "ra_kde_status_of_error_word": (ctypes.c_int, [ctypes.c_int]),
+    "ra_kde_check_noalloc": (ctypes.c_int, [_V]),
     "ra_kde_partials": (ctypes.c_int, [ctypes.POINTER(RaKdeDesc), _V, _SZ,
                                        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(_SZ),
                                        ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(_SZ)]),

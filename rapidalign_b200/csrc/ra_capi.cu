@@ -11,7 +11,6 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
-#include <mutex>
 
 #include "../../include/rapidalign_b200.h"
 #include "ra_chunks.cuh"
@@ -83,6 +82,7 @@ bool desc_ok(const ra_kde_desc *d) {
   if (d->shard_count < 0 || (d->shard_count > 1 &&
                              (d->shard_index < 0 || d->shard_index >= d->shard_count)))
     return false;
+  if ((d->test_hooks & ~RA_TEST_NO_MMA) != 0) return false;
   return true;
 }
 
@@ -497,6 +497,8 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.shard_index = sh_idx;
     T.shard_count = sh_cnt;
     T.err = at<int>(ws, L.hdr + kHdrErr);
+    T.no_mma = (d->test_hooks & RA_TEST_NO_MMA) ? 1 : 0;
+    T.spin_limit = T.no_mma ? 4096u : kTcSpinLimit;
     rc = use_tensor_cores(d, L.DP) ? launch_tilestc(L.DP, mode, L.max_items, T, st)
                                    : launch_tilesg(L.DP, mode, L.max_items, T, st);
     if (rc) return rc;
@@ -677,22 +679,25 @@ __global__ void fp32_probe_kernel(float *out, int iters, float seed) {
 constexpr size_t kNoallocScratchBytes = (size_t)64 << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void *g_noalloc_addr[kMaxDevices] = {};
-
+// The current device's address of the scratch array, looked up on every call
+// (the lookup allocates nothing; the first one on a device may load the
+// library's device code there, which is why that first call belongs before any
+// stream capture).  Not cached, so a device reset leaves nothing stale.
 int noalloc_scratch_address(void **out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess) return RA_ERR_CUDA;
-  if (dev < 0 || dev >= kMaxDevices) return RA_ERR_INVALID_ARGUMENT;
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
-    void *p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
-      return RA_ERR_CUDA;
-    g_noalloc_addr[dev] = p;
-  }
-  *out = g_noalloc_addr[dev];
+  void *p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+    return RA_ERR_CUDA;
+  *out = p;
+  return RA_OK;
+}
+
+int status_of_error_word(int err) {
+  if (err & kErrPtrStart) return RA_ERR_PTR_START;
+  if (err & kErrPtrEnd) return RA_ERR_PTR_END;
+  if (err & kErrPtrOrder) return RA_ERR_PTR_ORDER;
+  if (err & kErrWeightSum) return RA_ERR_WEIGHT_SUM;
+  if (err & kErrTimeout) return RA_ERR_DEVICE_TIMEOUT;
+  if (err & kErrSigma) return RA_ERR_SIGMA;
   return RA_OK;
 }
 
@@ -798,14 +803,10 @@ int ra_kde_check(const void *workspace, ra_stream_t stream) {
                       cudaMemcpyDeviceToHost, (cudaStream_t)stream) != cudaSuccess)
     return RA_ERR_CUDA;
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return RA_ERR_CUDA;
-  if (err & kErrPtrStart) return RA_ERR_PTR_START;
-  if (err & kErrPtrEnd) return RA_ERR_PTR_END;
-  if (err & kErrPtrOrder) return RA_ERR_PTR_ORDER;
-  if (err & kErrWeightSum) return RA_ERR_WEIGHT_SUM;
-  if (err & kErrTimeout) return RA_ERR_DEVICE_TIMEOUT;
-  if (err & kErrSigma) return RA_ERR_SIGMA;
-  return RA_OK;
+  return status_of_error_word(err);
 }
+
+int ra_kde_status_of_error_word(int word) { return status_of_error_word(word); }
 
 size_t ra_kde_mmd_forward_workspace_bytes(int64_t B, int64_t Nx, int64_t Ny, int32_t D) {
   ra_kde_desc d = legacy_desc(RA_LAYOUT_DENSE, B, B * Nx, B * Ny, Nx, Ny, D, 1.0, 0);
@@ -916,6 +917,13 @@ int ra_kde_mmd_forward_segmented_noalloc(const float *x, const float *y, const f
   // is written earlier in the same call
   return ra_kde_mmd_forward_segmented(x, y, w_x, w_y, ptr_x, ptr_y, P, NX, NY, D, sigma, Kxx,
                                       Kyy, Kxy, scratch, kNoallocScratchBytes, stream);
+}
+
+int ra_kde_check_noalloc(ra_stream_t stream) {
+  void *scratch = nullptr;
+  const int rc = noalloc_scratch_address(&scratch);
+  if (rc) return rc;
+  return ra_kde_check(scratch, stream);
 }
 
 unsigned long long ra_kernel_launch_count(void) { return g_launches.load(); }

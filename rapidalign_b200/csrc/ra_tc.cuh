@@ -107,9 +107,10 @@ __device__ __forceinline__ void tc_fence_after() {
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-// true when the barrier completed phase `parity` within the limit
-__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity) {
-  for (unsigned it = 0; it < kTcSpinLimit; ++it) {
+// true when the barrier completed phase `parity` within `limit` polls
+__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity,
+                                          unsigned limit = kTcSpinLimit) {
+  for (unsigned it = 0; it < limit; ++it) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred P1;\n\t"
@@ -233,6 +234,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
   const uint32_t mb = smem_u32(mbar);
   uint32_t phase = 0;
   bool ok = true;
+  bool pending = false;  // thread 0: a commit to `mb` not yet waited for
 
   const int64_t n_items = *A.n_items;
   for (int64_t it = (int64_t)blockIdx.x * A.shard_count + A.shard_index; it < n_items && ok;
@@ -382,7 +384,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
       tc_fence_after();
 
       // ---- GEMM 1: S = X Y^T (3xTF32), one thread issues -------------------
-      if (tid == 0) {
+      if (tid == 0 && !A.no_mma) {
         const uint32_t sh = smem_u32(yhi), sl = smem_u32(ylo);
 #pragma unroll 1
         for (int k = 0; k < DP / 8; ++k) {
@@ -394,6 +396,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
           tc_mma(tbase + C_S, tbase + C_XL + 8 * k, bh, IDESC1, 1u);
         }
         tc_commit(mb);
+        pending = true;
       }
       // |y'|^2 totals for the epilogue, while GEMM 1 runs (published by the
       // barrier after its wait)
@@ -405,10 +408,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
         yqf[tid] = t - log2f(bcol[tid]);  // +inf for zero weight and padding
       }
       // the decision to stop is taken by the whole CTA at once
-      if (__syncthreads_or(!mbar_wait(mb, phase))) {
+      if (__syncthreads_or(!mbar_wait(mb, phase, A.spin_limit))) {
         ok = false;
         break;
       }
+      pending = false;
       phase ^= 1u;
       tc_fence_after();
 
@@ -467,7 +471,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
         __syncthreads();
         tc_fence_after();
         // ---- GEMM 2: T += P Y (3xTF32), B = the transposed Y tile -----------
-        if (tid == 0) {
+        if (tid == 0 && !A.no_mma) {
           const uint32_t sh = smem_u32(yth), sl = smem_u32(ytl);
 #pragma unroll 1
           for (int k = 0; k < kTcCols / 8; ++k) {
@@ -480,12 +484,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
             tc_mma(tbase + C_T, tbase + C_PL + 8 * k, bh, IDESC2, 1u);
           }
           tc_commit(mb);
+          pending = true;
         }
         if (j0 + kTcCols < ccnt) load_tile(j0 + kTcCols);  // in flight during GEMM 2
-        if (__syncthreads_or(!mbar_wait(mb, phase))) {
+        if (__syncthreads_or(!mbar_wait(mb, phase, A.spin_limit))) {
           ok = false;
           break;
         }
+        pending = false;
         phase ^= 1u;
         tc_fence_after();
         first = false;
@@ -546,8 +552,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
   }
   if (!ok && tid == 0) {
     atomicOr(A.err, (int)kErrTimeout);
-    // give the MMAs in flight a last bounded chance to land before TMEM is freed
-    (void)mbar_wait(mb, phase);
+    // give the MMAs in flight a last bounded chance to land before TMEM is
+    // freed (the full limit, whatever the waits above used)
+    if (pending) (void)mbar_wait(mb, phase);
   }
   tc_fence_before();
   __syncthreads();

@@ -58,11 +58,11 @@ __device__ __forceinline__ void mbar_init(uint32_t a, unsigned count) {
 __device__ __forceinline__ void mbar_arrive(uint32_t a) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
 }
-// Wait for the phase of the given parity; false when the poll limit is
+// Wait for the phase of the given parity; false when `limit` polls are
 // reached or another role has raised the abort flag.
 __device__ __forceinline__ bool ws_wait(uint32_t mbar, uint32_t parity,
-                                        const volatile int *abort_flag) {
-  for (unsigned it = 0; it < kTcSpinLimit; ++it) {
+                                        const volatile int *abort_flag, unsigned limit) {
+  for (unsigned it = 0; it < limit; ++it) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred P1;\n\t"
@@ -224,7 +224,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
         for (int jt = 0; jt < ntiles; ++jt, ++t) {
           const int64_t j0 = (int64_t)jt * kTcCols;
           // the tile's weights and totals (producers), then S (GEMM 1)
-          const bool w_ok = ws_wait(b_ykfull, t & 1u, abortf) && ws_wait(b_g1, t & 1u, abortf);
+          const bool w_ok = ws_wait(b_ykfull, t & 1u, abortf, A.spin_limit) &&
+                            ws_wait(b_g1, t & 1u, abortf, A.spin_limit);
           if (role_sync_or(1, ET, !w_ok)) {
             ok = false;
             break;
@@ -287,7 +288,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
         }
         if (ok && GRAD) {
           // T of the item: after GEMM 2 of its last tile
-          const bool w_ok = ws_wait(b_g2, (t - 1u) & 1u, abortf);
+          const bool w_ok = ws_wait(b_g2, (t - 1u) & 1u, abortf, A.spin_limit);
           if (role_sync_or(1, ET, !w_ok)) ok = false;
           tc_fence_after();
         }
@@ -375,7 +376,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
         }
         // Y (GEMM 1 layout) is free once GEMM 1 of the previous tile is done;
         // the barrier also orders the previous tile's reads of ysq
-        const bool w1 = t == 0 || ws_wait(b_g1, (t - 1u) & 1u, abortf);
+        const bool w1 = t == 0 || ws_wait(b_g1, (t - 1u) & 1u, abortf, A.spin_limit);
         if (role_sync_or(2, PT, !w1)) {
           ok = false;
           break;
@@ -427,7 +428,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
         }
         if (ptid == 0) negf[pb] = anyneg;
         // hand the tile over only after the epilogue took the previous one
-        const bool w2 = t == 0 || ws_wait(b_pfull, (t - 1u) & 1u, abortf);
+        const bool w2 = t == 0 || ws_wait(b_pfull, (t - 1u) & 1u, abortf, A.spin_limit);
         if (role_sync_or(2, PT, !w2)) {
           ok = false;
           break;
@@ -435,7 +436,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
         mbar_arrive(b_ykfull);
         if (GRAD) {
           // transposed Y (GEMM 2) once GEMM 2 of the previous tile is done
-          const bool w3 = t == 0 || ws_wait(b_g2, (t - 1u) & 1u, abortf);
+          const bool w3 = t == 0 || ws_wait(b_g2, (t - 1u) & 1u, abortf, A.spin_limit);
           if (role_sync_or(2, PT, !w3)) {
             ok = false;
             break;
@@ -481,14 +482,15 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
     // =================== MMA issuer =========================================
     uint32_t t = 0, xk = 0, n_g1 = 0, n_g2 = 0;  // tiles, items, commits issued
     bool ok = true;
-    for (int64_t it = ifirst; it < n_items && ok && !*abortf; it += istep) {
+    // (test hook: no MMA at all, so every wait on a GEMM expires)
+    for (int64_t it = ifirst; it < n_items && ok && !*abortf && !A.no_mma; it += istep) {
       const Item item = A.items[it];
       const Seg sg = A.seg[item.pair];
       const bool cols_x = (item.block == 1 || item.block == 3);
       const int64_t ccnt = cols_x ? sg.xcount : sg.ycount;
       const int ntiles = (int)ceil_div(ccnt, (int64_t)kTcCols);
       if (ntiles == 0) continue;
-      if (!ws_wait(b_xfull, xk & 1u, abortf)) {
+      if (!ws_wait(b_xfull, xk & 1u, abortf, A.spin_limit)) {
         ok = false;
         break;
       }
@@ -496,8 +498,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
       for (int jt = 0; jt < ntiles; ++jt, ++t) {
         // GEMM 1 needs this tile's Y and a free S (GEMM 2, or without a
         // backward the epilogue, of the previous tile done)
-        if (!ws_wait(b_ykfull, t & 1u, abortf) ||
-            (t > 0 && !ws_wait(GRAD ? b_g2 : b_pfull, (t - 1u) & 1u, abortf))) {
+        if (!ws_wait(b_ykfull, t & 1u, abortf, A.spin_limit) ||
+            (t > 0 && !ws_wait(GRAD ? b_g2 : b_pfull, (t - 1u) & 1u, abortf, A.spin_limit))) {
           ok = false;
           break;
         }
@@ -516,7 +518,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
           ++n_g1;
         }
         if (GRAD) {
-          if (!ws_wait(b_pfull, t & 1u, abortf) || !ws_wait(b_ytfull, t & 1u, abortf)) {
+          if (!ws_wait(b_pfull, t & 1u, abortf, A.spin_limit) ||
+              !ws_wait(b_ytfull, t & 1u, abortf, A.spin_limit)) {
             ok = false;
             break;
           }

@@ -28,6 +28,8 @@ struct TilesGArgs {
   int need_rows;         // 1: write the per-point sums (backward requested)
   int shard_index, shard_count;  // evaluate only items shard_index + k * shard_count
   int *err;                      // error word (the tensor-core path's wait limits)
+  unsigned spin_limit;           // tensor-core path: polls of one wait before giving up
+  int no_mma;                    // test hook: the tensor-core path issues no MMA at all
 };
 
 // One staged column tile against this thread's row: st += sum w, T += sum w y'

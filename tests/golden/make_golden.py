@@ -1,8 +1,8 @@
 """Generate the golden fixtures in ``tests/golden/*.npz`` from the reference.
 
-Run in a checkout that has the reference package importable, e.g.::
+Run with a checkout of the reference on the import path, e.g.::
 
-    PYTHONPATH=/root/reference python tests/golden/make_golden.py
+    PYTHONPATH=<checkout of the reference> python tests/golden/make_golden.py
 
 Every case runs the reference's own CPU code path in float64 with PyTorch
 autograd (``rapidalign.kde``: kde.py:39-109, 211-299, 302-428;

@@ -1,0 +1,79 @@
+"""Failure paths of the tensor-core kernels, exercised without faulting the GPU.
+
+Every wait of the tensor-core kernels (ra_tc.cuh, ra_tcws.cuh) on an mbarrier is
+bounded; when one expires the kernel records a timeout in the workspace's error
+word, stops, frees its tensor memory and returns, and ra_kde_check reports
+RA_ERR_DEVICE_TIMEOUT.  The test hook RA_TEST_NO_MMA makes the kernels issue no
+MMA at all and bound each wait to 4096 polls: the first wait for a GEMM then
+expires with nothing asynchronous in flight.  Each test checks the status, then
+runs the same problem normally on the same device and compares it with the
+oracle, which also shows that the aborted launch freed its tensor memory (a
+persistent CTA of the next launch could not allocate it otherwise).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+K_TOL = 2e-6
+
+
+def _problem(seed, sizes, dim, dev):
+    rng = np.random.default_rng(seed)
+    ptr = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    x = (rng.standard_normal((ptr[-1], dim)) / np.sqrt(dim)).astype(np.float32)
+    y = (x + 0.1 * rng.standard_normal(x.shape)).astype(np.float32)
+    t = lambda a: torch.from_numpy(a).to(dev).contiguous()
+    return x, y, ptr, t(x), t(y), t(ptr)
+
+
+def _forward(lib, xt, yt, pt, P, dim, sigma, hooks, need_grad, dev):
+    from rapidalign_b200 import _lib
+    d = _lib.RaKdeDesc()
+    d.num_pairs, d.dim, d.layout = P, dim, _lib.RA_LAYOUT_RAGGED
+    d.num_x, d.num_y = xt.shape[0], yt.shape[0]
+    d.weights_x = d.weights_y = _lib.RA_WEIGHTS_UNIFORM
+    d.center, d.need_grad, d.need_sigma_grad = 0, need_grad, 0
+    d.shard_index, d.shard_count = 0, 1
+    d.sigma, d.engine, d.test_hooks = sigma, _lib.RA_ENGINE_TENSOR, hooks
+    inp = _lib.RaKdeInputs()
+    inp.x, inp.y, inp.ptr_x, inp.ptr_y = xt.data_ptr(), yt.data_ptr(), pt.data_ptr(), pt.data_ptr()
+    nbytes = lib.ra_kde_workspace_bytes(ctypes.byref(d))
+    assert nbytes > 0
+    ws = _lib.workspace(nbytes, dev)
+    K = torch.zeros(3 * P, dtype=torch.float64, device=dev)
+    stream = _lib.stream_handle(dev)
+    rc = lib.ra_kde_forward(ctypes.byref(d), ctypes.byref(inp), K.data_ptr(), ws.data_ptr(),
+                            ws.numel(), stream)
+    assert rc == 0, _lib.status_string(rc)
+    return K, lib.ra_kde_check(ws.data_ptr(), stream)
+
+
+@pytest.mark.parametrize("dim,need_grad", [(32, 0), (32, 1), (128, 0), (128, 1)])
+def test_expired_wait_is_reported_and_the_device_stays_usable(dim, need_grad, cuda_device):
+    """dim 32: the single-role kernel (tilestc_kernel); dim 128: the
+    warp-specialised one (tilestc_ws_kernel)."""
+    from rapidalign_b200 import _lib
+    lib = _lib.load()
+    dev = cuda_device
+    sizes = [300, 70, 129]
+    x, y, ptr, xt, yt, pt = _problem(31 + dim, sizes, dim, dev)
+    sigma = 1.0
+    _, status = _forward(lib, xt, yt, pt, len(sizes), dim, sigma, _lib.RA_TEST_NO_MMA,
+                         need_grad, dev)
+    assert status == _lib.RA_ERR_DEVICE_TIMEOUT, _lib.status_string(status)
+    # the same problem, normally, twice (a second launch needs every SM's TMEM)
+    for _ in range(2):
+        K, status = _forward(lib, xt, yt, pt, len(sizes), dim, sigma, 0, need_grad, dev)
+        assert status == _lib.RA_OK, _lib.status_string(status)
+        P = len(sizes)
+        a = np.concatenate([np.full(n, 1.0 / n) for n in sizes])
+        rs = O.raw_sums(x, y, a, a, ptr, ptr, sigma)
+        got = K.cpu().numpy().reshape(3, P)
+        for k in range(3):
+            assert np.all(np.abs(got[k] - rs.K[:, k]) <= K_TOL * np.abs(rs.K[:, k])), k
