@@ -111,6 +111,10 @@ typedef struct ra_kde_desc {
                           tensor cores when the padded dim is 32, 64 or 128, else SIMT;
                           RA_ENGINE_TENSOR on another padded dim is
                           RA_ERR_INVALID_ARGUMENT.  Ignored for dim <= 3. */
+  int32_t skip_weight_sums; /* 1: no weight gradient will be asked for, so the forward may
+                          leave out per-point sums that only grad_wx / grad_wy need
+                          (dim <= 3: one FP32 operation per kernel term); a backward
+                          that asks for them is then RA_ERR_STATE.  0: keep them. */
   int32_t test_hooks;  /* 0 in normal use.  Bits of enum ra_test_hook, for tests of the
                           library's own failure paths only. */
 } ra_kde_desc;

@@ -12,6 +12,7 @@ CPU path.
 from __future__ import annotations
 
 import ctypes
+import dataclasses
 from dataclasses import dataclass
 from typing import Optional, Tuple
 
@@ -51,6 +52,9 @@ class Spec:
     shard_count: int = 1
     engine: int = 0  # _lib.RA_ENGINE_*: kernel family for dim >= 4 (0 = automatic)
     weight_error_message: str = "weights must sum to a positive value per segment"
+    # no weight gradient can be asked for (set by forward_sums): the forward
+    # may leave out the per-point sums only grad_wx / grad_wy need
+    skip_weight_sums: bool = False
 
     def desc(self, need_grad: bool, need_sigma_grad: bool) -> _lib.RaKdeDesc:
         d = _lib.RaKdeDesc()
@@ -70,6 +74,8 @@ class Spec:
         d.shard_count = self.shard_count
         d.sigma = float(self.sigma)
         d.engine = int(self.engine)
+        d.skip_weight_sums = 1 if (need_grad and self.skip_weight_sums) else 0
+        d.test_hooks = 0
         return d
 
 
@@ -146,6 +152,9 @@ def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tens
     lib = _lib.load()
     device = x.device
     need_sigma_grad = need_grad and sigma_t is not None and sigma_t.requires_grad
+    weights_grad = any(w is not None and w.requires_grad for w in (w_x, w_y))
+    if need_grad and not weights_grad and not spec.skip_weight_sums:
+        spec = dataclasses.replace(spec, skip_weight_sums=True)
     x32, y32 = _f32(x), _f32(y)
     wx32, wy32 = _f32(w_x), _f32(w_y)
     desc = spec.desc(need_grad, need_sigma_grad)

@@ -65,6 +65,7 @@ class RaKdeDesc(ctypes.Structure):
         ("shard_count", ctypes.c_int32),
         ("sigma", ctypes.c_double),
         ("engine", ctypes.c_int32),
+        ("skip_weight_sums", ctypes.c_int32),
         ("test_hooks", ctypes.c_int32),
     ]
 

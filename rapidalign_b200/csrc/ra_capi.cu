@@ -51,8 +51,8 @@ struct Layout {
   int64_t max_items;
   int64_t max_tiles_x, max_tiles_y;  // packed3: bound on the padded tiles
   int64_t max_chunks;                // bound on the virtual chunks (ra_chunks.cuh)
-  size_t hdr, seg, meta, cnt, item_off, tbase_x, tbase_y, boff, items, itemK, itemS, Kws, Sws,
-      coef, Ktmp, chcnt, chx, choff, rec;
+  size_t hdr, seg, meta, cnt, item_off, tbase_x, tbase_y, boff, items, itemK, itemS, itemC, Kws,
+      Sws, Cws, coef, Ktmp, chcnt, chx, choff, rec;
   size_t tiles_x, tiles_y, Gx, Gy, Ax, Ay, accX, accY;
   size_t acc_x_bytes, acc_y_bytes;
   size_t total;
@@ -60,6 +60,7 @@ struct Layout {
 
 // header block: int err @0, unsigned ticket @4, int has_state @8, int64 n_items @16
 constexpr size_t kHdrErr = 0, kHdrTicket = 4, kHdrState = 8, kHdrNItems = 16;
+constexpr int kItemF64 = 5;  // fp64 partials per work item: K, S, C[3]
 
 bool desc_ok(const ra_kde_desc *d) {
   if (d == nullptr) return false;
@@ -83,6 +84,7 @@ bool desc_ok(const ra_kde_desc *d) {
                              (d->shard_index < 0 || d->shard_index >= d->shard_count)))
     return false;
   if ((d->test_hooks & ~RA_TEST_NO_MMA) != 0) return false;
+  if (d->skip_weight_sums != 0 && d->skip_weight_sums != 1) return false;
   return true;
 }
 
@@ -130,11 +132,14 @@ Layout make_layout(const ra_kde_desc *d) {
   L.tbase_y = take(sizeof(int64_t) * (P1 + 1));
   L.boff = take(sizeof(int64_t) * 4 * P1);
   L.items = take(sizeof(Item) * (size_t)L.max_items);
-  // itemK and itemS form one contiguous fp64 region (reduced across shards)
-  L.itemK = take(sizeof(double) * 2 * (size_t)L.max_items);
+  // itemK, itemS and itemC ([items][3]) form one contiguous fp64 region of
+  // kItemF64 values per item (reduced across shards)
+  L.itemK = take(sizeof(double) * kItemF64 * (size_t)L.max_items);
   L.itemS = L.itemK + sizeof(double) * (size_t)L.max_items;
+  L.itemC = L.itemS + sizeof(double) * (size_t)L.max_items;
   L.Kws = take(sizeof(double) * 3 * P1);
   L.Sws = take(sizeof(double) * 3 * P1);
+  L.Cws = take(sizeof(double) * 3 * P1);
   L.coef = take(sizeof(double) * 3 * P1);
   L.Ktmp = take(sizeof(double) * 3 * P1);
   L.chcnt = take(sizeof(int64_t) * P1);
@@ -202,8 +207,10 @@ int launch_tiles3(int mode, const Tiles3Args &Targs, cudaStream_t st) {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<0>, T, 0);
   else if (mode == 1)
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<1>, T, 0);
-  else
+  else if (mode == 2)
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<2>, T, 0);
+  else
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<3>, T, 0);
   if (e != cudaSuccess) return RA_ERR_CUDA;
   if (per_sm < 1) per_sm = 1;
   const int grid = sms * per_sm;
@@ -211,8 +218,10 @@ int launch_tiles3(int mode, const Tiles3Args &Targs, cudaStream_t st) {
     tiles3_kernel<0><<<grid, kT3Threads, 0, st>>>(Targs);
   else if (mode == 1)
     tiles3_kernel<1><<<grid, kT3Threads, 0, st>>>(Targs);
-  else
+  else if (mode == 2)
     tiles3_kernel<2><<<grid, kT3Threads, 0, st>>>(Targs);
+  else
+    tiles3_kernel<3><<<grid, kT3Threads, 0, st>>>(Targs);
   ++g_launches;
   return cuda_status(cudaGetLastError());
 }
@@ -319,7 +328,7 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   if (cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return RA_ERR_CUDA;
   if (P == 0) return RA_OK;
   const bool grad = d->need_grad != 0;
-  const int mode = !grad ? 0 : (d->need_sigma_grad ? 2 : 1);
+  const int mode = !grad ? 0 : (d->need_sigma_grad ? 2 : (d->skip_weight_sums ? 3 : 1));
   if (grad) {
     if (cudaMemsetAsync(at<char>(ws, L.accX), 0, L.acc_x_bytes, st) != cudaSuccess ||
         cudaMemsetAsync(at<char>(ws, L.accY), 0, L.acc_y_bytes, st) != cudaSuccess)
@@ -452,9 +461,9 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
 
   const bool sharded = d->shard_count > 1;
   const int sh_idx = sharded ? d->shard_index : 0, sh_cnt = sharded ? d->shard_count : 1;
-  if (sharded &&
-      cudaMemsetAsync(at<char>(ws, L.itemK), 0, sizeof(double) * 2 * (size_t)L.max_items, st) !=
-          cudaSuccess)
+  if (sharded && cudaMemsetAsync(at<char>(ws, L.itemK), 0,
+                                 sizeof(double) * kItemF64 * (size_t)L.max_items,
+                                 st) != cudaSuccess)
     return RA_ERR_CUDA;  // items of other shards contribute zeros to the reduction
 
   // ---- tiles ----
@@ -476,6 +485,7 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.acc_y = grad ? at<float>(ws, L.accY) : nullptr;
     T.itemK = at<double>(ws, L.itemK);
     T.itemS = at<double>(ws, L.itemS);
+    T.itemC = at<double>(ws, L.itemC);
     T.shard_index = sh_idx;
     T.shard_count = sh_cnt;
     rc = launch_tiles3(mode, T, st);
@@ -522,8 +532,10 @@ int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy,
   fa.boff = at<int64_t>(ws, L.boff);
   fa.itemK = at<double>(ws, L.itemK);
   fa.itemS = at<double>(ws, L.itemS);
+  fa.itemC = (grad && L.packed3) ? at<double>(ws, L.itemC) : nullptr;
   fa.K_ws = at<double>(ws, L.Kws);
   fa.S_ws = at<double>(ws, L.Sws);
+  fa.C_ws = at<double>(ws, L.Cws);
   // the caller's three K arrays are written by the kernel itself
   fa.K_out[0] = Kxx;
   fa.K_out[1] = Kyy;
@@ -544,6 +556,8 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   if (in == nullptr || gr == nullptr || coef == nullptr) return RA_ERR_INVALID_ARGUMENT;
   if (!d->need_grad) return RA_ERR_STATE;
   if (gr->grad_sigma != nullptr && !d->need_sigma_grad) return RA_ERR_STATE;
+  if (d->skip_weight_sums && (gr->grad_wx != nullptr || gr->grad_wy != nullptr))
+    return RA_ERR_STATE;
   const int64_t P = d->num_pairs;
   if (P == 0) return RA_OK;
   EpilogueArgs ea;
@@ -562,6 +576,8 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.meta = at<double>(ws, L.meta);
   ea.coef = coef;
   ea.S_ws = at<double>(ws, L.Sws);
+  ea.K_ws = at<double>(ws, L.Kws);
+  ea.C_ws = at<double>(ws, L.Cws);
   ea.choff = at<int64_t>(ws, L.choff);
   ea.chx = at<int64_t>(ws, L.chx);
   ea.rec = at<double>(ws, L.rec);
@@ -593,8 +609,9 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.grad_sigma = gr->grad_sigma;
   const unsigned cgrid = chunk_grid(L);
   if (L.packed3) {
-    epi3_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+    // one pass: the cloud-wide sums come from the forward's per-pair K and C
     epi3_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+    ++g_launches;
   } else if (L.DP >= 32) {
     switch (L.DP) {
       case 32:
@@ -618,7 +635,7 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
     epig_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
     epig_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
   }
-  g_launches += 2;
+  if (!L.packed3) g_launches += 2;
   if (ea.grad_sigma != nullptr) {
     sigma_grad_kernel<<<(unsigned)ceil_div(P, 256), 256, 0, st>>>(ea);
     ++g_launches;
@@ -775,7 +792,7 @@ int ra_kde_partials(const ra_kde_desc *desc, void *workspace, size_t workspace_b
   const Layout L = make_layout(desc);
   if (workspace == nullptr || workspace_bytes < L.total) return RA_ERR_WORKSPACE;
   *f64_buf = at<double>(workspace, L.itemK);
-  *f64_count = 2 * (size_t)L.max_items;
+  *f64_count = kItemF64 * (size_t)L.max_items;
   if (desc->need_grad) {
     *f32_buf = at<float>(workspace, L.accX);
     *f32_count = (L.accY + L.acc_y_bytes - L.accX) / sizeof(float);

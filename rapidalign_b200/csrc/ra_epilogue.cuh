@@ -25,9 +25,11 @@ struct FinalizeArgs {
   const int64_t *item_off;
   const int64_t *boff;
   const double *itemK, *itemS;
+  const double *itemC;  // [items][3] of the x-y items, or null (D <= 3 with gradients only)
   double *K_out[3];  // caller's Kxx, Kyy, Kxy ([P] each)
   double *K_ws;   // [3P] copy kept in the workspace
   double *S_ws;   // [3P]
+  double *C_ws;   // [P][3]: C = sum_ij a_i b_j k_ij (x'_i - y'_j) (when itemC is set)
   int *state;     // set to 1 when not null
 };
 
@@ -72,6 +74,18 @@ __global__ void __launch_bounds__(NT) finalize_kernel(FinalizeArgs A) {
       A.K_ws[kidx[b] * A.P + p] = kt;
       A.S_ws[kidx[b] * A.P + p] = st;
     }
+    if (b == 0 && A.itemC != nullptr) {
+      double c[3] = {0.0, 0.0, 0.0};
+      for (int64_t j = b0 + threadIdx.x; j < e; j += NT) {
+#pragma unroll
+        for (int d = 0; d < 3; ++d) c[d] += A.itemC[3 * j + d];
+      }
+#pragma unroll
+      for (int d = 0; d < 3; ++d) {
+        const double ct = block_sum(c[d], sh);
+        if (threadIdx.x == 0) A.C_ws[3 * p + d] = ct;
+      }
+    }
   }
 }
 
@@ -87,6 +101,8 @@ struct EpilogueArgs {
   const double *meta;
   const double *coef;  // [3P]: dL/dKxx | dL/dKyy | dL/dKxy
   const double *S_ws;  // [3P]
+  const double *K_ws;  // [3P]: Kxx | Kyy | Kxy
+  const double *C_ws;  // [P][3] (D <= 3 with per-pair sums, see epi3_write_kernel)
   const int64_t *choff, *chx;  // chunk map (ra_chunks.cuh)
   double *rec;         // per-chunk (Q, R[DP]) partials, stride stats_stride(DP)
   const float *x, *y;  // original coordinates
@@ -197,65 +213,27 @@ __device__ __forceinline__ double weight_grad(int wmode, double m, double gat, d
 }
 
 // ---- D <= 3 (packed3): one thread per point --------------------------------
-// Pass 1: per chunk, R = sum dL/dx~ (D values) and Q = sum a dL/da.
-template <int NT>
-__global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
-  __shared__ double sh[(NT / 32) * 4];
-  const ChunkMap M{A.P, A.choff, A.chx};
-  const int rs = stats_stride(A.DP);
-  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
-    const EpiSide E = epi_side(A, p, side);
-    const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
-    const int64_t b = c * kChunk, e = b + kChunk < E.count ? b + kChunk : E.count;
-    double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
-    // software-pipelined: the next point's record is in flight while this
-    // one is summed (same points, same order)
-    PointRec3 cur;
-    if (b + threadIdx.x < e) cur = load_point3(A, side, slot0 + b + threadIdx.x);
-    for (int64_t i = b + threadIdx.x; i < e; i += NT) {
-      PointRec3 nxt;
-      if (i + NT < e) nxt = load_point3(A, side, slot0 + i + NT);
-      double gxt[3], ga, a;
-      point_grads<3>(cur, A.D, E.cs, E.cc, E.k_x, E.m_own, E.m_par, gxt, ga, a);
-#pragma unroll
-      for (int d = 0; d < 3; ++d) R[d] += gxt[d];  // gxt[d >= D] == 0
-      Q += a * ga;
-      cur = nxt;
-    }
-    double *rec = A.rec + v * rs;
-    double vals[4] = {Q, R[0], R[1], R[2]};
-    block_sum_n<4>(vals, sh);
-    if (threadIdx.x == 0) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) rec[k] = vals[k];
-    }
-  });
-}
-
-// Pass 2: per chunk, combine the side's partials (thread-strided over the
-// chunks, fixed-order block sums) and write the gradients of the chunk's
-// points (zeros for the padded tail of a dense row).
+// One pass per chunk: the side's cloud-wide sums R = sum_i dL/dx~_i and
+// Q = sum_i a_i dL/da_i (for the centering and weight-normalisation
+// Jacobians), then the gradients of the chunk's points (zeros for the padded
+// tail of a dense row).  R and Q come from per-pair values of the forward, so
+// no pass over the points has to sum them first: the self block adds nothing
+// to R (sum_ij a_i a_j k_ij (x_i - x_j) = 0), and the cross block adds
+// -cxy C / (c sigma^2) for x and +cxy C / (c sigma^2) for y, with
+// C = sum_ij a_i b_j k_ij (x'_i - y'_j) summed by the tile kernel;
+// Q = sum_i a_i (2 cxx s^xx_i + cxy s^xy_i) = 2 cxx Kxx + cxy Kxy for x
+// (2 cyy Kyy + cxy Kxy for y).
 template <int NT>
 __global__ void __launch_bounds__(NT, 3) epi3_write_kernel(EpilogueArgs A) {
-  __shared__ double sh[(NT / 32) * 4];
   const ChunkMap M{A.P, A.choff, A.chx};
-  const int rs = stats_stride(A.DP);
-  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t first, int64_t n) {
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t, int64_t) {
     const EpiSide E = epi_side(A, p, side);
     const int D = A.D;
-    double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
-    for (int64_t k = threadIdx.x; k < n; k += NT) {
-      const double *r = A.rec + (first + k) * rs;
-      Q += r[0];
-      R[0] += r[1];
-      R[1] += r[2];
-      R[2] += r[3];
-    }
-    double vals[4] = {Q, R[0], R[1], R[2]};
-    block_sum_n<4>(vals, sh);
-    Q = vals[0];
+    double R[3];
+    const double f = (side == 0 ? -1.0 : 1.0) * E.k_x * E.cxy;
 #pragma unroll
-    for (int d = 0; d < 3; ++d) R[d] = vals[1 + d];
+    for (int d = 0; d < 3; ++d) R[d] = d < D ? f * A.C_ws[3 * p + d] : 0.0;
+    const double Q = E.cs * A.K_ws[side * A.P + p] + E.cxy * A.K_ws[2 * A.P + p];
     double Qt = Q;
     if (A.center) {
 #pragma unroll

@@ -78,14 +78,18 @@ struct Tiles3Args {
   const double *meta;                   // per-pair metadata (ra_prep.cuh)
   float *acc_x, *acc_y;                 // [tiles * 64][8]: self (s, G0..G2), cross (s, G0..G2)
   double *itemK, *itemS;
+  double *itemC;                        // [items][3]: x-y items' sum_i a_i G_i (with gradients)
   int shard_index, shard_count;  // this process evaluates items shard_index + k * shard_count
 };
 
 // MODE 0: K only.  MODE 1: K + per-point sums.  MODE 2: also S (sigma grad).
+// MODE 3: as MODE 1 without the columns' weight sums s_j, which only the
+// weight gradients need (one FP32 operation and one shuffle fewer per term).
 template <int MODE>
 struct Tiles3Mode {
   static constexpr bool GRAD = MODE >= 1;
   static constexpr bool SIG = MODE == 2;
+  static constexpr bool CSUM = MODE == 1 || MODE == 2;  // column weight sums
 };
 
 // One column half (32 columns: 8 per ring position) against the lane's 4 row
@@ -124,7 +128,7 @@ __device__ __forceinline__ void t3_half(const ulonglong2 q0, const ulonglong2 q1
     }
     if (COLS) {
       const f2_t wc = RUNI ? k : mul2(Aw[rp], k);  // a_i k_ij for the two rows
-      cs = add2(cs, wc);
+      if (Tiles3Mode<MODE>::CSUM) cs = add2(cs, wc);
       c0 = fma2(wc, dx, c0);
       c1 = fma2(wc, dy, c1);
       c2 = fma2(wc, dz, c2);
@@ -133,8 +137,9 @@ __device__ __forceinline__ void t3_half(const ulonglong2 q0, const ulonglong2 q1
 }
 
 // Pass a half's column sums one position back around the ring.
+template <bool CSUM>
 __device__ __forceinline__ void t3_rotate(f2_t &cs, f2_t &c0, f2_t &c1, f2_t &c2, int src) {
-  cs = __shfl_sync(kFull, cs, src);
+  if (CSUM) cs = __shfl_sync(kFull, cs, src);
   c0 = __shfl_sync(kFull, c0, src);
   c1 = __shfl_sync(kFull, c1, src);
   c2 = __shfl_sync(kFull, c2, src);
@@ -179,10 +184,10 @@ __device__ __forceinline__ void tiles3_coltile(
     const ulonglong2 a00 = cp[0], a01 = cp[kTile], a10 = cp[32], a11 = cp[32 + kTile];
     t3_half<MODE, COLS, FOLD, RUNI>(a00, a01, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[0], c0[0],
                                     c1[0], c2[0]);
-    if (t < 7) t3_rotate(cs[0], c0[0], c1[0], c2[0], src);
+    if (t < 7) t3_rotate<Tiles3Mode<MODE>::CSUM>(cs[0], c0[0], c1[0], c2[0], src);
     t3_half<MODE, COLS, FOLD, RUNI>(a10, a11, X0, X1, X2, Aw, st, G0, G1, G2, sgt, cs[1], c0[1],
                                     c1[1], c2[1]);
-    if (t < 7) t3_rotate(cs[1], c0[1], c1[1], c2[1], src);
+    if (t < 7) t3_rotate<Tiles3Mode<MODE>::CSUM>(cs[1], c0[1], c1[1], c2[1], src);
   }
   {
     // after step 7 this lane holds the sums of position (p + 7) & 7; the
@@ -255,6 +260,7 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
       if (lane == 0) {
         A.itemK[it] = 0.0;
         A.itemS[it] = 0.0;
+        if (GRAD && blk == 0) A.itemC[3 * it] = A.itemC[3 * it + 1] = A.itemC[3 * it + 2] = 0.0;
       }
       continue;
     }
@@ -361,11 +367,34 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     const double kw = warp_sum(kl);
     double sw = 0.0;
     if (SIG) sw = warp_sum(sym ? 2.0 * stot_sig - sd : stot_sig);
+    // K = m_r m_c sum a~_i s~_i
+    const double kscale = meta[meta_wscale(3) + rside] * meta[meta_wscale(3) + cside];
     if (lane == 0) {
-      // K = m_r m_c sum a~_i s~_i
-      const double kscale = meta[meta_wscale(3) + rside] * meta[meta_wscale(3) + cside];
       A.itemK[it] = kw * kscale;
       A.itemS[it] = sw * kscale;
+    }
+    // x-y items: this item's share of C = sum_ij a_i b_j k_ij (x'_i - y'_j),
+    // the one vector the backward needs to sum the gradients of a whole cloud
+    // (the self blocks' share of that sum is zero by antisymmetry)
+    if (GRAD && blk == 0) {
+      double cv[3] = {0.0, 0.0, 0.0};
+#pragma unroll
+      for (int rp = 0; rp < 4; ++rp) {
+        float a_lo, a_hi, g_lo, g_hi;
+        upk(Aw[rp], a_lo, a_hi);
+        upk(G0[rp], g_lo, g_hi);
+        cv[0] = fma((double)a_hi, (double)g_hi, fma((double)a_lo, (double)g_lo, cv[0]));
+        upk(G1[rp], g_lo, g_hi);
+        cv[1] = fma((double)a_hi, (double)g_hi, fma((double)a_lo, (double)g_lo, cv[1]));
+        upk(G2[rp], g_lo, g_hi);
+        cv[2] = fma((double)a_hi, (double)g_hi, fma((double)a_lo, (double)g_lo, cv[2]));
+      }
+#pragma unroll
+      for (int d = 0; d < 3; ++d) cv[d] = warp_sum(cv[d]);
+      if (lane == 0) {
+#pragma unroll
+        for (int d = 0; d < 3; ++d) A.itemC[3 * it + d] = cv[d] * kscale;
+      }
     }
 
     // ---- per-point row sums: combine the 4 rings, then one lane per row ----

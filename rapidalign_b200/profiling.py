@@ -21,7 +21,8 @@ def tiles_time(x: torch.Tensor, y: torch.Tensor, batch_x: torch.Tensor, batch_y:
     ptr_x, P, _ = _ensure_ptr(None, batch_x, x.shape[0], dev)
     ptr_y, _, _ = _ensure_ptr(None, batch_y, y.shape[0], dev)
     spec = Spec(layout=_lib.RA_LAYOUT_RAGGED, num_pairs=P, dim=x.shape[1], num_x=x.shape[0],
-                num_y=y.shape[0], center=center, sigma=sigma, ptr_x=ptr_x, ptr_y=ptr_y)
+                num_y=y.shape[0], center=center, sigma=sigma, ptr_x=ptr_x, ptr_y=ptr_y,
+                skip_weight_sums=True)
     x32, y32 = _f32(x), _f32(y)
     desc = spec.desc(need_grad, False)
     inp = _inputs(x32, y32, None, None, spec)
@@ -54,7 +55,7 @@ def tiles_time_dense(x: torch.Tensor, y: torch.Tensor, mask_x: torch.Tensor,
                 num_x=B * x.shape[1], num_y=B * y.shape[1], nmax_x=x.shape[1],
                 nmax_y=y.shape[1], weights_x=_lib.RA_WEIGHTS_SUM_CLAMPED,
                 weights_y=_lib.RA_WEIGHTS_SUM_CLAMPED, center=center, sigma=sigma,
-                mask_x=mx, mask_y=my)
+                mask_x=mx, mask_y=my, skip_weight_sums=True)
     x32, y32 = _f32(x), _f32(y)
     desc = spec.desc(True, False)
     inp = _inputs(x32, y32, None, None, spec)
@@ -81,7 +82,8 @@ def tiles_time_pair(x: torch.Tensor, y: torch.Tensor, sigma: float, reps: int = 
     dev = x.device
     spec = Spec(layout=_lib.RA_LAYOUT_DENSE, num_pairs=1, dim=x.shape[1], num_x=x.shape[0],
                 num_y=y.shape[0], nmax_x=x.shape[0], nmax_y=y.shape[0], center=center,
-                sigma=sigma, shard_index=shard_index, shard_count=shard_count)
+                sigma=sigma, shard_index=shard_index, shard_count=shard_count,
+                skip_weight_sums=True)
     x32, y32 = _f32(x), _f32(y)
     desc = spec.desc(True, False)
     inp = _inputs(x32, y32, None, None, spec)

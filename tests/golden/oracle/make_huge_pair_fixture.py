@@ -1,7 +1,7 @@
-"""Generate ``tests/golden/huge_pair_262144.npz``: the fp64 oracle's values for
+"""Generate ``tests/golden/oracle/huge_pair_262144.npz``: the fp64 oracle's values for
 the single-pair workload of 262144 points per cloud.
 
-    python tests/golden/make_huge_pair_fixture.py      (a few minutes on 8 cores)
+    python tests/golden/oracle/make_huge_pair_fixture.py      (a few minutes on 8 cores)
 
 The reference cannot evaluate this pair at all: its PyTorch path materialises
 N x M matrices (rapidalign/kde.py:83-101, 275 GB here) and its CUDA kernels
@@ -17,7 +17,8 @@ rapidalign/kde_gradients.py:39-132, with the centering and chain rules of
   fixture megabytes).
 
 The inputs are ``bench.huge_pair_data()`` (seeded), regenerated identically
-by the test, so only results are stored.
+by the test, so only results are stored.  This folder holds fixtures made by
+the oracle; the folder above holds those made by running the reference.
 """
 from __future__ import annotations
 
@@ -28,7 +29,7 @@ import time
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-ROOT = os.path.dirname(os.path.dirname(HERE))
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(HERE)))
 sys.path.insert(0, ROOT)
 
 N_POINTS = 262144

@@ -12,7 +12,7 @@ oracle:
   (``pyg_kde_mmd_loss`` on the tensor-core path);
 * one pair of 262144 points per cloud, D=3, sigma 0.2, centred
   (``kde_mmd_loss``; kde.py:39-109), against values the oracle computed once
-  over the whole pair (``tests/golden/make_huge_pair_fixture.py``): K, the
+  over the whole pair (``tests/golden/oracle/make_huge_pair_fixture.py``): K, the
   loss, and the gradients of 256 seeded rows of each cloud.
 
 Bars (the target's own): losses within 1e-5 relative with no floor, K within
@@ -128,7 +128,7 @@ def test_embeddings_1024_graphs_d128(cuda_device):
 
 def test_huge_pair_262144(cuda_device):
     import rapidalign_b200 as ra
-    path = os.path.join(GOLDEN_DIR, "huge_pair_262144.npz")
+    path = os.path.join(GOLDEN_DIR, "oracle", "huge_pair_262144.npz")
     with np.load(path) as z:
         fix = {k: z[k] for k in z.files}
     dev = cuda_device
