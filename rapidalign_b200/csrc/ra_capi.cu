@@ -51,8 +51,8 @@ struct Layout {
   int64_t max_items;
   int64_t max_tiles_x, max_tiles_y;  // packed3: bound on the padded tiles
   int64_t max_chunks;                // bound on the virtual chunks (ra_chunks.cuh)
-  size_t hdr, seg, meta, cnt, item_off, tbase_x, tbase_y, boff, items, itemK, itemS, itemC, Kws,
-      Sws, Cws, coef, Ktmp, chcnt, chx, choff, rec;
+  size_t hdr, seg, meta, cnt, item_off, tbase_x, tbase_y, boff, items, itemK, itemS, Kws, Sws,
+      coef, Ktmp, chcnt, chx, choff, rec;
   size_t tiles_x, tiles_y, Gx, Gy, Ax, Ay, accX, accY;
   size_t acc_x_bytes, acc_y_bytes;
   size_t total;
@@ -60,7 +60,7 @@ struct Layout {
 
 // header block: int err @0, unsigned ticket @4, int has_state @8, int64 n_items @16
 constexpr size_t kHdrErr = 0, kHdrTicket = 4, kHdrState = 8, kHdrNItems = 16;
-constexpr int kItemF64 = 5;  // fp64 partials per work item: K, S, C[3]
+constexpr int kItemF64 = 2;  // fp64 partials per work item: K, S
 
 bool desc_ok(const ra_kde_desc *d) {
   if (d == nullptr) return false;
@@ -132,14 +132,12 @@ Layout make_layout(const ra_kde_desc *d) {
   L.tbase_y = take(sizeof(int64_t) * (P1 + 1));
   L.boff = take(sizeof(int64_t) * 4 * P1);
   L.items = take(sizeof(Item) * (size_t)L.max_items);
-  // itemK, itemS and itemC ([items][3]) form one contiguous fp64 region of
-  // kItemF64 values per item (reduced across shards)
+  // itemK and itemS form one contiguous fp64 region of kItemF64 values per
+  // item (reduced across shards)
   L.itemK = take(sizeof(double) * kItemF64 * (size_t)L.max_items);
   L.itemS = L.itemK + sizeof(double) * (size_t)L.max_items;
-  L.itemC = L.itemS + sizeof(double) * (size_t)L.max_items;
   L.Kws = take(sizeof(double) * 3 * P1);
   L.Sws = take(sizeof(double) * 3 * P1);
-  L.Cws = take(sizeof(double) * 3 * P1);
   L.coef = take(sizeof(double) * 3 * P1);
   L.Ktmp = take(sizeof(double) * 3 * P1);
   L.chcnt = take(sizeof(int64_t) * P1);
@@ -311,6 +309,13 @@ int launch_tilesg(int DP, int mode, int64_t grid, const TilesGArgs &T, cudaStrea
 int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy, double *Kxy,
                 void *ws, cudaStream_t st);
 
+// Whether a pair may have more than kSmallPts points on a side (the D <= 3
+// layout's chunked passes are launched only then; they skip small pairs).
+bool may_have_large_pairs(const ra_kde_desc *d) {
+  return d->layout == RA_LAYOUT_DENSE ? (d->nmax_x > kSmallPts || d->nmax_y > kSmallPts)
+                                      : (d->num_x > kSmallPts || d->num_y > kSmallPts);
+}
+
 int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, double *Kyy,
                  double *Kxy, void *ws, size_t ws_bytes, cudaStream_t st,
                  cudaEvent_t ev0 = nullptr, cudaEvent_t ev1 = nullptr) {
@@ -375,60 +380,12 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     pa.Ax = at<float>(ws, L.Ax);
     pa.Ay = at<float>(ws, L.Ay);
   }
-  const unsigned cgrid = chunk_grid(L);
-  segment_kernel<<<1, 1024, 0, st>>>(pa);
-  if (L.packed3)
-    stats3_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
-  else if (L.DP == 32)
-    statsw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
-  else if (L.DP == 64)
-    statsw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
-  else if (L.DP == 128)
-    statsw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
-  else if (L.DP == 256)
-    statsw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
-  else
-    stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
-  meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
-  g_launches += 3;
-  if (!L.packed3) {
-    if (d->dim % 4 == 0 && L.DP == 32)
-      packgw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
-    else if (d->dim % 4 == 0 && L.DP == 64)
-      packgw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
-    else if (d->dim % 4 == 0 && L.DP == 128)
-      packgw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
-    else if (d->dim % 4 == 0 && L.DP == 256)
-      packgw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
-    else
-      packg_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
-    ++g_launches;
-  }
-  if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
-
-  // ---- plan ----
-  PlanArgs pl;
-  pl.P = P;
-  pl.generic = L.packed3 ? 0 : 1;
-  pl.seg = at<Seg>(ws, L.seg);
-  pl.cnt = at<int64_t>(ws, L.cnt);
-  pl.boff = at<int64_t>(ws, L.boff);
-  pl.item_off = at<int64_t>(ws, L.item_off);
-  pl.tbase_x = at<int64_t>(ws, L.tbase_x);
-  pl.tbase_y = at<int64_t>(ws, L.tbase_y);
-  pl.n_items = at<int64_t>(ws, L.hdr + kHdrNItems);
-  pl.items = at<Item>(ws, L.items);
-  pl.max_items = L.max_items;
-  plan_count_kernel<<<(unsigned)ceil_div(P, 256), 256, 0, st>>>(pl);
-  plan_scan_kernel<<<1, 1024, 0, st>>>(pl);
-  plan_emit_kernel<<<(unsigned)P, 256, 0, st>>>(pl);
-  g_launches += 3;
-  if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
-
-  // ---- pack the D <= 3 tile layout (needs the tile bases of all pairs) ----
+  PackArgs pk;
+  std::memset(&pk, 0, sizeof(pk));
   if (L.packed3) {
-    PackArgs pk;
-    std::memset(&pk, 0, sizeof(pk));
+    pa.tcnt = at<int64_t>(ws, L.cnt) + P;  // free until the plan counts items
+    pa.tbase_x = at<int64_t>(ws, L.tbase_x);
+    pa.tbase_y = at<int64_t>(ws, L.tbase_y);
     pk.P = P;
     pk.D = d->dim;
     pk.nq = L.nq;
@@ -454,6 +411,68 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     pk.tiles_y = at<ulonglong2>(ws, L.tiles_y);
     pk.aw_x = at<float>(ws, L.Ax);
     pk.aw_y = at<float>(ws, L.Ay);
+  }
+  const unsigned cgrid = chunk_grid(L);
+  segment_kernel<<<1, 1024, 0, st>>>(pa);
+  ++g_launches;
+  // D <= 3: pairs with at most kSmallPts points per side are prepared by one
+  // CTA each (sums, metadata, packing); the chunked passes below take the rest
+  // and are launched only when a pair can be larger
+  const bool may_be_large = may_have_large_pairs(d);
+  if (L.packed3) {
+    prep3_kernel<kPrepThreads>
+        <<<(unsigned)(P < (int64_t)cgrid ? P : (int64_t)cgrid), kPrepThreads, 0, st>>>(pa, pk);
+    ++g_launches;
+    if (may_be_large) {
+      stats3_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+      meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
+      g_launches += 2;
+    }
+  } else {
+    if (L.DP == 32)
+      statsw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.DP == 64)
+      statsw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.DP == 128)
+      statsw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.DP == 256)
+      statsw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
+    else
+      stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+    meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
+    if (d->dim % 4 == 0 && L.DP == 32)
+      packgw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
+    else if (d->dim % 4 == 0 && L.DP == 64)
+      packgw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
+    else if (d->dim % 4 == 0 && L.DP == 128)
+      packgw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
+    else if (d->dim % 4 == 0 && L.DP == 256)
+      packgw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
+    else
+      packg_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+    g_launches += 3;
+  }
+  if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
+
+  // ---- plan ----
+  PlanArgs pl;
+  pl.P = P;
+  pl.generic = L.packed3 ? 0 : 1;
+  pl.seg = at<Seg>(ws, L.seg);
+  pl.cnt = at<int64_t>(ws, L.cnt);
+  pl.boff = at<int64_t>(ws, L.boff);
+  pl.item_off = at<int64_t>(ws, L.item_off);
+  pl.n_items = at<int64_t>(ws, L.hdr + kHdrNItems);
+  pl.items = at<Item>(ws, L.items);
+  pl.max_items = L.max_items;
+  plan_count_kernel<<<(unsigned)ceil_div(P, 256), 256, 0, st>>>(pl);
+  plan_scan_kernel<<<1, 1024, 0, st>>>(pl);
+  plan_emit_kernel<<<(unsigned)P, 256, 0, st>>>(pl);
+  g_launches += 3;
+  if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
+
+  // ---- pack the large pairs' D <= 3 tiles (their metadata is complete) ----
+  if (L.packed3 && may_be_large) {
     pack3_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pk);
     ++g_launches;
     if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
@@ -485,7 +504,6 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.acc_y = grad ? at<float>(ws, L.accY) : nullptr;
     T.itemK = at<double>(ws, L.itemK);
     T.itemS = at<double>(ws, L.itemS);
-    T.itemC = at<double>(ws, L.itemC);
     T.shard_index = sh_idx;
     T.shard_count = sh_cnt;
     rc = launch_tiles3(mode, T, st);
@@ -532,10 +550,8 @@ int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy,
   fa.boff = at<int64_t>(ws, L.boff);
   fa.itemK = at<double>(ws, L.itemK);
   fa.itemS = at<double>(ws, L.itemS);
-  fa.itemC = (grad && L.packed3) ? at<double>(ws, L.itemC) : nullptr;
   fa.K_ws = at<double>(ws, L.Kws);
   fa.S_ws = at<double>(ws, L.Sws);
-  fa.C_ws = at<double>(ws, L.Cws);
   // the caller's three K arrays are written by the kernel itself
   fa.K_out[0] = Kxx;
   fa.K_out[1] = Kyy;
@@ -576,8 +592,6 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.meta = at<double>(ws, L.meta);
   ea.coef = coef;
   ea.S_ws = at<double>(ws, L.Sws);
-  ea.K_ws = at<double>(ws, L.Kws);
-  ea.C_ws = at<double>(ws, L.Cws);
   ea.choff = at<int64_t>(ws, L.choff);
   ea.chx = at<int64_t>(ws, L.chx);
   ea.rec = at<double>(ws, L.rec);
@@ -609,9 +623,15 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.grad_sigma = gr->grad_sigma;
   const unsigned cgrid = chunk_grid(L);
   if (L.packed3) {
-    // one pass: the cloud-wide sums come from the forward's per-pair K and C
-    epi3_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+    // small pairs: one CTA per pair (both passes); large pairs: chunked passes
+    epi3_small_kernel<kEpiThreads>
+        <<<(unsigned)(P < (int64_t)cgrid ? P : (int64_t)cgrid), kEpiThreads, 0, st>>>(ea);
     ++g_launches;
+    if (may_have_large_pairs(d)) {
+      epi3_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+      epi3_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+      g_launches += 2;
+    }
   } else if (L.DP >= 32) {
     switch (L.DP) {
       case 32:

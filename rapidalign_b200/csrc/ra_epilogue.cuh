@@ -25,11 +25,9 @@ struct FinalizeArgs {
   const int64_t *item_off;
   const int64_t *boff;
   const double *itemK, *itemS;
-  const double *itemC;  // [items][3] of the x-y items, or null (D <= 3 with gradients only)
   double *K_out[3];  // caller's Kxx, Kyy, Kxy ([P] each)
   double *K_ws;   // [3P] copy kept in the workspace
   double *S_ws;   // [3P]
-  double *C_ws;   // [P][3]: C = sum_ij a_i b_j k_ij (x'_i - y'_j) (when itemC is set)
   int *state;     // set to 1 when not null
 };
 
@@ -74,18 +72,6 @@ __global__ void __launch_bounds__(NT) finalize_kernel(FinalizeArgs A) {
       A.K_ws[kidx[b] * A.P + p] = kt;
       A.S_ws[kidx[b] * A.P + p] = st;
     }
-    if (b == 0 && A.itemC != nullptr) {
-      double c[3] = {0.0, 0.0, 0.0};
-      for (int64_t j = b0 + threadIdx.x; j < e; j += NT) {
-#pragma unroll
-        for (int d = 0; d < 3; ++d) c[d] += A.itemC[3 * j + d];
-      }
-#pragma unroll
-      for (int d = 0; d < 3; ++d) {
-        const double ct = block_sum(c[d], sh);
-        if (threadIdx.x == 0) A.C_ws[3 * p + d] = ct;
-      }
-    }
   }
 }
 
@@ -101,8 +87,6 @@ struct EpilogueArgs {
   const double *meta;
   const double *coef;  // [3P]: dL/dKxx | dL/dKyy | dL/dKxy
   const double *S_ws;  // [3P]
-  const double *K_ws;  // [3P]: Kxx | Kyy | Kxy
-  const double *C_ws;  // [P][3] (D <= 3 with per-pair sums, see epi3_write_kernel)
   const int64_t *choff, *chx;  // chunk map (ra_chunks.cuh)
   double *rec;         // per-chunk (Q, R[DP]) partials, stride stats_stride(DP)
   const float *x, *y;  // original coordinates
@@ -213,75 +197,157 @@ __device__ __forceinline__ double weight_grad(int wmode, double m, double gat, d
 }
 
 // ---- D <= 3 (packed3): one thread per point --------------------------------
-// One pass per chunk: the side's cloud-wide sums R = sum_i dL/dx~_i and
-// Q = sum_i a_i dL/da_i (for the centering and weight-normalisation
-// Jacobians), then the gradients of the chunk's points (zeros for the padded
-// tail of a dense row).  R and Q come from per-pair values of the forward, so
-// no pass over the points has to sum them first: the self block adds nothing
-// to R (sum_ij a_i a_j k_ij (x_i - x_j) = 0), and the cross block adds
-// -cxy C / (c sigma^2) for x and +cxy C / (c sigma^2) for y, with
-// C = sum_ij a_i b_j k_ij (x'_i - y'_j) summed by the tile kernel;
-// Q = sum_i a_i (2 cxx s^xx_i + cxy s^xy_i) = 2 cxx Kxx + cxy Kxy for x
-// (2 cyy Kyy + cxy Kxy for y).
-template <int NT>
-__global__ void __launch_bounds__(NT, 3) epi3_write_kernel(EpilogueArgs A) {
-  const ChunkMap M{A.P, A.choff, A.chx};
-  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t, int64_t) {
-    const EpiSide E = epi_side(A, p, side);
-    const int D = A.D;
-    double R[3];
-    const double f = (side == 0 ? -1.0 : 1.0) * E.k_x * E.cxy;
+// The cloud-wide sums of one side that the Jacobians need, over points
+// [b, e) of the side: R += dL/dx~_i (D values), Q += a_i dL/da_i.  The next
+// point's record is in flight while this one is summed.
+__device__ __forceinline__ void epi3_sum_points(const EpilogueArgs &A, const EpiSide &E, int side,
+                                                int64_t slot0, int64_t b, int64_t e, int stride,
+                                                double (&R)[3], double &Q) {
+  PointRec3 cur;
+  if (b < e) cur = load_point3(A, side, slot0 + b);
+  for (int64_t i = b; i < e; i += stride) {
+    PointRec3 nxt;
+    if (i + stride < e) nxt = load_point3(A, side, slot0 + i + stride);
+    double gxt[3], ga, a;
+    point_grads<3>(cur, A.D, E.cs, E.cc, E.k_x, E.m_own, E.m_par, gxt, ga, a);
 #pragma unroll
-    for (int d = 0; d < 3; ++d) R[d] = d < D ? f * A.C_ws[3 * p + d] : 0.0;
-    const double Q = E.cs * A.K_ws[side * A.P + p] + E.cxy * A.K_ws[2 * A.P + p];
-    double Qt = Q;
-    if (A.center) {
-#pragma unroll
-      for (int d = 0; d < 3; ++d)
-        if (d < D) Qt -= E.mu[d] * R[d];
-    }
+    for (int d = 0; d < 3; ++d) R[d] += gxt[d];  // gxt[d >= D] == 0
+    Q += a * ga;
+    cur = nxt;
+  }
+}
 
-    const float *pts = side == 0 ? A.x : A.y;
-    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
-    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-    float *gout = side == 0 ? A.grad_x : A.grad_y;
-    double *wout = side == 0 ? A.grad_wx : A.grad_wy;
+// Gradients of points [b, e) of one side (zeros for the padded tail of a
+// dense row, i >= count), given the side's totals R and Qt = Q - mu . R.
+__device__ __forceinline__ void epi3_write_points(const EpilogueArgs &A, const EpiSide &E,
+                                                  int side, int64_t slot0, int64_t b, int64_t e,
+                                                  int stride, const double (&R)[3], double Qt) {
+  const int D = A.D;
+  const float *pts = side == 0 ? A.x : A.y;
+  const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+  const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+  float *gout = side == 0 ? A.grad_x : A.grad_y;
+  double *wout = side == 0 ? A.grad_wx : A.grad_wy;
+  // the next point's record is loaded before this point's stores (which
+  // might alias it as far as the compiler knows)
+  PointRec3 cur;
+  if (b < e && b < E.count) cur = load_point3(A, side, slot0 + b);
+  for (int64_t i = b; i < e; i += stride) {
+    PointRec3 nxt;
+    if (i + stride < e && i + stride < E.count) nxt = load_point3(A, side, slot0 + i + stride);
+    const int64_t g = E.s + i;
+    double gxt[3] = {0.0, 0.0, 0.0}, ga = 0.0, a = 0.0;
+    const bool live = i < E.count;
+    if (live) point_grads<3>(cur, D, E.cs, E.cc, E.k_x, E.m_own, E.m_par, gxt, ga, a);
+    cur = nxt;
+    if (gout != nullptr) {
+#pragma unroll
+      for (int d = 0; d < 3; ++d) {
+        if (d >= D) break;
+        double val = gxt[d];
+        if (A.center && live) val -= a * R[d];
+        gout[g * D + d] = (float)val;
+      }
+    }
+    if (wout != nullptr && wmode != 3) {
+      double gat = ga;
+      if (A.center && live) {
+#pragma unroll
+        for (int d = 0; d < 3; ++d)
+          if (d < D) gat -= (double)pts[g * D + d] * R[d];
+      }
+      const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
+      wout[g] = live ? weight_grad(wmode, m, gat, Qt, E) : 0.0;
+    }
+  }
+}
+
+__device__ __forceinline__ double epi3_qt(const EpilogueArgs &A, const EpiSide &E, double Q,
+                                          const double (&R)[3]) {
+  double Qt = Q;
+  if (A.center) {
+#pragma unroll
+    for (int d = 0; d < 3; ++d)
+      if (d < A.D) Qt -= E.mu[d] * R[d];
+  }
+  return Qt;
+}
+
+// ---- D <= 3, pairs with more than kSmallPts points on a side: two chunked
+// passes, so that one pair spreads over many CTAs.
+// Pass 1: per chunk, R = sum dL/dx~ (D values) and Q = sum a dL/da.
+template <int NT>
+__global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
+  __shared__ double sh[(NT / 32) * 4];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int rs = stats_stride(A.DP);
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
+    if (small_pair(A.seg[p])) return;  // epi3_small_kernel
+    const EpiSide E = epi_side(A, p, side);
     const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
-    const int64_t b = c * kChunk, e = b + kChunk < E.span ? b + kChunk : E.span;
-    // software-pipelined: the next point's record is loaded before this
-    // point's stores (which might alias it as far as the compiler knows)
-    PointRec3 cur;
-    if (b + threadIdx.x < e && b + threadIdx.x < E.count)
-      cur = load_point3(A, side, slot0 + b + threadIdx.x);
-    for (int64_t i = b + threadIdx.x; i < e; i += NT) {
-      PointRec3 nxt;
-      if (i + NT < e && i + NT < E.count) nxt = load_point3(A, side, slot0 + i + NT);
-      const int64_t g = E.s + i;
-      double gxt[3] = {0.0, 0.0, 0.0}, ga = 0.0, a = 0.0;
-      const bool live = i < E.count;
-      if (live) point_grads<3>(cur, D, E.cs, E.cc, E.k_x, E.m_own, E.m_par, gxt, ga, a);
-      cur = nxt;
-      if (gout != nullptr) {
+    const int64_t b = c * kChunk, e = b + kChunk < E.count ? b + kChunk : E.count;
+    double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
+    epi3_sum_points(A, E, side, slot0, b + threadIdx.x, e, NT, R, Q);
+    double *rec = A.rec + v * rs;
+    double vals[4] = {Q, R[0], R[1], R[2]};
+    block_sum_n<4>(vals, sh);
+    if (threadIdx.x == 0) {
 #pragma unroll
-        for (int d = 0; d < 3; ++d) {
-          if (d >= D) break;
-          double val = gxt[d];
-          if (A.center && live) val -= a * R[d];
-          gout[g * D + d] = (float)val;
-        }
-      }
-      if (wout != nullptr && wmode != 3) {
-        double gat = ga;
-        if (A.center && live) {
-#pragma unroll
-          for (int d = 0; d < 3; ++d)
-            if (d < D) gat -= (double)pts[g * D + d] * R[d];
-        }
-        const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
-        wout[g] = live ? weight_grad(wmode, m, gat, Qt, E) : 0.0;
-      }
+      for (int k = 0; k < 4; ++k) rec[k] = vals[k];
     }
   });
+}
+
+// Pass 2: per chunk, combine the side's partials (thread-strided over the
+// chunks, fixed-order block sums) and write the gradients of the chunk's points.
+template <int NT>
+__global__ void __launch_bounds__(NT, 3) epi3_write_kernel(EpilogueArgs A) {
+  __shared__ double sh[(NT / 32) * 4];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int rs = stats_stride(A.DP);
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t first, int64_t n) {
+    if (small_pair(A.seg[p])) return;  // epi3_small_kernel
+    const EpiSide E = epi_side(A, p, side);
+    double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
+    for (int64_t k = threadIdx.x; k < n; k += NT) {
+      const double *r = A.rec + (first + k) * rs;
+      Q += r[0];
+      R[0] += r[1];
+      R[1] += r[2];
+      R[2] += r[3];
+    }
+    double vals[4] = {Q, R[0], R[1], R[2]};
+    block_sum_n<4>(vals, sh);
+    Q = vals[0];
+#pragma unroll
+    for (int d = 0; d < 3; ++d) R[d] = vals[1 + d];
+    const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
+    const int64_t b = c * kChunk, e = b + kChunk < E.span ? b + kChunk : E.span;
+    epi3_write_points(A, E, side, slot0, b + threadIdx.x, e, NT, R, epi3_qt(A, E, Q, R));
+  });
+}
+
+// ---- D <= 3, pairs with at most kSmallPts points per side (small_pair): one
+// CTA per pair and side sums R and Q over the side's points, then writes
+// their gradients (the records are re-read from cache), in one launch.
+template <int NT>
+__global__ void __launch_bounds__(NT, 3) epi3_small_kernel(EpilogueArgs A) {
+  __shared__ double sh[(NT / 32) * 4];
+  for (int64_t p = blockIdx.x; p < A.P; p += gridDim.x) {
+    if (!small_pair(A.seg[p])) continue;
+    for (int side = 0; side < 2; ++side) {
+      const EpiSide E = epi_side(A, p, side);
+      const int64_t slot0 = (side == 0 ? A.tbase_x : A.tbase_y)[p] * kTile;
+      double R[3] = {0.0, 0.0, 0.0}, Q = 0.0;
+      epi3_sum_points(A, E, side, slot0, threadIdx.x, E.count, NT, R, Q);
+      double vals[4] = {Q, R[0], R[1], R[2]};
+      block_sum_n<4>(vals, sh);
+      Q = vals[0];
+#pragma unroll
+      for (int d = 0; d < 3; ++d) R[d] = vals[1 + d];
+      epi3_write_points(A, E, side, slot0, threadIdx.x, E.span, NT, R, epi3_qt(A, E, Q, R));
+    }
+  }
 }
 
 // ---- generic D: RW = DP threads per point (one per dimension) -------------

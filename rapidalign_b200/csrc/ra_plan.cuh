@@ -11,11 +11,9 @@ struct PlanArgs {
   int64_t P;
   int generic;        // 0: D <= 3 tiles (3 blocks), 1: generic rows (4 orientations)
   const Seg *seg;
-  int64_t *cnt;       // [3][P]: items, x tiles, y tiles of pair p
+  int64_t *cnt;       // [P]: items of pair p
   int64_t *boff;      // [P * 4]: local start of each block inside the pair's items
   int64_t *item_off;  // [P + 1]
-  int64_t *tbase_x;   // [P + 1]: first x tile of each pair (D <= 3 tile layout)
-  int64_t *tbase_y;   // [P + 1]
   int64_t *n_items;   // device scalar (== item_off[P])
   Item *items;
   int64_t max_items;  // capacity of `items` (the host bound)
@@ -49,20 +47,17 @@ __global__ void plan_count_kernel(PlanArgs A) {
   A.boff[p * 4 + 2] = c[0] + c[1];
   A.boff[p * 4 + 3] = c[0] + c[1] + c[2];
   A.cnt[p] = c[0] + c[1] + c[2] + c[3];
-  const Seg &sg = A.seg[p];
-  A.cnt[A.P + p] = ceil_div(sg.xcount, (int64_t)kTile);
-  A.cnt[2 * A.P + p] = ceil_div(sg.ycount, (int64_t)kTile);
 }
 
-// Exclusive scans of the three per-pair counts (items, x tiles, y tiles) into
-// item_off, tbase_x and tbase_y (each [P + 1]); one CTA of 1024 threads.
+// Exclusive scan of the per-pair item counts into item_off ([P + 1]); one
+// CTA of 1024 threads.  (The D <= 3 tile bases are scanned by segment_kernel.)
 __global__ void __launch_bounds__(1024) plan_scan_kernel(PlanArgs A) {
   __shared__ int64_t warp_tot[32];
   __shared__ int64_t carry_sh;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  for (int arr = 0; arr < 3; ++arr) {
-    const int64_t *src = A.cnt + arr * A.P;
-    int64_t *dst = arr == 0 ? A.item_off : (arr == 1 ? A.tbase_x : A.tbase_y);
+  {
+    const int64_t *src = A.cnt;
+    int64_t *dst = A.item_off;
     if (tid == 0) carry_sh = 0;
     __syncthreads();
     for (int64_t base = 0; base < A.P; base += 1024) {
@@ -94,13 +89,10 @@ __global__ void __launch_bounds__(1024) plan_scan_kernel(PlanArgs A) {
     }
     if (tid == 0) {
       int64_t tot = carry_sh;
-      if (arr == 0) {
-        if (tot > A.max_items) tot = A.max_items;  // cannot happen with the host bound
-        *A.n_items = tot;
-      }
+      if (tot > A.max_items) tot = A.max_items;  // cannot happen with the host bound
+      *A.n_items = tot;
       dst[A.P] = tot;
     }
-    __syncthreads();
   }
 }
 

@@ -54,6 +54,15 @@ __host__ __device__ __forceinline__ int red_width(int D) {
   return r;
 }
 
+// D <= 3: a pair with at most kSmallPts points on each side (span) is
+// prepared by one CTA of prep3_kernel (sums, metadata and packing in one
+// pass over its points); larger pairs take the chunked passes stats3_kernel,
+// meta_kernel and pack3_kernel, which spread one pair over many CTAs.
+constexpr int64_t kSmallPts = 4096;
+__host__ __device__ __forceinline__ bool small_pair(const Seg &s) {
+  return s.xspan <= kSmallPts && s.yspan <= kSmallPts;
+}
+
 struct PrepArgs {
   int64_t P;
   int D, DP;     // DP: 3 for the D <= 3 path, else the padded generic width
@@ -70,6 +79,8 @@ struct PrepArgs {
   double *meta;
   double *rec;    // [chunk_cap][stats_stride]
   int64_t *chcnt, *chx, *choff;  // [P], [P], [P + 1]
+  int64_t *tcnt;                 // [2P] scratch: 64-point tiles of each side (D <= 3)
+  int64_t *tbase_x, *tbase_y;    // [P + 1]: first tile of each pair's cloud (D <= 3)
   int *err;
   int allow_fold;  // D <= 3: weights may be folded into the exponent (no sigma gradient)
   // generic layout (D >= 4): coords [num * DP] (zero padded) and weights [num]
@@ -136,11 +147,18 @@ __global__ void __launch_bounds__(1024) segment_kernel(PrepArgs A) {
         sg.yspan = span;
         A.chcnt[p] = A.chx[p] + ceil_div(span, (int64_t)kChunk);
       }
+      // D <= 3 tile layout: room for the whole span (a dense row's count,
+      // 1 + its last valid index, is known only after the sums)
+      if (A.tcnt != nullptr) A.tcnt[side * A.P + p] = ceil_div(span, (int64_t)kTile);
     }
     __syncthreads();
   }
   if (e) atomicOr(A.err, e);
   block_exclusive_scan(A.chcnt, A.choff, A.P, A.chunk_cap, warp_tot, &carry);
+  if (A.tcnt != nullptr) {
+    block_exclusive_scan(A.tcnt, A.tbase_x, A.P, INT64_MAX, warp_tot, &carry);
+    block_exclusive_scan(A.tcnt + A.P, A.tbase_y, A.P, INT64_MAX, warp_tot, &carry);
+  }
 }
 
 // Pass 1: per-chunk partial sums of weights and coordinates.
@@ -242,6 +260,7 @@ __global__ void __launch_bounds__(NT) stats3_kernel(PrepArgs A) {
     const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
     const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
     const Seg sg = A.seg[p];
+    if (small_pair(sg)) return;  // prepared by prep3_kernel
     const int64_t s = side == 0 ? sg.xs : sg.ys;
     const int64_t span = side == 0 ? sg.xspan : sg.yspan;
     const int64_t b = c * kChunk, e = b + kChunk < span ? b + kChunk : span;
@@ -378,6 +397,38 @@ __device__ __forceinline__ double warp_max(double v) {
   return v;
 }
 
+// Normaliser of one side's weights (kde.py:20-27, 115-121, 169-199) and,
+// for the D <= 3 layout, whether they fold into the exponent: when they are
+// all >= 0, k' = 2^(-(r^2 - log2(a / m))) = (a / m) k with m the largest
+// normalised weight.  W: sum of the effective weights, nv: valid points,
+// count: points the kernels visit, wmax / nwmin: largest weight and largest
+// negated weight.  werr: a SUM-normalised side with points sums to <= 0 (the
+// normaliser is then 1, which keeps the kernels finite; the error is
+// reported).
+__device__ __forceinline__ void side_normaliser(int wmode, double W, double nv, int64_t count,
+                                                bool may_fold, double wmax, double nwmin,
+                                                double &Wn, double &m, double &fold,
+                                                bool &werr) {
+  werr = false;
+  if (wmode == 0) {
+    Wn = 1.0;  // raw weights
+  } else if (wmode == 3) {
+    Wn = nv > 0 ? nv : 1.0;  // uniform 1/count
+  } else if (wmode == 2) {
+    Wn = W > 1e-8 ? W : 1e-8;  // clamp_min(1e-8)
+  } else {
+    Wn = W;
+    werr = count > 0 && !(W > 0.0) && !(W != W);
+    if (!(W > 0.0)) Wn = 1.0;
+  }
+  m = 1.0;
+  fold = 0.0;
+  if (may_fold && -nwmin >= 0.0 && wmax > 0.0 && Wn > 0.0 && wmax / Wn < INFINITY) {
+    m = wmax / Wn;
+    fold = -nwmin == wmax ? 2.0 : 1.0;
+  }
+}
+
 // Pass 2: one warp per pair combines its chunk records into the segment
 // bounds and normalisers (lane-strided over the chunks, then a fixed shuffle
 // tree) and the centroids and anchors (one lane per coordinate, the chunks in
@@ -387,6 +438,7 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
   const int lane = threadIdx.x & 31;
   if (p >= A.P) return;
   const int D = A.D, DP = A.DP;
+  if (DP == 3 && small_pair(A.seg[p])) return;  // prepared by prep3_kernel
   if (A.sigma_p != nullptr && lane == 0 && !(A.sigma_p[p] > 0.0)) atomicOr(A.err, (int)kErrSigma);
   const int rs = stats_stride(DP);
   double *meta = A.meta + p * meta_stride(DP);
@@ -410,34 +462,19 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
     const int64_t span = side == 0 ? A.seg[p].xspan : A.seg[p].yspan;
     const int64_t count = A.layout == 0 ? span : (int64_t)lst + 1;
     const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-    double Wn;
-    if (wmode == 0) {
-      Wn = 1.0;  // raw weights
-    } else if (wmode == 3) {
-      Wn = nv > 0 ? nv : 1.0;  // uniform 1/count
-    } else if (wmode == 2) {
-      Wn = W > 1e-8 ? W : 1e-8;  // clamp_min(1e-8)
-    } else {
-      Wn = W;
-      if (lane == 0 && count > 0 && !(W > 0.0) && !(W != W)) atomicOr(A.err, (int)kErrWeightSum);
-      if (!(W > 0.0)) Wn = 1.0;  // keep the kernels finite; the error is reported
-    }
-    // D <= 3: fold the weights into the exponent when they are all >= 0
-    // (k' = 2^(-(r^2 - log2(a / m))) = (a / m) k, m the largest weight)
-    double m = 1.0, fold = 0.0;
+    double wmax = -INFINITY, nwmin = -INFINITY;
     if (DP == 3) {
-      double wmax = -INFINITY, nwmin = -INFINITY;
       for (int64_t c = lane; c < n; c += 32) {
         wmax = fmax(wmax, r0[c * rs + 9]);
         nwmin = fmax(nwmin, -r0[c * rs + 10]);
       }
       wmax = warp_fmax(wmax);
       nwmin = warp_fmax(nwmin);
-      if (A.allow_fold && -nwmin >= 0.0 && wmax > 0.0 && Wn > 0.0 && wmax / Wn < INFINITY) {
-        m = wmax / Wn;
-        fold = -nwmin == wmax ? 2.0 : 1.0;
-      }
     }
+    double Wn, m, fold;
+    bool werr;
+    side_normaliser(wmode, W, nv, count, DP == 3 && A.allow_fold, wmax, nwmin, Wn, m, fold, werr);
+    if (lane == 0 && werr) atomicOr(A.err, (int)kErrWeightSum);
     if (lane == 0) {
       meta[side] = Wn;
       meta[2 + side] = W;
@@ -609,58 +646,242 @@ struct PackArgs {
   float *aw_x, *aw_y;                // [tiles * 64] a~ per slot
 };
 
+// Per-side constants of the D <= 3 packing (from the pair's metadata).
+struct Pack3Side {
+  int64_t s, count, t0, npad;
+  const float *pts, *w;
+  const uint8_t *mask;
+  int wmode;
+  ulonglong2 *tiles;
+  float *aw;
+  double Wm;  // a~ = w' / Wm
+  bool fold, uni;
+  float pad, ax, ay, az, scale;
+};
+
+__device__ __forceinline__ Pack3Side pack3_side(const PackArgs &A, int64_t p, int side,
+                                                const Seg &sg) {
+  Pack3Side S;
+  S.s = side == 0 ? sg.xs : sg.ys;
+  S.count = side == 0 ? sg.xcount : sg.ycount;
+  S.t0 = (side == 0 ? A.tbase_x : A.tbase_y)[p];
+  const int64_t t1 = (side == 0 ? A.tbase_x : A.tbase_y)[p + 1];
+  // the tiles the kernels read: ceil(count / 64), within the room reserved
+  const int64_t nt = ceil_div(S.count, (int64_t)kTile);
+  S.npad = (nt < t1 - S.t0 ? nt : t1 - S.t0) * kTile;
+  S.pts = side == 0 ? A.x : A.y;
+  S.w = side == 0 ? A.w_x : A.w_y;
+  S.mask = side == 0 ? A.mask_x : A.mask_y;
+  S.wmode = side == 0 ? A.wmode_x : A.wmode_y;
+  S.tiles = side == 0 ? A.tiles_x : A.tiles_y;
+  S.aw = side == 0 ? A.aw_x : A.aw_y;
+  const double *meta = A.meta + p * meta_stride(3);
+  S.Wm = meta[side] * meta[meta_wscale(3) + side];
+  S.fold = meta[meta_fold(3) + side] != 0.0;
+  S.uni = meta[meta_fold(3) + side] == 2.0;
+  S.pad = S.uni ? 1e18f : 0.f;
+  S.ax = (float)meta[4 + (2 + side) * 3 + 0];
+  S.ay = (float)meta[4 + (2 + side) * 3 + 1];
+  S.az = (float)meta[4 + (2 + side) * 3 + 2];
+  S.scale = pair_scale(A.scale, A.sigma_p, p);
+  return S;
+}
+
+// Slot i (< S.npad) of a side's tiles: a point (i < count) or padding.
+__device__ __forceinline__ void pack3_slot(const PackArgs &A, const Pack3Side &S, int64_t i) {
+  const int D = A.D;
+  float c0 = S.pad, c1 = S.pad, c2 = S.pad, a = 0.f, v = S.fold ? INFINITY : 0.f;
+  if (i < S.count) {
+    const int64_t g = S.s + i;
+    const double at = S.uni ? 1.0 : (double)eff_weight(S.w, S.mask, S.wmode, g) / S.Wm;
+    a = (float)at;
+    c1 = c2 = 0.f;
+    // folded: a~ in [0, 1]; a zero weight becomes 2^-64, which leaves the
+    // other points' sums unchanged to 5e-20 and keeps the point's own
+    // row sums (its weight gradient) finite
+    v = S.fold ? (at >= 1.0 ? 0.f : at > 0x1p-64 ? (float)-log2(at) : 64.f) : a;
+    c0 = S.scale * (S.pts[g * D + 0] - S.ax);
+    if (D > 1) c1 = S.scale * (S.pts[g * D + 1] - S.ay);
+    if (D > 2) c2 = S.scale * (S.pts[g * D + 2] - S.az);
+  }
+  const int64_t t = S.t0 + i / kTile;
+  ulonglong2 *tp = S.tiles + t * (int64_t)(A.nq * kTile) + (i % kTile);
+  tp[0] = make_ulonglong2(pk2u(c0, c0), pk2u(c1, c1));
+  tp[kTile] = make_ulonglong2(pk2u(c2, c2), pk2u(v, v));
+  S.aw[t * (int64_t)kTile + (i % kTile)] = a;
+}
+
 template <int NT>
 __global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
   const ChunkMap M{A.P, A.choff, A.chx};
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t, int64_t) {
     const Seg sg = A.seg[p];
-    const int D = A.D;
-    const int64_t s = side == 0 ? sg.xs : sg.ys;
-    const int64_t count = side == 0 ? sg.xcount : sg.ycount;
-    const int64_t t0 = (side == 0 ? A.tbase_x : A.tbase_y)[p];
-    const int64_t t1 = (side == 0 ? A.tbase_x : A.tbase_y)[p + 1];
+    if (small_pair(sg)) return;  // packed by prep3_kernel
+    const Pack3Side S = pack3_side(A, p, side, sg);
     const int64_t tmax = side == 0 ? A.max_tiles_x : A.max_tiles_y;
-    const float *pts = side == 0 ? A.x : A.y;
-    const float *w = side == 0 ? A.w_x : A.w_y;
-    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
-    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-    ulonglong2 *tiles = side == 0 ? A.tiles_x : A.tiles_y;
-    float *aw = side == 0 ? A.aw_x : A.aw_y;
-    const double *meta = A.meta + p * meta_stride(3);
-    const double Wm = meta[side] * meta[meta_wscale(3) + side];  // a~ = w' / Wm
-    const bool fold = meta[meta_fold(3) + side] != 0.0;
-    const bool uni = meta[meta_fold(3) + side] == 2.0;
-    const float pad = uni ? 1e18f : 0.f;
-    const float ax = (float)meta[4 + (2 + side) * 3 + 0];
-    const float ay = (float)meta[4 + (2 + side) * 3 + 1];
-    const float az = (float)meta[4 + (2 + side) * 3 + 2];
-    const float scale = pair_scale(A.scale, A.sigma_p, p);
-    const int nq = A.nq;
-    const int64_t npad = (t1 - t0) * kTile;
-    const int64_t b = c * kChunk, e = b + kChunk < npad ? b + kChunk : npad;
+    const int64_t b = c * kChunk, e = b + kChunk < S.npad ? b + kChunk : S.npad;
     for (int64_t i = b + threadIdx.x; i < e; i += NT) {
-      const int64_t t = t0 + i / kTile;
-      if (t >= tmax) break;  // malformed ptr overflowing the bound (error already flagged)
-      float c0 = pad, c1 = pad, c2 = pad, a = 0.f, v = fold ? INFINITY : 0.f;
-      if (i < count) {
-        const int64_t g = s + i;
-        const double at = uni ? 1.0 : (double)eff_weight(w, mask, wmode, g) / Wm;
-        a = (float)at;
-        c1 = c2 = 0.f;
-        // folded: a~ in [0, 1]; a zero weight becomes 2^-64, which leaves the
-        // other points' sums unchanged to 5e-20 and keeps the point's own
-        // row sums (its weight gradient) finite
-        v = fold ? (at >= 1.0 ? 0.f : at > 0x1p-64 ? (float)-log2(at) : 64.f) : a;
-        c0 = scale * (pts[g * D + 0] - ax);
-        if (D > 1) c1 = scale * (pts[g * D + 1] - ay);
-        if (D > 2) c2 = scale * (pts[g * D + 2] - az);
-      }
-      ulonglong2 *tp = tiles + t * (int64_t)(nq * kTile) + (i % kTile);
-      tp[0] = make_ulonglong2(pk2u(c0, c0), pk2u(c1, c1));
-      tp[kTile] = make_ulonglong2(pk2u(c2, c2), pk2u(v, v));
-      aw[t * (int64_t)kTile + (i % kTile)] = a;
+      if (S.t0 + i / kTile >= tmax) break;  // malformed ptr overflowing the bound (flagged)
+      pack3_slot(A, S, i);
     }
   });
+}
+
+// Error-free accumulation in float32 (Knuth's TwoSum, the running error kept
+// in a second float): a double-float sum of a few thousand floats, free of
+// float-to-double conversions per point, which run on the SM's narrow
+// conversion pipe.
+struct FSum {
+  float hi = 0.f, lo = 0.f;
+  __device__ __forceinline__ void add(float v) {
+    const float s = hi + v, bp = s - hi;
+    lo += (hi - (s - bp)) + (v - bp);
+    hi = s;
+  }
+  // adds the exact product a * b (TwoProduct by FMA)
+  __device__ __forceinline__ void add_prod(float a, float b) {
+    const float q = a * b;
+    add(q);
+    lo += fmaf(a, b, -q);
+  }
+  __device__ __forceinline__ double value() const { return (double)hi + (double)lo; }
+};
+
+// D <= 3, pairs with at most kSmallPts points per side (small_pair): one CTA
+// per pair does what stats3_kernel, meta_kernel and pack3_kernel do for the
+// large pairs -- the sums of both sides, the metadata, the packing -- so the
+// points are read from DRAM once (the packing pass re-reads them from cache).
+template <int NT>
+__global__ void __launch_bounds__(NT) prep3_kernel(PrepArgs A, PackArgs K) {
+  __shared__ double sh[(NT / 32) * 8];
+  __shared__ long long shl[NT / 32];
+  __shared__ float shm[NT / 32][2];
+  __shared__ double tot[2][12];  // per side: W, nv, sum w'p (3), sum p (3), last, wmax, nwmin
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int D = A.D;
+  for (int64_t p = blockIdx.x; p < A.P; p += gridDim.x) {
+    Seg sg = A.seg[p];
+    if (!small_pair(sg)) continue;
+    for (int side = 0; side < 2; ++side) {
+      const float *pts = side == 0 ? A.x : A.y;
+      const float *w = side == 0 ? A.w_x : A.w_y;
+      const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+      const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+      const int64_t s = side == 0 ? sg.xs : sg.ys;
+      const int64_t span = side == 0 ? sg.xspan : sg.yspan;
+      FSum W, cs[3], ps[3];
+      int nv = 0;
+      long long last = -1;
+      float wmax = -INFINITY, nwmin = -INFINITY;
+      for (int64_t i = tid; i < span; i += NT) {
+        const int64_t g = s + i;
+        const float wi = eff_weight(w, mask, wmode, g);
+        const bool valid = mask == nullptr || mask[g] != 0;
+        W.add(wi);
+        wmax = fmaxf(wmax, wi);
+        nwmin = fmaxf(nwmin, -wi);
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+          if (d < D) {
+            const float pv = pts[g * D + d];
+            cs[d].add_prod(wi, pv);
+            if (valid) ps[d].add(pv);
+          }
+        }
+        if (valid) {
+          ++nv;
+          last = i;
+        }
+      }
+      double vals[8] = {W.value(), (double)nv, cs[0].value(), cs[1].value(), cs[2].value(),
+                        ps[0].value(), ps[1].value(), ps[2].value()};
+      last = warp_max(last);
+      float wm = wmax, nw = nwmin;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        wm = fmaxf(wm, __shfl_xor_sync(kFull, wm, o));
+        nw = fmaxf(nw, __shfl_xor_sync(kFull, nw, o));
+      }
+      if (lane == 0) {
+        shl[wid] = last;
+        shm[wid][0] = wm;
+        shm[wid][1] = nw;
+      }
+      block_sum_n<8>(vals, sh);  // its first barrier also publishes shl and shm
+      if (tid == 0) {
+        long long lst = -1;
+        float mx = -INFINITY, nmn = -INFINITY;
+        for (int k = 0; k < NT / 32; ++k) {
+          lst = shl[k] > lst ? shl[k] : lst;
+          mx = fmaxf(mx, shm[k][0]);
+          nmn = fmaxf(nmn, shm[k][1]);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) tot[side][k] = vals[k];
+        tot[side][8] = (double)lst;
+        tot[side][9] = (double)mx;
+        tot[side][10] = (double)nmn;
+      }
+      // shl / shm are rewritten by the next side after block_sum_n's trailing barrier
+    }
+    __syncthreads();
+    // ---- metadata (meta_kernel's semantics), one thread -------------------
+    if (tid == 0) {
+      double *meta = A.meta + p * meta_stride(3);
+      if (A.sigma_p != nullptr && !(A.sigma_p[p] > 0.0)) atomicOr(A.err, (int)kErrSigma);
+      int64_t count_x = 0;
+      for (int side = 0; side < 2; ++side) {
+        const double *t = tot[side];
+        const double W = t[0], nv = t[1];
+        const int64_t span = side == 0 ? sg.xspan : sg.yspan;
+        const int64_t count = A.layout == 0 ? span : (int64_t)t[8] + 1;
+        const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+        double Wn, m, fold;
+        bool werr;
+        side_normaliser(wmode, W, nv, count, A.allow_fold != 0, t[9], t[10], Wn, m, fold, werr);
+        if (werr) atomicOr(A.err, (int)kErrWeightSum);
+        meta[side] = Wn;
+        meta[2 + side] = W;
+        meta[meta_wscale(3) + side] = m;
+        meta[meta_fold(3) + side] = fold;
+        if (side == 0) {
+          sg.xcount = count;
+          count_x = count;
+        } else {
+          sg.ycount = count;
+        }
+        for (int dd = 0; dd < 3; ++dd) {
+          const double mu = dd < D ? t[2 + dd] / Wn : 0.0;
+          const double mean = (dd < D && nv > 0) ? t[5 + dd] / nv : 0.0;
+          meta[4 + side * 3 + dd] = mu;
+          if (side == 0) {
+            meta[4 + 6 + dd] = mean;  // provisional: replaced by the anchor below
+          } else {
+            double ax, ay;
+            if (A.center) {
+              ax = meta[4 + dd];
+              ay = mu;
+            } else {
+              ax = count_x > 0 ? meta[4 + 6 + dd] : mean;
+              ay = ax;
+            }
+            meta[4 + 6 + dd] = ax;
+            meta[4 + 9 + dd] = ay;
+          }
+        }
+      }
+      A.seg[p].xcount = sg.xcount;
+      A.seg[p].ycount = sg.ycount;
+    }
+    __syncthreads();
+    // ---- packing: the tiles of both sides (points re-read from cache) -----
+    sg = A.seg[p];
+    for (int side = 0; side < 2; ++side) {
+      const Pack3Side S = pack3_side(K, p, side, sg);
+      for (int64_t i = tid; i < S.npad; i += NT) pack3_slot(K, S, i);
+    }
+    __syncthreads();  // tot is rewritten by the next pair
+  }
 }
 
 }  // namespace ra

@@ -78,7 +78,6 @@ struct Tiles3Args {
   const double *meta;                   // per-pair metadata (ra_prep.cuh)
   float *acc_x, *acc_y;                 // [tiles * 64][8]: self (s, G0..G2), cross (s, G0..G2)
   double *itemK, *itemS;
-  double *itemC;                        // [items][3]: x-y items' sum_i a_i G_i (with gradients)
   int shard_index, shard_count;  // this process evaluates items shard_index + k * shard_count
 };
 
@@ -260,7 +259,6 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
       if (lane == 0) {
         A.itemK[it] = 0.0;
         A.itemS[it] = 0.0;
-        if (GRAD && blk == 0) A.itemC[3 * it] = A.itemC[3 * it + 1] = A.itemC[3 * it + 2] = 0.0;
       }
       continue;
     }
@@ -372,29 +370,6 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     if (lane == 0) {
       A.itemK[it] = kw * kscale;
       A.itemS[it] = sw * kscale;
-    }
-    // x-y items: this item's share of C = sum_ij a_i b_j k_ij (x'_i - y'_j),
-    // the one vector the backward needs to sum the gradients of a whole cloud
-    // (the self blocks' share of that sum is zero by antisymmetry)
-    if (GRAD && blk == 0) {
-      double cv[3] = {0.0, 0.0, 0.0};
-#pragma unroll
-      for (int rp = 0; rp < 4; ++rp) {
-        float a_lo, a_hi, g_lo, g_hi;
-        upk(Aw[rp], a_lo, a_hi);
-        upk(G0[rp], g_lo, g_hi);
-        cv[0] = fma((double)a_hi, (double)g_hi, fma((double)a_lo, (double)g_lo, cv[0]));
-        upk(G1[rp], g_lo, g_hi);
-        cv[1] = fma((double)a_hi, (double)g_hi, fma((double)a_lo, (double)g_lo, cv[1]));
-        upk(G2[rp], g_lo, g_hi);
-        cv[2] = fma((double)a_hi, (double)g_hi, fma((double)a_lo, (double)g_lo, cv[2]));
-      }
-#pragma unroll
-      for (int d = 0; d < 3; ++d) cv[d] = warp_sum(cv[d]);
-      if (lane == 0) {
-#pragma unroll
-        for (int d = 0; d < 3; ++d) A.itemC[3 * it + d] = cv[d] * kscale;
-      }
     }
 
     // ---- per-point row sums: combine the 4 rings, then one lane per row ----

@@ -287,7 +287,8 @@ def test_split_evaluation_matches_unsplit(cuda_device):
     dev = cuda_device
     x = torch.from_numpy(rng.standard_normal((n, 3)).astype(np.float32)).to(dev)
     y = torch.from_numpy(rng.standard_normal((m, 3)).astype(np.float32)).to(dev)
-    wx = torch.from_numpy((rng.random(n) + 0.1).astype(np.float32)).to(dev)
+    # weights that require a gradient: the backward below asks for theirs
+    wx = torch.from_numpy((rng.random(n) + 0.1).astype(np.float32)).to(dev).requires_grad_(True)
 
     def spec(idx, cnt):
         return Spec(layout=_lib.RA_LAYOUT_DENSE, num_pairs=1, dim=3, num_x=n, num_y=m, nmax_x=n,
