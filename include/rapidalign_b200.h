@@ -163,6 +163,22 @@ RA_API int ra_kde_forward(const ra_kde_desc *desc, const ra_kde_inputs *in, doub
                    void *workspace, size_t workspace_bytes, ra_stream_t stream);
 
 /*
+ * ra_kde_forward in two phases on the same stream, for callers that read the
+ * device error word (ra_kde_status_of_error_word) without stopping the GPU:
+ * ra_kde_forward_prepare enqueues everything before the tile kernels
+ * (segments and ptr checks, weight sums, centroids, work plan, packing), after
+ * which the workspace's error word holds every data error the inputs have;
+ * ra_kde_forward_compute enqueues the tile kernels and forms K, exactly as
+ * ra_kde_forward would.  A caller can copy the word to host memory between the
+ * two and wait for that copy while the tile kernels run.  (The tensor-core
+ * kernels can still set RA_ERR_DEVICE_TIMEOUT during the compute phase.)
+ */
+RA_API int ra_kde_forward_prepare(const ra_kde_desc *desc, const ra_kde_inputs *in,
+                                  void *workspace, size_t workspace_bytes, ra_stream_t stream);
+RA_API int ra_kde_forward_compute(const ra_kde_desc *desc, const ra_kde_inputs *in, double *K,
+                                  void *workspace, size_t workspace_bytes, ra_stream_t stream);
+
+/*
  * Backward of the fused forward: given coef[0..P) = dL/dKxx, coef[P..2P) =
  * dL/dKyy, coef[2P..3P) = dL/dKxy (fp64, device), writes the requested
  * gradients including the centering and weight-normalisation Jacobians.
@@ -291,6 +307,23 @@ RA_API int ra_kde_mmd_forward_segmented_noalloc(const float *x, const float *y,
  * status (the same codes as ra_kde_check; synchronises `stream`).  Reports on
  * the last ra_kde_mmd_forward_segmented_noalloc enqueued on this device. */
 RA_API int ra_kde_check_noalloc(ra_stream_t stream);
+
+/* ---- batch vectors ----------------------------------------------------- */
+
+/* ptr offsets of a sorted batch vector, on the device: replaces the ptr
+ * construction of rapidalign/kde.py:142-156 (there: sort check, bincount,
+ * cumsum and host reads).  batch [n] int64 (device), num_graphs = the number
+ * of graphs the caller expects (batch[n - 1] + 1); writes ptr [num_graphs + 1]
+ * (device) and *flags (a device int, zeroed first) with bits of enum
+ * ra_batch_flag.  Nothing is read back: the caller checks the flags when it
+ * reads them.  ptr is exact when flags == 0. */
+enum ra_batch_flag {
+  RA_BATCH_UNSORTED = 1, /* "batch indices must be sorted for contiguous blocks" */
+  RA_BATCH_NEGATIVE = 2, /* the first graph id is negative */
+  RA_BATCH_COUNT = 4     /* batch[n - 1] + 1 != num_graphs */
+};
+RA_API int ra_ptr_from_batch(const int64_t *batch, int64_t n, int64_t num_graphs, int64_t *ptr,
+                             int *flags, ra_stream_t stream);
 
 /* ---- diagnostics ------------------------------------------------------- */
 

@@ -55,6 +55,9 @@ class Spec:
     # no weight gradient can be asked for (set by forward_sums): the forward
     # may leave out the per-point sums only grad_wx / grad_wy need
     skip_weight_sums: bool = False
+    # int32 [2] device flags of ra_ptr_from_batch for the two sides when ptr_x
+    # / ptr_y were built from batch vectors (checked with the error word)
+    batch_flags: Optional[Tensor] = None
 
     def desc(self, need_grad: bool, need_sigma_grad: bool) -> _lib.RaKdeDesc:
         d = _lib.RaKdeDesc()
@@ -99,6 +102,52 @@ def _inputs(x32, y32, wx32, wy32, spec: Spec) -> _lib.RaKdeInputs:
     return i
 
 
+class GraphCountMismatch(Exception):
+    """The graph count a batch-vector call was launched with is not the one
+    its batch vectors hold (raised before any result is returned; the caller
+    repeats the call with the exact count)."""
+
+
+def _raise_batch_flags(flags) -> None:
+    if any(f & _lib.RA_BATCH_UNSORTED for f in flags):
+        raise ValueError("batch indices must be sorted for contiguous blocks")
+    if any(f & _lib.RA_BATCH_NEGATIVE for f in flags):
+        raise ValueError("batch indices must be non-negative")
+    if any(f & _lib.RA_BATCH_COUNT for f in flags):
+        raise GraphCountMismatch()
+
+
+def uses_tensor_cores(spec: Spec) -> bool:
+    """Whether the forward runs the tensor-core kernels (padded dim 32, 64 or
+    128 on the automatic or tensor engine), whose bounded waits can expire."""
+    if spec.dim <= 3 or spec.engine == _lib.RA_ENGINE_SIMT:
+        return False
+    dp = 4
+    while dp < spec.dim:
+        dp <<= 1
+    return dp in (32, 64, 128)
+
+
+class _ErrorWord:
+    """An asynchronous read of the workspace's error word (and, optionally,
+    of batch flags): copied into pinned host memory on the stream and waited
+    for through an event, so the host stops only when it needs the answer --
+    typically while later kernels keep the GPU busy."""
+
+    def __init__(self, ws: Tensor, stream, flags: Optional[Tensor] = None):
+        n = 1 + (0 if flags is None else flags.numel())
+        self.host = torch.empty(n, dtype=torch.int32, pin_memory=True)
+        self.host[:1].copy_(ws[:4].view(torch.int32), non_blocking=True)
+        if flags is not None:
+            self.host[1:].copy_(flags, non_blocking=True)
+        self.event = torch.cuda.Event()
+        self.event.record(stream)
+
+    def read(self):
+        self.event.synchronize()
+        return self.host.tolist()
+
+
 def _raise_data_error(code: int, spec: Spec) -> None:
     if code == _lib.RA_OK:
         return
@@ -117,11 +166,12 @@ class _State:
     """What a backward needs from its forward: the fp32 inputs, the workspace
     holding the per-point sums, and the original dtypes/shapes."""
 
-    def __init__(self, spec, need_sigma_grad, keep, meta):
+    def __init__(self, spec, need_sigma_grad, keep, meta, pending=None):
         self.spec = spec
         self.need_sigma_grad = need_sigma_grad
         self.keep = keep
         self.meta = meta
+        self.pending = pending  # error word read after the tile kernels (tensor cores)
 
 
 def partial_buffers(lib, desc, ws: Tensor) -> Tuple[Tensor, Optional[Tensor]]:
@@ -164,11 +214,29 @@ def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tens
         raise RuntimeError("rapidalign_b200: invalid problem description")
     ws = _lib.workspace(nbytes, device)
     K = torch.empty(3 * spec.num_pairs, dtype=torch.float64, device=device)
-    stream = _lib.stream_handle(device)
+    tstream = torch.cuda.current_stream(device)
+    stream = tstream.cuda_stream
+    pending = None
     with torch.cuda.device(device):
-        rc = lib.ra_kde_forward(ctypes.byref(desc), ctypes.byref(inp), K.data_ptr(),
-                                ws.data_ptr(), ws.numel(), stream)
+        rc = lib.ra_kde_forward_prepare(ctypes.byref(desc), ctypes.byref(inp), ws.data_ptr(),
+                                        ws.numel(), stream)
         _lib.check(rc, "kde forward")
+        # the data errors are known once the preparation ran: read them while
+        # the tile kernels run, instead of stopping the GPU to ask
+        early = None
+        if spec.check_errors or spec.batch_flags is not None:
+            early = _ErrorWord(ws, tstream, spec.batch_flags)
+        rc = lib.ra_kde_forward_compute(ctypes.byref(desc), ctypes.byref(inp), K.data_ptr(),
+                                        ws.data_ptr(), ws.numel(), stream)
+        _lib.check(rc, "kde forward")
+        if uses_tensor_cores(spec):
+            pending = _ErrorWord(ws, tstream)  # an expired wait shows after the tiles
+        if early is not None:
+            words = early.read()
+            if len(words) > 1:
+                _raise_batch_flags(words[1:])
+            if spec.check_errors:
+                _raise_data_error(lib.ra_kde_status_of_error_word(words[0]), spec)
         if spec.shard_count > 1:
             if reduce is None:
                 raise RuntimeError("a split evaluation needs a reduction of its partials")
@@ -176,8 +244,9 @@ def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tens
             rc = lib.ra_kde_forward_finish(ctypes.byref(desc), K.data_ptr(), ws.data_ptr(),
                                            ws.numel(), stream)
             _lib.check(rc, "kde forward finish")
-        if spec.check_errors:
-            _raise_data_error(lib.ra_kde_check(ws.data_ptr(), stream), spec)
+        if pending is not None and not need_grad:
+            _check_pending(lib, pending)
+            pending = None
     state = None
     if need_grad:
         state = _State(spec, need_sigma_grad,
@@ -186,8 +255,15 @@ def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tens
                        (x.dtype, x.shape, y.dtype, y.shape,
                         None if w_x is None else (w_x.dtype, w_x.shape),
                         None if w_y is None else (w_y.dtype, w_y.shape),
-                        None if sigma_t is None else (sigma_t.dtype, sigma_t.shape)))
+                        None if sigma_t is None else (sigma_t.dtype, sigma_t.shape)),
+                       pending)
     return K, state
+
+
+def _check_pending(lib, pending: _ErrorWord) -> None:
+    code = lib.ra_kde_status_of_error_word(pending.read()[0])
+    if code != _lib.RA_OK:
+        _lib.check(code, "kde forward (tensor-core kernels)")
 
 
 def backward_sums(state: _State, coef: Tensor, need) -> tuple:
@@ -222,6 +298,11 @@ def backward_sums(state: _State, coef: Tensor, need) -> tuple:
                                  ctypes.byref(grads), ws.data_ptr(), ws.numel(),
                                  _lib.stream_handle(device))
     _lib.check(rc, "kde backward")
+    if state.pending is not None:
+        # the forward's tile kernels are done by the time this returns, while
+        # the backward just enqueued keeps the GPU busy
+        pending, state.pending = state.pending, None
+        _check_pending(lib, pending)
     xdt, xsh, ydt, ysh, wxm, wym, sm = state.meta
     out_x = gx.to(xdt).reshape(xsh) if gx is not None else None
     out_y = gy.to(ydt).reshape(ysh) if gy is not None else None

@@ -46,6 +46,10 @@ RA_ENGINE_TENSOR = 2
 
 RA_TEST_NO_MMA = 1
 
+RA_BATCH_UNSORTED = 1
+RA_BATCH_NEGATIVE = 2
+RA_BATCH_COUNT = 4
+
 
 class RaKdeDesc(ctypes.Structure):
     _fields_ = [
@@ -116,6 +120,11 @@ SIGNATURES = {
     "ra_kde_workspace_bytes": (_SZ, [ctypes.POINTER(RaKdeDesc)]),
     "ra_kde_forward": (ctypes.c_int, [ctypes.POINTER(RaKdeDesc), ctypes.POINTER(RaKdeInputs),
                                       _V, _V, _SZ, _V]),
+    "ra_kde_forward_prepare": (ctypes.c_int, [ctypes.POINTER(RaKdeDesc),
+                                              ctypes.POINTER(RaKdeInputs), _V, _SZ, _V]),
+    "ra_kde_forward_compute": (ctypes.c_int, [ctypes.POINTER(RaKdeDesc),
+                                              ctypes.POINTER(RaKdeInputs), _V, _V, _SZ, _V]),
+    "ra_ptr_from_batch": (ctypes.c_int, [_V, _I64, _I64, _V, _V, _V]),
     "ra_kde_backward": (ctypes.c_int, [ctypes.POINTER(RaKdeDesc), ctypes.POINTER(RaKdeInputs),
                                        _V, ctypes.POINTER(RaKdeGrads), _V, _SZ, _V]),
     "ra_kde_check": (ctypes.c_int, [_V, _V]),

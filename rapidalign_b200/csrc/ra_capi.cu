@@ -13,6 +13,7 @@
 #include <cstring>
 
 #include "../../include/rapidalign_b200.h"
+#include "ra_batch.cuh"
 #include "ra_chunks.cuh"
 #include "ra_common.cuh"
 #include "ra_epilogue.cuh"
@@ -316,19 +317,27 @@ bool may_have_large_pairs(const ra_kde_desc *d) {
                                       : (d->num_x > kSmallPts || d->num_y > kSmallPts);
 }
 
-int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, double *Kyy,
-                 double *Kxy, void *ws, size_t ws_bytes, cudaStream_t st,
-                 cudaEvent_t ev0 = nullptr, cudaEvent_t ev1 = nullptr) {
+int check_inputs(const ra_kde_desc *d, const ra_kde_inputs *in) {
+  if (in == nullptr) return RA_ERR_INVALID_ARGUMENT;
+  if ((d->num_x > 0 && in->x == nullptr) || (d->num_y > 0 && in->y == nullptr))
+    return RA_ERR_INVALID_ARGUMENT;
+  if (d->layout == RA_LAYOUT_RAGGED && d->num_pairs > 0 &&
+      (in->ptr_x == nullptr || in->ptr_y == nullptr))
+    return RA_ERR_INVALID_ARGUMENT;
+  return RA_OK;
+}
+
+// Forward, first phase: everything up to the tile kernels (segments, ptr
+// checks, sums, metadata, work plan, packing).  Every data error the forward
+// can find in its inputs is in the workspace's error word when it is done.
+int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t ws_bytes,
+                 cudaStream_t st) {
   const Layout L = make_layout(d);
   int rc = check_common(d, ws, ws_bytes, L.total);
   if (rc) return rc;
-  if (in == nullptr || Kxx == nullptr || Kyy == nullptr || Kxy == nullptr)
-    return RA_ERR_INVALID_ARGUMENT;
+  rc = check_inputs(d, in);
+  if (rc) return rc;
   const int64_t P = d->num_pairs;
-  if ((d->num_x > 0 && in->x == nullptr) || (d->num_y > 0 && in->y == nullptr))
-    return RA_ERR_INVALID_ARGUMENT;
-  if (d->layout == RA_LAYOUT_RAGGED && P > 0 && (in->ptr_x == nullptr || in->ptr_y == nullptr))
-    return RA_ERR_INVALID_ARGUMENT;
   // header: error word, ticket, state flag, item count
   if (cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return RA_ERR_CUDA;
   if (P == 0) return RA_OK;
@@ -477,6 +486,24 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     ++g_launches;
     if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
   }
+  return RA_OK;
+}
+
+// Forward, second phase: the tile kernels and (unless the problem is split
+// over shards) the per-pair K.  Follows prepare_impl on the same stream.
+int compute_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, double *Kyy,
+                 double *Kxy, void *ws, size_t ws_bytes, cudaStream_t st, cudaEvent_t ev0,
+                 cudaEvent_t ev1) {
+  const Layout L = make_layout(d);
+  int rc = check_common(d, ws, ws_bytes, L.total);
+  if (rc) return rc;
+  rc = check_inputs(d, in);
+  if (rc) return rc;
+  if (Kxx == nullptr || Kyy == nullptr || Kxy == nullptr) return RA_ERR_INVALID_ARGUMENT;
+  const int64_t P = d->num_pairs;
+  if (P == 0) return RA_OK;
+  const bool grad = d->need_grad != 0;
+  const int mode = !grad ? 0 : (d->need_sigma_grad ? 2 : (d->skip_weight_sums ? 3 : 1));
 
   const bool sharded = d->shard_count > 1;
   const int sh_idx = sharded ? d->shard_index : 0, sh_cnt = sharded ? d->shard_count : 1;
@@ -537,6 +564,15 @@ int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
   return finish_impl(d, L, Kxx, Kyy, Kxy, ws, st);
 }
 
+int forward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, double *Kyy,
+                 double *Kxy, void *ws, size_t ws_bytes, cudaStream_t st,
+                 cudaEvent_t ev0 = nullptr, cudaEvent_t ev1 = nullptr) {
+  if (Kxx == nullptr || Kyy == nullptr || Kxy == nullptr) return RA_ERR_INVALID_ARGUMENT;
+  const int rc = prepare_impl(d, in, ws, ws_bytes, st);
+  if (rc) return rc;
+  return compute_impl(d, in, Kxx, Kyy, Kxy, ws, ws_bytes, st, ev0, ev1);
+}
+
 // Per-pair K from the item partials (into the caller's arrays), the state flag.
 int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy, double *Kxy,
                 void *ws, cudaStream_t st) {
@@ -559,8 +595,14 @@ int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy,
   // the state flag marks a workspace whose forward kept what a backward needs;
   // the kernel writes it, so no host memory is involved
   fa.state = grad ? at<int>(ws, L.hdr + kHdrState) : nullptr;
-  finalize_kernel<256><<<(unsigned)P, 256, 0, st>>>(fa);
+  finalize_warp_kernel<<<(unsigned)ceil_div(P, 8), 256, 0, st>>>(fa);
   ++g_launches;
+  // pairs of at most kSmallPts points per side have at most 192 items
+  static_assert(kWarpItems >= 3 * (kSmallPts / kTile), "small pairs fit one warp");
+  if (may_have_large_pairs(d)) {
+    finalize_kernel<256><<<(unsigned)P, 256, 0, st>>>(fa);
+    ++g_launches;
+  }
   return cuda_status(cudaGetLastError());
 }
 
@@ -775,6 +817,20 @@ int ra_kde_forward(const ra_kde_desc *desc, const ra_kde_inputs *in, double *K, 
                       (cudaStream_t)stream);
 }
 
+int ra_kde_forward_prepare(const ra_kde_desc *desc, const ra_kde_inputs *in, void *workspace,
+                           size_t workspace_bytes, ra_stream_t stream) {
+  if (!desc_ok(desc)) return RA_ERR_INVALID_ARGUMENT;
+  return prepare_impl(desc, in, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int ra_kde_forward_compute(const ra_kde_desc *desc, const ra_kde_inputs *in, double *K,
+                           void *workspace, size_t workspace_bytes, ra_stream_t stream) {
+  if (!desc_ok(desc) || K == nullptr) return RA_ERR_INVALID_ARGUMENT;
+  const int64_t P = desc->num_pairs;
+  return compute_impl(desc, in, K, K + P, K + 2 * P, workspace, workspace_bytes,
+                      (cudaStream_t)stream, nullptr, nullptr);
+}
+
 int ra_kde_backward(const ra_kde_desc *desc, const ra_kde_inputs *in, const double *coef,
                     const ra_kde_grads *grads, void *workspace, size_t workspace_bytes,
                     ra_stream_t stream) {
@@ -961,6 +1017,23 @@ int ra_kde_check_noalloc(ra_stream_t stream) {
   const int rc = noalloc_scratch_address(&scratch);
   if (rc) return rc;
   return ra_kde_check(scratch, stream);
+}
+
+int ra_ptr_from_batch(const int64_t *batch, int64_t n, int64_t num_graphs, int64_t *ptr,
+                      int *flags, ra_stream_t stream) {
+  if (n < 0 || num_graphs < 0 || ptr == nullptr || flags == nullptr ||
+      (n > 0 && batch == nullptr))
+    return RA_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(flags, 0, sizeof(int), st) != cudaSuccess) return RA_ERR_CUDA;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = ceil_div(n + 1, (int64_t)256), cap = (int64_t)(sms > 0 ? sms : 1) * 8;
+  ptr_from_batch_kernel<<<(unsigned)(want < cap ? want : cap), 256, 0, st>>>(batch, n, num_graphs,
+                                                                           ptr, flags);
+  ++g_launches;
+  return cuda_status(cudaGetLastError());
 }
 
 unsigned long long ra_kernel_launch_count(void) { return g_launches.load(); }

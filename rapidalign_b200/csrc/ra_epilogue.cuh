@@ -31,20 +31,65 @@ struct FinalizeArgs {
   int *state;     // set to 1 when not null
 };
 
-// One CTA per pair; block b of the items maps to K index (xy -> 2, xx -> 0,
-// yy -> 1).  Four independent accumulators per thread keep enough loads in
-// flight for pairs with hundreds of thousands of items.
+// Pairs with at most kWarpItems work items are summed by one warp each
+// (finalize_warp_kernel), larger ones by one CTA each (finalize_kernel).
+constexpr int64_t kWarpItems = 256;
+
+// The item range [base, end) of pair p: item_off[P] is the (clamped) number
+// of items actually emitted, so partials beyond it are never read, even for
+// a malformed ptr that overflowed the bound.
+__device__ __forceinline__ void pair_items(const FinalizeArgs &A, int64_t p, int64_t &base,
+                                           int64_t &end) {
+  const int64_t lim = A.item_off[A.P];
+  base = A.item_off[p];
+  end = A.item_off[p + 1] < lim ? A.item_off[p + 1] : lim;
+  if (base > end) base = end;
+}
+
+// One warp per pair of at most kWarpItems items (lane-strided sums, then a
+// fixed shuffle tree: deterministic).  Block b of the items maps to K index
+// (xy -> 2, xx -> 0, yy -> 1).
+__global__ void __launch_bounds__(256) finalize_warp_kernel(FinalizeArgs A) {
+  const int64_t p = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (p >= A.P) return;
+  if (p == 0 && lane == 0 && A.state != nullptr) *A.state = 1;
+  int64_t base, end;
+  pair_items(A, p, base, end);
+  if (end - base > kWarpItems) return;  // finalize_kernel
+  const int kidx[3] = {2, 0, 1};
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    int64_t b0 = base + A.boff[p * 4 + b];
+    const int64_t b1 = b < 2 ? base + A.boff[p * 4 + b + 1] : base + A.boff[p * 4 + 3];
+    const int64_t e = b1 < end ? b1 : end;
+    if (b0 > e) b0 = e;
+    double k = 0.0, s = 0.0;
+    for (int64_t i = b0 + lane; i < e; i += 32) {
+      k += A.itemK[i];
+      s += A.itemS[i];
+    }
+    k = warp_sum(k);
+    s = warp_sum(s);
+    if (lane == 0) {
+      A.K_out[kidx[b]][p] = k;
+      A.K_ws[kidx[b] * A.P + p] = k;
+      A.S_ws[kidx[b] * A.P + p] = s;
+    }
+  }
+}
+
+// One CTA per pair of more than kWarpItems items.  Four independent
+// accumulators per thread keep enough loads in flight for pairs with hundreds
+// of thousands of items.
 template <int NT>
 __global__ void __launch_bounds__(NT) finalize_kernel(FinalizeArgs A) {
   __shared__ double sh[NT / 32];
   const int64_t p = blockIdx.x;
   if (p >= A.P) return;
-  if (p == 0 && threadIdx.x == 0 && A.state != nullptr) *A.state = 1;
-  // item_off[P] is the (clamped) number of items actually emitted: never read
-  // partials beyond it, even for a malformed ptr that overflowed the bound
-  const int64_t lim = A.item_off[A.P];
-  const int64_t base = A.item_off[p];
-  const int64_t end = A.item_off[p + 1] < lim ? A.item_off[p + 1] : lim;
+  int64_t base, end;
+  pair_items(A, p, base, end);
+  if (end - base <= kWarpItems) return;  // finalize_warp_kernel
   const int kidx[3] = {2, 0, 1};
 #pragma unroll 1
   for (int b = 0; b < 3; ++b) {

@@ -146,6 +146,9 @@ __global__ void __launch_bounds__(1024) segment_kernel(PrepArgs A) {
         sg.ys = s;
         sg.yspan = span;
         A.chcnt[p] = A.chx[p] + ceil_div(span, (int64_t)kChunk);
+        // D <= 3: the chunk map covers only the pairs the chunked passes
+        // prepare (small pairs have their own one-CTA kernels)
+        if (A.tcnt != nullptr && small_pair(sg)) A.chx[p] = A.chcnt[p] = 0;
       }
       // D <= 3 tile layout: room for the whole span (a dense row's count,
       // 1 + its last valid index, is known only after the sums)
@@ -154,10 +157,67 @@ __global__ void __launch_bounds__(1024) segment_kernel(PrepArgs A) {
     __syncthreads();
   }
   if (e) atomicOr(A.err, e);
-  block_exclusive_scan(A.chcnt, A.choff, A.P, A.chunk_cap, warp_tot, &carry);
-  if (A.tcnt != nullptr) {
-    block_exclusive_scan(A.tcnt, A.tbase_x, A.P, INT64_MAX, warp_tot, &carry);
-    block_exclusive_scan(A.tcnt + A.P, A.tbase_y, A.P, INT64_MAX, warp_tot, &carry);
+  if (A.tcnt == nullptr) {
+    block_exclusive_scan(A.chcnt, A.choff, A.P, A.chunk_cap, warp_tot, &carry);
+    return;
+  }
+  // the chunk map and both tile bases in one pass over the pairs
+  __shared__ int64_t warp_tot3[3][32];
+  __shared__ int64_t carry3[3];
+  if (tid < 3) carry3[tid] = 0;
+  __syncthreads();
+  const int lane = tid & 31, wid = tid >> 5;
+  for (int64_t base = 0; base < A.P; base += 1024) {
+    const int64_t p = base + tid;
+    const bool in = p < A.P;
+    const int64_t v[3] = {in ? A.chcnt[p] : 0, in ? A.tcnt[p] : 0, in ? A.tcnt[A.P + p] : 0};
+    int64_t inc[3] = {v[0], v[1], v[2]};
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const int64_t t = __shfl_up_sync(kFull, inc[k], o);
+        if (lane >= o) inc[k] += t;
+      }
+    }
+    if (lane == 31) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) warp_tot3[k][wid] = inc[k];
+    }
+    __syncthreads();
+    if (wid == 0) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        int64_t t = warp_tot3[k][lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int64_t u = __shfl_up_sync(kFull, t, o);
+          if (lane >= o) t += u;
+        }
+        warp_tot3[k][lane] = t;  // inclusive over warps
+      }
+    }
+    __syncthreads();
+    int64_t r[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) r[k] = inc[k] + (wid > 0 ? warp_tot3[k][wid - 1] : 0) + carry3[k];
+    if (in) {
+      const int64_t e0 = r[0] - v[0];
+      A.choff[p] = e0 < A.chunk_cap ? e0 : A.chunk_cap;
+      A.tbase_x[p] = r[1] - v[1];
+      A.tbase_y[p] = r[2] - v[2];
+    }
+    __syncthreads();
+    if (tid == 1023) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) carry3[k] = r[k];
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    A.choff[A.P] = carry3[0] < A.chunk_cap ? carry3[0] : A.chunk_cap;
+    A.tbase_x[A.P] = carry3[1];
+    A.tbase_y[A.P] = carry3[2];
   }
 }
 

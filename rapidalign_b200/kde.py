@@ -23,7 +23,7 @@ from typing import Optional, Tuple
 import torch
 
 from . import _lib
-from ._core import Spec, kde_sums
+from ._core import GraphCountMismatch, Spec, kde_sums
 
 Tensor = torch.Tensor
 
@@ -292,6 +292,31 @@ def batch_ptrs(src_batch: Tensor, tgt_batch: Tensor) -> Tuple[Tensor, Tensor]:
     return ps, pt
 
 
+# Graph count of the last batch-vector call on each device: a batch-vector
+# call starts its work with this count, builds ptr on the device and verifies
+# the count there; a wrong guess is found before any result is returned and
+# the call is repeated with the exact count.  The first call on a device (and
+# a repeat) reads the count back instead.
+_GRAPH_COUNT_HINT: dict = {}
+
+
+def _batch_ptrs_on_device(sb: Tensor, tb: Tensor, num_graphs: int):
+    """ptr offsets of both sides for a graph count, built on the device,
+    with the int32 [2] flags that check them (ra_ptr_from_batch)."""
+    lib = _lib.load()
+    dev = sb.device
+    ptr_x = torch.empty(num_graphs + 1, dtype=torch.long, device=dev)
+    ptr_y = torch.empty(num_graphs + 1, dtype=torch.long, device=dev)
+    flags = torch.empty(2, dtype=torch.int32, device=dev)
+    stream = _lib.stream_handle(dev)
+    with torch.cuda.device(dev):
+        for b, p, k in ((sb, ptr_x, 0), (tb, ptr_y, 1)):
+            rc = lib.ra_ptr_from_batch(b.data_ptr(), b.numel(), num_graphs, p.data_ptr(),
+                                       flags.data_ptr() + 4 * k, stream)
+            _lib.check(rc, "ptr from batch")
+    return ptr_x, ptr_y, flags
+
+
 def pyg_kde_mmd_loss(
     src_pos: Tensor,
     tgt_pos: Tensor,
@@ -321,15 +346,43 @@ def pyg_kde_mmd_loss(
         raise ValueError("sigma must be positive")
 
     device = src_pos.device
-    dtype = src_pos.dtype
     _lib.require_cuda(src_pos, tgt_pos)
+    kw = dict(src_w=src_w, tgt_w=tgt_w, sigma=sigma, center=center, cosine=cosine, eps=eps)
+
+    # both sides as batch vectors: start with the last call's graph count
+    # (verified on the device, repeated exactly if wrong), no host round trip
+    if (src_ptr is None and tgt_ptr is None and src_batch is not None and
+            tgt_batch is not None):
+        sb = src_batch.to(device=device, dtype=torch.long).contiguous()
+        tb = tgt_batch.to(device=device, dtype=torch.long).contiguous()
+        if sb.numel() != src_pos.size(0) or tb.numel() != tgt_pos.size(0):
+            raise ValueError("batch length must match number of nodes")
+        guess = _GRAPH_COUNT_HINT.get(device.index)
+        if guess is not None and sb.numel() > 0 and tb.numel() > 0:
+            ptr_x, ptr_y, flags = _batch_ptrs_on_device(sb, tb, guess)
+            try:
+                return _pyg_segments(src_pos, tgt_pos, ptr_x, ptr_y, guess, False, flags, **kw)
+            except GraphCountMismatch:
+                pass
+        src_batch, tgt_batch = sb, tb
 
     src_ptr_t, num_src, user_x, tgt_ptr_t, num_tgt, user_y = _ensure_ptrs(
         src_ptr, src_batch, src_pos.size(0), tgt_ptr, tgt_batch, tgt_pos.size(0), device)
     if num_src != num_tgt:
         raise ValueError("source and target batches must have the same length")
+    if not (user_x or user_y):
+        _GRAPH_COUNT_HINT[device.index] = num_src
+    return _pyg_segments(src_pos, tgt_pos, src_ptr_t, tgt_ptr_t, num_src, user_x or user_y,
+                         None, **kw)
 
-    num_pairs = num_src
+
+def _pyg_segments(src_pos, tgt_pos, src_ptr_t, tgt_ptr_t, num_pairs, user_ptr, batch_flags,
+                  src_w, tgt_w, sigma, center, cosine, eps):
+    """pyg_kde_mmd_loss once the segments are known: ptr offsets of both
+    sides (user-given, or built from batch vectors with `batch_flags` still to
+    be checked) for `num_pairs` graphs."""
+    device = src_pos.device
+    dtype = src_pos.dtype
     if num_pairs == 0:
         zero = torch.zeros((0,), device=device, dtype=dtype)
         return zero, zero, zero, zero
@@ -350,7 +403,8 @@ def pyg_kde_mmd_loss(
         weights_x=_lib.RA_WEIGHTS_SUM if src_w is not None else _lib.RA_WEIGHTS_UNIFORM,
         weights_y=_lib.RA_WEIGHTS_SUM if tgt_w is not None else _lib.RA_WEIGHTS_UNIFORM,
         center=center, sigma=sig, ptr_x=src_ptr_t, ptr_y=tgt_ptr_t,
-        check_errors=(user_x or user_y or src_w is not None or tgt_w is not None))
+        check_errors=(user_ptr or src_w is not None or tgt_w is not None),
+        batch_flags=batch_flags)
     xw = None if src_w is None else src_w.to(device).reshape(-1)
     yw = None if tgt_w is None else tgt_w.to(device).reshape(-1)
     Kxx, Kyy, Kxy = kde_sums(src_pos, tgt_pos, xw, yw, sig_t, spec)
