@@ -5,18 +5,19 @@ second, forward + backward, through the public API (``pyg_kde_mmd_loss``).
     torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
 
 Workload (a "step"): one forward + backward of ``pyg_kde_mmd_loss`` over a
-ragged batch of 4096 graphs per GPU, sizes uniform in [32, 2048] points,
-target sizes = source size +- uniform [0, 64], coordinates N(0, 1) in 3-D,
+ragged batch of 4096 graphs, sizes uniform in [32, 2048] points, target
+sizes = source size +- uniform [0, 64], coordinates N(0, 1) in 3-D,
 target = source + N(0, s^2) noise with s ~ U[0.05, 0.08] per graph,
 sigma = 0.25, centering on, sorted batch vectors.  Synthetic, seeded: each
 graph is generated from its own seed, so every rank can build its own share
-of a global batch without generating the rest.
+of the batch without generating the rest.
 
-Multi-GPU: weak scaling.  The global batch has N * 4096 graphs; graphs are
-assigned to ranks by a greedy longest-processing-time partition of their
-cost N_i^2 + M_i^2 + N_i M_i (rapidalign_b200.shard); ranks compute their
-shares with no collective in the data path and the per-graph K values are
-gathered once after the timed region.
+Multi-GPU (default): strong scaling.  The same 4096-graph batch at every N;
+graphs are assigned to ranks by a greedy longest-processing-time partition of
+their cost N_i^2 + M_i^2 + N_i M_i (rapidalign_b200.shard); ranks compute their
+shares with no collective in the data path and the per-graph results are
+gathered once after the timed region.  ``--scaling weak`` gives every GPU a
+batch of its own size instead (N times the graphs).
 
 Metric: full kernel terms (N^2 + M^2 + N M per graph, the reference's count)
 per second over the whole job.  The roofline fraction uses the unique terms
@@ -202,6 +203,15 @@ class ClockSampler:
 # CPU baseline: the oracle (C, float64, OpenMP) on a bounded sample
 # ----------------------------------------------------------------------------
 
+CPU_BASELINE_WHAT = (
+    "the oracle's C port (oracle/kde_oracle.c) of the reference's float64 sums "
+    "(rapidalign/kde_gradients.py:39-132): every kernel term of Kxx, Kyy, Kxy and the per-point "
+    "sums the gradients are made of, on all host threads; the O(N) centering and "
+    "normalisation chain rule is not timed.  The reference's own CPU path is PyTorch "
+    "(rapidalign/kde.py), which materialises N x M matrices and needs the reference "
+    "package, so it does not travel to the GPU box; it ran at ~3e7 terms/s on 8 cores "
+    "when measured here, about 40x slower than this port")
+
 def cpu_units(name: str):
     """Units of oracle work (C, float64, OpenMP) drawn from the named workload:
     yields (run, label) where run(cores) computes the forward+backward sums of
@@ -268,8 +278,8 @@ def cpu_baseline(name: str, budget_s: float = 15.0):
         if total_t > budget_s:
             break
     return {"value": total_full / total_t, "unit": "terms/s", "cores": cores, "kind": "port",
-            "sample": f"first {used} {label}, oracle (C, fp64, OpenMP) forward+backward sums, "
-                      f"{total_t:.1f} s"}
+            "sample": f"first {used} {label}, {total_t:.1f} s",
+            "what": CPU_BASELINE_WHAT}
 
 
 # ----------------------------------------------------------------------------
@@ -286,16 +296,23 @@ def random_rotation(rng) -> np.ndarray:
                      [2 * (x * z - y * w), 2 * (y * z + x * w), 1 - 2 * (x * x + y * y)]])
 
 
-class RaggedWorkload:
-    """4096 graphs per GPU (weak scaling), LPT-partitioned across ranks."""
-    scaling = "weak"
-    issued_ops = 14  # equal (uniform) weights on both clouds
+def job_graphs(per_batch: int, world: int, scaling: str) -> int:
+    """Graphs of the whole job: the batch itself (strong scaling) or one
+    batch per GPU (weak scaling)."""
+    return per_batch * (world if scaling == "weak" else 1)
 
-    def __init__(self, rank, world, dev, graphs_per_gpu=GRAPHS_PER_GPU, dim=3, lo=32, hi=2048,
-                 sigma=SIGMA, center=True):
+
+class RaggedWorkload:
+    """The 4096-graph batch, LPT-partitioned across ranks (strong scaling), or
+    4096 graphs per GPU (weak scaling)."""
+    issued_ops = 13  # equal weights on both clouds, no weight gradient
+
+    def __init__(self, rank, world, dev, scaling="strong", dim=3, lo=32, hi=2048, sigma=SIGMA,
+                 center=True):
         import torch
         from rapidalign_b200.shard import lpt_partition
-        total = graphs_per_gpu * world
+        self.scaling = scaling
+        total = job_graphs(GRAPHS_PER_GPU, world, scaling)
         sizes = ragged_sizes(range(total), lo=lo, hi=hi)
         cost = sizes[:, 0] ** 2 + sizes[:, 1] ** 2 + sizes[:, 0] * sizes[:, 1]
         self.mine = np.sort(lpt_partition(cost, world)[rank])
@@ -308,13 +325,18 @@ class RaggedWorkload:
         self.h = {k: torch.from_numpy(v).pin_memory() for k, v in
                   dict(x=x, y=y, bx=bx, by=by).items()}
         self.result_host = torch.empty(len(self.mine), dtype=torch.float32).pin_memory()
-        self.config = self.describe(world)
+        self.config = self.describe(world, scaling)
 
     @staticmethod
-    def describe(world):
-        return {"workload": f"ragged PyG batch, {GRAPHS_PER_GPU} graphs per GPU, 32-2048 points "
-                            f"each, D=3, sigma={SIGMA}, centred, pyg_kde_mmd_loss fwd+bwd",
-                "graphs": GRAPHS_PER_GPU * world}
+    def describe(world, scaling="strong"):
+        total = job_graphs(GRAPHS_PER_GPU, world, scaling)
+        sizes = ragged_sizes(range(total))
+        full, unique = term_counts(sizes[:, 0], sizes[:, 1])
+        return {"workload": f"ragged PyG batch of {GRAPHS_PER_GPU} graphs"
+                            f"{' per GPU' if scaling == 'weak' else ''}, 32-2048 points each, "
+                            f"D=3, sigma={SIGMA}, centred, pyg_kde_mmd_loss fwd+bwd",
+                "graphs": total, "full_terms_per_step": full, "unique_terms_per_step": unique,
+                "seed": SEED}
 
     def step(self, t):
         from rapidalign_b200 import pyg_kde_mmd_loss
@@ -335,10 +357,10 @@ class HugePairWorkload:
     """One pair of N = M = 262144 points split across the ranks (strong
     scaling): src ~ N(0, 1), tgt = R (src + 0.05 noise) with R uniform in
     SO(3), sigma 0.2, centred."""
-    scaling = "strong"
-    issued_ops = 14
+    issued_ops = 13
 
-    def __init__(self, rank, world, dev, n=262144, sigma=0.2):
+    def __init__(self, rank, world, dev, scaling="strong", n=262144, sigma=0.2):
+        self.scaling = "strong"  # one pair: the work is fixed whatever N is
         import torch
         import torch.distributed as dist
         src, tgt = huge_pair_data(n)
@@ -355,11 +377,13 @@ class HugePairWorkload:
         self.config = self.describe(world)
 
     @staticmethod
-    def describe(world):
+    def describe(world, scaling="strong"):
+        full, unique = term_counts(np.array([262144]), np.array([262144]))
         return {"workload": "single pair N = M = 262144, D=3, tgt = R(src + 0.05 noise), "
                             "sigma=0.2, centred, split over the GPUs by row tiles "
                             "(shard.split_pair_kde_mmd_loss) fwd+bwd",
-                "points": 262144}
+                "points": 262144, "full_terms_per_step": full, "unique_terms_per_step": unique,
+                "seed": SEED}
 
     def step(self, t):
         from rapidalign_b200.shard import split_pair_kde_mmd_loss
@@ -383,15 +407,22 @@ class HugePairWorkload:
 
 
 class DenseWorkload:
-    """Padded batch: B = 64 clouds of Nmax = 1024 points per GPU, valid lengths
+    """Padded batch: B = 64 clouds of Nmax = 1024 points, valid lengths
     uniform in [512, 1024] (prefix masks), tgt = src + 0.05 noise, sigma 0.25,
-    centred, kde_mmd_loss_dense fwd+bwd (weak scaling)."""
-    scaling = "weak"
-    issued_ops = 15  # masked (zero) weights: folded, not all equal
+    centred, kde_mmd_loss_dense fwd+bwd.  Strong scaling: the 64 clouds are
+    LPT-partitioned across the ranks; weak: 64 clouds per GPU."""
+    issued_ops = 14  # masked (zero) weights: folded, not all equal; no weight gradient
 
-    def __init__(self, rank, world, dev, B=64, nmax=1024, sigma=SIGMA):
+    def __init__(self, rank, world, dev, scaling="strong", B=64, nmax=1024, sigma=SIGMA):
         import torch
-        x, y, lx, ly = dense_data(rank, B, nmax)
+        from rapidalign_b200.shard import graph_costs, lpt_partition
+        self.scaling = scaling
+        if scaling == "weak":
+            x, y, lx, ly = dense_data(rank, B, nmax)
+        else:
+            x, y, lx, ly = dense_data(0, B, nmax)
+            mine = np.sort(lpt_partition(graph_costs(lx, ly), world)[rank])
+            x, y, lx, ly = x[mine], y[mine], lx[mine], ly[mine]
         mx = np.arange(nmax)[None, :] < lx[:, None]
         my = np.arange(nmax)[None, :] < ly[:, None]
         self.full_local, self.unique_local = term_counts(lx, ly)
@@ -400,14 +431,22 @@ class DenseWorkload:
         self.d = {k: torch.from_numpy(v).to(dev) for k, v in dict(x=x, y=y, mx=mx, my=my).items()}
         self.h = {k: torch.from_numpy(v).pin_memory() for k, v in
                   dict(x=x, y=y, mx=mx, my=my).items()}
-        self.result_host = torch.empty(B, dtype=torch.float32).pin_memory()
-        self.config = self.describe(world)
+        self.result_host = torch.empty(max(len(lx), 1), dtype=torch.float32).pin_memory()
+        self.config = self.describe(world, scaling)
 
     @staticmethod
-    def describe(world):
-        return {"workload": "dense padded batch, B=64 clouds of Nmax=1024 per GPU, valid "
-                            "512-1024 (prefix masks), D=3, sigma=0.25, centred, "
-                            "kde_mmd_loss_dense fwd+bwd", "clouds": 64 * world}
+    def describe(world, scaling="strong"):
+        ranks = range(world) if scaling == "weak" else range(1)
+        full = unique = 0.0
+        for r in ranks:
+            _, _, lx, ly = dense_data(r)
+            f, u = term_counts(lx, ly)
+            full, unique = full + f, unique + u
+        return {"workload": "dense padded batch, B=64 clouds of Nmax=1024"
+                            f"{' per GPU' if scaling == 'weak' else ''}, valid 512-1024 (prefix "
+                            "masks), D=3, sigma=0.25, centred, kde_mmd_loss_dense fwd+bwd",
+                "clouds": 64 * len(ranks), "full_terms_per_step": full,
+                "unique_terms_per_step": unique, "seed": SEED}
 
     def step(self, t):
         from rapidalign_b200 import kde_mmd_loss_dense
@@ -424,17 +463,22 @@ class DenseWorkload:
                                           self.sigma, reps=reps, center=True)
 
 
-class EmbedWorkload(RaggedWorkload):
-    """High-dimensional embeddings: 1024 graphs per GPU of 64-512 nodes, D=128,
-    x ~ N(0, 1/D), tgt = src + 0.1 noise (same sizes), sigma 1.0, uncentred."""
+def embed_sizes(total: int) -> np.ndarray:
+    return np.array([int(np.random.default_rng([SEED, 5, g]).integers(64, 513))
+                     for g in range(total)])
 
-    def __init__(self, rank, world, dev):
+
+class EmbedWorkload(RaggedWorkload):
+    """High-dimensional embeddings: 1024 graphs of 64-512 nodes (per GPU with
+    weak scaling), D=128, x ~ N(0, 1/D), tgt = src + 0.1 noise (same sizes),
+    sigma 1.0, uncentred."""
+
+    def __init__(self, rank, world, dev, scaling="strong"):
         import torch
         from rapidalign_b200.shard import lpt_partition
-        total = 1024 * world
-        rng_sizes = [int(np.random.default_rng([SEED, 5, g]).integers(64, 513))
-                     for g in range(total)]
-        sizes = np.array(rng_sizes)
+        self.scaling = scaling
+        total = job_graphs(1024, world, scaling)
+        sizes = embed_sizes(total)
         cost = 3.0 * sizes.astype(np.float64) ** 2
         self.mine = np.sort(lpt_partition(cost, world)[rank])
         xs, ys = [], []
@@ -459,13 +503,18 @@ class EmbedWorkload(RaggedWorkload):
         self.h = {k: torch.from_numpy(v).pin_memory() for k, v in
                   dict(x=x, y=y, bx=bx, by=bx).items()}
         self.result_host = torch.empty(len(self.mine), dtype=torch.float32).pin_memory()
-        self.config = self.describe(world)
+        self.config = self.describe(world, scaling)
 
     @staticmethod
-    def describe(world):
-        return {"workload": "graph embeddings, 1024 graphs per GPU of 64-512 nodes, D=128, "
+    def describe(world, scaling="strong"):
+        total = job_graphs(1024, world, scaling)
+        n = embed_sizes(total)
+        full, unique = term_counts(n, n)
+        return {"workload": "graph embeddings, 1024 graphs"
+                            f"{' per GPU' if scaling == 'weak' else ''} of 64-512 nodes, D=128, "
                             "sigma=1.0, uncentred, pyg_kde_mmd_loss fwd+bwd",
-                "graphs": 1024 * world}
+                "graphs": total, "full_terms_per_step": full, "unique_terms_per_step": unique,
+                "seed": SEED}
 
     def roofline(self, t_tiles, peak_fp32):
         """Tensor roofline: algorithmic flops = full terms x (Gram + weighted
@@ -530,7 +579,7 @@ def run_ours(args):
     from rapidalign_b200 import _lib, build as ra_build
     ra_build.build()
 
-    wl = WORKLOADS[args.workload](rank, world, dev)
+    wl = WORKLOADS[args.workload](rank, world, dev, scaling=args.scaling)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     h2d_times = []
@@ -607,15 +656,21 @@ def run_ours(args):
     t_tiles = wl.tiles_time(max(3, args.steps // 2))
     peak_ops = fp32_peak(dev)
 
+    h2d_local = int(sum(v.numel() * v.element_size() for v in wl.h.values()))
+    d2h_local = int(wl.result_host.numel() * 4)
+    mine = [t_dev, t_e2e, t_tiles, wl.full_local, wl.unique_local, h2d_local, d2h_local]
     if world > 1:
-        tmax = torch.tensor([t_dev, t_e2e], dtype=torch.float64, device=dev)
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        t_dev, t_e2e = tmax.tolist()
-        sums = torch.tensor([wl.full_local, wl.unique_local], dtype=torch.float64, device=dev)
-        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
-        full_all, unique_all = sums.tolist()
+        per_rank = [torch.zeros(len(mine), dtype=torch.float64, device=dev) for _ in range(world)]
+        dist.all_gather(per_rank, torch.tensor(mine, dtype=torch.float64, device=dev))
+        per_rank = [t.tolist() for t in per_rank]
     else:
-        full_all, unique_all = wl.full_local, wl.unique_local
+        per_rank = [mine]
+    t_dev = max(r[0] for r in per_rank)  # the job's time is the slowest rank's
+    t_e2e = max(r[1] for r in per_rank)
+    full_all = sum(r[3] for r in per_rank)
+    unique_all = sum(r[4] for r in per_rank)
+    h2d_all = int(sum(r[5] for r in per_rank))
+    d2h_all = int(sum(r[6] for r in per_rank))
 
     if rank == 0:
         K = args.steps
@@ -633,25 +688,22 @@ def run_ours(args):
                 "unit": "Tops/s (FP32-pipe lane ops, FMA = 1)",
                 "frac": achieved_ops / peak_ops,
                 "peak_source": "measured live: packed-FMA probe kernel (ra_probe_fp32_peak)",
-                "kernel": "tiles3_kernel<1> (fused fwd+bwd tile kernel)",
+                "kernel": "tiles3_kernel<3> (fused fwd+bwd tile kernel; rank 0)",
                 "kernel_ms": t_tiles * 1e3,
                 "ops_per_unique_term": FP32_OPS_PER_UNIQUE_TERM,
                 "issued_ops_per_unique_term": wl.issued_ops,
                 "issued_frac": wl.unique_local * wl.issued_ops / t_tiles / peak_ops,
                 "issued_note": "FP32 ops the kernel issues per unique term (weights folded into "
-                               "the exponent) over the same peak",
+                               "the exponent, no column weight sums without a weight gradient) "
+                               "over the same peak",
                 "traffic": read_traffic() if args.workload == "ragged" else None,
+                "traffic_source": ("dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
+                                   "from the committed ncu capture profiles/traffic.json (not "
+                                   "measured in this run)") if args.workload == "ragged" else None,
             }
         config = dict(wl.config)
-        config.update({
-            "full_terms_per_step": full_all,
-            "unique_terms_per_step": unique_all,
-            "l2": "flushed between steps (512 MB write, outside the timed events)",
-            "sharding": ("none" if world == 1 else
-                         ("LPT partition of graphs across ranks" if wl.scaling == "weak"
-                          else "work items of the one pair split round-robin, one all-reduce")),
-            "seed": SEED,
-        })
+        if abs(config.get("full_terms_per_step", full_all) - full_all) > 1e-6 * full_all:
+            raise SystemExit("the ranks' shares do not add up to the configured workload")
         line = {
             "metric": "Gaussian kernel-term evals/sec fwd+bwd",
             "value": value,
@@ -666,12 +718,27 @@ def run_ours(args):
             "dtype": "f32 (fp64 sums)",
             "data": "synthetic",
             "config": config,
+            "method": {
+                "l2": "flushed between steps (512 MB write, outside the timed events)",
+                "sharding": ("none" if world == 1 else
+                             ("work items of the one pair split round-robin, one all-reduce"
+                              if args.workload == "huge-pair" else
+                              "LPT partition of the graphs across ranks, no collective in "
+                              "the step")),
+                "time": "CUDA events on the launching stream, max over ranks",
+            },
+            "per_rank": {
+                "ms_per_step": [r[0] / K * 1e3 for r in per_rank],
+                "tile_kernel_ms": [r[2] * 1e3 for r in per_rank],
+                "tile_kernel_ms_min": min(r[2] for r in per_rank) * 1e3,
+                "tile_kernel_ms_max": max(r[2] for r in per_rank) * 1e3,
+                "full_terms": [r[3] for r in per_rank],
+            },
             "e2e": {"value": e2e_value, "unit": "terms/s",
                     "ms_per_step": t_e2e / K * 1e3,
                     "h2d_ms_per_step": (statistics.median(h2d_times[-K:]) if h2d_times else None),
-                    "h2d_bytes_per_step": int(sum(v.numel() * v.element_size()
-                                                  for v in wl.h.values())),
-                    "d2h_bytes_per_step": int(wl.result_host.numel() * 4),
+                    "h2d_bytes_per_step": h2d_all,
+                    "d2h_bytes_per_step": d2h_all,
                     "pipeline": "each step's inputs copied from pinned host memory on a side "
                                 "stream while the previous step computes "
                                 "(rapidalign_b200.prefetch.DevicePrefetcher); result read "
@@ -680,7 +747,7 @@ def run_ours(args):
             "roofline": roofline,
             "clocks": clocks,
         }
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(args.workload, budget_s=args.cpu_budget)
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -747,8 +814,7 @@ def run_reference(args):
             full += f_step
     value = full / sum(times)
     wl = WORKLOADS[args.workload]
-    config = dict(wl.describe(world))
-    config["seed"] = SEED
+    config = dict(wl.describe(world, args.scaling))
     line = {
         "impl": "reference",
         "metric": "Gaussian kernel-term evals/sec fwd+bwd",
@@ -759,15 +825,13 @@ def run_reference(args):
         "warmup": args.warmup,
         "ms_per_step": sum(times) / len(times) * 1e3,
         "higher_is_better": True,
-        "scaling": wl.scaling,
+        "scaling": "strong" if args.workload == "huge-pair" else args.scaling,
         "vs_baseline": None,
         "dtype": "f64",
         "data": "synthetic",
         "config": config,
         "cpu_baseline": {"value": value, "unit": "terms/s", "cores": cores, "kind": "port",
-                         "sample": f"{per_step} {label} per step, oracle (C, fp64, OpenMP) "
-                                   "forward+backward sums; the reference's CPU path is "
-                                   "PyTorch and does not travel"},
+                         "sample": f"{per_step} {label} per step", "what": CPU_BASELINE_WHAT},
         "e2e": {"value": value, "unit": "terms/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -782,6 +846,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="ragged", choices=sorted(WORKLOADS),
                     help="ragged (default, the headline workload), huge-pair, dense, embed128")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="strong (default): the same batch at every GPU count; weak: one batch "
+                         "per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--profile-step", action="store_true",

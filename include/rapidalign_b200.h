@@ -115,6 +115,11 @@ typedef struct ra_kde_desc {
                           leave out per-point sums that only grad_wx / grad_wy need
                           (dim <= 3: one FP32 operation per kernel term); a backward
                           that asks for them is then RA_ERR_STATE.  0: keep them. */
+  int32_t deterministic; /* 1: gradients bitwise independent of scheduling.  dim <= 3
+                          then evaluates every kernel term in both orientations with
+                          plain stores instead of adding column sums atomically (about
+                          1.5x the FP32 work).  dim >= 4 is deterministic either way;
+                          K and the losses always are. */
   int32_t test_hooks;  /* 0 in normal use.  Bits of enum ra_test_hook, for tests of the
                           library's own failure paths only. */
 } ra_kde_desc;

@@ -58,6 +58,9 @@ class Spec:
     # int32 [2] device flags of ra_ptr_from_batch for the two sides when ptr_x
     # / ptr_y were built from batch vectors (checked with the error word)
     batch_flags: Optional[Tensor] = None
+    # gradients bitwise independent of scheduling (ra_kde_desc.deterministic);
+    # None: follow torch.are_deterministic_algorithms_enabled() at the forward
+    deterministic: Optional[bool] = None
 
     def desc(self, need_grad: bool, need_sigma_grad: bool) -> _lib.RaKdeDesc:
         d = _lib.RaKdeDesc()
@@ -78,6 +81,10 @@ class Spec:
         d.sigma = float(self.sigma)
         d.engine = int(self.engine)
         d.skip_weight_sums = 1 if (need_grad and self.skip_weight_sums) else 0
+        det = self.deterministic
+        if det is None:
+            det = torch.are_deterministic_algorithms_enabled()
+        d.deterministic = 1 if det else 0
         d.test_hooks = 0
         return d
 
@@ -205,6 +212,9 @@ def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tens
     weights_grad = any(w is not None and w.requires_grad for w in (w_x, w_y))
     if need_grad and not weights_grad and not spec.skip_weight_sums:
         spec = dataclasses.replace(spec, skip_weight_sums=True)
+    if spec.deterministic is None:  # fixed now, so that the backward matches
+        spec = dataclasses.replace(spec,
+                                   deterministic=torch.are_deterministic_algorithms_enabled())
     x32, y32 = _f32(x), _f32(y)
     wx32, wy32 = _f32(w_x), _f32(w_y)
     desc = spec.desc(need_grad, need_sigma_grad)

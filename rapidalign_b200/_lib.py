@@ -70,6 +70,7 @@ class RaKdeDesc(ctypes.Structure):
         ("sigma", ctypes.c_double),
         ("engine", ctypes.c_int32),
         ("skip_weight_sums", ctypes.c_int32),
+        ("deterministic", ctypes.c_int32),
         ("test_hooks", ctypes.c_int32),
     ]
 

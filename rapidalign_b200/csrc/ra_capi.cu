@@ -86,6 +86,7 @@ bool desc_ok(const ra_kde_desc *d) {
     return false;
   if ((d->test_hooks & ~RA_TEST_NO_MMA) != 0) return false;
   if (d->skip_weight_sums != 0 && d->skip_weight_sums != 1) return false;
+  if (d->deterministic != 0 && d->deterministic != 1) return false;
   return true;
 }
 
@@ -196,10 +197,29 @@ unsigned chunk_grid(const Layout &L) {
   return (unsigned)(L.max_chunks < g ? L.max_chunks : g);
 }
 
-int launch_tiles3(int mode, const Tiles3Args &Targs, cudaStream_t st) {
+// The rows-only instantiations of the deterministic mode (a gradient mode:
+// without one the default kernel has no column sums and no atomics anyway).
+int launch_tiles3_rows(int mode, const Tiles3Args &Targs, cudaStream_t st, int sms) {
+  int per_sm = 0;
+  cudaError_t e = mode == 2
+      ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<2, true>, kT3Threads, 0)
+      : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiles3_kernel<1, true>, kT3Threads,
+                                                      0);
+  if (e != cudaSuccess) return RA_ERR_CUDA;
+  if (per_sm < 1) per_sm = 1;
+  if (mode == 2)
+    tiles3_kernel<2, true><<<sms * per_sm, kT3Threads, 0, st>>>(Targs);
+  else
+    tiles3_kernel<1, true><<<sms * per_sm, kT3Threads, 0, st>>>(Targs);
+  ++g_launches;
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_tiles3(int mode, bool rows, const Tiles3Args &Targs, cudaStream_t st) {
   int dev = 0, sms = 0, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (rows && mode != 0) return launch_tiles3_rows(mode, Targs, st, sms);
   cudaError_t e;
   constexpr int T = kT3Threads;
   if (mode == 0)
@@ -309,6 +329,12 @@ int launch_tilesg(int DP, int mode, int64_t grid, const TilesGArgs &T, cudaStrea
 
 int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy, double *Kxy,
                 void *ws, cudaStream_t st);
+
+// D <= 3 in the deterministic mode with gradients: both orientations, rows
+// only (tiles3_kernel<MODE, true>).
+bool rows_only(const ra_kde_desc *d) {
+  return d->dim <= 3 && d->deterministic && d->need_grad;
+}
 
 // Whether a pair may have more than kSmallPts points on a side (the D <= 3
 // layout's chunked passes are launched only then; they skip small pairs).
@@ -466,7 +492,7 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
   // ---- plan ----
   PlanArgs pl;
   pl.P = P;
-  pl.generic = L.packed3 ? 0 : 1;
+  pl.generic = L.packed3 ? (rows_only(d) ? 2 : 0) : 1;
   pl.seg = at<Seg>(ws, L.seg);
   pl.cnt = at<int64_t>(ws, L.cnt);
   pl.boff = at<int64_t>(ws, L.boff);
@@ -533,7 +559,7 @@ int compute_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.itemS = at<double>(ws, L.itemS);
     T.shard_index = sh_idx;
     T.shard_count = sh_cnt;
-    rc = launch_tiles3(mode, T, st);
+    rc = launch_tiles3(mode, rows_only(d), T, st);
     if (rc) return rc;
   } else {
     TilesGArgs T;

@@ -9,7 +9,8 @@ namespace ra {
 
 struct PlanArgs {
   int64_t P;
-  int generic;        // 0: D <= 3 tiles (3 blocks), 1: generic rows (4 orientations)
+  int generic;        // 0: D <= 3 tiles (3 blocks), 1: generic rows (4 orientations),
+                      // 2: D <= 3 tiles, both orientations, rows only (deterministic mode)
   const Seg *seg;
   int64_t *cnt;       // [P]: items of pair p
   int64_t *boff;      // [P * 4]: local start of each block inside the pair's items
@@ -20,7 +21,14 @@ struct PlanArgs {
 };
 
 __device__ __forceinline__ void block_counts(const Seg &s, int generic, int64_t c[4]) {
-  if (!generic) {
+  if (generic == 2) {
+    const int64_t nTx = ceil_div(s.xcount, (int64_t)kTile);
+    const int64_t nTy = ceil_div(s.ycount, (int64_t)kTile);
+    c[0] = nTx;  // x rows vs y cols
+    c[1] = nTx;  // x vs x
+    c[2] = nTy;  // y vs y
+    c[3] = nTy;  // y rows vs x cols
+  } else if (!generic) {
     const int64_t nTx = ceil_div(s.xcount, (int64_t)kTile);
     const int64_t nTy = ceil_div(s.ycount, (int64_t)kTile);
     c[0] = nTx * splits_for(nTy);  // x rows vs y cols
@@ -106,7 +114,7 @@ __global__ void plan_emit_kernel(PlanArgs A) {
   const int64_t base = A.item_off[p];
   const int64_t total = c[0] + c[1] + c[2] + c[3];
   int64_t S[4] = {1, 1, 1, 1};
-  if (!A.generic) {
+  if (A.generic == 0) {
     const int64_t nTx = ceil_div(s.xcount, (int64_t)kTile);
     const int64_t nTy = ceil_div(s.ycount, (int64_t)kTile);
     S[0] = splits_for(nTy);

@@ -212,7 +212,14 @@ __device__ __forceinline__ void tiles3_coltile(
   }
 }
 
-template <int MODE>
+// ROWS (the deterministic mode): every block is evaluated in both
+// orientations with row sums only -- items of blocks 0 (x rows, y columns),
+// 1 (x, x), 2 (y, y) and 3 (y rows, x columns), all column tiles, no column
+// splits -- so each point's record is written by exactly one item with plain
+// stores: no atomic addition anywhere, results independent of scheduling.
+// Costs about 1.5x the FP32 work of the symmetric default (10 operations per
+// term, every term twice, against 13-15 per unique term).
+template <int MODE, bool ROWS = false>
 __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3Args A) {
   constexpr bool GRAD = Tiles3Mode<MODE>::GRAD;
   constexpr bool SIG = Tiles3Mode<MODE>::SIG;
@@ -228,8 +235,8 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     const Item item = A.items[it];
     const Seg sg = A.seg[item.pair];
     const int blk = item.block;
-    const bool sym = blk != 0;
-    const bool rows_y = blk == 2, cols_x = blk == 1;
+    const bool sym = !ROWS && blk != 0;  // a self block visited as its upper triangle
+    const bool rows_y = blk == 2 || blk == 3, cols_x = blk == 1 || blk == 3;
     const int64_t rcnt = rows_y ? sg.ycount : sg.xcount;
     const int64_t ccnt = cols_x ? sg.xcount : sg.ycount;
     const int64_t rtb = (rows_y ? A.tbase_y : A.tbase_x)[item.pair];
@@ -238,7 +245,7 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     const ulonglong2 *__restrict__ ctiles = cols_x ? A.tiles_x : A.tiles_y;
     float *accR = rows_y ? A.acc_y : A.acc_x;
     float *accC = cols_x ? A.acc_x : A.acc_y;
-    const int off = blk == 0 ? kAcc3Block : 0;  // cross block after the self block
+    const int off = (blk == 0 || blk == 3) ? kAcc3Block : 0;  // cross block after the self
     const float *__restrict__ awr = rows_y ? A.aw_y : A.aw_x;
     const double *meta = A.meta + item.pair * (int64_t)meta_stride(3);
     const int rside = rows_y ? 1 : 0, cside = cols_x ? 0 : 1;
@@ -249,7 +256,7 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
 
     // 32-bit tile/column indices: a pair's cloud has < 2^31 points
     const int nTc = (int)ceil_div(ccnt, (int64_t)kTile);
-    const int S = (int)splits_for(nTc);
+    const int S = ROWS ? 1 : (int)splits_for(nTc);
     const int L = (nTc + S - 1) / S;
     const int I = item.tile;
     int J0 = item.split * L;
@@ -332,7 +339,7 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
         f2_t stt[4];
 #pragma unroll
         for (int rp = 0; rp < 4; ++rp) stt[rp] = z2;
-        tiles3_coltile<MODE, false, F, U>(ct, J * kTile, cc,
+        tiles3_coltile<MODE, ROWS, F, U>(ct, J * kTile, cc,
                                           accC0 + J * (kTile * kAcc3Stride), lane, X0, X1, X2,
                                           Aw, stt, G0, G1, G2, sgt);
 #pragma unroll
@@ -394,10 +401,19 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
           upk(G0[rp], g0l, g0h);
           upk(G1[rp], g1l, g1h);
           upk(G2[rp], g2l, g2h);
-          if ((int64_t)I * kTile + r0 < rcnt)
-            red_add_v4(accI + r0 * kAcc3Stride, s_lo, g0l, g1l, g2l);
-          if ((int64_t)I * kTile + r0 + 1 < rcnt)
-            red_add_v4(accI + (r0 + 1) * kAcc3Stride, s_hi, g0h, g1h, g2h);
+          if (ROWS) {  // the record's only writer
+            if ((int64_t)I * kTile + r0 < rcnt)
+              *reinterpret_cast<float4 *>(accI + r0 * kAcc3Stride) =
+                  make_float4(s_lo, g0l, g1l, g2l);
+            if ((int64_t)I * kTile + r0 + 1 < rcnt)
+              *reinterpret_cast<float4 *>(accI + (r0 + 1) * kAcc3Stride) =
+                  make_float4(s_hi, g0h, g1h, g2h);
+          } else {
+            if ((int64_t)I * kTile + r0 < rcnt)
+              red_add_v4(accI + r0 * kAcc3Stride, s_lo, g0l, g1l, g2l);
+            if ((int64_t)I * kTile + r0 + 1 < rcnt)
+              red_add_v4(accI + (r0 + 1) * kAcc3Stride, s_hi, g0h, g1h, g2h);
+          }
         }
       }
     }

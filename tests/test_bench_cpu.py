@@ -30,8 +30,11 @@ def test_reference_arm_line(workload):
     # the reference arm describes the same workload as ours
     sys.path.insert(0, ROOT)
     import bench
-    assert line["config"]["workload"] == bench.WORKLOADS[workload].describe(1)["workload"]
-    assert line["scaling"] == bench.WORKLOADS[workload].scaling
+    # identical config dicts in both arms (the workload and its term counts)
+    assert line["config"] == json.loads(json.dumps(bench.WORKLOADS[workload].describe(1)))
+    assert line["config"]["full_terms_per_step"] > 0
+    assert line["scaling"] == "strong"
+    assert "oracle" in line["cpu_baseline"]["what"]
 
 
 def test_cpu_units_count_terms():
@@ -43,3 +46,23 @@ def test_cpu_units_count_terms():
     x, y = bench.ragged_graph(0)
     n, m = x.shape[0], y.shape[0]
     assert run(1) == float(n * n + m * m + n * m)
+
+
+def test_strong_scaling_shares_cover_the_batch():
+    """The LPT shares of the 4096-graph batch at 1, 2, 4 and 8 ranks add up to
+    the configured term counts (what the multi-GPU line checks at run time)."""
+    sys.path.insert(0, ROOT)
+    import numpy as np
+    import bench
+    from rapidalign_b200.shard import lpt_partition
+    cfg = bench.RaggedWorkload.describe(1)
+    sizes = bench.ragged_sizes(range(cfg["graphs"]))
+    cost = sizes[:, 0] ** 2 + sizes[:, 1] ** 2 + sizes[:, 0] * sizes[:, 1]
+    for world in (1, 2, 4, 8):
+        assert bench.RaggedWorkload.describe(world) == cfg
+        full = 0.0
+        for part in lpt_partition(cost, world):
+            f, _ = bench.term_counts(sizes[part, 0], sizes[part, 1])
+            full += f
+        assert abs(full - cfg["full_terms_per_step"]) <= 1e-9 * full
+    assert bench.RaggedWorkload.describe(4, "weak")["graphs"] == 4 * cfg["graphs"]

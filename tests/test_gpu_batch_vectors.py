@@ -91,8 +91,11 @@ def test_gradients_through_the_batch_vector_path(cuda_device):
         xs, ys = x.clone().requires_grad_(True), y.clone().requires_grad_(True)
         ra.pyg_kde_mmd_loss(xs, ys, sigma=0.25, **kw)[0].sum().backward()
         grads.append((xs.grad, ys.grad))
+    # the default mode adds column sums atomically (order-dependent in the
+    # last bits): equal within rounding, not bitwise
     for g in grads[:2]:
-        assert torch.equal(g[0], grads[2][0]) and torch.equal(g[1], grads[2][1])
+        for a, b in zip(g, grads[2]):
+            assert float((a - b).abs().max()) <= 1e-6 * float(b.abs().max())
 
 
 def test_ptr_from_batch_flags(cuda_device):

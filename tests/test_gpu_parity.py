@@ -234,6 +234,40 @@ def test_deterministic_sums(cuda_device):
         assert torch.allclose(u, w, rtol=1e-6, atol=0)  # no-grad kernel agrees
 
 
+def test_deterministic_mode_gradients_are_bitwise_repeatable(cuda_device):
+    """torch.use_deterministic_algorithms(True) selects the deterministic mode:
+    K, losses and every gradient bitwise equal across runs, and equal to the
+    default mode's within the parity bars (D <= 3: both orientations, rows
+    only, no atomic additions; a big pair with column tiles of many items)."""
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(10)
+    x, y, ptr_x, ptr_y = _ragged(rng, [500, 1200, 77, 5000], [480, 1250, 90, 4800], 3)
+    wx = rng.uniform(0.2, 1.0, x.shape[0]).astype(np.float32)
+    dev = cuda_device
+    args = dict(src_ptr=_cuda(ptr_x, dev), tgt_ptr=_cuda(ptr_y, dev), sigma=0.25)
+
+    def run():
+        xs, ys, ws = _cuda(x, dev, True), _cuda(y, dev, True), _cuda(wx, dev, True)
+        outs = ra.pyg_kde_mmd_loss(xs, ys, src_w=ws, **args)
+        (outs[0].sum() + 0.5 * outs[3].sum()).backward()
+        return [o.detach() for o in outs] + [xs.grad, ys.grad, ws.grad]
+
+    prev = torch.are_deterministic_algorithms_enabled()
+    torch.use_deterministic_algorithms(True)
+    try:
+        a, b = run(), run()
+    finally:
+        torch.use_deterministic_algorithms(prev)
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
+    c = run()  # the default mode
+    assert_loss(_np(a[0]), _np(c[0]), _np(c[1]), _np(c[2]))
+    for u, v in zip(a[1:4], c[1:4]):
+        assert_k(_np(u), _np(v))
+    for u, v in zip(a[4:], c[4:]):
+        assert_grad(_np(u), _np(v))
+
+
 def test_device_detected_errors(cuda_device):
     import rapidalign_b200 as ra
     dev = cuda_device

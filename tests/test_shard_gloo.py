@@ -89,3 +89,50 @@ def test_two_rank_gather_matches_single_process(tmp_path):
     for rank in range(world):
         got = np.load(tmp_path / f"rank{rank}.npy")
         np.testing.assert_allclose(got, full, rtol=0, atol=0)
+
+
+def _packed_worker(rank, world, port, out_dir):
+    import datetime
+    import torch.distributed as dist
+    from rapidalign_b200.shard import _sharded, packed_all_reduce
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    # one collective over a float64 and a float32 buffer
+    f64 = torch.arange(5, dtype=torch.float64) * (rank + 1) + 0.25
+    f32 = torch.full((7,), 0.5 * (rank + 1), dtype=torch.float32)
+    packed_all_reduce(f64, f32)
+    # sharded per-graph results: values of every graph on every rank,
+    # gradients only into this rank's graphs
+    w = torch.ones(6, dtype=torch.float64, requires_grad=True)
+
+    def compute(ids):
+        ids_t = torch.as_tensor(ids, dtype=torch.long)
+        v = w.index_select(0, ids_t) * (ids_t.to(torch.float64) + 1.0)
+        return v, 2 * v, 3 * v, 4 * v
+
+    costs = [5.0, 1.0, 4.0, 2.0, 3.0, 6.0]
+    outs = _sharded(6, costs, compute, None)
+    outs[0].sum().backward()
+    np.savez(os.path.join(out_dir, f"packed{rank}.npz"), f64=f64.numpy(), f32=f32.numpy(),
+             outs=torch.stack([o.detach() for o in outs]).numpy(), grad=w.grad.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_packed_all_reduce_and_sharded_results(tmp_path):
+    world = 2
+    mp.start_processes(_packed_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    costs = [5.0, 1.0, 4.0, 2.0, 3.0, 6.0]
+    parts = lpt_partition(costs, world)
+    for rank in range(world):
+        z = np.load(tmp_path / f"packed{rank}.npz")
+        np.testing.assert_array_equal(z["f64"], np.arange(5) * 3.0 + 0.5)
+        np.testing.assert_array_equal(z["f32"], np.full(7, 1.5, dtype=np.float32))
+        g = np.arange(6) + 1.0
+        np.testing.assert_array_equal(z["outs"], np.stack([g, 2 * g, 3 * g, 4 * g]))
+        grad = np.zeros(6)
+        grad[parts[rank]] = g[parts[rank]]
+        np.testing.assert_array_equal(z["grad"], grad)
