@@ -275,11 +275,17 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
 
     // ---- rows: 8 per lane as 4 packed pairs (padding rows have zero weight) --
     f2_t X0[4], X1[4], X2[4], Aw[4];
+    const float4 *awp = reinterpret_cast<const float4 *>(awr + (rtb + I) * kTile + p * 8);
+    // the rows' weights a~ (loaded again after the column loop, so that a
+    // loop that does not use them -- equal weights -- holds no registers for them)
+    auto load_aw = [&]() {
+      const float4 aw0 = awp[0], aw1 = awp[1];
+      const float awv[8] = {aw0.x, aw0.y, aw0.z, aw0.w, aw1.x, aw1.y, aw1.z, aw1.w};
+#pragma unroll
+      for (int rp = 0; rp < 4; ++rp) Aw[rp] = pk(awv[2 * rp], awv[2 * rp + 1]);
+    };
     {
       const ulonglong2 *rp0 = rt + (rtb + I) * kT3TileU2 + p * 8;
-      const float4 *ap = reinterpret_cast<const float4 *>(awr + (rtb + I) * kTile + p * 8);
-      const float4 aw0 = ap[0], aw1 = ap[1];
-      const float awv[8] = {aw0.x, aw0.y, aw0.z, aw0.w, aw1.x, aw1.y, aw1.z, aw1.w};
 #pragma unroll
       for (int rp = 0; rp < 4; ++rp) {
         const ulonglong2 a0 = rp0[2 * rp], b0 = rp0[2 * rp + 1];                  // x', y'
@@ -287,8 +293,8 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
         X0[rp] = pk(lo_of(a0.x), lo_of(b0.x));
         X1[rp] = pk(lo_of(a0.y), lo_of(b0.y));
         X2[rp] = pk(lo_of(a1.x), lo_of(b1.x));
-        Aw[rp] = pk(awv[2 * rp], awv[2 * rp + 1]);
       }
+      load_aw();
     }
     f2_t st[4], G0[4], G1[4], G2[4], sgt[4];
     const f2_t z2 = pk(0.f, 0.f);
@@ -352,6 +358,7 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
       offdiag(BoolTag<!SIG>{}, BoolTag<false>{});
     else
       offdiag(BoolTag<false>{}, BoolTag<false>{});
+    load_aw();  // a fresh load: the loop's atomics are memory barriers to the compiler
     // row sums accumulated in fp32 over the item: fold once into fp64
 #pragma unroll
     for (int rp = 0; rp < 4; ++rp) {
