@@ -53,6 +53,24 @@
 
 namespace ra {
 
+#ifndef RA_T3_SMEM
+#define RA_T3_SMEM 0
+#endif
+#if RA_T3_SMEM
+// two 2 KB column-tile buffers per warp (4 warps per CTA)
+__shared__ __align__(16) ulonglong2 t3_stage[4][2][2 * kTile];
+// the warp copies one column tile (128 chunks of 16 bytes) into `dst`
+__device__ __forceinline__ void t3_stage_tile(ulonglong2 *dst, const ulonglong2 *src, int lane) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int c = lane + 32 * k;
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst + c);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src + c) : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+#endif
+
 template <bool V>
 struct BoolTag {
   static constexpr bool value = V;
@@ -331,8 +349,24 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     auto offdiag = [&](auto fold_tag, auto uni_tag) {
       constexpr bool F = decltype(fold_tag)::value;
       constexpr bool U = decltype(uni_tag)::value;
+#if RA_T3_SMEM
+      // measurement variant: column tiles staged in shared memory by cp.async
+      // (double-buffered per warp) instead of read through L1 after a prefetch
+      ulonglong2(*buf)[kT3TileU2] = t3_stage[threadIdx.x >> 5];
+      if (J0 < J1) t3_stage_tile(buf[0], ct0 + J0 * kT3TileU2, lane);
+#endif
 #pragma unroll 1
       for (int J = J0; J < J1; ++J) {
+#if RA_T3_SMEM
+        if (J + 1 < J1) {
+          t3_stage_tile(buf[(J + 1 - J0) & 1], ct0 + (J + 1) * kT3TileU2, lane);
+          asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+          asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncwarp();
+        const ulonglong2 *ct = buf[(J - J0) & 1];
+#else
         const ulonglong2 *ct = ct0 + J * kT3TileU2;
         if (J + 1 < J1) {
           // 2 KB tile = 16 lines of 128 bytes: lanes 0..15 prefetch one each
@@ -340,6 +374,7 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
           if (lane < kT3TileU2 / 8)
             asm volatile("prefetch.global.L1 [%0];" ::"l"(nxt + lane * 128));
         }
+#endif
         // row sums: a fresh fp32 subtotal per tile, added to the item's
         // total (64-term then tile-count-long fp32 sums instead of one long one)
         f2_t stt[4];
@@ -350,6 +385,9 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
                                           Aw, stt, G0, G1, G2, sgt);
 #pragma unroll
         for (int rp = 0; rp < 4; ++rp) st[rp] = add2(st[rp], stt[rp]);
+#if RA_T3_SMEM
+        __syncwarp();  // every lane is done with this buffer before it is refilled
+#endif
       }
     };
     if (runi)
