@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
       // ---- GEMM 1: S = X Y^T (3xTF32), one thread issues -------------------
       if (tid == 0 && !A.no_mma) {
         const uint32_t sh = smem_u32(yhi), sl = smem_u32(ylo);
-#pragma unroll 1
+#pragma unroll
         for (int k = 0; k < DP / 8; ++k) {
           // K-major B: LBO = next 4 coordinates (1024 B), SBO = next 8 points (128 B)
           const uint64_t bh = tc_desc(sh + 2 * k * (kTcCols * 16), kTcCols * 16, 128);
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tilestc_kernel(TilesGArgs A) {
         // ---- GEMM 2: T += P Y (3xTF32), B = the transposed Y tile -----------
         if (tid == 0 && !A.no_mma) {
           const uint32_t sh = smem_u32(yth), sl = smem_u32(ytl);
-#pragma unroll 1
+#pragma unroll
           for (int k = 0; k < kTcCols / 8; ++k) {
             // K-major B (N = d, K = j): LBO = next 4 points (128 B), SBO = next 8
             // coordinates (2048 B); a K step of 8 points is 2 chunks = 256 B

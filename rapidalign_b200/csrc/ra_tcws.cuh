@@ -506,7 +506,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
         tc_fence_after();
         {
           const uint32_t sh = smem_u32(yhi), sl = smem_u32(ylo);
-#pragma unroll 1
+#pragma unroll
           for (int k = 0; k < DP / 8; ++k) {
             const uint64_t bh = tc_desc(sh + 2 * k * (kTcCols * 16), kTcCols * 16, 128);
             const uint64_t bl = tc_desc(sl + 2 * k * (kTcCols * 16), kTcCols * 16, 128);
@@ -525,7 +525,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) tilestc_ws_kernel(TilesGArgs A)
           }
           tc_fence_after();
           const uint32_t sh = smem_u32(yth), sl = smem_u32(ytl);
-#pragma unroll 1
+#pragma unroll
           for (int k = 0; k < kTcCols / 8; ++k) {
             const uint64_t bh = tc_desc(sh + k * 256, 128, NQ * 128);
             const uint64_t bl = tc_desc(sl + k * 256, 128, NQ * 128);
