@@ -135,20 +135,40 @@ def uses_tensor_cores(spec: Spec) -> bool:
     return dp in (32, 64, 128)
 
 
+_READ_STREAMS: dict = {}
+
+
+def _read_stream(device) -> torch.cuda.Stream:
+    """A side stream per device for small device-to-host reads: a read
+    enqueued there waits for its data (an event), but the kernels enqueued
+    after it on the compute stream do not wait for the read -- which may
+    queue behind a large host-to-device copy on the copy engines."""
+    s = _READ_STREAMS.get(device.index)
+    if s is None:
+        s = _READ_STREAMS[device.index] = torch.cuda.Stream(device)
+    return s
+
+
 class _ErrorWord:
     """An asynchronous read of the workspace's error word (and, optionally,
-    of batch flags): copied into pinned host memory on the stream and waited
-    for through an event, so the host stops only when it needs the answer --
-    typically while later kernels keep the GPU busy."""
+    of batch flags): copied into pinned host memory on a side stream once the
+    compute stream has produced it, and waited for through an event, so the
+    host stops only when it needs the answer while later kernels keep the GPU
+    busy.  The caller keeps `ws` and `flags` alive until read() returns."""
 
     def __init__(self, ws: Tensor, stream, flags: Optional[Tensor] = None):
         n = 1 + (0 if flags is None else flags.numel())
         self.host = torch.empty(n, dtype=torch.int32, pin_memory=True)
-        self.host[:1].copy_(ws[:4].view(torch.int32), non_blocking=True)
-        if flags is not None:
-            self.host[1:].copy_(flags, non_blocking=True)
-        self.event = torch.cuda.Event()
-        self.event.record(stream)
+        ready = torch.cuda.Event()
+        ready.record(stream)
+        side = _read_stream(ws.device)
+        side.wait_event(ready)
+        with torch.cuda.stream(side):
+            self.host[:1].copy_(ws[:4].view(torch.int32), non_blocking=True)
+            if flags is not None:
+                self.host[1:].copy_(flags, non_blocking=True)
+            self.event = torch.cuda.Event()
+            self.event.record(side)
 
     def read(self):
         self.event.synchronize()

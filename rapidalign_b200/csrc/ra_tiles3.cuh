@@ -54,14 +54,14 @@
 namespace ra {
 
 // Column tiles are staged in shared memory by cp.async, NSTAGE buffers per
-// warp (the next tiles in flight while one is used); RA_T3_SMEM=0 builds the
-// variant that reads them through L1 after a prefetch instead (measured 4.7 %
-// slower on the 4096-graph batch).
+// warp (the next tiles in flight while one is used; 3 measured 0.6 % faster
+// than 2); RA_T3_SMEM=0 builds the variant that reads them through L1 after
+// a prefetch instead (measured 4.7 % slower on the 4096-graph batch).
 #ifndef RA_T3_SMEM
 #define RA_T3_SMEM 1
 #endif
 #ifndef RA_T3_NSTAGE
-#define RA_T3_NSTAGE 2
+#define RA_T3_NSTAGE 3
 #endif
 #if RA_T3_SMEM
 constexpr int kT3Stages = RA_T3_NSTAGE;
