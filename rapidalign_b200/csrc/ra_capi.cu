@@ -251,7 +251,7 @@ void launch_tilesg_dp(int mode, int64_t grid, const TilesGArgs &T, cudaStream_t 
     tilesg_kernel<DP, 0><<<(unsigned)grid, kGenRows, 0, st>>>(T);
   else if (mode == 1)
     tilesg_kernel<DP, 1><<<(unsigned)grid, kGenRows, 0, st>>>(T);
-  else
+  else  // mode 2: sigma gradient
     tilesg_kernel<DP, 2><<<(unsigned)grid, kGenRows, 0, st>>>(T);
 }
 
@@ -292,7 +292,7 @@ template <int DP>
 int launch_tilestc_d(int mode, int64_t max_items, const TilesGArgs &T, cudaStream_t st) {
   if (mode == 0) return launch_tilestc_dm<DP, 0>(max_items, T, st);
   if (mode == 1) return launch_tilestc_dm<DP, 1>(max_items, T, st);
-  return launch_tilestc_dm<DP, 2>(max_items, T, st);
+  return launch_tilestc_dm<DP, 2>(max_items, T, st);  // mode 2: sigma gradient
 }
 
 int launch_tilestc(int DP, int mode, int64_t max_items, const TilesGArgs &T, cudaStream_t st) {
@@ -580,8 +580,11 @@ int compute_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.err = at<int>(ws, L.hdr + kHdrErr);
     T.no_mma = (d->test_hooks & RA_TEST_NO_MMA) ? 1 : 0;
     T.spin_limit = T.no_mma ? 4096u : kTcSpinLimit;
-    rc = use_tensor_cores(d, L.DP) ? launch_tilestc(L.DP, mode, L.max_items, T, st)
-                                   : launch_tilesg(L.DP, mode, L.max_items, T, st);
+    // the generic kernels keep every per-point sum anyway: mode 3 (no column
+    // weight sums, a D <= 3 distinction) is their mode 1
+    const int gmode = mode == 3 ? 1 : mode;
+    rc = use_tensor_cores(d, L.DP) ? launch_tilestc(L.DP, gmode, L.max_items, T, st)
+                                   : launch_tilesg(L.DP, gmode, L.max_items, T, st);
     if (rc) return rc;
   }
 
@@ -626,7 +629,11 @@ int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy,
   // pairs of at most kSmallPts points per side have at most 192 items
   static_assert(kWarpItems >= 3 * (kSmallPts / kTile), "small pairs fit one warp");
   if (may_have_large_pairs(d)) {
-    finalize_kernel<256><<<(unsigned)P, 256, 0, st>>>(fa);
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t g = (int64_t)(sms > 0 ? sms : 1) * 4;  // a stride over the pairs
+    finalize_kernel<256><<<(unsigned)(P < g ? P : g), 256, 0, st>>>(fa);
     ++g_launches;
   }
   return cuda_status(cudaGetLastError());

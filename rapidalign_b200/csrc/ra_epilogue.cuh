@@ -85,37 +85,37 @@ __global__ void __launch_bounds__(256) finalize_warp_kernel(FinalizeArgs A) {
 template <int NT>
 __global__ void __launch_bounds__(NT) finalize_kernel(FinalizeArgs A) {
   __shared__ double sh[NT / 32];
-  const int64_t p = blockIdx.x;
-  if (p >= A.P) return;
-  int64_t base, end;
-  pair_items(A, p, base, end);
-  if (end - base <= kWarpItems) return;  // finalize_warp_kernel
-  const int kidx[3] = {2, 0, 1};
+  for (int64_t p = blockIdx.x; p < A.P; p += gridDim.x) {
+    int64_t base, end;
+    pair_items(A, p, base, end);
+    if (end - base <= kWarpItems) continue;  // finalize_warp_kernel
+    const int kidx[3] = {2, 0, 1};
 #pragma unroll 1
-  for (int b = 0; b < 3; ++b) {
-    int64_t b0 = base + A.boff[p * 4 + b];
-    const int64_t b1 = b < 2 ? base + A.boff[p * 4 + b + 1] : base + A.boff[p * 4 + 3];
-    const int64_t e = b1 < end ? b1 : end;
-    if (b0 > e) b0 = e;
-    double k[4] = {0.0, 0.0, 0.0, 0.0}, s[4] = {0.0, 0.0, 0.0, 0.0};
-    int64_t i = b0 + threadIdx.x;
-    for (; i + 3 * NT < e; i += 4 * NT) {
+    for (int b = 0; b < 3; ++b) {
+      int64_t b0 = base + A.boff[p * 4 + b];
+      const int64_t b1 = b < 2 ? base + A.boff[p * 4 + b + 1] : base + A.boff[p * 4 + 3];
+      const int64_t e = b1 < end ? b1 : end;
+      if (b0 > e) b0 = e;
+      double k[4] = {0.0, 0.0, 0.0, 0.0}, s[4] = {0.0, 0.0, 0.0, 0.0};
+      int64_t i = b0 + threadIdx.x;
+      for (; i + 3 * NT < e; i += 4 * NT) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        k[u] += A.itemK[i + u * NT];
-        s[u] += A.itemS[i + u * NT];
+        for (int u = 0; u < 4; ++u) {
+          k[u] += A.itemK[i + u * NT];
+          s[u] += A.itemS[i + u * NT];
+        }
       }
-    }
-    for (; i < e; i += NT) {
-      k[0] += A.itemK[i];
-      s[0] += A.itemS[i];
-    }
-    const double kt = block_sum((k[0] + k[1]) + (k[2] + k[3]), sh);
-    const double st = block_sum((s[0] + s[1]) + (s[2] + s[3]), sh);
-    if (threadIdx.x == 0) {
-      A.K_out[kidx[b]][p] = kt;
-      A.K_ws[kidx[b] * A.P + p] = kt;
-      A.S_ws[kidx[b] * A.P + p] = st;
+      for (; i < e; i += NT) {
+        k[0] += A.itemK[i];
+        s[0] += A.itemS[i];
+      }
+      const double kt = block_sum((k[0] + k[1]) + (k[2] + k[3]), sh);
+      const double st = block_sum((s[0] + s[1]) + (s[2] + s[3]), sh);
+      if (threadIdx.x == 0) {
+        A.K_out[kidx[b]][p] = kt;
+        A.K_ws[kidx[b] * A.P + p] = kt;
+        A.S_ws[kidx[b] * A.P + p] = st;
+      }
     }
   }
 }
