@@ -464,42 +464,28 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
       g_launches += 2;
     }
   } else {
-    // small pairs: one CTA per pair (sums, metadata, packing)
-    const unsigned sgrid = (unsigned)(P < (int64_t)cgrid ? P : (int64_t)cgrid);
-    switch (L.DP) {
-      case 4: prepw_small_kernel<4><<<sgrid, 256, 0, st>>>(pa); break;
-      case 8: prepw_small_kernel<8><<<sgrid, 256, 0, st>>>(pa); break;
-      case 16: prepw_small_kernel<16><<<sgrid, 256, 0, st>>>(pa); break;
-      case 32: prepw_small_kernel<32><<<sgrid, 256, 0, st>>>(pa); break;
-      case 64: prepw_small_kernel<64><<<sgrid, 256, 0, st>>>(pa); break;
-      case 128: prepw_small_kernel<128><<<sgrid, 256, 0, st>>>(pa); break;
-      default: prepw_small_kernel<256><<<sgrid, 256, 0, st>>>(pa); break;
-    }
-    ++g_launches;
-    if (may_be_large) {  // the chunked passes, which skip the small pairs
-      if (L.DP == 32)
-        statsw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
-      else if (L.DP == 64)
-        statsw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
-      else if (L.DP == 128)
-        statsw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
-      else if (L.DP == 256)
-        statsw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
-      else
-        stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
-      meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
-      if (d->dim % 4 == 0 && L.DP == 32)
-        packgw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
-      else if (d->dim % 4 == 0 && L.DP == 64)
-        packgw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
-      else if (d->dim % 4 == 0 && L.DP == 128)
-        packgw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
-      else if (d->dim % 4 == 0 && L.DP == 256)
-        packgw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
-      else
-        packg_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
-      g_launches += 3;
-    }
+    if (L.DP == 32)
+      statsw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.DP == 64)
+      statsw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.DP == 128)
+      statsw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.DP == 256)
+      statsw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
+    else
+      stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+    meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
+    if (d->dim % 4 == 0 && L.DP == 32)
+      packgw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
+    else if (d->dim % 4 == 0 && L.DP == 64)
+      packgw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
+    else if (d->dim % 4 == 0 && L.DP == 128)
+      packgw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
+    else if (d->dim % 4 == 0 && L.DP == 256)
+      packgw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
+    else
+      packg_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
+    g_launches += 3;
   }
   if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
 
@@ -653,20 +639,6 @@ int finish_impl(const ra_kde_desc *d, const Layout &L, double *Kxx, double *Kyy,
   return cuda_status(cudaGetLastError());
 }
 
-// The wide-point epilogue (DP >= 32): the one-CTA-per-pair kernel for small
-// pairs, and the chunked pair of passes when a pair can be large.
-template <int DP>
-void launch_epigw(unsigned sgrid, unsigned cgrid, bool large, const EpilogueArgs &ea,
-                  cudaStream_t st) {
-  epigw_small_kernel<DP><<<sgrid, 256, 0, st>>>(ea);
-  ++g_launches;
-  if (large) {
-    epigw_partial_kernel<DP><<<cgrid, 256, 0, st>>>(ea);
-    epigw_write_kernel<DP><<<cgrid, 256, 0, st>>>(ea);
-    g_launches += 2;
-  }
-}
-
 int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *coef,
                   const ra_kde_grads *gr, void *ws, size_t ws_bytes, cudaStream_t st) {
   const Layout L = make_layout(d);
@@ -736,20 +708,29 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
       g_launches += 2;
     }
   } else if (L.DP >= 32) {
-    // small pairs: one CTA per pair and side; large pairs: two chunked passes
-    const unsigned sgrid = (unsigned)(2 * P < (int64_t)cgrid ? 2 * P : (int64_t)cgrid);
-    const bool large = may_have_large_pairs(d);
     switch (L.DP) {
-      case 32: launch_epigw<32>(sgrid, cgrid, large, ea, st); break;
-      case 64: launch_epigw<64>(sgrid, cgrid, large, ea, st); break;
-      case 128: launch_epigw<128>(sgrid, cgrid, large, ea, st); break;
-      default: launch_epigw<256>(sgrid, cgrid, large, ea, st); break;
+      case 32:
+        epigw_partial_kernel<32><<<cgrid, 256, 0, st>>>(ea);
+        epigw_write_kernel<32><<<cgrid, 256, 0, st>>>(ea);
+        break;
+      case 64:
+        epigw_partial_kernel<64><<<cgrid, 256, 0, st>>>(ea);
+        epigw_write_kernel<64><<<cgrid, 256, 0, st>>>(ea);
+        break;
+      case 128:
+        epigw_partial_kernel<128><<<cgrid, 256, 0, st>>>(ea);
+        epigw_write_kernel<128><<<cgrid, 256, 0, st>>>(ea);
+        break;
+      default:
+        epigw_partial_kernel<256><<<cgrid, 256, 0, st>>>(ea);
+        epigw_write_kernel<256><<<cgrid, 256, 0, st>>>(ea);
+        break;
     }
   } else {
     epig_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
     epig_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
   }
-  if (!L.packed3 && L.DP < 32) g_launches += 2;
+  if (!L.packed3) g_launches += 2;
   if (ea.grad_sigma != nullptr) {
     sigma_grad_kernel<<<(unsigned)ceil_div(P, 256), 256, 0, st>>>(ea);
     ++g_launches;

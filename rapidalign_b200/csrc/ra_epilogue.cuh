@@ -523,73 +523,62 @@ __device__ __forceinline__ double genw_gxt(const EpilogueArgs &A, const float *a
   return -a * E.k_x * (E.cs * Gs + E.cc * Gc);
 }
 
-// The side's cloud-wide sums over points [b, e) (warp w takes points b + w,
-// b + w + 8, ...; the next point's loads are in flight while this one is
-// summed): R[k] += dL/dx~ of coordinate lane + 32 k, Q += a dL/da.
-template <int DP>
-__device__ __forceinline__ void epigw_sum_points(const EpilogueArgs &A, const EpiSide &E,
-                                                 int side, int64_t b, int64_t e, int wid,
-                                                 int lane, double (&R)[DP / 32], double &Q) {
-  constexpr int NW = 8, KL = DP / 32;
-  const int D = A.D;
-  const float *accb = side == 0 ? A.accX : A.accY;
-  const float *Gp = side == 0 ? A.Gx : A.Gy;
-  const float *Ap = side == 0 ? A.Ax : A.Ay;
-  struct Pt {
-    float a, ss, sc, ts[KL], tc[KL], xp[KL];
-  };
-  auto load = [&](int64_t i) {
-    Pt q;
-    const int64_t g = E.s + i;
-    const float *acc = accb + g * A.acc_stride;
-    q.a = Ap[g];
-    q.ss = acc[2 * DP];
-    q.sc = acc[2 * DP + 1];
-#pragma unroll
-    for (int k = 0; k < KL; ++k) {
-      const int d = lane + 32 * k;
-      q.ts[k] = d < D ? acc[d] : 0.f;
-      q.tc[k] = d < D ? acc[DP + d] : 0.f;
-      q.xp[k] = d < D ? Gp[g * DP + d] : 0.f;
-    }
-    return q;
-  };
-  Pt cur;
-  if (b + wid < e) cur = load(b + wid);
-  for (int64_t i = b + wid; i < e; i += NW) {
-    Pt nxt;
-    if (i + NW < e) nxt = load(i + NW);
-    const double a = cur.a, s_self = cur.ss, s_cross = cur.sc;
-#pragma unroll
-    for (int k = 0; k < KL; ++k) {
-      if (lane + 32 * k < D) {
-        const double xp = cur.xp[k];
-        const double Gs = xp * s_self - (double)cur.ts[k];
-        const double Gc = xp * s_cross - (double)cur.tc[k];
-        R[k] += -a * E.k_x * (E.cs * Gs + E.cc * Gc);
-      }
-    }
-    // the stored self sums leave out the diagonal term (k_ii = 1, weight a_i)
-    Q += a * (E.cs * (s_self + a) + E.cc * s_cross);
-    cur = nxt;
-  }
-}
-
 template <int DP>
 __global__ void __launch_bounds__(256) epigw_partial_kernel(EpilogueArgs A) {
   constexpr int NW = 8, KL = DP / 32;
   __shared__ double sh[NW][DP + 1];
   const ChunkMap M{A.P, A.choff, A.chx};
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const int rs = stats_stride(DP);
+  const int D = A.D, rs = stats_stride(DP);
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
-    if (small_pair(A.seg[p])) return;  // epigw_small_kernel
     const EpiSide E = epi_side(A, p, side);
+    const float *accb = side == 0 ? A.accX : A.accY;
+    const float *Gp = side == 0 ? A.Gx : A.Gy;
+    const float *Ap = side == 0 ? A.Ax : A.Ay;
     const int64_t b = c * kChunk, e = b + kChunk < E.count ? b + kChunk : E.count;
     double R[KL], Q = 0.0;
 #pragma unroll
     for (int k = 0; k < KL; ++k) R[k] = 0.0;
-    epigw_sum_points<DP>(A, E, side, b, e, wid, lane, R, Q);
+    // software-pipelined: the next point's loads are in flight while this
+    // one is summed (same points, same order)
+    struct Pt {
+      float a, ss, sc, ts[KL], tc[KL], xp[KL];
+    };
+    auto load = [&](int64_t i) {
+      Pt q;
+      const int64_t g = E.s + i;
+      const float *acc = accb + g * A.acc_stride;
+      q.a = Ap[g];
+      q.ss = acc[2 * DP];
+      q.sc = acc[2 * DP + 1];
+#pragma unroll
+      for (int k = 0; k < KL; ++k) {
+        const int d = lane + 32 * k;
+        q.ts[k] = d < D ? acc[d] : 0.f;
+        q.tc[k] = d < D ? acc[DP + d] : 0.f;
+        q.xp[k] = d < D ? Gp[g * DP + d] : 0.f;
+      }
+      return q;
+    };
+    Pt cur;
+    if (b + wid < e) cur = load(b + wid);
+    for (int64_t i = b + wid; i < e; i += NW) {
+      Pt nxt;
+      if (i + NW < e) nxt = load(i + NW);
+      const double a = cur.a, s_self = cur.ss, s_cross = cur.sc;
+#pragma unroll
+      for (int k = 0; k < KL; ++k) {
+        if (lane + 32 * k < D) {
+          const double xp = cur.xp[k];
+          const double Gs = xp * s_self - (double)cur.ts[k];
+          const double Gc = xp * s_cross - (double)cur.tc[k];
+          R[k] += -a * E.k_x * (E.cs * Gs + E.cc * Gc);
+        }
+      }
+      // the stored self sums leave out the diagonal term (k_ii = 1, weight a_i)
+      Q += a * (E.cs * (s_self + a) + E.cc * s_cross);
+      cur = nxt;
+    }
 #pragma unroll
     for (int k = 0; k < KL; ++k) sh[wid][lane + 32 * k] = R[k];
     if (lane == 0) sh[wid][DP] = Q;
@@ -605,169 +594,15 @@ __global__ void __launch_bounds__(256) epigw_partial_kernel(EpilogueArgs A) {
   });
 }
 
-// Gradients of points [b, e) of one side (zeros for the padded tail of a
-// dense row), given the side's totals Rsh[0..DP) = R, and Qt = Q - mu . R.
-template <int DP>
-__device__ __forceinline__ void epigw_write_points(const EpilogueArgs &A, const EpiSide &E,
-                                                   int side, int64_t b, int64_t e,
-                                                   const double *Rsh, double Qt, int tid,
-                                                   int lane, int wid) {
-  constexpr int NW = 8, KL = DP / 32;
-  const int D = A.D;
-  const float *pts = side == 0 ? A.x : A.y;
-  const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
-  const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-  float *gout = side == 0 ? A.grad_x : A.grad_y;
-  double *wout = side == 0 ? A.grad_wx : A.grad_wy;
-  const float *accb = side == 0 ? A.accX : A.accY;
-  const float *Gp = side == 0 ? A.Gx : A.Gy;
-  const float *Ap = side == 0 ? A.Ax : A.Ay;
-
-  // weight gradients: a warp per point, 4 points in flight, x . R by shuffles
-  if (wout != nullptr && wmode != 3) {
-    for (int64_t i0 = b + 4 * wid; i0 < e; i0 += 4 * NW) {
-      double xr[4] = {0.0, 0.0, 0.0, 0.0};
-      if (A.center) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int64_t i = i0 + u;
-          if (i < e && i < E.count) {
-            const int64_t g = E.s + i;
-#pragma unroll
-            for (int k = 0; k < KL; ++k) {
-              const int dd = lane + 32 * k;
-              if (dd < D) xr[u] += (double)pts[g * D + dd] * Rsh[dd];
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) xr[u] = warp_sum(xr[u]);
-      if (lane < 4) {
-        const int64_t i = i0 + lane;
-        if (i < e) {
-          const int64_t g = E.s + i;
-          double gw = 0.0;
-          if (i < E.count) {
-            const float *acc = accb + g * A.acc_stride;
-            const double a = Ap[g], s_self = acc[2 * DP], s_cross = acc[2 * DP + 1];
-            const double ga = E.cs * (s_self + a) + E.cc * s_cross;
-            const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
-            const double xrl = lane == 0 ? xr[0] : lane == 1 ? xr[1] : lane == 2 ? xr[2] : xr[3];
-            gw = weight_grad(wmode, m, ga - xrl, Qt, E);
-          }
-          wout[g] = gw;
-        }
-      }
-    }
-  }
-  // position gradients over flat elements: float4 (point, 4 coordinates)
-  // when D is a multiple of 4 -- a thread then keeps one coordinate chunk
-  // and loads each point's scalars once per 4 coordinates -- else scalars
-  if (gout != nullptr && D % 4 == 0) {
-    constexpr int NC = DP / 4;
-    const int ncd = D / 4;  // chunks that hold coordinates
-    const int cc = tid % NC;
-    const int64_t nel = (e - b) * NC;
-    constexpr int kAhead = 2;  // 4 doubles the registers (126 -> 156) for nothing
-    for (int64_t k0 = tid; k0 < nel; k0 += kAhead * 256) {
-      // the loads of kAhead elements go out before the first store (a
-      // store to gout might alias them as far as the compiler knows)
-      float4 ts[kAhead], tc[kAhead], xp[kAhead];
-      float av[kAhead], ssv[kAhead], scv[kAhead];
-#pragma unroll
-      for (int u = 0; u < kAhead; ++u) {
-        const int64_t k = k0 + u * 256;
-        const int64_t i = b + k / NC;
-        if (k < nel && cc < ncd && i < E.count) {
-          const int64_t g = E.s + i;
-          const float *acc = accb + g * A.acc_stride;
-          av[u] = Ap[g];
-          ssv[u] = acc[2 * DP];
-          scv[u] = acc[2 * DP + 1];
-          ts[u] = *reinterpret_cast<const float4 *>(acc + 4 * cc);
-          tc[u] = *reinterpret_cast<const float4 *>(acc + DP + 4 * cc);
-          xp[u] = *reinterpret_cast<const float4 *>(Gp + g * DP + 4 * cc);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kAhead; ++u) {
-        const int64_t k = k0 + u * 256;
-        if (k < nel && cc < ncd) {
-          const int64_t i = b + k / NC;
-          const int64_t g = E.s + i;
-          float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (i < E.count) {
-            const double a = av[u], s_self = ssv[u], s_cross = scv[u];
-            const float tsv[4] = {ts[u].x, ts[u].y, ts[u].z, ts[u].w};
-            const float tcv[4] = {tc[u].x, tc[u].y, tc[u].z, tc[u].w};
-            const float xv[4] = {xp[u].x, xp[u].y, xp[u].z, xp[u].w};
-            float r[4];
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              const double Gs = xv[v] * s_self - (double)tsv[v];
-              const double Gc = xv[v] * s_cross - (double)tcv[v];
-              double gx = -a * E.k_x * (E.cs * Gs + E.cc * Gc);
-              if (A.center) gx -= a * Rsh[4 * cc + v];
-              r[v] = (float)gx;
-            }
-            o = make_float4(r[0], r[1], r[2], r[3]);
-          }
-          *reinterpret_cast<float4 *>(gout + g * D + 4 * cc) = o;
-        }
-      }
-    }
-  } else if (gout != nullptr) {
-    const int64_t nel = (e - b) * D;
-    for (int64_t k0 = tid; k0 < nel; k0 += 4 * 256) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t k = k0 + u * 256;
-        if (k < nel) {
-          const int64_t i = b + k / D;
-          const int dd = (int)(k % D);
-          const int64_t g = E.s + i;
-          double gx = 0.0;
-          if (i < E.count) {
-            const float *acc = accb + g * A.acc_stride;
-            const double a = Ap[g];
-            gx = genw_gxt(A, acc, a, acc[2 * DP], acc[2 * DP + 1], Gp + g * DP, dd, E);
-            if (A.center) gx -= a * Rsh[dd];
-          }
-          gout[g * D + dd] = (float)gx;
-        }
-      }
-    }
-  }
-}
-
-// The side's totals R (Rsh[0..DP)) and Q (Rsh[DP]) are in shared memory;
-// Qt = Q - mu . R for the centering Jacobian (all threads, one barrier).
-template <int DP>
-__device__ __forceinline__ double epigw_qt(const EpilogueArgs &A, const EpiSide &E,
-                                          const double *Rsh, double *red, int tid, int lane,
-                                          int wid) {
-  constexpr int NW = 8;
-  double mr = 0.0;
-  for (int t = tid; t < A.D; t += 256) mr += E.mu[t] * Rsh[t];
-  mr = warp_sum(mr);
-  if (lane == 0) red[wid] = mr;
-  __syncthreads();
-  double muR = 0.0;
-  for (int q = 0; q < NW; ++q) muR += red[q];
-  return A.center ? Rsh[DP] - muR : Rsh[DP];
-}
-
 template <int DP>
 __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
-  constexpr int NW = 8;
+  constexpr int NW = 8, KL = DP / 32;
   __shared__ double Rsh[DP + 1];
   __shared__ double red[NW];
   const ChunkMap M{A.P, A.choff, A.chx};
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const int rs = stats_stride(DP);
+  const int D = A.D, rs = stats_stride(DP);
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t first, int64_t n) {
-    if (small_pair(A.seg[p])) return;  // epigw_small_kernel
     const EpiSide E = epi_side(A, p, side);
     // the side's totals, summed over its chunks in order
     for (int t = tid; t < DP + 1; t += 256) {
@@ -776,47 +611,143 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
       Rsh[t] = tot;  // Rsh[DP] = Q
     }
     __syncthreads();
-    const double Qt = epigw_qt<DP>(A, E, Rsh, red, tid, lane, wid);
+    double mr = 0.0;
+    for (int t = tid; t < D; t += 256) mr += E.mu[t] * Rsh[t];
+    mr = warp_sum(mr);
+    if (lane == 0) red[wid] = mr;
+    __syncthreads();
+    double muR = 0.0;
+    for (int q = 0; q < NW; ++q) muR += red[q];
+    const double Qt = A.center ? Rsh[DP] - muR : Rsh[DP];
+
+    const float *pts = side == 0 ? A.x : A.y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    float *gout = side == 0 ? A.grad_x : A.grad_y;
+    double *wout = side == 0 ? A.grad_wx : A.grad_wy;
+    const float *accb = side == 0 ? A.accX : A.accY;
+    const float *Gp = side == 0 ? A.Gx : A.Gy;
+    const float *Ap = side == 0 ? A.Ax : A.Ay;
     const int64_t b = c * kChunk, e = b + kChunk < E.span ? b + kChunk : E.span;
-    epigw_write_points<DP>(A, E, side, b, e, Rsh, Qt, tid, lane, wid);
+
+    // weight gradients: a warp per point, 4 points in flight, x . R by shuffles
+    if (wout != nullptr && wmode != 3) {
+      for (int64_t i0 = b + 4 * wid; i0 < e; i0 += 4 * NW) {
+        double xr[4] = {0.0, 0.0, 0.0, 0.0};
+        if (A.center) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int64_t i = i0 + u;
+            if (i < e && i < E.count) {
+              const int64_t g = E.s + i;
+#pragma unroll
+              for (int k = 0; k < KL; ++k) {
+                const int dd = lane + 32 * k;
+                if (dd < D) xr[u] += (double)pts[g * D + dd] * Rsh[dd];
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) xr[u] = warp_sum(xr[u]);
+        if (lane < 4) {
+          const int64_t i = i0 + lane;
+          if (i < e) {
+            const int64_t g = E.s + i;
+            double gw = 0.0;
+            if (i < E.count) {
+              const float *acc = accb + g * A.acc_stride;
+              const double a = Ap[g], s_self = acc[2 * DP], s_cross = acc[2 * DP + 1];
+              const double ga = E.cs * (s_self + a) + E.cc * s_cross;
+              const double m = (mask == nullptr || mask[g] != 0) ? 1.0 : 0.0;
+              const double xrl = lane == 0 ? xr[0] : lane == 1 ? xr[1] : lane == 2 ? xr[2] : xr[3];
+              gw = weight_grad(wmode, m, ga - xrl, Qt, E);
+            }
+            wout[g] = gw;
+          }
+        }
+      }
+    }
+    // position gradients over flat elements: float4 (point, 4 coordinates)
+    // when D is a multiple of 4 -- a thread then keeps one coordinate chunk
+    // and loads each point's scalars once per 4 coordinates -- else scalars
+    if (gout != nullptr && D % 4 == 0) {
+      constexpr int NC = DP / 4;
+      const int ncd = D / 4;  // chunks that hold coordinates
+      const int cc = tid % NC;
+      const int64_t nel = (e - b) * NC;
+      constexpr int kAhead = 2;  // 4 doubles the registers (126 -> 156) for nothing
+      for (int64_t k0 = tid; k0 < nel; k0 += kAhead * 256) {
+        // the loads of kAhead elements go out before the first store (a
+        // store to gout might alias them as far as the compiler knows)
+        float4 ts[kAhead], tc[kAhead], xp[kAhead];
+        float av[kAhead], ssv[kAhead], scv[kAhead];
+#pragma unroll
+        for (int u = 0; u < kAhead; ++u) {
+          const int64_t k = k0 + u * 256;
+          const int64_t i = b + k / NC;
+          if (k < nel && cc < ncd && i < E.count) {
+            const int64_t g = E.s + i;
+            const float *acc = accb + g * A.acc_stride;
+            av[u] = Ap[g];
+            ssv[u] = acc[2 * DP];
+            scv[u] = acc[2 * DP + 1];
+            ts[u] = *reinterpret_cast<const float4 *>(acc + 4 * cc);
+            tc[u] = *reinterpret_cast<const float4 *>(acc + DP + 4 * cc);
+            xp[u] = *reinterpret_cast<const float4 *>(Gp + g * DP + 4 * cc);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kAhead; ++u) {
+          const int64_t k = k0 + u * 256;
+          if (k < nel && cc < ncd) {
+            const int64_t i = b + k / NC;
+            const int64_t g = E.s + i;
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < E.count) {
+              const double a = av[u], s_self = ssv[u], s_cross = scv[u];
+              const float tsv[4] = {ts[u].x, ts[u].y, ts[u].z, ts[u].w};
+              const float tcv[4] = {tc[u].x, tc[u].y, tc[u].z, tc[u].w};
+              const float xv[4] = {xp[u].x, xp[u].y, xp[u].z, xp[u].w};
+              float r[4];
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                const double Gs = xv[v] * s_self - (double)tsv[v];
+                const double Gc = xv[v] * s_cross - (double)tcv[v];
+                double gx = -a * E.k_x * (E.cs * Gs + E.cc * Gc);
+                if (A.center) gx -= a * Rsh[4 * cc + v];
+                r[v] = (float)gx;
+              }
+              o = make_float4(r[0], r[1], r[2], r[3]);
+            }
+            *reinterpret_cast<float4 *>(gout + g * D + 4 * cc) = o;
+          }
+        }
+      }
+    } else if (gout != nullptr) {
+      const int64_t nel = (e - b) * D;
+      for (int64_t k0 = tid; k0 < nel; k0 += 4 * 256) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t k = k0 + u * 256;
+          if (k < nel) {
+            const int64_t i = b + k / D;
+            const int dd = (int)(k % D);
+            const int64_t g = E.s + i;
+            double gx = 0.0;
+            if (i < E.count) {
+              const float *acc = accb + g * A.acc_stride;
+              const double a = Ap[g];
+              gx = genw_gxt(A, acc, a, acc[2 * DP], acc[2 * DP + 1], Gp + g * DP, dd, E);
+              if (A.center) gx -= a * Rsh[dd];
+            }
+            gout[g * D + dd] = (float)gx;
+          }
+        }
+      }
+    }
     __syncthreads();  // Rsh and red are rewritten by the next chunk
   });
-}
-
-// Pairs with at most kSmallPts points per side (small_pair): one CTA per pair
-// and side sums R and Q over the side's points (fixed order: the warps' sums
-// in order), then writes their gradients (the records are re-read from
-// cache) -- the records cross DRAM once, and no chunk records are needed.
-template <int DP>
-__global__ void __launch_bounds__(256) epigw_small_kernel(EpilogueArgs A) {
-  constexpr int NW = 8, KL = DP / 32;
-  __shared__ double sh[NW][DP + 1];
-  __shared__ double Rsh[DP + 1];
-  __shared__ double red[NW];
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  for (int64_t u = blockIdx.x; u < 2 * A.P; u += gridDim.x) {
-    const int64_t p = u >> 1;
-    const int side = (int)(u & 1);
-    if (!small_pair(A.seg[p])) continue;
-    const EpiSide E = epi_side(A, p, side);
-    double R[KL], Q = 0.0;
-#pragma unroll
-    for (int k = 0; k < KL; ++k) R[k] = 0.0;
-    epigw_sum_points<DP>(A, E, side, 0, E.count, wid, lane, R, Q);
-#pragma unroll
-    for (int k = 0; k < KL; ++k) sh[wid][lane + 32 * k] = R[k];
-    if (lane == 0) sh[wid][DP] = Q;
-    __syncthreads();
-    for (int t = tid; t < DP + 1; t += 256) {
-      double tot = 0.0;
-      for (int q = 0; q < NW; ++q) tot += sh[q][t];
-      Rsh[t] = tot;
-    }
-    __syncthreads();
-    const double Qt = epigw_qt<DP>(A, E, Rsh, red, tid, lane, wid);
-    epigw_write_points<DP>(A, E, side, 0, E.span, Rsh, Qt, tid, lane, wid);
-    __syncthreads();  // sh, Rsh and red are rewritten by the next unit
-  }
 }
 
 }  // namespace ra

@@ -100,26 +100,6 @@ __device__ __forceinline__ float eff_weight(const float *w, const uint8_t *mask,
   return v;
 }
 
-// Error-free accumulation in float32 (Knuth's TwoSum, the running error kept
-// in a second float): a double-float sum of a few thousand floats, free of
-// float-to-double conversions per point, which run on the SM's narrow
-// conversion pipe.
-struct FSum {
-  float hi = 0.f, lo = 0.f;
-  __device__ __forceinline__ void add(float v) {
-    const float s = hi + v, bp = s - hi;
-    lo += (hi - (s - bp)) + (v - bp);
-    hi = s;
-  }
-  // adds the exact product a * b (TwoProduct by FMA)
-  __device__ __forceinline__ void add_prod(float a, float b) {
-    const float q = a * b;
-    add(q);
-    lo += fmaf(a, b, -q);
-  }
-  __device__ __forceinline__ double value() const { return (double)hi + (double)lo; }
-};
-
 // Segment bounds, chunk counts and the chunk map; one CTA of 1024 threads.
 // Ragged bounds come from the running maximum of ptr, clamped to [0, num]:
 // for a valid ptr that is ptr itself, and for a malformed one (reported
@@ -253,7 +233,6 @@ __global__ void __launch_bounds__(NT) stats_kernel(PrepArgs A) {
   const int lanes = NT / RW;
   const int d = tid % RW, pl = tid / RW;
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
-    if (small_pair(A.seg[p])) return;  // prepared by a one-CTA-per-pair kernel
     const float *pts = side == 0 ? A.x : A.y;
     const float *w = side == 0 ? A.w_x : A.w_y;
     const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
@@ -414,7 +393,6 @@ __global__ void __launch_bounds__(256) statsw_kernel(PrepArgs A) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int D = A.D;
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
-    if (small_pair(A.seg[p])) return;  // prepared by a one-CTA-per-pair kernel
     const float *pts = side == 0 ? A.x : A.y;
     const float *w = side == 0 ? A.w_x : A.w_y;
     const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
@@ -520,7 +498,7 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
   const int lane = threadIdx.x & 31;
   if (p >= A.P) return;
   const int D = A.D, DP = A.DP;
-  if (small_pair(A.seg[p])) return;  // prepared by prep3_kernel / prepw_small_kernel
+  if (DP == 3 && small_pair(A.seg[p])) return;  // prepared by prep3_kernel
   if (A.sigma_p != nullptr && lane == 0 && !(A.sigma_p[p] > 0.0)) atomicOr(A.err, (int)kErrSigma);
   const int rs = stats_stride(DP);
   double *meta = A.meta + p * meta_stride(DP);
@@ -612,7 +590,6 @@ __global__ void __launch_bounds__(NT) packg_kernel(PrepArgs A) {
   const int lanes = NT / RW;
   const int d = threadIdx.x % RW, pl = threadIdx.x / RW;
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t, int64_t) {
-    if (small_pair(A.seg[p])) return;  // prepared by a one-CTA-per-pair kernel
     const Seg sg = A.seg[p];
     const int64_t s = side == 0 ? sg.xs : sg.ys;
     const int64_t count = side == 0 ? sg.xcount : sg.ycount;
@@ -650,7 +627,6 @@ __global__ void __launch_bounds__(256, 4) packgw_kernel(PrepArgs A) {
   const ChunkMap M{A.P, A.choff, A.chx};
   const int D = A.D, c = threadIdx.x % NC;
   for_each_chunk(M, [&](int64_t p, int side, int64_t ch, int64_t, int64_t, int64_t) {
-    if (small_pair(A.seg[p])) return;  // prepared by a one-CTA-per-pair kernel
     const Seg sg = A.seg[p];
     const int64_t s = side == 0 ? sg.xs : sg.ys;
     const int64_t count = side == 0 ? sg.xcount : sg.ycount;
@@ -697,165 +673,6 @@ __global__ void __launch_bounds__(256, 4) packgw_kernel(PrepArgs A) {
     for (int64_t i = b + threadIdx.x; i < e; i += 256)
       Ap[s + i] = (float)((double)eff_weight(w, mask, wmode, s + i) / Wn);
   });
-}
-
-// Generic layout (D >= 4), pairs with at most kSmallPts points per side
-// (small_pair): one CTA per pair does what the chunked stats, meta and pack
-// passes do for the large pairs, reading the points from DRAM once (the
-// packing re-reads them from cache).  Thread t handles coordinates
-// t % RW + RW k of point lane t / RW (RW = min(DP, 32)); the sums are
-// compensated float32 per thread (no per-point float-to-double conversions),
-// then combined over the point lanes in order in float64.
-template <int DP>
-__global__ void __launch_bounds__(256) prepw_small_kernel(PrepArgs A) {
-  constexpr int NT = 256, RW = DP < 32 ? DP : 32, KL = DP / RW, PL = NT / RW;
-  __shared__ double shc[PL][DP], shp[PL][DP];
-  __shared__ double shs[PL][3];  // W, valid count, last valid index
-  __shared__ double tot[2][3];
-  const int tid = threadIdx.x, d0 = tid % RW, pl = tid / RW;
-  const int D = A.D;
-  for (int64_t p = blockIdx.x; p < A.P; p += gridDim.x) {
-    Seg sg = A.seg[p];
-    if (!small_pair(sg)) continue;
-    double *meta = A.meta + p * meta_stride(DP);
-    for (int side = 0; side < 2; ++side) {
-      const float *pts = side == 0 ? A.x : A.y;
-      const float *w = side == 0 ? A.w_x : A.w_y;
-      const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
-      const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-      const int64_t s = side == 0 ? sg.xs : sg.ys, span = side == 0 ? sg.xspan : sg.yspan;
-      FSum cs[KL], ps[KL], W;
-      int nv = 0;
-      long long last = -1;
-      for (int64_t i = pl; i < span; i += PL) {
-        const int64_t g = s + i;
-        const float wi = eff_weight(w, mask, wmode, g);
-        const bool valid = mask == nullptr || mask[g] != 0;
-#pragma unroll
-        for (int k = 0; k < KL; ++k) {
-          const int d = d0 + RW * k;
-          if (d < D) {
-            const float pv = pts[g * D + d];
-            cs[k].add_prod(wi, pv);
-            if (valid) ps[k].add(pv);
-          }
-        }
-        if (d0 == 0) {
-          W.add(wi);
-          if (valid) {
-            ++nv;
-            last = i;
-          }
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < KL; ++k) {
-        shc[pl][d0 + RW * k] = cs[k].value();
-        shp[pl][d0 + RW * k] = ps[k].value();
-      }
-      if (d0 == 0) {
-        shs[pl][0] = W.value();
-        shs[pl][1] = (double)nv;
-        shs[pl][2] = (double)last;
-      }
-      __syncthreads();
-      if (tid == 0) {
-        double Wt = 0.0, nvt = 0.0, lst = -1.0;
-        for (int q = 0; q < PL; ++q) {
-          Wt += shs[q][0];
-          nvt += shs[q][1];
-          lst = fmax(lst, shs[q][2]);
-        }
-        tot[side][0] = Wt;
-        tot[side][1] = nvt;
-        tot[side][2] = lst;
-      }
-      __syncthreads();
-      // ---- metadata (meta_kernel's semantics for the generic layout) -----
-      const double Wt = tot[side][0], nvt = tot[side][1];
-      const int64_t count = A.layout == 0 ? span : (int64_t)tot[side][2] + 1;
-      double Wn, m, fold;
-      bool werr;
-      side_normaliser(wmode, Wt, nvt, count, false, -INFINITY, -INFINITY, Wn, m, fold, werr);
-      if (tid == 0) {
-        if (side == 0 && A.sigma_p != nullptr && !(A.sigma_p[p] > 0.0))
-          atomicOr(A.err, (int)kErrSigma);
-        if (werr) atomicOr(A.err, (int)kErrWeightSum);
-        meta[side] = Wn;
-        meta[2 + side] = Wt;
-        meta[meta_wscale(DP) + side] = m;
-        meta[meta_fold(DP) + side] = fold;
-        if (side == 0) A.seg[p].xcount = count;
-        else A.seg[p].ycount = count;
-      }
-      for (int dd = tid; dd < DP; dd += NT) {
-        double c = 0.0, q = 0.0;
-        for (int l = 0; l < PL; ++l) {
-          c += shc[l][dd];
-          q += shp[l][dd];
-        }
-        const double mu = dd < D ? c / Wn : 0.0;
-        const double mean = (dd < D && nvt > 0) ? q / nvt : 0.0;
-        meta[4 + side * DP + dd] = mu;
-        if (side == 0) {
-          meta[4 + 2 * DP + dd] = mean;  // provisional: replaced by the anchor below
-        } else {
-          double ax, ay;
-          if (A.center) {
-            ax = meta[4 + dd];
-            ay = mu;
-          } else {
-            const int64_t count_x = A.layout == 0 ? sg.xspan : (int64_t)tot[0][2] + 1;
-            ax = count_x > 0 ? meta[4 + 2 * DP + dd] : mean;
-            ay = ax;
-          }
-          meta[4 + 2 * DP + dd] = ax;
-          meta[4 + 3 * DP + dd] = ay;
-        }
-      }
-      __syncthreads();  // shc, shp, shs, tot reused; meta visible to the packing
-    }
-    // ---- packing of both sides: scale * (p - anchor), zero padded; weights
-    sg = A.seg[p];
-    for (int side = 0; side < 2; ++side) {
-      const float *pts = side == 0 ? A.x : A.y;
-      const float *w = side == 0 ? A.w_x : A.w_y;
-      const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
-      const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-      float *Gp = side == 0 ? A.Gx : A.Gy;
-      float *Ap = side == 0 ? A.Ax : A.Ay;
-      const int64_t s = side == 0 ? sg.xs : sg.ys, count = side == 0 ? sg.xcount : sg.ycount;
-      const double Wn = meta[side];
-      const double *anc = meta + 4 + (2 + side) * DP;
-      const float sc = pair_scale(A.scale, A.sigma_p, p);
-      if (D % 4 == 0) {
-        // float4 elements (point, coordinates 4c..4c+3); DP / 4 divides the
-        // 256 threads, so a thread keeps one c and its four anchors
-        constexpr int NC = DP / 4;
-        const int c = tid % NC;
-        const bool live = 4 * c < D;
-        const float a0 = live ? (float)anc[4 * c] : 0.f, a1 = live ? (float)anc[4 * c + 1] : 0.f;
-        const float a2 = live ? (float)anc[4 * c + 2] : 0.f, a3 = live ? (float)anc[4 * c + 3] : 0.f;
-        for (int64_t i = tid / NC; i < count; i += NT / NC) {
-          float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (live) {
-            const float4 x = *reinterpret_cast<const float4 *>(pts + (s + i) * D + 4 * c);
-            o = make_float4(sc * (x.x - a0), sc * (x.y - a1), sc * (x.z - a2), sc * (x.w - a3));
-          }
-          reinterpret_cast<float4 *>(Gp)[(s + i) * NC + c] = o;
-        }
-      } else {
-        // scalar elements; DP divides the 256 threads: a thread keeps one d
-        const int d = tid % DP;
-        const float ad = d < D ? (float)anc[d] : 0.f;
-        for (int64_t i = tid / DP; i < count; i += NT / DP)
-          Gp[(s + i) * DP + d] = d < D ? sc * (pts[(s + i) * D + d] - ad) : 0.f;
-      }
-      for (int64_t i = tid; i < count; i += NT)
-        Ap[s + i] = (float)((double)eff_weight(w, mask, wmode, s + i) / Wn);
-    }
-    __syncthreads();  // meta of this pair read before the next pair's writes
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -970,6 +787,25 @@ __global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
   });
 }
 
+// Error-free accumulation in float32 (Knuth's TwoSum, the running error kept
+// in a second float): a double-float sum of a few thousand floats, free of
+// float-to-double conversions per point, which run on the SM's narrow
+// conversion pipe.
+struct FSum {
+  float hi = 0.f, lo = 0.f;
+  __device__ __forceinline__ void add(float v) {
+    const float s = hi + v, bp = s - hi;
+    lo += (hi - (s - bp)) + (v - bp);
+    hi = s;
+  }
+  // adds the exact product a * b (TwoProduct by FMA)
+  __device__ __forceinline__ void add_prod(float a, float b) {
+    const float q = a * b;
+    add(q);
+    lo += fmaf(a, b, -q);
+  }
+  __device__ __forceinline__ double value() const { return (double)hi + (double)lo; }
+};
 
 // D <= 3, pairs with at most kSmallPts points per side (small_pair): one CTA
 // per pair does what stats3_kernel, meta_kernel and pack3_kernel do for the
