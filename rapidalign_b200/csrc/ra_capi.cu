@@ -22,6 +22,7 @@
 #include "ra_plan.cuh"
 #include "ra_prep.cuh"
 #include "ra_tc.cuh"
+#include "ra_tc16.cuh"
 #include "ra_tcws.cuh"
 #include "ra_tiles3.cuh"
 #include "ra_tilesg.cuh"
@@ -46,6 +47,7 @@ int generic_dp(int D) {
 
 struct Layout {
   bool packed3;
+  bool tc16;        // generic layout on the tensor cores: fp16 tiles (ra_tc16.cuh)
   int DP;
   int nq;           // packed3: 16-byte arrays per tile
   int acc_stride;
@@ -55,6 +57,7 @@ struct Layout {
   size_t hdr, seg, meta, cnt, item_off, tbase_x, tbase_y, boff, items, itemK, itemS, Kws, Sws,
       coef, Ktmp, chcnt, chx, choff, rec;
   size_t tiles_x, tiles_y, Gx, Gy, Ax, Ay, accX, accY;
+  size_t hx, hy, lx, ly, cx, cy;  // tc16: fp16 hi / lo tiles and slot values
   size_t acc_x_bytes, acc_y_bytes;
   size_t total;
 };
@@ -90,12 +93,18 @@ bool desc_ok(const ra_kde_desc *d) {
   return true;
 }
 
+bool use_tensor_cores(const ra_kde_desc *d, int DP) {
+  if (d->dim <= 3 || d->engine == RA_ENGINE_SIMT) return false;
+  return DP == 32 || DP == 64 || DP == 128;
+}
+
 Layout make_layout(const ra_kde_desc *d) {
   Layout L;
   std::memset(&L, 0, sizeof(L));
   const int64_t P = d->num_pairs, NX = d->num_x, NY = d->num_y;
   L.packed3 = d->dim <= 3;
   L.DP = L.packed3 ? 3 : generic_dp(d->dim);
+  L.tc16 = !L.packed3 && use_tensor_cores(d, L.DP);
   L.acc_stride = L.packed3 ? kAcc3Stride : gen_acc_stride(L.DP);
   // host bound on the number of items
   int64_t tx, ty;  // sum over pairs of row tiles
@@ -116,6 +125,15 @@ Layout make_layout(const ra_kde_desc *d) {
   if (L.max_chunks < 1) L.max_chunks = 1;
   L.max_tiles_x = L.packed3 ? (tx > 0 ? tx : 1) : 0;
   L.max_tiles_y = L.packed3 ? (ty > 0 ? ty : 1) : 0;
+  if (L.tc16) {
+    // 64-point tiles of the fp16 layout: room for every pair's span
+    const int64_t t64x = d->layout == RA_LAYOUT_DENSE ? P * ceil_div(d->nmax_x, (int64_t)kTile)
+                                                      : ceil_div(NX, (int64_t)kTile) + P;
+    const int64_t t64y = d->layout == RA_LAYOUT_DENSE ? P * ceil_div(d->nmax_y, (int64_t)kTile)
+                                                      : ceil_div(NY, (int64_t)kTile) + P;
+    L.max_tiles_x = t64x > 0 ? t64x : 1;
+    L.max_tiles_y = t64y > 0 ? t64y : 1;
+  }
   const bool grad = d->need_grad != 0;
   L.nq = kT3Arrays;
   size_t o = 0;
@@ -159,6 +177,15 @@ Layout make_layout(const ra_kde_desc *d) {
     L.Gy = take(sizeof(float) * ny * L.DP);
     L.Ax = take(sizeof(float) * nx);
     L.Ay = take(sizeof(float) * ny);
+    if (L.tc16) {
+      const size_t tbytes = (size_t)t16_tile_bytes(L.DP);
+      L.hx = take(tbytes * (size_t)L.max_tiles_x);
+      L.lx = take(tbytes * (size_t)L.max_tiles_x);
+      L.hy = take(tbytes * (size_t)L.max_tiles_y);
+      L.ly = take(tbytes * (size_t)L.max_tiles_y);
+      L.cx = take(sizeof(float) * kT16SlotFloats * (size_t)L.max_tiles_x);
+      L.cy = take(sizeof(float) * kT16SlotFloats * (size_t)L.max_tiles_y);
+    }
     L.acc_x_bytes = sizeof(float) * nx * L.acc_stride;
     L.acc_y_bytes = sizeof(float) * ny * L.acc_stride;
   }
@@ -188,6 +215,11 @@ int check_common(const ra_kde_desc *d, void *ws, size_t ws_bytes, size_t need) {
 
 // Grid of the per-chunk passes: enough CTAs to fill the GPU, never more than
 // there can be chunks.
+// 16-byte vector loads and stores of caller memory need 16-byte aligned
+// pointers (a contiguous tensor can start at any float); null counts as
+// aligned.
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 unsigned chunk_grid(const Layout &L) {
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
@@ -295,6 +327,41 @@ int launch_tilestc_d(int mode, int64_t max_items, const TilesGArgs &T, cudaStrea
   return launch_tilestc_dm<DP, 2>(max_items, T, st);  // mode 2: sigma gradient
 }
 
+template <int DP, int MODE>
+int launch_tc16_dm(int64_t max_items, const Tc16Args &T, cudaStream_t st) {
+  const size_t smem = t16_smem_request(DP);
+  static_assert(t16_smem_bytes(DP) <= t16_smem_request(DP), "shared memory request too small");
+  if (cudaFuncSetAttribute(tilestc16_kernel<DP, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return RA_ERR_CUDA;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t grid = sms > 0 ? sms : 1;  // one persistent CTA per SM
+  if (grid > max_items) grid = max_items;
+  tilestc16_kernel<DP, MODE><<<(unsigned)grid, kT16Threads, smem, st>>>(T);
+  return cuda_status(cudaGetLastError());
+}
+
+template <int DP>
+int launch_tc16_d(int mode, int64_t max_items, const Tc16Args &T, cudaStream_t st) {
+  if (mode == 0) return launch_tc16_dm<DP, 0>(max_items, T, st);
+  if (mode == 1) return launch_tc16_dm<DP, 1>(max_items, T, st);
+  return launch_tc16_dm<DP, 2>(max_items, T, st);  // mode 2: sigma gradient
+}
+
+int launch_tc16(int DP, int mode, int64_t max_items, const Tc16Args &T, cudaStream_t st) {
+  int rc;
+  switch (DP) {
+    case 32: rc = launch_tc16_d<32>(mode, max_items, T, st); break;
+    case 64: rc = launch_tc16_d<64>(mode, max_items, T, st); break;
+    case 128: rc = launch_tc16_d<128>(mode, max_items, T, st); break;
+    default: return RA_ERR_INVALID_ARGUMENT;
+  }
+  ++g_launches;
+  return rc;
+}
+
 int launch_tilestc(int DP, int mode, int64_t max_items, const TilesGArgs &T, cudaStream_t st) {
   int rc;
   switch (DP) {
@@ -305,11 +372,6 @@ int launch_tilestc(int DP, int mode, int64_t max_items, const TilesGArgs &T, cud
   }
   ++g_launches;
   return rc;
-}
-
-bool use_tensor_cores(const ra_kde_desc *d, int DP) {
-  if (d->dim <= 3 || d->engine == RA_ENGINE_SIMT) return false;
-  return DP == 32 || DP == 64 || DP == 128;
 }
 
 int launch_tilesg(int DP, int mode, int64_t grid, const TilesGArgs &T, cudaStream_t st) {
@@ -415,6 +477,18 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
     pa.Ax = at<float>(ws, L.Ax);
     pa.Ay = at<float>(ws, L.Ay);
   }
+  if (L.tc16) {
+    pa.tc16 = 1;
+    pa.tcnt = at<int64_t>(ws, L.cnt) + P;  // free until the plan counts items
+    pa.tbase_x = at<int64_t>(ws, L.tbase_x);
+    pa.tbase_y = at<int64_t>(ws, L.tbase_y);
+    pa.hx = at<uint8_t>(ws, L.hx);
+    pa.hy = at<uint8_t>(ws, L.hy);
+    pa.lx = at<uint8_t>(ws, L.lx);
+    pa.ly = at<uint8_t>(ws, L.ly);
+    pa.cx = at<float>(ws, L.cx);
+    pa.cy = at<float>(ws, L.cy);
+  }
   PackArgs pk;
   std::memset(&pk, 0, sizeof(pk));
   if (L.packed3) {
@@ -464,7 +538,18 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
       g_launches += 2;
     }
   } else {
-    if (L.DP == 32)
+    // float4 loads of the caller's points need D % 4 == 0 and 16-byte
+    // aligned bases; anything else takes the scalar passes
+    const bool v4 = d->dim % 4 == 0 && aligned16(in->x) && aligned16(in->y);
+    if (v4 && L.DP == 32)
+      statsw4_kernel<32><<<cgrid, 256, 0, st>>>(pa);
+    else if (v4 && L.DP == 64)
+      statsw4_kernel<64><<<cgrid, 256, 0, st>>>(pa);
+    else if (v4 && L.DP == 128)
+      statsw4_kernel<128><<<cgrid, 256, 0, st>>>(pa);
+    else if (v4 && L.DP == 256)
+      statsw4_kernel<256><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.DP == 32)
       statsw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
     else if (L.DP == 64)
       statsw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
@@ -475,13 +560,19 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
     else
       stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
     meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
-    if (d->dim % 4 == 0 && L.DP == 32)
+    if (L.tc16 && L.DP == 32)
+      packtc_kernel<32><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.tc16 && L.DP == 64)
+      packtc_kernel<64><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.tc16 && L.DP == 128)
+      packtc_kernel<128><<<cgrid, 256, 0, st>>>(pa);
+    else if (v4 && L.DP == 32)
       packgw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
-    else if (d->dim % 4 == 0 && L.DP == 64)
+    else if (v4 && L.DP == 64)
       packgw_kernel<64><<<cgrid, 256, 0, st>>>(pa);
-    else if (d->dim % 4 == 0 && L.DP == 128)
+    else if (v4 && L.DP == 128)
       packgw_kernel<128><<<cgrid, 256, 0, st>>>(pa);
-    else if (d->dim % 4 == 0 && L.DP == 256)
+    else if (v4 && L.DP == 256)
       packgw_kernel<256><<<cgrid, 256, 0, st>>>(pa);
     else
       packg_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
@@ -583,8 +674,37 @@ int compute_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     // the generic kernels keep every per-point sum anyway: mode 3 (no column
     // weight sums, a D <= 3 distinction) is their mode 1
     const int gmode = mode == 3 ? 1 : mode;
-    rc = use_tensor_cores(d, L.DP) ? launch_tilestc(L.DP, gmode, L.max_items, T, st)
-                                   : launch_tilesg(L.DP, gmode, L.max_items, T, st);
+    if (L.tc16) {
+      Tc16Args C;
+      std::memset(&C, 0, sizeof(C));
+      C.items = T.items;
+      C.n_items = T.n_items;
+      C.seg = T.seg;
+      C.meta = at<double>(ws, L.meta);
+      C.tbase_x = at<int64_t>(ws, L.tbase_x);
+      C.tbase_y = at<int64_t>(ws, L.tbase_y);
+      C.hx = at<uint8_t>(ws, L.hx);
+      C.hy = at<uint8_t>(ws, L.hy);
+      C.lx = at<uint8_t>(ws, L.lx);
+      C.ly = at<uint8_t>(ws, L.ly);
+      C.cx = at<float>(ws, L.cx);
+      C.cy = at<float>(ws, L.cy);
+      C.Ax = T.Ax;
+      C.Ay = T.Ay;
+      C.accX = T.accX;
+      C.accY = T.accY;
+      C.itemK = T.itemK;
+      C.itemS = T.itemS;
+      C.need_rows = T.need_rows;
+      C.shard_index = T.shard_index;
+      C.shard_count = T.shard_count;
+      C.err = T.err;
+      C.spin_limit = T.spin_limit;
+      C.no_mma = T.no_mma;
+      rc = launch_tc16(L.DP, gmode, L.max_items, C, st);
+    } else {
+      rc = launch_tilesg(L.DP, gmode, L.max_items, T, st);
+    }
     if (rc) return rc;
   }
 
@@ -696,6 +816,9 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.grad_wx = gr->grad_wx;
   ea.grad_wy = gr->grad_wy;
   ea.grad_sigma = gr->grad_sigma;
+  ea.totals = d->center || (gr->grad_wx != nullptr && d->weights_x != RA_WEIGHTS_UNIFORM) ||
+              (gr->grad_wy != nullptr && d->weights_y != RA_WEIGHTS_UNIFORM);
+  ea.vec4 = d->dim % 4 == 0 && aligned16(gr->grad_x) && aligned16(gr->grad_y);
   const unsigned cgrid = chunk_grid(L);
   if (L.packed3) {
     // small pairs: one CTA per pair (both passes); large pairs: chunked passes
@@ -708,29 +831,32 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
       g_launches += 2;
     }
   } else if (L.DP >= 32) {
+    // the partial pass only makes the side totals R (centering) and Q (weight
+    // gradients); an uncentred call without weight gradients skips it
     switch (L.DP) {
       case 32:
-        epigw_partial_kernel<32><<<cgrid, 256, 0, st>>>(ea);
+        if (ea.totals) epigw_partial_kernel<32><<<cgrid, 256, 0, st>>>(ea);
         epigw_write_kernel<32><<<cgrid, 256, 0, st>>>(ea);
         break;
       case 64:
-        epigw_partial_kernel<64><<<cgrid, 256, 0, st>>>(ea);
+        if (ea.totals) epigw_partial_kernel<64><<<cgrid, 256, 0, st>>>(ea);
         epigw_write_kernel<64><<<cgrid, 256, 0, st>>>(ea);
         break;
       case 128:
-        epigw_partial_kernel<128><<<cgrid, 256, 0, st>>>(ea);
+        if (ea.totals) epigw_partial_kernel<128><<<cgrid, 256, 0, st>>>(ea);
         epigw_write_kernel<128><<<cgrid, 256, 0, st>>>(ea);
         break;
       default:
-        epigw_partial_kernel<256><<<cgrid, 256, 0, st>>>(ea);
+        if (ea.totals) epigw_partial_kernel<256><<<cgrid, 256, 0, st>>>(ea);
         epigw_write_kernel<256><<<cgrid, 256, 0, st>>>(ea);
         break;
     }
+    g_launches += ea.totals ? 2 : 1;
   } else {
     epig_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
     epig_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+    g_launches += 2;
   }
-  if (!L.packed3) g_launches += 2;
   if (ea.grad_sigma != nullptr) {
     sigma_grad_kernel<<<(unsigned)ceil_div(P, 256), 256, 0, st>>>(ea);
     ++g_launches;

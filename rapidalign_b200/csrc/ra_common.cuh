@@ -141,6 +141,11 @@ __device__ __forceinline__ double warp_fmax(double v) {
   for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(kFull, v, o));
   return v;
 }
+__device__ __forceinline__ float warp_fmaxf(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
 
 // ---------------------------------------------------------------------------
 // Internal data structures (live in the caller's workspace).

@@ -147,6 +147,8 @@ struct EpilogueArgs {
   float *grad_x, *grad_y;
   double *grad_wx, *grad_wy;
   double *grad_sigma;
+  int totals;  // the side totals R, Q are used (centering, or a weight gradient)
+  int vec4;    // D % 4 == 0 and grad_x, grad_y 16-byte aligned: float4 stores
 };
 
 // One point's record (self (s, G0..G2), cross (s, G0..G2), 32-byte aligned)
@@ -604,10 +606,12 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
   const int D = A.D, rs = stats_stride(DP);
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t first, int64_t n) {
     const EpiSide E = epi_side(A, p, side);
-    // the side's totals, summed over its chunks in order
+    // the side's totals, summed over its chunks in order (zero when no
+    // output uses them: the partial pass did not run)
     for (int t = tid; t < DP + 1; t += 256) {
       double tot = 0.0;
-      for (int64_t kk = 0; kk < n; ++kk) tot += A.rec[(first + kk) * rs + (t < DP ? 1 + t : 0)];
+      if (A.totals)
+        for (int64_t kk = 0; kk < n; ++kk) tot += A.rec[(first + kk) * rs + (t < DP ? 1 + t : 0)];
       Rsh[t] = tot;  // Rsh[DP] = Q
     }
     __syncthreads();
@@ -671,7 +675,7 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
     // position gradients over flat elements: float4 (point, 4 coordinates)
     // when D is a multiple of 4 -- a thread then keeps one coordinate chunk
     // and loads each point's scalars once per 4 coordinates -- else scalars
-    if (gout != nullptr && D % 4 == 0) {
+    if (gout != nullptr && A.vec4) {
       constexpr int NC = DP / 4;
       const int ncd = D / 4;  // chunks that hold coordinates
       const int cc = tid % NC;

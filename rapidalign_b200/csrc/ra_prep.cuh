@@ -15,6 +15,8 @@
 // the partials in chunk order) -> pack kernels (per chunk).
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "ra_chunks.cuh"
 #include "ra_common.cuh"
 
@@ -35,16 +37,28 @@ namespace ra {
 //   [6+4DP + side]   D <= 3 layout: 1 when the side's weights are folded
 //                    (all >= 0, some > 0, no sigma gradient), 2 when they are
 //                    moreover all equal (a~ = 1 on every point), else 0
-__host__ __device__ __forceinline__ int meta_stride(int DP) { return 8 + 4 * DP; }
+//   [8+4DP + side]   tensor-core layout (fp16 tiles): 2^e, the power of two
+//                    the side's packed coordinates are multiplied by before
+//                    the fp16 split (their magnitude bound times 2^e <= 2^15)
+//   [10+4DP + side]  tensor-core layout: 2^-f, the power of two the side's
+//                    normalised weights are multiplied by (largest |a| 2^-f
+//                    in (1/2, 1])
+//   [12+4DP + side]  tensor-core layout: 1 when the side's weights are all
+//                    >= 0 (folded into the exponent as columns), else 0
+__host__ __device__ __forceinline__ int meta_stride(int DP) { return 14 + 4 * DP; }
 __host__ __device__ __forceinline__ int meta_wscale(int DP) { return 4 + 4 * DP; }
 __host__ __device__ __forceinline__ int meta_fold(int DP) { return 6 + 4 * DP; }
+__host__ __device__ __forceinline__ int meta_tc_cscale(int DP) { return 8 + 4 * DP; }
+__host__ __device__ __forceinline__ int meta_tc_wscale(int DP) { return 10 + 4 * DP; }
+__host__ __device__ __forceinline__ int meta_tc_fold(int DP) { return 12 + 4 * DP; }
 
 // Partial-sum record of one chunk (fp64): [0] sum of effective weights,
 // [1] valid points, [2] last valid index (-1: none), [3, 3+DP) sum w' p,
 // [3+DP, 3+2DP) sum p over the valid points, [3+2DP] largest and [4+2DP]
-// smallest effective weight (D <= 3 layout only).  The backward epilogue
-// reuses the same slots for its (Q, R[DP]) partials.
-__host__ __device__ __forceinline__ int stats_stride(int DP) { return 5 + 2 * DP; }
+// smallest effective weight (D <= 3 layout, and the wide generic passes),
+// [5+2DP] largest |coordinate| of a valid point (wide generic passes).  The
+// backward epilogue reuses the same slots for its (Q, R[DP]) partials.
+__host__ __device__ __forceinline__ int stats_stride(int DP) { return 6 + 2 * DP; }
 
 // Reduction width: power of two >= D (at least 4); thread (pl, d) of a CTA
 // handles dimension d of point lane pl.
@@ -85,6 +99,11 @@ struct PrepArgs {
   int allow_fold;  // D <= 3: weights may be folded into the exponent (no sigma gradient)
   // generic layout (D >= 4): coords [num * DP] (zero padded) and weights [num]
   float *Gx, *Gy, *Ax, *Ay;
+  // tensor-core layout (ra_tc16.cuh): fp16 hi / lo tiles of 64 points and
+  // kT16SlotFloats slot values per tile, from tile tbase_x / tbase_y of a pair
+  int tc16;
+  uint8_t *hx, *hy, *lx, *ly;
+  float *cx, *cy;
 };
 
 // The coordinate pre-scale of pair p.
@@ -148,10 +167,10 @@ __global__ void __launch_bounds__(1024) segment_kernel(PrepArgs A) {
         A.chcnt[p] = A.chx[p] + ceil_div(span, (int64_t)kChunk);
         // D <= 3: the chunk map covers only the pairs the chunked passes
         // prepare (small pairs have their own one-CTA kernels)
-        if (A.tcnt != nullptr && small_pair(sg)) A.chx[p] = A.chcnt[p] = 0;
+        if (A.DP == 3 && A.tcnt != nullptr && small_pair(sg)) A.chx[p] = A.chcnt[p] = 0;
       }
-      // D <= 3 tile layout: room for the whole span (a dense row's count,
-      // 1 + its last valid index, is known only after the sums)
+      // tile layouts (D <= 3, tensor-core): room for the whole span (a dense
+      // row's count, 1 + its last valid index, is known only after the sums)
       if (A.tcnt != nullptr) A.tcnt[side * A.P + p] = ceil_div(span, (int64_t)kTile);
     }
     __syncthreads();
@@ -389,6 +408,7 @@ __global__ void __launch_bounds__(256) statsw_kernel(PrepArgs A) {
   constexpr int NW = 8, KL = DP / 32;
   __shared__ double sh[NW][2 * DP + 2];
   __shared__ long long shl[NW];
+  __shared__ float shm[NW][3];
   const ChunkMap M{A.P, A.choff, A.chx};
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int D = A.D;
@@ -403,6 +423,7 @@ __global__ void __launch_bounds__(256) statsw_kernel(PrepArgs A) {
     const int64_t b = c * kChunk, e = b + kChunk < span ? b + kChunk : span;
     double acc[KL], accu[KL], W = 0.0, nv = 0.0;
     long long last = -1;
+    float wmax = -INFINITY, wmin = INFINITY, cmax = 0.f;
 #pragma unroll
     for (int k = 0; k < KL; ++k) acc[k] = accu[k] = 0.0;
     for (int64_t i = b + wid; i < e; i += NW) {
@@ -413,17 +434,26 @@ __global__ void __launch_bounds__(256) statsw_kernel(PrepArgs A) {
       for (int k = 0; k < KL; ++k) {
         const int d = lane + 32 * k;
         if (d < D) {
-          const double pv = (double)pts[g * D + d];
+          const float pf = pts[g * D + d];
+          const double pv = (double)pf;
           acc[k] += (double)wi * pv;
-          if (valid) accu[k] += pv;
+          if (valid) {
+            accu[k] += pv;
+            cmax = fmaxf(cmax, fabsf(pf));
+          }
         }
       }
       W += (double)wi;
+      wmax = fmaxf(wmax, wi);
+      wmin = fminf(wmin, wi);
       if (valid) {
         nv += 1.0;
         last = i;
       }
     }
+    wmax = warp_fmaxf(wmax);
+    wmin = -warp_fmaxf(-wmin);
+    cmax = warp_fmaxf(cmax);
 #pragma unroll
     for (int k = 0; k < KL; ++k) {
       sh[wid][lane + 32 * k] = acc[k];
@@ -433,6 +463,9 @@ __global__ void __launch_bounds__(256) statsw_kernel(PrepArgs A) {
       sh[wid][2 * DP] = W;
       sh[wid][2 * DP + 1] = nv;
       shl[wid] = last;
+      shm[wid][0] = wmax;
+      shm[wid][1] = wmin;
+      shm[wid][2] = cmax;
     }
     __syncthreads();
     double *rec = A.rec + v * stats_stride(DP);
@@ -444,8 +477,161 @@ __global__ void __launch_bounds__(256) statsw_kernel(PrepArgs A) {
     }
     if (tid == 0) {
       long long lst = -1;
-      for (int q = 0; q < NW; ++q) lst = shl[q] > lst ? shl[q] : lst;
+      float m0 = -INFINITY, m1 = INFINITY, m2 = 0.f;
+      for (int q = 0; q < NW; ++q) {
+        lst = shl[q] > lst ? shl[q] : lst;
+        m0 = fmaxf(m0, shm[q][0]);
+        m1 = fminf(m1, shm[q][1]);
+        m2 = fmaxf(m2, shm[q][2]);
+      }
       rec[2] = (double)lst;
+      rec[3 + 2 * DP] = m0;
+      rec[4 + 2 * DP] = m1;
+      rec[5 + 2 * DP] = m2;
+    }
+    __syncthreads();
+  });
+}
+
+// Pass 1 for wide points whose coordinates load as float4 (D % 4 == 0,
+// 16-byte aligned bases): LPP lanes share a point (one float4 chunk or two
+// each), a warp covers PPW points per step and keeps kU steps of loads in
+// flight, so a CTA has ~16 KB of reads outstanding.  Partials are combined
+// over the PPW point slots of a warp by shuffles, then over the 8 warps in
+// order: a fixed summation order, independent of scheduling.
+template <int DP>
+__global__ void __launch_bounds__(256) statsw4_kernel(PrepArgs A) {
+  constexpr int NW = 8, NC = DP / 4;
+  constexpr int LPP = NC < 32 ? NC : 32;  // lanes per point
+  constexpr int CPL = NC / LPP;           // float4 chunks per lane
+  constexpr int PPW = 32 / LPP;           // points per warp step
+  constexpr int kU = 4;                   // warp steps in flight
+  static_assert(NC % LPP == 0 && 32 % LPP == 0, "chunk split");
+  __shared__ double sh[NW][2 * DP + 2];
+  __shared__ long long shl[NW];
+  __shared__ float shm[NW][3];
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int cl = lane % LPP, q = lane / LPP;
+  const int D = A.D;
+  for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
+    const float *pts = side == 0 ? A.x : A.y;
+    const float *w = side == 0 ? A.w_x : A.w_y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    const Seg sg = A.seg[p];
+    const int64_t s = side == 0 ? sg.xs : sg.ys;
+    const int64_t span = side == 0 ? sg.xspan : sg.yspan;
+    const int64_t b = c * kChunk, e = b + kChunk < span ? b + kChunk : span;
+    double acc[CPL][4], accu[CPL][4], W = 0.0, nv = 0.0;
+    long long last = -1;
+    float wmax = -INFINITY, wmin = INFINITY, cmax = 0.f;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[k][j] = accu[k][j] = 0.0;
+    constexpr int kStep = NW * PPW;  // points of one CTA step
+    for (int64_t i0 = b + wid * PPW + q; i0 < e; i0 += (int64_t)kU * kStep) {
+      float4 xv[kU][CPL];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t i = i0 + (int64_t)u * kStep;
+#pragma unroll
+        for (int k = 0; k < CPL; ++k) {
+          const int cc = cl + LPP * k;
+          xv[u][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (i < e && 4 * cc < D)
+            xv[u][k] = *reinterpret_cast<const float4 *>(pts + (s + i) * D + 4 * cc);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t i = i0 + (int64_t)u * kStep;
+        if (i < e) {
+          const int64_t g = s + i;
+          const double wi = (double)eff_weight(w, mask, wmode, g);
+          const bool valid = mask == nullptr || mask[g] != 0;
+#pragma unroll
+          for (int k = 0; k < CPL; ++k) {
+            const float xs[4] = {xv[u][k].x, xv[u][k].y, xv[u][k].z, xv[u][k].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const double pv = (double)xs[j];
+              acc[k][j] += wi * pv;
+              if (valid) {
+                accu[k][j] += pv;
+                cmax = fmaxf(cmax, fabsf(xs[j]));
+              }
+            }
+          }
+          wmax = fmaxf(wmax, (float)wi);
+          wmin = fminf(wmin, (float)wi);
+          if (cl == 0) {
+            W += wi;
+            if (valid) {
+              nv += 1.0;
+              last = i;
+            }
+          }
+        }
+      }
+    }
+    // combine the PPW point slots of the warp (lanes cl, cl + LPP, ...)
+#pragma unroll
+    for (int o = LPP; o < 32; o <<= 1) {
+#pragma unroll
+      for (int k = 0; k < CPL; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[k][j] += __shfl_xor_sync(kFull, acc[k][j], o);
+          accu[k][j] += __shfl_xor_sync(kFull, accu[k][j], o);
+        }
+      W += __shfl_xor_sync(kFull, W, o);
+      nv += __shfl_xor_sync(kFull, nv, o);
+      const long long lo = __shfl_xor_sync(kFull, last, o);
+      last = lo > last ? lo : last;
+    }
+    if (q == 0) {
+#pragma unroll
+      for (int k = 0; k < CPL; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sh[wid][4 * (cl + LPP * k) + j] = acc[k][j];
+          sh[wid][DP + 4 * (cl + LPP * k) + j] = accu[k][j];
+        }
+    }
+    wmax = warp_fmaxf(wmax);
+    wmin = -warp_fmaxf(-wmin);
+    cmax = warp_fmaxf(cmax);
+    if (lane == 0) {
+      sh[wid][2 * DP] = W;
+      sh[wid][2 * DP + 1] = nv;
+      shl[wid] = last;
+      shm[wid][0] = wmax;
+      shm[wid][1] = wmin;
+      shm[wid][2] = cmax;
+    }
+    __syncthreads();
+    double *rec = A.rec + v * stats_stride(DP);
+    for (int t = tid; t < 2 * DP + 2; t += 256) {
+      double tot = 0.0;
+      for (int qq = 0; qq < NW; ++qq) tot += sh[qq][t];
+      if (t < 2 * DP) rec[3 + t] = tot;  // sum w' p, then sum p (valid points)
+      else rec[t - 2 * DP] = tot;        // W, valid count
+    }
+    if (tid == 0) {
+      long long lst = -1;
+      float m0 = -INFINITY, m1 = INFINITY, m2 = 0.f;
+      for (int qq = 0; qq < NW; ++qq) {
+        lst = shl[qq] > lst ? shl[qq] : lst;
+        m0 = fmaxf(m0, shm[qq][0]);
+        m1 = fminf(m1, shm[qq][1]);
+        m2 = fmaxf(m2, shm[qq][2]);
+      }
+      rec[2] = (double)lst;
+      rec[3 + 2 * DP] = m0;  // largest and smallest effective weight
+      rec[4 + 2 * DP] = m1;
+      rec[5 + 2 * DP] = m2;  // largest |coordinate| of a valid point
     }
     __syncthreads();
   });
@@ -506,6 +692,7 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
   int64_t cxn = A.chx[p];
   if (cxn > hi - lo) cxn = hi - lo;
   int64_t count_x = 0;
+  double cmax[2] = {0.0, 0.0};  // largest |coordinate| of each side (tensor-core layout)
   for (int side = 0; side < 2; ++side) {
     const int64_t first = side == 0 ? lo : lo + cxn;
     const int64_t n = side == 0 ? cxn : (hi - lo) - cxn;
@@ -544,6 +731,28 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
       else A.seg[p].ycount = count;
     }
     if (side == 0) count_x = count;
+    if (A.tc16) {
+      // fp16 operand scales (ra_tc16.cuh): weights |a| 2^-f <= 1; the
+      // coordinates' bound is finished below, once the anchors are known
+      double w0 = -INFINITY, w1 = INFINITY, c0 = 0.0;
+      for (int64_t c = lane; c < n; c += 32) {
+        w0 = fmax(w0, r0[c * rs + 3 + 2 * DP]);
+        w1 = fmin(w1, r0[c * rs + 4 + 2 * DP]);
+        c0 = fmax(c0, r0[c * rs + 5 + 2 * DP]);
+      }
+      w0 = warp_fmax(w0);
+      w1 = -warp_fmax(-w1);
+      cmax[side] = warp_fmax(c0);
+      if (lane == 0) {
+        // the largest |a| 2^-f lands in (1/2, 1]: small weights (1/n) are
+        // scaled up, so a kernel term's fp16 low half stays a normal number
+        const double amax = fmax(fabs(w0), fabs(w1)) / Wn;
+        double f = (amax > 0.0 && amax < INFINITY) ? ceil(log2(amax)) : 0.0;
+        f = f < -100.0 ? -100.0 : (f > 100.0 ? 100.0 : f);
+        meta[meta_tc_wscale(DP) + side] = exp2(-f);
+        meta[meta_tc_fold(DP) + side] = w1 >= 0.0 ? 1.0 : 0.0;
+      }
+    }
     // one lane per coordinate, the chunks summed in order (fixed order:
     // deterministic); each lane also finishes its own coordinates below
     for (int dd = lane; dd < DP; dd += 32) {
@@ -576,6 +785,26 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
           meta[4 + 2 * DP + dd] = ax;
           meta[4 + 3 * DP + dd] = ay;
         }
+      }
+    }
+  }
+  if (A.tc16) {
+    // |x'| <= c (max |x| + max |anchor|); 2^e keeps that bound <= 2^15
+    __syncwarp();
+    double am[2] = {0.0, 0.0};
+    for (int dd = lane; dd < DP; dd += 32) {
+      am[0] = fmax(am[0], fabs(meta[4 + 2 * DP + dd]));
+      am[1] = fmax(am[1], fabs(meta[4 + 3 * DP + dd]));
+    }
+    am[0] = warp_fmax(am[0]);
+    am[1] = warp_fmax(am[1]);
+    if (lane == 0) {
+      const double sc = (double)pair_scale(A.scale, A.sigma_p, p);
+      for (int side = 0; side < 2; ++side) {
+        const double bound = sc * (cmax[side] + am[side]);
+        double e = (bound > 0.0 && bound < INFINITY) ? floor(log2(32768.0 / bound)) : 0.0;
+        e = e < -60.0 ? -60.0 : (e > 60.0 ? 60.0 : e);
+        meta[meta_tc_cscale(DP) + side] = exp2(e);
       }
     }
   }
@@ -672,6 +901,98 @@ __global__ void __launch_bounds__(256, 4) packgw_kernel(PrepArgs A) {
     // normalised weights, one point per thread
     for (int64_t i = b + threadIdx.x; i < e; i += 256)
       Ap[s + i] = (float)((double)eff_weight(w, mask, wmode, s + i) / Wn);
+  });
+}
+
+// Tensor-core layout (ra_tc16.cuh), on top of what packgw_kernel writes (Gx,
+// Ax, read by the backward epilogue): per 64-point tile, the fp16 hi and lo
+// halves of x' 2^e in the canonical core-matrix layout (byte offset of point
+// j, coordinate d: (d/8)*1024 + (j/8)*128 + (j%8)*16 + (d%8)*2), and per slot
+// |x'|^2, |x'|^2 - log2 a (+inf for a <= 0) and a 2^-f.  Masked points and the
+// padding slots up to the tile boundary are zero points of zero weight.  One
+// thread per (point, 8 coordinates); |x'|^2 is summed over the point's
+// threads in a fixed order.
+template <int DP>
+__global__ void __launch_bounds__(256) packtc_kernel(PrepArgs A) {
+  constexpr int NG = DP / 8;      // threads per point
+  constexpr int PPC = 256 / NG;   // points per CTA step
+  constexpr int TB = DP * 128;    // bytes of a hi (or lo) tile
+  static_assert(NG >= 4 && NG <= 32 && (NG & (NG - 1)) == 0, "point groups");
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int D = A.D, g = threadIdx.x % NG, pl = threadIdx.x / NG;
+  const unsigned gmask = (NG == 32 ? 0xffffffffu : ((1u << NG) - 1u)) << ((threadIdx.x & 31) & ~(NG - 1));
+  for_each_chunk(M, [&](int64_t p, int side, int64_t ch, int64_t, int64_t, int64_t) {
+    const Seg sg = A.seg[p];
+    const int64_t s = side == 0 ? sg.xs : sg.ys;
+    const int64_t count = side == 0 ? sg.xcount : sg.ycount;
+    const float *pts = side == 0 ? A.x : A.y;
+    const float *w = side == 0 ? A.w_x : A.w_y;
+    const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
+    const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
+    float *Gp = side == 0 ? A.Gx : A.Gy;
+    float *Ap = side == 0 ? A.Ax : A.Ay;
+    uint8_t *hp = side == 0 ? A.hx : A.hy;
+    uint8_t *lp = side == 0 ? A.lx : A.ly;
+    float *cp = side == 0 ? A.cx : A.cy;
+    const int64_t tb = (side == 0 ? A.tbase_x : A.tbase_y)[p];
+    const double *meta = A.meta + p * meta_stride(DP);
+    const double Wn = meta[side];
+    const double *anc = meta + 4 + (2 + side) * DP;
+    const float sc = pair_scale(A.scale, A.sigma_p, p);
+    const float cs = (float)meta[meta_tc_cscale(DP) + side];
+    const float wsc = (float)meta[meta_tc_wscale(DP) + side];
+    double ag[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) ag[u] = 8 * g + u < D ? anc[8 * g + u] : 0.0;
+    const int64_t b = ch * kChunk;
+    const int64_t cend = ceil_div(count, (int64_t)kTile) * kTile;  // through the last tile
+    const int64_t e = b + kChunk < cend ? b + kChunk : cend;
+    for (int64_t i = b + pl; i < e; i += PPC) {
+      const int64_t gi = s + i;
+      const bool real = i < count;
+      const bool valid = real && (mask == nullptr || mask[gi] != 0);
+      float xv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int d = 8 * g + u;
+        xv[u] = (real && d < D) ? sc * (float)((double)pts[gi * D + d] - ag[u]) : 0.f;
+      }
+      if (real) {
+        float4 *gp = reinterpret_cast<float4 *>(Gp + gi * DP + 8 * g);
+        gp[0] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+        gp[1] = make_float4(xv[4], xv[5], xv[6], xv[7]);
+      }
+      uint32_t hh[4], ll[4];
+      float sq = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float v0 = valid ? xv[2 * c] * cs : 0.f, v1 = valid ? xv[2 * c + 1] * cs : 0.f;
+        const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+        const __half l0 = __float2half_rn(v0 - __half2float(h0));
+        const __half l1 = __float2half_rn(v1 - __half2float(h1));
+        hh[c] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        ll[c] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        if (valid) {
+          sq = fmaf(xv[2 * c], xv[2 * c], sq);
+          sq = fmaf(xv[2 * c + 1], xv[2 * c + 1], sq);
+        }
+      }
+      const int64_t tile = tb + i / kTile;
+      const int j = (int)(i % kTile);
+      const size_t off = (size_t)tile * TB + (size_t)(g * 1024 + (j >> 3) * 128 + (j & 7) * 16);
+      *reinterpret_cast<uint4 *>(hp + off) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+      *reinterpret_cast<uint4 *>(lp + off) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+#pragma unroll
+      for (int o = 1; o < NG; o <<= 1) sq += __shfl_xor_sync(gmask, sq, o);
+      if (g == 0) {
+        const float a = real ? (float)((double)eff_weight(w, mask, wmode, gi) / Wn) : 0.f;
+        if (real) Ap[gi] = a;
+        float *cv = cp + tile * (3 * kTile);
+        cv[j] = sq;
+        cv[kTile + j] = a > 0.f ? sq - log2f(a) : INFINITY;
+        cv[2 * kTile + j] = a * wsc;
+      }
+    }
   });
 }
 
