@@ -493,7 +493,7 @@ class EmbedWorkload(RaggedWorkload):
         # tensor work of one launch of the tensor-core kernel: per graph 4 row-only
         # orientations of ceil(n/128) row tiles x ceil(n/64) column tiles, each a
         # 128 x 64 x 128 Gram GEMM and a 128 x 128 x 64 weighted-sum GEMM,
-        # three TF32 products apiece (hi*hi + hi*lo + lo*hi)
+        # three fp16 products apiece (hi*hi + hi*lo + lo*hi)
         tiles = float(np.sum(4 * np.ceil(nx / 128.0) * np.ceil(nx / 64.0)))
         self.tensor_flops_issued = tiles * 2 * 3 * (2.0 * 128 * 64 * 128)
         self.sigma, self.center, self.dim = 1.0, False, 128
@@ -518,27 +518,27 @@ class EmbedWorkload(RaggedWorkload):
 
     def roofline(self, t_tiles, peak_fp32):
         """Tensor roofline: algorithmic flops = full terms x (Gram + weighted
-        sum) x 2 D, against the TF32 peak (half the measured dense bf16 rate)."""
+        sum) x 2 D, against the dense fp16 tensor peak (the kernel issues
+        kind::f16 MMAs, which run at the measured dense bf16 rate)."""
         peaks = read_measured_peaks()
         measured = bool(peaks and peaks.get("bf16_tflops"))
         bf16 = peaks["bf16_tflops"] if measured else 1590.0  # fallback: earlier pool measurement
-        tf32 = bf16 * 1e12 / 2.0
+        f16 = bf16 * 1e12
         algo = self.full_local * 2 * 2.0 * self.dim
         return {
             "bound": "tensor",
             "achieved": algo / t_tiles / 1e12,
-            "peak": tf32 / 1e12,
+            "peak": f16 / 1e12,
             "unit": "TFLOP/s",
-            "frac": algo / t_tiles / tf32,
+            "frac": algo / t_tiles / f16,
             "peak_source": ("MEASURED_PEAKS.json bf16_tflops" if measured else
-                            "fallback 1.59 PFLOP/s bf16") + " / 2 (dense TF32 runs at half the "
-                           "bf16 rate)",
-            "kernel": "tilestc_kernel<128,1> (tcgen05 kind::tf32, 3xTF32)",
+                            "fallback 1.59 PFLOP/s bf16") + " (dense fp16 = dense bf16 rate)",
+            "kernel": "tilestc16_kernel<128,1> (tcgen05 kind::f16, three fp16 products per GEMM)",
             "kernel_ms": t_tiles * 1e3,
             "flops_per_full_term": 4.0 * self.dim,
-            "issued_frac": self.tensor_flops_issued / t_tiles / tf32,
-            "issued_note": "tensor flops the kernel issues (three TF32 products, four row-only "
-                           "orientations, tile padding) over the same peak",
+            "issued_frac": self.tensor_flops_issued / t_tiles / f16,
+            "issued_note": "tensor flops the kernel issues (three fp16 products for fp32 accuracy, "
+                           "four row-only orientations, tile padding) over the same peak",
             "traffic": None,
         }
 

@@ -21,9 +21,7 @@
 #include "ra_pdl.cuh"
 #include "ra_plan.cuh"
 #include "ra_prep.cuh"
-#include "ra_tc.cuh"
 #include "ra_tc16.cuh"
-#include "ra_tcws.cuh"
 #include "ra_tiles3.cuh"
 #include "ra_tilesg.cuh"
 
@@ -58,6 +56,7 @@ struct Layout {
       coef, Ktmp, chcnt, chx, choff, rec;
   size_t tiles_x, tiles_y, Gx, Gy, Ax, Ay, accX, accY;
   size_t hx, hy, lx, ly, cx, cy;  // tc16: fp16 hi / lo tiles and slot values
+  size_t ix;                      // tc16: one ItemX record per work item
   size_t acc_x_bytes, acc_y_bytes;
   size_t total;
 };
@@ -185,6 +184,7 @@ Layout make_layout(const ra_kde_desc *d) {
       L.ly = take(tbytes * (size_t)L.max_tiles_y);
       L.cx = take(sizeof(float) * kT16SlotFloats * (size_t)L.max_tiles_x);
       L.cy = take(sizeof(float) * kT16SlotFloats * (size_t)L.max_tiles_y);
+      L.ix = take(sizeof(ItemX) * (size_t)L.max_items);
     }
     L.acc_x_bytes = sizeof(float) * nx * L.acc_stride;
     L.acc_y_bytes = sizeof(float) * ny * L.acc_stride;
@@ -287,46 +287,6 @@ void launch_tilesg_dp(int mode, int64_t grid, const TilesGArgs &T, cudaStream_t 
     tilesg_kernel<DP, 2><<<(unsigned)grid, kGenRows, 0, st>>>(T);
 }
 
-// Tensor-core path: a persistent grid, as many CTAs per SM as TMEM allows.
-// Padded widths 64 and 128 (one CTA per SM) take the warp-specialised kernel.
-template <int DP, int MODE>
-int launch_tilestc_dm(int64_t max_items, const TilesGArgs &T, cudaStream_t st) {
-  if constexpr (DP >= 64) {
-    const size_t smem = tc_ws_smem_request(DP);
-    if (cudaFuncSetAttribute(tilestc_ws_kernel<DP, MODE>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return RA_ERR_CUDA;
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int64_t grid = sms > 0 ? sms : 1;
-    if (grid > max_items) grid = max_items;
-    tilestc_ws_kernel<DP, MODE><<<(unsigned)grid, kWsThreads, smem, st>>>(T);
-    return cuda_status(cudaGetLastError());
-  }
-  const size_t smem = tc_smem_request(DP);
-  static_assert(tc_smem_bytes(DP) <= tc_smem_request(DP), "shared memory request too small");
-  if (cudaFuncSetAttribute(tilestc_kernel<DP, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem) != cudaSuccess)
-    return RA_ERR_CUDA;
-  int dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t per_sm = 512 / tc_tmem_cols(DP);
-  int64_t grid = (int64_t)(sms > 0 ? sms : 1) * per_sm;
-  if (grid > max_items) grid = max_items;
-  tilestc_kernel<DP, MODE><<<(unsigned)grid, kTcThreads, smem, st>>>(T);
-  return cuda_status(cudaGetLastError());
-}
-
-template <int DP>
-int launch_tilestc_d(int mode, int64_t max_items, const TilesGArgs &T, cudaStream_t st) {
-  if (mode == 0) return launch_tilestc_dm<DP, 0>(max_items, T, st);
-  if (mode == 1) return launch_tilestc_dm<DP, 1>(max_items, T, st);
-  return launch_tilestc_dm<DP, 2>(max_items, T, st);  // mode 2: sigma gradient
-}
-
 template <int DP, int MODE>
 int launch_tc16_dm(int64_t max_items, const Tc16Args &T, cudaStream_t st) {
   const size_t smem = t16_smem_request(DP);
@@ -356,18 +316,6 @@ int launch_tc16(int DP, int mode, int64_t max_items, const Tc16Args &T, cudaStre
     case 32: rc = launch_tc16_d<32>(mode, max_items, T, st); break;
     case 64: rc = launch_tc16_d<64>(mode, max_items, T, st); break;
     case 128: rc = launch_tc16_d<128>(mode, max_items, T, st); break;
-    default: return RA_ERR_INVALID_ARGUMENT;
-  }
-  ++g_launches;
-  return rc;
-}
-
-int launch_tilestc(int DP, int mode, int64_t max_items, const TilesGArgs &T, cudaStream_t st) {
-  int rc;
-  switch (DP) {
-    case 32: rc = launch_tilestc_d<32>(mode, max_items, T, st); break;
-    case 64: rc = launch_tilestc_d<64>(mode, max_items, T, st); break;
-    case 128: rc = launch_tilestc_d<128>(mode, max_items, T, st); break;
     default: return RA_ERR_INVALID_ARGUMENT;
   }
   ++g_launches;
@@ -597,6 +545,26 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
   g_launches += 3;
   if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
 
+  // ---- the tensor-core path's per-item records (the plan is complete) ----
+  if (L.tc16) {
+    const Seg *sg = at<Seg>(ws, L.seg);
+    const double *mt = at<double>(ws, L.meta);
+    const int64_t *tbx = at<int64_t>(ws, L.tbase_x), *tby = at<int64_t>(ws, L.tbase_y);
+    const Item *itm = at<Item>(ws, L.items);
+    const int64_t *nit = at<int64_t>(ws, L.hdr + kHdrNItems);
+    ItemX *ixp = at<ItemX>(ws, L.ix);
+    const unsigned ig = (unsigned)(L.max_items < 256 * 1184 ? ceil_div(L.max_items, (int64_t)256)
+                                                            : 1184);
+    if (L.DP == 32)
+      t16_items_kernel<32><<<ig, 256, 0, st>>>(itm, nit, sg, mt, tbx, tby, ixp);
+    else if (L.DP == 64)
+      t16_items_kernel<64><<<ig, 256, 0, st>>>(itm, nit, sg, mt, tbx, tby, ixp);
+    else
+      t16_items_kernel<128><<<ig, 256, 0, st>>>(itm, nit, sg, mt, tbx, tby, ixp);
+    ++g_launches;
+    if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
+  }
+
   // ---- pack the large pairs' D <= 3 tiles (their metadata is complete) ----
   if (L.packed3 && may_be_large) {
     pack3_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pk);
@@ -678,6 +646,7 @@ int compute_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
       Tc16Args C;
       std::memset(&C, 0, sizeof(C));
       C.items = T.items;
+      C.ix = at<ItemX>(ws, L.ix);
       C.n_items = T.n_items;
       C.seg = T.seg;
       C.meta = at<double>(ws, L.meta);

@@ -38,7 +38,8 @@
 //              (cp.async.bulk, no multicast, this GPU's memory only).
 //   warp 9     lane 0 issues the MMAs: GEMM 1 of tile t into S stage t % 2,
 //              then GEMM 2 of tile t - 1, so the tensor core has GEMM 1 of
-//              the next tile while the epilogue works on the current one.
+//              the next tile while the epilogue works on the current one (at
+//              an item boundary the previous item's last GEMM 2 goes first).
 // TMEM columns: X buffers [0, DP) and [DP, 2DP) (hi in the first half, lo in
 // the second, two fp16 per column), T [2DP, 3DP), S/P stages [3DP, 3DP+64)
 // and [3DP+64, 3DP+128).  P (hi then lo, 16 columns each per 32-point half)
@@ -49,7 +50,8 @@
 // returns (the same contract as the other tensor-core kernels).
 #pragma once
 
-#include "ra_tcws.cuh"
+#include "ra_prep.cuh"
+#include "ra_tcprim.cuh"
 
 namespace ra {
 
@@ -65,11 +67,16 @@ __host__ __device__ constexpr int t16_tile_bytes(int DP) { return DP * 128; }  /
 __host__ __device__ constexpr int t16_stage_bytes(int DP) {
   return 2 * t16_tile_bytes(DP) + kT16SlotFloats * 4;
 }
-__host__ __device__ constexpr int t16_tmem_cols(int DP) { return 3 * DP + 128 <= 256 ? 256 : 512; }
-constexpr int kT16Bars = 2 * kT16Stages + 9;
+constexpr int kT16SStages = 3;   // S / P stages in TMEM
+__host__ __device__ constexpr int t16_tmem_cols(int DP) {
+  return 2 * DP + 64 * kT16SStages <= 256 ? 256 : 512;
+}
+constexpr int kT16Bars = 2 * kT16Stages + 3 * kT16SStages + 2;
 __host__ __device__ constexpr size_t t16_smem_bytes(int DP) {
-  // stages, barriers, TMEM address + abort flag, the epilogue's reductions
-  return (size_t)kT16Stages * t16_stage_bytes(DP) + kT16Bars * 8 + 16 + 128 * 8 * 2 + 16 * 8;
+  // stages, the epilogue's row staging (2 DP bytes per thread), barriers,
+  // TMEM address + abort flag, the epilogue's reductions
+  return (size_t)kT16Stages * t16_stage_bytes(DP) + (size_t)32 * kT16EpiWarps * (2 * DP + 16) +
+         kT16Bars * 8 + 16 + 2 * 128 * 8 * 2 + 2 * 8 * 8;
 }
 __host__ __device__ constexpr size_t t16_smem_request(int DP) {
   // at least 120 KB: one CTA per SM (each takes the TMEM columns it needs
@@ -77,8 +84,29 @@ __host__ __device__ constexpr size_t t16_smem_request(int DP) {
   return t16_smem_bytes(DP) > (size_t)120 * 1024 ? t16_smem_bytes(DP) : (size_t)120 * 1024;
 }
 
+// Everything a role needs about one work item, in one 64-byte record
+// (t16_items_kernel), so that no role walks item -> pair -> metadata with
+// dependent loads inside its loop.
+struct ItemX {
+  int64_t rbase;   // first point of the row cloud
+  int64_t rcnt;    // points of the row cloud
+  int64_t tb_row;  // first 64-point tile of the row cloud
+  int64_t tb_col;  // first 64-point tile of the column cloud
+  int32_t tile;    // 128-row tile of the item
+  int32_t ntiles;  // 64-point column tiles
+  int32_t flags;   // kIx* bits, block id << 4
+  float cS;        // 2 / (2^e_row 2^e_col): 2 x'.y' from the scaled GEMM
+  float lwsc;      // -f: log2 of the column weights' scale
+  float tsc;       // 2^f / 2^e_col: T from the scaled GEMM
+  float f2;        // 2^f
+  int32_t pad;
+};
+static_assert(sizeof(ItemX) == 64, "one 64-byte record per item");
+constexpr int kIxRowsX = 1, kIxColsX = 2, kIxSelf = 4, kIxFold = 8;
+
 struct Tc16Args {
   const Item *items;
+  const ItemX *ix;
   const int64_t *n_items;
   const Seg *seg;
   const double *meta;                   // per pair (meta_tc_* scales)
@@ -142,30 +170,75 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   return r;
 }
 
+// The ItemX records of all items (grid-stride over the device-side count).
+template <int DP>
+__global__ void __launch_bounds__(256) t16_items_kernel(const Item *items, const int64_t *n_items,
+                                                         const Seg *seg, const double *meta_all,
+                                                         const int64_t *tbase_x,
+                                                         const int64_t *tbase_y, ItemX *ix) {
+  const int64_t n = *n_items;
+  for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < n;
+       it += (int64_t)gridDim.x * blockDim.x) {
+    const Item item = items[it];
+    const Seg sg = seg[item.pair];
+    const int o = item.block;  // 0: x-y, 1: x-x, 2: y-y, 3: y-x
+    const bool rows_x = (o == 0 || o == 1), cols_x = (o == 1 || o == 3);
+    const int rside = rows_x ? 0 : 1, cside = cols_x ? 0 : 1;
+    const double *meta = meta_all + item.pair * (int64_t)meta_stride(DP);
+    const double csr = meta[meta_tc_cscale(DP) + rside], csc = meta[meta_tc_cscale(DP) + cside];
+    const double wsc = meta[meta_tc_wscale(DP) + cside];
+    ItemX x;
+    x.rbase = rows_x ? sg.xs : sg.ys;
+    x.rcnt = rows_x ? sg.xcount : sg.ycount;
+    x.tb_row = (rows_x ? tbase_x : tbase_y)[item.pair];
+    x.tb_col = (cols_x ? tbase_x : tbase_y)[item.pair];
+    x.tile = item.tile;
+    x.ntiles = (int32_t)ceil_div(cols_x ? sg.xcount : sg.ycount, (int64_t)kT16Cols);
+    x.flags = (rows_x ? kIxRowsX : 0) | (cols_x ? kIxColsX : 0) | ((o == 1 || o == 2) ? kIxSelf : 0) |
+              (meta[meta_tc_fold(DP) + cside] != 0.0 ? kIxFold : 0) | (o << 4);
+    x.cS = (float)(2.0 / (csr * csc));
+    x.lwsc = (float)log2(wsc);
+    x.tsc = (float)(1.0 / (wsc * csc));
+    x.f2 = (float)(1.0 / wsc);
+    x.pad = 0;
+    ix[it] = x;
+  }
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
 template <int DP, int MODE>
 __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
   static_assert(DP == 32 || DP == 64 || DP == 128, "tensor-core path: DP in {32, 64, 128}");
   constexpr bool GRAD = MODE >= 1;
   constexpr bool SIG = MODE == 2;
   constexpr int NCOLS = t16_tmem_cols(DP);
-  constexpr int C_T = 2 * DP, C_S = 3 * DP;
+  constexpr int C_T = DP, C_S = 2 * DP;  // X at [0, DP)
+  constexpr int NS = kT16SStages;
   constexpr int TB = t16_tile_bytes(DP), SB = t16_stage_bytes(DP);
   constexpr uint32_t IDESC1 = t16_idesc(kT16Cols, 0), IDESC2 = t16_idesc(DP, 1);
   constexpr int ET = 32 * kT16EpiWarps;  // epilogue threads
   constexpr int NST = kT16Stages;
   constexpr int HC = DP / 4;  // TMEM cells per thread per X half (hi or lo)
+  // staging bytes per epilogue thread: its half row (hi + lo chunks) on the
+  // way into TMEM, or its half row of T on the way out; the 16-byte pad puts
+  // consecutive threads' slots in different banks
+  constexpr int XSB = 2 * DP + 16;
 
   extern __shared__ __align__(1024) uint8_t t16_smem[];
-  uint64_t *bars = reinterpret_cast<uint64_t *>(t16_smem + NST * SB);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(t16_smem + NST * SB + ET * XSB);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + kT16Bars);
   volatile int *abortf = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  double *red_s = reinterpret_cast<double *>(tmem_slot + 4);  // [128] row sums of half 1
-  double *red_g = red_s + 128;                                // [128] sigma sums of half 1
-  double *red_w = red_g + 128;                                // [16] per-warp K, S
+  double *red_s = reinterpret_cast<double *>(tmem_slot + 4);  // [2][128] row sums of half 1
+  double *red_g = red_s + 256;                                // [2][128] sigma sums of half 1
+  double *red_w = red_g + 256;                                // [2][8] per-warp K, S
   auto bar = [&](int i) { return smem_u32(bars + i); };
-  // barrier ids: yfull[s], yfree[s], xfull[2], g1[2], pfull[2], g2[2], tfree
-  const int B_YFULL = 0, B_YFREE = NST, B_XFULL = 2 * NST, B_G1 = 2 * NST + 2,
-            B_PFULL = 2 * NST + 4, B_G2 = 2 * NST + 6, B_TFREE = 2 * NST + 8;
+  // barrier ids: yfull[NST], yfree[NST], xfull, g1[NS], pfull[NS], g2[NS], tfree
+  const int B_YFULL = 0, B_YFREE = NST, B_XFULL = 2 * NST, B_G1 = 2 * NST + 1,
+            B_PFULL = 2 * NST + 1 + NS, B_G2 = 2 * NST + 1 + 2 * NS, B_TFREE = 2 * NST + 1 + 3 * NS;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (warp == 0) {
@@ -180,8 +253,8 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
       mbar_init(bar(B_YFULL + s), 1);
       mbar_init(bar(B_YFREE + s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(B_XFULL + b), ET);
+    mbar_init(bar(B_XFULL), ET);
+    for (int b = 0; b < NS; ++b) {
       mbar_init(bar(B_G1 + b), 1);
       mbar_init(bar(B_PFULL + b), ET);
       mbar_init(bar(B_G2 + b), 1);
@@ -204,163 +277,99 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
       atomicOr(A.err, (int)kErrTimeout);
     }
   };
-  // column tiles of an item
-  auto item_tiles = [&](const Item &item, const Seg &sg) {
-    const bool cols_x = (item.block == 1 || item.block == 3);
-    return (int)ceil_div(cols_x ? sg.xcount : sg.ycount, (int64_t)kT16Cols);
-  };
 
   if (warp < kT16EpiWarps) {
     // =========================== epilogue ===================================
     const int q = warp & 3, h = warp >> 2;
     const int r = 32 * q + lane;  // row within the item's 128-row tile
     const uint32_t tlane = tbase + ((uint32_t)(32 * q) << 16);
-    // this thread's half of the next item's rows (hi, lo) into X buffer b
-    auto load_x = [&](int64_t it, int b) {
-      const Item item = A.items[it];
-      const Seg sg = A.seg[item.pair];
-      const bool rows_x = (item.block == 0 || item.block == 1);
-      const int64_t rcnt = rows_x ? sg.xcount : sg.ycount;
-      const int64_t sub = 2 * (int64_t)item.tile + (r >> 6);  // 64-point tile of this row
-      const bool have = sub < ceil_div(rcnt, (int64_t)kT16Cols);
-      const int64_t tile = (rows_x ? A.tbase_x : A.tbase_y)[item.pair] + sub;
+    // this thread's staging slot for its half of a row (hi chunks, lo chunks)
+    const uint32_t xslot = smem_u32(t16_smem + NST * SB) + (uint32_t)(tid * XSB);
+    // Row data of an item: the weight and |x'|^2 of this thread's row, and,
+    // for an item with column tiles, its hi / lo chunks copied into the
+    // staging slot (cp.async, zero-filled beyond the cloud).  Nothing here
+    // waits: the loads land while the current item's tiles are processed.
+    // X is committed (and `xfull` completes a phase) only for items with
+    // column tiles, the items the MMA issuer waits for, so neither side can
+    // run two phases ahead of the other.
+    auto stage_rows = [&](const ItemX &I, float &a_out, float &xsq_out) {
+      // the slot may still be the source of this thread's last T store
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      const bool rows_x = (I.flags & kIxRowsX) != 0;
+      const int64_t row = (int64_t)I.tile * 128 + r;
+      const int64_t sub = 2 * (int64_t)I.tile + (r >> 6);  // 64-point tile of this row
+      const bool have = sub < ceil_div(I.rcnt, (int64_t)kT16Cols);
+      const int64_t tile = I.tb_row + (have ? sub : 0);
       const int j = r & 63;
+      a_out = row < I.rcnt ? (rows_x ? A.Ax : A.Ay)[I.rbase + row] : 0.f;
+      xsq_out = have ? (rows_x ? A.cx : A.cy)[tile * kT16SlotFloats + j] : 0.f;
+      if (I.ntiles == 0) return;  // no GEMM reads this item's rows
       const size_t off = (size_t)tile * TB + (size_t)((j >> 3) * 128 + (j & 7) * 16);
       const uint8_t *hs = (rows_x ? A.hx : A.hy) + off;
       const uint8_t *ls = (rows_x ? A.lx : A.ly) + off;
-      uint32_t ch[HC], cl[HC];
 #pragma unroll
       for (int g = 0; g < DP / 16; ++g) {
         const int dg = h * (DP / 16) + g;  // coordinate group (8 coordinates, 16 bytes)
-        uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
-        if (have) {
-          vh = *reinterpret_cast<const uint4 *>(hs + dg * 1024);
-          vl = *reinterpret_cast<const uint4 *>(ls + dg * 1024);
-        }
-        ch[4 * g] = vh.x; ch[4 * g + 1] = vh.y; ch[4 * g + 2] = vh.z; ch[4 * g + 3] = vh.w;
-        cl[4 * g] = vl.x; cl[4 * g + 1] = vl.y; cl[4 * g + 2] = vl.z; cl[4 * g + 3] = vl.w;
+        cp_async16(xslot + 16 * g, hs + dg * 1024, have ? 16u : 0u);
+        cp_async16(xslot + 16 * (DP / 16 + g), ls + dg * 1024, have ? 16u : 0u);
       }
-      const uint32_t cx = (uint32_t)(b * DP);
-      tmem_st_n<HC>(tlane + cx + h * HC, ch);           // hi: columns [cx, cx + DP/2)
-      tmem_st_n<HC>(tlane + cx + DP / 2 + h * HC, cl);  // lo: columns [cx + DP/2, cx + DP)
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // the staged rows into X (this thread's lane, its half)
+    auto commit_rows = [&]() {
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      uint32_t ch[HC], cl[HC];
+#pragma unroll
+      for (int g = 0; g < DP / 16; ++g) {
+        uint32_t v0, v1, v2, v3, w0, w1, w2, w3;
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(v0), "=r"(v1), "=r"(v2), "=r"(v3)
+                     : "r"(xslot + 16 * g));
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                     : "r"(xslot + 16 * (DP / 16 + g)));
+        ch[4 * g] = v0; ch[4 * g + 1] = v1; ch[4 * g + 2] = v2; ch[4 * g + 3] = v3;
+        cl[4 * g] = w0; cl[4 * g + 1] = w1; cl[4 * g + 2] = w2; cl[4 * g + 3] = w3;
+      }
+      tmem_st_n<HC>(tlane + h * HC, ch);           // hi: columns [0, DP/2)
+      tmem_st_n<HC>(tlane + DP / 2 + h * HC, cl);  // lo: columns [DP/2, DP)
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
-      mbar_arrive(bar(B_XFULL + b));
+      mbar_arrive(bar(B_XFULL));
     };
 
-    uint32_t t = 0;  // column tiles seen (all items)
-    int k = 0;       // items seen
-    if (ifirst < n_items) load_x(ifirst, 0);
-    for (int64_t it = ifirst; it < n_items; it += istep, ++k) {
-      if (it + istep < n_items) load_x(it + istep, (k + 1) & 1);
-      const Item item = A.items[it];
-      const Seg sg = A.seg[item.pair];
-      const int o = item.block;  // 0: x-y, 1: x-x, 2: y-y, 3: y-x
-      const bool rows_x = (o == 0 || o == 1), cols_x = (o == 1 || o == 3);
-      const bool self = (o == 1 || o == 2);
-      const int rside = rows_x ? 0 : 1, cside = cols_x ? 0 : 1;
-      const int64_t rbase = rows_x ? sg.xs : sg.ys, rcnt = rows_x ? sg.xcount : sg.ycount;
-      const int64_t row0 = (int64_t)item.tile * 128;
-      const int64_t row = row0 + r;
-      const bool rv = row < rcnt;
-      const float a = rv ? (rows_x ? A.Ax : A.Ay)[rbase + row] : 0.f;
-      const int ntiles = item_tiles(item, sg);
-      // |x'|^2 of this row (packed slot value; 0 beyond the cloud)
-      float xsq = 0.f;
-      {
-        const int64_t sub = 2 * (int64_t)item.tile + (r >> 6);
-        if (sub < ceil_div(rcnt, (int64_t)kT16Cols))
-          xsq = (rows_x ? A.cx : A.cy)[((rows_x ? A.tbase_x : A.tbase_y)[item.pair] + sub) *
-                                           kT16SlotFloats + (r & 63)];
+    // An item's outputs are written after the FIRST tile of the next item
+    // (or after the loop): GEMM 2 of its last tile has landed by then, and
+    // the tensor core has the next GEMM 1 while T is read out.
+    struct Out {
+      int64_t it, rbase, row;
+      double s64, sg64;
+      float a, tsc, f2;
+      uint32_t tlast;  // the item's last column tile (if it has any)
+      int flags, ntiles;
+      bool rv;
+    };
+    bool ok = true;
+    // all 256 threads, ok uniform: T into the records, the item's K and S
+    auto outputs = [&](const Out &P, int rb) {
+      const int o = P.flags >> 4;  // 0: x-y, 1: x-x, 2: y-y, 3: y-x
+      const bool rows_x = (P.flags & kIxRowsX) != 0, self = (P.flags & kIxSelf) != 0;
+      const bool crossb = (o == 0 || o == 3);
+      if (h == 1) {
+        red_s[rb * 128 + r] = P.s64;
+        red_g[rb * 128 + r] = P.sg64;
       }
-      const double *meta = A.meta + item.pair * (int64_t)meta_stride(DP);
-      const double csr = meta[meta_tc_cscale(DP) + rside], csc = meta[meta_tc_cscale(DP) + cside];
-      const double wsc = meta[meta_tc_wscale(DP) + cside];  // 2^-f of the column weights
-      const bool fold = meta[meta_tc_fold(DP) + cside] != 0.0;
-      const float cS = (float)(2.0 / (csr * csc));      // 2 S = cS S'
-      const float nxf = -xsq + (float)log2(wsc);        // - |x'|^2 - f
-      float sr = 0.f;
-      double s64 = 0.0, sg64 = 0.0;
-      bool ok = true;
-      for (int jt = 0; jt < ntiles; ++jt, ++t) {
-        const int ss = (int)(t & 1u), ys = (int)(t % NST);
-        const bool w_ok = ws_wait(bar(B_YFULL + ys), (t / NST) & 1u, abortf, A.spin_limit) &&
-                          ws_wait(bar(B_G1 + ss), (t >> 1) & 1u, abortf, A.spin_limit);
-        if (role_sync_or(1, ET, !w_ok)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const float *cb = reinterpret_cast<const float *>(t16_smem + ys * SB + 2 * TB);
-        const float *ysq = cb, *yq = cb + kT16Cols, *bw = cb + 2 * kT16Cols;
-        const int64_t j0 = (int64_t)jt * kT16Cols + 32 * h;
-        const int64_t dj = row - j0;
-        const int diag = (self && dj >= 0 && dj < 32) ? (int)dj : -1;
-        float S[32];
-        tmem_ld32(tlane + C_S + 64 * ss + 32 * h, S);
-        float st = 0.f, sgt = 0.f;
-        uint32_t ph[16], pl[16];
-#pragma unroll
-        for (int u2 = 0; u2 < 16; ++u2) {
-          float wv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int u = 2 * u2 + e, j = 32 * h + u;
-            float w, r2 = 0.f;
-            if (fold) {
-              w = ex2(fmaf(S[u], cS, nxf - yq[j]));
-              if (SIG) r2 = fmaxf(fmaf(-S[u], cS, xsq + ysq[j]), 0.f);
-            } else {
-              r2 = fmaxf(fmaf(-S[u], cS, xsq + ysq[j]), 0.f);
-              w = bw[j] * ex2(-r2);
-            }
-            if (u == diag) w = 0.f;
-            st += w;
-            if (SIG) sgt = fmaf(w, r2, sgt);
-            wv[e] = w;
-          }
-          if (GRAD) {
-            const float h0 = __uint_as_float(__float_as_uint(wv[0]) & 0xFFFFE000u);
-            const float h1 = __uint_as_float(__float_as_uint(wv[1]) & 0xFFFFE000u);
-            ph[u2] = pack_f16x2(h0, h1);
-            pl[u2] = pack_f16x2(wv[0] - h0, wv[1] - h1);
-          }
-        }
-        if (GRAD) {
-          tmem_st16(tlane + C_S + 64 * ss + 32 * h, ph);
-          tmem_st16(tlane + C_S + 64 * ss + 32 * h + 16, pl);
-          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        }
-        sr += st;
-        s64 += (double)st;
-        if (SIG) sg64 += (double)sgt;
-        tc_fence_before();
-        mbar_arrive(bar(B_PFULL + ss));  // P ready, S and the slot values read
-      }
-      (void)sr;
-      if (ok && GRAD && ntiles > 0) {
-        // T of the item: after GEMM 2 of its last tile
-        const uint32_t tl = t - 1u;
-        const bool w_ok = ws_wait(bar(B_G2 + (int)(tl & 1u)), (tl >> 1) & 1u, abortf, A.spin_limit);
-        if (role_sync_or(1, ET, !w_ok)) ok = false;
-        tc_fence_after();
-      }
-      if (!ok) {
-        fail();
-        break;
-      }
-      const double f2 = 1.0 / wsc;  // 2^f
-      // ---- item outputs -------------------------------------------------------
       if (GRAD && A.need_rows) {
-        float *dst = (rows_x ? A.accX : A.accY) + (rbase + row) * gen_acc_stride(DP);
-        const bool crossb = (o == 0 || o == 3);
-        const int toff = crossb ? DP : 0, soff = 2 * DP + (crossb ? 1 : 0);
-        const float tsc = (float)(f2 / csc);  // T = T' 2^f / 2^e
+        // this thread's half row of T: scaled into the staging slot, then one
+        // bulk store of 2 DP bytes to its record (16-byte aligned: the record
+        // stride is (2 DP + 4) floats).  The TMEM loads are warp-collective,
+        // so every lane makes them; only rows inside the cloud store.
+        const int toff = crossb ? DP : 0;
+        constexpr int NW = DP / 2 < 32 ? DP / 2 : 32;
 #pragma unroll
-        for (int d0 = 0; d0 < DP / 2; d0 += (DP / 2 < 32 ? DP / 2 : 32)) {
-          constexpr int NW = DP / 2 < 32 ? DP / 2 : 32;
+        for (int d0 = 0; d0 < DP / 2; d0 += NW) {
           float T[32];
-          if (ntiles == 0) {
+          if (P.ntiles == 0) {
 #pragma unroll
             for (int u = 0; u < 32; ++u) T[u] = 0.f;
           } else if (NW == 32) {
@@ -371,50 +380,211 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
 #pragma unroll
             for (int u = 0; u < 16; ++u) T[u] = T16[u];
           }
-          if (rv) {
+          if (P.rv) {
 #pragma unroll
             for (int u = 0; u < NW; u += 4)
-              *reinterpret_cast<float4 *>(dst + toff + h * (DP / 2) + d0 + u) =
-                  make_float4(T[u] * tsc, T[u + 1] * tsc, T[u + 2] * tsc, T[u + 3] * tsc);
+              asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(xslot + 4 * (d0 + u)),
+                           "f"(T[u] * P.tsc), "f"(T[u + 1] * P.tsc), "f"(T[u + 2] * P.tsc),
+                           "f"(T[u + 3] * P.tsc)
+                           : "memory");
           }
         }
-        // the row's total over both halves, in a fixed order
-        if (h == 1) red_s[r] = s64;
-        role_sync(1, ET);
-        if (h == 0 && rv) dst[soff] = (float)((s64 + red_s[r]) * f2);
-        role_sync(1, ET);
+        if (P.rv) {
+          float *dst = (rows_x ? A.accX : A.accY) + (P.rbase + P.row) * gen_acc_stride(DP);
+          fence_async_smem();
+          asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                           dst + toff + h * (DP / 2)),
+                       "r"(xslot), "r"((uint32_t)(2 * DP))
+                       : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
       }
-      if (GRAD && ntiles > 0) {
+      if (GRAD && P.ntiles > 0) {
         tc_fence_before();
         mbar_arrive(bar(B_TFREE));  // T read: GEMM 2 of the next item may overwrite it
       }
-      // K (and S) partial of the item: a_i (s_i + [self] a_i), fixed order
-      if (h == 1) {
-        red_s[r] = s64;
-        red_g[r] = sg64;
-      }
-      role_sync(1, ET);
+      role_sync(1, ET);  // the half-1 sums are in red_s / red_g
       double kv = 0.0, sv = 0.0;
       if (h == 0) {
-        const double sfull = (s64 + red_s[r]) * f2;
-        kv = (double)a * (sfull + (self ? (double)a : 0.0));
-        sv = (double)a * (sg64 + red_g[r]) * f2;
+        const double f2 = (double)P.f2;
+        const double sfull = (P.s64 + red_s[rb * 128 + r]) * f2;
+        if (GRAD && A.need_rows && P.rv) {
+          float *dst = (rows_x ? A.accX : A.accY) + (P.rbase + P.row) * gen_acc_stride(DP);
+          dst[2 * DP + (crossb ? 1 : 0)] = (float)sfull;
+        }
+        // K (and S) partial of the item: a_i (s_i + [self] a_i), fixed order
+        kv = (double)P.a * (sfull + (self ? (double)P.a : 0.0));
+        sv = (double)P.a * (P.sg64 + red_g[rb * 128 + r]) * f2;
       }
       kv = warp_sum(kv);
       sv = warp_sum(sv);
       if (lane == 0 && h == 0) {
-        red_w[q] = kv;
-        red_w[4 + q] = sv;
+        red_w[rb * 8 + q] = kv;
+        red_w[rb * 8 + 4 + q] = sv;
       }
       role_sync(1, ET);
       if (tid == 0) {
-        const double K = red_w[0] + red_w[1] + red_w[2] + red_w[3];
-        const double Sg = red_w[4] + red_w[5] + red_w[6] + red_w[7];
-        A.itemK[it] = o == 3 ? 0.0 : K;
-        A.itemS[it] = o == 3 ? 0.0 : Sg;
+        const double K = red_w[rb * 8 + 0] + red_w[rb * 8 + 1] + red_w[rb * 8 + 2] + red_w[rb * 8 + 3];
+        const double Sg = red_w[rb * 8 + 4] + red_w[rb * 8 + 5] + red_w[rb * 8 + 6] + red_w[rb * 8 + 7];
+        A.itemK[P.it] = o == 3 ? 0.0 : K;
+        A.itemS[P.it] = o == 3 ? 0.0 : Sg;
       }
-      role_sync(1, ET);  // red_* are rewritten by the next item
+    };
+    // all 256 threads: wait for GEMM 2 of the item's last tile, agree, write
+    auto finish = [&](const Out &P, int rb) {
+      bool w = ok;
+      if (ok && GRAD && P.ntiles > 0) {
+        w = __all_sync(kFull, ws_wait(bar(B_G2 + (int)(P.tlast % NS)), (P.tlast / NS) & 1u,
+                                      abortf, A.spin_limit));
+        if (!w) fail();
+      }
+      if (role_sync_or(1, ET, !w)) ok = false;
+      tc_fence_after();
+      if (ok) outputs(P, rb);
+    };
+
+    uint32_t t = 0;  // column tiles seen (all items)
+    int k = 0;       // items seen
+    ItemX cur;
+    float ca = 0.f, cxsq = 0.f;
+    bool pending = false;
+    Out prev;
+    int prev_rb = 0;
+    if (ifirst < n_items) {
+      cur = A.ix[ifirst];
+      stage_rows(cur, ca, cxsq);
+      if (cur.ntiles > 0) commit_rows();
     }
+    // Every warp runs the same sequence of named barriers whatever happens:
+    // after a failed wait a warp skips the work but not the barriers, and
+    // the agreements (bar.red.or) make `ok` uniform before any barrier that
+    // only some paths would reach.
+    for (int64_t it = ifirst; it < n_items; it += istep, ++k) {
+      const bool has_next = it + istep < n_items;
+      ItemX nxt;
+      float na = 0.f, nxsq = 0.f;
+      if (has_next) nxt = A.ix[it + istep];  // used after this item's first tile
+      bool staged = false;
+      const bool self = (cur.flags & kIxSelf) != 0, fold = (cur.flags & kIxFold) != 0;
+      const int64_t row0 = (int64_t)cur.tile * 128;
+      const int64_t row = row0 + r;
+      const bool rv = row < cur.rcnt;
+      const float a = ca, xsq = cxsq;
+      const int ntiles = cur.ntiles;
+      const float cS = cur.cS;
+      const float nxf = -xsq + cur.lwsc;  // - |x'|^2 - f
+      double s64 = 0.0, sg64 = 0.0;
+      for (int jt = 0; jt < ntiles; ++jt, ++t) {
+        const int ss = (int)(t % NS), ys = (int)(t % NST);
+        if (ok) {
+          // each warp waits for itself (warp-uniform outcome); a failed wait
+          // records the abort at once, so the other warps' waits end too
+          const bool w_ok = ws_wait(bar(B_YFULL + ys), (t / NST) & 1u, abortf, A.spin_limit) &&
+                            ws_wait(bar(B_G1 + ss), (t / NS) & 1u, abortf, A.spin_limit);
+          if (!__all_sync(kFull, w_ok)) {
+            fail();
+            ok = false;
+          }
+        }
+        if (ok) {
+          tc_fence_after();
+          const float *cb = reinterpret_cast<const float *>(t16_smem + ys * SB + 2 * TB);
+          const float *ysq = cb + 32 * h, *yq = cb + kT16Cols + 32 * h,
+                      *bw = cb + 2 * kT16Cols + 32 * h;
+          const int64_t j0 = (int64_t)jt * kT16Cols + 32 * h;
+          const int64_t dj = row - j0;
+          const int diag = (self && dj >= 0 && dj < 32) ? (int)dj : -1;
+          // this warp's 32 columns meet the item's diagonal (warp-uniform)
+          const bool dtile = self && j0 < row0 + 128 && row0 < j0 + 32;
+          float S[32];
+          tmem_ld32(tlane + C_S + 64 * ss + 32 * h, S);
+          float st = 0.f, sgt = 0.f;
+          uint32_t ph[16], pl[16];
+          auto tile = [&](auto fold_t, auto diag_t) {
+            constexpr bool FOLD = decltype(fold_t)::value, DG = decltype(diag_t)::value;
+#pragma unroll
+            for (int u2 = 0; u2 < 16; ++u2) {
+              float wv[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int u = 2 * u2 + e;
+                float w, r2 = 0.f;
+                if (FOLD) {
+                  w = ex2(fmaf(S[u], cS, nxf - yq[u]));
+                  if (SIG) r2 = fmaxf(fmaf(-S[u], cS, xsq + ysq[u]), 0.f);
+                } else {
+                  r2 = fmaxf(fmaf(-S[u], cS, xsq + ysq[u]), 0.f);
+                  w = bw[u] * ex2(-r2);
+                }
+                if (DG && u == diag) w = 0.f;
+                st += w;
+                if (SIG) sgt = fmaf(w, r2, sgt);
+                wv[e] = w;
+              }
+              if (GRAD) {
+                const float h0 = __uint_as_float(__float_as_uint(wv[0]) & 0xFFFFE000u);
+                const float h1 = __uint_as_float(__float_as_uint(wv[1]) & 0xFFFFE000u);
+                ph[u2] = pack_f16x2(h0, h1);
+                pl[u2] = pack_f16x2(wv[0] - h0, wv[1] - h1);
+              }
+            }
+          };
+          if (!fold)
+            tile(BoolC<false>{}, BoolC<true>{});
+          else if (dtile)
+            tile(BoolC<true>{}, BoolC<true>{});
+          else
+            tile(BoolC<true>{}, BoolC<false>{});
+          if (GRAD) {
+            tmem_st16(tlane + C_S + 64 * ss + 32 * h, ph);
+            tmem_st16(tlane + C_S + 64 * ss + 32 * h + 16, pl);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          }
+          s64 += (double)st;
+          if (SIG) sg64 += (double)sgt;
+          tc_fence_before();
+          mbar_arrive(bar(B_PFULL + ss));  // P ready, S and the slot values read
+        }
+        if (jt == 0 && pending) {
+          finish(prev, prev_rb);  // the previous item's outputs
+          pending = false;
+        }
+        if (ok && jt == 0 && has_next) {
+          stage_rows(nxt, na, nxsq);  // the next item's rows, in flight during this item
+          staged = true;
+        }
+      }
+      if (ntiles == 0 && pending) {
+        finish(prev, prev_rb);
+        pending = false;
+      }
+      if (ok && has_next && !staged) stage_rows(nxt, na, nxsq);
+      // every GEMM 1 of this item has landed (its S tiles were read): the next
+      // item's rows replace X
+      if (ok && has_next && nxt.ntiles > 0) commit_rows();
+      if (role_sync_or(1, ET, !ok)) ok = false;  // one agreement per item
+      if (!ok) break;
+      prev.it = it;
+      prev.rbase = cur.rbase;
+      prev.row = row;
+      prev.s64 = s64;
+      prev.sg64 = sg64;
+      prev.a = a;
+      prev.tsc = cur.tsc;
+      prev.f2 = cur.f2;
+      prev.tlast = t - 1u;
+      prev.flags = cur.flags;
+      prev.ntiles = ntiles;
+      prev.rv = rv;
+      prev_rb = k & 1;
+      pending = true;
+      cur = nxt;
+      ca = na;
+      cxsq = nxsq;
+    }
+    if (pending) finish(prev, prev_rb);  // every thread: `pending` and the agreements are uniform
+    asm volatile("cp.async.wait_all;" ::: "memory");  // no copy in flight at exit
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   } else if (warp == kT16ProdWarp) {
     // ====================== producer: column tiles ===========================
     uint32_t t = 0;
@@ -423,11 +593,10 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
     for (int s = 0; s < NST; ++s) armed[s] = 0;
     if (lane == 0) {
       for (int64_t it = ifirst; it < n_items && !*abortf; it += istep) {
-        const Item item = A.items[it];
-        const Seg sg = A.seg[item.pair];
-        const bool cols_x = (item.block == 1 || item.block == 3);
-        const int ntiles = item_tiles(item, sg);
-        const int64_t tb0 = (cols_x ? A.tbase_x : A.tbase_y)[item.pair];
+        const ItemX I = A.ix[it];
+        const bool cols_x = (I.flags & kIxColsX) != 0;
+        const int ntiles = I.ntiles;
+        const int64_t tb0 = I.tb_col;
         const uint8_t *hs = cols_x ? A.hx : A.hy, *ls = cols_x ? A.lx : A.ly;
         const float *cs = cols_x ? A.cx : A.cy;
         bool ok = true;
@@ -469,8 +638,8 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
     uint32_t p_t = 0, p_m = 0;
     bool p_first = false;
     auto issue_g2 = [&]() -> bool {
-      const int ss = (int)(p_t & 1u), ys = (int)(p_t % NST);
-      if (!ws_wait(bar(B_PFULL + ss), (p_t >> 1) & 1u, abortf, A.spin_limit)) return false;
+      const int ss = (int)(p_t % NS), ys = (int)(p_t % NST);
+      if (!ws_wait(bar(B_PFULL + ss), (p_t / NS) & 1u, abortf, A.spin_limit)) return false;
       if (GRAD && p_first && p_m > 0 &&
           !ws_wait(bar(B_TFREE), (p_m - 1u) & 1u, abortf, A.spin_limit))
         return false;
@@ -497,28 +666,40 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
       pend = false;
       return true;
     };
-    int k = 0;
-    for (int64_t it = ifirst; it < n_items && ok && !*abortf && !A.no_mma; it += istep, ++k) {
-      const Item item = A.items[it];
-      const Seg sg = A.seg[item.pair];
-      const int ntiles = item_tiles(item, sg);
-      if (ntiles == 0) continue;
-      const int xb = k & 1;
-      if (!ws_wait(bar(B_XFULL + xb), ((uint32_t)k >> 1) & 1u, abortf, A.spin_limit)) {
+    for (int64_t it = ifirst; it < n_items && ok && !*abortf && !A.no_mma; it += istep) {
+      const int ntiles = A.ix[it].ntiles;
+      if (ntiles == 0) {
+        // no GEMM for this item, but the epilogue writes the previous item's
+        // outputs before its own and waits for that item's last GEMM 2
+        if (pend && !issue_g2()) {
+          ok = false;
+          break;
+        }
+        continue;
+      }
+      // X holds this item's rows once the epilogue's m-th commit has landed
+      // (one commit per item with column tiles)
+      if (!ws_wait(bar(B_XFULL), m & 1u, abortf, A.spin_limit)) {
         ok = false;
         break;
       }
       for (int jt = 0; jt < ntiles; ++jt, ++t) {
-        const int ss = (int)(t & 1u), ys = (int)(t % NST);
+        const int ss = (int)(t % NS), ys = (int)(t % NST);
+        // at an item boundary the previous item's last GEMM 2 goes first: the
+        // epilogue waits for it before it reads T, and is the busier role
+        if (jt == 0 && pend && !issue_g2()) {
+          ok = false;
+          break;
+        }
         if (!ws_wait(bar(B_YFULL + ys), (t / NST) & 1u, abortf, A.spin_limit)) {
           ok = false;
           break;
         }
-        // S stage ss is free once the tile two back is fully consumed: its
+        // S stage ss is free once the tile NS back is fully consumed: its
         // GEMM 2 done (gradients) or its epilogue done (K only)
-        if (t >= 2u) {
-          const bool w = GRAD ? ws_wait(bar(B_G2 + ss), ((t >> 1) - 1u) & 1u, abortf, A.spin_limit)
-                              : ws_wait(bar(B_PFULL + ss), ((t >> 1) - 1u) & 1u, abortf,
+        if (t >= (uint32_t)NS) {
+          const bool w = GRAD ? ws_wait(bar(B_G2 + ss), ((t / NS) - 1u) & 1u, abortf, A.spin_limit)
+                              : ws_wait(bar(B_PFULL + ss), ((t / NS) - 1u) & 1u, abortf,
                                         A.spin_limit);
           if (!w) {
             ok = false;
@@ -528,7 +709,7 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
         tc_fence_after();
         {
           const uint32_t yh = smem_u32(t16_smem + ys * SB), yl = yh + TB;
-          const uint32_t xh = tbase + (uint32_t)(xb * DP), xl = xh + DP / 2;
+          const uint32_t xh = tbase, xl = xh + DP / 2;
 #pragma unroll
           for (int kk = 0; kk < DP / 16; ++kk) {
             const uint64_t bh = tc_desc(yh + kk * 2048, 1024, 128);
@@ -556,8 +737,8 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
     if (ok && pend && !*abortf && !issue_g2()) ok = false;
     if (!ok) fail();
     // every MMA issued has landed before TMEM is freed (bounded)
-    if (n_g1 > 0) (void)mbar_wait(bar(B_G1 + (int)(last_g1 & 1u)), (last_g1 >> 1) & 1u);
-    if (n_g2 > 0) (void)mbar_wait(bar(B_G2 + (int)(last_g2 & 1u)), (last_g2 >> 1) & 1u);
+    if (n_g1 > 0) (void)mbar_wait(bar(B_G1 + (int)(last_g1 % NS)), (last_g1 / NS) & 1u);
+    if (n_g2 > 0) (void)mbar_wait(bar(B_G2 + (int)(last_g2 % NS)), (last_g2 / NS) & 1u);
   }
   tc_fence_before();
   __syncthreads();

@@ -1,9 +1,10 @@
 """Failure paths of the tensor-core kernels, exercised without faulting the GPU.
 
-Every wait of the tensor-core kernels (ra_tc.cuh, ra_tcws.cuh) on an mbarrier is
-bounded; when one expires the kernel records a timeout in the workspace's error
-word, stops, frees its tensor memory and returns, and ra_kde_check reports
-RA_ERR_DEVICE_TIMEOUT.  The test hook RA_TEST_NO_MMA makes the kernels issue no
+Every wait of the tensor-core kernel (ra_tc16.cuh) on an mbarrier is bounded;
+when one expires the kernel records a timeout in the workspace's error word,
+its roles stop (the epilogue warps agree on it before any named barrier),
+it waits for the copies it issued, frees its tensor memory and returns, and
+ra_kde_check reports RA_ERR_DEVICE_TIMEOUT.  The test hook RA_TEST_NO_MMA makes the kernels issue no
 MMA at all and bound each wait to 4096 polls: the first wait for a GEMM then
 expires with nothing asynchronous in flight.  Each test checks the status, then
 runs the same problem normally on the same device and compares it with the
@@ -56,8 +57,8 @@ def _forward(lib, xt, yt, pt, P, dim, sigma, hooks, need_grad, dev):
 
 @pytest.mark.parametrize("dim,need_grad", [(32, 0), (32, 1), (128, 0), (128, 1)])
 def test_expired_wait_is_reported_and_the_device_stays_usable(dim, need_grad, cuda_device):
-    """dim 32: the single-role kernel (tilestc_kernel); dim 128: the
-    warp-specialised one (tilestc_ws_kernel)."""
+    """Padded widths 32 and 128 of the same kernel (different TMEM and
+    shared-memory footprints)."""
     from rapidalign_b200 import _lib
     lib = _lib.load()
     dev = cuda_device

@@ -188,3 +188,34 @@ def test_tensor_core_embedding_workload_loss_is_relative(cuda_device):
     assert np.all(rel <= 1e-5), float(rel.max())
     assert_grad(_np(xt.grad), r.grad_x, "grad_x")
     assert_grad(_np(yt.grad), r.grad_y, "grad_y")
+
+
+@pytest.mark.parametrize("d", [32, 128])
+def test_tensor_core_many_items_with_empty_clouds(d, cuda_device):
+    """More items than the persistent grid has CTAs, with empty clouds among
+    them: items whose column cloud is empty (no GEMM at all) fall between
+    items with column tiles in one CTA's sequence.  The kernel writes an
+    item's outputs after the first tile of the next item, so this checks that
+    hand-off across an item without tiles (and every other item's sums)."""
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(90 + d)
+    G = 700
+    sx = rng.integers(1, 200, G)
+    sy = rng.integers(1, 200, G)
+    sx[rng.random(G) < 0.15] = 0
+    sy[rng.random(G) < 0.15] = 0
+    x, y, ptr_x, ptr_y = _embed_batch(rng, list(sx), list(sy), d)
+    dev = cuda_device
+    xt, yt = _cuda(x, dev, True), _cuda(y, dev, True)
+    outs = ra.pyg_kde_mmd_loss(xt, yt, src_ptr=_cuda(ptr_x, dev), tgt_ptr=_cuda(ptr_y, dev),
+                               sigma=1.0, center=False)
+    up = [rng.uniform(0.5, 1.5, G) for _ in range(4)]
+    total = sum((torch.as_tensor(u, device=dev) * o.double()).sum() for u, o in zip(up, outs))
+    total.backward()
+    r = O.pyg_kde_mmd_loss(x, y, ptr_x, ptr_y, sigma=1.0, center=False, upstream=up)
+    assert_k(_np(outs[1]), r.Kxx, "Kxx")
+    assert_k(_np(outs[2]), r.Kyy, "Kyy")
+    assert_k(_np(outs[3]), r.Kxy, "Kxy")
+    assert_loss(_np(outs[0]), r.loss, r.Kxx, r.Kyy, "loss")
+    assert_grad(_np(xt.grad), r.grad_x, "grad_x")
+    assert_grad(_np(yt.grad), r.grad_y, "grad_y")
