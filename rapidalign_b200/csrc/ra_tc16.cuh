@@ -28,22 +28,25 @@
 // operand (N = coordinate, K = point: leading byte offset 128 between point
 // groups, stride byte offset 1024 between coordinate groups).
 //
-// Roles (320 threads, one CTA per SM, persistent over the items):
+// Roles (352 threads, one CTA per SM, persistent over the items):
 //   warps 0-7  epilogue.  Warp w reads TMEM lanes 32 (w % 4) .. +31 (row =
 //              lane) and columns [32 (w / 4), +32) of each S tile.  Per item
-//              it first writes the NEXT item's rows (hi/lo) into the other X
-//              buffer, then turns each S tile into P, and at the end of the
-//              item reads T and writes the per-point records.
+//              it turns each S tile into P; after the item's first tile it
+//              writes the previous item's outputs (T into the per-point
+//              records, the item's K) and starts copying the next item's rows,
+//              which replace X once this item's last GEMM 1 has landed.
 //   warp 8     lane 0 copies column tiles into a 4-stage shared-memory ring
 //              (cp.async.bulk, no multicast, this GPU's memory only).
-//   warp 9     lane 0 issues the MMAs: GEMM 1 of tile t into S stage t % 2,
-//              then GEMM 2 of tile t - 1, so the tensor core has GEMM 1 of
-//              the next tile while the epilogue works on the current one (at
-//              an item boundary the previous item's last GEMM 2 goes first).
-// TMEM columns: X buffers [0, DP) and [DP, 2DP) (hi in the first half, lo in
-// the second, two fp16 per column), T [2DP, 3DP), S/P stages [3DP, 3DP+64)
-// and [3DP+64, 3DP+128).  P (hi then lo, 16 columns each per 32-point half)
-// overwrites the S columns its thread has already read.
+//   warp 9     lane 0 issues GEMM 1 of each tile into S stage t % 3 as soon
+//              as its column tile has landed and the stage is free.
+//   warp 10    lane 0 issues GEMM 2 of each tile as soon as its P is ready.
+//              Two issuers, because tcgen05.mma issue is synchronous and a
+//              barrier wait is slow: one issuer's waits are covered by the
+//              other's MMAs.
+// TMEM columns: X [0, DP) (hi in the first half, lo in the second, two fp16
+// per column), T [DP, 2DP), three S/P stages of 64 columns from 2DP.  P (hi
+// then lo, 16 columns each per 32-point half) overwrites the S columns its
+// thread has already read.
 //
 // Every wait is bounded and gives up when another role has aborted; on expiry
 // the kernel records kErrTimeout, drains what it issued, frees its TMEM and
@@ -59,8 +62,9 @@ constexpr int kT16Cols = 64;     // points per column tile
 constexpr int kT16Stages = 4;    // column tiles in shared memory
 constexpr int kT16EpiWarps = 8;
 constexpr int kT16ProdWarp = 8;
-constexpr int kT16MmaWarp = 9;
-constexpr int kT16Threads = 320;
+constexpr int kT16MmaWarp = 9;    // GEMM 1 issuer
+constexpr int kT16Mma2Warp = 10;  // GEMM 2 issuer
+constexpr int kT16Threads = 352;
 constexpr int kT16SlotFloats = 3 * kT16Cols;  // per tile: |x'|^2, |x'|^2 - log2 a, a 2^-f
 
 __host__ __device__ constexpr int t16_tile_bytes(int DP) { return DP * 128; }  // hi or lo
@@ -626,57 +630,19 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
       for (int s = 0; s < NST; ++s)
         if (armed[s] > 0) (void)mbar_wait(bar(B_YFULL + s), (armed[s] - 1u) & 1u);
     }
-  } else if (lane == 0) {
-    // ============================ MMA issuer =================================
-    uint32_t t = 0;           // column tiles (all items)
-    uint32_t m = 0;           // items with column tiles
-    uint32_t n_g1 = 0, n_g2 = 0;
-    uint32_t last_g1 = 0, last_g2 = 0;
+  } else if (warp == kT16MmaWarp && lane == 0) {
+    // ======================= GEMM 1 issuer ==================================
+    // tcgen05.mma issue is synchronous (the tensor core queues only a few
+    // instructions) and a barrier wait costs ~150 cycles even when it is
+    // already satisfied, so each GEMM has its own issuing warp: one issuer's
+    // waits are covered by the other's MMAs.  Ordering between the two goes
+    // through the barriers: GEMM 1 of tile t waits for GEMM 2 of tile t - 3
+    // (its S stage), GEMM 2 of tile t for the epilogue's P of tile t.
+    uint32_t t = 0, m = 0, n_g1 = 0, last_g1 = 0;
     bool ok = true;
-    // pending GEMM 2: the previous tile's
-    bool pend = false;
-    uint32_t p_t = 0, p_m = 0;
-    bool p_first = false;
-    auto issue_g2 = [&]() -> bool {
-      const int ss = (int)(p_t % NS), ys = (int)(p_t % NST);
-      if (!ws_wait(bar(B_PFULL + ss), (p_t / NS) & 1u, abortf, A.spin_limit)) return false;
-      if (GRAD && p_first && p_m > 0 &&
-          !ws_wait(bar(B_TFREE), (p_m - 1u) & 1u, abortf, A.spin_limit))
-        return false;
-      tc_fence_after();
-      if (GRAD) {
-        const uint32_t yh = smem_u32(t16_smem + ys * SB), yl = yh + TB;
-#pragma unroll
-        for (int kk = 0; kk < kT16Cols / 16; ++kk) {
-          const uint32_t pa = tbase + C_S + 64 * ss + 32 * (kk >> 1) + 8 * (kk & 1);
-          const uint64_t bh = tc_desc(yh + kk * 256, 128, 1024);
-          const uint64_t bl = tc_desc(yl + kk * 256, 128, 1024);
-          t16_mma(tbase + C_T, pa, bh, IDESC2, (p_first && kk == 0) ? 0u : 1u);
-          t16_mma(tbase + C_T, pa, bl, IDESC2, 1u);
-          t16_mma(tbase + C_T, pa + 16, bh, IDESC2, 1u);
-        }
-        tc_commit(bar(B_G2 + ss));
-        tc_commit(bar(B_YFREE + ys));
-        ++n_g2;
-        last_g2 = p_t;
-      } else {
-        // K only: the stage's slot values were read by the epilogue
-        mbar_arrive(bar(B_YFREE + ys));
-      }
-      pend = false;
-      return true;
-    };
     for (int64_t it = ifirst; it < n_items && ok && !*abortf && !A.no_mma; it += istep) {
       const int ntiles = A.ix[it].ntiles;
-      if (ntiles == 0) {
-        // no GEMM for this item, but the epilogue writes the previous item's
-        // outputs before its own and waits for that item's last GEMM 2
-        if (pend && !issue_g2()) {
-          ok = false;
-          break;
-        }
-        continue;
-      }
+      if (ntiles == 0) continue;
       // X holds this item's rows once the epilogue's m-th commit has landed
       // (one commit per item with column tiles)
       if (!ws_wait(bar(B_XFULL), m & 1u, abortf, A.spin_limit)) {
@@ -685,12 +651,6 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
       }
       for (int jt = 0; jt < ntiles; ++jt, ++t) {
         const int ss = (int)(t % NS), ys = (int)(t % NST);
-        // at an item boundary the previous item's last GEMM 2 goes first: the
-        // epilogue waits for it before it reads T, and is the busier role
-        if (jt == 0 && pend && !issue_g2()) {
-          ok = false;
-          break;
-        }
         if (!ws_wait(bar(B_YFULL + ys), (t / NST) & 1u, abortf, A.spin_limit)) {
           ok = false;
           break;
@@ -707,37 +667,69 @@ __global__ void __launch_bounds__(kT16Threads, 1) tilestc16_kernel(Tc16Args A) {
           }
         }
         tc_fence_after();
-        {
-          const uint32_t yh = smem_u32(t16_smem + ys * SB), yl = yh + TB;
-          const uint32_t xh = tbase, xl = xh + DP / 2;
+        const uint32_t yh = smem_u32(t16_smem + ys * SB), yl = yh + TB;
+        const uint32_t xh = tbase, xl = xh + DP / 2;
+        const uint32_t d = tbase + C_S + 64 * ss;
 #pragma unroll
-          for (int kk = 0; kk < DP / 16; ++kk) {
-            const uint64_t bh = tc_desc(yh + kk * 2048, 1024, 128);
-            const uint64_t bl = tc_desc(yl + kk * 2048, 1024, 128);
-            const uint32_t d = tbase + C_S + 64 * ss;
-            t16_mma(d, xh + 8 * kk, bh, IDESC1, kk > 0 ? 1u : 0u);
-            t16_mma(d, xh + 8 * kk, bl, IDESC1, 1u);
-            t16_mma(d, xl + 8 * kk, bh, IDESC1, 1u);
-          }
-          tc_commit(bar(B_G1 + ss));
-          ++n_g1;
-          last_g1 = t;
+        for (int kk = 0; kk < DP / 16; ++kk) {
+          const uint64_t bh = tc_desc(yh + kk * 2048, 1024, 128);
+          const uint64_t bl = tc_desc(yl + kk * 2048, 1024, 128);
+          t16_mma(d, xh + 8 * kk, bh, IDESC1, kk > 0 ? 1u : 0u);
+          t16_mma(d, xh + 8 * kk, bl, IDESC1, 1u);
+          t16_mma(d, xl + 8 * kk, bh, IDESC1, 1u);
         }
-        if (pend && !issue_g2()) {
-          ok = false;
-          break;
-        }
-        pend = true;
-        p_t = t;
-        p_m = m;
-        p_first = jt == 0;
+        tc_commit(bar(B_G1 + ss));
+        ++n_g1;
+        last_g1 = t;
       }
       ++m;
     }
-    if (ok && pend && !*abortf && !issue_g2()) ok = false;
     if (!ok) fail();
-    // every MMA issued has landed before TMEM is freed (bounded)
+    // every MMA this thread issued has landed before TMEM is freed (bounded)
     if (n_g1 > 0) (void)mbar_wait(bar(B_G1 + (int)(last_g1 % NS)), (last_g1 / NS) & 1u);
+  } else if (warp == kT16Mma2Warp && lane == 0) {
+    // ======================= GEMM 2 issuer ==================================
+    uint32_t t = 0, m = 0, n_g2 = 0, last_g2 = 0;
+    bool ok = true;
+    for (int64_t it = ifirst; it < n_items && ok && !*abortf && !A.no_mma; it += istep) {
+      const int ntiles = A.ix[it].ntiles;
+      if (ntiles == 0) continue;
+      for (int jt = 0; jt < ntiles; ++jt, ++t) {
+        const int ss = (int)(t % NS), ys = (int)(t % NST);
+        if (!ws_wait(bar(B_PFULL + ss), (t / NS) & 1u, abortf, A.spin_limit)) {
+          ok = false;
+          break;
+        }
+        // the item's first GEMM 2 overwrites T: the previous item's T read
+        if (GRAD && jt == 0 && m > 0 &&
+            !ws_wait(bar(B_TFREE), (m - 1u) & 1u, abortf, A.spin_limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (GRAD) {
+          const uint32_t yh = smem_u32(t16_smem + ys * SB), yl = yh + TB;
+#pragma unroll
+          for (int kk = 0; kk < kT16Cols / 16; ++kk) {
+            const uint32_t pa = tbase + C_S + 64 * ss + 32 * (kk >> 1) + 8 * (kk & 1);
+            const uint64_t bh = tc_desc(yh + kk * 256, 128, 1024);
+            const uint64_t bl = tc_desc(yl + kk * 256, 128, 1024);
+            t16_mma(tbase + C_T, pa, bh, IDESC2, (jt == 0 && kk == 0) ? 0u : 1u);
+            t16_mma(tbase + C_T, pa, bl, IDESC2, 1u);
+            t16_mma(tbase + C_T, pa + 16, bh, IDESC2, 1u);
+          }
+          tc_commit(bar(B_G2 + ss));
+          tc_commit(bar(B_YFREE + ys));
+          ++n_g2;
+          last_g2 = t;
+        } else {
+          // K only: the stage's slot values were read by the epilogue
+          mbar_arrive(bar(B_YFREE + ys));
+        }
+      }
+      ++m;
+    }
+    if (!ok) fail();
     if (n_g2 > 0) (void)mbar_wait(bar(B_G2 + (int)(last_g2 % NS)), (last_g2 / NS) & 1u);
   }
   tc_fence_before();
