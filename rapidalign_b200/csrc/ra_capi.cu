@@ -508,12 +508,18 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
     else
       stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
     meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
-    if (L.tc16 && L.DP == 32)
-      packtc_kernel<32><<<cgrid, 256, 0, st>>>(pa);
+    if (L.tc16 && v4 && L.DP == 32)
+      packtc_kernel<32, true><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.tc16 && v4 && L.DP == 64)
+      packtc_kernel<64, true><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.tc16 && v4 && L.DP == 128)
+      packtc_kernel<128, true><<<cgrid, 256, 0, st>>>(pa);
+    else if (L.tc16 && L.DP == 32)
+      packtc_kernel<32, false><<<cgrid, 256, 0, st>>>(pa);
     else if (L.tc16 && L.DP == 64)
-      packtc_kernel<64><<<cgrid, 256, 0, st>>>(pa);
+      packtc_kernel<64, false><<<cgrid, 256, 0, st>>>(pa);
     else if (L.tc16 && L.DP == 128)
-      packtc_kernel<128><<<cgrid, 256, 0, st>>>(pa);
+      packtc_kernel<128, false><<<cgrid, 256, 0, st>>>(pa);
     else if (v4 && L.DP == 32)
       packgw_kernel<32><<<cgrid, 256, 0, st>>>(pa);
     else if (v4 && L.DP == 64)
@@ -787,7 +793,11 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.grad_sigma = gr->grad_sigma;
   ea.totals = d->center || (gr->grad_wx != nullptr && d->weights_x != RA_WEIGHTS_UNIFORM) ||
               (gr->grad_wy != nullptr && d->weights_y != RA_WEIGHTS_UNIFORM);
-  ea.vec4 = d->dim % 4 == 0 && aligned16(gr->grad_x) && aligned16(gr->grad_y);
+  // tensor-core layout: no fp32 copy of the packed coordinates; the backward
+  // packs them again from the points
+  ea.xraw = L.tc16 ? 1 : 0;
+  ea.vec4 = d->dim % 4 == 0 && aligned16(gr->grad_x) && aligned16(gr->grad_y) &&
+            (!ea.xraw || (aligned16(in->x) && aligned16(in->y)));
   const unsigned cgrid = chunk_grid(L);
   if (L.packed3) {
     // small pairs: one CTA per pair (both passes); large pairs: chunked passes

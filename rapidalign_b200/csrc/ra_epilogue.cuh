@@ -148,8 +148,25 @@ struct EpilogueArgs {
   double *grad_wx, *grad_wy;
   double *grad_sigma;
   int totals;  // the side totals R, Q are used (centering, or a weight gradient)
-  int vec4;    // D % 4 == 0 and grad_x, grad_y 16-byte aligned: float4 stores
+  int vec4;    // D % 4 == 0, grad_x, grad_y (and x, y when xraw) 16-byte aligned
+  int xraw;    // no Gx / Gy (tensor-core layout): x' = c (x - anchor) from the points
 };
+
+// The packed coordinate x'_d of point g: stored (Gx / Gy), or recomputed from
+// the caller's points exactly as the packing pass computes it (same fp64
+// difference, same fp32 rounding), for layouts that store only fp16 tiles.
+__device__ __forceinline__ float packed_coord(const EpilogueArgs &A, int side, int64_t g, int d,
+                                              const double *anc, float sc) {
+  if (!A.xraw) return (side == 0 ? A.Gx : A.Gy)[g * A.DP + d];
+  if (d >= A.D) return 0.f;
+  return sc * (float)((double)(side == 0 ? A.x : A.y)[g * A.D + d] - anc[d]);
+}
+__device__ __forceinline__ const double *side_anchor(const EpilogueArgs &A, int64_t p, int side) {
+  return A.meta + p * meta_stride(A.DP) + 4 + (2 + side) * A.DP;
+}
+__device__ __forceinline__ float side_scale(const EpilogueArgs &A, int64_t p) {
+  return A.sigma_p != nullptr ? scale_of_sigma(A.sigma_p[p]) : (float)A.scale;
+}
 
 // One point's record (self (s, G0..G2), cross (s, G0..G2), 32-byte aligned)
 // and packed weight, loaded ahead of point_grads.
@@ -516,10 +533,9 @@ __global__ void __launch_bounds__(NT) epig_write_kernel(EpilogueArgs A) {
 // the 8 warps in order (deterministic), the dot products x . R by warp
 // shuffles -- no barrier per point.
 __device__ __forceinline__ double genw_gxt(const EpilogueArgs &A, const float *acc, double a,
-                                           double s_self, double s_cross, const float *gp,
+                                           double s_self, double s_cross, double xp,
                                            int d, const EpiSide &E) {
   const int DP = A.DP;
-  const double xp = gp[d];
   const double Gs = xp * s_self - (double)acc[d];
   const double Gc = xp * s_cross - (double)acc[DP + d];
   return -a * E.k_x * (E.cs * Gs + E.cc * Gc);
@@ -535,8 +551,9 @@ __global__ void __launch_bounds__(256) epigw_partial_kernel(EpilogueArgs A) {
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
     const EpiSide E = epi_side(A, p, side);
     const float *accb = side == 0 ? A.accX : A.accY;
-    const float *Gp = side == 0 ? A.Gx : A.Gy;
     const float *Ap = side == 0 ? A.Ax : A.Ay;
+    const double *anc = side_anchor(A, p, side);
+    const float scl = side_scale(A, p);
     const int64_t b = c * kChunk, e = b + kChunk < E.count ? b + kChunk : E.count;
     double R[KL], Q = 0.0;
 #pragma unroll
@@ -558,7 +575,7 @@ __global__ void __launch_bounds__(256) epigw_partial_kernel(EpilogueArgs A) {
         const int d = lane + 32 * k;
         q.ts[k] = d < D ? acc[d] : 0.f;
         q.tc[k] = d < D ? acc[DP + d] : 0.f;
-        q.xp[k] = d < D ? Gp[g * DP + d] : 0.f;
+        q.xp[k] = d < D ? packed_coord(A, side, g, d, anc, scl) : 0.f;
       }
       return q;
     };
@@ -632,6 +649,8 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
     const float *accb = side == 0 ? A.accX : A.accY;
     const float *Gp = side == 0 ? A.Gx : A.Gy;
     const float *Ap = side == 0 ? A.Ax : A.Ay;
+    const double *anc = side_anchor(A, p, side);
+    const float scl = side_scale(A, p);
     const int64_t b = c * kChunk, e = b + kChunk < E.span ? b + kChunk : E.span;
 
     // weight gradients: a warp per point, 4 points in flight, x . R by shuffles
@@ -679,6 +698,10 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
       constexpr int NC = DP / 4;
       const int ncd = D / 4;  // chunks that hold coordinates
       const int cc = tid % NC;
+      // this thread's anchors (its coordinate chunk is fixed)
+      const bool cl = A.xraw && cc < ncd;
+      const double an0 = cl ? anc[4 * cc] : 0.0, an1 = cl ? anc[4 * cc + 1] : 0.0;
+      const double an2 = cl ? anc[4 * cc + 2] : 0.0, an3 = cl ? anc[4 * cc + 3] : 0.0;
       const int64_t nel = (e - b) * NC;
       constexpr int kAhead = 2;  // 4 doubles the registers (126 -> 156) for nothing
       for (int64_t k0 = tid; k0 < nel; k0 += kAhead * 256) {
@@ -698,7 +721,14 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
             scv[u] = acc[2 * DP + 1];
             ts[u] = *reinterpret_cast<const float4 *>(acc + 4 * cc);
             tc[u] = *reinterpret_cast<const float4 *>(acc + DP + 4 * cc);
-            xp[u] = *reinterpret_cast<const float4 *>(Gp + g * DP + 4 * cc);
+            if (A.xraw) {
+              // the points themselves (16-byte aligned: vec4), packed here
+              const float4 r = *reinterpret_cast<const float4 *>(pts + g * D + 4 * cc);
+              xp[u] = make_float4(scl * (float)((double)r.x - an0), scl * (float)((double)r.y - an1),
+                                  scl * (float)((double)r.z - an2), scl * (float)((double)r.w - an3));
+            } else {
+              xp[u] = *reinterpret_cast<const float4 *>(Gp + g * DP + 4 * cc);
+            }
           }
         }
 #pragma unroll
@@ -742,7 +772,8 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
             if (i < E.count) {
               const float *acc = accb + g * A.acc_stride;
               const double a = Ap[g];
-              gx = genw_gxt(A, acc, a, acc[2 * DP], acc[2 * DP + 1], Gp + g * DP, dd, E);
+              gx = genw_gxt(A, acc, a, acc[2 * DP], acc[2 * DP + 1],
+                            (double)packed_coord(A, side, g, dd, anc, scl), dd, E);
               if (A.center) gx -= a * Rsh[dd];
             }
             gout[g * D + dd] = (float)gx;

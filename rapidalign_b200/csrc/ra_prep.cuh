@@ -496,16 +496,16 @@ __global__ void __launch_bounds__(256) statsw_kernel(PrepArgs A) {
 // Pass 1 for wide points whose coordinates load as float4 (D % 4 == 0,
 // 16-byte aligned bases): LPP lanes share a point (one float4 chunk or two
 // each), a warp covers PPW points per step and keeps kU steps of loads in
-// flight, so a CTA has ~16 KB of reads outstanding.  Partials are combined
+// flight, so a CTA has 16-32 KB of reads outstanding.  Partials are combined
 // over the PPW point slots of a warp by shuffles, then over the 8 warps in
 // order: a fixed summation order, independent of scheduling.
 template <int DP>
-__global__ void __launch_bounds__(256) statsw4_kernel(PrepArgs A) {
+__global__ void __launch_bounds__(256, 2) statsw4_kernel(PrepArgs A) {
   constexpr int NW = 8, NC = DP / 4;
   constexpr int LPP = NC < 32 ? NC : 32;  // lanes per point
   constexpr int CPL = NC / LPP;           // float4 chunks per lane
   constexpr int PPW = 32 / LPP;           // points per warp step
-  constexpr int kU = 4;                   // warp steps in flight
+  constexpr int kU = CPL == 1 ? 8 : 4;    // warp steps in flight
   static_assert(NC % LPP == 0 && 32 % LPP == 0, "chunk split");
   __shared__ double sh[NW][2 * DP + 2];
   __shared__ long long shl[NW];
@@ -904,23 +904,21 @@ __global__ void __launch_bounds__(256, 4) packgw_kernel(PrepArgs A) {
   });
 }
 
-// Tensor-core layout (ra_tc16.cuh), on top of what packgw_kernel writes (Gx,
-// Ax, read by the backward epilogue): per 64-point tile, the fp16 hi and lo
+// Tensor-core layout (ra_tc16.cuh): per 64-point tile, the fp16 hi and lo
 // halves of x' 2^e in the canonical core-matrix layout (byte offset of point
-// j, coordinate d: (d/8)*1024 + (j/8)*128 + (j%8)*16 + (d%8)*2), and per slot
-// |x'|^2, |x'|^2 - log2 a (+inf for a <= 0) and a 2^-f.  Masked points and the
-// padding slots up to the tile boundary are zero points of zero weight.  One
-// thread per (point, 8 coordinates); |x'|^2 is summed over the point's
-// threads in a fixed order.
-template <int DP>
+// j, coordinate d: (d/8)*1024 + (j/8)*128 + (j%8)*16 + (d%8)*2), per slot
+// |x'|^2, |x'|^2 - log2 a (+inf for a <= 0) and a 2^-f, and the normalised
+// weights Ax / Ay.  No fp32 copy of x' (the backward packs it again from the
+// points).  Masked points and the padding slots up to the tile boundary are
+// zero points of zero weight.  One thread per point, walking its coordinate
+// groups: a warp's stores of one group are 32 consecutive 16-byte chunks.
+// V4: float4 loads of the points (D % 4 == 0, 16-byte aligned bases).
+template <int DP, bool V4>
 __global__ void __launch_bounds__(256) packtc_kernel(PrepArgs A) {
-  constexpr int NG = DP / 8;      // threads per point
-  constexpr int PPC = 256 / NG;   // points per CTA step
-  constexpr int TB = DP * 128;    // bytes of a hi (or lo) tile
-  static_assert(NG >= 4 && NG <= 32 && (NG & (NG - 1)) == 0, "point groups");
+  constexpr int NG = DP / 8;     // coordinate groups per point
+  constexpr int TB = DP * 128;   // bytes of a hi (or lo) tile
   const ChunkMap M{A.P, A.choff, A.chx};
-  const int D = A.D, g = threadIdx.x % NG, pl = threadIdx.x / NG;
-  const unsigned gmask = (NG == 32 ? 0xffffffffu : ((1u << NG) - 1u)) << ((threadIdx.x & 31) & ~(NG - 1));
+  const int D = A.D;
   for_each_chunk(M, [&](int64_t p, int side, int64_t ch, int64_t, int64_t, int64_t) {
     const Seg sg = A.seg[p];
     const int64_t s = side == 0 ? sg.xs : sg.ys;
@@ -929,7 +927,6 @@ __global__ void __launch_bounds__(256) packtc_kernel(PrepArgs A) {
     const float *w = side == 0 ? A.w_x : A.w_y;
     const uint8_t *mask = side == 0 ? A.mask_x : A.mask_y;
     const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
-    float *Gp = side == 0 ? A.Gx : A.Gy;
     float *Ap = side == 0 ? A.Ax : A.Ay;
     uint8_t *hp = side == 0 ? A.hx : A.hy;
     uint8_t *lp = side == 0 ? A.lx : A.ly;
@@ -941,57 +938,56 @@ __global__ void __launch_bounds__(256) packtc_kernel(PrepArgs A) {
     const float sc = pair_scale(A.scale, A.sigma_p, p);
     const float cs = (float)meta[meta_tc_cscale(DP) + side];
     const float wsc = (float)meta[meta_tc_wscale(DP) + side];
-    double ag[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) ag[u] = 8 * g + u < D ? anc[8 * g + u] : 0.0;
     const int64_t b = ch * kChunk;
     const int64_t cend = ceil_div(count, (int64_t)kTile) * kTile;  // through the last tile
     const int64_t e = b + kChunk < cend ? b + kChunk : cend;
-    for (int64_t i = b + pl; i < e; i += PPC) {
+    for (int64_t i = b + threadIdx.x; i < e; i += 256) {
       const int64_t gi = s + i;
       const bool real = i < count;
       const bool valid = real && (mask == nullptr || mask[gi] != 0);
-      float xv[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int d = 8 * g + u;
-        xv[u] = (real && d < D) ? sc * (float)((double)pts[gi * D + d] - ag[u]) : 0.f;
-      }
-      if (real) {
-        float4 *gp = reinterpret_cast<float4 *>(Gp + gi * DP + 8 * g);
-        gp[0] = make_float4(xv[0], xv[1], xv[2], xv[3]);
-        gp[1] = make_float4(xv[4], xv[5], xv[6], xv[7]);
-      }
-      uint32_t hh[4], ll[4];
+      const int64_t tile = tb + i / kTile;
+      const int j = (int)(i % kTile);
+      uint8_t *ht = hp + (size_t)tile * TB + (size_t)((j >> 3) * 128 + (j & 7) * 16);
+      uint8_t *lt = lp + (size_t)tile * TB + (size_t)((j >> 3) * 128 + (j & 7) * 16);
       float sq = 0.f;
+#pragma unroll 4
+      for (int g = 0; g < NG; ++g) {
+        float xv[8];
+        if (V4 && valid && 8 * g + 8 <= D) {
+          const float4 r0 = *reinterpret_cast<const float4 *>(pts + gi * D + 8 * g);
+          const float4 r1 = *reinterpret_cast<const float4 *>(pts + gi * D + 8 * g + 4);
+          const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float v0 = valid ? xv[2 * c] * cs : 0.f, v1 = valid ? xv[2 * c + 1] * cs : 0.f;
-        const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-        const __half l0 = __float2half_rn(v0 - __half2float(h0));
-        const __half l1 = __float2half_rn(v1 - __half2float(h1));
-        hh[c] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-        ll[c] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-        if (valid) {
+          for (int u = 0; u < 8; ++u)
+            xv[u] = sc * (float)((double)rv[u] - anc[8 * g + u]);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int d = 8 * g + u;
+            xv[u] = (valid && d < D) ? sc * (float)((double)pts[gi * D + d] - anc[d]) : 0.f;
+          }
+        }
+        uint32_t hh[4], ll[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float v0 = xv[2 * c] * cs, v1 = xv[2 * c + 1] * cs;
+          const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+          const __half l0 = __float2half_rn(v0 - __half2float(h0));
+          const __half l1 = __float2half_rn(v1 - __half2float(h1));
+          hh[c] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+          ll[c] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
           sq = fmaf(xv[2 * c], xv[2 * c], sq);
           sq = fmaf(xv[2 * c + 1], xv[2 * c + 1], sq);
         }
+        *reinterpret_cast<uint4 *>(ht + g * 1024) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+        *reinterpret_cast<uint4 *>(lt + g * 1024) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
       }
-      const int64_t tile = tb + i / kTile;
-      const int j = (int)(i % kTile);
-      const size_t off = (size_t)tile * TB + (size_t)(g * 1024 + (j >> 3) * 128 + (j & 7) * 16);
-      *reinterpret_cast<uint4 *>(hp + off) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
-      *reinterpret_cast<uint4 *>(lp + off) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
-#pragma unroll
-      for (int o = 1; o < NG; o <<= 1) sq += __shfl_xor_sync(gmask, sq, o);
-      if (g == 0) {
-        const float a = real ? (float)((double)eff_weight(w, mask, wmode, gi) / Wn) : 0.f;
-        if (real) Ap[gi] = a;
-        float *cv = cp + tile * (3 * kTile);
-        cv[j] = sq;
-        cv[kTile + j] = a > 0.f ? sq - log2f(a) : INFINITY;
-        cv[2 * kTile + j] = a * wsc;
-      }
+      const float a = real ? (float)((double)eff_weight(w, mask, wmode, gi) / Wn) : 0.f;
+      if (real) Ap[gi] = a;
+      float *cv = cp + tile * (3 * kTile);
+      cv[j] = sq;
+      cv[kTile + j] = a > 0.f ? sq - log2f(a) : INFINITY;
+      cv[2 * kTile + j] = a * wsc;
     }
   });
 }
