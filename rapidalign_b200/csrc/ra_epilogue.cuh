@@ -153,16 +153,18 @@ struct EpilogueArgs {
 };
 
 // The packed coordinate x'_d of point g: stored (Gx / Gy), or recomputed from
-// the caller's points exactly as the packing pass computes it (same fp64
-// difference, same fp32 rounding), for layouts that store only fp16 tiles.
+// the caller's points exactly as the tensor-core packing pass computes it
+// (x' = c ((x - hi) - lo) in fp32 from the anchor's fp32 pair), for the
+// layout that stores only fp16 tiles.
 __device__ __forceinline__ float packed_coord(const EpilogueArgs &A, int side, int64_t g, int d,
-                                              const double *anc, float sc) {
+                                              const float *anc, float sc) {
   if (!A.xraw) return (side == 0 ? A.Gx : A.Gy)[g * A.DP + d];
   if (d >= A.D) return 0.f;
-  return sc * (float)((double)(side == 0 ? A.x : A.y)[g * A.D + d] - anc[d]);
+  return sc * (((side == 0 ? A.x : A.y)[g * A.D + d] - anc[d]) - anc[A.DP + d]);
 }
-__device__ __forceinline__ const double *side_anchor(const EpilogueArgs &A, int64_t p, int side) {
-  return A.meta + p * meta_stride(A.DP) + 4 + (2 + side) * A.DP;
+// the anchor pairs (hi [DP], then lo [DP]) of a side, tensor-core layout
+__device__ __forceinline__ const float *side_anchor(const EpilogueArgs &A, int64_t p, int side) {
+  return tc_anchor(A.meta + p * meta_stride(A.DP), A.DP, side);
 }
 __device__ __forceinline__ float side_scale(const EpilogueArgs &A, int64_t p) {
   return A.sigma_p != nullptr ? scale_of_sigma(A.sigma_p[p]) : (float)A.scale;
@@ -552,7 +554,7 @@ __global__ void __launch_bounds__(256) epigw_partial_kernel(EpilogueArgs A) {
     const EpiSide E = epi_side(A, p, side);
     const float *accb = side == 0 ? A.accX : A.accY;
     const float *Ap = side == 0 ? A.Ax : A.Ay;
-    const double *anc = side_anchor(A, p, side);
+    const float *anc = side_anchor(A, p, side);
     const float scl = side_scale(A, p);
     const int64_t b = c * kChunk, e = b + kChunk < E.count ? b + kChunk : E.count;
     double R[KL], Q = 0.0;
@@ -649,7 +651,7 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
     const float *accb = side == 0 ? A.accX : A.accY;
     const float *Gp = side == 0 ? A.Gx : A.Gy;
     const float *Ap = side == 0 ? A.Ax : A.Ay;
-    const double *anc = side_anchor(A, p, side);
+    const float *anc = side_anchor(A, p, side);
     const float scl = side_scale(A, p);
     const int64_t b = c * kChunk, e = b + kChunk < E.span ? b + kChunk : E.span;
 
@@ -698,10 +700,12 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
       constexpr int NC = DP / 4;
       const int ncd = D / 4;  // chunks that hold coordinates
       const int cc = tid % NC;
-      // this thread's anchors (its coordinate chunk is fixed)
+      // this thread's anchor pairs (its coordinate chunk is fixed)
       const bool cl = A.xraw && cc < ncd;
-      const double an0 = cl ? anc[4 * cc] : 0.0, an1 = cl ? anc[4 * cc + 1] : 0.0;
-      const double an2 = cl ? anc[4 * cc + 2] : 0.0, an3 = cl ? anc[4 * cc + 3] : 0.0;
+      const float ah0 = cl ? anc[4 * cc] : 0.f, ah1 = cl ? anc[4 * cc + 1] : 0.f;
+      const float ah2 = cl ? anc[4 * cc + 2] : 0.f, ah3 = cl ? anc[4 * cc + 3] : 0.f;
+      const float al0 = cl ? anc[DP + 4 * cc] : 0.f, al1 = cl ? anc[DP + 4 * cc + 1] : 0.f;
+      const float al2 = cl ? anc[DP + 4 * cc + 2] : 0.f, al3 = cl ? anc[DP + 4 * cc + 3] : 0.f;
       const int64_t nel = (e - b) * NC;
       constexpr int kAhead = 2;  // 4 doubles the registers (126 -> 156) for nothing
       for (int64_t k0 = tid; k0 < nel; k0 += kAhead * 256) {
@@ -724,8 +728,8 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
             if (A.xraw) {
               // the points themselves (16-byte aligned: vec4), packed here
               const float4 r = *reinterpret_cast<const float4 *>(pts + g * D + 4 * cc);
-              xp[u] = make_float4(scl * (float)((double)r.x - an0), scl * (float)((double)r.y - an1),
-                                  scl * (float)((double)r.z - an2), scl * (float)((double)r.w - an3));
+              xp[u] = make_float4(scl * ((r.x - ah0) - al0), scl * ((r.y - ah1) - al1),
+                                  scl * ((r.z - ah2) - al2), scl * ((r.w - ah3) - al3));
             } else {
               xp[u] = *reinterpret_cast<const float4 *>(Gp + g * DP + 4 * cc);
             }

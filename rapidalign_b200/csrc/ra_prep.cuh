@@ -45,12 +45,20 @@ namespace ra {
 //                    in (1/2, 1])
 //   [12+4DP + side]  tensor-core layout: 1 when the side's weights are all
 //                    >= 0 (folded into the exponent as columns), else 0
-__host__ __device__ __forceinline__ int meta_stride(int DP) { return 14 + 4 * DP; }
+//   [14+4DP, 14+6DP) tensor-core layout: the anchors as fp32 pairs (hi, lo
+//                    with hi + lo = anchor to ~48 bits), floats [side][2][DP]:
+//                    x' = c ((x - hi) - lo) in fp32 without fp64 conversions
+__host__ __device__ __forceinline__ int meta_stride(int DP) { return 14 + 6 * DP; }
 __host__ __device__ __forceinline__ int meta_wscale(int DP) { return 4 + 4 * DP; }
 __host__ __device__ __forceinline__ int meta_fold(int DP) { return 6 + 4 * DP; }
 __host__ __device__ __forceinline__ int meta_tc_cscale(int DP) { return 8 + 4 * DP; }
 __host__ __device__ __forceinline__ int meta_tc_wscale(int DP) { return 10 + 4 * DP; }
 __host__ __device__ __forceinline__ int meta_tc_fold(int DP) { return 12 + 4 * DP; }
+__host__ __device__ __forceinline__ int meta_tc_anchor(int DP) { return 14 + 4 * DP; }
+// x' = c ((x - hi) - lo) from a side's fp32 anchor pairs (tensor-core layout)
+__device__ __forceinline__ const float *tc_anchor(const double *meta, int DP, int side) {
+  return reinterpret_cast<const float *>(meta + meta_tc_anchor(DP)) + side * 2 * DP;
+}
 
 // Partial-sum record of one chunk (fp64): [0] sum of effective weights,
 // [1] valid points, [2] last valid index (-1: none), [3, 3+DP) sum w' p,
@@ -792,9 +800,16 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
     // |x'| <= c (max |x| + max |anchor|); 2^e keeps that bound <= 2^15
     __syncwarp();
     double am[2] = {0.0, 0.0};
+    float *af = reinterpret_cast<float *>(meta + meta_tc_anchor(DP));
     for (int dd = lane; dd < DP; dd += 32) {
       am[0] = fmax(am[0], fabs(meta[4 + 2 * DP + dd]));
       am[1] = fmax(am[1], fabs(meta[4 + 3 * DP + dd]));
+      for (int sd = 0; sd < 2; ++sd) {
+        const double an = meta[4 + (2 + sd) * DP + dd];
+        const float hi = (float)an;
+        af[sd * 2 * DP + dd] = hi;
+        af[sd * 2 * DP + DP + dd] = (float)(an - (double)hi);
+      }
     }
     am[0] = warp_fmax(am[0]);
     am[1] = warp_fmax(am[1]);
@@ -913,6 +928,25 @@ __global__ void __launch_bounds__(256, 4) packgw_kernel(PrepArgs A) {
 // zero points of zero weight.  One thread per point, walking its coordinate
 // groups: a warp's stores of one group are 32 consecutive 16-byte chunks.
 // V4: float4 loads of the points (D % 4 == 0, 16-byte aligned bases).
+// fp16 high half of v: v with its low 13 mantissa bits cleared, exactly an
+// fp16 number when |v| is in fp16's normal range; 0 below it (|v| < 2^-14:
+// the low half then carries all of v).  |v| <= 2^15 by the scale choice.
+__device__ __forceinline__ float tc_hi16(float v) {
+  return fabsf(v) >= 6.103515625e-05f ? __uint_as_float(__float_as_uint(v) & 0xFFFFE000u) : 0.f;
+}
+// the fp16 bits of a value tc_hi16 returned (sign, exponent - 112, mantissa)
+__device__ __forceinline__ uint32_t tc_f16_bits(float h) {
+  const uint32_t b = __float_as_uint(h);
+  if ((b & 0x7FFFFFFFu) == 0u) return (b >> 16) & 0x8000u;
+  return ((b >> 16) & 0x8000u) | ((((b >> 13) & 0x3FFFFu) - (112u << 10)) & 0x7FFFu);
+}
+// two floats rounded to fp16, lo in bits 0-15
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 template <int DP, bool V4>
 __global__ void __launch_bounds__(256) packtc_kernel(PrepArgs A) {
   constexpr int NG = DP / 8;     // coordinate groups per point
@@ -934,7 +968,7 @@ __global__ void __launch_bounds__(256) packtc_kernel(PrepArgs A) {
     const int64_t tb = (side == 0 ? A.tbase_x : A.tbase_y)[p];
     const double *meta = A.meta + p * meta_stride(DP);
     const double Wn = meta[side];
-    const double *anc = meta + 4 + (2 + side) * DP;
+    const float *ahi = tc_anchor(meta, DP, side), *alo = ahi + DP;
     const float sc = pair_scale(A.scale, A.sigma_p, p);
     const float cs = (float)meta[meta_tc_cscale(DP) + side];
     const float wsc = (float)meta[meta_tc_wscale(DP) + side];
@@ -958,24 +992,25 @@ __global__ void __launch_bounds__(256) packtc_kernel(PrepArgs A) {
           const float4 r1 = *reinterpret_cast<const float4 *>(pts + gi * D + 8 * g + 4);
           const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            xv[u] = sc * (float)((double)rv[u] - anc[8 * g + u]);
+          for (int u = 0; u < 8; ++u) xv[u] = sc * ((rv[u] - ahi[8 * g + u]) - alo[8 * g + u]);
         } else {
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const int d = 8 * g + u;
-            xv[u] = (valid && d < D) ? sc * (float)((double)pts[gi * D + d] - anc[d]) : 0.f;
+            xv[u] = (valid && d < D) ? sc * ((pts[gi * D + d] - ahi[d]) - alo[d]) : 0.f;
           }
         }
         uint32_t hh[4], ll[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const float v0 = xv[2 * c] * cs, v1 = xv[2 * c + 1] * cs;
-          const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-          const __half l0 = __float2half_rn(v0 - __half2float(h0));
-          const __half l1 = __float2half_rn(v1 - __half2float(h1));
-          hh[c] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-          ll[c] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+          float hv[2], lv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            hv[e] = tc_hi16(xv[2 * c + e] * cs);
+            lv[e] = xv[2 * c + e] * cs - hv[e];
+          }
+          hh[c] = tc_f16_bits(hv[0]) | (tc_f16_bits(hv[1]) << 16);
+          ll[c] = pack_half2(lv[0], lv[1]);
           sq = fmaf(xv[2 * c], xv[2 * c], sq);
           sq = fmaf(xv[2 * c + 1], xv[2 * c + 1], sq);
         }
