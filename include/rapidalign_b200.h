@@ -228,6 +228,24 @@ RA_API int ra_kde_check(const void *workspace, ra_stream_t stream);
  * read it without synchronising the stream. */
 RA_API int ra_kde_status_of_error_word(int word);
 
+/* ---- the loss and the outputs in one launch -----------------------------
+ * From the P-pair sums K = (Kxx | Kyy | Kxy) (float64 [3P]) write the
+ * per-pair loss and the three sums in the caller's dtype: out_f64 = 1 for
+ * float64 outputs, 0 for float32.  The loss is Kxx + Kyy - 2 Kxy, or with
+ * cosine = 1, 1 - Kxy / sqrt(max(Kxx Kyy, eps)) (rapidalign/kde.py:103-107,
+ * 265-268, 368-371), evaluated in float64 in the order the reference
+ * writes it.  Replaces the reference's tensor expressions after
+ * _cuda.kde_mmd_forward* (kde.py:265-274, 368-377). */
+RA_API int ra_mmd_outputs(const double *K, int64_t P, int cosine, double eps, int out_f64,
+                          void *loss, void *Kxx, void *Kyy, void *Kxy, ra_stream_t stream);
+/* Its derivative: coef (float64 [3P]) = dL/dK from the gradients of the four
+ * outputs (each nullable = zero; float32 or float64 as out_f64 says), for
+ * ra_kde_backward. */
+RA_API int ra_mmd_outputs_backward(const double *K, int64_t P, int cosine, double eps,
+                                   int out_f64, const void *g_loss, const void *g_Kxx,
+                                   const void *g_Kyy, const void *g_Kxy, double *coef,
+                                   ra_stream_t stream);
+
 /* ---- legacy operator set: one entry point per op of csrc/bindings.cpp ---- */
 
 /*

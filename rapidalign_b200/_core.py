@@ -376,9 +376,78 @@ class KDESums(torch.autograd.Function):
                 return torch.zeros(P, dtype=torch.float64, device=device)
             return g.to(torch.float64)
 
-        coef = torch.cat([g_or_zero(gKxx), g_or_zero(gKyy), g_or_zero(gKxy)])
+        coef = _adjacent(gKxx, gKyy, gKxy, P)
+        if coef is None:
+            coef = torch.cat([g_or_zero(gKxx), g_or_zero(gKyy), g_or_zero(gKxy)])
         grads = backward_sums(state, coef, ctx.needs_input_grad[:5])
         return grads + (None, None, None)
+
+
+def _adjacent(a: Optional[Tensor], b: Optional[Tensor], c: Optional[Tensor],
+              P: int) -> Optional[Tensor]:
+    """The float64 [3P] buffer whose thirds a, b, c are, when they are (no copy
+    needed), else None."""
+    if a is None or b is None or c is None or P == 0:
+        return None
+    for t in (a, b, c):
+        if t.dtype != torch.float64 or not t.is_contiguous() or t.numel() != P:
+            return None
+    if (a.untyped_storage().data_ptr() != b.untyped_storage().data_ptr() or
+            a.untyped_storage().data_ptr() != c.untyped_storage().data_ptr()):
+        return None
+    if b.data_ptr() != a.data_ptr() + 8 * P or c.data_ptr() != a.data_ptr() + 16 * P:
+        return None
+    return a.as_strided((3 * P,), (1,), a.storage_offset())
+
+
+class MMDOutputs(torch.autograd.Function):
+    """(Kxx, Kyy, Kxy) float64 (P,) -> (loss, Kxx, Kyy, Kxy) as float32 or
+    float64, in one launch (ra_mmd_outputs); the backward writes dL/dK for
+    KDESums in one launch (ra_mmd_outputs_backward).  The loss is that of
+    rapidalign/kde.py:103-107 (or the cosine form), in float64."""
+
+    @staticmethod
+    def forward(ctx, Kxx: Tensor, Kyy: Tensor, Kxy: Tensor, cosine: bool, eps: float,
+                f64: bool):
+        lib = _lib.load()
+        P = Kxx.numel()
+        K = _adjacent(Kxx, Kyy, Kxy, P)
+        if K is None:
+            K = torch.cat([Kxx.reshape(-1), Kyy.reshape(-1), Kxy.reshape(-1)]).to(torch.float64)
+        odt = torch.float64 if f64 else torch.float32
+        outs = [torch.empty(P, dtype=odt, device=K.device) for _ in range(4)]
+        with torch.cuda.device(K.device):
+            rc = lib.ra_mmd_outputs(K.data_ptr() if P else None, P, int(bool(cosine)),
+                                    float(eps), int(f64), *[_lib.ptr(o) for o in outs],
+                                    _lib.stream_handle(K.device))
+        _lib.check(rc, "mmd outputs")
+        ctx.save_for_backward(K)
+        ctx.cosine, ctx.eps, ctx.f64, ctx.odt = bool(cosine), float(eps), bool(f64), odt
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, gl, ga, gb, gc):
+        lib = _lib.load()
+        K, = ctx.saved_tensors
+        P = K.numel() // 3
+        gs = [None if g is None else g.to(ctx.odt).contiguous() for g in (gl, ga, gb, gc)]
+        coef = torch.empty(3 * P, dtype=torch.float64, device=K.device)
+        with torch.cuda.device(K.device):
+            rc = lib.ra_mmd_outputs_backward(K.data_ptr() if P else None, P, int(ctx.cosine),
+                                             ctx.eps, int(ctx.f64), *[_lib.ptr(g) for g in gs],
+                                             _lib.ptr(coef), _lib.stream_handle(K.device))
+        _lib.check(rc, "mmd outputs backward")
+        return coef[:P], coef[P:2 * P], coef[2 * P:], None, None, None
+
+
+def mmd_outputs(Kxx: Tensor, Kyy: Tensor, Kxy: Tensor, cosine: bool, eps: float,
+                dtype: torch.dtype) -> Tuple[Tensor, Tensor, Tensor, Tensor]:
+    """(loss, Kxx, Kyy, Kxy) in `dtype` from the float64 sums (one launch for
+    float32 or float64 outputs; other dtypes are rounded once from float64)."""
+    if dtype in (torch.float32, torch.float64):
+        return MMDOutputs.apply(Kxx, Kyy, Kxy, cosine, eps, dtype == torch.float64)
+    outs = MMDOutputs.apply(Kxx, Kyy, Kxy, cosine, eps, True)
+    return tuple(o.to(dtype) for o in outs)
 
 
 def kde_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tensor],

@@ -920,6 +920,53 @@ int status_of_error_word(int err) {
 
 }  // namespace
 
+// Loss and outputs of the P pairs from the float64 sums, and its derivative
+// (ra_mmd_outputs, ra_mmd_outputs_backward).
+namespace {
+template <typename T>
+__global__ void mmd_outputs_kernel(const double *K, int64_t P, int cosine, double eps, T *loss,
+                                   T *kxx, T *kyy, T *kxy) {
+  const int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (p >= P) return;
+  const double a = K[p], b = K[P + p], c = K[2 * P + p];
+  const double l = cosine ? 1.0 - c / sqrt(fmax(a * b, eps)) : a + b - 2.0 * c;
+  loss[p] = (T)l;
+  kxx[p] = (T)a;
+  kyy[p] = (T)b;
+  kxy[p] = (T)c;
+}
+template <typename T>
+__device__ __forceinline__ double grad_at(const void *g, int64_t p) {
+  return g == nullptr ? 0.0 : (double)static_cast<const T *>(g)[p];
+}
+template <typename T>
+__global__ void mmd_outputs_backward_kernel(const double *K, int64_t P, int cosine, double eps,
+                                            const void *gl, const void *ga, const void *gb,
+                                            const void *gc, double *coef) {
+  const int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (p >= P) return;
+  const double gL = grad_at<T>(gl, p);
+  double da, db, dc;  // dL/dKxx, dL/dKyy, dL/dKxy
+  if (cosine) {
+    const double a = K[p], b = K[P + p], c = K[2 * P + p];
+    const double ab = a * b;
+    const double s = sqrt(fmax(ab, eps));
+    dc = -1.0 / s;
+    // clamp_min passes its gradient where the product is not below eps
+    const double ds = ab >= eps ? c / (2.0 * s * s * s) : 0.0;
+    da = ds * b;
+    db = ds * a;
+  } else {
+    da = 1.0;
+    db = 1.0;
+    dc = -2.0;
+  }
+  coef[p] = grad_at<T>(ga, p) + gL * da;
+  coef[P + p] = grad_at<T>(gb, p) + gL * db;
+  coef[2 * P + p] = grad_at<T>(gc, p) + gL * dc;
+}
+}  // namespace
+
 extern "C" {
 
 const char *ra_status_string(int status) {
@@ -1038,6 +1085,42 @@ int ra_kde_check(const void *workspace, ra_stream_t stream) {
 }
 
 int ra_kde_status_of_error_word(int word) { return status_of_error_word(word); }
+
+int ra_mmd_outputs(const double *K, int64_t P, int cosine, double eps, int out_f64, void *loss,
+                   void *Kxx, void *Kyy, void *Kxy, ra_stream_t stream) {
+  if (P < 0 || (P > 0 && (K == nullptr || loss == nullptr || Kxx == nullptr || Kyy == nullptr ||
+                          Kxy == nullptr)))
+    return RA_ERR_INVALID_ARGUMENT;
+  if (P == 0) return RA_OK;
+  const unsigned grid = (unsigned)ceil_div(P, (int64_t)256);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (out_f64)
+    mmd_outputs_kernel<double><<<grid, 256, 0, st>>>(K, P, cosine, eps, (double *)loss,
+                                                      (double *)Kxx, (double *)Kyy,
+                                                      (double *)Kxy);
+  else
+    mmd_outputs_kernel<float><<<grid, 256, 0, st>>>(K, P, cosine, eps, (float *)loss,
+                                                     (float *)Kxx, (float *)Kyy, (float *)Kxy);
+  ++g_launches;
+  return cuda_status(cudaGetLastError());
+}
+
+int ra_mmd_outputs_backward(const double *K, int64_t P, int cosine, double eps, int out_f64,
+                            const void *g_loss, const void *g_Kxx, const void *g_Kyy,
+                            const void *g_Kxy, double *coef, ra_stream_t stream) {
+  if (P < 0 || (P > 0 && (K == nullptr || coef == nullptr))) return RA_ERR_INVALID_ARGUMENT;
+  if (P == 0) return RA_OK;
+  const unsigned grid = (unsigned)ceil_div(P, (int64_t)256);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (out_f64)
+    mmd_outputs_backward_kernel<double><<<grid, 256, 0, st>>>(K, P, cosine, eps, g_loss, g_Kxx,
+                                                               g_Kyy, g_Kxy, coef);
+  else
+    mmd_outputs_backward_kernel<float><<<grid, 256, 0, st>>>(K, P, cosine, eps, g_loss, g_Kxx,
+                                                              g_Kyy, g_Kxy, coef);
+  ++g_launches;
+  return cuda_status(cudaGetLastError());
+}
 
 size_t ra_kde_mmd_forward_workspace_bytes(int64_t B, int64_t Nx, int64_t Ny, int32_t D) {
   ra_kde_desc d = legacy_desc(RA_LAYOUT_DENSE, B, B * Nx, B * Ny, Nx, Ny, D, 1.0, 0);

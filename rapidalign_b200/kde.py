@@ -23,7 +23,7 @@ from typing import Optional, Tuple
 import torch
 
 from . import _lib
-from ._core import GraphCountMismatch, Spec, kde_sums
+from ._core import GraphCountMismatch, Spec, kde_sums, mmd_outputs
 
 Tensor = torch.Tensor
 
@@ -91,8 +91,8 @@ def kde_mmd_loss(
         check_errors=(x_w is not None or y_w is not None),
         weight_error_message="weights must sum to a positive value")
     Kxx, Kyy, Kxy = kde_sums(x, y, x_w, y_w, sig_t, spec)
-    loss = _loss_from_k(Kxx, Kyy, Kxy, cosine, eps)
-    return (loss[0].to(dtype), Kxx[0].to(dtype), Kyy[0].to(dtype), Kxy[0].to(dtype))
+    loss, Kxx, Kyy, Kxy = mmd_outputs(Kxx, Kyy, Kxy, cosine, eps, dtype)
+    return loss[0], Kxx[0], Kyy[0], Kxy[0]
 
 
 def kde_mmd_loss_bands(
@@ -148,8 +148,7 @@ def kde_mmd_loss_bands(
     ywr = None if y_w is None else y_w.reshape(1, M).expand(S, M)
     sig_t = sig.to(device) if isinstance(sigmas, Tensor) and sigmas.requires_grad else None
     Kxx, Kyy, Kxy = kde_sums(xr, yr, xwr, ywr, sig_t, spec)
-    loss = _loss_from_k(Kxx, Kyy, Kxy, cosine, eps)
-    return loss.to(dtype), Kxx.to(dtype), Kyy.to(dtype), Kxy.to(dtype)
+    return mmd_outputs(Kxx, Kyy, Kxy, cosine, eps, dtype)
 
 
 def kde_mmd_loss_dense(
@@ -200,8 +199,7 @@ def kde_mmd_loss_dense(
     xw = None if x_w is None else x_w.to(device)
     yw = None if y_w is None else y_w.to(device)
     Kxx, Kyy, Kxy = kde_sums(x, y, xw, yw, sig_t, spec)
-    loss = _loss_from_k(Kxx, Kyy, Kxy, cosine, eps)
-    return loss.to(dtype), Kxx.to(dtype), Kyy.to(dtype), Kxy.to(dtype)
+    return mmd_outputs(Kxx, Kyy, Kxy, cosine, eps, dtype)
 
 
 def _read_back(values: Tensor) -> list:
@@ -408,8 +406,7 @@ def _pyg_segments(src_pos, tgt_pos, src_ptr_t, tgt_ptr_t, num_pairs, user_ptr, b
     xw = None if src_w is None else src_w.to(device).reshape(-1)
     yw = None if tgt_w is None else tgt_w.to(device).reshape(-1)
     Kxx, Kyy, Kxy = kde_sums(src_pos, tgt_pos, xw, yw, sig_t, spec)
-    loss = _loss_from_k(Kxx, Kyy, Kxy, cosine, eps)
-    return loss.to(dtype), Kxx.to(dtype), Kyy.to(dtype), Kxy.to(dtype)
+    return mmd_outputs(Kxx, Kyy, Kxy, cosine, eps, dtype)
 
 
 def pyg_batch_kde_mmd_loss(src, tgt, *, pos: str = "pos", weight: Optional[str] = None,

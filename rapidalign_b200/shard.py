@@ -195,7 +195,8 @@ def split_pair_kde_mmd_loss(x: torch.Tensor, y: torch.Tensor, x_w=None, y_w=None
     import torch.distributed as dist
     from . import _lib
     from ._core import Spec, kde_sums
-    from .kde import _loss_from_k, _sigma_value
+    from ._core import mmd_outputs
+    from .kde import _sigma_value
     if x.ndim != 2 or y.ndim != 2 or x.size(-1) != y.size(-1):
         raise ValueError("x and y must be (N,d) and (M,d) with same d")
     if (isinstance(sigma, torch.Tensor) and bool((sigma <= 0).any())) or \
@@ -217,6 +218,5 @@ def split_pair_kde_mmd_loss(x: torch.Tensor, y: torch.Tensor, x_w=None, y_w=None
     Kxx, Kyy, Kxy = kde_sums(x, y, x_w, y_w, sig_t, spec,
                              reduce=(lambda f64, f32: packed_all_reduce(f64, f32, group))
                              if world > 1 else None)
-    loss = _loss_from_k(Kxx, Kyy, Kxy, cosine, eps)
-    dtype = x.dtype
-    return loss[0].to(dtype), Kxx[0].to(dtype), Kyy[0].to(dtype), Kxy[0].to(dtype)
+    loss, Kxx, Kyy, Kxy = mmd_outputs(Kxx, Kyy, Kxy, cosine, eps, x.dtype)
+    return loss[0], Kxx[0], Kyy[0], Kxy[0]
