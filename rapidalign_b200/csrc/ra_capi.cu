@@ -57,6 +57,7 @@ struct Layout {
   size_t tiles_x, tiles_y, Gx, Gy, Ax, Ay, accX, accY;
   size_t hx, hy, lx, ly, cx, cy;  // tc16: fp16 hi / lo tiles and slot values
   size_t ix;                      // tc16: one ItemX record per work item
+  size_t order, cost, hist;       // packed3: the tile kernel's item order (ra_plan.cuh)
   size_t acc_x_bytes, acc_y_bytes;
   size_t total;
 };
@@ -165,6 +166,9 @@ Layout make_layout(const ra_kde_desc *d) {
   L.rec = take(sizeof(double) * (size_t)L.max_chunks * stats_stride(L.DP));
   const size_t nx = (size_t)(NX > 0 ? NX : 1), ny = (size_t)(NY > 0 ? NY : 1);
   if (L.packed3) {
+    L.order = take(sizeof(int32_t) * (size_t)L.max_items);
+    L.cost = take((size_t)L.max_items);
+    L.hist = take(sizeof(int32_t) * 2 * kCostBuckets);
     L.tiles_x = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_x);
     L.tiles_y = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_y);
     L.Ax = take(sizeof(float) * kTile * (size_t)L.max_tiles_x);  // a~ per slot
@@ -545,10 +549,20 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
   pl.n_items = at<int64_t>(ws, L.hdr + kHdrNItems);
   pl.items = at<Item>(ws, L.items);
   pl.max_items = L.max_items;
-  plan_count_kernel<<<(unsigned)ceil_div(P, 256), 256, 0, st>>>(pl);
+  pl.order = L.packed3 ? at<int32_t>(ws, L.order) : nullptr;
+  pl.cost = L.packed3 ? at<uint8_t>(ws, L.cost) : nullptr;
+  pl.hist = L.packed3 ? at<int32_t>(ws, L.hist) : nullptr;
+  pl.cursor = L.packed3 ? pl.hist + kCostBuckets : nullptr;
+  plan_count_kernel<<<(unsigned)ceil_div(P > kCostBuckets ? P : kCostBuckets, 256), 256, 0, st>>>(pl);
   plan_scan_kernel<<<1, 1024, 0, st>>>(pl);
   plan_emit_kernel<<<(unsigned)P, 256, 0, st>>>(pl);
   g_launches += 3;
+  if (L.packed3) {
+    const unsigned og = (unsigned)(L.max_items < 256 * 592 ? ceil_div(L.max_items, (int64_t)256)
+                                                           : 592);
+    plan_order_kernel<<<og, 256, 0, st>>>(pl);
+    ++g_launches;
+  }
   if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
 
   // ---- the tensor-core path's per-item records (the plan is complete) ----
@@ -624,6 +638,9 @@ int compute_impl(const ra_kde_desc *d, const ra_kde_inputs *in, double *Kxx, dou
     T.itemS = at<double>(ws, L.itemS);
     T.shard_index = sh_idx;
     T.shard_count = sh_cnt;
+    // largest items first; a split evaluation keeps the plan order, which
+    // every shard derives alike (the sorted order within a cost is not)
+    T.order = sharded ? nullptr : at<int32_t>(ws, L.order);
     rc = launch_tiles3(mode, rows_only(d), T, st);
     if (rc) return rc;
   } else {

@@ -104,6 +104,7 @@ struct Tiles3Args {
   float *acc_x, *acc_y;                 // [tiles * 64][8]: self (s, G0..G2), cross (s, G0..G2)
   double *itemK, *itemS;
   int shard_index, shard_count;  // this process evaluates items shard_index + k * shard_count
+  const int32_t *order;          // ticket k takes item order[k] (null: item k)
 };
 
 // MODE 0: K only.  MODE 1: K + per-point sums.  MODE 2: also S (sigma grad).
@@ -255,8 +256,9 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     unsigned ticket = 0;
     if (lane == 0) ticket = atomicAdd(A.ticket, 1u);
     ticket = __shfl_sync(kFull, ticket, 0);
-    const int64_t it = A.shard_index + (int64_t)ticket * A.shard_count;
-    if (it >= total) break;
+    const int64_t k = A.shard_index + (int64_t)ticket * A.shard_count;
+    if (k >= total) break;
+    const int64_t it = A.order != nullptr ? A.order[k] : k;  // largest items first
     const Item item = A.items[it];
     const Seg sg = A.seg[item.pair];
     const int blk = item.block;
