@@ -163,6 +163,11 @@ class ClockSampler:
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        # nvidia-smi's start-up (NVML initialisation) can hold the driver for
+        # a moment: let it pass before anything is timed
+        t0 = time.monotonic()
+        while not self.lines and time.monotonic() - t0 < 10.0 and self.proc.poll() is None:
+            time.sleep(0.02)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -742,6 +747,7 @@ def run_ours(args):
             },
             "per_rank": {
                 "ms_per_step": [r[0] / K * 1e3 for r in per_rank],
+                "e2e_ms_per_step": [r[1] / K * 1e3 for r in per_rank],
                 "tile_kernel_ms": [r[2] * 1e3 for r in per_rank],
                 "tile_kernel_ms_min": min(r[2] for r in per_rank) * 1e3,
                 "tile_kernel_ms_max": max(r[2] for r in per_rank) * 1e3,

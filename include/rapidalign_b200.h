@@ -228,6 +228,14 @@ RA_API int ra_kde_check(const void *workspace, ra_stream_t stream);
  * read it without synchronising the stream. */
 RA_API int ra_kde_status_of_error_word(int word);
 
+/* Enqueues on `stream` the copy of the workspace's error word into host[0]
+ * and, when nflags > 0, of the int32 flags[0..nflags) (ra_ptr_from_batch)
+ * into host[1..nflags]; `host` should be page-locked for the copies to stay
+ * asynchronous.  For a status read on a side stream that waits for the
+ * preparation (an event) while the tile kernels run. */
+RA_API int ra_kde_error_word_async(const void *workspace, const int32_t *flags, int32_t nflags,
+                                   int32_t *host, ra_stream_t stream);
+
 /* ---- the loss and the outputs in one launch -----------------------------
  * From the P-pair sums K = (Kxx | Kyy | Kxy) (float64 [3P]) write the
  * per-pair loss and the three sums in the caller's dtype: out_f64 = 1 for

@@ -138,41 +138,62 @@ def uses_tensor_cores(spec: Spec) -> bool:
 _READ_STREAMS: dict = {}
 
 
-def _read_stream(device) -> torch.cuda.Stream:
-    """A side stream per device for small device-to-host reads: a read
-    enqueued there waits for its data (an event), but the kernels enqueued
-    after it on the compute stream do not wait for the read -- which may
-    queue behind a large host-to-device copy on the copy engines."""
+def _read_stream(device):
+    """A side stream per device for small device-to-host reads, with its raw
+    handle: a read enqueued there waits for its data (an event), but the
+    kernels enqueued after it on the compute stream do not wait for the read
+    -- which may queue behind a large host-to-device copy on the copy
+    engines."""
     s = _READ_STREAMS.get(device.index)
     if s is None:
-        s = _READ_STREAMS[device.index] = torch.cuda.Stream(device)
+        st = torch.cuda.Stream(device)
+        s = _READ_STREAMS[device.index] = (st, st.cuda_stream)
     return s
+
+
+_PINNED_WORDS: list = []  # page-locked int32 [16] buffers of finished reads
+_WORDS_MAX = 16
+
+
+def _mark(stream) -> torch.cuda.Event:
+    """An event at the current end of `stream` (what a later read waits for)."""
+    ev = torch.cuda.Event()
+    ev.record(stream)
+    return ev
 
 
 class _ErrorWord:
     """An asynchronous read of the workspace's error word (and, optionally,
     of batch flags): copied into pinned host memory on a side stream once the
-    compute stream has produced it, and waited for through an event, so the
-    host stops only when it needs the answer while later kernels keep the GPU
-    busy.  The caller keeps `ws` and `flags` alive until read() returns."""
+    compute stream has passed `ready` (an event), and waited for through an
+    event, so the host stops only when it needs the answer while later kernels
+    keep the GPU busy.  Created after the kernels that follow `ready` are
+    enqueued, so they do not wait for the host to set up the read.  The
+    caller keeps `ws` and `flags` alive until read() returns."""
 
-    def __init__(self, ws: Tensor, stream, flags: Optional[Tensor] = None):
-        n = 1 + (0 if flags is None else flags.numel())
-        self.host = torch.empty(n, dtype=torch.int32, pin_memory=True)
-        ready = torch.cuda.Event()
-        ready.record(stream)
-        side = _read_stream(ws.device)
+    def __init__(self, ws: Tensor, ready: torch.cuda.Event, flags: Optional[Tensor] = None):
+        self.n = 1 + (0 if flags is None else flags.numel())
+        if self.n > _WORDS_MAX:
+            raise RuntimeError("too many flags for an error-word read")
+        try:
+            self.host = _PINNED_WORDS.pop()
+        except IndexError:
+            self.host = torch.empty(_WORDS_MAX, dtype=torch.int32, pin_memory=True)
+        side, handle = _read_stream(ws.device)
         side.wait_event(ready)
-        with torch.cuda.stream(side):
-            self.host[:1].copy_(ws[:4].view(torch.int32), non_blocking=True)
-            if flags is not None:
-                self.host[1:].copy_(flags, non_blocking=True)
-            self.event = torch.cuda.Event()
-            self.event.record(side)
+        rc = _lib.load().ra_kde_error_word_async(
+            ws.data_ptr(), None if flags is None else flags.data_ptr(), self.n - 1,
+            self.host.data_ptr(), handle)
+        _lib.check(rc, "error word read")
+        self.event = torch.cuda.Event()
+        self.event.record(side)
 
     def read(self):
         self.event.synchronize()
-        return self.host.tolist()
+        words = self.host[:self.n].tolist()
+        _PINNED_WORDS.append(self.host)  # the copies are done: reusable
+        self.host = None
+        return words
 
 
 def _raise_data_error(code: int, spec: Spec) -> None:
@@ -253,14 +274,15 @@ def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tens
         _lib.check(rc, "kde forward")
         # the data errors are known once the preparation ran: read them while
         # the tile kernels run, instead of stopping the GPU to ask
-        early = None
+        prepared = None
         if spec.check_errors or spec.batch_flags is not None:
-            early = _ErrorWord(ws, tstream, spec.batch_flags)
+            prepared = _mark(tstream)
         rc = lib.ra_kde_forward_compute(ctypes.byref(desc), ctypes.byref(inp), K.data_ptr(),
                                         ws.data_ptr(), ws.numel(), stream)
         _lib.check(rc, "kde forward")
+        early = None if prepared is None else _ErrorWord(ws, prepared, spec.batch_flags)
         if uses_tensor_cores(spec):
-            pending = _ErrorWord(ws, tstream)  # an expired wait shows after the tiles
+            pending = _ErrorWord(ws, _mark(tstream))  # an expired wait shows after the tiles
         if early is not None:
             words = early.read()
             if len(words) > 1:
@@ -423,6 +445,9 @@ class MMDOutputs(torch.autograd.Function):
         _lib.check(rc, "mmd outputs")
         ctx.save_for_backward(K)
         ctx.cosine, ctx.eps, ctx.f64, ctx.odt = bool(cosine), float(eps), bool(f64), odt
+        # an output without a gradient stays None (a null pointer, read as zero)
+        # instead of a zero tensor filled on the device
+        ctx.set_materialize_grads(False)
         return tuple(outs)
 
     @staticmethod

@@ -130,6 +130,8 @@ SIGNATURES = {
                                        _V, ctypes.POINTER(RaKdeGrads), _V, _SZ, _V]),
     "ra_kde_check": (ctypes.c_int, [_V, _V]),
     "ra_kde_status_of_error_word": (ctypes.c_int, [ctypes.c_int]),
+    "ra_kde_error_word_async": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                               ctypes.c_void_p, ctypes.c_void_p]),
     "ra_mmd_outputs": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
                                       ctypes.c_double, ctypes.c_int, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,

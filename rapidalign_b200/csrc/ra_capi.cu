@@ -53,7 +53,7 @@ struct Layout {
   int64_t max_tiles_x, max_tiles_y;  // packed3: bound on the padded tiles
   int64_t max_chunks;                // bound on the virtual chunks (ra_chunks.cuh)
   size_t hdr, seg, meta, cnt, item_off, tbase_x, tbase_y, boff, items, itemK, itemS, Kws, Sws,
-      coef, Ktmp, chcnt, chx, choff, rec;
+      coef, Ktmp, chcnt, chx, choff, rec, cpair;
   size_t tiles_x, tiles_y, Gx, Gy, Ax, Ay, accX, accY;
   size_t hx, hy, lx, ly, cx, cy;  // tc16: fp16 hi / lo tiles and slot values
   size_t ix;                      // tc16: one ItemX record per work item
@@ -62,8 +62,11 @@ struct Layout {
   size_t total;
 };
 
-// header block: int err @0, unsigned ticket @4, int has_state @8, int64 n_items @16
-constexpr size_t kHdrErr = 0, kHdrTicket = 4, kHdrState = 8, kHdrNItems = 16;
+// header block: int err @0, unsigned ticket @4, int has_state @8, int64 n_items @16,
+// unsigned chunk tickets @32 (ra_chunks.cuh): [0] the sums pass, [1] packing,
+// [2] [3] the backward's partial and write passes
+constexpr size_t kHdrErr = 0, kHdrTicket = 4, kHdrState = 8, kHdrNItems = 16,
+                 kHdrChunkTickets = 32;
 constexpr int kItemF64 = 2;  // fp64 partials per work item: K, S
 
 bool desc_ok(const ra_kde_desc *d) {
@@ -164,6 +167,7 @@ Layout make_layout(const ra_kde_desc *d) {
   L.chx = take(sizeof(int64_t) * P1);
   L.choff = take(sizeof(int64_t) * (P1 + 1));
   L.rec = take(sizeof(double) * (size_t)L.max_chunks * stats_stride(L.DP));
+  L.cpair = take(sizeof(int32_t) * (size_t)L.max_chunks);
   const size_t nx = (size_t)(NX > 0 ? NX : 1), ny = (size_t)(NY > 0 ? NY : 1);
   if (L.packed3) {
     L.order = take(sizeof(int32_t) * (size_t)L.max_items);
@@ -421,6 +425,8 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
   pa.chcnt = at<int64_t>(ws, L.chcnt);
   pa.chx = at<int64_t>(ws, L.chx);
   pa.choff = at<int64_t>(ws, L.choff);
+  pa.cpair = at<int32_t>(ws, L.cpair);
+  pa.ticket = at<unsigned>(ws, L.hdr + kHdrChunkTickets);  // the sums pass
   pa.err = at<int>(ws, L.hdr + kHdrErr);
   pa.allow_fold = mode == 2 ? 0 : 1;
   if (!L.packed3) {
@@ -464,6 +470,8 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
     pk.meta = at<double>(ws, L.meta);
     pk.choff = at<int64_t>(ws, L.choff);
     pk.chx = at<int64_t>(ws, L.chx);
+    pk.cpair = at<int32_t>(ws, L.cpair);
+    pk.ticket = at<unsigned>(ws, L.hdr + kHdrChunkTickets) + 1;  // packing
     pk.tbase_x = at<int64_t>(ws, L.tbase_x);
     pk.tbase_y = at<int64_t>(ws, L.tbase_y);
     pk.max_tiles_x = L.max_tiles_x;
@@ -512,6 +520,7 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
     else
       stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
     meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
+    pa.ticket = at<unsigned>(ws, L.hdr + kHdrChunkTickets) + 1;  // packing
     if (L.tc16 && v4 && L.DP == 32)
       packtc_kernel<32, true><<<cgrid, 256, 0, st>>>(pa);
     else if (L.tc16 && v4 && L.DP == 64)
@@ -781,6 +790,13 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.S_ws = at<double>(ws, L.Sws);
   ea.choff = at<int64_t>(ws, L.choff);
   ea.chx = at<int64_t>(ws, L.chx);
+  ea.cpair = at<int32_t>(ws, L.cpair);
+  // the chunked passes' tickets, zeroed here: a backward may run more than
+  // once after its forward
+  unsigned *const etk = at<unsigned>(ws, L.hdr + kHdrChunkTickets) + 2;
+  if ((!L.packed3 || may_have_large_pairs(d)) &&
+      cudaMemsetAsync(etk, 0, 2 * sizeof(unsigned), st) != cudaSuccess)
+    return RA_ERR_CUDA;
   ea.rec = at<double>(ws, L.rec);
   ea.x = in->x;
   ea.y = in->y;
@@ -822,7 +838,9 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
         <<<(unsigned)(P < (int64_t)cgrid ? P : (int64_t)cgrid), kEpiThreads, 0, st>>>(ea);
     ++g_launches;
     if (may_have_large_pairs(d)) {
+      ea.ticket = etk;
       epi3_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+      ea.ticket = etk + 1;
       epi3_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
       g_launches += 2;
     }
@@ -831,25 +849,35 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
     // gradients); an uncentred call without weight gradients skips it
     switch (L.DP) {
       case 32:
+        ea.ticket = etk;
         if (ea.totals) epigw_partial_kernel<32><<<cgrid, 256, 0, st>>>(ea);
+        ea.ticket = etk + 1;
         epigw_write_kernel<32><<<cgrid, 256, 0, st>>>(ea);
         break;
       case 64:
+        ea.ticket = etk;
         if (ea.totals) epigw_partial_kernel<64><<<cgrid, 256, 0, st>>>(ea);
+        ea.ticket = etk + 1;
         epigw_write_kernel<64><<<cgrid, 256, 0, st>>>(ea);
         break;
       case 128:
+        ea.ticket = etk;
         if (ea.totals) epigw_partial_kernel<128><<<cgrid, 256, 0, st>>>(ea);
+        ea.ticket = etk + 1;
         epigw_write_kernel<128><<<cgrid, 256, 0, st>>>(ea);
         break;
       default:
+        ea.ticket = etk;
         if (ea.totals) epigw_partial_kernel<256><<<cgrid, 256, 0, st>>>(ea);
+        ea.ticket = etk + 1;
         epigw_write_kernel<256><<<cgrid, 256, 0, st>>>(ea);
         break;
     }
     g_launches += ea.totals ? 2 : 1;
   } else {
+    ea.ticket = etk;
     epig_partial_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
+    ea.ticket = etk + 1;
     epig_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
     g_launches += 2;
   }
@@ -1102,6 +1130,20 @@ int ra_kde_check(const void *workspace, ra_stream_t stream) {
 }
 
 int ra_kde_status_of_error_word(int word) { return status_of_error_word(word); }
+
+int ra_kde_error_word_async(const void *workspace, const int32_t *flags, int32_t nflags,
+                            int32_t *host, ra_stream_t stream) {
+  if (workspace == nullptr || host == nullptr || nflags < 0 || (nflags > 0 && flags == nullptr))
+    return RA_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemcpyAsync(host, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, st) !=
+      cudaSuccess)
+    return RA_ERR_CUDA;
+  if (nflags > 0 && cudaMemcpyAsync(host + 1, flags, sizeof(int32_t) * (size_t)nflags,
+                                    cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return RA_ERR_CUDA;
+  return RA_OK;
+}
 
 int ra_mmd_outputs(const double *K, int64_t P, int cosine, double eps, int out_f64, void *loss,
                    void *Kxx, void *Kyy, void *Kxy, ra_stream_t stream) {

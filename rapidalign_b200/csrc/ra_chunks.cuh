@@ -8,6 +8,12 @@
 // spreads over many SMs while a batch of small pairs costs one CTA visit per
 // chunk.  Partial sums are stored per virtual chunk and combined per pair in
 // chunk order, which keeps every result independent of scheduling.
+//
+// With a chunk ticket (ChunkMap::ticket, zeroed before the launch) the CTAs
+// instead take chunks one at a time from a shared counter, each chunk's pair
+// read from cpair[v]: chunks differ in size by up to kChunk / 32 (a batch of
+// graphs of 32-1024 points), and a fixed range of them per CTA leaves the
+// slowest CTA with about half again the mean work.
 #pragma once
 
 #include "ra_common.cuh"
@@ -75,6 +81,8 @@ struct ChunkMap {
   int64_t P;
   const int64_t *choff;  // [P + 1], clamped to the workspace bound
   const int64_t *chx;    // [P]: chunks of the x side
+  const int32_t *cpair = nullptr;  // [choff[P]]: the pair of each virtual chunk
+  unsigned *ticket = nullptr;      // chunk counter of this launch (null: fixed ranges)
 };
 
 // Largest p in [0, P) with choff[p] <= v (v < choff[P]).
@@ -95,6 +103,35 @@ __device__ __forceinline__ int64_t chunk_pair(const ChunkMap &M, int64_t v) {
 template <typename F>
 __device__ __forceinline__ void for_each_chunk(const ChunkMap &M, F &&f) {
   const int64_t total = M.choff[M.P];
+  if (M.ticket != nullptr && M.cpair != nullptr) {
+    // one chunk per ticket; thread 0 takes the next ticket while the current
+    // chunk runs, and publishes it in the other of two slots before the
+    // barrier that ends the chunk (a slot is rewritten only two barriers
+    // after it was read)
+    __shared__ unsigned fec_slot[2];
+    if (threadIdx.x == 0) fec_slot[0] = atomicAdd(M.ticket, 1u);
+    __syncthreads();
+    unsigned cur = fec_slot[0];
+    for (int k = 1; (int64_t)cur < total; ++k) {
+      unsigned nxt = 0;
+      if (threadIdx.x == 0) nxt = atomicAdd(M.ticket, 1u);
+      const int64_t v = cur;
+      const int64_t p = M.cpair[v];
+      const int64_t lo = M.choff[p], hi = M.choff[p + 1];
+      int64_t cx = M.chx[p];
+      if (cx > hi - lo) cx = hi - lo;
+      const int64_t local = v - lo;
+      const int side = local < cx ? 0 : 1;
+      const int64_t c = side == 0 ? local : local - cx;
+      const int64_t first = side == 0 ? lo : lo + cx;
+      const int64_t n = side == 0 ? cx : (hi - lo) - cx;
+      f(p, side, c, v, first, n);
+      if (threadIdx.x == 0) fec_slot[k & 1] = nxt;
+      __syncthreads();
+      cur = fec_slot[k & 1];
+    }
+    return;
+  }
   const int64_t per = ceil_div(total, (int64_t)gridDim.x);
   int64_t v = (int64_t)blockIdx.x * per;
   const int64_t v1 = v + per < total ? v + per : total;

@@ -133,6 +133,8 @@ struct EpilogueArgs {
   const double *coef;  // [3P]: dL/dKxx | dL/dKyy | dL/dKxy
   const double *S_ws;  // [3P]
   const int64_t *choff, *chx;  // chunk map (ra_chunks.cuh)
+  const int32_t *cpair;
+  unsigned *ticket;            // chunk counter of the launch, zeroed
   double *rec;         // per-chunk (Q, R[DP]) partials, stride stats_stride(DP)
   const float *x, *y;  // original coordinates
   const uint8_t *mask_x, *mask_y;
@@ -345,7 +347,7 @@ __device__ __forceinline__ double epi3_qt(const EpilogueArgs &A, const EpiSide &
 template <int NT>
 __global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
   __shared__ double sh[(NT / 32) * 4];
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int rs = stats_stride(A.DP);
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
     if (small_pair(A.seg[p])) return;  // epi3_small_kernel
@@ -369,7 +371,7 @@ __global__ void __launch_bounds__(NT) epi3_partial_kernel(EpilogueArgs A) {
 template <int NT>
 __global__ void __launch_bounds__(NT, 3) epi3_write_kernel(EpilogueArgs A) {
   __shared__ double sh[(NT / 32) * 4];
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int rs = stats_stride(A.DP);
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t first, int64_t n) {
     if (small_pair(A.seg[p])) return;  // epi3_small_kernel
@@ -436,7 +438,7 @@ template <int NT>
 __global__ void __launch_bounds__(NT) epig_partial_kernel(EpilogueArgs A) {
   __shared__ double sh[NT];
   __shared__ double shd[NT];
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int DP = A.DP, RW = DP;  // generic DP is a power of two >= 4 and <= NT
   const int lanes = NT / RW;
   const int tid = threadIdx.x, d = tid % RW, pl = tid / RW;
@@ -472,7 +474,7 @@ template <int NT>
 __global__ void __launch_bounds__(NT) epig_write_kernel(EpilogueArgs A) {
   __shared__ double sh[NT];
   __shared__ double shd[NT];
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int D = A.D, DP = A.DP, RW = DP;
   const int lanes = NT / RW;
   const int tid = threadIdx.x, d = tid % RW, pl = tid / RW;
@@ -547,7 +549,7 @@ template <int DP>
 __global__ void __launch_bounds__(256) epigw_partial_kernel(EpilogueArgs A) {
   constexpr int NW = 8, KL = DP / 32;
   __shared__ double sh[NW][DP + 1];
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int D = A.D, rs = stats_stride(DP);
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
@@ -620,7 +622,7 @@ __global__ void __launch_bounds__(256) epigw_write_kernel(EpilogueArgs A) {
   constexpr int NW = 8, KL = DP / 32;
   __shared__ double Rsh[DP + 1];
   __shared__ double red[NW];
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int D = A.D, rs = stats_stride(DP);
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t first, int64_t n) {

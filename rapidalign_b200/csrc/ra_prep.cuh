@@ -101,6 +101,8 @@ struct PrepArgs {
   double *meta;
   double *rec;    // [chunk_cap][stats_stride]
   int64_t *chcnt, *chx, *choff;  // [P], [P], [P + 1]
+  int32_t *cpair;                // [chunk_cap]: pair of each virtual chunk
+  unsigned *ticket;              // chunk counter of the launch (ra_chunks.cuh), zeroed
   int64_t *tcnt;                 // [2P] scratch: 64-point tiles of each side (D <= 3)
   int64_t *tbase_x, *tbase_y;    // [P + 1]: first tile of each pair's cloud (D <= 3)
   int *err;
@@ -125,6 +127,14 @@ __device__ __forceinline__ float eff_weight(const float *w, const uint8_t *mask,
   float v = (wmode == 3 || w == nullptr) ? 1.0f : w[i];
   if (mask != nullptr && mask[i] == 0) v = 0.0f;
   return v;
+}
+
+// cpair[v] = the pair of virtual chunk v, once choff is complete (the
+// segment kernel's CTA, after a barrier).
+__device__ __forceinline__ void chunk_pairs(const PrepArgs &A) {
+  const ChunkMap M{A.P, A.choff, A.chx};
+  const int64_t total = A.choff[A.P];
+  for (int64_t v = threadIdx.x; v < total; v += blockDim.x) A.cpair[v] = (int32_t)chunk_pair(M, v);
 }
 
 // Segment bounds, chunk counts and the chunk map; one CTA of 1024 threads.
@@ -186,6 +196,7 @@ __global__ void __launch_bounds__(1024) segment_kernel(PrepArgs A) {
   if (e) atomicOr(A.err, e);
   if (A.tcnt == nullptr) {
     block_exclusive_scan(A.chcnt, A.choff, A.P, A.chunk_cap, warp_tot, &carry);
+    chunk_pairs(A);
     return;
   }
   // the chunk map and both tile bases in one pass over the pairs
@@ -246,6 +257,8 @@ __global__ void __launch_bounds__(1024) segment_kernel(PrepArgs A) {
     A.tbase_x[A.P] = carry3[1];
     A.tbase_y[A.P] = carry3[2];
   }
+  __syncthreads();
+  chunk_pairs(A);
 }
 
 // Pass 1: per-chunk partial sums of weights and coordinates.
@@ -253,7 +266,7 @@ template <int NT>
 __global__ void __launch_bounds__(NT) stats_kernel(PrepArgs A) {
   __shared__ double sh[NT];
   __shared__ int64_t shl[NT];
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int tid = threadIdx.x;
   const int D = A.D, DP = A.DP;
   const int RW = red_width(D);
@@ -338,7 +351,7 @@ __global__ void __launch_bounds__(NT) stats3_kernel(PrepArgs A) {
   __shared__ double sh[(NT / 32) * 8];
   __shared__ long long shl[NT / 32];
   __shared__ double shm[NT / 32][2];
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int D = A.D;
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
@@ -417,7 +430,7 @@ __global__ void __launch_bounds__(256) statsw_kernel(PrepArgs A) {
   __shared__ double sh[NW][2 * DP + 2];
   __shared__ long long shl[NW];
   __shared__ float shm[NW][3];
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int D = A.D;
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t v, int64_t, int64_t) {
@@ -518,7 +531,7 @@ __global__ void __launch_bounds__(256, 2) statsw4_kernel(PrepArgs A) {
   __shared__ double sh[NW][2 * DP + 2];
   __shared__ long long shl[NW];
   __shared__ float shm[NW][3];
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int cl = lane % LPP, q = lane / LPP;
   const int D = A.D;
@@ -828,7 +841,7 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
 // Generic layout (D >= 4): scaled, anchored coordinates and normalised weights.
 template <int NT>
 __global__ void __launch_bounds__(NT) packg_kernel(PrepArgs A) {
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int D = A.D, DP = A.DP;
   const int RW = red_width(D);
   const int lanes = NT / RW;
@@ -868,7 +881,7 @@ template <int DP>
 __global__ void __launch_bounds__(256, 4) packgw_kernel(PrepArgs A) {
   constexpr int NC = DP / 4;  // float4 chunks per packed point
   static_assert(256 % NC == 0, "a thread keeps one chunk");
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int D = A.D, c = threadIdx.x % NC;
   for_each_chunk(M, [&](int64_t p, int side, int64_t ch, int64_t, int64_t, int64_t) {
     const Seg sg = A.seg[p];
@@ -951,7 +964,7 @@ template <int DP, bool V4>
 __global__ void __launch_bounds__(256) packtc_kernel(PrepArgs A) {
   constexpr int NG = DP / 8;     // coordinate groups per point
   constexpr int TB = DP * 128;   // bytes of a hi (or lo) tile
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   const int D = A.D;
   for_each_chunk(M, [&](int64_t p, int side, int64_t ch, int64_t, int64_t, int64_t) {
     const Seg sg = A.seg[p];
@@ -1052,6 +1065,8 @@ struct PackArgs {
   const Seg *seg;
   const double *meta;
   const int64_t *choff, *chx;
+  const int32_t *cpair;
+  unsigned *ticket;
   const int64_t *tbase_x, *tbase_y;  // [P + 1]
   int64_t max_tiles_x, max_tiles_y;
   ulonglong2 *tiles_x, *tiles_y;     // [tiles][nq = 2][64]
@@ -1125,7 +1140,7 @@ __device__ __forceinline__ void pack3_slot(const PackArgs &A, const Pack3Side &S
 
 template <int NT>
 __global__ void __launch_bounds__(NT) pack3_kernel(PackArgs A) {
-  const ChunkMap M{A.P, A.choff, A.chx};
+  const ChunkMap M{A.P, A.choff, A.chx, A.cpair, A.ticket};
   for_each_chunk(M, [&](int64_t p, int side, int64_t c, int64_t, int64_t, int64_t) {
     const Seg sg = A.seg[p];
     if (small_pair(sg)) return;  // packed by prep3_kernel
