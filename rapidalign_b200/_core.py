@@ -129,10 +129,39 @@ def uses_tensor_cores(spec: Spec) -> bool:
     128 on the automatic or tensor engine), whose bounded waits can expire."""
     if spec.dim <= 3 or spec.engine == _lib.RA_ENGINE_SIMT:
         return False
+    return _wide(spec)
+
+
+def _wide(spec: Spec) -> bool:
+    """Padded dim 32, 64 or 128: the O(N) passes may stream their rows by bulk
+    copies (equal weights, no mask), whose bounded waits can expire too."""
+    if spec.dim <= 3:
+        return False
     dp = 4
     while dp < spec.dim:
         dp <<= 1
     return dp in (32, 64, 128)
+
+
+# error words of finished backward passes, read once their copies are done
+# (at the next forward or backward): a backward returns without stopping the
+# GPU, and an expired wait in it still raises, one call later
+_LATE_WORDS: list = []
+
+
+def _check_late(lib) -> None:
+    keep = []
+    failed = None
+    for w in _LATE_WORDS:
+        if w.event.query():
+            code = lib.ra_kde_status_of_error_word(w.read()[0])
+            if code != _lib.RA_OK and failed is None:
+                failed = code
+        else:
+            keep.append(w)
+    _LATE_WORDS[:] = keep
+    if failed is not None:
+        _lib.check(failed, "kde backward (an earlier call)")
 
 
 _READ_STREAMS: dict = {}
@@ -248,6 +277,8 @@ def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tens
     only; `reduce(f64_view, f32_view)` must then sum the partial buffers
     across the group in place before K is formed."""
     lib = _lib.load()
+    if _LATE_WORDS:
+        _check_late(lib)
     device = x.device
     need_sigma_grad = need_grad and sigma_t is not None and sigma_t.requires_grad
     weights_grad = any(w is not None and w.requires_grad for w in (w_x, w_y))
@@ -281,7 +312,7 @@ def forward_sums(x: Tensor, y: Tensor, w_x: Optional[Tensor], w_y: Optional[Tens
                                         ws.data_ptr(), ws.numel(), stream)
         _lib.check(rc, "kde forward")
         early = None if prepared is None else _ErrorWord(ws, prepared, spec.batch_flags)
-        if uses_tensor_cores(spec):
+        if _wide(spec):
             pending = _ErrorWord(ws, _mark(tstream))  # an expired wait shows after the tiles
         if early is not None:
             words = early.read()
@@ -322,6 +353,8 @@ def backward_sums(state: _State, coef: Tensor, need) -> tuple:
     """Gradients (x, y, w_x, w_y, sigma) for coefficients coef = dL/d(Kxx|Kyy|Kxy)
     (float64 [3P]); `need` flags which of the five are wanted."""
     lib = _lib.load()
+    if _LATE_WORDS:
+        _check_late(lib)
     spec = state.spec
     x32, y32, wx32, wy32, ws = state.keep[:5]
     device = x32.device
@@ -350,6 +383,11 @@ def backward_sums(state: _State, coef: Tensor, need) -> tuple:
                                  ctypes.byref(grads), ws.data_ptr(), ws.numel(),
                                  _lib.stream_handle(device))
     _lib.check(rc, "kde backward")
+    if _wide(spec):
+        # the backward's own bounded waits: its error word, read later
+        word = _ErrorWord(ws, _mark(torch.cuda.current_stream(device)))
+        ws.record_stream(_read_stream(device)[0])  # not reused before the copy
+        _LATE_WORDS.append(word)
     if state.pending is not None:
         # the forward's tile kernels are done by the time this returns, while
         # the backward just enqueued keeps the GPU busy

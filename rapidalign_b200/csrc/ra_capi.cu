@@ -21,6 +21,7 @@
 #include "ra_pdl.cuh"
 #include "ra_plan.cuh"
 #include "ra_prep.cuh"
+#include "ra_ring.cuh"
 #include "ra_tc16.cuh"
 #include "ra_tiles3.cuh"
 #include "ra_tilesg.cuh"
@@ -227,6 +228,63 @@ int check_common(const ra_kde_desc *d, void *ws, size_t ws_bytes, size_t need) {
 // pointers (a contiguous tensor can start at any float); null counts as
 // aligned.
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// The sums pass on the bulk-copy ring: two CTAs per SM (dynamic shared
+// memory above the 48 KB default).
+template <int DP>
+int launch_statsw_ring_d(const PrepArgs &pa, cudaStream_t st) {
+  const size_t smem = ring_sum_smem();
+  if (cudaFuncSetAttribute(statsw_ring_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return RA_ERR_CUDA;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  statsw_ring_kernel<DP><<<(unsigned)(sms > 0 ? 2 * sms : 2), kRingThreads, smem, st>>>(
+      pa, kTcSpinLimit);
+  return RA_OK;
+}
+template <int DP>
+int launch_write_ring_d(const EpilogueArgs &ea, cudaStream_t st) {
+  const size_t smem = ring_write_smem<DP>();
+  if (cudaFuncSetAttribute(epigw_ring_write_kernel<DP>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return RA_ERR_CUDA;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  epigw_ring_write_kernel<DP><<<(unsigned)(sms > 0 ? 2 * sms : 2), kRingThreads, smem, st>>>(
+      ea, kTcSpinLimit);
+  return RA_OK;
+}
+int launch_write_ring(int DP, const EpilogueArgs &ea, cudaStream_t st) {
+  if (DP == 32) return launch_write_ring_d<32>(ea, st);
+  if (DP == 64) return launch_write_ring_d<64>(ea, st);
+  return launch_write_ring_d<128>(ea, st);
+}
+template <int DP>
+int launch_pack_ring_d(const PrepArgs &pa, cudaStream_t st) {
+  const size_t smem = ring_pack_smem<DP>();
+  if (cudaFuncSetAttribute(packtc_ring_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return RA_ERR_CUDA;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  packtc_ring_kernel<DP><<<(unsigned)(sms > 0 ? 2 * sms : 2), kRingThreads, smem, st>>>(
+      pa, kTcSpinLimit);
+  return RA_OK;
+}
+int launch_pack_ring(int DP, const PrepArgs &pa, cudaStream_t st) {
+  if (DP == 32) return launch_pack_ring_d<32>(pa, st);
+  if (DP == 64) return launch_pack_ring_d<64>(pa, st);
+  return launch_pack_ring_d<128>(pa, st);
+}
+int launch_statsw_ring(int DP, const PrepArgs &pa, cudaStream_t st) {
+  if (DP == 32) return launch_statsw_ring_d<32>(pa, st);
+  if (DP == 64) return launch_statsw_ring_d<64>(pa, st);
+  return launch_statsw_ring_d<128>(pa, st);
+}
 
 unsigned chunk_grid(const Layout &L) {
   int dev = 0, sms = 0;
@@ -501,7 +559,15 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
     // float4 loads of the caller's points need D % 4 == 0 and 16-byte
     // aligned bases; anything else takes the scalar passes
     const bool v4 = d->dim % 4 == 0 && aligned16(in->x) && aligned16(in->y);
-    if (v4 && L.DP == 32)
+    // equal weights and no mask: the rows are the points alone, streamed by
+    // bulk copies (ra_ring.cuh)
+    const bool ring = v4 && L.DP >= 32 && L.DP <= 128 && pa.mask_x == nullptr && pa.mask_y == nullptr &&
+                      (d->weights_x == RA_WEIGHTS_UNIFORM || in->w_x == nullptr) &&
+                      (d->weights_y == RA_WEIGHTS_UNIFORM || in->w_y == nullptr);
+    if (ring) {
+      const int rg = launch_statsw_ring(L.DP, pa, st);
+      if (rg) return rg;
+    } else if (v4 && L.DP == 32)
       statsw4_kernel<32><<<cgrid, 256, 0, st>>>(pa);
     else if (v4 && L.DP == 64)
       statsw4_kernel<64><<<cgrid, 256, 0, st>>>(pa);
@@ -521,7 +587,10 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
       stats_kernel<kPrepThreads><<<cgrid, kPrepThreads, 0, st>>>(pa);
     meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
     pa.ticket = at<unsigned>(ws, L.hdr + kHdrChunkTickets) + 1;  // packing
-    if (L.tc16 && v4 && L.DP == 32)
+    if (L.tc16 && ring) {
+      const int rg = launch_pack_ring(L.DP, pa, st);
+      if (rg) return rg;
+    } else if (L.tc16 && v4 && L.DP == 32)
       packtc_kernel<32, true><<<cgrid, 256, 0, st>>>(pa);
     else if (L.tc16 && v4 && L.DP == 64)
       packtc_kernel<64, true><<<cgrid, 256, 0, st>>>(pa);
@@ -844,6 +913,21 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
       epi3_write_kernel<kEpiThreads><<<cgrid, kEpiThreads, 0, st>>>(ea);
       g_launches += 2;
     }
+  } else if (L.DP >= 32 && L.DP <= 128 && ea.vec4 && ea.xraw && ea.mask_x == nullptr &&
+             ea.mask_y == nullptr && ea.grad_wx == nullptr && ea.grad_wy == nullptr) {
+    // tensor-core layout, position gradients only: the write pass streams its
+    // rows by bulk copies (ra_ring.cuh); the partial pass (centring) as below
+    ea.err = at<int>(ws, L.hdr + kHdrErr);
+    ea.ticket = etk;
+    if (ea.totals) {
+      if (L.DP == 32) epigw_partial_kernel<32><<<cgrid, 256, 0, st>>>(ea);
+      else if (L.DP == 64) epigw_partial_kernel<64><<<cgrid, 256, 0, st>>>(ea);
+      else epigw_partial_kernel<128><<<cgrid, 256, 0, st>>>(ea);
+    }
+    ea.ticket = etk + 1;
+    const int rg = launch_write_ring(L.DP, ea, st);
+    if (rg) return rg;
+    g_launches += ea.totals ? 2 : 1;
   } else if (L.DP >= 32) {
     // the partial pass only makes the side totals R (centering) and Q (weight
     // gradients); an uncentred call without weight gradients skips it

@@ -152,6 +152,7 @@ struct EpilogueArgs {
   int totals;  // the side totals R, Q are used (centering, or a weight gradient)
   int vec4;    // D % 4 == 0, grad_x, grad_y (and x, y when xraw) 16-byte aligned
   int xraw;    // no Gx / Gy (tensor-core layout): x' = c (x - anchor) from the points
+  int *err;    // the workspace's error word (bounded waits of the ring passes)
 };
 
 // The packed coordinate x'_d of point g: stored (Gx / Gy), or recomputed from

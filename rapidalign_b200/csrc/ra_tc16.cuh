@@ -127,18 +127,6 @@ struct Tc16Args {
   int no_mma;
 };
 
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
-                                         uint32_t mbar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst),
-      "l"(src), "r"(bytes), "r"(mbar)
-      : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes)
-               : "memory");
-}
 __host__ __device__ constexpr uint32_t t16_idesc(int N, int b_major) {
   // D f32, A and B f16, A K-major, B K-major (0) or MN-major (1), M = 128
   return (1u << 4) | ((uint32_t)b_major << 16) | ((uint32_t)(N >> 3) << 17) | (8u << 24);

@@ -100,6 +100,28 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+// Bulk copy (no multicast) of `bytes` (a multiple of 16, both addresses
+// 16-byte aligned) from global memory into this CTA's shared memory,
+// completing its bytes on mbarrier `mbar`.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
+                                         uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(mbar)
+      : "memory");
+}
+// Arrive on `mbar` and expect `bytes` more of asynchronous copies.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes)
+               : "memory");
+}
+// Expect `bytes` more of asynchronous copies on `mbar`, without arriving.
+__device__ __forceinline__ void mbar_tx(uint32_t mbar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(mbar), "r"(bytes)
+               : "memory");
+}
+
 template <bool V>
 struct BoolC {
   static constexpr bool value = V;

@@ -69,10 +69,13 @@ def test_unaligned_points_match_aligned_and_oracle(d, center, cuda_device):
         assert_k(kxy, r.Kxy, f"Kxy {kind}")
         assert_grad(gx, r.grad_x, f"grad_x {kind}")
         assert_grad(gy, r.grad_y, f"grad_y {kind}")
-    # the two call kinds differ only in the summation order of the side sums
+    # the two call kinds take different O(N) kernels (aligned points: the
+    # bulk-copy passes; offset points: scalar loads), which add the fp64 side
+    # sums and the fp32 |x'|^2 of each point in different orders: a few
+    # float32 roundings apart, far inside the oracle tolerance above
     for a, b in zip(res["aligned"], res["offset"]):
         scale = max(float(np.abs(a).max()), 1e-30)
-        assert float(np.abs(a - b).max()) <= 1e-6 * scale
+        assert float(np.abs(a - b).max()) <= 4e-6 * scale
 
 
 @pytest.mark.parametrize("d", [64, 128])

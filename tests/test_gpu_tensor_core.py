@@ -219,3 +219,31 @@ def test_tensor_core_many_items_with_empty_clouds(d, cuda_device):
     assert_loss(_np(outs[0]), r.loss, r.Kxx, r.Kyy, "loss")
     assert_grad(_np(xt.grad), r.grad_x, "grad_x")
     assert_grad(_np(yt.grad), r.grad_y, "grad_y")
+
+
+@pytest.mark.parametrize("d", [32, 64, 100, 128])
+@pytest.mark.parametrize("center", [False, True])
+def test_equal_weight_sums_over_many_chunks(d, center, cuda_device):
+    """Equal weights and no mask: the sums pass streams the points through
+    shared memory by bulk copies, a stage of rows at a time, chunks of 1024
+    points taken from a ticket.  Sides of 2100 and 1990 points (three and two
+    chunks, the last ones ragged), 1025 against 1100 (a chunk of one point),
+    an empty side; d = 100 leaves zero-padded coordinates in the 128-wide
+    records."""
+    import rapidalign_b200 as ra
+    rng = np.random.default_rng(500 + d + int(center))
+    x, y, ptr_x, ptr_y = _embed_batch(rng, [2100, 17, 1025, 0, 64], [1990, 40, 1100, 5, 70], d)
+    dev = cuda_device
+    xt, yt = _cuda(x, dev, True), _cuda(y, dev, True)
+    outs = ra.pyg_kde_mmd_loss(xt, yt, src_ptr=_cuda(ptr_x, dev), tgt_ptr=_cuda(ptr_y, dev),
+                               sigma=1.0, center=center)
+    up = [rng.uniform(0.5, 1.5, len(ptr_x) - 1) for _ in range(4)]
+    total = sum((torch.as_tensor(u, device=dev) * o.double()).sum() for u, o in zip(up, outs))
+    total.backward()
+    r = O.pyg_kde_mmd_loss(x, y, ptr_x, ptr_y, sigma=1.0, center=center, upstream=up)
+    assert_k(_np(outs[1]), r.Kxx, "Kxx")
+    assert_k(_np(outs[2]), r.Kyy, "Kyy")
+    assert_k(_np(outs[3]), r.Kxy, "Kxy")
+    assert_loss(_np(outs[0]), r.loss, r.Kxx, r.Kyy, "loss")
+    assert_grad(_np(xt.grad), r.grad_x, "grad_x")
+    assert_grad(_np(yt.grad), r.grad_y, "grad_y")
