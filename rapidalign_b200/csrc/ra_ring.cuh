@@ -348,8 +348,7 @@ constexpr size_t ring_sum_smem() { return (size_t)kRingSumStages * kRingSumStage
 // tile of a side as fp16 hi and lo halves in the core-matrix layout, byte
 // (d/8)*1024 + j*16 + (d%8)*2 for point j, coordinate d, and its slot values
 // (|x'|^2, |x'|^2 - log2 a, a * weight scale), as packtc_kernel writes them.
-// A stage holds R rows (a power of two, so stages never straddle a tile) of
-// a chunk's real points -- tile padding past the side's count is not copied
+// A stage holds the rows of one tile (R = 64) of a chunk's real points -- tile padding past the side's count is not copied
 // and packs as zeros -- plus, in a chunk's first stage, the side's anchor
 // pairs.  Lane l of a warp packs coordinate group l % NG (8 coordinates) of
 // point l / NG of the warp's step: its two float4 reads from shared memory
@@ -357,27 +356,26 @@ constexpr size_t ring_sum_smem() { return (size_t)kRingSumStages * kRingSumStage
 // 32-byte sectors of the tile (NG groups x 32 / NG consecutive points).
 // |x'|^2 is summed over a point's lanes by shuffles.
 // ---------------------------------------------------------------------------
-constexpr int kRingPackStages = 5;
-
 template <int DP>
 struct RingPackGeom {
   static constexpr int NG = DP / 8;     // coordinate groups per point
   static constexpr int PPI = 32 / NG;   // points per warp step
-  static constexpr int R = DP >= 128 ? 32 : 64;  // rows per stage (16 KB at most)
+  static constexpr int R = 64;          // rows per stage: one tile
+  static constexpr int NS = DP >= 128 ? 3 : 5;  // stages (~100 KB or less per CTA)
   static constexpr uint32_t OANC = R * DP * 4;
   static constexpr uint32_t SB = (OANC + 2 * DP * 4 + 127) / 128 * 128;
 };
 
 template <int DP>
 constexpr size_t ring_pack_smem() {
-  return (size_t)kRingPackStages * RingPackGeom<DP>::SB;
+  return (size_t)RingPackGeom<DP>::NS * RingPackGeom<DP>::SB;
 }
 
 template <int DP>
 __global__ void __launch_bounds__(kRingThreads, 2) packtc_ring_kernel(PrepArgs A,
                                                                       unsigned limit) {
   using G = RingPackGeom<DP>;
-  constexpr int NS = kRingPackStages, NG = G::NG, PPI = G::PPI, R = G::R;
+  constexpr int NS = G::NS, NG = G::NG, PPI = G::PPI, R = G::R;
   constexpr int TB = DP * 128;  // bytes of a hi (or lo) tile
   extern __shared__ __align__(128) uint8_t ring_buf[];
   __shared__ RingCtl<NS> RC;
@@ -477,7 +475,9 @@ __global__ void __launch_bounds__(kRingThreads, 2) packtc_ring_kernel(PrepArgs A
               hv[e] = tc_hi16(xv[2 * c + e] * cs);
               lv[e] = xv[2 * c + e] * cs - hv[e];
             }
-            hh[c] = tc_f16_bits(hv[0]) | (tc_f16_bits(hv[1]) << 16);
+            // hi has 11 significant bits inside fp16's normal range (the
+            // coordinate scale bounds it by 2^15): the conversion is exact
+            hh[c] = pack_half2(hv[0], hv[1]);
             ll[c] = pack_half2(lv[0], lv[1]);
             sq = fmaf(xv[2 * c], xv[2 * c], sq);
             sq = fmaf(xv[2 * c + 1], xv[2 * c + 1], sq);
