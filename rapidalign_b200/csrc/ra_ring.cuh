@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kRingThreads, 2) statsw_ring_kernel(PrepArgs A
 
   // ---- consumers ----
   const int cl = lane % LPP, q = lane / LPP;
-  double acc[CPL][4], W = 0.0;
+  double acc[CPL][4], acc2[CPL][4], W = 0.0;  // two sets: even and odd warp steps
   long long last = -1;
   float cmax = 0.f;
   bool any = false;
@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(kRingThreads, 2) statsw_ring_kernel(PrepArgs A
 #pragma unroll
           for (int k = 0; k < CPL; ++k)
 #pragma unroll
-            for (int j = 0; j < 4; ++j) acc[k][j] = 0.0;
+            for (int j = 0; j < 4; ++j) acc[k][j] = acc2[k][j] = 0.0;
           W = 0.0;
           last = -1;
           cmax = 0.f;
@@ -261,29 +261,44 @@ __global__ void __launch_bounds__(kRingThreads, 2) statsw_ring_kernel(PrepArgs A
         }
         const float *sp = reinterpret_cast<const float *>(st);
         // every point weighs 1 and is valid (equal weights, no mask), so the
-        // weighted and the plain coordinate sums are the same
-        for (int r = wid * PPW + q; r < h.nr; r += NW * PPW) {
+        // weighted and the plain coordinate sums are the same; two warp steps
+        // per iteration into two accumulator sets (independent add chains)
+        constexpr int STEP = NW * PPW;
+        for (int r = wid * PPW + q; r < h.nr; r += 2 * STEP) {
+          const int r2 = r + STEP;
+          const bool two = r2 < h.nr;
 #pragma unroll
           for (int k = 0; k < CPL; ++k) {
             const int cc = cl + LPP * k;
             if (4 * cc < D) {
               const float4 xv = *reinterpret_cast<const float4 *>(sp + (size_t)r * D + 4 * cc);
+              const float4 xw = two ? *reinterpret_cast<const float4 *>(sp + (size_t)r2 * D + 4 * cc)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
               acc[k][0] += (double)xv.x;
               acc[k][1] += (double)xv.y;
               acc[k][2] += (double)xv.z;
               acc[k][3] += (double)xv.w;
-              cmax = fmaxf(cmax, fmaxf(fmaxf(fabsf(xv.x), fabsf(xv.y)),
-                                       fmaxf(fabsf(xv.z), fabsf(xv.w))));
+              acc2[k][0] += (double)xw.x;
+              acc2[k][1] += (double)xw.y;
+              acc2[k][2] += (double)xw.z;
+              acc2[k][3] += (double)xw.w;
+              const float m0 = fmaxf(fmaxf(fabsf(xv.x), fabsf(xv.y)), fmaxf(fabsf(xv.z), fabsf(xv.w)));
+              const float m1 = fmaxf(fmaxf(fabsf(xw.x), fabsf(xw.y)), fmaxf(fabsf(xw.z), fabsf(xw.w)));
+              cmax = fmaxf(cmax, fmaxf(m0, m1));
             }
           }
           if (cl == 0) {
-            W += 1.0;
-            last = h.r0 + r;
+            W += two ? 2.0 : 1.0;
+            last = h.r0 + (two ? r2 : r);
           }
           any = true;
         }
         if (!(h.flags & kRingLast)) return true;
         // ---- the chunk's records: warp slots, then the 8 warps in order ----
+#pragma unroll
+        for (int k = 0; k < CPL; ++k)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[k][j] += acc2[k][j];
 #pragma unroll
         for (int o = LPP; o < 32; o <<= 1) {
 #pragma unroll
@@ -444,58 +459,75 @@ __global__ void __launch_bounds__(kRingThreads, 2) packtc_ring_kernel(PrepArgs A
         float *Ap = h.side == 0 ? A.Ax : A.Ay;
         const float sc = h.scl, cs = (float)h.cs, wsc = (float)h.cc;
         const float ar = (float)h.k_x;
-        // a warp-uniform loop: every lane takes part in the shuffles
-        for (int base = wid * PPI; base < h.nr; base += kRingWarps * PPI) {
-          const int pi = base + lane / NG;  // point of the stage
-          const bool act = pi < h.nr;
-          const int64_t i = h.r0 + pi;      // row of the side
-          const bool real = act && i < h.count;
-          float xv[8];
-          const float *row = reinterpret_cast<const float *>(st) + (size_t)pi * D;
-          if (real && 8 * g + 8 <= D) {
-            const float4 r0 = *reinterpret_cast<const float4 *>(row + 8 * g);
-            const float4 r1 = *reinterpret_cast<const float4 *>(row + 8 * g + 4);
-            const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+        const float lga = log2f(ar);  // a is the same for every point of the side
+        // a warp-uniform loop (every lane takes part in the shuffles) over two
+        // independent sets of points per iteration, loads first
+        constexpr int STEP = kRingWarps * PPI;
+        for (int base = wid * PPI; base < h.nr; base += 2 * STEP) {
+          float xv[2][8];
+          bool act[2], real[2];
+          int64_t i[2];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) xv[u] = sc * ((rv[u] - ah[u]) - al[u]);
-          } else {
+          for (int u = 0; u < 2; ++u) {
+            const int pi = base + u * STEP + lane / NG;  // point of the stage
+            act[u] = pi < h.nr;
+            i[u] = h.r0 + pi;  // row of the side
+            real[u] = act[u] && i[u] < h.count;
+            const float *row = reinterpret_cast<const float *>(st) + (size_t)pi * D;
+            if (real[u] && 8 * g + 8 <= D) {
+              const float4 r0 = *reinterpret_cast<const float4 *>(row + 8 * g);
+              const float4 r1 = *reinterpret_cast<const float4 *>(row + 8 * g + 4);
+              const float rv[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int d = 8 * g + u;
-              xv[u] = (real && d < D) ? sc * ((row[d] - ah[u]) - al[u]) : 0.f;
+              for (int q = 0; q < 8; ++q) xv[u][q] = sc * ((rv[q] - ah[q]) - al[q]);
+            } else {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const int d = 8 * g + q;
+                xv[u][q] = (real[u] && d < D) ? sc * ((row[d] - ah[q]) - al[q]) : 0.f;
+              }
             }
           }
-          uint32_t hh[4], ll[4];
-          float sq = 0.f;
+          uint32_t hh[2][4], ll[2][4];
+          float sq[2] = {0.f, 0.f};
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float hv[2], lv[2];
+          for (int u = 0; u < 2; ++u)
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              hv[e] = tc_hi16(xv[2 * c + e] * cs);
-              lv[e] = xv[2 * c + e] * cs - hv[e];
+            for (int c = 0; c < 4; ++c) {
+              float hv[2], lv[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                hv[e] = tc_hi16(xv[u][2 * c + e] * cs);
+                lv[e] = xv[u][2 * c + e] * cs - hv[e];
+              }
+              // hi has 11 significant bits inside fp16's normal range (the
+              // coordinate scale bounds it by 2^15): the conversion is exact
+              hh[u][c] = pack_half2(hv[0], hv[1]);
+              ll[u][c] = pack_half2(lv[0], lv[1]);
+              sq[u] = fmaf(xv[u][2 * c], xv[u][2 * c], sq[u]);
+              sq[u] = fmaf(xv[u][2 * c + 1], xv[u][2 * c + 1], sq[u]);
             }
-            // hi has 11 significant bits inside fp16's normal range (the
-            // coordinate scale bounds it by 2^15): the conversion is exact
-            hh[c] = pack_half2(hv[0], hv[1]);
-            ll[c] = pack_half2(lv[0], lv[1]);
-            sq = fmaf(xv[2 * c], xv[2 * c], sq);
-            sq = fmaf(xv[2 * c + 1], xv[2 * c + 1], sq);
+#pragma unroll
+          for (int o = NG / 2; o > 0; o >>= 1) {
+            sq[0] += __shfl_xor_sync(kFull, sq[0], o);
+            sq[1] += __shfl_xor_sync(kFull, sq[1], o);
           }
 #pragma unroll
-          for (int o = NG / 2; o > 0; o >>= 1) sq += __shfl_xor_sync(kFull, sq, o);
-          if (act) {
-            const int64_t tile = h.tb + i / kTile;
-            const int j = (int)(i % kTile);
+          for (int u = 0; u < 2; ++u) {
+            if (!act[u]) continue;
+            const int64_t tile = h.tb + i[u] / kTile;
+            const int j = (int)(i[u] % kTile);
             const size_t off = (size_t)tile * TB + (size_t)g * 1024 + (size_t)j * 16;
-            *reinterpret_cast<uint4 *>(hp + off) = make_uint4(hh[0], hh[1], hh[2], hh[3]);
-            *reinterpret_cast<uint4 *>(lp + off) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+            *reinterpret_cast<uint4 *>(hp + off) =
+                make_uint4(hh[u][0], hh[u][1], hh[u][2], hh[u][3]);
+            *reinterpret_cast<uint4 *>(lp + off) =
+                make_uint4(ll[u][0], ll[u][1], ll[u][2], ll[u][3]);
             if (g == 0) {
-              const float a = real ? ar : 0.f;
-              if (real) Ap[h.s + i] = a;
+              const float a = real[u] ? ar : 0.f;
+              if (real[u]) Ap[h.s + i[u]] = a;
               float *cv = cp + tile * (3 * kTile);
-              cv[j] = sq;
-              cv[kTile + j] = a > 0.f ? sq - log2f(a) : INFINITY;
+              cv[j] = sq[u];
+              cv[kTile + j] = a > 0.f ? sq[u] - lga : INFINITY;
               cv[2 * kTile + j] = a * wsc;
             }
           }
