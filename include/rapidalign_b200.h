@@ -232,7 +232,9 @@ RA_API int ra_kde_status_of_error_word(int word);
  * and, when nflags > 0, of the int32 flags[0..nflags) (ra_ptr_from_batch)
  * into host[1..nflags]; `host` should be page-locked for the copies to stay
  * asynchronous.  For a status read on a side stream that waits for the
- * preparation (an event) while the tile kernels run. */
+ * preparation (an event) while the tile kernels run.  Replaces the
+ * reference's host reads behind its ptr, batch and weight checks
+ * (rapidalign/kde.py:136-151, 198: .item() calls that stop the stream). */
 RA_API int ra_kde_error_word_async(const void *workspace, const int32_t *flags, int32_t nflags,
                                    int32_t *host, ra_stream_t stream);
 
