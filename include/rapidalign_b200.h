@@ -128,9 +128,12 @@ typedef struct ra_kde_desc {
  * (dim >= 4 on the tensor-core engine) issue no MMA at all and bound each wait
  * to 4096 polls, so their first wait for a GEMM expires with nothing in flight:
  * the kernel records the timeout, frees its tensor memory and returns, and
- * ra_kde_check reports RA_ERR_DEVICE_TIMEOUT.  The results of such a call are
- * invalid. */
-enum ra_test_hook { RA_TEST_NO_MMA = 1 };
+ * ra_kde_check reports RA_ERR_DEVICE_TIMEOUT.  RA_TEST_RING_IDLE: the O(N)
+ * passes that stream rows by bulk copies (padded dim 32-128, equal weights, no
+ * mask) copy nothing and bound each wait to 4096 polls, so their consumers'
+ * first wait expires: the same status, from the forward (sums and packing)
+ * or the backward (write pass).  The results of such a call are invalid. */
+enum ra_test_hook { RA_TEST_NO_MMA = 1, RA_TEST_RING_IDLE = 2 };
 
 typedef struct ra_kde_inputs {
   const float *x;        /* [num_x * D] */

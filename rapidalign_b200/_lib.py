@@ -45,6 +45,7 @@ RA_ENGINE_SIMT = 1
 RA_ENGINE_TENSOR = 2
 
 RA_TEST_NO_MMA = 1
+RA_TEST_RING_IDLE = 2
 
 RA_BATCH_UNSORTED = 1
 RA_BATCH_NEGATIVE = 2

@@ -91,7 +91,7 @@ bool desc_ok(const ra_kde_desc *d) {
   if (d->shard_count < 0 || (d->shard_count > 1 &&
                              (d->shard_index < 0 || d->shard_index >= d->shard_count)))
     return false;
-  if ((d->test_hooks & ~RA_TEST_NO_MMA) != 0) return false;
+  if ((d->test_hooks & ~(RA_TEST_NO_MMA | RA_TEST_RING_IDLE)) != 0) return false;
   if (d->skip_weight_sums != 0 && d->skip_weight_sums != 1) return false;
   if (d->deterministic != 0 && d->deterministic != 1) return false;
   return true;
@@ -229,10 +229,20 @@ int check_common(const ra_kde_desc *d, void *ws, size_t ws_bytes, size_t need) {
 // aligned.
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// The ring passes' wait bound (RA_TEST_RING_IDLE: idle producers and short
+// waits, for the failure-path tests).
+RingRun ring_run(const ra_kde_desc *d) {
+  RingRun r;
+  const bool idle = (d->test_hooks & RA_TEST_RING_IDLE) != 0;
+  r.limit = idle ? 4096u : kTcSpinLimit;
+  r.idle = idle ? 1 : 0;
+  return r;
+}
+
 // The sums pass on the bulk-copy ring: two CTAs per SM (dynamic shared
 // memory above the 48 KB default).
 template <int DP>
-int launch_statsw_ring_d(const PrepArgs &pa, cudaStream_t st) {
+int launch_statsw_ring_d(const PrepArgs &pa, const RingRun &run, cudaStream_t st) {
   const size_t smem = ring_sum_smem();
   if (cudaFuncSetAttribute(statsw_ring_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)
@@ -241,11 +251,11 @@ int launch_statsw_ring_d(const PrepArgs &pa, cudaStream_t st) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   statsw_ring_kernel<DP><<<(unsigned)(sms > 0 ? 2 * sms : 2), kRingThreads, smem, st>>>(
-      pa, kTcSpinLimit);
+      pa, run);
   return RA_OK;
 }
 template <int DP>
-int launch_write_ring_d(const EpilogueArgs &ea, cudaStream_t st) {
+int launch_write_ring_d(const EpilogueArgs &ea, const RingRun &run, cudaStream_t st) {
   const size_t smem = ring_write_smem<DP>();
   if (cudaFuncSetAttribute(epigw_ring_write_kernel<DP>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -254,16 +264,16 @@ int launch_write_ring_d(const EpilogueArgs &ea, cudaStream_t st) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   epigw_ring_write_kernel<DP><<<(unsigned)(sms > 0 ? 2 * sms : 2), kRingThreads, smem, st>>>(
-      ea, kTcSpinLimit);
+      ea, run);
   return RA_OK;
 }
-int launch_write_ring(int DP, const EpilogueArgs &ea, cudaStream_t st) {
-  if (DP == 32) return launch_write_ring_d<32>(ea, st);
-  if (DP == 64) return launch_write_ring_d<64>(ea, st);
-  return launch_write_ring_d<128>(ea, st);
+int launch_write_ring(int DP, const EpilogueArgs &ea, const RingRun &run, cudaStream_t st) {
+  if (DP == 32) return launch_write_ring_d<32>(ea, run, st);
+  if (DP == 64) return launch_write_ring_d<64>(ea, run, st);
+  return launch_write_ring_d<128>(ea, run, st);
 }
 template <int DP>
-int launch_pack_ring_d(const PrepArgs &pa, cudaStream_t st) {
+int launch_pack_ring_d(const PrepArgs &pa, const RingRun &run, cudaStream_t st) {
   const size_t smem = ring_pack_smem<DP>();
   if (cudaFuncSetAttribute(packtc_ring_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem) != cudaSuccess)
@@ -272,18 +282,18 @@ int launch_pack_ring_d(const PrepArgs &pa, cudaStream_t st) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   packtc_ring_kernel<DP><<<(unsigned)(sms > 0 ? 2 * sms : 2), kRingThreads, smem, st>>>(
-      pa, kTcSpinLimit);
+      pa, run);
   return RA_OK;
 }
-int launch_pack_ring(int DP, const PrepArgs &pa, cudaStream_t st) {
-  if (DP == 32) return launch_pack_ring_d<32>(pa, st);
-  if (DP == 64) return launch_pack_ring_d<64>(pa, st);
-  return launch_pack_ring_d<128>(pa, st);
+int launch_pack_ring(int DP, const PrepArgs &pa, const RingRun &run, cudaStream_t st) {
+  if (DP == 32) return launch_pack_ring_d<32>(pa, run, st);
+  if (DP == 64) return launch_pack_ring_d<64>(pa, run, st);
+  return launch_pack_ring_d<128>(pa, run, st);
 }
-int launch_statsw_ring(int DP, const PrepArgs &pa, cudaStream_t st) {
-  if (DP == 32) return launch_statsw_ring_d<32>(pa, st);
-  if (DP == 64) return launch_statsw_ring_d<64>(pa, st);
-  return launch_statsw_ring_d<128>(pa, st);
+int launch_statsw_ring(int DP, const PrepArgs &pa, const RingRun &run, cudaStream_t st) {
+  if (DP == 32) return launch_statsw_ring_d<32>(pa, run, st);
+  if (DP == 64) return launch_statsw_ring_d<64>(pa, run, st);
+  return launch_statsw_ring_d<128>(pa, run, st);
 }
 
 unsigned chunk_grid(const Layout &L) {
@@ -565,7 +575,7 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
                       (d->weights_x == RA_WEIGHTS_UNIFORM || in->w_x == nullptr) &&
                       (d->weights_y == RA_WEIGHTS_UNIFORM || in->w_y == nullptr);
     if (ring) {
-      const int rg = launch_statsw_ring(L.DP, pa, st);
+      const int rg = launch_statsw_ring(L.DP, pa, ring_run(d), st);
       if (rg) return rg;
     } else if (v4 && L.DP == 32)
       statsw4_kernel<32><<<cgrid, 256, 0, st>>>(pa);
@@ -588,7 +598,7 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
     meta_kernel<<<(unsigned)ceil_div(P, 4), 128, 0, st>>>(pa);
     pa.ticket = at<unsigned>(ws, L.hdr + kHdrChunkTickets) + 1;  // packing
     if (L.tc16 && ring) {
-      const int rg = launch_pack_ring(L.DP, pa, st);
+      const int rg = launch_pack_ring(L.DP, pa, ring_run(d), st);
       if (rg) return rg;
     } else if (L.tc16 && v4 && L.DP == 32)
       packtc_kernel<32, true><<<cgrid, 256, 0, st>>>(pa);
@@ -925,7 +935,7 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
       else epigw_partial_kernel<128><<<cgrid, 256, 0, st>>>(ea);
     }
     ea.ticket = etk + 1;
-    const int rg = launch_write_ring(L.DP, ea, st);
+    const int rg = launch_write_ring(L.DP, ea, ring_run(d), st);
     if (rg) return rg;
     g_launches += ea.totals ? 2 : 1;
   } else if (L.DP >= 32) {

@@ -728,7 +728,11 @@ __global__ void __launch_bounds__(128) meta_kernel(PrepArgs A) {
     nv = warp_sum(nv);
     lst = warp_max(lst);
     const int64_t span = side == 0 ? A.seg[p].xspan : A.seg[p].yspan;
-    const int64_t count = A.layout == 0 ? span : (int64_t)lst + 1;
+    int64_t count = A.layout == 0 ? span : (int64_t)lst + 1;
+    // within [0, span] whatever the records hold (a pass that gave up on a
+    // bounded wait leaves them unwritten): later kernels index by it
+    if (!(count >= 0)) count = 0;
+    if (count > span) count = span;
     const int wmode = side == 0 ? A.wmode_x : A.wmode_y;
     double wmax = -INFINITY, nwmin = -INFINITY;
     if (DP == 3) {

@@ -43,6 +43,15 @@ struct RingHdr {
   int side, nr, flags, aoff;  // aoff: byte offset of the stage's first weight
 };
 
+// How a ring kernel runs: the polls of one role wait (kTcSpinLimit), and, for
+// tests of the failure path only, an idle producer that copies nothing, so
+// the consumers' first wait expires with no copy in flight.  The producer's
+// final drain keeps kTcSpinLimit whatever `limit` says.
+struct RingRun {
+  unsigned limit;
+  int idle;
+};
+
 // The ring's shared state (static shared memory of the kernel).
 template <int NS>
 struct RingCtl {
@@ -199,7 +208,8 @@ constexpr uint32_t kRingSumStageBytes = 16384;
 
 template <int DP>
 __global__ void __launch_bounds__(kRingThreads, 2) statsw_ring_kernel(PrepArgs A,
-                                                                       unsigned limit) {
+                                                                       RingRun run) {
+  const unsigned limit = run.limit;
   constexpr int NS = kRingSumStages, NW = kRingWarps, NC = DP / 4;
   constexpr int LPP = NC < 32 ? NC : 32;  // lanes per point
   constexpr int CPL = NC / LPP;           // float4 chunks per lane
@@ -217,7 +227,7 @@ __global__ void __launch_bounds__(kRingThreads, 2) statsw_ring_kernel(PrepArgs A
   ring_init(R);
 
   if (wid == kRingProdWarp) {
-    if (lane == 0) {
+    if (lane == 0 && !run.idle) {
       const uint32_t k = ring_produce(
           M, R, smem_u32(ring_buf), SB, rows,
           [&](RingHdr &h, int64_t &b, int64_t &e) {
@@ -234,7 +244,7 @@ __global__ void __launch_bounds__(kRingThreads, 2) statsw_ring_kernel(PrepArgs A
             bulk_g2s(dst, pts + (h.s + h.r0) * D, bytes, bar);
           },
           A.err, limit);
-      ring_drain(R, k, limit);
+      ring_drain(R, k, kTcSpinLimit);
     }
     return;
   }
@@ -388,7 +398,8 @@ constexpr size_t ring_pack_smem() {
 
 template <int DP>
 __global__ void __launch_bounds__(kRingThreads, 2) packtc_ring_kernel(PrepArgs A,
-                                                                      unsigned limit) {
+                                                                      RingRun run) {
+  const unsigned limit = run.limit;
   using G = RingPackGeom<DP>;
   constexpr int NS = G::NS, NG = G::NG, PPI = G::PPI, R = G::R;
   constexpr int TB = DP * 128;  // bytes of a hi (or lo) tile
@@ -400,7 +411,7 @@ __global__ void __launch_bounds__(kRingThreads, 2) packtc_ring_kernel(PrepArgs A
   ring_init(RC);
 
   if (wid == kRingProdWarp) {
-    if (lane == 0) {
+    if (lane == 0 && !run.idle) {
       const uint32_t k = ring_produce(
           M, RC, smem_u32(ring_buf), G::SB, R,
           [&](RingHdr &h, int64_t &b, int64_t &e) {
@@ -432,7 +443,7 @@ __global__ void __launch_bounds__(kRingThreads, 2) packtc_ring_kernel(PrepArgs A
             }
           },
           A.err, limit);
-      ring_drain(RC, k, limit);
+      ring_drain(RC, k, kTcSpinLimit);
     }
     return;
   }
@@ -572,7 +583,8 @@ constexpr size_t ring_write_smem() {
 
 template <int DP>
 __global__ void __launch_bounds__(kRingThreads, 2) epigw_ring_write_kernel(EpilogueArgs A,
-                                                                           unsigned limit) {
+                                                                           RingRun run) {
+  const unsigned limit = run.limit;
   using G = RingWriteGeom<DP>;
   constexpr int NS = kRingWriteStages, NC = G::NC, R = G::R;
   extern __shared__ __align__(128) uint8_t ring_buf[];
@@ -583,7 +595,7 @@ __global__ void __launch_bounds__(kRingThreads, 2) epigw_ring_write_kernel(Epilo
   ring_init(RC);
 
   if (wid == kRingProdWarp) {
-    if (lane == 0) {
+    if (lane == 0 && !run.idle) {
       const uint32_t k = ring_produce(
           M, RC, smem_u32(ring_buf), G::SB, R,
           [&](RingHdr &h, int64_t &b, int64_t &e) {
@@ -618,7 +630,7 @@ __global__ void __launch_bounds__(kRingThreads, 2) epigw_ring_write_kernel(Epilo
             if (anc) bulk_g2s(dst + G::OANC, side_anchor(A, h.p, h.side), 2u * DP * 4, bar);
           },
           A.err, limit);
-      ring_drain(RC, k, limit);
+      ring_drain(RC, k, kTcSpinLimit);
     }
     return;
   }
