@@ -65,7 +65,8 @@ struct Layout {
 
 // header block: int err @0, unsigned ticket @4, int has_state @8, int64 n_items @16,
 // unsigned chunk tickets @32 (ra_chunks.cuh): [0] the sums pass, [1] packing,
-// [2] [3] the backward's partial and write passes
+// [2] [3] the backward's partial and write passes; pair tickets: [4]
+// prep3_kernel, [5] epi3_small_kernel
 constexpr size_t kHdrErr = 0, kHdrTicket = 4, kHdrState = 8, kHdrNItems = 16,
                  kHdrChunkTickets = 32;
 constexpr int kItemF64 = 2;  // fp64 partials per work item: K, S
@@ -495,6 +496,7 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
   pa.choff = at<int64_t>(ws, L.choff);
   pa.cpair = at<int32_t>(ws, L.cpair);
   pa.ticket = at<unsigned>(ws, L.hdr + kHdrChunkTickets);  // the sums pass
+  pa.pair_ticket = at<unsigned>(ws, L.hdr + kHdrChunkTickets) + 4;
   pa.err = at<int>(ws, L.hdr + kHdrErr);
   pa.allow_fold = mode == 2 ? 0 : 1;
   if (!L.packed3) {
@@ -870,12 +872,11 @@ int backward_impl(const ra_kde_desc *d, const ra_kde_inputs *in, const double *c
   ea.choff = at<int64_t>(ws, L.choff);
   ea.chx = at<int64_t>(ws, L.chx);
   ea.cpair = at<int32_t>(ws, L.cpair);
-  // the chunked passes' tickets, zeroed here: a backward may run more than
-  // once after its forward
+  // the chunked passes' and epi3_small_kernel's tickets, zeroed here: a
+  // backward may run more than once after its forward
   unsigned *const etk = at<unsigned>(ws, L.hdr + kHdrChunkTickets) + 2;
-  if ((!L.packed3 || may_have_large_pairs(d)) &&
-      cudaMemsetAsync(etk, 0, 2 * sizeof(unsigned), st) != cudaSuccess)
-    return RA_ERR_CUDA;
+  if (cudaMemsetAsync(etk, 0, 4 * sizeof(unsigned), st) != cudaSuccess) return RA_ERR_CUDA;
+  ea.pair_ticket = etk + 3;
   ea.rec = at<double>(ws, L.rec);
   ea.x = in->x;
   ea.y = in->y;

@@ -100,6 +100,30 @@ __device__ __forceinline__ int64_t chunk_pair(const ChunkMap &M, int64_t v) {
 // range: chunk c of the side's n chunks, whose records start at virtual index
 // `first`.  The range and all arguments are uniform over the CTA, so f may
 // synchronise the block.
+// Pair tickets for the one-CTA-per-pair kernels, in a for loop's three parts:
+//   for (p = pair_ticket_first(ctr, slot); p < P; p = pair_ticket_next(slot, ++k, nxt)) {
+//     nxt = pair_ticket_take(ctr);  // the next pair, fetched while this one runs
+//     ...                           // `continue` still reaches the barrier
+//   }
+// Thread 0 draws; the CTA reads the draw after a barrier, from two slots (a
+// slot is rewritten only two barriers after it was read).  Pairs differ in
+// size by up to 64x (a batch of graphs of 32-2048 points), and a fixed
+// round-robin share per CTA left the slowest CTA with ~40 % more work than
+// the mean.
+__device__ __forceinline__ int64_t pair_ticket_first(unsigned *ctr, unsigned *slot) {
+  if (threadIdx.x == 0) slot[0] = atomicAdd(ctr, 1u);
+  __syncthreads();
+  return slot[0];
+}
+__device__ __forceinline__ unsigned pair_ticket_take(unsigned *ctr) {
+  return threadIdx.x == 0 ? atomicAdd(ctr, 1u) : 0u;
+}
+__device__ __forceinline__ int64_t pair_ticket_next(unsigned *slot, int k, unsigned nxt) {
+  if (threadIdx.x == 0) slot[k & 1] = nxt;
+  __syncthreads();
+  return slot[k & 1];
+}
+
 template <typename F>
 __device__ __forceinline__ void for_each_chunk(const ChunkMap &M, F &&f) {
   const int64_t total = M.choff[M.P];

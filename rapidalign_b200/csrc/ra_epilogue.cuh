@@ -135,6 +135,7 @@ struct EpilogueArgs {
   const int64_t *choff, *chx;  // chunk map (ra_chunks.cuh)
   const int32_t *cpair;
   unsigned *ticket;            // chunk counter of the launch, zeroed
+  unsigned *pair_ticket;       // pair counter of epi3_small_kernel, zeroed
   double *rec;         // per-chunk (Q, R[DP]) partials, stride stats_stride(DP)
   const float *x, *y;  // original coordinates
   const uint8_t *mask_x, *mask_y;
@@ -402,7 +403,12 @@ __global__ void __launch_bounds__(NT, 3) epi3_write_kernel(EpilogueArgs A) {
 template <int NT>
 __global__ void __launch_bounds__(NT, 3) epi3_small_kernel(EpilogueArgs A) {
   __shared__ double sh[(NT / 32) * 4];
-  for (int64_t p = blockIdx.x; p < A.P; p += gridDim.x) {
+  __shared__ unsigned pt_slot[2];
+  unsigned pt_nxt = 0;
+  int pt_k = 0;
+  for (int64_t p = pair_ticket_first(A.pair_ticket, pt_slot); p < A.P;
+       p = pair_ticket_next(pt_slot, ++pt_k, pt_nxt)) {
+    pt_nxt = pair_ticket_take(A.pair_ticket);
     if (!small_pair(A.seg[p])) continue;
     for (int side = 0; side < 2; ++side) {
       const EpiSide E = epi_side(A, p, side);

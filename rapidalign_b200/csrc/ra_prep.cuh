@@ -103,6 +103,7 @@ struct PrepArgs {
   int64_t *chcnt, *chx, *choff;  // [P], [P], [P + 1]
   int32_t *cpair;                // [chunk_cap]: pair of each virtual chunk
   unsigned *ticket;              // chunk counter of the launch (ra_chunks.cuh), zeroed
+  unsigned *pair_ticket;         // pair counter of prep3_kernel, zeroed
   int64_t *tcnt;                 // [2P] scratch: 64-point tiles of each side (D <= 3)
   int64_t *tbase_x, *tbase_y;    // [P + 1]: first tile of each pair's cloud (D <= 3)
   int *err;
@@ -1188,9 +1189,14 @@ __global__ void __launch_bounds__(NT) prep3_kernel(PrepArgs A, PackArgs K) {
   __shared__ long long shl[NT / 32];
   __shared__ float shm[NT / 32][2];
   __shared__ double tot[2][12];  // per side: W, nv, sum w'p (3), sum p (3), last, wmax, nwmin
+  __shared__ unsigned pt_slot[2];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int D = A.D;
-  for (int64_t p = blockIdx.x; p < A.P; p += gridDim.x) {
+  unsigned pt_nxt = 0;
+  int pt_k = 0;
+  for (int64_t p = pair_ticket_first(A.pair_ticket, pt_slot); p < A.P;
+       p = pair_ticket_next(pt_slot, ++pt_k, pt_nxt)) {
+    pt_nxt = pair_ticket_take(A.pair_ticket);
     Seg sg = A.seg[p];
     if (!small_pair(sg)) continue;
     for (int side = 0; side < 2; ++side) {
