@@ -458,11 +458,13 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
   const int mode = !grad ? 0 : (d->need_sigma_grad ? 2 : (d->skip_weight_sums ? 3 : 1));
   // the per-point sums start at zero where kernels add into them (the D <= 3
   // tile kernel's column sums) or where a split evaluation sums the records
-  // of all shards; the tensor-core kernel writes every field of every valid
+  // of all shards.  The tensor-core kernel writes every field of every valid
   // row itself (an item exists for each orientation and row tile, zeros when
-  // it has no column tiles), so there the clear would only cost bandwidth
-  // (0.6 GB per step for 1024 graphs at D=128)
-  const bool acc_written = L.tc16 && !(d->shard_count > 1);
+  // it has no column tiles), so there a clear would only cost bandwidth (0.6
+  // GB per step for 1024 graphs at D=128); in the D <= 3 layout the packing
+  // clears each slot it packs (prep3_kernel, pack3_kernel), stores that a
+  // latency-bound kernel absorbs, instead of a separate pass.
+  const bool acc_written = (L.tc16 || L.packed3) && !(d->shard_count > 1);
   if (grad && !acc_written) {
     if (cudaMemsetAsync(at<char>(ws, L.accX), 0, L.acc_x_bytes, st) != cudaSuccess ||
         cudaMemsetAsync(at<char>(ws, L.accY), 0, L.acc_y_bytes, st) != cudaSuccess)
@@ -557,6 +559,10 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
     pk.tiles_y = at<ulonglong2>(ws, L.tiles_y);
     pk.aw_x = at<float>(ws, L.Ax);
     pk.aw_y = at<float>(ws, L.Ay);
+    if (grad && !(d->shard_count > 1)) {  // cleared with the packing (below)
+      pk.acc_x = at<float>(ws, L.accX);
+      pk.acc_y = at<float>(ws, L.accY);
+    }
   }
   const unsigned cgrid = chunk_grid(L);
   segment_kernel<<<1, 1024, 0, st>>>(pa);

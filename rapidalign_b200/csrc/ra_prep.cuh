@@ -1076,6 +1076,8 @@ struct PackArgs {
   int64_t max_tiles_x, max_tiles_y;
   ulonglong2 *tiles_x, *tiles_y;     // [tiles][nq = 2][64]
   float *aw_x, *aw_y;                // [tiles * 64] a~ per slot
+  float *acc_x, *acc_y;              // [tiles * 64][kAcc3Stride] per-point sums, cleared
+                                     // here when the tile kernel adds into them (or null)
 };
 
 // Per-side constants of the D <= 3 packing (from the pair's metadata).
@@ -1086,6 +1088,7 @@ struct Pack3Side {
   int wmode;
   ulonglong2 *tiles;
   float *aw;
+  float *acc;  // the slots' per-point sums, zeroed with the packing (or null)
   double Wm;  // a~ = w' / Wm
   bool fold, uni;
   float pad, ax, ay, az, scale;
@@ -1107,6 +1110,7 @@ __device__ __forceinline__ Pack3Side pack3_side(const PackArgs &A, int64_t p, in
   S.wmode = side == 0 ? A.wmode_x : A.wmode_y;
   S.tiles = side == 0 ? A.tiles_x : A.tiles_y;
   S.aw = side == 0 ? A.aw_x : A.aw_y;
+  S.acc = side == 0 ? A.acc_x : A.acc_y;
   const double *meta = A.meta + p * meta_stride(3);
   S.Wm = meta[side] * meta[meta_wscale(3) + side];
   S.fold = meta[meta_fold(3) + side] != 0.0;
@@ -1141,6 +1145,12 @@ __device__ __forceinline__ void pack3_slot(const PackArgs &A, const Pack3Side &S
   tp[0] = make_ulonglong2(pk2u(c0, c0), pk2u(c1, c1));
   tp[kTile] = make_ulonglong2(pk2u(c2, c2), pk2u(v, v));
   S.aw[t * (int64_t)kTile + (i % kTile)] = a;
+  if (S.acc != nullptr) {
+    // the slot's sums start at zero: the tile kernel adds its column sums in
+    float4 *r = reinterpret_cast<float4 *>(S.acc + (t * (int64_t)kTile + (i % kTile)) * kAcc3Stride);
+    r[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    r[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 }
 
 template <int NT>
