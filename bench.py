@@ -214,7 +214,7 @@ CPU_BASELINE_WHAT = (
     "sums the gradients are made of, on all host threads; the O(N) centering and "
     "normalisation chain rule is not timed.  The reference's own CPU path is PyTorch "
     "(rapidalign/kde.py), which materialises N x M matrices and needs the reference "
-    "package, so it does not travel to the GPU box; it ran at ~3e7 terms/s on 8 cores "
+    "package, which is not installed where this bench runs; it ran at ~3e7 terms/s on 8 cores "
     "when measured here, about 40x slower than this port")
 
 def cpu_units(name: str):

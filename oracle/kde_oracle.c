@@ -1,8 +1,8 @@
 /*
  * kde_oracle.c -- CPU fp64 oracle for the Gaussian-kernel KDE/MMD sums.
  *
- * TEST INFRASTRUCTURE ONLY.  This file is the checker the CUDA path is
- * compared against (tests, the smoke check and the CPU-baseline leg of the
+ * TEST INFRASTRUCTURE ONLY.  The CUDA path is compared against this file's
+ * results (tests, the smoke check and the CPU-baseline leg of the
  * benchmark).  Nothing in the product package links, loads or calls it.
  *
  * It restates, in plain C and in double precision, the analytic forward and

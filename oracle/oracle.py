@@ -2,7 +2,7 @@
 
 TEST INFRASTRUCTURE ONLY: imported by ``tests/``, by the smoke check in
 ``__graft_entry__.py`` and by the CPU-baseline leg of ``bench.py``, always as
-the checker.  The product package (``rapidalign_b200``) never imports it.
+the reference the CUDA path is compared with.  The product package (``rapidalign_b200``) never imports it.
 
 The heavy O(N*M) part is ``kde_oracle.c`` (a plain-C, double-precision
 restatement of ``rapidalign/kde_gradients.py:32-193``) loaded through ctypes.

@@ -6,7 +6,7 @@ the single-pair workload of 262144 points per cloud.
 The reference cannot evaluate this pair at all: its PyTorch path materialises
 N x M matrices (rapidalign/kde.py:83-101, 275 GB here) and its CUDA kernels
 put one pair on one thread block (csrc/kde_similarity.cu:196-233).  So the
-checker is the oracle (``oracle/kde_oracle.c``, a float64 restatement of
+reference values come from the oracle (``oracle/kde_oracle.c``, a float64 restatement of
 rapidalign/kde_gradients.py:39-132, with the centering and chain rules of
 ``oracle/oracle.py``), run once over the whole pair here and stored:
 
