@@ -1,7 +1,7 @@
 """Benchmark of the KDE/MMD hot path: Gaussian kernel-term evaluations per
 second, forward + backward, through the public API (``pyg_kde_mmd_loss``).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference-gpu]
     torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
 
 Workload (a "step"): one forward + backward of ``pyg_kde_mmd_loss`` over a
@@ -857,12 +857,102 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------
+# the reference's own GPU kernels (context: the same box, the same batch)
+# ----------------------------------------------------------------------------
+
+REF_GPU_UNAVAILABLE = {
+    "embed128": "the reference's segmented backward holds a point's difference in a "
+                "3-element array (csrc/kde_similarity.cu), so it is undefined for D > 3",
+    "dense": "the reference's dense op is forward-only (no dense backward in its extension)",
+    "huge-pair": "the reference puts one pair on one thread block: a 262144-point pair "
+                 "would take hours",
+}
+
+
+def run_reference_gpu(args):
+    """The reference's CUDA extension (its csrc/ sources built for sm_100a by
+    baseline/build_ref_cuda.py) on the same 4096-graph batch, as its
+    segmented_kde_loss runs it: kde_mmd_forward_segmented, the loss
+    Kxx + Kyy - 2 Kxy, then kde_mmd_backward_segmented with dL/dloss = 1.
+    Raw weights 1/n per graph, points as given (that path has no centring);
+    the kernel terms per step are the same as ours."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    base = {"impl": "reference-gpu", "metric": "Gaussian kernel-term evals/sec fwd+bwd",
+            "unit": "terms/s", "higher_is_better": True}
+    if args.workload in REF_GPU_UNAVAILABLE:
+        print(json.dumps(dict(base, unavailable=REF_GPU_UNAVAILABLE[args.workload])), flush=True)
+        return
+    import glob
+    import importlib.util
+    import torch
+    hits = sorted(glob.glob(os.path.join(ROOT, "baseline", "_ref", "rapidalign_ref_cuda*.so")))
+    if not hits or not torch.cuda.is_available():
+        why = "the reference extension is not built (baseline/build_ref_cuda.py)" if not hits \
+            else "no CUDA device"
+        print(json.dumps(dict(base, unavailable=why)), flush=True)
+        return
+    spec = importlib.util.spec_from_file_location("rapidalign_ref_cuda", hits[0])
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    wl = RaggedWorkload(0, 1, dev)
+    x, y = wl.d["x"].contiguous(), wl.d["y"].contiguous()
+    P = len(wl.mine)
+    cnt_x = torch.bincount(wl.d["bx"], minlength=P)
+    cnt_y = torch.bincount(wl.d["by"], minlength=P)
+    zero = torch.zeros(1, dtype=torch.long, device=dev)
+    px = torch.cat([zero, torch.cumsum(cnt_x, 0)])
+    py = torch.cat([zero, torch.cumsum(cnt_y, 0)])
+    wx = (1.0 / cnt_x.clamp_min(1).double()).repeat_interleave(cnt_x).float()
+    wy = (1.0 / cnt_y.clamp_min(1).double()).repeat_interleave(cnt_y).float()
+    g = torch.ones(P, dtype=torch.float64, device=dev)
+    sigma = float(wl.sigma)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        kxx, kyy, kxy = ref.kde_mmd_forward_segmented(x, y, wx, wy, px, py, sigma)
+        loss = kxx + kyy - 2.0 * kxy
+        ref.kde_mmd_backward_segmented(x, y, wx, wy, px, py, g, sigma)
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    evs = []
+    loss = None
+    for _ in range(args.steps):
+        flush.fill_(1)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        loss = step()
+        e1.record(stream)
+        evs.append((e0, e1))
+    torch.cuda.synchronize(dev)
+    t = sum(a.elapsed_time(b) for a, b in evs) / 1e3
+    config = dict(wl.describe(1, "strong"))
+    line = dict(base, value=wl.full_local * args.steps / t, n_gpus=1, steps=args.steps,
+                warmup=args.warmup, ms_per_step=t / args.steps * 1e3, scaling="strong",
+                vs_baseline=None, dtype="f64 (fp32 inputs)", data="synthetic", config=config,
+                what="the reference's segmented CUDA forward + backward (one thread block per "
+                     "pair, fp64), weights 1/n per graph, no centring",
+                loss_mean=float(loss.mean()))
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"],
+                    help="ours; reference (its CPU path: the fp64 port on the host cores); "
+                         "reference-gpu (its own CUDA kernels, built by baseline/build_ref_cuda.py)")
     ap.add_argument("--workload", default="ragged", choices=sorted(WORKLOADS),
                     help="ragged (default, the headline workload), huge-pair, dense, embed128")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
@@ -877,6 +967,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "reference-gpu":
+        run_reference_gpu(args)
     else:
         run_ours(args)
 
