@@ -66,3 +66,22 @@ def test_strong_scaling_shares_cover_the_batch():
             full += f
         assert abs(full - cfg["full_terms_per_step"]) <= 1e-9 * full
     assert bench.RaggedWorkload.describe(4, "weak")["graphs"] == 4 * cfg["graphs"]
+
+
+@pytest.mark.parametrize("workload", ["ragged", "embed128", "dense", "huge-pair"])
+def test_reference_gpu_arm_without_a_gpu(workload):
+    """The reference's own CUDA kernels are timed only on a GPU and only for
+    the D=3 ragged batch; otherwise the arm prints why, and exits 0."""
+    out = subprocess.run(
+        [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference-gpu",
+         "--workload", workload, "--steps", "1", "--warmup", "0"],
+        capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference-gpu"
+    if workload != "ragged":
+        assert line["unavailable"]
+    else:
+        import torch
+        if not torch.cuda.is_available():
+            assert line["unavailable"]
