@@ -31,13 +31,6 @@ __all__ = ["kde_mmd_loss", "kde_mmd_loss_bands", "kde_mmd_loss_dense", "pyg_kde_
            "pyg_batch_kde_mmd_loss", "batch_ptrs"]
 
 
-def _loss_from_k(Kxx: Tensor, Kyy: Tensor, Kxy: Tensor, cosine: bool, eps: float) -> Tensor:
-    """kde.py:103-107 / 265-268 / 368-371."""
-    if cosine:
-        return 1.0 - Kxy / (Kxx * Kyy).clamp_min(eps).sqrt()
-    return Kxx + Kyy - 2.0 * Kxy
-
-
 def _sigma_value(sigma, device) -> Tuple[float, Optional[Tensor]]:
     """sigma as a float for the kernels, plus the tensor if gradients flow to it."""
     if isinstance(sigma, Tensor):
