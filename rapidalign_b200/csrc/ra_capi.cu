@@ -1135,7 +1135,8 @@ const char *ra_status_string(int status) {
     case RA_ERR_WEIGHT_SUM: return "weights must sum to a positive value per segment";
     case RA_ERR_STATE: return "backward needs a forward run with need_grad (and need_sigma_grad)";
     case RA_ERR_DEVICE_TIMEOUT:
-      return "a bounded wait inside a kernel expired (tensor-core path); results are invalid";
+      return "a bounded wait inside a kernel expired (tensor-core kernels or bulk-copy passes); "
+             "results are invalid";
     case RA_ERR_SCRATCH_LIMIT:
       return "problem too large for the 64 MiB fixed scratch of the no-alloc entry point";
     default: return "unknown status";

@@ -157,7 +157,7 @@ enum : int {
   kErrPtrEnd = 2,
   kErrPtrOrder = 4,
   kErrWeightSum = 8,
-  kErrTimeout = 16,  // a bounded device-side wait expired (tensor-core path)
+  kErrTimeout = 16,  // a bounded device-side wait expired (tensor-core kernels, ring passes)
   kErrSigma = 32,    // a per-pair bandwidth is not > 0
 };
 

@@ -74,3 +74,38 @@ def test_legacy_ops_check_device():
     with pytest.raises(RuntimeError, match="must be CUDA tensor"):
         _cuda.kde_mmd_forward(x[None], x[None], w[None], w[None], w[None].bool(),
                               w[None].bool(), 0.2)
+
+
+def test_backward_error_words_are_read_at_the_next_call():
+    """A backward returns without stopping the GPU; the copy of its error word
+    is read at the next forward or backward: a finished clean word is
+    dropped, an unfinished one kept, a finished word with the timeout bit
+    raises (stand-in words, no GPU)."""
+    from rapidalign_b200 import _core, _lib
+    lib = _lib.load()
+
+    class Event:
+        def __init__(self, done):
+            self.done = done
+
+        def query(self):
+            return self.done
+
+    class Word:
+        def __init__(self, value, done):
+            self.event, self.value = Event(done), value
+
+        def read(self):
+            return [self.value]
+
+    saved = list(_core._LATE_WORDS)
+    try:
+        _core._LATE_WORDS[:] = [Word(0, True), Word(16, False)]
+        _core._check_late(lib)
+        assert len(_core._LATE_WORDS) == 1
+        _core._LATE_WORDS[0].event.done = True
+        with pytest.raises(RuntimeError, match="bounded wait"):
+            _core._check_late(lib)
+        assert _core._LATE_WORDS == []
+    finally:
+        _core._LATE_WORDS[:] = saved
