@@ -58,7 +58,7 @@ struct Layout {
   size_t tiles_x, tiles_y, Gx, Gy, Ax, Ay, accX, accY;
   size_t hx, hy, lx, ly, cx, cy;  // tc16: fp16 hi / lo tiles and slot values
   size_t ix;                      // tc16: one ItemX record per work item
-  size_t order, cost, hist;       // packed3: the tile kernel's item order (ra_plan.cuh)
+  size_t order;                   // packed3: the tile kernel's item order (ra_plan.cuh)
   size_t acc_x_bytes, acc_y_bytes;
   size_t total;
 };
@@ -69,6 +69,11 @@ struct Layout {
 // prep3_kernel, [5] epi3_small_kernel
 constexpr size_t kHdrErr = 0, kHdrTicket = 4, kHdrState = 8, kHdrNItems = 16,
                  kHdrChunkTickets = 32;
+// then the item order's size-bucket counters (ra_plan.cuh): hist @256,
+// cursor @256 + 4 kSizeBuckets, bbase @256 + 8 kSizeBuckets; the whole
+// header is zeroed at the start of every forward
+constexpr size_t kHdrSizeHist = 256, kHdrBytes = 4096;
+static_assert(kHdrSizeHist + 3 * 4 * kSizeBuckets <= kHdrBytes, "header too small");
 constexpr int kItemF64 = 2;  // fp64 partials per work item: K, S
 
 bool desc_ok(const ra_kde_desc *d) {
@@ -148,7 +153,7 @@ Layout make_layout(const ra_kde_desc *d) {
     return at;
   };
   const size_t P1 = (size_t)(P > 0 ? P : 1);
-  L.hdr = take(256);
+  L.hdr = take(kHdrBytes);
   L.seg = take(sizeof(Seg) * P1);
   L.meta = take(sizeof(double) * P1 * meta_stride(L.DP));
   L.cnt = take(sizeof(int64_t) * 3 * P1);
@@ -173,8 +178,6 @@ Layout make_layout(const ra_kde_desc *d) {
   const size_t nx = (size_t)(NX > 0 ? NX : 1), ny = (size_t)(NY > 0 ? NY : 1);
   if (L.packed3) {
     L.order = take(sizeof(int32_t) * (size_t)L.max_items);
-    L.cost = take((size_t)L.max_items);
-    L.hist = take(sizeof(int32_t) * 2 * kCostBuckets);
     L.tiles_x = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_x);
     L.tiles_y = take((size_t)16 * L.nq * kTile * (size_t)L.max_tiles_y);
     L.Ax = take(sizeof(float) * kTile * (size_t)L.max_tiles_x);  // a~ per slot
@@ -452,7 +455,7 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
   if (rc) return rc;
   const int64_t P = d->num_pairs;
   // header: error word, ticket, state flag, item count
-  if (cudaMemsetAsync(ws, 0, 256, st) != cudaSuccess) return RA_ERR_CUDA;
+  if (cudaMemsetAsync(ws, 0, kHdrBytes, st) != cudaSuccess) return RA_ERR_CUDA;
   if (P == 0) return RA_OK;
   const bool grad = d->need_grad != 0;
   const int mode = !grad ? 0 : (d->need_sigma_grad ? 2 : (d->skip_weight_sums ? 3 : 1));
@@ -653,19 +656,13 @@ int prepare_impl(const ra_kde_desc *d, const ra_kde_inputs *in, void *ws, size_t
   pl.items = at<Item>(ws, L.items);
   pl.max_items = L.max_items;
   pl.order = L.packed3 ? at<int32_t>(ws, L.order) : nullptr;
-  pl.cost = L.packed3 ? at<uint8_t>(ws, L.cost) : nullptr;
-  pl.hist = L.packed3 ? at<int32_t>(ws, L.hist) : nullptr;
-  pl.cursor = L.packed3 ? pl.hist + kCostBuckets : nullptr;
-  plan_count_kernel<<<(unsigned)ceil_div(P > kCostBuckets ? P : kCostBuckets, 256), 256, 0, st>>>(pl);
+  pl.hist = L.packed3 ? at<int32_t>(ws, L.hdr + kHdrSizeHist) : nullptr;
+  pl.cursor = L.packed3 ? pl.hist + kSizeBuckets : nullptr;
+  pl.bbase = L.packed3 ? pl.hist + 2 * kSizeBuckets : nullptr;
+  plan_count_kernel<<<(unsigned)ceil_div(P, 256), 256, 0, st>>>(pl);
   plan_scan_kernel<<<1, 1024, 0, st>>>(pl);
   plan_emit_kernel<<<(unsigned)P, 256, 0, st>>>(pl);
   g_launches += 3;
-  if (L.packed3) {
-    const unsigned og = (unsigned)(L.max_items < 256 * 592 ? ceil_div(L.max_items, (int64_t)256)
-                                                           : 592);
-    plan_order_kernel<<<og, 256, 0, st>>>(pl);
-    ++g_launches;
-  }
   if (cudaGetLastError() != cudaSuccess) return RA_ERR_CUDA;
 
   // ---- the tensor-core path's per-item records (the plan is complete) ----

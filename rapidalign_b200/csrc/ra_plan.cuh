@@ -18,26 +18,21 @@ struct PlanArgs {
   int64_t *n_items;   // device scalar (== item_off[P])
   Item *items;
   int64_t max_items;  // capacity of `items` (the host bound)
-  // D <= 3 tiles: the order the tile kernel takes the items in, largest
-  // first (null: plan order).  cost[i] = column tiles of item i (capped at
-  // kCostBuckets - 1), hist / cursor: [kCostBuckets] counters.
+  // D <= 3 tiles: the order the tile kernel takes the items in (null: plan
+  // order): pairs by decreasing size, each pair's items contiguous and in
+  // plan order.  hist (items per size bucket), cursor and bbase (first
+  // position of a bucket): [kSizeBuckets] counters, zeroed before the plan.
   int32_t *order;
-  uint8_t *cost;
-  int32_t *hist, *cursor;
+  int32_t *hist, *cursor, *bbase;
 };
 
-constexpr int kCostBuckets = 256;
+constexpr int kSizeBuckets = 256;
 
-// atomicAdd(&ctr[key], 1) for every active lane, one atomic per distinct key
-// in the warp; returns the lane's value (the counter before its own +1)
-__device__ __forceinline__ int32_t warp_count_add(int32_t *ctr, int key) {
-  const unsigned peers = __match_any_sync(__activemask(), key);
-  const int lane = threadIdx.x & 31;
-  const int leader = __ffs(peers) - 1;
-  int32_t base = 0;
-  if (lane == leader) base = atomicAdd(ctr + key, __popc(peers));
-  base = __shfl_sync(peers, base, leader);
-  return base + __popc(peers & ((1u << lane) - 1u));
+// A pair's size bucket: 64-point tiles of its larger side, capped.
+__device__ __forceinline__ int pair_size_key(const Seg &s) {
+  const int64_t n = s.xcount > s.ycount ? s.xcount : s.ycount;
+  const int64_t t = ceil_div(n, (int64_t)kTile);
+  return t > kSizeBuckets - 1 ? kSizeBuckets - 1 : (int)t;
 }
 
 __device__ __forceinline__ void block_counts(const Seg &s, int generic, int64_t c[4]) {
@@ -67,18 +62,16 @@ __device__ __forceinline__ void block_counts(const Seg &s, int generic, int64_t 
 
 __global__ void plan_count_kernel(PlanArgs A) {
   const int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (A.order != nullptr && blockIdx.x == 0 && threadIdx.x < kCostBuckets) {
-    A.hist[threadIdx.x] = 0;
-    A.cursor[threadIdx.x] = 0;
-  }
   if (p >= A.P) return;
   int64_t c[4];
-  block_counts(A.seg[p], A.generic, c);
+  const Seg sg = A.seg[p];
+  block_counts(sg, A.generic, c);
   A.boff[p * 4 + 0] = 0;
   A.boff[p * 4 + 1] = c[0];
   A.boff[p * 4 + 2] = c[0] + c[1];
   A.boff[p * 4 + 3] = c[0] + c[1] + c[2];
   A.cnt[p] = c[0] + c[1] + c[2] + c[3];
+  if (A.order != nullptr && A.cnt[p] > 0) atomicAdd(&A.hist[pair_size_key(sg)], (int)A.cnt[p]);
 }
 
 // Exclusive scan of the per-pair item counts into item_off ([P + 1]); one
@@ -126,6 +119,19 @@ __global__ void __launch_bounds__(1024) plan_scan_kernel(PlanArgs A) {
       dst[A.P] = tot;
     }
   }
+  if (A.order != nullptr) {
+    // first position of each size bucket, the largest pairs first
+    __shared__ int32_t hs[kSizeBuckets];
+    for (int b = tid; b < kSizeBuckets; b += blockDim.x) hs[b] = A.hist[b];
+    __syncthreads();
+    if (tid == 0) {
+      int32_t run = 0;
+      for (int b = kSizeBuckets - 1; b >= 0; --b) {
+        A.bbase[b] = run;
+        run += hs[b];
+      }
+    }
+  }
 }
 
 // One CTA per pair writes that pair's items.
@@ -164,47 +170,17 @@ __global__ void plan_emit_kernel(PlanArgs A) {
     it.tile = (int)(loc % nr);
     it.split = (int)(loc / nr);
     A.items[base + l] = it;
-    if (A.order != nullptr) {
-      // the item's column tiles, as the tile kernel derives its range
-      const int64_t ncols = (b == 1 || b == 3) ? s.xcount : s.ycount;
-      const int64_t nTc = ceil_div(ncols, (int64_t)kTile);
-      const int64_t L = (nTc + S[b] - 1) / S[b];
-      int64_t J0 = (int64_t)it.split * L;
-      const int64_t J1 = J0 + L < nTc ? J0 + L : nTc;
-      if (A.generic == 0 && (b == 1 || b == 2) && J0 < it.tile) J0 = it.tile;  // upper triangle
-      int64_t cst = J1 > J0 ? J1 - J0 : 0;
-      if (cst > kCostBuckets - 1) cst = kCostBuckets - 1;
-      A.cost[base + l] = (uint8_t)cst;
-      warp_count_add(A.hist, (int)cst);
-    }
   }
-}
-
-// The tile kernel's item order, largest first (a counting sort by column
-// tiles; ties in any order: every item writes its own partials, reduced later
-// in plan order, so the results do not depend on it).  Each CTA scans the
-// histogram itself.  Not used when the items are split over shards: the order
-// of equal costs differs from one run to the next, and the shards must
-// partition the same list.
-__global__ void __launch_bounds__(256) plan_order_kernel(PlanArgs A) {
-  __shared__ int32_t off[kCostBuckets];
-  const int t = threadIdx.x;
-  // off[b] = items with a larger cost
-  if (t < kCostBuckets) off[t] = A.hist[t];
-  __syncthreads();
-  if (t == 0) {
-    int32_t run = 0;
-    for (int b = kCostBuckets - 1; b >= 0; --b) {
-      const int32_t h = off[b];
-      off[b] = run;
-      run += h;
-    }
-  }
-  __syncthreads();
-  const int64_t n = *A.n_items;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + t; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int b = A.cost[i];
-    A.order[off[b] + warp_count_add(A.cursor, b)] = (int32_t)i;
+  if (A.order != nullptr && total > 0) {
+    // the pair's items take one contiguous run of the order, in plan order,
+    // at a place in their size bucket (pairs of one bucket in any order:
+    // every item writes its own partials, reduced later in plan order)
+    __shared__ int64_t pos;
+    if (threadIdx.x == 0)
+      pos = (int64_t)A.bbase[pair_size_key(s)] + atomicAdd(&A.cursor[pair_size_key(s)], (int)total);
+    __syncthreads();
+    for (int64_t l = threadIdx.x; l < total; l += blockDim.x)
+      if (pos + l < A.max_items && base + l < A.max_items) A.order[pos + l] = (int32_t)(base + l);
   }
 }
 

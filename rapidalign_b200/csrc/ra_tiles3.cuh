@@ -258,7 +258,8 @@ __global__ void __launch_bounds__(kT3Threads, kT3MinBlocks) tiles3_kernel(Tiles3
     ticket = __shfl_sync(kFull, ticket, 0);
     const int64_t k = A.shard_index + (int64_t)ticket * A.shard_count;
     if (k >= total) break;
-    const int64_t it = A.order != nullptr ? A.order[k] : k;  // largest items first
+    const int64_t it = A.order != nullptr ? A.order[k] : k;  // largest pairs first
+    if (it < 0 || it >= total) continue;  // (an order entry the plan could not write)
     const Item item = A.items[it];
     const Seg sg = A.seg[item.pair];
     const int blk = item.block;
