@@ -17,7 +17,9 @@
 //
 // Work decomposition (B200: 148 SMs, FP32-pipe bound): a persistent grid of
 // independent warps pulls items (pair, block, 64-row tile, column split) from
-// a global ticket.  Inside a warp the 32 lanes form 4 rings of 8 lanes.  Every
+// a global ticket, in the plan's order (ra_plan.cuh: the largest pairs first,
+// each pair's items together, so neighbouring items share column tiles in
+// L2).  Inside a warp the 32 lanes form 4 rings of 8 lanes.  Every
 // ring holds the same 64 rows (8 per lane, as 4 packed row pairs) and owns 16
 // of the 64 columns of the current column tile; the column accumulators
 // travel around the ring (one shuffle per step), so each column sum is
